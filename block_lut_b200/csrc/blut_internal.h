@@ -1,0 +1,69 @@
+// Internal declarations shared by the libblut translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/blut.h"
+
+namespace blut {
+
+constexpr int kMaxExperts = 1024;
+constexpr int kMaxSlots = 2048;   // T * top_k of the decode path
+constexpr int kDevBadExpert = 2;  // device status bit: an expert id was out of range
+
+struct MMParams;
+
+// Routing plan in the workspace.
+struct PlanPtrs {
+  int* status;
+  int* meta;  // [0] groups, [1] n-tiles, [2] shared groups, [3] shared n-tiles
+  int *g_expert, *g_slot0, *g_ntok, *g_nt0;
+  int *nt_slot0, *nt_cnt;
+  int *sg_expert, *sg_slot0, *sg_ntok, *sg_nt0;
+  int* tk_slot;   // [T*k] slot of (token, j), -1 if the id was invalid
+  int* slot_tok;  // [T*k] token of each slot
+};
+
+struct MoEWs {
+  int* status;
+  int32_t* ids;
+  float* tw;
+  float* sg;
+  PlanPtrs pp;
+  uint8_t *xf, *af, *xfs, *afs;
+  float *y, *ys;
+  int64_t ntmax, sntmax;
+};
+
+int num_sms();
+size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws);
+int validate_moe(const blut_moe_args& a);
+int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaStream_t stream);
+int moe_launch_count(const blut_moe_args& a);
+int router(const void* x, const void* w, int T, int H, int E, int K, int renorm, int has_sg, int dtype,
+           int32_t* ids, float* tw, float* sg, cudaStream_t stream);
+
+// LUT matmul dispatch over formats (blut_mm_inst_*.cu).
+cudaError_t launch_lut_mm(const blut_mat_desc& d, bool pair, const MMParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_mm_b4(int group, bool pair, const MMParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_mm_b3(int group, bool pair, const MMParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_mm_b2(int group, bool pair, const MMParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_mm_nested(int group, bool pair, const MMParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_mm_r8(bool pair, const MMParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_mm_dense(bool bf16, bool pair, const MMParams& p, int sms, cudaStream_t stream);
+
+// Canonical-layout kernels (blut_pack.cu, blut_gemv.cu).
+int dequant(const blut_mat_desc& d, const blut_canon& c, void* out, cudaStream_t stream);
+int pack_tiled(const blut_mat_desc& d, const blut_canon& c, void* tiled, cudaStream_t stream);
+int encode(const blut_mat_desc& d, const float* w, void* codes, void* tables, void* codes2, void* tables2,
+           cudaStream_t stream);
+int encode_r(const void* w, int64_t n, const void* cb, int block_size, void* idx, void* absmax,
+             cudaStream_t stream);
+int blocklut_decompress(void* out, const void* idx, const void* absmax, const void* cb, int64_t num_experts,
+                        int64_t elems, int64_t blocks_per_expert, int block_size, cudaStream_t stream);
+int lut_recover(void* out, const void* idx, const void* lut, int64_t n, cudaStream_t stream);
+int lut_gemv(const void* x, const void* idx, const void* cb, const void* absmax, void* y, int64_t m, int64_t k,
+             int64_t nb, cudaStream_t stream);
+
+}  // namespace blut

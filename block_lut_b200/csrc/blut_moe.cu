@@ -1,0 +1,525 @@
+// MoE layer orchestration: router, routing plan, B-fragment gather, the LUT
+// matmul launches and the weighted combine.  All launches go on the caller's
+// stream; nothing synchronises the host and nothing allocates.
+#include <algorithm>
+#include <mutex>
+
+#include "blut_mm.cuh"
+#include "blut_internal.h"
+
+namespace blut {
+
+// --------------------------------------------------------------- router ---
+// One CTA per token: logits of all experts (+ the shared-expert gate row),
+// softmax, top-k with lowest-index tie-breaking, optional renormalisation.
+template <bool BF16>
+__global__ void __launch_bounds__(256) router_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                     int hidden, int num_experts, int top_k, int renorm,
+                                                     int has_sg, int do_topk, int32_t* __restrict__ ids,
+                                                     float* __restrict__ tw, float* __restrict__ sg) {
+  extern __shared__ float logits[];
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = (do_topk ? num_experts : 0) + (has_sg ? 1 : 0);
+  const uint16_t* xr = x + (int64_t)t * hidden;
+  for (int rr = warp; rr < rows; rr += 8) {
+    const int r = do_topk ? rr : num_experts;  // gate-only mode reads row E
+    const uint16_t* wr = w + (int64_t)r * hidden;
+    float acc = 0.f;
+    for (int k = lane * 8; k < hidden; k += 256) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
+      const uint4 wv = *reinterpret_cast<const uint4*>(wr + k);
+      const uint16_t* xs = reinterpret_cast<const uint16_t*>(&xv);
+      const uint16_t* ws = reinterpret_cast<const uint16_t*>(&wv);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc = fmaf(act_to_f32<BF16>(xs[q]), act_to_f32<BF16>(ws[q]), acc);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) logits[rr] = acc;
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  if (has_sg) {
+    const float z = logits[rows - 1];
+    if (lane == 0) sg[t] = 1.f / (1.f + expf(-z));
+  }
+  if (!do_topk) return;
+  float mx = -INFINITY;
+  for (int e = lane; e < num_experts; e += 32) mx = fmaxf(mx, logits[e]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+  for (int e = lane; e < num_experts; e += 32) {
+    const float v = expf(logits[e] - mx);
+    logits[e] = v;
+    sum += v;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  __syncwarp();
+  const float inv = 1.f / sum;
+  float wsum = 0.f;
+  float myw = 0.f;
+  int myid = 0;
+  for (int j = 0; j < top_k; ++j) {
+    float best = -1.f;
+    int bi = 0x7fffffff;
+    for (int e = lane; e < num_experts; e += 32) {
+      const float v = logits[e];
+      if (v > best) { best = v; bi = e; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    const float p = best * inv;
+    wsum += p;
+    if (lane == j) { myw = p; myid = bi; }
+    if (lane == (bi & 31)) logits[bi] = -2.f;  // taken
+    __syncwarp();
+  }
+  if (lane < top_k) {
+    ids[(int64_t)t * top_k + lane] = myid;
+    tw[(int64_t)t * top_k + lane] = renorm ? myw / wsum : myw;
+  }
+}
+
+// ----------------------------------------------------------------- plan ---
+// Single CTA: per-expert counts, slots (tokens of an expert are contiguous,
+// in (token, k) order), groups of <= 32 tokens and their 8-token n-tiles;
+// also the shared expert's groups (identity slots).
+__global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ ids, int num_tokens, int top_k,
+                                                     int num_experts, int has_shared, PlanPtrs pp) {
+  __shared__ int cnt[kMaxExperts];
+  __shared__ int off[kMaxExperts];
+  const int S = num_tokens * top_k;
+  if (threadIdx.x == 0) *pp.status = 0;
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int q = threadIdx.x; q < S; q += blockDim.x) {
+    const int e = ids[q];
+    if (e >= 0 && e < num_experts) atomicAdd(&cnt[e], 1);
+    else atomicOr(pp.status, kDevBadExpert);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, ng = 0, nnt = 0;
+    for (int e = 0; e < num_experts; ++e) {
+      off[e] = acc;
+      const int c = cnt[e];
+      for (int q = 0; q * kGroupTok < c; ++q) {
+        const int ntok = min(kGroupTok, c - q * kGroupTok);
+        pp.g_expert[ng] = e;
+        pp.g_slot0[ng] = acc + q * kGroupTok;
+        pp.g_ntok[ng] = ntok;
+        pp.g_nt0[ng] = nnt;
+        for (int i = 0; i * kNTile < ntok; ++i) {
+          pp.nt_slot0[nnt] = acc + q * kGroupTok + i * kNTile;
+          pp.nt_cnt[nnt] = min(kNTile, ntok - i * kNTile);
+          ++nnt;
+        }
+        ++ng;
+      }
+      acc += c;
+    }
+    pp.meta[0] = ng;
+    pp.meta[1] = nnt;
+    int sng = 0, snt = 0;
+    if (has_shared) {
+      for (int q = 0; q * kGroupTok < num_tokens; ++q) {
+        const int ntok = min(kGroupTok, num_tokens - q * kGroupTok);
+        pp.sg_expert[sng] = 0;
+        pp.sg_slot0[sng] = q * kGroupTok;
+        pp.sg_ntok[sng] = ntok;
+        pp.sg_nt0[sng] = snt;
+        snt += (ntok + kNTile - 1) / kNTile;
+        ++sng;
+      }
+    }
+    pp.meta[2] = sng;
+    pp.meta[3] = snt;
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < S; q += blockDim.x) {
+    const int e = ids[q];
+    if (e < 0 || e >= num_experts) {
+      pp.tk_slot[q] = -1;
+      continue;
+    }
+    int rank = 0;
+    for (int r = 0; r < q; ++r) rank += ids[r] == e;
+    const int slot = off[e] + rank;
+    pp.tk_slot[q] = slot;
+    pp.slot_tok[slot] = q / top_k;
+  }
+}
+
+// --------------------------------------------------------------- gather ---
+// B fragments of the activations: block (n-tile, chunk), 32 threads = lanes.
+// z = 0: routed n-tiles (token of slot via slot_tok), z = 1: shared expert
+// (slot = token).
+__global__ void __launch_bounds__(32) gather_bfrag_kernel(const uint16_t* __restrict__ x, int hidden, PlanPtrs pp,
+                                                          uint8_t* __restrict__ xf, uint8_t* __restrict__ xfs) {
+  const bool shared = blockIdx.z == 1;
+  const int nt = blockIdx.x;
+  const int c = blockIdx.y;
+  const int n_nt = shared ? pp.meta[3] : pp.meta[1];
+  if (nt >= n_nt) return;
+  const int nchunks = hidden / kChunk;
+  const int lane = threadIdx.x;
+  const int g = lane >> 2, tq = lane & 3;
+  int cntv, slot0;
+  if (shared) {
+    slot0 = nt * kNTile;  // shared groups are 32-aligned, n-tiles 8-aligned
+    cntv = 0;
+    // count tokens of this n-tile: the last group may be partial
+    const int sng = pp.meta[2];
+    for (int q = 0; q < sng; ++q) {
+      const int nt0 = pp.sg_nt0[q];
+      const int ntok = pp.sg_ntok[q];
+      if (nt >= nt0 && nt < nt0 + (ntok + kNTile - 1) / kNTile) {
+        slot0 = pp.sg_slot0[q] + (nt - nt0) * kNTile;
+        cntv = min(kNTile, ntok - (nt - nt0) * kNTile);
+      }
+    }
+  } else {
+    slot0 = pp.nt_slot0[nt];
+    cntv = pp.nt_cnt[nt];
+  }
+  uint32_t wv[16];
+  if (g < cntv) {
+    const int slot = slot0 + g;
+    const int tok = shared ? slot : pp.slot_tok[slot];
+    const uint32_t* row = reinterpret_cast<const uint32_t*>(x + (int64_t)tok * hidden + c * kChunk);
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      wv[2 * s] = row[(16 * s + 2 * tq) >> 1];
+      wv[2 * s + 1] = row[(16 * s + 2 * tq + 8) >> 1];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) wv[i] = 0;
+  }
+  uint8_t* dst = (shared ? xfs : xf) + ((int64_t)nt * nchunks + c) * kBfragChunkBytes + lane * 64;
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
+}
+
+// -------------------------------------------------------------- combine ---
+// out[t] = sum_j w[t,j] * y[slot(t,j)] (+ g_t * y_shared[t]), fp32, one rounding.
+template <bool BF16>
+__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, const float* __restrict__ ys,
+                                                      const float* __restrict__ tw, const int* __restrict__ tk_slot,
+                                                      const float* __restrict__ sg, int top_k, int hidden,
+                                                      int shared_mode, uint16_t* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int h = threadIdx.x * 4; h < hidden; h += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < top_k; ++j) {
+      const int slot = tk_slot[(int64_t)t * top_k + j];
+      if (slot < 0) continue;
+      const float w = tw[(int64_t)t * top_k + j];
+      const float4 v = *reinterpret_cast<const float4*>(y + (int64_t)slot * hidden + h);
+      acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+    }
+    if (shared_mode >= 0) {
+      const float g = shared_mode == 1 ? sg[t] : 1.f;
+      const float4 v = *reinterpret_cast<const float4*>(ys + (int64_t)t * hidden + h);
+      acc.x += g * v.x; acc.y += g * v.y; acc.z += g * v.z; acc.w += g * v.w;
+    }
+    uint2 o;
+    o.x = uint32_t(f32_to_act<BF16>(acc.x)) | (uint32_t(f32_to_act<BF16>(acc.y)) << 16);
+    o.y = uint32_t(f32_to_act<BF16>(acc.z)) | (uint32_t(f32_to_act<BF16>(acc.w)) << 16);
+    *reinterpret_cast<uint2*>(out + (int64_t)t * hidden + h) = o;
+  }
+}
+
+// ------------------------------------------------------------ host side ---
+int num_sms() {
+  static int sms = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  });
+  return sms;
+}
+
+static bool same_format(const blut_mat_desc& a, const blut_mat_desc& b) {
+  return a.format == b.format && a.bits == b.bits && a.group == b.group && a.tier == b.tier && a.dtype == b.dtype;
+}
+
+// Workspace carve-up; returns total bytes, fills pointers when base != null.
+size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
+  const int64_t T = a.num_tokens, K = a.top_k, E = a.num_experts, H = a.hidden, I = a.inter;
+  const int64_t S = T * K;
+  const int64_t gmax = E + (S + kGroupTok - 1) / kGroupTok + 1;
+  const int64_t ntmax = (S + kNTile - 1) / kNTile + gmax;
+  const int64_t sgmax = (T + kGroupTok - 1) / kGroupTok + 1;
+  const int64_t sntmax = (T + kNTile - 1) / kNTile + 1;
+  const bool sh = a.shared_inter > 0;
+  size_t off = 0;
+  auto take = [&](int64_t bytes) {
+    const size_t o = off;
+    off = (size_t)align256(off + bytes);
+    return o;
+  };
+  MoEWs w{};
+  size_t o_status = take(256);
+  size_t o_ids = take(S * 4), o_tw = take(S * 4), o_sg = take(T * 4);
+  size_t o_meta = take(64);
+  size_t o_g = take(gmax * 4 * 4), o_nt = take(ntmax * 4 * 2), o_sgp = take(sgmax * 4 * 4);
+  size_t o_tk = take(S * 4), o_st = take(S * 4);
+  size_t o_xf = take(ntmax * (H / kChunk) * kBfragChunkBytes);
+  size_t o_af = take(ntmax * (I / kChunk) * kBfragChunkBytes);
+  size_t o_y = take(S * H * 4);
+  size_t o_xfs = sh ? take(sntmax * (H / kChunk) * kBfragChunkBytes) : 0;
+  size_t o_afs = sh ? take(sntmax * (a.shared_inter / kChunk) * kBfragChunkBytes) : 0;
+  size_t o_ys = sh ? take(T * H * 4) : 0;
+  if (base && ws) {
+    w.status = reinterpret_cast<int*>(base + o_status);
+    w.ids = reinterpret_cast<int32_t*>(base + o_ids);
+    w.tw = reinterpret_cast<float*>(base + o_tw);
+    w.sg = reinterpret_cast<float*>(base + o_sg);
+    int* g = reinterpret_cast<int*>(base + o_g);
+    int* nt = reinterpret_cast<int*>(base + o_nt);
+    int* sg = reinterpret_cast<int*>(base + o_sgp);
+    w.pp.status = w.status;
+    w.pp.meta = reinterpret_cast<int*>(base + o_meta);
+    w.pp.g_expert = g;
+    w.pp.g_slot0 = g + gmax;
+    w.pp.g_ntok = g + 2 * gmax;
+    w.pp.g_nt0 = g + 3 * gmax;
+    w.pp.nt_slot0 = nt;
+    w.pp.nt_cnt = nt + ntmax;
+    w.pp.sg_expert = sg;
+    w.pp.sg_slot0 = sg + sgmax;
+    w.pp.sg_ntok = sg + 2 * sgmax;
+    w.pp.sg_nt0 = sg + 3 * sgmax;
+    w.pp.tk_slot = reinterpret_cast<int*>(base + o_tk);
+    w.pp.slot_tok = reinterpret_cast<int*>(base + o_st);
+    w.xf = base + o_xf;
+    w.af = base + o_af;
+    w.y = reinterpret_cast<float*>(base + o_y);
+    w.xfs = sh ? base + o_xfs : nullptr;
+    w.afs = sh ? base + o_afs : nullptr;
+    w.ys = sh ? reinterpret_cast<float*>(base + o_ys) : nullptr;
+    w.ntmax = ntmax;
+    w.sntmax = sntmax;
+    *ws = w;
+  }
+  return off;
+}
+
+int validate_moe(const blut_moe_args& a) {
+  if (a.num_tokens <= 0 || a.hidden <= 0 || a.inter <= 0 || a.num_experts <= 0 || a.top_k <= 0) return BLUT_ERR_INVALID;
+  if (a.num_experts > kMaxExperts || a.top_k > 32 || a.top_k > a.num_experts) return BLUT_ERR_UNSUPPORTED;
+  if ((int64_t)a.num_tokens * a.top_k > kMaxSlots) return BLUT_ERR_UNSUPPORTED;
+  if (a.hidden % kChunk || a.inter % kChunk) return BLUT_ERR_UNSUPPORTED;
+  if (a.dtype != BLUT_F16 && a.dtype != BLUT_BF16) return BLUT_ERR_INVALID;
+  if (!a.x || !a.out || !a.w13_tiled || !a.w2_tiled) return BLUT_ERR_INVALID;
+  if (!a.topk_ids && !a.router_w) return BLUT_ERR_INVALID;
+  if (a.topk_ids && !a.topk_weights) return BLUT_ERR_INVALID;
+  if (!same_format(a.w13, a.w2)) return BLUT_ERR_UNSUPPORTED;
+  if (a.w13.rows != 2LL * a.inter || a.w13.cols != a.hidden || a.w2.rows != a.hidden || a.w2.cols != a.inter)
+    return BLUT_ERR_INVALID;
+  if (a.w13.dtype != a.dtype) return BLUT_ERR_UNSUPPORTED;
+  if (a.w13.format == BLUT_FMT_R8 && !a.lut_table) return BLUT_ERR_INVALID;
+  TiledLayout L13, L2;
+  if (!make_layout(a.w13, L13) || !make_layout(a.w2, L2)) return BLUT_ERR_UNSUPPORTED;
+  if (a.w13_stride < L13.total || a.w2_stride < L2.total) return BLUT_ERR_INVALID;
+  if ((a.w13_stride | a.w2_stride) & 255) return BLUT_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(a.w13_tiled) | reinterpret_cast<uintptr_t>(a.w2_tiled) |
+       reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.out)) & 15)
+    return BLUT_ERR_INVALID;
+  if (a.shared_inter > 0) {
+    if (a.shared_inter % kChunk || !a.s13_tiled || !a.s2_tiled) return BLUT_ERR_INVALID;
+    if (a.s13.format != BLUT_FMT_DENSE || a.s2.format != BLUT_FMT_DENSE) return BLUT_ERR_UNSUPPORTED;
+    if (a.s13.dtype != a.dtype || a.s2.dtype != a.dtype) return BLUT_ERR_UNSUPPORTED;
+    if (a.s13.rows != 2LL * a.shared_inter || a.s13.cols != a.hidden || a.s2.rows != a.hidden ||
+        a.s2.cols != a.shared_inter)
+      return BLUT_ERR_INVALID;
+    if (a.shared_gate_mode == 1 && !a.shared_gate_w && !(a.router_w && !a.topk_ids)) return BLUT_ERR_INVALID;
+  }
+  return BLUT_OK;
+}
+
+// Fills the plane part of MMParams for matrix `d`.
+bool mm_planes(const blut_mat_desc& d, bool pair, MMParams& p) {
+  TiledLayout L;
+  if (!make_layout(d, L)) return false;
+  int idx[3] = {0, 1, 2};
+  int np = L.nplanes;
+  if (d.format == BLUT_FMT_NESTED) {
+    if (d.tier == 0) {
+      idx[0] = 0; idx[1] = 2; idx[2] = 3; np = 3;
+    } else {
+      np = 2;
+    }
+  }
+  int tb = 0;
+  for (int q = 0; q < 3; ++q) {
+    p.plane_off[q] = q < np ? L.off[idx[q]] : 0;
+    p.piece[q] = q < np ? (int)L.piece[idx[q]] : 0;
+    tb += p.piece[q];
+  }
+  p.tile_bytes = tb;
+  p.ntiles = (int)L.ntiles;
+  p.nchunks = (int)L.nchunks;
+  const int stage = (pair ? 2 : 1) * tb;
+  p.stages = std::max(2, std::min(8, kWarpRingBytes / stage));
+  p.r8_mask = d.tier == 1 ? 0x3Fu : d.tier == 2 ? 0x0Fu : 0xFFu;
+  return true;
+}
+
+int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  int rc = validate_moe(a);
+  if (rc != BLUT_OK) return rc;
+  if (!workspace) return BLUT_ERR_INVALID;
+  const size_t need = moe_workspace(a, nullptr, nullptr);
+  if (ws_bytes < need) return BLUT_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return BLUT_ERR_INVALID;
+  MoEWs ws;
+  moe_workspace(a, static_cast<uint8_t*>(workspace), &ws);
+  const bool bf16 = a.dtype == BLUT_BF16;
+  const bool sh = a.shared_inter > 0;
+  const int T = a.num_tokens, K = a.top_k, E = a.num_experts, H = a.hidden;
+  const int sms = num_sms();
+
+  // 1. routing (or the caller's routing) and the shared-expert gate
+  const int32_t* ids = a.topk_ids;
+  const float* tw = a.topk_weights;
+  const bool route = a.topk_ids == nullptr;
+  const bool sg_from_router = sh && a.shared_gate_mode == 1 && route && !a.shared_gate_w;
+  if (route) {
+    const size_t smem = (E + 1) * sizeof(float);
+    if (bf16)
+      router_kernel<true><<<T, 256, smem, stream>>>((const uint16_t*)a.x, (const uint16_t*)a.router_w, H, E, K,
+                                                      a.renorm, sg_from_router, 1, ws.ids, ws.tw, ws.sg);
+    else
+      router_kernel<false><<<T, 256, smem, stream>>>((const uint16_t*)a.x, (const uint16_t*)a.router_w, H, E, K,
+                                                       a.renorm, sg_from_router, 1, ws.ids, ws.tw, ws.sg);
+    ids = ws.ids;
+    tw = ws.tw;
+  }
+  if (sh && a.shared_gate_mode == 1 && !sg_from_router) {
+    // gate-only pass over the single row shared_gate_w (as row "E" of a 0-expert router)
+    const uint16_t* gw = (const uint16_t*)a.shared_gate_w;
+    if (bf16)
+      router_kernel<true><<<T, 256, 2 * sizeof(float), stream>>>((const uint16_t*)a.x, gw, H, 0, 0, 0, 1, 0,
+                                                                   nullptr, nullptr, ws.sg);
+    else
+      router_kernel<false><<<T, 256, 2 * sizeof(float), stream>>>((const uint16_t*)a.x, gw, H, 0, 0, 0, 1, 0,
+                                                                    nullptr, nullptr, ws.sg);
+  }
+  // 2. plan
+  plan_kernel<<<1, 1024, 0, stream>>>(ids, T, K, E, sh ? 1 : 0, ws.pp);
+  // 3. B fragments of x (routed and shared)
+  {
+    dim3 grid((unsigned)std::max<int64_t>(ws.ntmax, sh ? ws.sntmax : 0), (unsigned)(H / kChunk), sh ? 2 : 1);
+    gather_bfrag_kernel<<<grid, 32, 0, stream>>>((const uint16_t*)a.x, H, ws.pp, ws.xf, ws.xfs);
+  }
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return BLUT_ERR_LAUNCH;
+
+  // 4. gate/up + SiLU*up, 5. down -- routed experts
+  MMParams p{};
+  p.status = ws.status;
+  p.r8_table = (const uint16_t*)a.lut_table;
+  p.gt = GroupTab{ws.pp.meta + 0, ws.pp.g_expert, ws.pp.g_slot0, ws.pp.g_ntok, ws.pp.g_nt0};
+
+  MMParams p13 = p;
+  if (!mm_planes(a.w13, true, p13)) return BLUT_ERR_UNSUPPORTED;
+  p13.w = (const uint8_t*)a.w13_tiled;
+  p13.wstride = a.w13_stride;
+  p13.bin = ws.xf;
+  p13.act_out = ws.af;
+  p13.out_nchunks = a.inter / kChunk;
+  cudaEvent_t* ev = a.prof_events ? (cudaEvent_t*)a.prof_events : nullptr;
+  if (ev) cudaEventRecord(ev[0], stream);
+  if (launch_lut_mm(a.w13, true, p13, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  if (ev) cudaEventRecord(ev[1], stream);
+
+  MMParams pS13 = p;
+  if (sh) {
+    pS13.gt = GroupTab{ws.pp.meta + 2, ws.pp.sg_expert, ws.pp.sg_slot0, ws.pp.sg_ntok, ws.pp.sg_nt0};
+    if (!mm_planes(a.s13, true, pS13)) return BLUT_ERR_UNSUPPORTED;
+    pS13.w = (const uint8_t*)a.s13_tiled;
+    pS13.wstride = 0;
+    pS13.bin = ws.xfs;
+    pS13.act_out = ws.afs;
+    pS13.out_nchunks = a.shared_inter / kChunk;
+    if (launch_lut_mm(a.s13, true, pS13, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  }
+
+  MMParams p2 = p;
+  if (!mm_planes(a.w2, false, p2)) return BLUT_ERR_UNSUPPORTED;
+  p2.w = (const uint8_t*)a.w2_tiled;
+  p2.wstride = a.w2_stride;
+  p2.bin = ws.af;
+  p2.y_out = ws.y;
+  p2.y_ld = H;
+  if (ev) cudaEventRecord(ev[2], stream);
+  if (launch_lut_mm(a.w2, false, p2, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  if (ev) cudaEventRecord(ev[3], stream);
+
+  if (sh) {
+    MMParams pS2 = pS13;
+    if (!mm_planes(a.s2, false, pS2)) return BLUT_ERR_UNSUPPORTED;
+    pS2.w = (const uint8_t*)a.s2_tiled;
+    pS2.wstride = 0;
+    pS2.bin = ws.afs;
+    pS2.act_out = nullptr;
+    pS2.y_out = ws.ys;
+    pS2.y_ld = H;
+    if (launch_lut_mm(a.s2, false, pS2, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  }
+
+  // 6. combine
+  const int smode = sh ? a.shared_gate_mode : -1;
+  if (bf16)
+    combine_kernel<true><<<T, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode,
+                                                (uint16_t*)a.out);
+  else
+    combine_kernel<false><<<T, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode,
+                                                 (uint16_t*)a.out);
+  err = cudaGetLastError();
+  return err == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
+}
+
+int moe_launch_count(const blut_moe_args& a) {
+  const bool sh = a.shared_inter > 0;
+  int n = 0;
+  if (!a.topk_ids) ++n;                                                       // router
+  if (sh && a.shared_gate_mode == 1 && !(!a.topk_ids && !a.shared_gate_w)) ++n; // gate-only
+  n += 2;                                                                     // plan, gather
+  n += 2;                                                                     // routed gate/up, down
+  if (sh) n += 2;                                                             // shared gate/up, down
+  n += 1;                                                                     // combine
+  return n;
+}
+
+int router(const void* x, const void* w, int T, int H, int E, int K, int renorm, int has_sg, int dtype,
+           int32_t* ids, float* tw, float* sg, cudaStream_t stream) {
+  if (!x || !w || !ids || !tw || T <= 0 || H <= 0 || E <= 0 || K <= 0 || K > 32 || K > E) return BLUT_ERR_INVALID;
+  if (H % 8 || (has_sg && !sg)) return BLUT_ERR_INVALID;
+  if (E > kMaxExperts) return BLUT_ERR_UNSUPPORTED;
+  const size_t smem = (E + 1) * sizeof(float);
+  if (dtype == BLUT_BF16)
+    router_kernel<true><<<T, 256, smem, stream>>>((const uint16_t*)x, (const uint16_t*)w, H, E, K, renorm, has_sg, 1,
+                                                    ids, tw, sg);
+  else if (dtype == BLUT_F16)
+    router_kernel<false><<<T, 256, smem, stream>>>((const uint16_t*)x, (const uint16_t*)w, H, E, K, renorm, has_sg, 1,
+                                                     ids, tw, sg);
+  else
+    return BLUT_ERR_INVALID;
+  return cudaGetLastError() == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
+}
+
+}  // namespace blut

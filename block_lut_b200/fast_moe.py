@@ -1,0 +1,51 @@
+"""``fused_lut_moe``, the reference's ``vllm_lut/fast_moe.py`` entry point.
+
+Same arguments as the reference (fast_moe.py:30-80): reference-format
+(uint8 index, bf16 absmax, bf16[256] codebook) expert stacks plus the
+router's ``topk_ids`` / ``topk_weights``.  Instead of a Python loop over the
+unique experts (one GEMV launch and host sync per expert), every active
+(token, expert) pair runs in one ``blut_moe_forward`` call.  The first call
+on a weight stack repacks it into the tiled layout and caches it (keyed by
+the tensors' storage and version, like the reference's id-keyed cache).
+"""
+from __future__ import annotations
+
+import torch
+
+from .formats import LUTFormat, QuantizedMatrix
+from .moe import LUTExperts, LUTMoELayer
+
+_CACHE: dict = {}
+
+
+def _key(*ts):
+    return tuple((t.data_ptr(), tuple(t.shape), t._version) for t in ts)
+
+
+def r8_layer(w13_weight, w13_absmax, w2_weight, w2_absmax, codebook, top_k: int, tier: int = 0) -> LUTMoELayer:
+    """Tiled ``LUTMoELayer`` for reference-format stacks (cached)."""
+    key = _key(w13_weight, w13_absmax, w2_weight, w2_absmax, codebook) + (top_k, tier)
+    layer = _CACHE.get(key)
+    if layer is None:
+        if len(_CACHE) > 64:
+            _CACHE.clear()
+        fmt = LUTFormat("r8", 8, 128, tier)
+        e_n, two_i, h = w13_weight.shape
+        cb = codebook.to(device=w13_weight.device, dtype=torch.bfloat16).contiguous()
+        w13 = QuantizedMatrix(fmt, two_i, h, w13_weight.reshape(e_n, -1), cb,
+                              scales=w13_absmax.to(torch.bfloat16).reshape(e_n, -1))
+        w2 = QuantizedMatrix(fmt, w2_weight.shape[1], w2_weight.shape[2], w2_weight.reshape(e_n, -1), cb,
+                             scales=w2_absmax.to(torch.bfloat16).reshape(e_n, -1))
+        experts = LUTExperts.from_quantized([w13.expert(e) for e in range(e_n)],
+                                            [w2.expert(e) for e in range(e_n)], cb)
+        layer = LUTMoELayer(experts, top_k)
+        _CACHE[key] = layer
+    return layer
+
+
+def fused_lut_moe(x, topk_ids, topk_weights, w13_weight, w13_absmax, w2_weight, w2_absmax, codebook):
+    """[T, H] (or [H]) activations -> [T, H] MoE output (reference-format experts)."""
+    x2 = x.reshape(1, -1) if x.dim() == 1 else x
+    ids = topk_ids.reshape(x2.shape[0], -1)
+    layer = r8_layer(w13_weight, w13_absmax, w2_weight, w2_absmax, codebook, ids.shape[1])
+    return layer.forward(x2, ids, topk_weights.reshape(ids.shape))

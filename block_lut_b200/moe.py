@@ -1,0 +1,206 @@
+"""One MoE layer of LUT-quantised routed experts (+ optional shared expert).
+
+``LUTMoELayer.forward`` is a single call into ``blut_moe_forward`` (router or
+caller routing -> plan -> B-fragment gather -> gate/up + SiLU*up -> down ->
+weighted combine), all stream-ordered on the caller's stream with a
+caller-owned workspace, so it can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from .formats import LUTFormat, QuantizedMatrix, dense_matrix, pack_tiled
+
+
+@dataclass
+class LUTExperts:
+    """E routed experts of one layer, tiled: w13 [E][2I, H] and w2 [E][H, I]."""
+    fmt: LUTFormat
+    num_experts: int
+    hidden: int
+    inter: int
+    w13: torch.Tensor
+    w13_stride: int
+    w2: torch.Tensor
+    w2_stride: int
+    lut_table: Optional[torch.Tensor] = None  # r8: bf16 [256] tier table
+
+    @classmethod
+    def from_quantized(cls, w13: Sequence[QuantizedMatrix], w2: Sequence[QuantizedMatrix],
+                       lut_table: Optional[torch.Tensor] = None, stream=None) -> "LUTExperts":
+        w13, w2 = list(w13), list(w2)
+        fmt = w13[0].fmt
+        b13, s13 = pack_tiled(w13, stream)
+        b2, s2 = pack_tiled(w2, stream)
+        if fmt.kind == "r8":
+            if lut_table is None:
+                lut_table = w13[0].tables
+            lut_table = lut_table.to(device=b13.device, dtype=torch.bfloat16).contiguous()
+        return cls(fmt, len(w13), w13[0].cols, w13[0].rows // 2, b13, s13, b2, s2, lut_table)
+
+    def weight_bytes(self, experts: int = 1) -> float:
+        """Bytes streamed for ``experts`` experts (gate/up/down), per the format."""
+        return experts * 3 * self.inter * self.hidden * self.fmt.bytes_per_weight()
+
+
+@dataclass
+class SharedExpert:
+    """Dense shared expert: s13 [2 I_s, H], s2 [H, I_s] tiled, optional gate vector [H]."""
+    inter: int
+    s13: torch.Tensor
+    s2: torch.Tensor
+    desc13: _lib.MatDesc
+    desc2: _lib.MatDesc
+    gate: Optional[torch.Tensor] = None
+
+    @classmethod
+    def from_dense(cls, w13: torch.Tensor, w2: torch.Tensor, gate: Optional[torch.Tensor] = None,
+                   stream=None) -> "SharedExpert":
+        m13, m2 = dense_matrix(w13), dense_matrix(w2)
+        b13, _ = pack_tiled([m13], stream)
+        b2, _ = pack_tiled([m2], stream)
+        g = None if gate is None else gate.reshape(-1).to(w13.dtype).contiguous()
+        return cls(w13.shape[0] // 2, b13, b2, m13.fmt.desc(*w13.shape), m2.fmt.desc(*w2.shape), g)
+
+    def weight_bytes(self) -> float:
+        """Bytes of the dense shared expert (gate, up and down, 2 bytes per weight)."""
+        return 2.0 * (self.desc13.rows * self.desc13.cols + self.desc2.rows * self.desc2.cols)
+
+
+_WS: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Grow-only workspace per device (layers run in stream order and share it)."""
+    key = (device.type, device.index)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+class LUTMoELayer:
+    """Routed LUT experts of one layer, optionally with a router and a shared expert.
+
+    ``router_w``: [E (+1)] x H gate weights; when the shared expert is gated by
+    ``sigmoid(x . g)`` and no separate gate vector is given, row E of
+    ``router_w`` is that gate (the Qwen2-MoE ``shared_expert_gate``).
+    """
+
+    def __init__(self, experts: LUTExperts, top_k: int, router_w: Optional[torch.Tensor] = None,
+                 renorm: bool = False, shared: Optional[SharedExpert] = None, shared_gate_mode: int = 1):
+        self.experts = experts
+        self.top_k = int(top_k)
+        self.router_w = None if router_w is None else router_w.to(experts.fmt.compute_dtype).contiguous()
+        self.renorm = bool(renorm)
+        self.shared = shared
+        self.shared_gate_mode = int(shared_gate_mode)
+        self.dtype = experts.fmt.compute_dtype
+        self._args = self._make_args()
+
+    def _make_args(self) -> _lib.MoEArgs:
+        ex = self.experts
+        a = _lib.MoEArgs()
+        a.hidden, a.inter, a.num_experts, a.top_k = ex.hidden, ex.inter, ex.num_experts, self.top_k
+        a.dtype = _lib.BF16 if self.dtype == torch.bfloat16 else _lib.F16
+        a.w13 = ex.fmt.desc(2 * ex.inter, ex.hidden)
+        a.w2 = ex.fmt.desc(ex.hidden, ex.inter)
+        a.w13_tiled, a.w2_tiled = ex.w13.data_ptr(), ex.w2.data_ptr()
+        a.w13_stride, a.w2_stride = ex.w13_stride, ex.w2_stride
+        a.lut_table = None if ex.lut_table is None else ex.lut_table.data_ptr()
+        a.router_w = None if self.router_w is None else self.router_w.data_ptr()
+        a.renorm = int(self.renorm)
+        if self.shared is not None:
+            sh = self.shared
+            a.shared_inter = sh.inter
+            a.shared_gate_mode = self.shared_gate_mode
+            a.s13, a.s2 = sh.desc13, sh.desc2
+            a.s13_tiled, a.s2_tiled = sh.s13.data_ptr(), sh.s2.data_ptr()
+            a.shared_gate_w = None if sh.gate is None else sh.gate.data_ptr()
+        return a
+
+    def launch_count(self, num_tokens: int, caller_routing: bool) -> int:
+        """Kernel launches one forward issues (the count only tests pointers for NULL)."""
+        a = _lib.MoEArgs.from_buffer_copy(self._args)
+        a.num_tokens = num_tokens
+        a.topk_ids = 1 if caller_routing else None
+        return int(_lib.lib().blut_moe_launch_count(C.byref(a)))
+
+    def forward(self, x: torch.Tensor, topk_ids: Optional[torch.Tensor] = None,
+                topk_weights: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                stream=None) -> torch.Tensor:
+        """out[t] = sum_j w[t,j] * expert_{ids[t,j]}(x_t) (+ shared(x_t)); x [T, H]."""
+        if not x.is_cuda:
+            raise ValueError("LUTMoELayer.forward expects CUDA tensors (no CPU path)")
+        in_dtype = x.dtype
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.dtype != self.dtype:
+            x2 = x2.to(self.dtype)
+        x2 = x2.contiguous()
+        T = x2.shape[0]
+        a = self._args
+        a.num_tokens = T
+        a.x = x2.data_ptr()
+        keep = [x2]
+        if topk_ids is not None:
+            ids = topk_ids.reshape(T, -1)
+            if ids.dtype != torch.int32:
+                ids = ids.to(torch.int32)
+            tw = topk_weights.reshape(T, -1)
+            if tw.dtype != torch.float32:
+                tw = tw.to(torch.float32)
+            ids, tw = ids.contiguous(), tw.contiguous()
+            keep += [ids, tw]
+            a.topk_ids, a.topk_weights = ids.data_ptr(), tw.data_ptr()
+        else:
+            if self.router_w is None:
+                raise ValueError("no routing given and the layer has no router weights")
+            a.topk_ids = a.topk_weights = None
+        if out is None or out.dtype != self.dtype:
+            res = torch.empty(T, x2.shape[1], dtype=self.dtype, device=x2.device)
+        else:
+            res = out.reshape(T, -1)
+        a.out = res.data_ptr()
+        lib = _lib.lib()
+        need = lib.blut_moe_workspace_size(C.byref(a))
+        if need == 0:
+            raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
+        ws = workspace(x2.device, need)
+        _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
+                   "moe_forward")
+        if out is not None and res.data_ptr() != out.data_ptr():
+            out.copy_(res.reshape(out.shape))
+            return out
+        res = res.reshape(x.shape)
+        return res if in_dtype == self.dtype else res.to(in_dtype)
+
+    __call__ = forward
+
+    def check_status(self, stream=None) -> None:
+        """Synchronise and raise if a kernel reported a device-side error."""
+        ws = _WS.get((self.experts.w13.device.type, self.experts.w13.device.index))
+        if ws is not None:
+            _lib.check(_lib.lib().blut_moe_check_status(ws.data_ptr(), _lib.stream_ptr(stream)), "device status")
+
+
+def router(x: torch.Tensor, w_router: torch.Tensor, top_k: int, renorm: bool = False,
+           shared_gate: bool = False, stream=None):
+    """Fused router on the GPU: (topk_ids int32 [T,k], topk_weights f32 [T,k], gate f32 [T] | None)."""
+    x = x.contiguous()
+    w = w_router.to(x.dtype).contiguous()
+    T, H = x.shape
+    E = w.shape[0] - (1 if shared_gate else 0)
+    ids = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+    tw = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+    sg = torch.empty(T, dtype=torch.float32, device=x.device) if shared_gate else None
+    dt = _lib.BF16 if x.dtype == torch.bfloat16 else _lib.F16
+    _lib.check(_lib.lib().blut_router(x.data_ptr(), w.data_ptr(), T, H, E, top_k, int(renorm), int(shared_gate), dt,
+                                      ids.data_ptr(), tw.data_ptr(), None if sg is None else sg.data_ptr(),
+                                      _lib.stream_ptr(stream)), "router")
+    return ids, tw, sg

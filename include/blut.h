@@ -1,0 +1,240 @@
+/*
+ * blut.h -- C ABI of libblut.so, the B200 (sm_100a) LUT-dequantised MoE
+ * expert forward of block_lut.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream, never allocates,
+ * never synchronises the device and returns an int status (0 = ok, < 0 =
+ * error, see blut_status_string).  No C++ exceptions cross this boundary.
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths inside the hu-jinzhao/block_lut project).
+ */
+#ifndef BLUT_H_
+#define BLUT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BLUT_API __attribute__((visibility("default")))
+#else
+#define BLUT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status -- */
+enum {
+  BLUT_OK = 0,
+  BLUT_ERR_INVALID = -1,     /* null pointer, bad size or misaligned buffer   */
+  BLUT_ERR_UNSUPPORTED = -2, /* format / shape combination not implemented    */
+  BLUT_ERR_WORKSPACE = -3,   /* caller workspace smaller than required        */
+  BLUT_ERR_LAUNCH = -4,      /* a kernel launch failed                        */
+  BLUT_ERR_TIMEOUT = -5,     /* a device-side wait gave up (device status)    */
+  BLUT_ERR_CUDA = -6         /* another CUDA runtime error                    */
+};
+
+/* Human-readable text of a status code (static storage). */
+BLUT_API const char* blut_status_string(int status);
+
+/* ---------------------------------------------------------------- formats -- */
+enum {
+  BLUT_FMT_R8 = 1,     /* reference BlockLUT: uint8 index per weight, one global
+                          256-entry bf16 table, bf16 absmax per `group` flat
+                          elements (vllm_lut/quant_method.py:117-163)            */
+  BLUT_FMT_B = 2,      /* packed b-bit codes (b = 2, 3, 4), one sorted fp16
+                          table of 2^b entries per (row, block of `group` along K) */
+  BLUT_FMT_NESTED = 3, /* NestedLUT 2+2: 2-bit coarse code into a 4-entry fp16
+                          table per block plus a 2-bit residual code into a 4x4
+                          refinement table; w = fp16(coarse[c] + refine[c][r])   */
+  BLUT_FMT_DENSE = 4   /* plain fp16 / bf16 weights (shared expert)             */
+};
+
+enum { BLUT_F16 = 0, BLUT_BF16 = 1, BLUT_F32 = 2 };
+
+/* Description of one weight matrix W [rows, cols] (y = W x, cols = K). */
+typedef struct {
+  int32_t format; /* BLUT_FMT_*                                                  */
+  int32_t bits;   /* FMT_B: 2, 3, 4.  FMT_R8: 8.  FMT_NESTED: 4.  DENSE: 16      */
+  int32_t group;  /* FMT_B / NESTED: table block along K (32, 64, 128).
+                     FMT_R8: absmax block in flat elements (the reference: 128)  */
+  int32_t tier;   /* FMT_R8: 0 full table (idx), 1 mapped64 (idx & 0x3F),
+                     2 mapped16 (idx & 0x0F) -- runtime/model_offload.py:751-758.
+                     FMT_NESTED: 0 full (coarse + residual), 1 coarse only       */
+  int32_t dtype;  /* compute dtype of weights and activations: BLUT_F16 / BF16.
+                     FMT_R8 computes in bf16, FMT_B / NESTED in fp16             */
+  int32_t reserved;
+  int64_t rows;   /* N: output features                                        */
+  int64_t cols;   /* K: input features                                         */
+} blut_mat_desc;
+
+/* Canonical (checkpoint) layout of one matrix.  Unused pointers are NULL.
+ *  FMT_R8    codes  u8   [rows*cols] (row-major, as the reference's uint8 params)
+ *            tables bf16 [256]       (the tier's 256-entry table)
+ *            scales bf16 [ceil(rows*cols/group)] (flat absmax blocks)
+ *  FMT_B     codes  u8   [rows][cols*bits/8]: element k at bits [k*b, k*b+b)
+ *                        of the row's little-endian bit stream (element 0 in
+ *                        the low bits, as the reference's bit-plane packing)
+ *            tables f16  [rows][cols/group][2^bits] (sorted)
+ *  FMT_NESTED codes u8   [rows][cols/4] coarse codes (2-bit stream)
+ *            codes2 u8   [rows][cols/4] residual codes (2-bit stream)
+ *            tables f16  [rows][cols/group][4]  coarse tables
+ *            tables2 f16 [rows][cols/group][16] refinement tables (refine[c*4+r])
+ *  FMT_DENSE codes  f16/bf16 [rows][cols]                                     */
+typedef struct {
+  const void* codes;
+  const void* codes2;
+  const void* tables;
+  const void* tables2;
+  const void* scales;
+} blut_canon;
+
+/* ------------------------------------------------------------ dequantise -- */
+
+/* Dequantise one matrix from the canonical layout into out [rows][cols]
+ * (bf16 for FMT_R8, fp16 for FMT_B / NESTED).  Bit-exact pure table lookup:
+ *   R8:     bf16(f32(table[tier(idx)]) * f32(absmax[min(i / group, nb - 1)]))
+ *   B:      tables[row][k / group][code]
+ *   NESTED: fp16(f32(coarse[c]) + f32(refine[c][r]))  (or coarse[c], tier 1)
+ * Replaces vllm_lut/quantizer.py:449-477 (decompress_blocklut),
+ * vllm_lut/quant_method.py:281-308 (_decompress_one / _batch_decompress). */
+BLUT_API int blut_dequant(const blut_mat_desc* desc, const blut_canon* src, void* out, void* stream);
+
+/* Reference-shaped BlockLUT decompress: out[i] = bf16(cb[idx[i]] * absmax[i / block_size]).
+ * Replaces launch_blocklut_decompress (vllm_lut/cuda/lut_decompress_kernel.cu:125-154)
+ * and lut_moe_launch_blocklut_recover (csrc/kernels/tensor_recover.hpp:31-38),
+ * without their device synchronisation. */
+BLUT_API int blut_blocklut_decompress(void* out_bf16, const void* idx_u8, const void* absmax_bf16,
+                             const void* codebook_bf16, int64_t n, int32_t block_size,
+                             void* stream);
+
+/* Batched per-expert decompress with per-expert absmax blocks.
+ * Replaces launch_batch_blocklut_decompress (lut_decompress_kernel.cu:156-180),
+ * which is limited to 1024 elements per expert; this one is not. */
+BLUT_API int blut_batch_blocklut_decompress(void* out_bf16, const void* idx_u8, const void* absmax_bf16,
+                                   const void* codebook_bf16, int64_t num_experts,
+                                   int64_t elements_per_expert, int64_t blocks_per_expert,
+                                   int32_t block_size, void* stream);
+
+/* Plain LUT recover out[i] = lut[idx[i]] (no scale).
+ * Replaces lut_moe_launch_lut_recover (csrc/kernels/tensor_recover.hpp:23-29). */
+BLUT_API int blut_lut_recover(void* out_u16, const void* idx_u8, const void* lut_u16, int64_t n, void* stream);
+
+/* ------------------------------------------------------- tiled layout ---- */
+
+/* Bytes of the tiled device layout of one matrix (16-row tiles x 128-column
+ * chunks, codes and tables in MMA-fragment order, 256-byte aligned).  The
+ * layout needs rows % 16 == 0 and cols % 128 == 0; returns < 0 otherwise. */
+BLUT_API int64_t blut_tiled_bytes(const blut_mat_desc* desc);
+
+/* Repack one matrix from the canonical layout into the tiled layout
+ * (load time; the tiled buffer is what blut_moe_forward streams). */
+BLUT_API int blut_pack_tiled(const blut_mat_desc* desc, const blut_canon* src, void* tiled, void* stream);
+
+/* ---------------------------------------------------------------- encode -- */
+
+/* Format B / NestedLUT encoder: per (row, block) 1-D Lloyd k-means (10
+ * iterations, uniform-grid initialisation, float32 means), fp16 sorted
+ * tables, nearest-entry codes; bit-identical to the CPU restatement.
+ * w: f32 [rows][cols]; writes the canonical layout (codes, tables[, codes2,
+ * tables2]).  New format: the reference's per-block Lloyd is
+ * vllm_lut/quantizer.py:120-178, its assignment quantizer.py:292-296. */
+BLUT_API int blut_encode(const blut_mat_desc* desc, const float* w, void* codes, void* tables,
+                void* codes2, void* tables2, void* stream);
+
+/* Reference BlockLUT encoder on bf16 input (block absmax, bf16 normalisation,
+ * first-index argmin over the 256-entry table).  Bit-exact with
+ * LUTQuantizer.quantize (vllm_lut/quantizer.py:243-306); replaces the GPU
+ * encoder encode_blocklut_kernel (vllm_lut/fast_encode.py:22-102). */
+BLUT_API int blut_encode_r(const void* w_bf16, int64_t n, const void* codebook_bf16, int32_t block_size,
+                  void* idx_u8, void* absmax_bf16, void* stream);
+
+/* ------------------------------------------------------------------ GEMV -- */
+
+/* Fused Format-R LUT-dequant GEMV on the canonical layout (one token):
+ *   y[r] = sum_c x[c] * cb[idx[r, c]] * absmax[min((r*K + c) / 128, nb - 1)]
+ * fp32 accumulation, bf16 in/out.  Replaces lut_gemv
+ * (vllm_lut/cuda_lut_gemv.py:23-81,153-169) without its per-call device
+ * synchronisation. */
+BLUT_API int blut_lut_gemv(const void* x_bf16, const void* idx_u8, const void* codebook_bf16,
+                  const void* absmax_bf16, void* y_bf16, int64_t m, int64_t k, int64_t num_blocks,
+                  void* stream);
+
+/* ---------------------------------------------------------------- router -- */
+
+/* Fused router: logits = x W_r^T (fp32 accumulation), softmax (fp32), top-k
+ * (descending, lowest expert index on ties), optional renormalisation, and,
+ * when has_shared_gate, sigmoid(x . W_r[num_experts]) for the shared expert.
+ * x [T][hidden], w_router [num_experts (+1)][hidden] in `dtype`.
+ * Replaces vllm_lut/moe_layer.py:358-376 (_routing) and
+ * customized/qwen.py:44-54,99. */
+BLUT_API int blut_router(const void* x, const void* w_router, int32_t num_tokens, int32_t hidden,
+                int32_t num_experts, int32_t top_k, int32_t renorm, int32_t has_shared_gate,
+                int32_t dtype, int32_t* topk_ids, float* topk_weights, float* shared_gate,
+                void* stream);
+
+/* ------------------------------------------------------------------- MoE -- */
+
+typedef struct {
+  int32_t num_tokens;  /* T                                                     */
+  int32_t hidden;      /* H                                                     */
+  int32_t inter;       /* I (per routed expert)                                 */
+  int32_t num_experts; /* E                                                     */
+  int32_t top_k;       /* k                                                     */
+  int32_t dtype;       /* activation / output dtype: BLUT_F16 or BLUT_BF16      */
+  blut_mat_desc w13;   /* per expert [2I, H]: rows 0..I-1 gate, I..2I-1 up      */
+  blut_mat_desc w2;    /* per expert [H, I]                                     */
+  const void* w13_tiled;  /* E matrices in the tiled layout, stride below       */
+  const void* w2_tiled;
+  int64_t w13_stride;     /* bytes between experts (>= blut_tiled_bytes(&w13))  */
+  int64_t w2_stride;
+  const void* lut_table;  /* FMT_R8: bf16 [256] tier table; NULL otherwise      */
+  const void* x;          /* [T][H]                                             */
+  const int32_t* topk_ids;  /* [T][k]; NULL: route with router_w               */
+  const float* topk_weights;/* [T][k]                                           */
+  const void* router_w;     /* [E (+1 with shared gate)][H], used when topk_ids==NULL */
+  int32_t renorm;           /* renormalise the top-k weights (router only)     */
+  int32_t shared_inter;     /* I_s of the shared expert; 0 = none              */
+  int32_t shared_gate_mode; /* 0: shared output added unscaled; 1: scaled by
+                               sigmoid(x . g_s), g_s = shared_gate_w or router row E */
+  int32_t reserved;
+  blut_mat_desc s13;        /* shared expert [2 I_s, H]                         */
+  blut_mat_desc s2;         /* shared expert [H, I_s]                           */
+  const void* s13_tiled;
+  const void* s2_tiled;
+  const void* shared_gate_w;/* [H] or NULL (then router row E when routing)   */
+  void* out;                /* [T][H]                                           */
+  void* const* prof_events; /* NULL, or 4 cudaEvent_t recorded on the stream
+                               before/after the routed gate/up launch and
+                               before/after the routed down launch (timing)   */
+} blut_moe_args;
+
+/* Workspace bytes blut_moe_forward needs for these arguments (0 on error). */
+BLUT_API size_t blut_moe_workspace_size(const blut_moe_args* args);
+
+/* One MoE layer of routed LUT experts (+ optional shared expert):
+ *   out[t] = sum_j w[t,j] * W2_e(silu(W1_e x_t) * W3_e x_t)  (+ g_t * shared(x_t))
+ * with e = topk_ids[t, j]; every active (token, expert) pair of the layer runs
+ * in one launch per stage (router, plan, gate/up+SiLU*up, down, combine).
+ * Replaces LUTFusedMoEMethod.apply (vllm_lut/quant_method.py:230-279) and
+ * fused_lut_moe (vllm_lut/fast_moe.py:30-80).  Decode regime: T*k <= 2048. */
+BLUT_API int blut_moe_forward(const blut_moe_args* args, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Read (and clear) the device-side status word of a workspace last used by
+ * blut_moe_forward on `stream`: synchronises the stream, returns BLUT_OK or
+ * BLUT_ERR_TIMEOUT when a kernel's bounded wait gave up.  Diagnostic only. */
+BLUT_API int blut_moe_check_status(void* workspace, void* stream);
+
+/* Number of this library's kernel launches one blut_moe_forward issues for
+ * these arguments (used to report launch counts). */
+BLUT_API int blut_moe_launch_count(const blut_moe_args* args);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BLUT_H_ */

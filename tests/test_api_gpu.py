@@ -1,0 +1,144 @@
+"""The reference-facing operator API on the GPU: LUTFusedMoEMethod (vLLM plugin),
+fused_lut_moe, lut_gemv, DeepseekV2MoE_LUT and the fused router."""
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import blut_oracle as O
+from tests._helpers import bf16_tensor, check_layer, cuda, routing_inputs
+from tests.golden.make_golden import small_layer_indices
+
+from block_lut_b200.cuda_lut_gemv import lut_gemv
+from block_lut_b200.fast_moe import fused_lut_moe
+from block_lut_b200.moe import router
+
+pytestmark = pytest.mark.gpu
+
+
+def _small_r8_layer(golden):
+    s = golden("apply_small.npz")
+    w13, w2 = small_layer_indices(int(s["idx_seed"]), 8, 256, 128)
+    layer = SimpleNamespace(w13_weight=cuda(w13), w2_weight=cuda(w2), w13_absmax=bf16_tensor(s["a13"]),
+                            w2_absmax=bf16_tensor(s["a2"]), _codebook=bf16_tensor(s["table"]))
+    return s, layer
+
+
+def test_quant_method_apply_matches_reference_golden(golden):
+    from block_lut_b200.quant_method import LUTConfig, LUTFusedMoEMethod
+    s, layer = _small_r8_layer(golden)
+    method = LUTFusedMoEMethod(LUTConfig(code_type="BLOCKLUT"))
+    for T in (2, 8):
+        out = method.apply(layer, bf16_tensor(s[f"x{T}"]), bf16_tensor(s[f"tw{T}"]), cuda(s[f"ti{T}"]).long())
+        assert out.dtype == torch.bfloat16 and out.shape == (T, 256)
+        ref = O.bf16_to_f32(s[f"out{T}"])
+        o = out.float().cpu().numpy()
+        assert np.abs(o - ref).max() <= 2e-3 and O.rel_l2(o, ref) <= 1e-2
+        # same call through fused_lut_moe (fast_moe.py:30) gives the same bits
+        f = fused_lut_moe(bf16_tensor(s[f"x{T}"]), cuda(s[f"ti{T}"]), bf16_tensor(s[f"tw{T}"]), layer.w13_weight,
+                          layer.w13_absmax, layer.w2_weight, layer.w2_absmax, layer._codebook)
+        assert torch.equal(f, out)
+
+
+def test_quant_method_create_weights_format_b():
+    from block_lut_b200.formats import LUTFormat, encode
+    from block_lut_b200.quant_method import LUTConfig, LUTFusedMoEMethod
+    cfg = LUTConfig.from_config({"quant_method": "lut", "code_type": "BLOCKLUT", "codebook_scope": "row_block",
+                                 "index_bits": 4, "lut_block": 64})
+    assert cfg.lut_format() == LUTFormat("b", 4, 64)
+    method = LUTFusedMoEMethod(cfg)
+    layer = torch.nn.Module()
+    E, H, I = 3, 256, 128
+    method.create_weights(layer, E, H, I, torch.float16)
+    assert layer.w13_weight.shape == (E, 2 * I, H // 2) and layer.w13_weight.dtype == torch.uint8
+    assert layer.w13_tables.shape == (E, 2 * I, H // 64, 16) and layer.w13_tables.dtype == torch.float16
+    rng = np.random.Generator(np.random.PCG64(4))
+    W13, W2 = [], []
+    for e in range(E):
+        a, b = O.student_t_weights(rng, (2 * I, H)), O.student_t_weights(rng, (H, I))
+        qa, qb = encode(cuda(a), cfg.lut_format()), encode(cuda(b), cfg.lut_format())
+        layer.w13_weight.data[e].copy_(qa.codes)
+        layer.w13_tables.data[e].copy_(qa.tables)
+        layer.w2_weight.data[e].copy_(qb.codes)
+        layer.w2_tables.data[e].copy_(qb.tables)
+        W13.append(O.dequant_b(qa.codes.cpu().numpy(), qa.tables.cpu().numpy(), 4, 64).astype(np.float32))
+        W2.append(O.dequant_b(qb.codes.cpu().numpy(), qb.tables.cpu().numpy(), 4, 64).astype(np.float32))
+    method.process_weights_after_loading(layer)
+    x = cuda(O.rms_activations(rng, 5, H).astype(np.float16))
+    ids, tw = routing_inputs(rng, 5, E, 2)
+    out = method.apply(layer, x, cuda(tw), cuda(ids))
+    ref = O.moe_forward(x.float().cpu().numpy(), ids, tw, W13, W2, act_dtype="f16")
+    check_layer(out, ref, torch.float16, "quant_method format b")
+
+
+@pytest.mark.parametrize("m,k", [(2816, 2048), (2048, 1408), (64, 1000)])
+def test_lut_gemv(m, k):
+    rng = np.random.Generator(np.random.PCG64(m + k))
+    idx = rng.integers(0, 256, (m, k), dtype=np.uint8)
+    nb = (m * k + 127) // 128
+    am = O.f32_to_bf16(rng.uniform(0.01, 0.1, nb).astype(np.float32))
+    tab = O.f32_to_bf16(np.sort(rng.uniform(-1, 1, 256)).astype(np.float32))
+    x = O.f32_to_bf16(rng.standard_normal(k).astype(np.float32))
+    y = lut_gemv(bf16_tensor(x), cuda(idx), bf16_tensor(tab), bf16_tensor(am))
+    # cuda_lut_gemv.py:48-58 keeps the fp32 product (no bf16 rounding of the weight)
+    blk = np.minimum(np.arange(m * k) // 128, nb - 1).reshape(m, k)
+    w = O.bf16_to_f32(tab)[idx].astype(np.float64) * O.bf16_to_f32(am)[blk].astype(np.float64)
+    ref = w @ O.bf16_to_f32(x).astype(np.float64)
+    rb = O.round_to(ref.astype(np.float32), "bf16")
+    o = y.float().cpu().numpy()
+    ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(rb), 1e-30))) - 7)
+    assert (np.abs(o - rb) <= ulp).all()
+
+
+def test_router_kernel_against_oracle(golden):
+    rng = np.random.Generator(np.random.PCG64(13))
+    T, H, E, k = 32, 2048, 60, 4
+    x = cuda(O.rms_activations(rng, T, H).astype(np.float16))
+    w = cuda((rng.standard_normal((E + 1, H)) * 0.02).astype(np.float16))
+    ids, tw, sg = router(x, w, k, shared_gate=True)
+    logits = x.float().cpu().numpy().astype(np.float64) @ w.float().cpu().numpy().astype(np.float64).T
+    rids, rtw = O.routing(logits[:, :E], k)
+    srt = np.sort(logits[:, :E], axis=1)
+    keep = srt[:, -k] - srt[:, -k - 1] > 1e-4
+    assert np.array_equal(ids.cpu().numpy()[keep], rids[keep])
+    np.testing.assert_allclose(tw.cpu().numpy()[keep], rtw[keep], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(sg.cpu().numpy(), 1 / (1 + np.exp(-logits[:, E])), rtol=1e-5, atol=1e-6)
+
+
+def test_deepseek_v2_moe_lut_forward():
+    from block_lut_b200.formats import LUTFormat
+    from block_lut_b200.moe_layer import DeepseekV2MoE_LUT, _routing
+    cfg = SimpleNamespace(hidden_size=256, moe_intermediate_size=128, n_routed_experts=6, num_experts_per_tok=2,
+                          n_shared_experts=1, norm_topk_prob=False)
+    lut_cfg = SimpleNamespace(lut_format=lambda: LUTFormat("b", 4, 64))
+    m = DeepseekV2MoE_LUT(cfg, lut_config=lut_cfg)
+    rng = np.random.Generator(np.random.PCG64(6))
+    with torch.no_grad():
+        m.gate.weight.copy_(torch.from_numpy((rng.standard_normal((6, 256)) * 0.1).astype(np.float16)))
+    w13 = torch.from_numpy(O.student_t_weights(rng, (6, 256, 256)))
+    w2 = torch.from_numpy(O.student_t_weights(rng, (6, 256, 128)))
+    sgu = torch.from_numpy(O.student_t_weights(rng, (256, 256))).half()
+    sd = torch.from_numpy(O.student_t_weights(rng, (256, 128))).half()
+    m.quantize_expert_weights(w13, w2, sgu, sd)
+    x = cuda(O.rms_activations(rng, 10, 256).astype(np.float16)).reshape(2, 5, 256)
+    out = m(x)
+    assert out.shape == x.shape
+    # oracle: same encoded weights, the reference's _routing on fp64 logits
+    xn = x.reshape(10, 256).float().cpu().numpy().astype(np.float64)
+    logits = xn @ m.gate.weight.float().cpu().numpy().astype(np.float64).T
+    ids, tw = O.routing(logits, 2)
+    tw_ref, ids_ref = _routing(torch.from_numpy(logits), 2)
+    assert np.array_equal(ids_ref.numpy(), ids)
+    ex = m._moe.experts
+    from block_lut_b200.formats import encode
+    W13 = [O.dequant_b(*[t.cpu().numpy() for t in (q.codes, q.tables)], 4, 64).astype(np.float32)
+           for q in (encode(w13[e].cuda(), LUTFormat("b", 4, 64)) for e in range(6))]
+    W2 = [O.dequant_b(*[t.cpu().numpy() for t in (q.codes, q.tables)], 4, 64).astype(np.float32)
+          for q in (encode(w2[e].cuda(), LUTFormat("b", 4, 64)) for e in range(6))]
+    xs = xn
+    h = xs @ sgu.double().numpy().T
+    a = O.round_to((O.silu(h[:, :128]) * h[:, 128:]).astype(np.float32), "f16").astype(np.float64)
+    ref = O.moe_forward(xn, ids, tw, W13, W2, act_dtype="f16") + a @ sd.double().numpy().T
+    assert ex.num_experts == 6
+    check_layer(out.reshape(10, 256), ref, torch.float16, "DeepseekV2MoE_LUT")

@@ -1,0 +1,164 @@
+"""libblut.so without a GPU: it loads, exports every symbol of include/blut.h,
+and its host-side argument checks answer before any CUDA call."""
+import ctypes as C
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+from tests.conftest import ROOT
+
+from block_lut_b200 import _lib
+from block_lut_b200.formats import LUTFormat, tiled_bytes
+
+HEADER = os.path.join(ROOT, "include", "blut.h")
+
+
+def header_symbols():
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"BLUT_API\s+[\w\s\*]+?\b(blut_\w+)\s*\(", txt)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    declared = header_symbols()
+    assert len(declared) >= 15
+    for name in declared:
+        assert hasattr(lib, name), name
+    # the ctypes table covers exactly the header
+    assert sorted(n for n, _, _ in _lib.SIGNATURES) == declared
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = sorted(set(re.findall(r"\bT (blut_\w+)", out)))
+    assert exported == declared
+
+
+def test_status_strings():
+    for rc in (0, -1, -2, -3, -4, -5, -6):
+        assert _lib.status_string(rc)
+    assert "unknown" in _lib.status_string(-99)
+
+
+@pytest.mark.parametrize("fmt,bpw", [
+    (LUTFormat("b", 4, 64), 1.0), (LUTFormat("b", 2, 64), 0.375), (LUTFormat("b", 3, 64), 0.625),
+    (LUTFormat("b", 4, 32), 1.5), (LUTFormat("b", 2, 128), 0.3125),
+    (LUTFormat("nested", 4, 64, 1), 0.375), (LUTFormat("r8", 8, 128), 1 + 2 / 128),
+])
+def test_tiled_bytes_match_format_bytes(fmt, bpw):
+    rows, cols = 1408, 2048
+    n = tiled_bytes(fmt, rows, cols)
+    assert abs(fmt.bytes_per_weight() - bpw) < 1e-9
+    # the buffer holds every plane (NestedLUT: both tiers, 0.25+0.125+0.25+0.5 B per
+    # weight); planes are 256-aligned, so at most 256 B of padding per plane
+    stored = 1.125 if fmt.kind == "nested" else bpw
+    assert rows * cols * stored <= n <= rows * cols * stored + 4 * 256
+
+
+def test_tiled_bytes_rejects_bad_shapes():
+    with pytest.raises(ValueError):
+        tiled_bytes(LUTFormat("b", 4, 64), 1400, 2048)  # rows % 16
+    with pytest.raises(ValueError):
+        tiled_bytes(LUTFormat("b", 4, 64), 1408, 2000)  # cols % 128
+
+
+def _args(**kw):
+    fmt = LUTFormat("b", 4, 64)
+    a = _lib.MoEArgs()
+    a.num_tokens, a.hidden, a.inter, a.num_experts, a.top_k, a.dtype = 8, 2048, 1408, 60, 4, _lib.F16
+    a.w13, a.w2 = fmt.desc(2816, 2048), fmt.desc(2048, 1408)
+    a.w13_tiled = a.w2_tiled = a.x = a.out = 1 << 20
+    a.w13_stride, a.w2_stride = tiled_bytes(fmt, 2816, 2048), tiled_bytes(fmt, 2048, 1408)
+    a.topk_ids = a.topk_weights = 1 << 21
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_moe_workspace_size_host_only():
+    lib = _lib.lib()
+    n = lib.blut_moe_workspace_size(C.byref(_args()))
+    assert n > 8 * 4 * 2048 * 4  # holds at least the fp32 expert outputs
+    assert lib.blut_moe_workspace_size(C.byref(_args(num_tokens=0))) == 0
+    assert lib.blut_moe_workspace_size(C.byref(_args(hidden=2000))) == 0
+
+
+@pytest.mark.parametrize("kw,rc", [
+    (dict(num_tokens=0), _lib.BLUT_ERR_INVALID),
+    (dict(x=None), _lib.BLUT_ERR_INVALID),
+    (dict(topk_ids=None), _lib.BLUT_ERR_INVALID),  # no routing and no router weights
+    (dict(num_tokens=1024), _lib.BLUT_ERR_UNSUPPORTED),  # T*k beyond the decode path
+    (dict(x=(1 << 20) + 2), _lib.BLUT_ERR_INVALID),  # misaligned activations
+    (dict(w13_stride=1024), _lib.BLUT_ERR_INVALID),
+])
+def test_moe_forward_rejects_bad_arguments_before_launching(kw, rc):
+    lib = _lib.lib()
+    assert lib.blut_moe_forward(C.byref(_args(**kw)), None, 0, None) == rc
+
+
+def test_moe_forward_rejects_small_workspace():
+    lib = _lib.lib()
+    assert lib.blut_moe_forward(C.byref(_args()), 1 << 22, 16, None) == _lib.BLUT_ERR_WORKSPACE
+
+
+def test_launch_count():
+    lib = _lib.lib()
+    assert lib.blut_moe_launch_count(C.byref(_args())) == 5  # plan, gather, gate/up, down, combine
+
+
+LAYOUT_PROBE = r"""
+#include <cstdio>
+#include <set>
+#include "blut_common.cuh"
+using namespace blut;
+// every (row, k) of a (tile, chunk) piece must map to a distinct bit range inside the piece
+template <class F> int check(const char* name, int piece_bytes, int bits, F pos) {
+  std::set<long> used;
+  for (int r = 0; r < 16; ++r)
+    for (int k = 0; k < 128; ++k) {
+      int word, bit;
+      pos(r, k, word, bit);
+      for (int b = 0; b < bits; ++b) {
+        long g = (long)word * 32 + bit + b;
+        if (g < 0 || g >= (long)piece_bytes * 8 || bit + b >= 32 || !used.insert(g).second) {
+          printf("%s: bad position r=%d k=%d\n", name, r, k);
+          return 1;
+        }
+      }
+    }
+  if ((long)used.size() != (long)piece_bytes * 8) { printf("%s: not dense\n", name); return 1; }
+  return 0;
+}
+int main() {
+  int bad = 0;
+  bad |= check("codes4", 1024, 4, codes4_pos);
+  bad |= check("codes2", 512, 2, codes2_pos);
+  bad |= check("codes1", 256, 1, codes1_pos);
+  bad |= check("codes8", 2048, 8, codes8_pos);
+  bad |= check("dense", 4096, 16, [](int r, int k, int& w, int& b) { int o = dense_byte(r, k); w = o / 4; b = 8 * (o % 4); });
+  bad |= check("bfrag", 2048, 16, [](int n, int k, int& w, int& b) { int o = bfrag_byte(n % 8, k); w = o / 4 + (n / 8) * 512; b = 8 * (o % 4); });
+  // fragment ownership: lane (g, t) holds rows g, g+8 and columns {2t, 2t+1, 2t+8, 2t+9} of each slab
+  for (int r = 0; r < 16; ++r) for (int k = 0; k < 128; ++k) {
+    FragPos p = frag_pos(r, k);
+    int kk = k & 15, col = 2 * (p.lane & 3) + (p.q & 1) + 8 * (p.q >> 1);
+    if (p.lane / 4 != (r & 7) || p.h != r / 8 || col != kk || p.s != k / 16) { printf("frag_pos r=%d k=%d\n", r, k); bad = 1; }
+  }
+  printf(bad ? "FAIL\n" : "OK\n");
+  return bad;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which("nvcc") is None and not os.path.exists("/usr/local/cuda/bin/nvcc"),
+                    reason="needs nvcc for the host-side layout probe")
+def test_tiled_layout_position_maps_are_bijective(tmp_path):
+    # dense bfrag check covers 16 tokens (two n-tiles side by side) -> use a 2-tile piece size
+    src = tmp_path / "probe.cu"
+    src.write_text(LAYOUT_PROBE.replace('check("bfrag", 2048', 'check("bfrag", 4096'))
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    exe = tmp_path / "probe"
+    r = subprocess.run([nvcc, "-std=c++17", "-I", os.path.join(ROOT, "block_lut_b200", "csrc"), str(src), "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout

@@ -1,0 +1,140 @@
+"""Bit-exact dequantisation and encoding on the GPU against the oracle and the
+reference's golden vectors."""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import blut_oracle as O
+from tests._helpers import bf16_tensor, cuda, qm_from_numpy, to_u16
+
+from block_lut_b200 import _lib
+from block_lut_b200.formats import LUTFormat, QuantizedMatrix, dequant, encode, encode_r
+from block_lut_b200.quantizer import LUTQuantizer, decompress_blocklut
+
+pytestmark = pytest.mark.gpu
+
+
+def test_decompress_kat_golden(golden):
+    d = golden("dequant_kat.npz")
+    out = decompress_blocklut(cuda(d["idx"]), bf16_tensor(d["absmax"]), bf16_tensor(d["table"]), 128)
+    assert np.array_equal(to_u16(out), d["expected"])
+
+
+def test_quantizer_api_golden(golden):
+    e = golden("encode_r.npz")
+    q = LUTQuantizer("BLOCKLUT", 128)
+    res = q.quantize(bf16_tensor(e["w"]).reshape(96, 384), bf16_tensor(e["table"]))
+    assert np.array_equal(res["indices"].numpy(), e["idx"].reshape(-1))
+    assert np.array_equal(to_u16(res["absmax"]), e["absmax"].reshape(-1))
+    deq = q.decompress(res["indices"], res["absmax"], res["codebook"])
+    assert np.array_equal(to_u16(deq), e["dequant"].reshape(-1))
+
+
+@pytest.mark.parametrize("tier,table", [(1, "mapped64"), (2, "mapped16")])
+def test_r8_tiers_golden(golden, tier, table):
+    t = golden("tiers.npz")
+    n = t["idx"].size
+    qm = QuantizedMatrix(LUTFormat("r8", 8, 128, tier), 1, n, cuda(t["idx"].reshape(-1)), bf16_tensor(t[table]),
+                         scales=bf16_tensor(t["absmax"]))
+    assert np.array_equal(to_u16(dequant(qm)).reshape(-1), t[f"tier{tier}"].reshape(-1))
+
+
+@pytest.mark.parametrize("n,bs", [(1, 128), (15, 128), (16, 128), (4097, 128), (128 * 33, 128), (1000, 64),
+                                  (2048, 32)])
+def test_r8_random_shapes(n, bs):
+    rng = np.random.Generator(np.random.PCG64(n))
+    idx = rng.integers(0, 256, n, dtype=np.uint8)
+    am = O.f32_to_bf16(rng.uniform(0.01, 0.1, (n + bs - 1) // bs).astype(np.float32))
+    tab = O.f32_to_bf16(rng.uniform(-1, 1, 256).astype(np.float32))
+    out = decompress_blocklut(cuda(idx), bf16_tensor(am), bf16_tensor(tab), bs)
+    assert np.array_equal(to_u16(out), O.dequant_r(idx, am, tab, bs))
+
+
+def test_batch_decompress_and_recover():
+    rng = np.random.Generator(np.random.PCG64(3))
+    E, n = 5, 4096 + 16
+    nb = (n + 127) // 128
+    idx = rng.integers(0, 256, (E, n), dtype=np.uint8)
+    am = O.f32_to_bf16(rng.uniform(0.01, 0.1, (E, nb)).astype(np.float32))
+    tab = O.f32_to_bf16(rng.uniform(-1, 1, 256).astype(np.float32))
+    out = torch.empty(E, n, dtype=torch.bfloat16, device="cuda")
+    ti, ta, tt = cuda(idx), bf16_tensor(am), bf16_tensor(tab)
+    _lib.check(_lib.lib().blut_batch_blocklut_decompress(out.data_ptr(), ti.data_ptr(), ta.data_ptr(), tt.data_ptr(),
+                                                         E, n, nb, 128, _lib.stream_ptr()))
+    ref = np.stack([O.dequant_r(idx[e], am[e], tab, 128) for e in range(E)])
+    assert np.array_equal(to_u16(out), ref)
+    rec = torch.empty(E * n, dtype=torch.int16, device="cuda")
+    _lib.check(_lib.lib().blut_lut_recover(rec.data_ptr(), ti.data_ptr(), tt.data_ptr(), E * n, _lib.stream_ptr()))
+    assert np.array_equal(rec.cpu().numpy().view(np.uint16), tab[idx.reshape(-1)])
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_format_b_dequant_bit_exact(bits, group):
+    rng = np.random.Generator(np.random.PCG64(bits * 1000 + group))
+    rows, cols = 48, 384
+    w = O.student_t_weights(rng, (rows, cols))
+    packed, tables = O.encode_b(w, bits, group)
+    fmt = LUTFormat("b", bits, group)
+    qm = qm_from_numpy(fmt, rows, cols, {"codes": packed, "tables": tables})
+    out = dequant(qm).cpu().numpy()
+    assert np.array_equal(out.view(np.uint16), O.dequant_b(packed, tables, bits, group).view(np.uint16))
+
+
+@pytest.mark.parametrize("tier", [0, 1])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_nested_dequant_bit_exact(tier, group):
+    rng = np.random.Generator(np.random.PCG64(77 + group))
+    rows, cols = 32, 256
+    w = O.student_t_weights(rng, (rows, cols))
+    cp, rp, ct, rt = O.encode_nested(w, group)
+    fmt = LUTFormat("nested", 4, group, tier)
+    qm = qm_from_numpy(fmt, rows, cols, {"codes": cp, "codes2": rp, "tables": ct, "tables2": rt})
+    out = dequant(qm).cpu().numpy()
+    ref = O.dequant_nested(cp, rp, ct, rt, group, coarse_only=tier == 1)
+    assert np.array_equal(out.view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_gpu_encoder_bit_identical_to_oracle(bits, group):
+    rng = np.random.Generator(np.random.PCG64(5 + bits + group))
+    rows, cols = 24, 512
+    w = O.student_t_weights(rng, (rows, cols))
+    qm = encode(cuda(w), LUTFormat("b", bits, group))
+    packed, tables = O.encode_b(w, bits, group)
+    assert np.array_equal(qm.tables.cpu().numpy().view(np.uint16), tables.view(np.uint16))
+    assert np.array_equal(qm.codes.cpu().numpy(), packed)
+
+
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_gpu_nested_encoder_bit_identical_to_oracle(group):
+    rng = np.random.Generator(np.random.PCG64(9 + group))
+    rows, cols = 16, 256
+    w = O.student_t_weights(rng, (rows, cols))
+    qm = encode(cuda(w), LUTFormat("nested", 4, group))
+    cp, rp, ct, rt = O.encode_nested(w, group)
+    assert np.array_equal(qm.tables.cpu().numpy().view(np.uint16), ct.view(np.uint16))
+    assert np.array_equal(qm.tables2.cpu().numpy().view(np.uint16), rt.view(np.uint16))
+    assert np.array_equal(qm.codes.cpu().numpy(), cp)
+    assert np.array_equal(qm.codes2.cpu().numpy(), rp)
+
+
+def test_encode_r_padding_tail():
+    rng = np.random.Generator(np.random.PCG64(11))
+    n = 1000  # not a multiple of the block
+    w = O.f32_to_bf16(O.student_t_weights(rng, (n,)))
+    tab = O.f32_to_bf16(np.sort(rng.uniform(-1, 1, 256)).astype(np.float32))
+    idx, am = encode_r(bf16_tensor(w), bf16_tensor(tab), 128)
+    ridx, ram = O.encode_r(w, tab, 128)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    assert np.array_equal(to_u16(am), ram)
+
+
+def test_dequant_rejects_bad_args():
+    fmt = LUTFormat("b", 4, 64)
+    d = fmt.desc(16, 100)  # cols not a multiple of the group
+    c = _lib.Canon(1 << 20, None, 1 << 20, None, None)
+    assert _lib.lib().blut_dequant(C.byref(d), C.byref(c), 1 << 20, None) == _lib.BLUT_ERR_UNSUPPORTED

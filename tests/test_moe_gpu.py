@@ -1,0 +1,219 @@
+"""MoE layer parity: blut_moe_forward against the float64 oracle on the same
+quantised weights and routing (tolerance in tests/_helpers.check_layer)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import blut_oracle as O
+from tests._helpers import (bf16_tensor, build_b_layer, build_r8_layer, check_layer, cuda, routing_inputs)
+from tests.golden.make_golden import qwen_layer_weights, small_layer_indices
+
+from block_lut_b200.formats import LUTFormat, QuantizedMatrix, encode
+from block_lut_b200.moe import LUTExperts, LUTMoELayer, SharedExpert
+
+pytestmark = pytest.mark.gpu
+
+FORMATS = [LUTFormat("b", 4, 64), LUTFormat("b", 4, 32), LUTFormat("b", 4, 128), LUTFormat("b", 3, 64),
+           LUTFormat("b", 2, 64), LUTFormat("b", 2, 128), LUTFormat("nested", 4, 64, 0),
+           LUTFormat("nested", 4, 64, 1)]
+
+
+@pytest.fixture(scope="module", params=FORMATS, ids=lambda f: f"{f.kind}{f.bits}g{f.group}t{f.tier}")
+def b_layer(request):
+    return request.param, build_b_layer(request.param, E=6, H=256, I=256, seed=1)
+
+
+@pytest.mark.parametrize("T,k", [(1, 2), (3, 2), (8, 2), (16, 3), (80, 2)])
+def test_format_b_layer(b_layer, T, k):
+    fmt, (experts, W13, W2) = b_layer
+    rng = np.random.Generator(np.random.PCG64(T * 31 + k))
+    x = O.rms_activations(rng, T, 256)
+    ids, tw = routing_inputs(rng, T, 6, k)
+    layer = LUTMoELayer(experts, k)
+    xh = cuda(x.astype(np.float16))
+    out = layer.forward(xh, cuda(ids), cuda(tw))
+    ref = O.moe_forward(xh.float().cpu().numpy(), ids, tw, W13, W2, act_dtype="f16")
+    check_layer(out, ref, torch.float16, f"{fmt} T={T}")
+    layer.check_status()
+
+
+def test_r8_layer_and_tiers():
+    for tier in (0, 1, 2):
+        experts, W13, W2, _ = build_r8_layer(5, 256, 384, seed=tier, tier=tier)
+        rng = np.random.Generator(np.random.PCG64(4 + tier))
+        for T in (1, 8, 24):
+            x = O.rms_activations(rng, T, 256)
+            ids, tw = routing_inputs(rng, T, 5, 2)
+            xb = cuda(O.f32_to_bf16(x)).view(torch.bfloat16)
+            out = LUTMoELayer(experts, 2).forward(xb, cuda(ids), cuda(tw))
+            ref = O.moe_forward(xb.float().cpu().numpy(), ids, tw, W13, W2, act_dtype="bf16")
+            check_layer(out, ref, torch.bfloat16, f"r8 tier {tier} T={T}")
+
+
+@pytest.mark.parametrize("T", [2, 8])
+def test_r8_against_reference_apply_golden(golden, T):
+    """The reference's own apply() outputs (bf16 per-op rounding) vs this path.
+
+    The reference rounds gate_up, silu, *up, the down projection, *w and the
+    accumulation to bf16 (quant_method.py:262-277); this path keeps fp32 until
+    one final rounding, so the two agree within the reference's own bf16
+    rounding: max-abs 2e-3 (outputs ~0.2) and rel-L2 1e-2.
+    """
+    s = golden("apply_small.npz")
+    w13, w2 = small_layer_indices(int(s["idx_seed"]), 8, 256, 128)
+    fmt = LUTFormat("r8", 8, 128)
+    tab = bf16_tensor(s["table"])
+    q13 = [QuantizedMatrix(fmt, 256, 256, cuda(w13[e].reshape(-1)), tab, scales=bf16_tensor(s["a13"][e]))
+           for e in range(8)]
+    q2 = [QuantizedMatrix(fmt, 256, 128, cuda(w2[e].reshape(-1)), tab, scales=bf16_tensor(s["a2"][e]))
+          for e in range(8)]
+    layer = LUTMoELayer(LUTExperts.from_quantized(q13, q2, tab), 2)
+    out = layer.forward(bf16_tensor(s[f"x{T}"]), cuda(s[f"ti{T}"]), bf16_tensor(s[f"tw{T}"]).float())
+    ref = O.bf16_to_f32(s[f"out{T}"])
+    o = out.float().cpu().numpy()
+    assert np.abs(o - ref).max() <= 2e-3
+    assert O.rel_l2(o, ref) <= 1e-2
+
+
+def test_r8_qwen_shape_against_reference_golden(golden):
+    q = golden("apply_qwen.npz")
+    w13, w2, a13, a2, _ = qwen_layer_weights(int(q["seed"]), 60, 2048, 1408)
+    fmt = LUTFormat("r8", 8, 128)
+    tab = bf16_tensor(q["table"])
+    q13 = [QuantizedMatrix(fmt, 2816, 2048, cuda(w13[e].reshape(-1)), tab, scales=bf16_tensor(a13[e]))
+           for e in range(60)]
+    q2 = [QuantizedMatrix(fmt, 2048, 1408, cuda(w2[e].reshape(-1)), tab, scales=bf16_tensor(a2[e]))
+          for e in range(60)]
+    layer = LUTMoELayer(LUTExperts.from_quantized(q13, q2, tab), 4)
+    x = bf16_tensor(q["x"])
+    out = layer.forward(x, cuda(q["ti"]), bf16_tensor(q["tw"]).float())
+    ref = O.bf16_to_f32(q["out"])
+    o = out.float().cpu().numpy()
+    # x spans [-2, 2] here, outputs reach ~2: the reference's bf16 per-op rounding
+    # (measured 0.015 max-abs, 5e-3 rel-L2 against float64) dominates
+    assert O.rel_l2(o, ref) <= 1e-2
+    # strict check against the float64 oracle with this path's rounding points
+    W13 = lambda e: O.bf16_to_f32(O.dequant_r(w13[e].reshape(-1), a13[e], q["table"])).reshape(2816, 2048)  # noqa
+    W2 = lambda e: O.bf16_to_f32(O.dequant_r(w2[e].reshape(-1), a2[e], q["table"])).reshape(2048, 1408)  # noqa
+    ex = O.moe_forward(x.float().cpu().numpy(), q["ti"], O.bf16_to_f32(q["tw"]), W13, W2, act_dtype="bf16")
+    check_layer(out, ex, torch.bfloat16, "r8 qwen")
+
+
+@pytest.mark.parametrize("T", [1, 8, 16])
+def test_qwen15_layer_format_b_4bit_g64(T):
+    """Config 1: Qwen1.5-MoE layer (H 2048, 60 experts of I 1408, top-4 softmax,
+    shared expert I 5632 with sigmoid gate), BlockLUT 4-bit g64, seed 0."""
+    H, I, E, k, Is = 2048, 1408, 60, 4, 5632
+    fmt = LUTFormat("b", 4, 64)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    st = torch.distributions.StudentT(torch.tensor(5.0, device="cuda"))
+    scale = 0.02 / (5.0 / 3.0) ** 0.5
+    torch.manual_seed(0)
+    q13, q2 = [], []
+    for _ in range(E):
+        q13.append(encode(st.sample((2 * I, H)) * scale, fmt))
+        q2.append(encode(st.sample((H, I)) * scale, fmt))
+    experts = LUTExperts.from_quantized(q13, q2)
+    router_w = (st.sample((E + 1, H)) * scale).half()
+    s13 = (st.sample((2 * Is, H)) * scale).half()
+    s2 = (st.sample((H, Is)) * scale).half()
+    layer = LUTMoELayer(experts, k, router_w=router_w, shared=SharedExpert.from_dense(s13, s2), shared_gate_mode=1)
+    rng = np.random.Generator(np.random.PCG64(T))
+    x = cuda(O.rms_activations(rng, T, H).astype(np.float16))
+    out = layer.forward(x)
+    layer.check_status()
+    # oracle: routing from the same fp16 inputs, dequant from the same canonical tensors
+    xn = x.float().cpu().numpy()
+    rw = router_w.float().cpu().numpy()
+    logits = xn.astype(np.float64) @ rw[:E].T.astype(np.float64)
+    ids, tw = O.routing(logits, k)
+    srt = np.sort(logits, axis=1)
+    assert (srt[:, -k] - srt[:, -k - 1] > 1e-4).all(), "near-tie in routing; pick another seed"
+    cache = {}
+
+    def deq(lst, e):
+        m = lst[e]
+        return O.dequant_b(m.codes.cpu().numpy(), m.tables.cpu().numpy(), 4, 64).astype(np.float32)
+    ref = O.moe_forward(xn, ids, tw, lambda e: deq(q13, e), lambda e: deq(q2, e), act_dtype="f16",
+                        shared13=s13.float().cpu().numpy(), shared2=s2.float().cpu().numpy(),
+                        shared_gate=rw[E])
+    check_layer(out, ref, torch.float16, f"qwen1.5 layer T={T}")
+
+
+def test_shared_expert_modes_and_graph_capture():
+    fmt = LUTFormat("b", 4, 64)
+    experts, W13, W2 = build_b_layer(fmt, E=4, H=256, I=128, seed=5)
+    rng = np.random.Generator(np.random.PCG64(12))
+    s13 = O.student_t_weights(rng, (256, 256)).astype(np.float16)
+    s2 = O.student_t_weights(rng, (256, 128)).astype(np.float16)
+    gate = O.student_t_weights(rng, (256,)).astype(np.float16)
+    T = 12
+    x = cuda(O.rms_activations(rng, T, 256).astype(np.float16))
+    ids, tw = routing_inputs(rng, T, 4, 2)
+    for mode in (0, 1):
+        sh = SharedExpert.from_dense(cuda(s13), cuda(s2), cuda(gate) if mode else None)
+        layer = LUTMoELayer(experts, 2, shared=sh, shared_gate_mode=mode)
+        out = layer.forward(x, cuda(ids), cuda(tw))
+        ref = O.moe_forward(x.float().cpu().numpy(), ids, tw, W13, W2, act_dtype="f16",
+                            shared13=s13.astype(np.float32), shared2=s2.astype(np.float32),
+                            shared_gate=gate.astype(np.float32) if mode else None)
+        if mode == 0:  # unscaled shared output
+            xs = x.float().cpu().numpy().astype(np.float64)
+            h = xs @ s13.astype(np.float64).T
+            a = O.round_to((O.silu(h[:, :128]) * h[:, 128:]).astype(np.float32), "f16").astype(np.float64)
+            ref = O.moe_forward(xs, ids, tw, W13, W2, act_dtype="f16") + a @ s2.astype(np.float64).T
+        check_layer(out, ref, torch.float16, f"shared mode {mode}")
+    # CUDA graph capture replays the same result, bit for bit
+    ti, tww = cuda(ids), cuda(tw)
+    res = layer.forward(x, ti, tww)
+    static_out = torch.empty_like(res)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        layer.forward(x, ti, tww, out=static_out)
+    torch.cuda.current_stream().wait_stream(s)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        layer.forward(x, ti, tww, out=static_out)
+    static_out.zero_()
+    gr.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(static_out, res)
+
+
+def test_router_path_matches_oracle_routing():
+    fmt = LUTFormat("b", 4, 64)
+    E, k = 8, 3
+    experts, W13, W2 = build_b_layer(fmt, E=E, H=256, I=128, seed=8)
+    rng = np.random.Generator(np.random.PCG64(21))
+    rw = (rng.standard_normal((E, 256)) * 0.1).astype(np.float16)
+    for renorm in (False, True):
+        T = 20
+        x = cuda(O.rms_activations(rng, T, 256).astype(np.float16))
+        layer = LUTMoELayer(experts, k, router_w=cuda(rw), renorm=renorm)
+        out = layer.forward(x)
+        xn = x.float().cpu().numpy().astype(np.float64)
+        logits = xn @ rw.astype(np.float64).T
+        ids, tw = O.routing(logits, k, renorm)
+        srt = np.sort(logits, axis=1)
+        keep = srt[:, -k] - srt[:, -k - 1] > 1e-4  # skip tokens with near-ties at the k-th expert
+        ref = O.moe_forward(xn, ids, tw, W13, W2, act_dtype="f16")
+        check_layer(out[torch.from_numpy(keep).cuda()], ref[keep], torch.float16, f"router renorm={renorm}")
+
+
+def test_deterministic_and_invalid_ids_reported():
+    fmt = LUTFormat("b", 2, 64)
+    experts, W13, W2 = build_b_layer(fmt, E=4, H=256, I=128, seed=2)
+    rng = np.random.Generator(np.random.PCG64(2))
+    x = cuda(O.rms_activations(rng, 9, 256).astype(np.float16))
+    ids, tw = routing_inputs(rng, 9, 4, 2)
+    layer = LUTMoELayer(experts, 2)
+    a = layer.forward(x, cuda(ids), cuda(tw))
+    b = layer.forward(x, cuda(ids), cuda(tw))
+    assert torch.equal(a, b)
+    bad = ids.copy()
+    bad[0, 0] = 17  # out of range: skipped on the device and reported
+    layer.forward(x, cuda(bad), cuda(tw))
+    with pytest.raises(RuntimeError, match="invalid"):
+        layer.check_status()
+    layer.check_status()  # the status word was cleared by the read
