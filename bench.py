@@ -239,6 +239,10 @@ def run_ours(a):
         ids, _, _ = router(x, m.router_w, TOPK, shared_gate=True)
         n_active.append(int(torch.unique(ids).numel()))
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in moes]
+    for ev in evs:  # torch creates the CUDA event on its first record
+        for e in ev:
+            e.record()
+    torch.cuda.synchronize()
     import ctypes as C
     t_gu, t_dn, reps = 0.0, 0.0, 5
     for _ in range(reps):

@@ -23,12 +23,13 @@ BLUT_ERR_CUDA = -6
 
 # formats / dtypes
 FMT_R8, FMT_B, FMT_NESTED, FMT_DENSE = 1, 2, 3, 4
+LAYOUT_PAIRED = 1
 F16, BF16, F32 = 0, 1, 2
 
 
 class MatDesc(C.Structure):
     _fields_ = [("format", C.c_int32), ("bits", C.c_int32), ("group", C.c_int32), ("tier", C.c_int32),
-                ("dtype", C.c_int32), ("reserved", C.c_int32), ("rows", C.c_int64), ("cols", C.c_int64)]
+                ("dtype", C.c_int32), ("layout", C.c_int32), ("rows", C.c_int64), ("cols", C.c_int64)]
 
 
 class Canon(C.Structure):
@@ -48,7 +49,8 @@ class MoEArgs(C.Structure):
                 ("reserved", C.c_int32),
                 ("s13", MatDesc), ("s2", MatDesc),
                 ("s13_tiled", C.c_void_p), ("s2_tiled", C.c_void_p),
-                ("shared_gate_w", C.c_void_p), ("out", C.c_void_p), ("prof_events", C.c_void_p)]
+                ("shared_gate_w", C.c_void_p), ("out", C.c_void_p), ("prof_events", C.c_void_p),
+                ("out_f32", C.c_int32), ("reserved2", C.c_int32)]
 
 
 # (name, restype, argtypes) of every exported entry point, in blut.h order.
@@ -61,6 +63,7 @@ SIGNATURES = [
     ("blut_lut_recover", C.c_int, [_VP, _VP, _VP, _I64, _VP]),
     ("blut_tiled_bytes", C.c_int64, [C.POINTER(MatDesc)]),
     ("blut_pack_tiled", C.c_int, [C.POINTER(MatDesc), C.POINTER(Canon), _VP, _VP]),
+    ("blut_dequant_tiled", C.c_int, [C.POINTER(MatDesc), _VP, _VP, _VP, _VP]),
     ("blut_encode", C.c_int, [C.POINTER(MatDesc), _VP, _VP, _VP, _VP, _VP, _VP]),
     ("blut_encode_r", C.c_int, [_VP, _I64, _VP, _I32, _VP, _VP, _VP]),
     ("blut_lut_gemv", C.c_int, [_VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _VP]),

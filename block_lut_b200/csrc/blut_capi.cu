@@ -55,6 +55,12 @@ int blut_pack_tiled(const blut_mat_desc* desc, const blut_canon* src, void* tile
   return pack_tiled(*desc, *src, tiled, S(stream));
 }
 
+int blut_dequant_tiled(const blut_mat_desc* desc, const void* tiled, const void* lut_table, void* out,
+                       void* stream) {
+  if (!desc) return BLUT_ERR_INVALID;
+  return dequant_tiled(*desc, tiled, lut_table, out, S(stream));
+}
+
 int blut_encode(const blut_mat_desc* desc, const float* w, void* codes, void* tables, void* codes2, void* tables2,
                 void* stream) {
   if (!desc) return BLUT_ERR_INVALID;

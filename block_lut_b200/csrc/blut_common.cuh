@@ -58,6 +58,8 @@ __host__ __device__ inline int64_t table_piece_bytes(int entries, int group) {
 // Fills `L` for `d`.  Returns false if the shape/format has no tiled layout.
 __host__ inline bool make_layout(const blut_mat_desc& d, TiledLayout& L) {
   if (d.rows <= 0 || d.cols <= 0 || d.rows % kTileRows || d.cols % kChunk) return false;
+  if ((d.layout & ~BLUT_LAYOUT_PAIRED) != 0) return false;
+  if ((d.layout & BLUT_LAYOUT_PAIRED) && d.rows % (2 * kTileRows)) return false;
   L = TiledLayout{};
   L.ntiles = d.rows / kTileRows;
   L.nchunks = d.cols / kChunk;
@@ -111,6 +113,24 @@ __host__ inline bool make_layout(const blut_mat_desc& d, TiledLayout& L) {
   }
   L.total = off;
   return true;
+}
+
+// Pieces are stored chunk-major inside each plane: piece (chunk c, physical
+// tile pt) sits at plane_off + (c * ntiles + pt) * piece, so the tiles a CTA
+// streams together at one chunk are one contiguous range.  With
+// BLUT_LAYOUT_PAIRED, logical tile t of the first half of the rows (gate) is
+// physical tile 2t and tile t of the second half (up) is physical tile 2t+1.
+__host__ __device__ inline int64_t piece_off(const TiledLayout& L, int plane, int64_t chunk, int64_t pt) {
+  return L.off[plane] + (chunk * L.ntiles + pt) * L.piece[plane];
+}
+__host__ __device__ inline int64_t phys_tile(int64_t t, int64_t ntiles, bool paired) {
+  if (!paired) return t;
+  const int64_t half = ntiles / 2;
+  return t < half ? 2 * t : 2 * (t - half) + 1;
+}
+__host__ __device__ inline int64_t logical_tile(int64_t pt, int64_t ntiles, bool paired) {
+  if (!paired) return pt;
+  return (pt & 1) ? ntiles / 2 + pt / 2 : pt / 2;
 }
 
 // Position of element (r, k) of a (tile, chunk) piece: r in [0,16), k in [0,128).

@@ -53,6 +53,9 @@ cudaError_t launch_mm_nested(int group, bool pair, const MMParams& p, int sms, c
 cudaError_t launch_mm_r8(bool pair, const MMParams& p, int sms, cudaStream_t stream);
 cudaError_t launch_mm_dense(bool bf16, bool pair, const MMParams& p, int sms, cudaStream_t stream);
 
+bool mm_planes(const blut_mat_desc& d, bool pair, MMParams& p);
+int dequant_tiled(const blut_mat_desc& d, const void* tiled, const void* table, void* out, cudaStream_t stream);
+
 // Canonical-layout kernels (blut_pack.cu, blut_gemv.cu).
 int dequant(const blut_mat_desc& d, const blut_canon& c, void* out, cudaStream_t stream);
 int pack_tiled(const blut_mat_desc& d, const blut_canon& c, void* tiled, cudaStream_t stream);

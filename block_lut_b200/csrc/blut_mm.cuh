@@ -1,16 +1,25 @@
 // LUT matmul mainloop: every (token group, weight tile) of a layer in one launch.
 //
-// Work item = (group of <= 32 tokens routed to one expert, 16-row tile of
-// the expert's matrix; a gate tile and its up tile together for the gate/up
-// projection).  A CTA of 4 warps owns an item; the K chunks are split among
-// the warps (split-K), each warp streams its chunks through its own ring of
-// shared-memory stages filled by bulk TMA copies (cp.async.bulk, one per
-// plane per tile, completing on an mbarrier), looks codes up into A
-// fragments and runs mma.m16n8k16 against the tokens' B fragments.  The
-// ring runs ahead across items, so a CTA's stream of chunks never drains
-// between items.  Partial sums meet in shared memory; the epilogue applies
-// SiLU(gate) * up and writes the next projection's B fragments, or writes
-// fp32 rows of the expert outputs.
+// Work item = (group of <= 32 tokens routed to one expert, W consecutive
+// tile units of that expert's matrix); a unit is a gate tile plus its up tile
+// for the gate/up projection (paired layout), or one 16-row tile for the
+// down projection.  A CTA has one producer warp and W consumer warps:
+//
+//  * the producer's elected lane streams, chunk by chunk (128 columns), the
+//    code/table planes of the item's W units -- one bulk TMA copy
+//    (cp.async.bulk) per plane, contiguous thanks to the chunk-major tiled
+//    layout -- plus the group's B fragments of that chunk, into a ring of
+//    shared-memory stages (full barrier: transaction bytes; empty barrier:
+//    one arrival per consumer warp);
+//  * each consumer warp owns one unit for the whole K loop: it looks codes
+//    up into mma.m16n8k16 A fragments, multiplies them against the shared
+//    B fragments of up to 4 n-tiles (8 tokens each), accumulates in fp32
+//    registers and finishes with the epilogue -- SiLU(gate) * up written as
+//    the down projection's B fragments, or fp32 expert-output rows.
+//
+// Every wait is bounded: a wait that runs out sets a CTA-wide abort flag and
+// the device status word, all warps skip the remaining work, and the
+// producer lets the copies it still has in flight land before exiting.
 #pragma once
 
 #include <mutex>
@@ -19,9 +28,9 @@
 
 namespace blut {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kWarpRingBytes = 20 * 1024;
+constexpr int kMaxConsumers = 4;
+constexpr int kRingBudget = 96 * 1024;       // shared-memory ring bytes per CTA
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 struct GroupTab {
   const int* n_groups;  // device scalar
@@ -36,17 +45,18 @@ struct MMParams {
   int64_t wstride;         // bytes between experts
   int64_t plane_off[3];    // matrix-relative offsets of the planes this kernel reads
   int piece[3];            // bytes per (tile, chunk) piece of those planes
-  int tile_bytes;          // sum of piece[] (one tile's share of a stage)
-  int stages;              // ring stages per warp
-  int ntiles;              // 16-row tiles of the matrix
+  int tile_bytes;          // sum of piece[]
+  int ntiles;              // physical 16-row tiles of the matrix
   int nchunks;             // 128-column chunks (K / 128)
+  int units;               // pairs (gate/up) or tiles (down)
+  int W;                   // units per work item = consumer warps
+  int b_ntiles;            // B n-tiles reserved per stage (max over groups)
+  int stages;              // ring stages
   GroupTab gt;
   const uint8_t* bin;      // B fragments of the input, [n-tile][chunk][2 KB]
-  // pair epilogue: B fragments of SiLU(gate) * up, [n-tile][out_nchunks][2 KB]
-  uint8_t* act_out;
+  uint8_t* act_out;        // pair epilogue: B fragments of SiLU(gate)*up
   int out_nchunks;
-  // single epilogue: fp32 rows y[slot][y_ld]
-  float* y_out;
+  float* y_out;            // single epilogue: fp32 rows y[slot][y_ld]
   int y_ld;
   const uint16_t* r8_table;  // global bf16 [256], FMT_R8 only
   uint32_t r8_mask;
@@ -60,85 +70,140 @@ __host__ __device__ constexpr int mm_r8_smem() {
   return Pol::kR8 ? 256 * 32 * 4 : 0;
 }
 
-template <class Pol, bool kPair>
-__host__ __device__ constexpr int mm_red_bytes() {
-  return kWarps * (kPair ? 2 : 1) * kMaxNT * 32 * 16;
+__host__ __device__ inline int mm_stage_bytes(const MMParams& p, int ntl) {
+  return ((p.W * ntl * p.tile_bytes + p.b_ntiles * kBfragChunkBytes) + 127) & ~127;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Bounded wait that also gives up as soon as another warp aborted.
+__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                              int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (*abort_flag) return false;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1; i < (1u << 31); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+  }
+  *abort_flag = 1;
+  atomicOr(status, kDevTimeout);
+  return false;
+}
+
+// Bounded wait that ignores the abort flag (used to drain copies in flight).
+__device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 31); ++i) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((i & 63) == 63 && globaltimer_ns() - t0 > kWaitLimitNs) return;
+  }
 }
 
 template <class Pol, bool kPair>
-__global__ void __launch_bounds__(kThreads) lut_mm_kernel(const MMParams p) {
+__global__ void __launch_bounds__(32 * (kMaxConsumers + 1)) lut_mm_kernel(const MMParams p) {
   constexpr int NTL = kPair ? 2 : 1;
   constexpr int kR8Bytes = mm_r8_smem<Pol>();
   extern __shared__ __align__(128) uint8_t smem[];
+  const int S = p.stages;
   uint32_t* r8tab = reinterpret_cast<uint32_t*>(smem);
-  float4* red = reinterpret_cast<float4*>(smem + kR8Bytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kR8Bytes + mm_red_bytes<Pol, kPair>());
-  uint8_t* ring = smem + kR8Bytes + mm_red_bytes<Pol, kPair>() + kWarps * 8 * 8;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kR8Bytes);
+  uint64_t* empty = full + 8;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 16);
+  uint8_t* ring = smem + kR8Bytes + 256;
+  const int stage_bytes = mm_stage_bytes(p, NTL);
+  const int W = p.W;
+  // stage layout: plane q of the W*NTL tiles at qoff[q], then the B n-tiles at boff
+  int qoff[3];
+  {
+    int o = 0;
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      qoff[q] = o;
+      o += q < Pol::kNumPlanes ? W * NTL * p.piece[q] : 0;
+    }
+  }
+  const int boff = W * NTL * p.tile_bytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int S = p.stages;
-  const int stage_bytes = NTL * p.tile_bytes;
-  uint8_t* my_ring = ring + warp * S * stage_bytes;
-  const uint32_t my_bar0 = smem_u32(bars + warp * 8);
-
   if constexpr (kR8Bytes > 0) {
-    for (int i = threadIdx.x; i < 256 * 32; i += kThreads) r8tab[i] = p.r8_table[i >> 5];
+    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) r8tab[i] = p.r8_table[i >> 5];
   }
-  if (lane == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(my_bar0 + 8 * s, 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(full + s), 1);
+      mbar_init(smem_u32(empty + s), W);
+    }
+    *abort_flag = 0;
     fence_mbar_init();
   }
   __syncthreads();
 
+  const int ipg = (p.units + W - 1) / W;  // items per group
+  const int64_t n_items = (int64_t)(*p.gt.n_groups) * ipg;
+  const int64_t i0 = n_items * blockIdx.x / gridDim.x;
+  const int64_t i1 = n_items * (blockIdx.x + 1) / gridDim.x;
+  const int64_t total = (i1 - i0) * p.nchunks;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane != 0) return;
+    int64_t n = 0;
+    for (; n < total; ++n) {
+      const int slot = (int)(n % S);
+      const int64_t use = n / S;
+      if (use > 0 && !wait_or_abort(smem_u32(empty + slot), (uint32_t)((use - 1) & 1), abort_flag, p.status))
+        break;
+      if (*abort_flag) break;
+      const int64_t item = i0 + n / p.nchunks;
+      const int c = (int)(n % p.nchunks);
+      const int gi = (int)(item / ipg);
+      const int u0 = (int)(item % ipg) * W;
+      const int nu = min(W, p.units - u0);
+      const int ntv = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
+      const int nt0 = p.gt.nt0[gi];
+      const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
+      uint8_t* dst = ring + (int64_t)slot * stage_bytes;
+      const uint32_t bar = smem_u32(full + slot);
+      mbar_expect_tx(bar, (uint32_t)(nu * NTL * p.tile_bytes + ntv * kBfragChunkBytes));
+      const int64_t pt0 = (int64_t)u0 * NTL;
+#pragma unroll
+      for (int q = 0; q < Pol::kNumPlanes; ++q) {
+        const uint8_t* src = base + p.plane_off[q] + ((int64_t)c * p.ntiles + pt0) * p.piece[q];
+        bulk_g2s(smem_u32(dst + qoff[q]), src, (uint32_t)(nu * NTL * p.piece[q]), bar);
+      }
+      for (int i = 0; i < ntv; ++i) {
+        const uint8_t* src = p.bin + ((int64_t)(nt0 + i) * p.nchunks + c) * kBfragChunkBytes;
+        bulk_g2s(smem_u32(dst + boff + i * kBfragChunkBytes), src, kBfragChunkBytes, bar);
+      }
+    }
+    if (*abort_flag) {
+      // let the copies already issued land before the CTA's shared memory goes away
+      for (int64_t m = n - S > 0 ? n - S : 0; m < n; ++m) wait_drain(smem_u32(full + m % S), (uint32_t)((m / S) & 1));
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers --
+  const int cw = warp - 1;
   PolExtra ex;
   ex.r8_table = r8tab;
   ex.r8_mask = p.r8_mask;
-
-  const int tiles_per_item = kPair ? p.ntiles / 2 : p.ntiles;
-  const int n_items = *p.gt.n_groups * tiles_per_item;
-  const int c0 = warp * p.nchunks / kWarps;
-  const int cpw = (warp + 1) * p.nchunks / kWarps - c0;
-  const int my_items = n_items > (int)blockIdx.x ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int total = my_items * cpw;
-
-  // Producer side (lane 0): issue the copies of step n into stage n % S.
-  auto issue = [&](int n) {
-    const int item = blockIdx.x + (n / cpw) * gridDim.x;
-    const int c = c0 + n % cpw;
-    const int gi = item / tiles_per_item;
-    const int ti = item - gi * tiles_per_item;
-    const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
-    const int slot = n % S;
-    const uint32_t bar = my_bar0 + 8 * slot;
-    uint8_t* dst = my_ring + slot * stage_bytes;
-    mbar_expect_tx(bar, stage_bytes);
-#pragma unroll
-    for (int t = 0; t < NTL; ++t) {
-      const int tile = t == 0 ? ti : ti + tiles_per_item;
-      int doff = t * p.tile_bytes;
-#pragma unroll
-      for (int q = 0; q < Pol::kNumPlanes; ++q) {
-        const uint8_t* src = base + p.plane_off[q] + ((int64_t)tile * p.nchunks + c) * p.piece[q];
-        bulk_g2s(smem_u32(dst + doff), src, p.piece[q], bar);
-        doff += p.piece[q];
-      }
-    }
-  };
-
-  int issued = 0;
-  if (lane == 0) {
-    for (; issued < total && issued < S; ++issued) issue(issued);
-  }
-  bool ok = true;
-  int n = 0;
-  for (int j = 0; j < my_items; ++j) {
-    const int item = blockIdx.x + j * gridDim.x;
-    const int gi = item / tiles_per_item;
-    const int ti = item - gi * tiles_per_item;
+  int64_t n = 0;
+  for (int64_t item = i0; item < i1; ++item) {
+    const int gi = (int)(item / ipg);
+    const int u0 = (int)(item % ipg) * W;
+    const int nu = min(W, p.units - u0);
     const int ntok = p.gt.ntok[gi];
     const int ntv = (ntok + kNTile - 1) / kNTile;
     const int nt0 = p.gt.nt0[gi];
+    const bool mine = cw < nu;
 
     float acc[NTL][kMaxNT][4];
 #pragma unroll
@@ -148,35 +213,28 @@ __global__ void __launch_bounds__(kThreads) lut_mm_kernel(const MMParams p) {
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[t][i][r] = 0.f;
 
-    for (int cc = 0; cc < cpw; ++cc, ++n) {
-      const int slot = n % S;
-      if (ok) {
-        bool w_ok = mbar_wait_bounded(my_bar0 + 8 * slot, (n / S) & 1, p.status);
-        ok = __shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0) != 0;
-      }
-      if (ok) {
-        const int c = c0 + cc;
-        const uint8_t* st = my_ring + slot * stage_bytes;
+    for (int c = 0; c < p.nchunks; ++c, ++n) {
+      const int slot = (int)(n % S);
+      bool ok = wait_or_abort(smem_u32(full + slot), (uint32_t)((n / S) & 1), abort_flag, p.status);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (ok && mine) {
+        const uint8_t* st = ring + (int64_t)slot * stage_bytes;
         Pol P[NTL];
 #pragma unroll
         for (int t = 0; t < NTL; ++t) {
+          const int lt = cw * NTL + t;
           const uint8_t* planes[3];
-          int off = t * p.tile_bytes;
 #pragma unroll
-          for (int q = 0; q < Pol::kNumPlanes; ++q) {
-            planes[q] = st + off;
-            off += p.piece[q];
-          }
+          for (int q = 0; q < Pol::kNumPlanes; ++q) planes[q] = st + qoff[q] + lt * p.piece[q];
           P[t].begin(planes, lane, ex);
         }
-        const uint8_t* bsrc = p.bin + ((int64_t)nt0 * p.nchunks + c) * kBfragChunkBytes + lane * 64;
-        const int64_t bstep = (int64_t)p.nchunks * kBfragChunkBytes;
+        const uint8_t* bsrc = st + boff + lane * 64;
 #pragma unroll
         for (int sp = 0; sp < 4; ++sp) {
           uint4 b[kMaxNT];
 #pragma unroll
           for (int i = 0; i < kMaxNT; ++i) {
-            if (i < ntv) b[i] = __ldg(reinterpret_cast<const uint4*>(bsrc + i * bstep + sp * 16));
+            if (i < ntv) b[i] = lds128(bsrc + i * kBfragChunkBytes + sp * 16);
           }
 #pragma unroll
           for (int s2 = 0; s2 < 2; ++s2) {
@@ -198,90 +256,69 @@ __global__ void __launch_bounds__(kThreads) lut_mm_kernel(const MMParams p) {
         }
       }
       __syncwarp();
-      if (lane == 0 && ok && issued < total) {
-        fence_proxy_async();
-        issue(issued++);
-      }
+      if (lane == 0) mbar_arrive(smem_u32(empty + slot));
     }
 
-    // split-K reduction across the warps
+    if (!mine) continue;
+    const int u = u0 + cw;  // logical unit: I-tile of the pair, or H-tile
+    const int g = lane >> 2, tq = lane & 3;
 #pragma unroll
-    for (int t = 0; t < NTL; ++t)
-#pragma unroll
-      for (int i = 0; i < kMaxNT; ++i)
-        red[((warp * NTL + t) * kMaxNT + i) * 32 + lane] = make_float4(acc[t][i][0], acc[t][i][1], acc[t][i][2], acc[t][i][3]);
-    __syncthreads();
-    if (warp < ntv) {
-      const int i = warp;
-      float v[NTL][4];
-#pragma unroll
-      for (int t = 0; t < NTL; ++t) {
-        float4 s4 = red[((0 * NTL + t) * kMaxNT + i) * 32 + lane];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) {
-          const float4 o = red[((w * NTL + t) * kMaxNT + i) * 32 + lane];
-          s4.x += o.x; s4.y += o.y; s4.z += o.z; s4.w += o.w;
-        }
-        v[t][0] = s4.x; v[t][1] = s4.y; v[t][2] = s4.z; v[t][3] = s4.w;
-      }
-      const int g = lane >> 2, tq = lane & 3;
+    for (int i = 0; i < kMaxNT; ++i) {
+      if (i >= ntv) break;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const int row = g + 8 * (r >> 1);     // tile row
-        const int tok = 2 * tq + (r & 1);     // token inside the n-tile
+        const int row = g + 8 * (r >> 1);
+        const int tok = 2 * tq + (r & 1);
         const bool valid = i * kNTile + tok < ntok;
         if constexpr (kPair) {
-          const float val = valid ? silu_f(v[0][r]) * v[1][r] : 0.f;
-          const int col = ti * kTileRows + row;  // column of the next projection's K
+          const float val = valid ? silu_f(acc[0][i][r]) * acc[1][i][r] : 0.f;
+          const int col = u * kTileRows + row;  // K index of the next projection
           uint8_t* dst = p.act_out + ((int64_t)(nt0 + i) * p.out_nchunks + (col >> 7)) * kBfragChunkBytes +
                          bfrag_byte(tok, col & 127);
           *reinterpret_cast<uint16_t*>(dst) = f32_to_act<Pol::kBF16>(val);
         } else {
           if (valid) {
             const int slot = p.gt.slot0[gi] + i * kNTile + tok;
-            p.y_out[(int64_t)slot * p.y_ld + ti * kTileRows + row] = v[0][r];
+            p.y_out[(int64_t)slot * p.y_ld + u * kTileRows + row] = acc[0][i][r];
           }
         }
       }
     }
-    __syncthreads();
-  }
-
-  // After a timed-out wait, let copies still in flight land before exiting.
-  if (!ok && lane == 0) {
-    for (int m = n; m < issued; ++m) mbar_wait_bounded(my_bar0 + 8 * (m % S), (m / S) & 1, p.status);
   }
 }
 
-// Host-side launch helper: dynamic smem and grid for one instantiation.
+// Host-side launch: ring depth from the shared-memory budget, grid from occupancy.
 template <class Pol, bool kPair>
-inline int mm_smem_bytes(int stages, int tile_bytes) {
-  return mm_r8_smem<Pol>() + mm_red_bytes<Pol, kPair>() + kWarps * 8 * 8 +
-         kWarps * stages * (kPair ? 2 : 1) * tile_bytes;
+inline int mm_smem_bytes(const MMParams& p) {
+  return mm_r8_smem<Pol>() + 256 + p.stages * mm_stage_bytes(p, kPair ? 2 : 1);
 }
 
 template <class Pol, bool kPair>
 inline cudaError_t launch_mm(MMParams p, int num_sms, cudaStream_t stream) {
-  const int smem = mm_smem_bytes<Pol, kPair>(p.stages, p.tile_bytes);
+  const int stage = mm_stage_bytes(p, kPair ? 2 : 1);
+  p.stages = std::max(2, std::min(8, kRingBudget / stage));
+  const int smem = mm_smem_bytes<Pol, kPair>(p);
+  const int threads = 32 * (p.W + 1);
   auto kern = lut_mm_kernel<Pol, kPair>;
-  // attribute + occupancy per (instantiation, smem size), computed once
+  // attribute + occupancy per (instantiation, smem size, block size), computed once
   static std::mutex mu;
-  static int cached_smem = -1, cached_per_sm = 1;
+  static int cached_smem = -1, cached_threads = -1, cached_per_sm = 1;
   int per_sm;
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (cached_smem != smem) {
+    if (cached_smem != smem || cached_threads != threads) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
-      int n = 0;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem);
+      int nb = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, threads, smem);
       if (e != cudaSuccess) return e;
-      cached_per_sm = n < 1 ? 1 : n;
+      cached_per_sm = nb < 1 ? 1 : nb;
       cached_smem = smem;
+      cached_threads = threads;
     }
     per_sm = cached_per_sm;
   }
-  kern<<<num_sms * per_sm, kThreads, smem, stream>>>(p);
+  kern<<<num_sms * per_sm, threads, smem, stream>>>(p);
   return cudaGetLastError();
 }
 

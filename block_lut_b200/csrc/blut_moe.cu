@@ -2,6 +2,8 @@
 // matmul launches and the weighted combine.  All launches go on the caller's
 // stream; nothing synchronises the host and nothing allocates.
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "blut_mm.cuh"
@@ -102,7 +104,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
   for (int q = threadIdx.x; q < S; q += blockDim.x) {
     const int e = ids[q];
     if (e >= 0 && e < num_experts) atomicAdd(&cnt[e], 1);
-    else atomicOr(pp.status, kDevBadExpert);
+    else if (e != -1) atomicOr(pp.status, kDevBadExpert);  // -1 = empty slot
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -215,7 +217,7 @@ template <bool BF16>
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, const float* __restrict__ ys,
                                                       const float* __restrict__ tw, const int* __restrict__ tk_slot,
                                                       const float* __restrict__ sg, int top_k, int hidden,
-                                                      int shared_mode, uint16_t* __restrict__ out) {
+                                                      int shared_mode, void* __restrict__ out_v, int out_f32) {
   const int t = blockIdx.x;
   for (int h = threadIdx.x * 4; h < hidden; h += blockDim.x * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -231,10 +233,14 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
       const float4 v = *reinterpret_cast<const float4*>(ys + (int64_t)t * hidden + h);
       acc.x += g * v.x; acc.y += g * v.y; acc.z += g * v.z; acc.w += g * v.w;
     }
-    uint2 o;
-    o.x = uint32_t(f32_to_act<BF16>(acc.x)) | (uint32_t(f32_to_act<BF16>(acc.y)) << 16);
-    o.y = uint32_t(f32_to_act<BF16>(acc.z)) | (uint32_t(f32_to_act<BF16>(acc.w)) << 16);
-    *reinterpret_cast<uint2*>(out + (int64_t)t * hidden + h) = o;
+    if (out_f32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(out_v) + (int64_t)t * hidden + h) = acc;
+    } else {
+      uint2 o;
+      o.x = uint32_t(f32_to_act<BF16>(acc.x)) | (uint32_t(f32_to_act<BF16>(acc.y)) << 16);
+      o.y = uint32_t(f32_to_act<BF16>(acc.z)) | (uint32_t(f32_to_act<BF16>(acc.w)) << 16);
+      *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out_v) + (int64_t)t * hidden + h) = o;
+    }
   }
 }
 
@@ -330,6 +336,10 @@ int validate_moe(const blut_moe_args& a) {
   if (a.w13.rows != 2LL * a.inter || a.w13.cols != a.hidden || a.w2.rows != a.hidden || a.w2.cols != a.inter)
     return BLUT_ERR_INVALID;
   if (a.w13.dtype != a.dtype) return BLUT_ERR_UNSUPPORTED;
+  // gate/up tiles must be paired in the tiled layout, the down projection not
+  if (!(a.w13.layout & BLUT_LAYOUT_PAIRED) || (a.w2.layout & BLUT_LAYOUT_PAIRED)) return BLUT_ERR_INVALID;
+  if (a.shared_inter > 0 && (!(a.s13.layout & BLUT_LAYOUT_PAIRED) || (a.s2.layout & BLUT_LAYOUT_PAIRED)))
+    return BLUT_ERR_INVALID;
   if (a.w13.format == BLUT_FMT_R8 && !a.lut_table) return BLUT_ERR_INVALID;
   TiledLayout L13, L2;
   if (!make_layout(a.w13, L13) || !make_layout(a.w2, L2)) return BLUT_ERR_UNSUPPORTED;
@@ -372,10 +382,49 @@ bool mm_planes(const blut_mat_desc& d, bool pair, MMParams& p) {
   p.tile_bytes = tb;
   p.ntiles = (int)L.ntiles;
   p.nchunks = (int)L.nchunks;
-  const int stage = (pair ? 2 : 1) * tb;
-  p.stages = std::max(2, std::min(8, kWarpRingBytes / stage));
+  p.units = pair ? p.ntiles / 2 : p.ntiles;
+  p.W = 1;
+  p.b_ntiles = kMaxNT;
+  p.stages = 2;
   p.r8_mask = d.tier == 1 ? 0x3Fu : d.tier == 2 ? 0x0Fu : 0xFFu;
   return true;
+}
+
+// Units per work item: as many consumer warps per CTA as keeps at least two
+// items per SM for the expected number of token groups.
+static int choose_units_per_item(double est_groups, int units, int sms) {
+  int w = kMaxConsumers;
+  while (w > 1 && est_groups * ((units + w - 1) / w) < 2.0 * sms) w /= 2;
+  return w;
+}
+
+// Expected number of experts hit by T tokens choosing k of E uniformly.
+static double expected_active(int T, int k, int E) {
+  double miss = 1.0;
+  for (int t = 0; t < T; ++t) miss *= 1.0 - (double)k / E;
+  return E * (1.0 - miss);
+}
+
+// Error check after a stage.  With BLUT_DEBUG_SYNC set, every stage also
+// synchronises the stream, so a failing kernel is named by its own stage.
+static bool debug_sync() {
+  static const bool on = std::getenv("BLUT_DEBUG_SYNC") != nullptr;
+  return on;
+}
+
+static int stage_done(const char* stage, cudaStream_t s) {
+  cudaError_t e = cudaGetLastError();
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (e == cudaSuccess && debug_sync() && cudaStreamIsCapturing(s, &cap) == cudaSuccess &&
+      cap == cudaStreamCaptureStatusNone) {
+    e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess) e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "libblut: %s: %s\n", stage, cudaGetErrorString(e));
+    return BLUT_ERR_LAUNCH;
+  }
+  return BLUT_OK;
 }
 
 int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaStream_t stream) {
@@ -391,6 +440,9 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   const bool sh = a.shared_inter > 0;
   const int T = a.num_tokens, K = a.top_k, E = a.num_experts, H = a.hidden;
   const int sms = num_sms();
+  const double est_groups = expected_active(T, K, E) + (double)T * K / kGroupTok;
+  const double est_sgroups = (T + kGroupTok - 1) / kGroupTok;
+  const int b_ntiles = (std::min(T, kGroupTok) + kNTile - 1) / kNTile;
 
   // 1. routing (or the caller's routing) and the shared-expert gate
   const int32_t* ids = a.topk_ids;
@@ -407,6 +459,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
                                                        a.renorm, sg_from_router, 1, ws.ids, ws.tw, ws.sg);
     ids = ws.ids;
     tw = ws.tw;
+    if ((rc = stage_done("router", stream)) != BLUT_OK) return rc;
   }
   if (sh && a.shared_gate_mode == 1 && !sg_from_router) {
     // gate-only pass over the single row shared_gate_w (as row "E" of a 0-expert router)
@@ -417,16 +470,17 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
     else
       router_kernel<false><<<T, 256, 2 * sizeof(float), stream>>>((const uint16_t*)a.x, gw, H, 0, 0, 0, 1, 0,
                                                                     nullptr, nullptr, ws.sg);
+    if ((rc = stage_done("shared gate", stream)) != BLUT_OK) return rc;
   }
   // 2. plan
   plan_kernel<<<1, 1024, 0, stream>>>(ids, T, K, E, sh ? 1 : 0, ws.pp);
+  if ((rc = stage_done("plan", stream)) != BLUT_OK) return rc;
   // 3. B fragments of x (routed and shared)
   {
     dim3 grid((unsigned)std::max<int64_t>(ws.ntmax, sh ? ws.sntmax : 0), (unsigned)(H / kChunk), sh ? 2 : 1);
     gather_bfrag_kernel<<<grid, 32, 0, stream>>>((const uint16_t*)a.x, H, ws.pp, ws.xf, ws.xfs);
   }
-  cudaError_t err = cudaGetLastError();
-  if (err != cudaSuccess) return BLUT_ERR_LAUNCH;
+  if ((rc = stage_done("gather", stream)) != BLUT_OK) return rc;
 
   // 4. gate/up + SiLU*up, 5. down -- routed experts
   MMParams p{};
@@ -441,10 +495,13 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   p13.bin = ws.xf;
   p13.act_out = ws.af;
   p13.out_nchunks = a.inter / kChunk;
+  p13.W = choose_units_per_item(est_groups, p13.units, sms);
+  p13.b_ntiles = b_ntiles;
   cudaEvent_t* ev = a.prof_events ? (cudaEvent_t*)a.prof_events : nullptr;
-  if (ev) cudaEventRecord(ev[0], stream);
+  if (ev && cudaEventRecord(ev[0], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if (launch_lut_mm(a.w13, true, p13, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
-  if (ev) cudaEventRecord(ev[1], stream);
+  if ((rc = stage_done("routed gate/up", stream)) != BLUT_OK) return rc;
+  if (ev && cudaEventRecord(ev[1], stream) != cudaSuccess) return BLUT_ERR_INVALID;
 
   MMParams pS13 = p;
   if (sh) {
@@ -455,7 +512,10 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
     pS13.bin = ws.xfs;
     pS13.act_out = ws.afs;
     pS13.out_nchunks = a.shared_inter / kChunk;
+    pS13.W = choose_units_per_item(est_sgroups, pS13.units, sms);
+    pS13.b_ntiles = b_ntiles;
     if (launch_lut_mm(a.s13, true, pS13, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+    if ((rc = stage_done("shared gate/up", stream)) != BLUT_OK) return rc;
   }
 
   MMParams p2 = p;
@@ -465,9 +525,12 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   p2.bin = ws.af;
   p2.y_out = ws.y;
   p2.y_ld = H;
-  if (ev) cudaEventRecord(ev[2], stream);
+  p2.W = choose_units_per_item(est_groups, p2.units, sms);
+  p2.b_ntiles = b_ntiles;
+  if (ev && cudaEventRecord(ev[2], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if (launch_lut_mm(a.w2, false, p2, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
-  if (ev) cudaEventRecord(ev[3], stream);
+  if ((rc = stage_done("routed down", stream)) != BLUT_OK) return rc;
+  if (ev && cudaEventRecord(ev[3], stream) != cudaSuccess) return BLUT_ERR_INVALID;
 
   if (sh) {
     MMParams pS2 = pS13;
@@ -478,19 +541,21 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
     pS2.act_out = nullptr;
     pS2.y_out = ws.ys;
     pS2.y_ld = H;
+    pS2.W = choose_units_per_item(est_sgroups, pS2.units, sms);
+    pS2.b_ntiles = b_ntiles;
     if (launch_lut_mm(a.s2, false, pS2, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+    if ((rc = stage_done("shared down", stream)) != BLUT_OK) return rc;
   }
 
   // 6. combine
   const int smode = sh ? a.shared_gate_mode : -1;
   if (bf16)
-    combine_kernel<true><<<T, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode,
-                                                (uint16_t*)a.out);
+    combine_kernel<true><<<T, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
+                                                a.out_f32);
   else
-    combine_kernel<false><<<T, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode,
-                                                 (uint16_t*)a.out);
-  err = cudaGetLastError();
-  return err == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
+    combine_kernel<false><<<T, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
+                                                 a.out_f32);
+  return stage_done("combine", stream);
 }
 
 int moe_launch_count(const blut_moe_args& a) {

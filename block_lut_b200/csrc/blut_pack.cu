@@ -121,7 +121,7 @@ __global__ void lut_recover_kernel(uint16_t* __restrict__ out, const uint8_t* __
 // zeroed tiled buffer (whose planes are 256-byte aligned and padded).
 struct PackArgs {
   TiledLayout L;
-  int format, bits, group, tier;
+  int format, bits, group, tier, layout;
   int64_t rows, cols;
   uint8_t* dst;
   const uint8_t* codes;
@@ -132,8 +132,8 @@ struct PackArgs {
 };
 
 __device__ __forceinline__ uint8_t* piece_ptr(const PackArgs& a, int plane, int64_t r, int64_t k) {
-  const int64_t tile = r / kTileRows, chunk = k / kChunk;
-  return a.dst + a.L.off[plane] + (tile * a.L.nchunks + chunk) * a.L.piece[plane];
+  const int64_t pt = phys_tile(r / kTileRows, a.L.ntiles, (a.layout & BLUT_LAYOUT_PAIRED) != 0);
+  return a.dst + piece_off(a.L, plane, k / kChunk, pt);
 }
 
 __device__ __forceinline__ void or_code(uint8_t* piece, int word, int bit, uint32_t v) {
@@ -194,40 +194,43 @@ __global__ void pack_tables_kernel(PackArgs a) {
     }
     return;
   }
+  // One thread per table byte: (row, block, plane byte b) with b < 2 * entries;
+  // byte b holds the high byte of entry b (b < entries) or the low byte of
+  // entry b - entries.  FMT_B: one table plane; NESTED: the coarse plane
+  // (4 entries, bytes 0..7) and the combined plane (16 entries, bytes 8..39).
   const int64_t nb = a.cols / a.group;
-  const int ent_main = a.format == BLUT_FMT_NESTED ? 4 : (1 << a.bits);
-  const int64_t n = a.rows * nb * 16;
+  const int per_block = a.format == BLUT_FMT_NESTED ? 8 + 32 : 2 * (1 << a.bits);
+  const int64_t n = a.rows * nb * per_block;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int e = int(i % 16);
-    const int64_t rb = i / 16;
+    int b = int(i % per_block);
+    const int64_t rb = i / per_block;
     const int64_t r = rb / nb, j = rb - r * nb;
     const int64_t k0 = j * a.group;
     const int rr = int(r % kTileRows);
     const int jb = int((k0 % kChunk) / a.group);
+    int plane, ent;
+    uint16_t v;
     if (a.format == BLUT_FMT_B) {
-      if (e >= ent_main) continue;
-      const uint16_t v = a.tables[rb * ent_main + e];
-      uint8_t* p = piece_ptr(a, a.L.nplanes - 1, r, k0);
-      const int off = table_hi_byte(rr, jb, e, ent_main);
-      p[off] = uint8_t(v >> 8);
-      p[off + ent_main] = uint8_t(v & 0xFF);
-    } else {  // NESTED: coarse table (plane 1) and combined table (plane 3)
-      if (e < 4) {
-        const uint16_t v = a.tables[rb * 4 + e];
-        uint8_t* p = piece_ptr(a, 1, r, k0);
-        const int off = table_hi_byte(rr, jb, e, 4);
-        p[off] = uint8_t(v >> 8);
-        p[off + 4] = uint8_t(v & 0xFF);
-      }
-      const int c = e >> 2;
-      const float cv = __half2float(__ushort_as_half(a.tables[rb * 4 + c]));
+      plane = a.L.nplanes - 1;
+      ent = 1 << a.bits;
+      v = a.tables[rb * ent + (b % ent)];
+    } else if (b < 8) {  // NESTED coarse table
+      plane = 1;
+      ent = 4;
+      v = a.tables[rb * 4 + (b % 4)];
+    } else {             // NESTED combined table: fp16(coarse[c] + refine[c * 4 + r])
+      b -= 8;
+      plane = 3;
+      ent = 16;
+      const int e = b % 16;
+      const float cv = __half2float(__ushort_as_half(a.tables[rb * 4 + (e >> 2)]));
       const float rv = __half2float(__ushort_as_half(a.tables2[rb * 16 + e]));
-      const uint16_t v = __half_as_ushort(__float2half_rn(__fadd_rn(cv, rv)));
-      uint8_t* p = piece_ptr(a, 3, r, k0);
-      const int off = table_hi_byte(rr, jb, e, 16);
-      p[off] = uint8_t(v >> 8);
-      p[off + 16] = uint8_t(v & 0xFF);
+      v = __half_as_ushort(__float2half_rn(__fadd_rn(cv, rv)));
     }
+    const int e = b % ent;
+    const bool hi = b < ent;
+    uint8_t* p = piece_ptr(a, plane, r, k0);
+    p[table_hi_byte(rr, jb, e, ent) + (hi ? 0 : ent)] = hi ? uint8_t(v >> 8) : uint8_t(v & 0xFF);
   }
 }
 
@@ -526,6 +529,7 @@ int pack_tiled(const blut_mat_desc& d, const blut_canon& c, void* tiled, cudaStr
   a.bits = d.bits;
   a.group = d.group;
   a.tier = d.tier;
+  a.layout = d.layout;
   a.rows = d.rows;
   a.cols = d.cols;
   a.dst = (uint8_t*)tiled;
@@ -538,7 +542,8 @@ int pack_tiled(const blut_mat_desc& d, const blut_canon& c, void* tiled, cudaStr
   const int64_t n = d.rows * d.cols;
   pack_codes_kernel<<<std::min<unsigned>(grid1d(n, 256), 1u << 20), 256, 0, stream>>>(a);
   if (d.format != BLUT_FMT_DENSE) {
-    const int64_t nt = d.format == BLUT_FMT_R8 ? d.rows * L.nchunks : d.rows * (d.cols / d.group) * 16;
+    const int per_block = d.format == BLUT_FMT_NESTED ? 8 + 32 : 2 * (1 << d.bits);
+    const int64_t nt = d.format == BLUT_FMT_R8 ? d.rows * L.nchunks : d.rows * (d.cols / d.group) * per_block;
     pack_tables_kernel<<<std::min<unsigned>(grid1d(nt, 256), 1u << 20), 256, 0, stream>>>(a);
   }
   return cudaGetLastError() == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;

@@ -1,0 +1,176 @@
+"""Expert parallelism over the GPUs of one box (torch.distributed, NCCL).
+
+Experts shard naturally: rank r owns the contiguous expert range
+``expert_ranges(E, world)[r]`` of every layer (E=60 on 8 ranks -> 8,8,8,8,7,7,7,7),
+dense weights are replicated, and every rank routes its own decode batch.
+One layer:
+
+1. router on the rank's own tokens (global expert ids, weights, shared gate);
+2. dispatch: every token travels to every rank with its k slots rewritten to
+   that rank's local expert ids, -1 where the expert lives elsewhere
+   (fixed T rows per destination, so no count exchange is needed);
+   three ``all_to_all_single`` calls (activations, ids, weights);
+3. each rank runs its local experts on the N*T received tokens in one
+   ``blut_moe_forward`` (empty slots are skipped) with fp32 partial sums;
+4. combine: ``all_to_all_single`` sends the partials back; the owner sums the
+   N partials and adds its shared expert.
+
+These are the message shapes of the reference's only EP code (the DeepSeek
+remote code's dispatch/combine all_to_all, models/deepseek/modeling_deepseek.py:604-660).
+The exchange functions are device-agnostic (CPU tensors under gloo in the
+tests); the expert compute is the CUDA path.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from .formats import dense_matrix
+from .moe import LUTExperts, LUTMoELayer, SharedExpert, router
+
+
+def expert_ranges(num_experts: int, world: int) -> List[Tuple[int, int]]:
+    """Contiguous (start, count) per rank; the first E % world ranks get one more."""
+    base, extra = divmod(num_experts, world)
+    out, s = [], 0
+    for r in range(world):
+        c = base + (1 if r < extra else 0)
+        out.append((s, c))
+        s += c
+    return out
+
+
+def owner_tables(num_experts: int, world: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """owner[e] = rank of expert e, local[e] = e - start(owner)."""
+    owner = torch.empty(num_experts, dtype=torch.int32)
+    local = torch.empty(num_experts, dtype=torch.int32)
+    for r, (s, c) in enumerate(expert_ranges(num_experts, world)):
+        owner[s:s + c] = r
+        local[s:s + c] = torch.arange(c, dtype=torch.int32)
+    return owner.to(device), local.to(device)
+
+
+def build_dispatch(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, owner: torch.Tensor,
+                   local: torch.Tensor, world: int):
+    """Send buffers [world, T, ...]: x replicated, per-destination local ids (-1 elsewhere), weights."""
+    T, k = ids.shape
+    ids_l = ids.long()
+    own = owner[ids_l]                                             # [T, k]
+    loc = local[ids_l]                                             # [T, k]
+    dest = torch.arange(world, device=ids.device, dtype=own.dtype).view(world, 1, 1)
+    send_ids = torch.where(own.unsqueeze(0) == dest, loc.unsqueeze(0), torch.full_like(loc, -1).unsqueeze(0))
+    send_x = x.unsqueeze(0).expand(world, T, x.shape[1]).contiguous()
+    send_w = tw.float().unsqueeze(0).expand(world, T, k).contiguous()
+    return send_x, send_ids.to(torch.int32).contiguous(), send_w
+
+
+def exchange(send_x, send_ids, send_w, group=None):
+    """Dispatch all-to-all (equal splits): row block d of each buffer goes to rank d."""
+    recv_x, recv_ids, recv_w = torch.empty_like(send_x), torch.empty_like(send_ids), torch.empty_like(send_w)
+    dist.all_to_all_single(recv_x, send_x, group=group)
+    dist.all_to_all_single(recv_ids, send_ids, group=group)
+    dist.all_to_all_single(recv_w, send_w, group=group)
+    return recv_x, recv_ids, recv_w
+
+
+def combine(partials: torch.Tensor, group=None) -> torch.Tensor:
+    """Combine all-to-all: partials [world, T, H] (block d = tokens of rank d) -> summed [T, H]."""
+    back = torch.empty_like(partials)
+    dist.all_to_all_single(back, partials, group=group)
+    return back.sum(dim=0)
+
+
+class EPMoELayer:
+    """One MoE layer, expert-parallel: this rank's experts + replicated router and shared expert."""
+
+    def __init__(self, local_experts: LUTExperts, num_experts: int, top_k: int, router_w: torch.Tensor,
+                 shared: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, renorm: bool = False, group=None):
+        self.world = dist.get_world_size(group)
+        self.group = group
+        self.top_k = top_k
+        self.renorm = renorm
+        self.local = LUTMoELayer(local_experts, top_k)
+        self.router_w = router_w.to(local_experts.fmt.compute_dtype).contiguous()
+        self.num_experts = num_experts
+        self.owner, self.local_id = owner_tables(num_experts, self.world, router_w.device)
+        self.shared = None
+        if shared is not None:
+            s13, s2 = shared
+            ex = LUTExperts.from_quantized([dense_matrix(s13)], [dense_matrix(s2)])
+            self.shared = LUTMoELayer(ex, 1)
+            self._zero_ids = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        T, H = x.shape
+        ids, tw, sg = router(x, self.router_w, self.top_k, self.renorm, shared_gate=self.shared is not None)
+        sx, si, sw = build_dispatch(x, ids, tw, self.owner, self.local_id, self.world)
+        rx, ri, rw = exchange(sx, si, sw, self.group)
+        part = self.local.forward(rx.view(-1, H), ri.view(-1, self.top_k), rw.view(-1, self.top_k), out_f32=True)
+        out = combine(part.view(self.world, T, H), self.group)
+        if self.shared is not None:
+            if self._zero_ids is None or self._zero_ids.shape[0] != T:
+                self._zero_ids = torch.zeros(T, 1, dtype=torch.int32, device=x.device)
+            out += self.shared.forward(x, self._zero_ids, sg.view(T, 1), out_f32=True)
+        return out.to(x.dtype)
+
+    __call__ = forward
+
+
+def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, metric, shp):
+    """bench.py --gpus N: every rank owns E/N experts of each layer and a decode
+    batch of its own; value = total tokens of all ranks / max step time."""
+    import json
+
+    H, E, I, TOPK, IS = shp["H"], shp["E"], shp["I"], shp["TOPK"], shp["IS"]
+    s, c = expert_ranges(E, world)[rank]
+    fmt, layers = build_layers(a.layers, c, s, a.bits, a.group, dev)
+    eps = []
+    g = torch.Generator(device=dev).manual_seed(99)
+    for ex, rw, sh in layers:
+        s13 = (torch.randn(2 * IS, H, generator=g, device=dev) * 0.02).half()
+        s2 = (torch.randn(H, IS, generator=g, device=dev) * 0.02).half()
+        eps.append(EPMoELayer(ex, E, TOPK, rw, shared=(s13, s2)))
+    xs = make_inputs(a.layers, a.batch, rank, dev)
+
+    def step():
+        for m, x in zip(eps, xs):
+            m.forward(x)
+
+    for _ in range(max(2, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    for m in eps:
+        m.local.check_status()
+    dist.barrier()
+    clk = Clocks(torch.cuda.current_device())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0.record()
+    for _ in range(a.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = clk.stop()
+    ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    total_tokens = a.batch * world
+    peak, _ = peaks()
+    if rank == 0:
+        res = {"metric": metric, "value": total_tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+               "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+               "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU Lloyd-encoded; N(0,1) RMS-normalised fp16",
+               "config": {"workload": f"Qwen1.5-MoE-A2.7B MoE stack, decode batch {a.batch} per rank",
+                          "layers": a.layers, "global_batch": total_tokens, "experts": E, "top_k": TOPK,
+                          "format": f"BlockLUT {a.bits}-bit g{a.group}", "parallelism": f"ep{world}",
+                          "exchange": "NCCL all_to_all_single dispatch (x, ids, w) + combine (fp32 partials)"},
+               "roofline": None, "cpu_baseline": None, "e2e": None,
+               "gpu_launches": None, "clocks": clocks}
+        print(json.dumps(res), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()

@@ -64,11 +64,12 @@ class LUTFormat:
     def table_entries(self) -> int:
         return 4 if self.kind == "nested" else (1 << self.bits)
 
-    def desc(self, rows: int, cols: int) -> _lib.MatDesc:
+    def desc(self, rows: int, cols: int, paired: bool = False) -> _lib.MatDesc:
+        """C descriptor; ``paired`` selects the gate/up-paired tiled layout."""
         bits = {"r8": 8, "b": self.bits, "nested": 4, "dense": 16}[self.kind]
         group = 128 if self.kind == "r8" and self.group not in (128,) else self.group
-        return _lib.MatDesc(_KIND[self.kind], bits, group, self.tier, _dt_code(self.compute_dtype), 0,
-                            int(rows), int(cols))
+        return _lib.MatDesc(_KIND[self.kind], bits, group, self.tier, _dt_code(self.compute_dtype),
+                            _lib.LAYOUT_PAIRED if paired else 0, int(rows), int(cols))
 
     def bytes_per_weight(self) -> float:
         """Bytes the tiled layout streams per weight element (the roofline basis)."""
@@ -171,20 +172,32 @@ def tiled_bytes(fmt: LUTFormat, rows: int, cols: int) -> int:
     return int(n)
 
 
-def pack_tiled(mats, stream=None) -> tuple[torch.Tensor, int]:
+def pack_tiled(mats, stream=None, paired: bool = False) -> tuple[torch.Tensor, int]:
     """Repack canonical matrices (a list, all of one format and shape) into one
-    tiled buffer; returns (uint8 buffer, per-matrix stride in bytes)."""
+    tiled buffer; returns (uint8 buffer, per-matrix stride in bytes).
+    ``paired`` interleaves the row tiles of the two halves (gate/up)."""
     mats = list(mats)
     fmt, rows, cols = mats[0].fmt, mats[0].rows, mats[0].cols
     stride = tiled_bytes(fmt, rows, cols)
     dev = mats[0].codes.device
     buf = torch.empty(len(mats) * stride, dtype=torch.uint8, device=dev)
-    d = fmt.desc(rows, cols)
+    d = fmt.desc(rows, cols, paired)
     s = _lib.stream_ptr(stream)
     for i, m in enumerate(mats):
         c = m.canon()
         _lib.check(_lib.lib().blut_pack_tiled(C.byref(d), C.byref(c), buf.data_ptr() + i * stride, s), "pack_tiled")
     return buf, stride
+
+
+def dequant_tiled(fmt: LUTFormat, rows: int, cols: int, tiled: torch.Tensor, lut_table: Optional[torch.Tensor] = None,
+                  stream=None, paired: bool = False) -> torch.Tensor:
+    """Dense matrix rebuilt from one tiled matrix through the kernels' fragment lookups."""
+    out = torch.empty(rows, cols, dtype=fmt.compute_dtype, device=tiled.device)
+    d = fmt.desc(rows, cols, paired)
+    _lib.check(_lib.lib().blut_dequant_tiled(C.byref(d), tiled.data_ptr(),
+                                             None if lut_table is None else lut_table.data_ptr(), out.data_ptr(),
+                                             _lib.stream_ptr(stream)), "dequant_tiled")
+    return out
 
 
 def dense_matrix(w: torch.Tensor) -> QuantizedMatrix:

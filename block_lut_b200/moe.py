@@ -35,7 +35,7 @@ class LUTExperts:
                        lut_table: Optional[torch.Tensor] = None, stream=None) -> "LUTExperts":
         w13, w2 = list(w13), list(w2)
         fmt = w13[0].fmt
-        b13, s13 = pack_tiled(w13, stream)
+        b13, s13 = pack_tiled(w13, stream, paired=True)
         b2, s2 = pack_tiled(w2, stream)
         if fmt.kind == "r8":
             if lut_table is None:
@@ -62,10 +62,10 @@ class SharedExpert:
     def from_dense(cls, w13: torch.Tensor, w2: torch.Tensor, gate: Optional[torch.Tensor] = None,
                    stream=None) -> "SharedExpert":
         m13, m2 = dense_matrix(w13), dense_matrix(w2)
-        b13, _ = pack_tiled([m13], stream)
+        b13, _ = pack_tiled([m13], stream, paired=True)
         b2, _ = pack_tiled([m2], stream)
         g = None if gate is None else gate.reshape(-1).to(w13.dtype).contiguous()
-        return cls(w13.shape[0] // 2, b13, b2, m13.fmt.desc(*w13.shape), m2.fmt.desc(*w2.shape), g)
+        return cls(w13.shape[0] // 2, b13, b2, m13.fmt.desc(*w13.shape, paired=True), m2.fmt.desc(*w2.shape), g)
 
     def weight_bytes(self) -> float:
         """Bytes of the dense shared expert (gate, up and down, 2 bytes per weight)."""
@@ -109,7 +109,7 @@ class LUTMoELayer:
         a = _lib.MoEArgs()
         a.hidden, a.inter, a.num_experts, a.top_k = ex.hidden, ex.inter, ex.num_experts, self.top_k
         a.dtype = _lib.BF16 if self.dtype == torch.bfloat16 else _lib.F16
-        a.w13 = ex.fmt.desc(2 * ex.inter, ex.hidden)
+        a.w13 = ex.fmt.desc(2 * ex.inter, ex.hidden, paired=True)
         a.w2 = ex.fmt.desc(ex.hidden, ex.inter)
         a.w13_tiled, a.w2_tiled = ex.w13.data_ptr(), ex.w2.data_ptr()
         a.w13_stride, a.w2_stride = ex.w13_stride, ex.w2_stride
@@ -134,34 +134,19 @@ class LUTMoELayer:
 
     def forward(self, x: torch.Tensor, topk_ids: Optional[torch.Tensor] = None,
                 topk_weights: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                stream=None) -> torch.Tensor:
-        """out[t] = sum_j w[t,j] * expert_{ids[t,j]}(x_t) (+ shared(x_t)); x [T, H]."""
+                stream=None, out_f32: bool = False) -> torch.Tensor:
+        """out[t] = sum_j w[t,j] * expert_{ids[t,j]}(x_t) (+ shared(x_t)); x [T, H].
+
+        ``out_f32`` returns the unrounded float32 sums (expert-parallel partials).
+        """
         if not x.is_cuda:
             raise ValueError("LUTMoELayer.forward expects CUDA tensors (no CPU path)")
+        if out_f32:
+            return self._forward_f32(x, topk_ids, topk_weights, out, stream)
         in_dtype = x.dtype
-        x2 = x.reshape(-1, x.shape[-1])
-        if x2.dtype != self.dtype:
-            x2 = x2.to(self.dtype)
-        x2 = x2.contiguous()
+        x2, keep = self._prepare(x, topk_ids, topk_weights)
         T = x2.shape[0]
         a = self._args
-        a.num_tokens = T
-        a.x = x2.data_ptr()
-        keep = [x2]
-        if topk_ids is not None:
-            ids = topk_ids.reshape(T, -1)
-            if ids.dtype != torch.int32:
-                ids = ids.to(torch.int32)
-            tw = topk_weights.reshape(T, -1)
-            if tw.dtype != torch.float32:
-                tw = tw.to(torch.float32)
-            ids, tw = ids.contiguous(), tw.contiguous()
-            keep += [ids, tw]
-            a.topk_ids, a.topk_weights = ids.data_ptr(), tw.data_ptr()
-        else:
-            if self.router_w is None:
-                raise ValueError("no routing given and the layer has no router weights")
-            a.topk_ids = a.topk_weights = None
         if out is None or out.dtype != self.dtype:
             res = torch.empty(T, x2.shape[1], dtype=self.dtype, device=x2.device)
         else:
@@ -181,6 +166,50 @@ class LUTMoELayer:
         return res if in_dtype == self.dtype else res.to(in_dtype)
 
     __call__ = forward
+
+    def _prepare(self, x, topk_ids, topk_weights):
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.dtype != self.dtype:
+            x2 = x2.to(self.dtype)
+        x2 = x2.contiguous()
+        T = x2.shape[0]
+        a = self._args
+        a.num_tokens = T
+        a.x = x2.data_ptr()
+        keep = [x2]
+        if topk_ids is not None:
+            ids = topk_ids.reshape(T, -1)
+            ids = (ids if ids.dtype == torch.int32 else ids.to(torch.int32)).contiguous()
+            tw = topk_weights.reshape(T, -1)
+            tw = (tw if tw.dtype == torch.float32 else tw.to(torch.float32)).contiguous()
+            keep += [ids, tw]
+            a.topk_ids, a.topk_weights = ids.data_ptr(), tw.data_ptr()
+        else:
+            if self.router_w is None:
+                raise ValueError("no routing given and the layer has no router weights")
+            a.topk_ids = a.topk_weights = None
+        return x2, keep
+
+    def _forward_f32(self, x, topk_ids, topk_weights, out, stream):
+        x2, keep = self._prepare(x, topk_ids, topk_weights)
+        a = self._args
+        res = out if out is not None else torch.empty(x2.shape[0], x2.shape[1], dtype=torch.float32,
+                                                      device=x2.device)
+        if res.dtype != torch.float32 or not res.is_contiguous():
+            raise ValueError("out_f32 needs a contiguous float32 output")
+        a.out = res.data_ptr()
+        a.out_f32 = 1
+        try:
+            lib = _lib.lib()
+            need = lib.blut_moe_workspace_size(C.byref(a))
+            if need == 0:
+                raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
+            ws = workspace(x2.device, need)
+            _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
+                       "moe_forward")
+        finally:
+            a.out_f32 = 0
+        return res
 
     def check_status(self, stream=None) -> None:
         """Synchronise and raise if a kernel reported a device-side error."""

@@ -55,6 +55,8 @@ enum {
 
 enum { BLUT_F16 = 0, BLUT_BF16 = 1, BLUT_F32 = 2 };
 
+enum { BLUT_LAYOUT_PAIRED = 1 };
+
 /* Description of one weight matrix W [rows, cols] (y = W x, cols = K). */
 typedef struct {
   int32_t format; /* BLUT_FMT_*                                                  */
@@ -66,7 +68,9 @@ typedef struct {
                      FMT_NESTED: 0 full (coarse + residual), 1 coarse only       */
   int32_t dtype;  /* compute dtype of weights and activations: BLUT_F16 / BF16.
                      FMT_R8 computes in bf16, FMT_B / NESTED in fp16             */
-  int32_t reserved;
+  int32_t layout; /* tiled layout flags: BLUT_LAYOUT_PAIRED stores row tile t
+                     of the first half (gate) and tile t of the second half (up)
+                     next to each other; blut_moe_forward needs it on w13     */
   int64_t rows;   /* N: output features                                        */
   int64_t cols;   /* K: input features                                         */
 } blut_mat_desc;
@@ -134,6 +138,13 @@ BLUT_API int64_t blut_tiled_bytes(const blut_mat_desc* desc);
  * (load time; the tiled buffer is what blut_moe_forward streams). */
 BLUT_API int blut_pack_tiled(const blut_mat_desc* desc, const blut_canon* src, void* tiled, void* stream);
 
+/* Dense [rows][cols] matrix rebuilt from the tiled layout through the same
+ * fragment lookups the MoE kernels use (bf16 for FMT_R8, else fp16); equal
+ * bit for bit to blut_dequant of the canonical tensors.  Diagnostic entry
+ * point with no counterpart in the reference; lut_table is FMT_R8's table. */
+BLUT_API int blut_dequant_tiled(const blut_mat_desc* desc, const void* tiled, const void* lut_table, void* out,
+                                void* stream);
+
 /* ---------------------------------------------------------------- encode -- */
 
 /* Format B / NestedLUT encoder: per (row, block) 1-D Lloyd k-means (10
@@ -193,7 +204,11 @@ typedef struct {
   int64_t w2_stride;
   const void* lut_table;  /* FMT_R8: bf16 [256] tier table; NULL otherwise      */
   const void* x;          /* [T][H]                                             */
-  const int32_t* topk_ids;  /* [T][k]; NULL: route with router_w               */
+  const int32_t* topk_ids;  /* [T][k]; NULL: route with router_w.  An id of -1
+                               marks an empty slot (skipped; expert parallelism
+                               uses it for experts owned by other ranks); other
+                               ids outside [0, E) are skipped and reported by
+                               blut_moe_check_status                           */
   const float* topk_weights;/* [T][k]                                           */
   const void* router_w;     /* [E (+1 with shared gate)][H], used when topk_ids==NULL */
   int32_t renorm;           /* renormalise the top-k weights (router only)     */
@@ -210,6 +225,9 @@ typedef struct {
   void* const* prof_events; /* NULL, or 4 cudaEvent_t recorded on the stream
                                before/after the routed gate/up launch and
                                before/after the routed down launch (timing)   */
+  int32_t out_f32;          /* 1: out is float32 [T][H] (unrounded partial sums,
+                               used by expert parallelism); 0: out is `dtype` */
+  int32_t reserved2;
 } blut_moe_args;
 
 /* Workspace bytes blut_moe_forward needs for these arguments (0 on error). */

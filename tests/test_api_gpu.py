@@ -126,7 +126,7 @@ def test_deepseek_v2_moe_lut_forward():
     assert out.shape == x.shape
     # oracle: same encoded weights, the reference's _routing on fp64 logits
     xn = x.reshape(10, 256).float().cpu().numpy().astype(np.float64)
-    logits = xn @ m.gate.weight.float().cpu().numpy().astype(np.float64).T
+    logits = xn @ m.gate.weight.detach().float().cpu().numpy().astype(np.float64).T
     ids, tw = O.routing(logits, 2)
     tw_ref, ids_ref = _routing(torch.from_numpy(logits), 2)
     assert np.array_equal(ids_ref.numpy(), ids)

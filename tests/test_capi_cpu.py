@@ -66,7 +66,7 @@ def _args(**kw):
     fmt = LUTFormat("b", 4, 64)
     a = _lib.MoEArgs()
     a.num_tokens, a.hidden, a.inter, a.num_experts, a.top_k, a.dtype = 8, 2048, 1408, 60, 4, _lib.F16
-    a.w13, a.w2 = fmt.desc(2816, 2048), fmt.desc(2048, 1408)
+    a.w13, a.w2 = fmt.desc(2816, 2048, paired=True), fmt.desc(2048, 1408)
     a.w13_tiled = a.w2_tiled = a.x = a.out = 1 << 20
     a.w13_stride, a.w2_stride = tiled_bytes(fmt, 2816, 2048), tiled_bytes(fmt, 2048, 1408)
     a.topk_ids = a.topk_weights = 1 << 21

@@ -138,3 +138,40 @@ def test_dequant_rejects_bad_args():
     d = fmt.desc(16, 100)  # cols not a multiple of the group
     c = _lib.Canon(1 << 20, None, 1 << 20, None, None)
     assert _lib.lib().blut_dequant(C.byref(d), C.byref(c), 1 << 20, None) == _lib.BLUT_ERR_UNSUPPORTED
+
+
+TILED_FORMATS = [LUTFormat("b", b, g) for b in (2, 3, 4) for g in (32, 64, 128)] + \
+    [LUTFormat("nested", 4, g, t) for g in (32, 64, 128) for t in (0, 1)]
+
+
+@pytest.mark.parametrize("paired", [False, True])
+@pytest.mark.parametrize("fmt", TILED_FORMATS, ids=lambda f: f"{f.kind}{f.bits}g{f.group}t{f.tier}")
+def test_tiled_layout_lookup_bit_exact(fmt, paired):
+    """pack_tiled + the MoE kernels' fragment lookups reproduce the canonical dequant exactly."""
+    from block_lut_b200.formats import dequant_tiled, pack_tiled
+    rng = np.random.Generator(np.random.PCG64(fmt.bits * 100 + fmt.group + fmt.tier))
+    rows, cols = 64, 384
+    w = O.student_t_weights(rng, (rows, cols))
+    qm = encode(cuda(w), fmt)
+    ref = dequant(qm)
+    buf, _ = pack_tiled([qm], paired=paired)
+    out = dequant_tiled(fmt, rows, cols, buf, paired=paired)
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("tier", [0, 1, 2])
+def test_tiled_layout_r8_and_dense(tier):
+    from block_lut_b200.formats import dense_matrix, dequant_tiled, pack_tiled
+    rng = np.random.Generator(np.random.PCG64(40 + tier))
+    rows, cols = 32, 256
+    idx = rng.integers(0, 256, rows * cols, dtype=np.uint8)
+    am = O.f32_to_bf16(rng.uniform(0.01, 0.1, rows * cols // 128).astype(np.float32))
+    tab = bf16_tensor(O.f32_to_bf16(rng.uniform(-1, 1, 256).astype(np.float32)))
+    fmt = LUTFormat("r8", 8, 128, tier)
+    qm = QuantizedMatrix(fmt, rows, cols, cuda(idx), tab, scales=bf16_tensor(am))
+    buf, _ = pack_tiled([qm])
+    out = dequant_tiled(fmt, rows, cols, buf, tab)
+    assert torch.equal(out.view(torch.int16), dequant(qm).view(torch.int16))
+    dm = dense_matrix(torch.from_numpy(rng.standard_normal((rows, cols)).astype(np.float16)).cuda())
+    dbuf, _ = pack_tiled([dm])
+    assert torch.equal(dequant_tiled(dm.fmt, rows, cols, dbuf), dm.codes)

@@ -1,0 +1,128 @@
+"""Expert-parallel host logic on CPU: two gloo ranks run the dispatch /
+combine exchange of block_lut_b200.ep, with the oracle standing in for the
+CUDA expert compute, and must reproduce the single-process layer output.
+A rank that fails before the exchange makes its peer's collective raise
+(short process-group timeout) instead of hanging."""
+import multiprocessing as mp
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+E, H, I, K, T = 6, 32, 16, 2, 5
+
+
+def _weights():
+    rng = np.random.Generator(np.random.PCG64(123))
+    W13 = [rng.standard_normal((2 * I, H)).astype(np.float32) * 0.1 for _ in range(E)]
+    W2 = [rng.standard_normal((H, I)).astype(np.float32) * 0.1 for _ in range(E)]
+    return W13, W2
+
+
+def _tokens(rank):
+    from oracle import blut_oracle as O
+    rng = np.random.Generator(np.random.PCG64(7 + rank))
+    x = O.rms_activations(rng, T, H)
+    ids, tw = O.routing(rng.standard_normal((T, E)).astype(np.float32), K)
+    return x, ids, tw
+
+
+def _local_partial(x, ids, tw, W13, W2, start):
+    """Oracle compute of this rank's experts on received tokens (-1 slots skipped)."""
+    from oracle import blut_oracle as O
+    out = np.zeros((x.shape[0], H), dtype=np.float64)
+    for e in np.unique(ids):
+        if e < 0:
+            continue
+        tok, slot = np.nonzero(ids == e)
+        w13, w2 = W13[start + e].astype(np.float64), W2[start + e].astype(np.float64)
+        h = x[tok].astype(np.float64) @ w13.T
+        a = O.round_to((O.silu(h[:, :I]) * h[:, I:]).astype(np.float32), "f16").astype(np.float64)
+        out[tok] += tw[tok, slot][:, None].astype(np.float64) * (a @ w2.T)
+    return out
+
+
+def _rank_main(rank, world, port, q, fail_rank):
+    try:
+        import sys
+        from datetime import timedelta
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        import torch
+        import torch.distributed as dist
+        from block_lut_b200 import ep
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+        if rank == fail_rank:
+            raise RuntimeError("injected failure before the exchange")
+        W13, W2 = _weights()
+        x, ids, tw = _tokens(rank)
+        owner, local = ep.owner_tables(E, world, "cpu")
+        sx, si, sw = ep.build_dispatch(torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(tw),
+                                       owner, local, world)
+        try:
+            rx, ri, rw = ep.exchange(sx, si, sw)
+        except Exception as exc:  # the peer died: the collective must fail, not hang
+            q.put((rank, "collective-error", type(exc).__name__))
+            return
+        start = ep.expert_ranges(E, world)[rank][0]
+        part = _local_partial(rx.view(-1, H).numpy(), ri.view(-1, K).numpy(), rw.view(-1, K).numpy(), W13, W2, start)
+        out = ep.combine(torch.from_numpy(part).view(world, T, H))
+        q.put((rank, "ok", out.numpy()))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "raised", traceback.format_exc()))
+
+
+def _run(world, fail_rank=-1):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank_main, args=(r, world, port, q, fail_rank)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, status, payload = q.get(timeout=120)
+        res[r] = (status, payload)
+    for p in ps:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return res
+
+
+def test_expert_ranges():
+    from block_lut_b200.ep import expert_ranges
+    assert [c for _, c in expert_ranges(60, 8)] == [8, 8, 8, 8, 7, 7, 7, 7]
+    assert expert_ranges(128, 8) == [(16 * r, 16) for r in range(8)]
+    assert sum(c for _, c in expert_ranges(64, 3)) == 64
+
+
+def test_ep_dispatch_combine_matches_single_process():
+    from oracle import blut_oracle as O
+    res = _run(2)
+    W13, W2 = _weights()
+    for r in (0, 1):
+        status, out = res[r]
+        assert status == "ok", out
+        x, ids, tw = _tokens(r)
+        ref = O.moe_forward(x, ids, tw, W13, W2, act_dtype="f16")
+        np.testing.assert_allclose(out, ref, rtol=1e-9, atol=1e-12)
+
+
+def test_rank_failure_surfaces_as_error_not_hang():
+    res = _run(2, fail_rank=1)
+    assert res[1][0] == "raised" and "injected failure" in res[1][1]
+    assert res[0][0] == "collective-error", res[0]

@@ -154,10 +154,11 @@ def test_shared_expert_modes_and_graph_capture():
         sh = SharedExpert.from_dense(cuda(s13), cuda(s2), cuda(gate) if mode else None)
         layer = LUTMoELayer(experts, 2, shared=sh, shared_gate_mode=mode)
         out = layer.forward(x, cuda(ids), cuda(tw))
-        ref = O.moe_forward(x.float().cpu().numpy(), ids, tw, W13, W2, act_dtype="f16",
-                            shared13=s13.astype(np.float32), shared2=s2.astype(np.float32),
-                            shared_gate=gate.astype(np.float32) if mode else None)
-        if mode == 0:  # unscaled shared output
+        if mode == 1:
+            ref = O.moe_forward(x.float().cpu().numpy(), ids, tw, W13, W2, act_dtype="f16",
+                                shared13=s13.astype(np.float32), shared2=s2.astype(np.float32),
+                                shared_gate=gate.astype(np.float32))
+        else:  # unscaled shared output
             xs = x.float().cpu().numpy().astype(np.float64)
             h = xs @ s13.astype(np.float64).T
             a = O.round_to((O.silu(h[:, :128]) * h[:, 128:]).astype(np.float32), "f16").astype(np.float64)
@@ -217,3 +218,39 @@ def test_deterministic_and_invalid_ids_reported():
     with pytest.raises(RuntimeError, match="invalid"):
         layer.check_status()
     layer.check_status()  # the status word was cleared by the read
+
+
+def test_qwen15_layer_decode_batch32_bench_shape():
+    """The bench's layer at its decode batch (config 2: batch 32), router + shared expert."""
+    H, I, E, k, Is, T = 2048, 1408, 60, 4, 5632, 32
+    fmt = LUTFormat("b", 4, 64)
+    torch.manual_seed(1)
+    st = torch.distributions.StudentT(torch.tensor(5.0, device="cuda"))
+    scale = 0.02 / (5.0 / 3.0) ** 0.5
+    q13 = [encode(st.sample((2 * I, H)) * scale, fmt) for _ in range(E)]
+    q2 = [encode(st.sample((H, I)) * scale, fmt) for _ in range(E)]
+    g = torch.Generator(device="cuda").manual_seed(3)
+    router_w = (torch.randn(E + 1, H, generator=g, device="cuda") * 0.02).half()
+    s13 = (torch.randn(2 * Is, H, generator=g, device="cuda") * 0.02).half()
+    s2 = (torch.randn(H, Is, generator=g, device="cuda") * 0.02).half()
+    layer = LUTMoELayer(LUTExperts.from_quantized(q13, q2), k, router_w=router_w,
+                        shared=SharedExpert.from_dense(s13, s2), shared_gate_mode=1)
+    x = torch.randn(T, H, generator=g, device="cuda")
+    x = (x / x.pow(2).mean(dim=1, keepdim=True).sqrt()).half()
+    out = torch.empty_like(x)
+    layer.forward(x, out=out)
+    torch.cuda.synchronize()
+    layer.check_status()
+    xn = x.float().cpu().numpy()
+    rw = router_w.float().cpu().numpy()
+    logits = xn.astype(np.float64) @ rw[:E].T.astype(np.float64)
+    ids, tw = O.routing(logits, k)
+    srt = np.sort(logits, axis=1)
+    keep = srt[:, -k] - srt[:, -k - 1] > 1e-4
+
+    def deq(lst, e):
+        m = lst[e]
+        return O.dequant_b(m.codes.cpu().numpy(), m.tables.cpu().numpy(), 4, 64).astype(np.float32)
+    ref = O.moe_forward(xn, ids, tw, lambda e: deq(q13, e), lambda e: deq(q2, e), act_dtype="f16",
+                        shared13=s13.float().cpu().numpy(), shared2=s2.float().cpu().numpy(), shared_gate=rw[E])
+    check_layer(out[torch.from_numpy(keep).cuda()], ref[keep], torch.float16, "bench-shaped layer")
