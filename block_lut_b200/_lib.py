@@ -67,7 +67,7 @@ SIGNATURES = [
     ("blut_encode", C.c_int, [C.POINTER(MatDesc), _VP, _VP, _VP, _VP, _VP, _VP]),
     ("blut_encode_r", C.c_int, [_VP, _I64, _VP, _I32, _VP, _VP, _VP]),
     ("blut_lut_gemv", C.c_int, [_VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _VP]),
-    ("blut_router", C.c_int, [_VP, _VP, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _VP, _VP, _VP, _VP]),
+    ("blut_router", C.c_int, [_VP, _VP, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _VP, _VP, _VP, _VP, _VP]),
     ("blut_moe_workspace_size", C.c_size_t, [C.POINTER(MoEArgs)]),
     ("blut_moe_forward", C.c_int, [C.POINTER(MoEArgs), _VP, C.c_size_t, _VP]),
     ("blut_moe_check_status", C.c_int, [_VP, _VP]),

@@ -79,9 +79,9 @@ int blut_lut_gemv(const void* x_bf16, const void* idx_u8, const void* codebook_b
 
 int blut_router(const void* x, const void* w_router, int32_t num_tokens, int32_t hidden, int32_t num_experts,
                 int32_t top_k, int32_t renorm, int32_t has_shared_gate, int32_t dtype, int32_t* topk_ids,
-                float* topk_weights, float* shared_gate, void* stream) {
+                float* topk_weights, float* shared_gate, float* logits, void* stream) {
   return router(x, w_router, num_tokens, hidden, num_experts, top_k, renorm, has_shared_gate, dtype, topk_ids,
-                topk_weights, shared_gate, S(stream));
+                topk_weights, shared_gate, logits, S(stream));
 }
 
 size_t blut_moe_workspace_size(const blut_moe_args* args) {

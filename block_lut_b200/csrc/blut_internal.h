@@ -30,6 +30,7 @@ struct MoEWs {
   int32_t* ids;
   float* tw;
   float* sg;
+  float* logits;  // [T][E (+1)] router logits (fp32)
   PlanPtrs pp;
   uint8_t *xf, *af, *xfs, *afs;
   float *y, *ys;
@@ -42,7 +43,7 @@ int validate_moe(const blut_moe_args& a);
 int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaStream_t stream);
 int moe_launch_count(const blut_moe_args& a);
 int router(const void* x, const void* w, int T, int H, int E, int K, int renorm, int has_sg, int dtype,
-           int32_t* ids, float* tw, float* sg, cudaStream_t stream);
+           int32_t* ids, float* tw, float* sg, float* logits, cudaStream_t stream);
 
 // LUT matmul dispatch over formats (blut_mm_inst_*.cu).
 cudaError_t launch_lut_mm(const blut_mat_desc& d, bool pair, const MMParams& p, int sms, cudaStream_t stream);

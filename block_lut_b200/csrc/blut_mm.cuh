@@ -28,7 +28,7 @@
 
 namespace blut {
 
-constexpr int kMaxConsumers = 4;
+constexpr int kMaxConsumers = 6;
 constexpr int kRingBudget = 96 * 1024;       // shared-memory ring bytes per CTA
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
@@ -105,8 +105,115 @@ __device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity) {
   }
 }
 
+// Per-CTA state a consumer warp needs for the ring.
+struct ConsumerCtx {
+  uint8_t* ring;
+  int stage_bytes;
+  int S;
+  int boff;
+  int qoff[3];
+  uint64_t* full;
+  uint64_t* empty;
+  volatile int* abort_flag;
+  int cw;
+  int lane;
+  PolExtra ex;
+};
+
+// One work item of one consumer warp: the whole K loop for its unit with NTV
+// n-tiles of tokens, then the epilogue.  n is the ring step of the item's
+// first chunk.
+template <class Pol, bool kPair, int NTV>
+__device__ __forceinline__ void consume_item(const MMParams& p, const ConsumerCtx& x, int64_t item, int ipg,
+                                             int64_t n) {
+  constexpr int NTL = kPair ? 2 : 1;
+  const int gi = (int)(item / ipg);
+  const int u0 = (int)(item % ipg) * p.W;
+  const int nu = min(p.W, p.units - u0);
+  const int ntok = p.gt.ntok[gi];
+  const int nt0 = p.gt.nt0[gi];
+  const bool mine = x.cw < nu;
+  const int lane = x.lane;
+  // byte offsets of this warp's tile planes inside a stage (fixed for the item)
+  int toff[NTL][3];
+#pragma unroll
+  for (int t = 0; t < NTL; ++t)
+#pragma unroll
+    for (int q = 0; q < 3; ++q) toff[t][q] = x.qoff[q] + (x.cw * NTL + t) * p.piece[q];
+  const int boff = x.boff + lane * 64;
+
+  float acc[NTL][NTV][4];
+#pragma unroll
+  for (int t = 0; t < NTL; ++t)
+#pragma unroll
+    for (int i = 0; i < NTV; ++i)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[t][i][r] = 0.f;
+
+  for (int c = 0; c < p.nchunks; ++c, ++n) {
+    const int slot = (int)(n % x.S);
+    bool ok = wait_or_abort(smem_u32(x.full + slot), (uint32_t)((n / x.S) & 1), x.abort_flag, p.status);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (ok && mine) {
+      const uint8_t* st = x.ring + (int64_t)slot * x.stage_bytes;
+      Pol P[NTL];
+#pragma unroll
+      for (int t = 0; t < NTL; ++t) {
+        const uint8_t* planes[3] = {st + toff[t][0], st + toff[t][1], st + toff[t][2]};
+        P[t].begin(planes, lane, x.ex);
+      }
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+        uint4 b[NTV];
+#pragma unroll
+        for (int i = 0; i < NTV; ++i) b[i] = lds128(st + boff + i * kBfragChunkBytes + sp * 16);
+        if ((2 * sp) % Pol::kSlabsPerBlock == 0) {
+#pragma unroll
+          for (int t = 0; t < NTL; ++t) P[t].block((2 * sp) / Pol::kSlabsPerBlock);
+        }
+#pragma unroll
+        for (int t = 0; t < NTL; ++t) {
+          uint32_t a0[4], a1[4];
+          P[t].frag2(sp, a0, a1);
+#pragma unroll
+          for (int i = 0; i < NTV; ++i) mma16816<Pol::kBF16>(acc[t][i], a0, b[i].x, b[i].y);
+#pragma unroll
+          for (int i = 0; i < NTV; ++i) mma16816<Pol::kBF16>(acc[t][i], a1, b[i].z, b[i].w);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(x.empty + slot));
+  }
+
+  if (!mine) return;
+  const int u = u0 + x.cw;  // logical unit: I-tile of the pair, or H-tile
+  const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int i = 0; i < NTV; ++i) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int row = g + 8 * (r >> 1);
+      const int tok = 2 * tq + (r & 1);
+      const bool valid = i * kNTile + tok < ntok;
+      if constexpr (kPair) {
+        const float val = valid ? silu_f(acc[0][i][r]) * acc[1][i][r] : 0.f;
+        const int col = u * kTileRows + row;  // K index of the next projection
+        uint8_t* dst = p.act_out + ((int64_t)(nt0 + i) * p.out_nchunks + (col >> 7)) * kBfragChunkBytes +
+                       bfrag_byte(tok, col & 127);
+        *reinterpret_cast<uint16_t*>(dst) = f32_to_act<Pol::kBF16>(val);
+      } else {
+        if (valid) {
+          const int slot = p.gt.slot0[gi] + i * kNTile + tok;
+          p.y_out[(int64_t)slot * p.y_ld + u * kTileRows + row] = acc[0][i][r];
+        }
+      }
+    }
+  }
+}
+
 template <class Pol, bool kPair>
-__global__ void __launch_bounds__(32 * (kMaxConsumers + 1)) lut_mm_kernel(const MMParams p) {
+__global__ void __launch_bounds__(32 * (kMaxConsumers + 1), 2) lut_mm_kernel(const MMParams p) {
   constexpr int NTL = kPair ? 2 : 1;
   constexpr int kR8Bytes = mm_r8_smem<Pol>();
   extern __shared__ __align__(128) uint8_t smem[];
@@ -195,95 +302,18 @@ __global__ void __launch_bounds__(32 * (kMaxConsumers + 1)) lut_mm_kernel(const 
   PolExtra ex;
   ex.r8_table = r8tab;
   ex.r8_mask = p.r8_mask;
+  ConsumerCtx ctx{ring, stage_bytes, S, boff, {qoff[0], qoff[1], qoff[2]}, full, empty, abort_flag, cw, lane, ex};
   int64_t n = 0;
   for (int64_t item = i0; item < i1; ++item) {
     const int gi = (int)(item / ipg);
-    const int u0 = (int)(item % ipg) * W;
-    const int nu = min(W, p.units - u0);
-    const int ntok = p.gt.ntok[gi];
-    const int ntv = (ntok + kNTile - 1) / kNTile;
-    const int nt0 = p.gt.nt0[gi];
-    const bool mine = cw < nu;
-
-    float acc[NTL][kMaxNT][4];
-#pragma unroll
-    for (int t = 0; t < NTL; ++t)
-#pragma unroll
-      for (int i = 0; i < kMaxNT; ++i)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[t][i][r] = 0.f;
-
-    for (int c = 0; c < p.nchunks; ++c, ++n) {
-      const int slot = (int)(n % S);
-      bool ok = wait_or_abort(smem_u32(full + slot), (uint32_t)((n / S) & 1), abort_flag, p.status);
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (ok && mine) {
-        const uint8_t* st = ring + (int64_t)slot * stage_bytes;
-        Pol P[NTL];
-#pragma unroll
-        for (int t = 0; t < NTL; ++t) {
-          const int lt = cw * NTL + t;
-          const uint8_t* planes[3];
-#pragma unroll
-          for (int q = 0; q < Pol::kNumPlanes; ++q) planes[q] = st + qoff[q] + lt * p.piece[q];
-          P[t].begin(planes, lane, ex);
-        }
-        const uint8_t* bsrc = st + boff + lane * 64;
-#pragma unroll
-        for (int sp = 0; sp < 4; ++sp) {
-          uint4 b[kMaxNT];
-#pragma unroll
-          for (int i = 0; i < kMaxNT; ++i) {
-            if (i < ntv) b[i] = lds128(bsrc + i * kBfragChunkBytes + sp * 16);
-          }
-#pragma unroll
-          for (int s2 = 0; s2 < 2; ++s2) {
-            const int s = 2 * sp + s2;
-            if (s % Pol::kSlabsPerBlock == 0) {
-#pragma unroll
-              for (int t = 0; t < NTL; ++t) P[t].block(s / Pol::kSlabsPerBlock);
-            }
-#pragma unroll
-            for (int t = 0; t < NTL; ++t) {
-              uint32_t a[4];
-              P[t].frag(s, a);
-#pragma unroll
-              for (int i = 0; i < kMaxNT; ++i) {
-                if (i < ntv) mma16816<Pol::kBF16>(acc[t][i], a, s2 ? b[i].z : b[i].x, s2 ? b[i].w : b[i].y);
-              }
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(empty + slot));
+    const int ntv = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
+    switch (ntv) {  // the n-tile count is fixed per item: one branch-free instance each
+      case 1: consume_item<Pol, kPair, 1>(p, ctx, item, ipg, n); break;
+      case 2: consume_item<Pol, kPair, 2>(p, ctx, item, ipg, n); break;
+      case 3: consume_item<Pol, kPair, 3>(p, ctx, item, ipg, n); break;
+      default: consume_item<Pol, kPair, 4>(p, ctx, item, ipg, n); break;
     }
-
-    if (!mine) continue;
-    const int u = u0 + cw;  // logical unit: I-tile of the pair, or H-tile
-    const int g = lane >> 2, tq = lane & 3;
-#pragma unroll
-    for (int i = 0; i < kMaxNT; ++i) {
-      if (i >= ntv) break;
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int row = g + 8 * (r >> 1);
-        const int tok = 2 * tq + (r & 1);
-        const bool valid = i * kNTile + tok < ntok;
-        if constexpr (kPair) {
-          const float val = valid ? silu_f(acc[0][i][r]) * acc[1][i][r] : 0.f;
-          const int col = u * kTileRows + row;  // K index of the next projection
-          uint8_t* dst = p.act_out + ((int64_t)(nt0 + i) * p.out_nchunks + (col >> 7)) * kBfragChunkBytes +
-                         bfrag_byte(tok, col & 127);
-          *reinterpret_cast<uint16_t*>(dst) = f32_to_act<Pol::kBF16>(val);
-        } else {
-          if (valid) {
-            const int slot = p.gt.slot0[gi] + i * kNTile + tok;
-            p.y_out[(int64_t)slot * p.y_ld + u * kTileRows + row] = acc[0][i][r];
-          }
-        }
-      }
-    }
+    n += p.nchunks;
   }
 }
 
@@ -296,7 +326,7 @@ inline int mm_smem_bytes(const MMParams& p) {
 template <class Pol, bool kPair>
 inline cudaError_t launch_mm(MMParams p, int num_sms, cudaStream_t stream) {
   const int stage = mm_stage_bytes(p, kPair ? 2 : 1);
-  p.stages = std::max(2, std::min(8, kRingBudget / stage));
+  p.stages = std::max(3, std::min(8, kRingBudget / stage));
   const int smem = mm_smem_bytes<Pol, kPair>(p);
   const int threads = 32 * (p.W + 1);
   auto kern = lut_mm_kernel<Pol, kPair>;

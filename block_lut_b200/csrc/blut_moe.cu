@@ -12,64 +12,79 @@
 namespace blut {
 
 // --------------------------------------------------------------- router ---
-// One CTA per token: logits of all experts (+ the shared-expert gate row),
-// softmax, top-k with lowest-index tie-breaking, optional renormalisation.
+// Router logits, fp32 accumulation: one warp per (row, token) dot product,
+// 8 warps per CTA; each lane issues all of its 16-byte loads before the FMAs
+// (4 independent accumulators).  Row r < E reads w_main[r]; row E (when
+// w_gate is set) reads the shared-expert gate vector.
 template <bool BF16>
-__global__ void __launch_bounds__(256) router_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
-                                                     int hidden, int num_experts, int top_k, int renorm,
-                                                     int has_sg, int do_topk, int32_t* __restrict__ ids,
-                                                     float* __restrict__ tw, float* __restrict__ sg) {
-  extern __shared__ float logits[];
-  const int t = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows = (do_topk ? num_experts : 0) + (has_sg ? 1 : 0);
-  const uint16_t* xr = x + (int64_t)t * hidden;
-  for (int rr = warp; rr < rows; rr += 8) {
-    const int r = do_topk ? rr : num_experts;  // gate-only mode reads row E
-    const uint16_t* wr = w + (int64_t)r * hidden;
-    float acc = 0.f;
-    for (int k = lane * 8; k < hidden; k += 256) {
-      const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
-      const uint4 wv = *reinterpret_cast<const uint4*>(wr + k);
-      const uint16_t* xs = reinterpret_cast<const uint16_t*>(&xv);
-      const uint16_t* ws = reinterpret_cast<const uint16_t*>(&wv);
+__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
+                                                            const uint16_t* __restrict__ w_main,
+                                                            const uint16_t* __restrict__ w_gate, int T, int H,
+                                                            int E, float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31;
+  const int R = E + (w_gate ? 1 : 0);
+  const int64_t task = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (task >= (int64_t)R * T) return;
+  const int t = (int)(task / R), r = (int)(task % R);
+  const uint16_t* wr = r < E ? w_main + (int64_t)r * H : w_gate;
+  const uint16_t* xr = x + (int64_t)t * H;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = lane * 8; k0 < H; k0 += 32 * 8 * 4) {
+    uint4 xv[4], wv[4];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc = fmaf(act_to_f32<BF16>(xs[q]), act_to_f32<BF16>(ws[q]), acc);
+    for (int q = 0; q < 4; ++q) {
+      const int k = k0 + q * 256;
+      xv[q] = k < H ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
+      wv[q] = k < H ? *reinterpret_cast<const uint4*>(wr + k) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) logits[rr] = acc;
+    for (int q = 0; q < 4; ++q) {
+      const uint16_t* xs = reinterpret_cast<const uint16_t*>(&xv[q]);
+      const uint16_t* ws = reinterpret_cast<const uint16_t*>(&wv[q]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[q] = fmaf(act_to_f32<BF16>(xs[e]), act_to_f32<BF16>(ws[e]), acc[q]);
+    }
   }
-  __syncthreads();
-  if (warp != 0) return;
-  if (has_sg) {
-    const float z = logits[rows - 1];
-    if (lane == 0) sg[t] = 1.f / (1.f + expf(-z));
-  }
-  if (!do_topk) return;
+  float s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) logits[(int64_t)t * R + r] = s;
+}
+
+// Softmax over E logits (fp32) and top-k with the lowest expert index winning
+// ties, optional renormalisation; one warp per token.  Row R-1 of a logits
+// row with a gate entry yields sigmoid(logit) in *sg.
+template <int kPer>  // expert logits per lane: E <= 32 * kPer
+__device__ void warp_topk_n(const float* __restrict__ lg, int E, int K, int renorm, int32_t* ids, float* tw) {
+  const int lane = threadIdx.x & 31;
+  float v[kPer];
   float mx = -INFINITY;
-  for (int e = lane; e < num_experts; e += 32) mx = fmaxf(mx, logits[e]);
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? lg[e] : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float sum = 0.f;
-  for (int e = lane; e < num_experts; e += 32) {
-    const float v = expf(logits[e] - mx);
-    logits[e] = v;
-    sum += v;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? expf(v[i] - mx) : -1.f;
+    sum += e < E ? v[i] : 0.f;
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  __syncwarp();
   const float inv = 1.f / sum;
-  float wsum = 0.f;
-  float myw = 0.f;
+  float wsum = 0.f, myw = 0.f;
   int myid = 0;
-  for (int j = 0; j < top_k; ++j) {
+  for (int j = 0; j < K; ++j) {
     float best = -1.f;
     int bi = 0x7fffffff;
-    for (int e = lane; e < num_experts; e += 32) {
-      const float v = logits[e];
-      if (v > best) { best = v; bi = e; }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      if (v[i] > best) { best = v[i]; bi = lane + 32 * i; }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
@@ -80,55 +95,128 @@ __global__ void __launch_bounds__(256) router_kernel(const uint16_t* __restrict_
     const float p = best * inv;
     wsum += p;
     if (lane == j) { myw = p; myid = bi; }
-    if (lane == (bi & 31)) logits[bi] = -2.f;  // taken
-    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      if (lane + 32 * i == bi) v[i] = -2.f;  // taken
+    }
   }
-  if (lane < top_k) {
-    ids[(int64_t)t * top_k + lane] = myid;
-    tw[(int64_t)t * top_k + lane] = renorm ? myw / wsum : myw;
+  if (lane < K) {
+    ids[lane] = myid;
+    tw[lane] = renorm ? myw / wsum : myw;
   }
 }
 
+__device__ void warp_topk(const float* __restrict__ lg, int E, int K, int renorm, int32_t* ids, float* tw,
+                          float* sg_out, bool has_gate) {
+  if (has_gate && (threadIdx.x & 31) == 0) *sg_out = 1.f / (1.f + expf(-lg[E]));
+  if (K <= 0) return;
+  if (E <= 64) warp_topk_n<2>(lg, E, K, renorm, ids, tw);
+  else if (E <= 128) warp_topk_n<4>(lg, E, K, renorm, ids, tw);
+  else if (E <= 256) warp_topk_n<8>(lg, E, K, renorm, ids, tw);
+  else warp_topk_n<kMaxExperts / 32>(lg, E, K, renorm, ids, tw);
+}
+
+// Standalone top-k over router logits (the blut_router entry point).
+__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int T, int E, int K,
+                                                   int renorm, int has_gate, int32_t* __restrict__ ids,
+                                                   float* __restrict__ tw, float* __restrict__ sg) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const int R = E + (has_gate ? 1 : 0);
+  warp_topk(logits + (int64_t)t * R, E, K, renorm, ids + (int64_t)t * K, tw + (int64_t)t * K,
+            has_gate ? sg + t : nullptr, has_gate != 0);
+}
+
 // ----------------------------------------------------------------- plan ---
-// Single CTA: per-expert counts, slots (tokens of an expert are contiguous,
-// in (token, k) order), groups of <= 32 tokens and their 8-token n-tiles;
-// also the shared expert's groups (identity slots).
-__global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ ids, int num_tokens, int top_k,
-                                                     int num_experts, int has_shared, PlanPtrs pp) {
+// Single CTA.  (1) With router logits: top-k per token (a warp per token)
+// and the shared-expert gate.  (2) Per-expert counts; parallel exclusive
+// scans give each expert its slot range, its groups of <= 32 tokens and their
+// 8-token n-tiles (ceil(count / 8) of them).  (3) Slots are taken with
+// per-expert atomic counters: which slot a (token, k) pair gets inside its
+// expert does not change any result, because every token is its own MMA
+// column.  (4) The shared expert's groups cover the tokens in order.
+__global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ ids_in,
+                                                    const float* __restrict__ logits, int topk_e, int R,
+                                                    int num_tokens, int top_k, int num_experts, int renorm,
+                                                    int has_gate, int has_shared, PlanPtrs pp,
+                                                    int32_t* __restrict__ ids_out, float* __restrict__ tw_out,
+                                                    float* __restrict__ sg_out) {
   __shared__ int cnt[kMaxExperts];
   __shared__ int off[kMaxExperts];
+  __shared__ int goff[kMaxExperts];
+  __shared__ int toff[kMaxExperts];
+  __shared__ int fill[kMaxExperts];
+  __shared__ int tot[3];
   const int S = num_tokens * top_k;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) *pp.status = 0;
-  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) cnt[e] = 0;
+  if (logits) {  // row t: topk_e expert logits, then the gate logit when has_gate
+    for (int t = warp; t < num_tokens; t += 32) {
+      warp_topk(logits + (int64_t)t * R, topk_e, ids_in ? 0 : top_k, renorm, ids_out + (int64_t)t * top_k,
+                tw_out + (int64_t)t * top_k, sg_out + t, has_gate != 0);
+    }
+  }
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
+    cnt[e] = 0;
+    fill[e] = 0;
+  }
   __syncthreads();
+  const int32_t* ids = ids_in ? ids_in : ids_out;
   for (int q = threadIdx.x; q < S; q += blockDim.x) {
     const int e = ids[q];
     if (e >= 0 && e < num_experts) atomicAdd(&cnt[e], 1);
     else if (e != -1) atomicOr(pp.status, kDevBadExpert);  // -1 = empty slot
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0, ng = 0, nnt = 0;
-    for (int e = 0; e < num_experts; ++e) {
-      off[e] = acc;
-      const int c = cnt[e];
-      for (int q = 0; q * kGroupTok < c; ++q) {
-        const int ntok = min(kGroupTok, c - q * kGroupTok);
-        pp.g_expert[ng] = e;
-        pp.g_slot0[ng] = acc + q * kGroupTok;
-        pp.g_ntok[ng] = ntok;
-        pp.g_nt0[ng] = nnt;
-        for (int i = 0; i * kNTile < ntok; ++i) {
-          pp.nt_slot0[nnt] = acc + q * kGroupTok + i * kNTile;
-          pp.nt_cnt[nnt] = min(kNTile, ntok - i * kNTile);
-          ++nnt;
-        }
-        ++ng;
+  if (warp == 0) {  // exclusive scans of tokens, groups and n-tiles over the experts
+    int run_t = 0, run_g = 0, run_n = 0;
+    for (int base = 0; base < num_experts; base += 32) {
+      const int e = base + lane;
+      const int c = e < num_experts ? cnt[e] : 0;
+      int vt = c, vg = (c + kGroupTok - 1) / kGroupTok, vn = (c + kNTile - 1) / kNTile;
+      int st = vt, sgp = vg, sn = vn;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, st, o);
+        const int b = __shfl_up_sync(0xffffffffu, sgp, o);
+        const int d = __shfl_up_sync(0xffffffffu, sn, o);
+        if (lane >= o) { st += a; sgp += b; sn += d; }
       }
-      acc += c;
+      if (e < num_experts) {
+        off[e] = run_t + st - vt;
+        goff[e] = run_g + sgp - vg;
+        toff[e] = run_n + sn - vn;
+      }
+      run_t += __shfl_sync(0xffffffffu, st, 31);
+      run_g += __shfl_sync(0xffffffffu, sgp, 31);
+      run_n += __shfl_sync(0xffffffffu, sn, 31);
     }
-    pp.meta[0] = ng;
-    pp.meta[1] = nnt;
+    if (lane == 0) {
+      tot[0] = run_t;
+      tot[1] = run_g;
+      tot[2] = run_n;
+    }
+  }
+  __syncthreads();
+  // groups and n-tiles of each expert (a thread per expert)
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
+    const int c = cnt[e];
+    int gi = goff[e], nt = toff[e];
+    for (int q = 0; q * kGroupTok < c; ++q, ++gi) {
+      const int ntok = min(kGroupTok, c - q * kGroupTok);
+      pp.g_expert[gi] = e;
+      pp.g_slot0[gi] = off[e] + q * kGroupTok;
+      pp.g_ntok[gi] = ntok;
+      pp.g_nt0[gi] = nt;
+      for (int i = 0; i * kNTile < ntok; ++i, ++nt) {
+        pp.nt_slot0[nt] = off[e] + q * kGroupTok + i * kNTile;
+        pp.nt_cnt[nt] = min(kNTile, ntok - i * kNTile);
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    pp.meta[0] = tot[1];
+    pp.meta[1] = tot[2];
     int sng = 0, snt = 0;
     if (has_shared) {
       for (int q = 0; q * kGroupTok < num_tokens; ++q) {
@@ -144,16 +232,13 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
     pp.meta[2] = sng;
     pp.meta[3] = snt;
   }
-  __syncthreads();
   for (int q = threadIdx.x; q < S; q += blockDim.x) {
     const int e = ids[q];
     if (e < 0 || e >= num_experts) {
       pp.tk_slot[q] = -1;
       continue;
     }
-    int rank = 0;
-    for (int r = 0; r < q; ++r) rank += ids[r] == e;
-    const int slot = off[e] + rank;
+    const int slot = off[e] + atomicAdd(&fill[e], 1);
     pp.tk_slot[q] = slot;
     pp.slot_tok[slot] = q / top_k;
   }
@@ -219,7 +304,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
                                                       const float* __restrict__ sg, int top_k, int hidden,
                                                       int shared_mode, void* __restrict__ out_v, int out_f32) {
   const int t = blockIdx.x;
-  for (int h = threadIdx.x * 4; h < hidden; h += blockDim.x * 4) {
+  for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < hidden; h += gridDim.y * blockDim.x * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < top_k; ++j) {
       const int slot = tk_slot[(int64_t)t * top_k + j];
@@ -279,6 +364,7 @@ size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
   MoEWs w{};
   size_t o_status = take(256);
   size_t o_ids = take(S * 4), o_tw = take(S * 4), o_sg = take(T * 4);
+  size_t o_lg = take(T * (E + 1) * 4);
   size_t o_meta = take(64);
   size_t o_g = take(gmax * 4 * 4), o_nt = take(ntmax * 4 * 2), o_sgp = take(sgmax * 4 * 4);
   size_t o_tk = take(S * 4), o_st = take(S * 4);
@@ -293,6 +379,7 @@ size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
     w.ids = reinterpret_cast<int32_t*>(base + o_ids);
     w.tw = reinterpret_cast<float*>(base + o_tw);
     w.sg = reinterpret_cast<float*>(base + o_sg);
+    w.logits = reinterpret_cast<float*>(base + o_lg);
     int* g = reinterpret_cast<int*>(base + o_g);
     int* nt = reinterpret_cast<int*>(base + o_nt);
     int* sg = reinterpret_cast<int*>(base + o_sgp);
@@ -445,35 +532,29 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   const int b_ntiles = (std::min(T, kGroupTok) + kNTile - 1) / kNTile;
 
   // 1. routing (or the caller's routing) and the shared-expert gate
-  const int32_t* ids = a.topk_ids;
-  const float* tw = a.topk_weights;
   const bool route = a.topk_ids == nullptr;
-  const bool sg_from_router = sh && a.shared_gate_mode == 1 && route && !a.shared_gate_w;
-  if (route) {
-    const size_t smem = (E + 1) * sizeof(float);
+  const bool gate = sh && a.shared_gate_mode == 1;
+  const float* tw = route ? ws.tw : a.topk_weights;
+  if (route || gate) {
+    // logits of the experts (when routing) and of the shared-expert gate row
+    const uint16_t* w_main = route ? (const uint16_t*)a.router_w : nullptr;
+    const uint16_t* w_gate =
+        !gate ? nullptr : a.shared_gate_w ? (const uint16_t*)a.shared_gate_w : (const uint16_t*)a.router_w + (int64_t)E * H;
+    const int e_main = route ? E : 0;
+    const int R = e_main + (gate ? 1 : 0);
+    const unsigned grid = (unsigned)(((int64_t)R * T + 7) / 8);
     if (bf16)
-      router_kernel<true><<<T, 256, smem, stream>>>((const uint16_t*)a.x, (const uint16_t*)a.router_w, H, E, K,
-                                                      a.renorm, sg_from_router, 1, ws.ids, ws.tw, ws.sg);
+      router_logits_kernel<true><<<grid, 256, 0, stream>>>((const uint16_t*)a.x, w_main, w_gate, T, H, e_main,
+                                                           ws.logits);
     else
-      router_kernel<false><<<T, 256, smem, stream>>>((const uint16_t*)a.x, (const uint16_t*)a.router_w, H, E, K,
-                                                       a.renorm, sg_from_router, 1, ws.ids, ws.tw, ws.sg);
-    ids = ws.ids;
-    tw = ws.tw;
-    if ((rc = stage_done("router", stream)) != BLUT_OK) return rc;
+      router_logits_kernel<false><<<grid, 256, 0, stream>>>((const uint16_t*)a.x, w_main, w_gate, T, H, e_main,
+                                                            ws.logits);
+    if ((rc = stage_done("router logits", stream)) != BLUT_OK) return rc;
   }
-  if (sh && a.shared_gate_mode == 1 && !sg_from_router) {
-    // gate-only pass over the single row shared_gate_w (as row "E" of a 0-expert router)
-    const uint16_t* gw = (const uint16_t*)a.shared_gate_w;
-    if (bf16)
-      router_kernel<true><<<T, 256, 2 * sizeof(float), stream>>>((const uint16_t*)a.x, gw, H, 0, 0, 0, 1, 0,
-                                                                   nullptr, nullptr, ws.sg);
-    else
-      router_kernel<false><<<T, 256, 2 * sizeof(float), stream>>>((const uint16_t*)a.x, gw, H, 0, 0, 0, 1, 0,
-                                                                    nullptr, nullptr, ws.sg);
-    if ((rc = stage_done("shared gate", stream)) != BLUT_OK) return rc;
-  }
-  // 2. plan
-  plan_kernel<<<1, 1024, 0, stream>>>(ids, T, K, E, sh ? 1 : 0, ws.pp);
+  // 2. top-k (when routing) + plan
+  plan_kernel<<<1, 1024, 0, stream>>>(a.topk_ids, (route || gate) ? ws.logits : nullptr, route ? E : 0,
+                                      (route ? E : 0) + (gate ? 1 : 0), T, K, E, a.renorm, gate ? 1 : 0,
+                                      sh ? 1 : 0, ws.pp, ws.ids, ws.tw, ws.sg);
   if ((rc = stage_done("plan", stream)) != BLUT_OK) return rc;
   // 3. B fragments of x (routed and shared)
   {
@@ -550,10 +631,10 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   // 6. combine
   const int smode = sh ? a.shared_gate_mode : -1;
   if (bf16)
-    combine_kernel<true><<<T, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
+    combine_kernel<true><<<dim3(T, (H + 1023) / 1024), 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
                                                 a.out_f32);
   else
-    combine_kernel<false><<<T, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
+    combine_kernel<false><<<dim3(T, (H + 1023) / 1024), 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
                                                  a.out_f32);
   return stage_done("combine", stream);
 }
@@ -561,29 +642,28 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
 int moe_launch_count(const blut_moe_args& a) {
   const bool sh = a.shared_inter > 0;
   int n = 0;
-  if (!a.topk_ids) ++n;                                                       // router
-  if (sh && a.shared_gate_mode == 1 && !(!a.topk_ids && !a.shared_gate_w)) ++n; // gate-only
-  n += 2;                                                                     // plan, gather
-  n += 2;                                                                     // routed gate/up, down
-  if (sh) n += 2;                                                             // shared gate/up, down
-  n += 1;                                                                     // combine
+  if (!a.topk_ids || (sh && a.shared_gate_mode == 1)) ++n;  // router / gate logits
+  n += 2;                                                  // top-k + plan, gather
+  n += 2;                                                  // routed gate/up, down
+  if (sh) n += 2;                                          // shared gate/up, down
+  n += 1;                                                  // combine
   return n;
 }
 
 int router(const void* x, const void* w, int T, int H, int E, int K, int renorm, int has_sg, int dtype,
-           int32_t* ids, float* tw, float* sg, cudaStream_t stream) {
-  if (!x || !w || !ids || !tw || T <= 0 || H <= 0 || E <= 0 || K <= 0 || K > 32 || K > E) return BLUT_ERR_INVALID;
-  if (H % 8 || (has_sg && !sg)) return BLUT_ERR_INVALID;
-  if (E > kMaxExperts) return BLUT_ERR_UNSUPPORTED;
-  const size_t smem = (E + 1) * sizeof(float);
-  if (dtype == BLUT_BF16)
-    router_kernel<true><<<T, 256, smem, stream>>>((const uint16_t*)x, (const uint16_t*)w, H, E, K, renorm, has_sg, 1,
-                                                    ids, tw, sg);
-  else if (dtype == BLUT_F16)
-    router_kernel<false><<<T, 256, smem, stream>>>((const uint16_t*)x, (const uint16_t*)w, H, E, K, renorm, has_sg, 1,
-                                                     ids, tw, sg);
-  else
+           int32_t* ids, float* tw, float* sg, float* logits, cudaStream_t stream) {
+  if (!x || !w || !ids || !tw || !logits || T <= 0 || H <= 0 || E <= 0 || K <= 0 || K > 32 || K > E)
     return BLUT_ERR_INVALID;
+  if (H % 8 || (has_sg && !sg) || (dtype != BLUT_BF16 && dtype != BLUT_F16)) return BLUT_ERR_INVALID;
+  if (E > kMaxExperts) return BLUT_ERR_UNSUPPORTED;
+  const uint16_t* wm = (const uint16_t*)w;
+  const uint16_t* wg = has_sg ? wm + (int64_t)E * H : nullptr;
+  const unsigned grid = (unsigned)(((int64_t)(E + (has_sg ? 1 : 0)) * T + 7) / 8);
+  if (dtype == BLUT_BF16)
+    router_logits_kernel<true><<<grid, 256, 0, stream>>>((const uint16_t*)x, wm, wg, T, H, E, logits);
+  else
+    router_logits_kernel<false><<<grid, 256, 0, stream>>>((const uint16_t*)x, wm, wg, T, H, E, logits);
+  topk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(logits, T, E, K, renorm, has_sg, ids, tw, sg);
   return cudaGetLastError() == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
 }
 

@@ -37,14 +37,19 @@ __device__ __forceinline__ void interleave(uint32_t lo, uint32_t hi, uint32_t& a
   a23 = prmt(lo, hi, 0x7362);
 }
 
-// 16-entry byte-plane lookup of 4 codes held in the low 16 bits of f (nibbles).
-__device__ __forceinline__ void lookup16(uint32_t f, const uint32_t (&H)[4], const uint32_t (&L)[4],
-                                         uint32_t& a01, uint32_t& a23) {
-  const uint32_t sel = f & 0x7777u;
-  const uint32_t sel2 = ((f >> 1) & 0x4444u) | 0x3210u;
+// 16-entry byte-plane lookup of 4 codes given their selectors: sel holds the
+// low three code bits per nibble, sel2 picks the half (code bit 3) per byte.
+__device__ __forceinline__ void lookup16s(uint32_t sel, uint32_t sel2, const uint32_t (&H)[4],
+                                          const uint32_t (&L)[4], uint32_t& a01, uint32_t& a23) {
   const uint32_t hi = prmt(prmt(H[0], H[1], sel), prmt(H[2], H[3], sel), sel2);
   const uint32_t lo = prmt(prmt(L[0], L[1], sel), prmt(L[2], L[3], sel), sel2);
   interleave(lo, hi, a01, a23);
+}
+
+// 16-entry byte-plane lookup of 4 codes held in the low 16 bits of f (nibbles).
+__device__ __forceinline__ void lookup16(uint32_t f, const uint32_t (&H)[4], const uint32_t (&L)[4],
+                                         uint32_t& a01, uint32_t& a23) {
+  lookup16s(f & 0x7777u, ((f >> 1) & 0x4444u) | 0x3210u, H, L, a01, a23);
 }
 
 // ---------------------------------------------------------------- FMT_B 4-bit
@@ -80,6 +85,18 @@ struct PolB4 {
       lookup16(f, H[h], L[h], a[h], a[2 + h]);
     }
   }
+  // Slabs 2sp and 2sp+1 share one code word: their selectors come from one
+  // mask (and one shift for the odd slab's half).
+  __device__ __forceinline__ void frag2(int sp, uint32_t (&a0)[4], uint32_t (&a1)[4]) const {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t w = c[h][sp];
+      const uint32_t sel = w & 0x77777777u;
+      const uint32_t sel2 = ((w >> 1) & 0x44444444u) | 0x32103210u;
+      lookup16s(sel, sel2, H[h], L[h], a0[h], a0[2 + h]);
+      lookup16s(sel >> 16, sel2 >> 16, H[h], L[h], a1[h], a1[2 + h]);
+    }
+  }
 };
 
 // ---------------------------------------------------------------- FMT_B 2-bit
@@ -110,6 +127,10 @@ struct PolB2 {
       const uint32_t sel = (c[h][s >> 2] >> sh) & 0x3333u;
       interleave(prmt(L[h], L[h], sel), prmt(H[h], H[h], sel), a[h], a[2 + h]);
     }
+  }
+  __device__ __forceinline__ void frag2(int sp, uint32_t (&a0)[4], uint32_t (&a1)[4]) const {
+    frag(2 * sp, a0);
+    frag(2 * sp + 1, a1);
   }
 };
 
@@ -147,6 +168,10 @@ struct PolB3 {
       const uint32_t sel = ((c[h][s >> 2] >> sh) & 0x3333u) | (hb & 0x4444u);
       interleave(prmt(L[h][0], L[h][1], sel), prmt(H[h][0], H[h][1], sel), a[h], a[2 + h]);
     }
+  }
+  __device__ __forceinline__ void frag2(int sp, uint32_t (&a0)[4], uint32_t (&a1)[4]) const {
+    frag(2 * sp, a0);
+    frag(2 * sp + 1, a1);
   }
 };
 
@@ -192,6 +217,10 @@ struct PolNestedFull {
       interleave(lo, hi, a[h], a[2 + h]);
     }
   }
+  __device__ __forceinline__ void frag2(int sp, uint32_t (&a0)[4], uint32_t (&a1)[4]) const {
+    frag(2 * sp, a0);
+    frag(2 * sp + 1, a1);
+  }
 };
 
 // ------------------------------------------------------------------- FMT_R8
@@ -226,6 +255,10 @@ struct PolR8 {
       a[2 + h] = bf16x2_mul(prmt(v2, v3, 0x5410), sc[h]);
     }
   }
+  __device__ __forceinline__ void frag2(int sp, uint32_t (&a0)[4], uint32_t (&a1)[4]) const {
+    frag(2 * sp, a0);
+    frag(2 * sp + 1, a1);
+  }
 };
 
 // ---------------------------------------------------------------- FMT_DENSE
@@ -244,6 +277,10 @@ struct PolDense {
     const uint2 r0 = lds64(p + s * 8);
     const uint2 r1 = lds64(p + 2048 + s * 8);
     a[0] = r0.x; a[2] = r0.y; a[1] = r1.x; a[3] = r1.y;
+  }
+  __device__ __forceinline__ void frag2(int sp, uint32_t (&a0)[4], uint32_t (&a1)[4]) const {
+    frag(2 * sp, a0);
+    frag(2 * sp + 1, a1);
   }
 };
 

@@ -228,8 +228,9 @@ def router(x: torch.Tensor, w_router: torch.Tensor, top_k: int, renorm: bool = F
     ids = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
     tw = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
     sg = torch.empty(T, dtype=torch.float32, device=x.device) if shared_gate else None
+    logits = torch.empty(T, w.shape[0], dtype=torch.float32, device=x.device)
     dt = _lib.BF16 if x.dtype == torch.bfloat16 else _lib.F16
     _lib.check(_lib.lib().blut_router(x.data_ptr(), w.data_ptr(), T, H, E, top_k, int(renorm), int(shared_gate), dt,
                                       ids.data_ptr(), tw.data_ptr(), None if sg is None else sg.data_ptr(),
-                                      _lib.stream_ptr(stream)), "router")
+                                      logits.data_ptr(), _lib.stream_ptr(stream)), "router")
     return ids, tw, sg

@@ -179,13 +179,14 @@ BLUT_API int blut_lut_gemv(const void* x_bf16, const void* idx_u8, const void* c
 /* Fused router: logits = x W_r^T (fp32 accumulation), softmax (fp32), top-k
  * (descending, lowest expert index on ties), optional renormalisation, and,
  * when has_shared_gate, sigmoid(x . W_r[num_experts]) for the shared expert.
- * x [T][hidden], w_router [num_experts (+1)][hidden] in `dtype`.
- * Replaces vllm_lut/moe_layer.py:358-376 (_routing) and
+ * x [T][hidden], w_router [num_experts (+1)][hidden] in `dtype`; logits is a
+ * caller buffer of T * (num_experts + has_shared_gate) floats that receives
+ * the router logits.  Replaces vllm_lut/moe_layer.py:358-376 (_routing) and
  * customized/qwen.py:44-54,99. */
 BLUT_API int blut_router(const void* x, const void* w_router, int32_t num_tokens, int32_t hidden,
                 int32_t num_experts, int32_t top_k, int32_t renorm, int32_t has_shared_gate,
                 int32_t dtype, int32_t* topk_ids, float* topk_weights, float* shared_gate,
-                void* stream);
+                float* logits, void* stream);
 
 /* ------------------------------------------------------------------- MoE -- */
 
