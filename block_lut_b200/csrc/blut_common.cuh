@@ -24,8 +24,11 @@ constexpr int kBfragChunkBytes = 32 * 64;  // one (n-tile, chunk) of B fragments
 // ------------------------------------------------------------------------
 // Tiled layout of one matrix.  The matrix is cut into 16-row tiles and
 // 128-column chunks; each "plane" (a code plane or a table plane) stores its
-// (tile, chunk) pieces contiguously, tile-major, so that one bulk copy per
-// plane fetches a whole chunk of a tile.  Inside a piece, data sits in the
+// (tile, chunk) pieces chunk-major (all tiles of chunk 0, then of chunk 1,
+// ...), so that one bulk copy per plane fetches one chunk of W consecutive
+// tiles.  With BLUT_LAYOUT_PAIRED, gate tile t sits at physical tile 2t and
+// up tile t at 2t + 1, so a gate/up pair is one contiguous run.  Inside a
+// piece, data sits in the
 // order the mma.m16n8k16 A fragment consumes it (lane = 4 * (row & 7) +
 // ((k & 7) >> 1)), see the *_pos helpers below.
 // ------------------------------------------------------------------------
