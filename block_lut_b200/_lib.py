@@ -70,6 +70,7 @@ SIGNATURES = [
     ("blut_router", C.c_int, [_VP, _VP, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _VP, _VP, _VP, _VP, _VP]),
     ("blut_moe_workspace_size", C.c_size_t, [C.POINTER(MoEArgs)]),
     ("blut_moe_forward", C.c_int, [C.POINTER(MoEArgs), _VP, C.c_size_t, _VP]),
+    ("blut_moe_forward_noalloc", C.c_int, [C.POINTER(MoEArgs), _VP]),
     ("blut_moe_check_status", C.c_int, [_VP, _VP]),
     ("blut_moe_launch_count", C.c_int, [C.POINTER(MoEArgs)]),
 ]

@@ -243,6 +243,21 @@ BLUT_API size_t blut_moe_workspace_size(const blut_moe_args* args);
 BLUT_API int blut_moe_forward(const blut_moe_args* args, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* blut_moe_forward without a caller workspace, for callers that cannot
+ * allocate device memory when they call (a plugin that a host framework hands
+ * only its input and output pointers, a serving loop that must not call
+ * cudaMalloc).  No counterpart in the reference.  The scratch is one
+ * library-owned device array of 16 MiB per GPU, reserved from the moment the
+ * library is loaded until the process exits; layers whose
+ * blut_moe_workspace_size exceeds 16 MiB are rejected with
+ * BLUT_ERR_WORKSPACE before anything is launched.  The first call on a
+ * device looks the array's device address up (make it before any stream
+ * capture).  Nothing is allocated and nothing synchronised.  All calls on a
+ * GPU share the array, so calls that can overlap on that GPU (different
+ * streams without ordering between them) race and must be serialised by the
+ * caller. */
+BLUT_API int blut_moe_forward_noalloc(const blut_moe_args* args, void* stream);
+
 /* Read (and clear) the device-side status word of a workspace last used by
  * blut_moe_forward on `stream`: synchronises the stream, returns BLUT_OK or
  * BLUT_ERR_TIMEOUT when a kernel's bounded wait gave up.  Diagnostic only. */
