@@ -23,7 +23,7 @@ BLUT_ERR_CUDA = -6
 
 # formats / dtypes
 FMT_R8, FMT_B, FMT_NESTED, FMT_DENSE = 1, 2, 3, 4
-LAYOUT_PAIRED = 1
+LAYOUT_PAIRED, LAYOUT_TC = 1, 2
 F16, BF16, F32 = 0, 1, 2
 
 

@@ -50,9 +50,79 @@ struct TiledLayout {
   int64_t off[4];       // plane byte offset inside the matrix buffer
   int64_t total;        // matrix bytes (256-aligned)
   int64_t ntiles, nchunks;
+  // BLUT_LAYOUT_TC: tiles of kTcRows rows, "chunks" are blocks of kb columns,
+  // and bpr[p] is the bytes one row holds per block in plane p.
+  int tc, kb;
+  int bpr[4];
 };
 
 __host__ __device__ inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+// ------------------------------------------------------------------------
+// TC layout (BLUT_LAYOUT_TC): 128-row tiles for the tcgen05 matmuls, where
+// one thread decodes one weight row into tensor memory.  A (tile, block)
+// piece of a plane holds bpr bytes per row, cut into units of
+// u = min(16, bpr) bytes and stored unit-major: byte o of row r sits at
+// (o / u) * 128 * u + r * u + o % u.  A warp's 32 rows reading one unit
+// touch one contiguous 32 * u byte range (no bank conflicts), and for dense
+// weights the piece is exactly the canonical no-swizzle K-major operand
+// layout of tcgen05.mma (8-row x 16-byte core matrices).  Per plane and row,
+// the block's bytes are:
+//   codes4  the row's canonical 4-bit code bytes of the block (LSB first)
+//   tables  per table of the block: 2^b high bytes, then 2^b low bytes
+//   dense   the row's fp16 / bf16 values of the block
+// ------------------------------------------------------------------------
+constexpr int kTcRows = 128;
+
+__host__ __device__ inline int tc_unit(int bpr) { return bpr < 16 ? bpr : 16; }
+__host__ __device__ inline int tc_pos(int bpr, int row, int o) {
+  const int u = tc_unit(bpr);
+  return (o / u) * (kTcRows * u) + row * u + o % u;
+}
+// Columns per block: dense 32 (two k16 MMA slabs per pipeline stage), LUT
+// formats max(64, group) so that a block holds whole tables.
+__host__ __device__ inline int tc_block_cols(int format, int group) {
+  return format == BLUT_FMT_DENSE ? 32 : (group > 64 ? group : 64);
+}
+
+__host__ inline bool make_tc_layout(const blut_mat_desc& d, TiledLayout& L) {
+  const bool paired = (d.layout & BLUT_LAYOUT_PAIRED) != 0;
+  if (d.rows <= 0 || d.cols <= 0 || d.rows % (paired ? 2 * kTcRows : kTcRows)) return false;
+  L = TiledLayout{};
+  L.tc = 1;
+  L.kb = tc_block_cols(d.format, d.group);
+  if (d.cols % L.kb) return false;
+  L.ntiles = d.rows / kTcRows;
+  L.nchunks = d.cols / L.kb;
+  auto add = [&](int kind, int bpr, int entries) {
+    L.kind[L.nplanes] = kind;
+    L.bpr[L.nplanes] = bpr;
+    L.piece[L.nplanes] = (int64_t)kTcRows * bpr;
+    L.entries[L.nplanes] = entries;
+    L.nplanes++;
+  };
+  switch (d.format) {
+    case BLUT_FMT_B:
+      if (d.bits != 4 || d.dtype != BLUT_F16) return false;
+      if (d.group != 32 && d.group != 64 && d.group != 128) return false;
+      add(kPlaneCodes4, L.kb / 2, 0);
+      add(kPlaneTables, (L.kb / d.group) * 32, 16);
+      break;
+    case BLUT_FMT_DENSE:
+      if (d.dtype != BLUT_F16 && d.dtype != BLUT_BF16) return false;
+      add(kPlaneDense, L.kb * 2, 0);
+      break;
+    default:
+      return false;
+  }
+  int64_t off = 0;
+  for (int p = 0; p < L.nplanes; ++p) {
+    L.off[p] = off;
+    off = align256(off + L.piece[p] * L.ntiles * L.nchunks);
+  }
+  L.total = off;
+  return true;
+}
 
 __host__ __device__ inline int64_t table_piece_bytes(int entries, int group) {
   return int64_t(kChunk / group) * kTileRows * entries * 2;
@@ -60,8 +130,9 @@ __host__ __device__ inline int64_t table_piece_bytes(int entries, int group) {
 
 // Fills `L` for `d`.  Returns false if the shape/format has no tiled layout.
 __host__ inline bool make_layout(const blut_mat_desc& d, TiledLayout& L) {
+  if ((d.layout & ~(BLUT_LAYOUT_PAIRED | BLUT_LAYOUT_TC)) != 0) return false;
+  if (d.layout & BLUT_LAYOUT_TC) return make_tc_layout(d, L);
   if (d.rows <= 0 || d.cols <= 0 || d.rows % kTileRows || d.cols % kChunk) return false;
-  if ((d.layout & ~BLUT_LAYOUT_PAIRED) != 0) return false;
   if ((d.layout & BLUT_LAYOUT_PAIRED) && d.rows % (2 * kTileRows)) return false;
   L = TiledLayout{};
   L.ntiles = d.rows / kTileRows;

@@ -23,7 +23,10 @@ struct PlanPtrs {
   int *sg_expert, *sg_slot0, *sg_ntok, *sg_nt0;
   int* tk_slot;   // [T*k] slot of (token, j), -1 if the id was invalid
   int* slot_tok;  // [T*k] token of each slot
+  int* counters;  // [kNumCounters] work-item counters of the tcgen05 launches
 };
+
+constexpr int kNumCounters = 4;  // routed gate/up, routed down, shared gate/up, shared down
 
 struct MoEWs {
   int* status;
@@ -55,6 +58,12 @@ cudaError_t launch_mm_r8(bool pair, const MMParams& p, int sms, cudaStream_t str
 cudaError_t launch_mm_dense(bool bf16, bool pair, const MMParams& p, int sms, cudaStream_t stream);
 
 bool mm_planes(const blut_mat_desc& d, bool pair, MMParams& p);
+
+// tcgen05 matmul for BLUT_LAYOUT_TC matrices (blut_tc_inst.cu).
+struct TcParams;
+bool tc_planes(const blut_mat_desc& d, bool pair, TcParams& p);
+cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int sms, cudaStream_t stream);
+int dequant_tiled_tc(const blut_mat_desc& d, const void* tiled, void* out, cudaStream_t stream);
 int dequant_tiled(const blut_mat_desc& d, const void* tiled, const void* table, void* out, cudaStream_t stream);
 
 // Canonical-layout kernels (blut_pack.cu, blut_gemv.cu).

@@ -6,8 +6,8 @@
 #include <cstdlib>
 #include <mutex>
 
-#include "blut_mm.cuh"
 #include "blut_internal.h"
+#include "blut_tc.cuh"
 
 namespace blut {
 
@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
   const int S = num_tokens * top_k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) *pp.status = 0;
+  if (threadIdx.x < kNumCounters) pp.counters[threadIdx.x] = 0;
   if (logits) {  // row t: topk_e expert logits, then the gate logit when has_gate
     for (int t = warp; t < num_tokens; t += 32) {
       warp_topk(logits + (int64_t)t * R, topk_e, ids_in ? 0 : top_k, renorm, ids_out + (int64_t)t * top_k,
@@ -245,11 +246,13 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
 }
 
 // --------------------------------------------------------------- gather ---
-// B fragments of the activations: block (n-tile, chunk), 32 threads = lanes.
-// z = 0: routed n-tiles (token of slot via slot_tok), z = 1: shared expert
-// (slot = token).
+// Activations of one (n-tile, 128-column chunk) block, 32 threads.  z = 0:
+// routed n-tiles (token of slot via slot_tok), z = 1: shared expert (slot =
+// token).  Bit z of tc_mask selects the tcgen05 operand order
+// (tc_bact_byte) for that destination instead of mma.sync B fragments.
 __global__ void __launch_bounds__(32) gather_bfrag_kernel(const uint16_t* __restrict__ x, int hidden, PlanPtrs pp,
-                                                          uint8_t* __restrict__ xf, uint8_t* __restrict__ xfs) {
+                                                          uint8_t* __restrict__ xf, uint8_t* __restrict__ xfs,
+                                                          int tc_mask) {
   const bool shared = blockIdx.z == 1;
   const int nt = blockIdx.x;
   const int c = blockIdx.y;
@@ -275,6 +278,23 @@ __global__ void __launch_bounds__(32) gather_bfrag_kernel(const uint16_t* __rest
   } else {
     slot0 = pp.nt_slot0[nt];
     cntv = pp.nt_cnt[nt];
+  }
+  if ((tc_mask >> blockIdx.z) & 1) {
+    // 16 column groups x 8 tokens of 16 bytes: lane -> token lane & 7, groups (lane >> 3) + 4i
+    const int tok = lane & 7;
+    const uint16_t* row = nullptr;
+    if (tok < cntv) {
+      const int slot = slot0 + tok;
+      row = x + (int64_t)(shared ? slot : pp.slot_tok[slot]) * hidden + c * kChunk;
+    }
+    uint8_t* dst = (shared ? xfs : xf) + ((int64_t)nt * nchunks + c) * kBfragChunkBytes;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int kg = (lane >> 3) + 4 * i;
+      const uint4 v = row ? *reinterpret_cast<const uint4*>(row + kg * 8) : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(dst + kg * 128 + tok * 16) = v;
+    }
+    return;
   }
   uint32_t wv[16];
   if (g < cntv) {
@@ -384,6 +404,7 @@ size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
     int* nt = reinterpret_cast<int*>(base + o_nt);
     int* sg = reinterpret_cast<int*>(base + o_sgp);
     w.pp.status = w.status;
+    w.pp.counters = w.status + 16;  // inside the 256-byte status block
     w.pp.meta = reinterpret_cast<int*>(base + o_meta);
     w.pp.g_expert = g;
     w.pp.g_slot0 = g + gmax;
@@ -427,6 +448,9 @@ int validate_moe(const blut_moe_args& a) {
   if (!(a.w13.layout & BLUT_LAYOUT_PAIRED) || (a.w2.layout & BLUT_LAYOUT_PAIRED)) return BLUT_ERR_INVALID;
   if (a.shared_inter > 0 && (!(a.s13.layout & BLUT_LAYOUT_PAIRED) || (a.s2.layout & BLUT_LAYOUT_PAIRED)))
     return BLUT_ERR_INVALID;
+  // a projection pair runs on one matmul path: both tcgen05 or both mma.sync
+  if ((a.w13.layout ^ a.w2.layout) & BLUT_LAYOUT_TC) return BLUT_ERR_INVALID;
+  if (a.shared_inter > 0 && ((a.s13.layout ^ a.s2.layout) & BLUT_LAYOUT_TC)) return BLUT_ERR_INVALID;
   if (a.w13.format == BLUT_FMT_R8 && !a.lut_table) return BLUT_ERR_INVALID;
   TiledLayout L13, L2;
   if (!make_layout(a.w13, L13) || !make_layout(a.w2, L2)) return BLUT_ERR_UNSUPPORTED;
@@ -556,75 +580,79 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
                                       (route ? E : 0) + (gate ? 1 : 0), T, K, E, a.renorm, gate ? 1 : 0,
                                       sh ? 1 : 0, ws.pp, ws.ids, ws.tw, ws.sg);
   if ((rc = stage_done("plan", stream)) != BLUT_OK) return rc;
-  // 3. B fragments of x (routed and shared)
+  // 3. activations of x in the operand order of each matmul path
+  const bool tc = (a.w13.layout & BLUT_LAYOUT_TC) != 0;
+  const bool stc = sh && (a.s13.layout & BLUT_LAYOUT_TC) != 0;
   {
     dim3 grid((unsigned)std::max<int64_t>(ws.ntmax, sh ? ws.sntmax : 0), (unsigned)(H / kChunk), sh ? 2 : 1);
-    gather_bfrag_kernel<<<grid, 32, 0, stream>>>((const uint16_t*)a.x, H, ws.pp, ws.xf, ws.xfs);
+    gather_bfrag_kernel<<<grid, 32, 0, stream>>>((const uint16_t*)a.x, H, ws.pp, ws.xf, ws.xfs,
+                                                 (tc ? 1 : 0) | (stc ? 2 : 0));
   }
   if ((rc = stage_done("gather", stream)) != BLUT_OK) return rc;
 
-  // 4. gate/up + SiLU*up, 5. down -- routed experts
-  MMParams p{};
-  p.status = ws.status;
-  p.r8_table = (const uint16_t*)a.lut_table;
-  p.gt = GroupTab{ws.pp.meta + 0, ws.pp.g_expert, ws.pp.g_slot0, ws.pp.g_ntok, ws.pp.g_nt0};
-
-  MMParams p13 = p;
-  if (!mm_planes(a.w13, true, p13)) return BLUT_ERR_UNSUPPORTED;
-  p13.w = (const uint8_t*)a.w13_tiled;
-  p13.wstride = a.w13_stride;
-  p13.bin = ws.xf;
-  p13.act_out = ws.af;
-  p13.out_nchunks = a.inter / kChunk;
-  p13.W = choose_units_per_item(est_groups, p13.units, sms);
-  p13.b_ntiles = b_ntiles;
+  // One projection of all groups: gate/up (pair) writes the down projection's
+  // activations, down writes fp32 rows.
+  const GroupTab routed{ws.pp.meta + 0, ws.pp.g_expert, ws.pp.g_slot0, ws.pp.g_ntok, ws.pp.g_nt0};
+  const GroupTab shared{ws.pp.meta + 2, ws.pp.sg_expert, ws.pp.sg_slot0, ws.pp.sg_ntok, ws.pp.sg_nt0};
+  auto pass = [&](const blut_mat_desc& d, const void* w, int64_t stride, const GroupTab& gt, double est,
+                  const uint8_t* bin, uint8_t* act, int out_k, float* y, int counter) -> int {
+    const bool pair = act != nullptr;
+    const int K = (int)d.cols;
+    if (d.layout & BLUT_LAYOUT_TC) {
+      TcParams t{};
+      if (!tc_planes(d, pair, t)) return BLUT_ERR_UNSUPPORTED;
+      t.w = (const uint8_t*)w;
+      t.wstride = stride;
+      t.gt = gt;
+      t.bin = bin;
+      t.bin_nch = K / kChunk;
+      t.act_out = act;
+      t.out_nch = out_k / kChunk;
+      t.y_out = y;
+      t.y_ld = H;
+      t.counter = ws.pp.counters + counter;
+      t.status = ws.status;
+      return launch_tc_mm(d, t, sms, stream) == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
+    }
+    MMParams m{};
+    if (!mm_planes(d, pair, m)) return BLUT_ERR_UNSUPPORTED;
+    m.status = ws.status;
+    m.r8_table = (const uint16_t*)a.lut_table;
+    m.gt = gt;
+    m.w = (const uint8_t*)w;
+    m.wstride = stride;
+    m.bin = bin;
+    m.act_out = act;
+    m.out_nchunks = out_k / kChunk;
+    m.y_out = y;
+    m.y_ld = H;
+    m.W = choose_units_per_item(est, m.units, sms);
+    m.b_ntiles = b_ntiles;
+    return launch_lut_mm(d, pair, m, sms, stream) == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
+  };
   cudaEvent_t* ev = a.prof_events ? (cudaEvent_t*)a.prof_events : nullptr;
+
+  // 4. gate/up + SiLU*up (routed, then shared)
   if (ev && cudaEventRecord(ev[0], stream) != cudaSuccess) return BLUT_ERR_INVALID;
-  if (launch_lut_mm(a.w13, true, p13, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  if ((rc = pass(a.w13, a.w13_tiled, a.w13_stride, routed, est_groups, ws.xf, ws.af, a.inter, nullptr, 0)) !=
+      BLUT_OK)
+    return rc;
   if ((rc = stage_done("routed gate/up", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[1], stream) != cudaSuccess) return BLUT_ERR_INVALID;
-
-  MMParams pS13 = p;
   if (sh) {
-    pS13.gt = GroupTab{ws.pp.meta + 2, ws.pp.sg_expert, ws.pp.sg_slot0, ws.pp.sg_ntok, ws.pp.sg_nt0};
-    if (!mm_planes(a.s13, true, pS13)) return BLUT_ERR_UNSUPPORTED;
-    pS13.w = (const uint8_t*)a.s13_tiled;
-    pS13.wstride = 0;
-    pS13.bin = ws.xfs;
-    pS13.act_out = ws.afs;
-    pS13.out_nchunks = a.shared_inter / kChunk;
-    pS13.W = choose_units_per_item(est_sgroups, pS13.units, sms);
-    pS13.b_ntiles = b_ntiles;
-    if (launch_lut_mm(a.s13, true, pS13, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+    if ((rc = pass(a.s13, a.s13_tiled, 0, shared, est_sgroups, ws.xfs, ws.afs, a.shared_inter, nullptr, 2)) !=
+        BLUT_OK)
+      return rc;
     if ((rc = stage_done("shared gate/up", stream)) != BLUT_OK) return rc;
   }
-
-  MMParams p2 = p;
-  if (!mm_planes(a.w2, false, p2)) return BLUT_ERR_UNSUPPORTED;
-  p2.w = (const uint8_t*)a.w2_tiled;
-  p2.wstride = a.w2_stride;
-  p2.bin = ws.af;
-  p2.y_out = ws.y;
-  p2.y_ld = H;
-  p2.W = choose_units_per_item(est_groups, p2.units, sms);
-  p2.b_ntiles = b_ntiles;
+  // 5. down (routed, then shared)
   if (ev && cudaEventRecord(ev[2], stream) != cudaSuccess) return BLUT_ERR_INVALID;
-  if (launch_lut_mm(a.w2, false, p2, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  if ((rc = pass(a.w2, a.w2_tiled, a.w2_stride, routed, est_groups, ws.af, nullptr, 0, ws.y, 1)) != BLUT_OK)
+    return rc;
   if ((rc = stage_done("routed down", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[3], stream) != cudaSuccess) return BLUT_ERR_INVALID;
-
   if (sh) {
-    MMParams pS2 = pS13;
-    if (!mm_planes(a.s2, false, pS2)) return BLUT_ERR_UNSUPPORTED;
-    pS2.w = (const uint8_t*)a.s2_tiled;
-    pS2.wstride = 0;
-    pS2.bin = ws.afs;
-    pS2.act_out = nullptr;
-    pS2.y_out = ws.ys;
-    pS2.y_ld = H;
-    pS2.W = choose_units_per_item(est_sgroups, pS2.units, sms);
-    pS2.b_ntiles = b_ntiles;
-    if (launch_lut_mm(a.s2, false, pS2, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+    if ((rc = pass(a.s2, a.s2_tiled, 0, shared, est_sgroups, ws.afs, nullptr, 0, ws.ys, 3)) != BLUT_OK) return rc;
     if ((rc = stage_done("shared down", stream)) != BLUT_OK) return rc;
   }
 

@@ -234,6 +234,47 @@ __global__ void pack_tables_kernel(PackArgs a) {
   }
 }
 
+// TC layout: one thread per byte of plane `plane` (block-major, then physical
+// tile, then the unit-major piece), fetching that byte from the canonical
+// arrays.
+__global__ void pack_tc_kernel(PackArgs a, int plane) {
+  const TiledLayout& L = a.L;
+  const int bpr = L.bpr[plane];
+  const int unit = tc_unit(bpr);
+  const int64_t piece = L.piece[plane];
+  const int64_t n = piece * L.ntiles * L.nchunks;
+  const bool paired = (a.layout & BLUT_LAYOUT_PAIRED) != 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t blk = i / (piece * L.ntiles);
+    const int64_t rem = i - blk * piece * L.ntiles;
+    const int64_t pt = rem / piece;
+    const int x = (int)(rem - pt * piece);
+    const int rr = (x / unit) % kTcRows;
+    const int o = (x / (kTcRows * unit)) * unit + x % unit;  // byte of the row's block data
+    const int64_t r = logical_tile(pt, L.ntiles, paired) * kTcRows + rr;
+    uint8_t v = 0;
+    switch (L.kind[plane]) {
+      case kPlaneCodes4:
+        v = a.codes[r * (a.cols / 2) + blk * (L.kb / 2) + o];
+        break;
+      case kPlaneTables: {
+        const int ent = L.entries[plane];
+        const int m = o / (2 * ent), wb = o % (2 * ent);
+        const int64_t tb = r * (a.cols / a.group) + blk * (L.kb / a.group) + m;
+        const uint16_t e = a.tables[tb * ent + (wb % ent)];
+        v = wb < ent ? uint8_t(e >> 8) : uint8_t(e & 0xFF);
+        break;
+      }
+      case kPlaneDense: {
+        const uint16_t e = reinterpret_cast<const uint16_t*>(a.codes)[r * a.cols + blk * L.kb + o / 2];
+        v = (o & 1) ? uint8_t(e >> 8) : uint8_t(e & 0xFF);
+        break;
+      }
+    }
+    a.dst[L.off[plane] + i] = v;
+  }
+}
+
 // ------------------------------------------------------------- encoders ----
 // Per (row, block) Lloyd k-means, one warp per block, g / 32 values per lane
 // (lane l holds elements l, l + 32, ...).  Every floating-point step is an
@@ -539,6 +580,13 @@ int pack_tiled(const blut_mat_desc& d, const blut_canon& c, void* tiled, cudaStr
   a.tables2 = (const uint16_t*)c.tables2;
   a.scales = (const uint16_t*)c.scales;
   if (cudaMemsetAsync(tiled, 0, L.total, stream) != cudaSuccess) return BLUT_ERR_CUDA;
+  if (L.tc) {
+    for (int p = 0; p < L.nplanes; ++p) {
+      const int64_t nb = L.piece[p] * L.ntiles * L.nchunks;
+      pack_tc_kernel<<<std::min<unsigned>(grid1d(nb, 256), 1u << 20), 256, 0, stream>>>(a, p);
+    }
+    return cudaGetLastError() == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
+  }
   const int64_t n = d.rows * d.cols;
   pack_codes_kernel<<<std::min<unsigned>(grid1d(n, 256), 1u << 20), 256, 0, stream>>>(a);
   if (d.format != BLUT_FMT_DENSE) {

@@ -1,0 +1,543 @@
+// tcgen05 LUT matmul: every (token group, 256-row unit) of a layer in one
+// persistent launch, with the tensor core's accumulators in tensor memory.
+//
+// A work item is a group of <= 32 tokens routed to one expert times one unit
+// of two 128-row tiles of that expert's matrix (the gate tile and the up tile
+// of a BLUT_LAYOUT_PAIRED gate/up matrix, or two consecutive tiles of a down
+// matrix).  Items are handed out by a global atomic counter, so CTAs that
+// finish early take more.  A CTA has ten warps:
+//
+//  * warp 0 (producer): takes items from the counter, posts them to a small
+//    shared-memory queue and streams each item's planes, block by block,
+//    with one bulk copy (cp.async.bulk) per plane and per 8-token n-tile of
+//    activations into a ring of shared-memory stages;
+//  * warp 1 (MMA): allocates the tensor memory and issues, from one thread,
+//    tcgen05.mma M=128 x N=16|32 x K=16 per tile and slab, fp32 accumulators
+//    in tensor memory (double-buffered across items);
+//  * warps 2..9 (decode): one thread per weight row.  For LUT formats each
+//    thread looks its row's codes up in its row's tables (byte permutes in
+//    registers) and writes the fp16 A operand of a 64-column half-block to
+//    tensor memory (tcgen05.st), which the MMA reads directly
+//    (A-from-tensor-memory form).  Dense weights skip this: the MMA reads
+//    them from shared memory.  After the K loop the same warps run the
+//    epilogue from tensor memory: SiLU(gate) * up written as the down
+//    projection's activations, or fp32 expert-output rows.
+//
+// Every wait is bounded (2 s); one that runs out sets the CTA's abort flag
+// and the device status word, the roles leave their loops, the producer lets
+// the copies it has in flight land, the MMA thread waits for its last MMAs,
+// and the tensor memory is released before the CTA exits.
+#pragma once
+
+#include "blut_mm.cuh"
+
+namespace blut {
+
+constexpr int kTcDecodeWarps = 8;
+constexpr int kTcThreads = 32 * (2 + kTcDecodeWarps);
+constexpr int kTcRingBudget = 96 * 1024;
+constexpr int kTcQueue = 4;          // depth of the shared-memory item queue
+constexpr int kTcDCols = 64;         // tensor-memory columns of one accumulator buffer (2 tiles x N<=32)
+constexpr int kTcACol0 = 2 * kTcDCols;  // first column of the A ring (2 slots x 2 tiles x 32)
+
+struct TcParams {
+  const uint8_t* w;        // tiled (BLUT_LAYOUT_TC) matrices of all experts
+  int64_t wstride;         // bytes between experts
+  int64_t plane_off[2];    // plane offsets inside one matrix
+  int piece[2];            // bytes of one (tile, block) piece per plane
+  int nplanes;
+  int tile_bytes;          // sum of piece[]
+  int ntiles;              // 128-row tiles of the matrix
+  int nblocks;             // column blocks (K / kb)
+  int units;               // ceil(ntiles / 2)
+  int pair;                // 1: gate/up epilogue (SiLU(gate) * up); 0: fp32 rows
+  GroupTab gt;
+  const uint8_t* bin;      // activations, [n-tile][K / 128][2 KB] (tc_bact_byte order)
+  int bin_nch;             // K / 128
+  uint8_t* act_out;        // pair epilogue: down-projection activations, same order
+  int out_nch;             // I / 128
+  float* y_out;            // single epilogue: y[slot][y_ld]
+  int y_ld;
+  int* counter;            // item counter (zeroed by the plan kernel)
+  int* status;
+  int stages;
+};
+
+// Byte offset of activation (token n in [0, 8), column k in [0, 128)) inside
+// one (n-tile, 128-column chunk) block: 16 core matrices of 8 tokens x 8
+// columns, K-major, as the tcgen05.mma B operand reads them without swizzle.
+__host__ __device__ inline int tc_bact_byte(int n, int k) { return (k >> 3) * 128 + n * 16 + (k & 7) * 2; }
+
+// ------------------------------------------------------------ PTX helpers --
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Shared-memory matrix descriptor, no swizzle, K-major: lbo = bytes between
+// core matrices adjacent in K, sbo = bytes between 8-row groups.
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulate, A and B K-major,
+// M = 128, N = n.
+__host__ __device__ inline uint32_t tc_idesc(bool bf16, int n) {
+  const uint32_t ab = bf16 ? 1u : 0u;
+  return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(n >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 16 consecutive 32-bit columns, then the wait; the registers are tied to the
+// wait so that no use is scheduled before it.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld16(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 tc_lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// ------------------------------------------------------- decode policies --
+// 4-bit codes into a 16-entry fp16 table held as high / low byte planes:
+// byte permutes pick entries 0-7 and 8-15 with the low three code bits, a
+// third permute picks between them with bit 3, and two more interleave the
+// low and high bytes into fp16 pairs.  `w` holds 8 codes (k = 0..7, code j
+// in bits 4j..4j+3); out[0..3] receive the fp16 pairs (k, k+1).
+__device__ __forceinline__ void tc_lut16x8(uint32_t w, const uint4& th, const uint4& tl, uint32_t* out) {
+  const uint32_t s1 = w & 0x77777777u;
+  const uint32_t s2 = ((w >> 1) & 0x44444444u) | 0x32103210u;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t a = h ? s1 >> 16 : s1;
+    const uint32_t b = h ? s2 >> 16 : s2;
+    const uint32_t hi = prmt(prmt(th.x, th.y, a), prmt(th.z, th.w, a), b);
+    const uint32_t lo = prmt(prmt(tl.x, tl.y, a), prmt(tl.z, tl.w, a), b);
+    out[2 * h] = prmt(lo, hi, 0x5140u);
+    out[2 * h + 1] = prmt(lo, hi, 0x7362u);
+  }
+}
+
+// FMT_B, 4-bit codes, tables per `G` columns.
+template <int G>
+struct TcDecB4 {
+  static constexpr bool kDense = false;
+  static constexpr bool kBF16 = false;
+  static constexpr int KB = G > 64 ? G : 64;  // columns per block
+  static constexpr int kHalves = KB / 64;     // 64-column halves per block
+  static constexpr int kNumPlanes = 2;
+  // Decodes half h (64 columns) of row `row` of one tile: cp / tp are the
+  // tile's code and table pieces inside the stage.
+  __device__ __forceinline__ static void decode(const uint8_t* cp, const uint8_t* tp, int row, int h,
+                                                uint32_t (&out)[32]) {
+    const uint4 c0 = tc_lds128(cp + ((2 * h) * kTcRows + row) * 16);
+    const uint4 c1 = tc_lds128(cp + ((2 * h + 1) * kTcRows + row) * 16);
+    if constexpr (G == 32) {
+      const uint4 th0 = tc_lds128(tp + ((4 * h + 0) * kTcRows + row) * 16);
+      const uint4 tl0 = tc_lds128(tp + ((4 * h + 1) * kTcRows + row) * 16);
+      const uint4 th1 = tc_lds128(tp + ((4 * h + 2) * kTcRows + row) * 16);
+      const uint4 tl1 = tc_lds128(tp + ((4 * h + 3) * kTcRows + row) * 16);
+      tc_lut16x8(c0.x, th0, tl0, out + 0);
+      tc_lut16x8(c0.y, th0, tl0, out + 4);
+      tc_lut16x8(c0.z, th0, tl0, out + 8);
+      tc_lut16x8(c0.w, th0, tl0, out + 12);
+      tc_lut16x8(c1.x, th1, tl1, out + 16);
+      tc_lut16x8(c1.y, th1, tl1, out + 20);
+      tc_lut16x8(c1.z, th1, tl1, out + 24);
+      tc_lut16x8(c1.w, th1, tl1, out + 28);
+    } else {
+      const int m = G == 64 ? h : 0;
+      const uint4 th = tc_lds128(tp + ((2 * m) * kTcRows + row) * 16);
+      const uint4 tl = tc_lds128(tp + ((2 * m + 1) * kTcRows + row) * 16);
+      tc_lut16x8(c0.x, th, tl, out + 0);
+      tc_lut16x8(c0.y, th, tl, out + 4);
+      tc_lut16x8(c0.z, th, tl, out + 8);
+      tc_lut16x8(c0.w, th, tl, out + 12);
+      tc_lut16x8(c1.x, th, tl, out + 16);
+      tc_lut16x8(c1.y, th, tl, out + 20);
+      tc_lut16x8(c1.z, th, tl, out + 24);
+      tc_lut16x8(c1.w, th, tl, out + 28);
+    }
+  }
+};
+
+// Dense fp16 / bf16 weights: the MMA reads them from shared memory.
+template <bool BF16>
+struct TcDecDense {
+  static constexpr bool kDense = true;
+  static constexpr bool kBF16 = BF16;
+  static constexpr int KB = 32;
+  static constexpr int kHalves = 0;
+  static constexpr int kNumPlanes = 1;
+  __device__ __forceinline__ static void decode(const uint8_t*, const uint8_t*, int, int, uint32_t (&)[32]) {}
+};
+
+// ------------------------------------------------------------------ kernel --
+template <class Dec>
+__host__ __device__ inline int tc_stage_bytes(const TcParams& p) {
+  return (2 * p.tile_bytes + kMaxNT * Dec::KB * 16 + 127) & ~127;
+}
+
+// Barriers, queue and flags take the first 512 bytes, the ring follows.
+template <class Dec>
+__host__ inline int tc_smem_bytes(const TcParams& p) {
+  return 512 + p.stages * tc_stage_bytes<Dec>(p);
+}
+
+template <class Dec>
+__global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) {
+  constexpr bool kDense = Dec::kDense;
+  constexpr int KB = Dec::KB;
+  constexpr uint32_t kCols = kDense ? 128 : 256;  // tensor-memory columns of this CTA
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [8]
+  uint64_t* empty = full + 8;                          // [8]
+  uint64_t* afull = full + 16;                         // [2] A slot written (decode warps)
+  uint64_t* aempty = full + 18;                        // [2] A slot read (MMA commit)
+  uint64_t* dfull = full + 20;                         // [2] accumulators complete (MMA commit)
+  uint64_t* dempty = full + 22;                        // [2] accumulators read (epilogue warps)
+  uint64_t* qfull = full + 24;                         // [kTcQueue] item posted
+  uint64_t* qempty = full + 28;                        // [kTcQueue] item taken by every role
+  uint64_t* fin = full + 32;                           // last MMAs complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 33);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 34);
+  volatile int* qitem = reinterpret_cast<volatile int*>(full + 35);  // [kTcQueue]
+  uint8_t* ring = smem + 512;
+  const int S = p.stages;
+  const int stage_bytes = tc_stage_bytes<Dec>(p);
+  const int boff = 2 * p.tile_bytes;  // activations inside a stage
+  const int qoff1 = 2 * p.piece[0];   // second plane inside a stage
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(full + s), 1);
+      mbar_init(smem_u32(empty + s), kDense ? 1 : 1 + kTcDecodeWarps);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(smem_u32(afull + j), kTcDecodeWarps);
+      mbar_init(smem_u32(aempty + j), 1);
+      mbar_init(smem_u32(dfull + j), 1);
+      mbar_init(smem_u32(dempty + j), kTcDecodeWarps);
+    }
+    for (int j = 0; j < kTcQueue; ++j) {
+      mbar_init(smem_u32(qfull + j), 1);
+      mbar_init(smem_u32(qempty + j), 1 + kTcDecodeWarps);
+    }
+    mbar_init(smem_u32(fin), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_items = *p.gt.n_groups * p.units;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      int64_t it = 0;
+      for (int k = 0;; ++k) {
+        const int qs = k % kTcQueue;
+        if (k >= kTcQueue &&
+            !wait_or_abort(smem_u32(qempty + qs), (uint32_t)(((k / kTcQueue) - 1) & 1), abort_flag, p.status))
+          break;
+        int item = atomicAdd(p.counter, 1);
+        if (item >= n_items || *abort_flag) item = -1;
+        qitem[qs] = item;
+        mbar_arrive(smem_u32(qfull + qs));
+        if (item < 0) break;
+        const int gi = item / p.units, u = item % p.units;
+        const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
+        const int nt0 = p.gt.nt0[gi];
+        const int ntl = min(2, p.ntiles - 2 * u);
+        const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
+        bool ok = true;
+        for (int b = 0; b < p.nblocks; ++b, ++it) {
+          const int s = (int)(it % S);
+          const int64_t use = it / S;
+          if (use > 0 && !wait_or_abort(smem_u32(empty + s), (uint32_t)((use - 1) & 1), abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = ring + (int64_t)s * stage_bytes;
+          const uint32_t bar = smem_u32(full + s);
+          mbar_expect_tx(bar, (uint32_t)(ntl * p.tile_bytes + nnt * KB * 16));
+          const int64_t pt = (int64_t)b * p.ntiles + 2 * u;
+          bulk_g2s(smem_u32(dst), base + p.plane_off[0] + pt * p.piece[0], (uint32_t)(ntl * p.piece[0]), bar);
+          if (Dec::kNumPlanes > 1)
+            bulk_g2s(smem_u32(dst + qoff1), base + p.plane_off[1] + pt * p.piece[1], (uint32_t)(ntl * p.piece[1]),
+                     bar);
+          const int64_t boffg = (int64_t)((b * KB) >> 7) * 2048 + ((b * KB) & 127) * 16;
+          for (int i = 0; i < nnt; ++i)
+            bulk_g2s(smem_u32(dst + boff + i * KB * 16), p.bin + (int64_t)(nt0 + i) * p.bin_nch * 2048 + boffg,
+                     (uint32_t)(KB * 16), bar);
+        }
+        if (!ok) break;
+      }
+      if (*abort_flag) {
+        // let the copies already issued land before the CTA's shared memory goes away
+        for (int64_t m = it - S > 0 ? it - S : 0; m < it; ++m) wait_drain(smem_u32(full + m % S), (uint32_t)((m / S) & 1));
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA --
+    if (lane == 0) {
+      int64_t it = 0, ia = 0, id = 0;
+      for (int k = 0;; ++k) {
+        const int qs = k % kTcQueue;
+        if (!wait_or_abort(smem_u32(qfull + qs), (uint32_t)((k / kTcQueue) & 1), abort_flag, p.status)) break;
+        const int item = qitem[qs];
+        mbar_arrive(smem_u32(qempty + qs));
+        if (item < 0) break;
+        const int gi = item / p.units, u = item % p.units;
+        const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
+        const int ntl = min(2, p.ntiles - 2 * u);
+        const uint32_t idesc = tc_idesc(Dec::kBF16, nnt <= 2 ? 16 : 32);
+        const int db = (int)(id & 1);
+        if (id >= 2 && !wait_or_abort(smem_u32(dempty + db), (uint32_t)(((id >> 1) - 1) & 1), abort_flag, p.status))
+          break;
+        tc_fence_after();
+        const uint32_t dcol = tmem + db * kTcDCols;
+        bool ok = true;
+        for (int b = 0; b < p.nblocks && ok; ++b, ++it) {
+          const int s = (int)(it % S);
+          if (!wait_or_abort(smem_u32(full + s), (uint32_t)((it / S) & 1), abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(ring + (int64_t)s * stage_bytes);
+          if constexpr (kDense) {
+#pragma unroll
+            for (int sl = 0; sl < KB / 16; ++sl) {
+              const uint64_t bd = tc_desc(st + boff + sl * 256, 128, KB * 16);
+              for (int t = 0; t < ntl; ++t) {
+                const uint64_t ad = tc_desc(st + t * p.piece[0] + sl * 2 * 2048, 2048, 128);
+                tc_mma_ss(dcol + t * 32, ad, bd, idesc, (b | sl) != 0);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int h = 0; h < Dec::kHalves; ++h, ++ia) {
+              const int j = (int)(ia & 1);
+              if (!wait_or_abort(smem_u32(afull + j), (uint32_t)((ia >> 1) & 1), abort_flag, p.status)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+#pragma unroll
+              for (int sl = 0; sl < 4; ++sl) {
+                const uint64_t bd = tc_desc(st + boff + (h * 4 + sl) * 256, 128, KB * 16);
+                for (int t = 0; t < ntl; ++t)
+                  tc_mma_ts(dcol + t * 32, tmem + kTcACol0 + j * 64 + t * 32 + sl * 8, bd, idesc, (b | h | sl) != 0);
+              }
+              tc_commit(smem_u32(aempty + j));
+            }
+          }
+          tc_commit(smem_u32(empty + s));
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(dfull + db));
+        ++id;
+      }
+      // all MMAs this thread issued are complete before the memory goes away
+      tc_commit(smem_u32(fin));
+      wait_drain(smem_u32(fin), 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------- decode and epilogue --
+    const int dw = warp - 2;
+    const int t = dw >> 2;             // tile of the unit (decode) / token half or tile (epilogue)
+    const int q = warp & 3;            // tensor-memory lane quarter this warp may access
+    const int row = 32 * q + lane;     // row inside the 128-row tile
+    const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    int64_t it = 0, ia = 0, id = 0;
+    for (int k = 0;; ++k) {
+      const int qs = k % kTcQueue;
+      bool ok = wait_or_abort(smem_u32(qfull + qs), (uint32_t)((k / kTcQueue) & 1), abort_flag, p.status);
+      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+      const int item = qitem[qs];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(qempty + qs));
+      if (item < 0) break;
+      const int gi = item / p.units, u = item % p.units;
+      const int ntok = p.gt.ntok[gi];
+      const int ntl = min(2, p.ntiles - 2 * u);
+      if constexpr (!kDense) {
+        const bool active = t < ntl;
+        for (int b = 0; b < p.nblocks; ++b, ++it) {
+          const int s = (int)(it % S);
+          ok = wait_or_abort(smem_u32(full + s), (uint32_t)((it / S) & 1), abort_flag, p.status);
+          if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+          const uint8_t* st = ring + (int64_t)s * stage_bytes;
+          const uint8_t* cp = st + t * p.piece[0];
+          const uint8_t* tp = st + qoff1 + t * p.piece[1];
+#pragma unroll
+          for (int h = 0; h < Dec::kHalves; ++h, ++ia) {
+            const int j = (int)(ia & 1);
+            if (ia >= 2) {
+              ok = wait_or_abort(smem_u32(aempty + j), (uint32_t)(((ia >> 1) - 1) & 1), abort_flag, p.status);
+              if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+            }
+            tc_fence_after();
+            if (active) {
+              uint32_t a[32];
+              Dec::decode(cp, tp, row, h, a);
+              tc_st32(tmem + lane_base + kTcACol0 + j * 64 + t * 32, a);
+              tc_wait_st();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(afull + j));
+          }
+          if (*abort_flag) break;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(empty + s));
+        }
+        if (*abort_flag) break;
+      }
+      // epilogue
+      const int db = (int)(id & 1);
+      ok = wait_or_abort(smem_u32(dfull + db), (uint32_t)((id >> 1) & 1), abort_flag, p.status);
+      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+      tc_fence_after();
+      const uint32_t dcol = tmem + lane_base + db * kTcDCols;
+      if (p.pair) {
+        // tokens 16t .. 16t+15 of unit row `row`: gate tile at columns 0..31, up tile at 32..63
+        uint32_t g[16], v[16];
+        tc_ld16(dcol + 16 * t, g);
+        tc_wait_ld16(g);
+        tc_ld16(dcol + 32 + 16 * t, v);
+        tc_wait_ld16(v);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(dempty + db));
+        const int col = u * kTcRows + row;  // K index of the down projection
+        const int nt0 = p.gt.nt0[gi];
+        uint8_t* dst = p.act_out + (int64_t)(col >> 7) * 2048 + tc_bact_byte(0, col & 127);
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          const int tok = 16 * t + n;
+          if (tok < ntok) {
+            const float val = silu_f(__uint_as_float(g[n])) * __uint_as_float(v[n]);
+            *reinterpret_cast<uint16_t*>(dst + (int64_t)(nt0 + (tok >> 3)) * p.out_nch * 2048 + (tok & 7) * 16) =
+                f32_to_act<Dec::kBF16>(val);
+          }
+        }
+      } else {
+        // tile t of the unit, tokens 0..31
+        uint32_t v0[16], v1[16];
+        if (t < ntl) {
+          tc_ld16(dcol + 32 * t, v0);
+          tc_wait_ld16(v0);
+          tc_ld16(dcol + 32 * t + 16, v1);
+          tc_wait_ld16(v1);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(dempty + db));
+        if (t < ntl) {
+          const int hrow = (2 * u + t) * kTcRows + row;
+          float* y = p.y_out + (int64_t)p.gt.slot0[gi] * p.y_ld + hrow;
+#pragma unroll
+          for (int n = 0; n < 16; ++n)
+            if (n < ntok) y[(int64_t)n * p.y_ld] = __uint_as_float(v0[n]);
+#pragma unroll
+          for (int n = 0; n < 16; ++n)
+            if (16 + n < ntok) y[(int64_t)(16 + n) * p.y_ld] = __uint_as_float(v1[n]);
+        }
+      }
+      ++id;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+  }
+}
+
+// Host-side launch: ring depth from the shared-memory budget, one persistent
+// CTA per resident slot.
+template <class Dec>
+inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
+  const int stage = tc_stage_bytes<Dec>(p);
+  p.stages = std::max(2, std::min(8, kTcRingBudget / stage));
+  const int smem = tc_smem_bytes<Dec>(p);
+  auto kern = tc_mm_kernel<Dec>;
+  static std::mutex mu;
+  static int cached_smem = -1, cached_per_sm = 1;
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached_smem != smem) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      int nb = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kTcThreads, smem);
+      if (e != cudaSuccess) return e;
+      // two CTAs share the 512 tensor-memory columns of an SM
+      cached_per_sm = nb < 1 ? 1 : (nb > 2 ? 2 : nb);
+      cached_smem = smem;
+    }
+    per_sm = cached_per_sm;
+  }
+  kern<<<num_sms * per_sm, kTcThreads, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace blut

@@ -64,12 +64,19 @@ class LUTFormat:
     def table_entries(self) -> int:
         return 4 if self.kind == "nested" else (1 << self.bits)
 
-    def desc(self, rows: int, cols: int, paired: bool = False) -> _lib.MatDesc:
-        """C descriptor; ``paired`` selects the gate/up-paired tiled layout."""
+    def desc(self, rows: int, cols: int, paired: bool = False, tc: bool = False) -> _lib.MatDesc:
+        """C descriptor; ``paired`` selects the gate/up-paired tiled layout,
+        ``tc`` the 128-row layout of the tcgen05 matmuls."""
         bits = {"r8": 8, "b": self.bits, "nested": 4, "dense": 16}[self.kind]
         group = 128 if self.kind == "r8" and self.group not in (128,) else self.group
+        layout = (_lib.LAYOUT_PAIRED if paired else 0) | (_lib.LAYOUT_TC if tc else 0)
         return _lib.MatDesc(_KIND[self.kind], bits, group, self.tier, _dt_code(self.compute_dtype),
-                            _lib.LAYOUT_PAIRED if paired else 0, int(rows), int(cols))
+                            layout, int(rows), int(cols))
+
+    def has_tc_layout(self, rows: int, cols: int, paired: bool = False) -> bool:
+        """Whether the tcgen05 (BLUT_LAYOUT_TC) layout exists for this format and shape."""
+        d = self.desc(rows, cols, paired, tc=True)
+        return _lib.lib().blut_tiled_bytes(C.byref(d)) >= 0
 
     def bytes_per_weight(self) -> float:
         """Bytes the tiled layout streams per weight element (the roofline basis)."""
@@ -164,24 +171,26 @@ def dequant(qm: QuantizedMatrix, stream=None) -> torch.Tensor:
     return out
 
 
-def tiled_bytes(fmt: LUTFormat, rows: int, cols: int) -> int:
-    d = fmt.desc(rows, cols)
+def tiled_bytes(fmt: LUTFormat, rows: int, cols: int, paired: bool = False, tc: bool = False) -> int:
+    d = fmt.desc(rows, cols, paired, tc)
     n = _lib.lib().blut_tiled_bytes(C.byref(d))
     if n < 0:
-        raise ValueError(f"no tiled layout for {fmt} [{rows}, {cols}]: rows % 16 and cols % 128 must be 0")
+        need = "rows % 128 (256 paired) == 0, a 4-bit or dense format" if tc else "rows % 16 and cols % 128 == 0"
+        raise ValueError(f"no tiled layout for {fmt} [{rows}, {cols}]: needs {need}")
     return int(n)
 
 
-def pack_tiled(mats, stream=None, paired: bool = False) -> tuple[torch.Tensor, int]:
+def pack_tiled(mats, stream=None, paired: bool = False, tc: bool = False) -> tuple[torch.Tensor, int]:
     """Repack canonical matrices (a list, all of one format and shape) into one
     tiled buffer; returns (uint8 buffer, per-matrix stride in bytes).
-    ``paired`` interleaves the row tiles of the two halves (gate/up)."""
+    ``paired`` interleaves the row tiles of the two halves (gate/up); ``tc``
+    selects the layout of the tcgen05 matmuls."""
     mats = list(mats)
     fmt, rows, cols = mats[0].fmt, mats[0].rows, mats[0].cols
-    stride = tiled_bytes(fmt, rows, cols)
+    stride = tiled_bytes(fmt, rows, cols, paired, tc)
     dev = mats[0].codes.device
     buf = torch.empty(len(mats) * stride, dtype=torch.uint8, device=dev)
-    d = fmt.desc(rows, cols, paired)
+    d = fmt.desc(rows, cols, paired, tc)
     s = _lib.stream_ptr(stream)
     for i, m in enumerate(mats):
         c = m.canon()
@@ -190,10 +199,10 @@ def pack_tiled(mats, stream=None, paired: bool = False) -> tuple[torch.Tensor, i
 
 
 def dequant_tiled(fmt: LUTFormat, rows: int, cols: int, tiled: torch.Tensor, lut_table: Optional[torch.Tensor] = None,
-                  stream=None, paired: bool = False) -> torch.Tensor:
-    """Dense matrix rebuilt from one tiled matrix through the kernels' fragment lookups."""
+                  stream=None, paired: bool = False, tc: bool = False) -> torch.Tensor:
+    """Dense matrix rebuilt from one tiled matrix through the kernels' lookups."""
     out = torch.empty(rows, cols, dtype=fmt.compute_dtype, device=tiled.device)
-    d = fmt.desc(rows, cols, paired)
+    d = fmt.desc(rows, cols, paired, tc)
     _lib.check(_lib.lib().blut_dequant_tiled(C.byref(d), tiled.data_ptr(),
                                              None if lut_table is None else lut_table.data_ptr(), out.data_ptr(),
                                              _lib.stream_ptr(stream)), "dequant_tiled")

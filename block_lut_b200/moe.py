@@ -29,19 +29,26 @@ class LUTExperts:
     w2: torch.Tensor
     w2_stride: int
     lut_table: Optional[torch.Tensor] = None  # r8: bf16 [256] tier table
+    tc: bool = False  # tiled for the tcgen05 matmuls (BLUT_LAYOUT_TC)
 
     @classmethod
     def from_quantized(cls, w13: Sequence[QuantizedMatrix], w2: Sequence[QuantizedMatrix],
-                       lut_table: Optional[torch.Tensor] = None, stream=None) -> "LUTExperts":
+                       lut_table: Optional[torch.Tensor] = None, stream=None,
+                       tc: Optional[bool] = None) -> "LUTExperts":
+        """Tile the experts.  ``tc`` None picks the tcgen05 layout whenever the
+        format and shapes have one, else the mma.sync layout."""
         w13, w2 = list(w13), list(w2)
         fmt = w13[0].fmt
-        b13, s13 = pack_tiled(w13, stream, paired=True)
-        b2, s2 = pack_tiled(w2, stream)
+        if tc is None:
+            tc = fmt.has_tc_layout(w13[0].rows, w13[0].cols, paired=True) and \
+                fmt.has_tc_layout(w2[0].rows, w2[0].cols)
+        b13, s13 = pack_tiled(w13, stream, paired=True, tc=tc)
+        b2, s2 = pack_tiled(w2, stream, tc=tc)
         if fmt.kind == "r8":
             if lut_table is None:
                 lut_table = w13[0].tables
             lut_table = lut_table.to(device=b13.device, dtype=torch.bfloat16).contiguous()
-        return cls(fmt, len(w13), w13[0].cols, w13[0].rows // 2, b13, s13, b2, s2, lut_table)
+        return cls(fmt, len(w13), w13[0].cols, w13[0].rows // 2, b13, s13, b2, s2, lut_table, bool(tc))
 
     def weight_bytes(self, experts: int = 1) -> float:
         """Bytes streamed for ``experts`` experts (gate/up/down), per the format."""
@@ -60,12 +67,16 @@ class SharedExpert:
 
     @classmethod
     def from_dense(cls, w13: torch.Tensor, w2: torch.Tensor, gate: Optional[torch.Tensor] = None,
-                   stream=None) -> "SharedExpert":
+                   stream=None, tc: Optional[bool] = None) -> "SharedExpert":
+        """Tile the shared expert; ``tc`` as in ``LUTExperts.from_quantized``."""
         m13, m2 = dense_matrix(w13), dense_matrix(w2)
-        b13, _ = pack_tiled([m13], stream, paired=True)
-        b2, _ = pack_tiled([m2], stream)
+        if tc is None:
+            tc = m13.fmt.has_tc_layout(*w13.shape, paired=True) and m2.fmt.has_tc_layout(*w2.shape)
+        b13, _ = pack_tiled([m13], stream, paired=True, tc=tc)
+        b2, _ = pack_tiled([m2], stream, tc=tc)
         g = None if gate is None else gate.reshape(-1).to(w13.dtype).contiguous()
-        return cls(w13.shape[0] // 2, b13, b2, m13.fmt.desc(*w13.shape, paired=True), m2.fmt.desc(*w2.shape), g)
+        return cls(w13.shape[0] // 2, b13, b2, m13.fmt.desc(*w13.shape, paired=True, tc=tc),
+                   m2.fmt.desc(*w2.shape, tc=tc), g)
 
     def weight_bytes(self) -> float:
         """Bytes of the dense shared expert (gate, up and down, 2 bytes per weight)."""
@@ -109,8 +120,8 @@ class LUTMoELayer:
         a = _lib.MoEArgs()
         a.hidden, a.inter, a.num_experts, a.top_k = ex.hidden, ex.inter, ex.num_experts, self.top_k
         a.dtype = _lib.BF16 if self.dtype == torch.bfloat16 else _lib.F16
-        a.w13 = ex.fmt.desc(2 * ex.inter, ex.hidden, paired=True)
-        a.w2 = ex.fmt.desc(ex.hidden, ex.inter)
+        a.w13 = ex.fmt.desc(2 * ex.inter, ex.hidden, paired=True, tc=ex.tc)
+        a.w2 = ex.fmt.desc(ex.hidden, ex.inter, tc=ex.tc)
         a.w13_tiled, a.w2_tiled = ex.w13.data_ptr(), ex.w2.data_ptr()
         a.w13_stride, a.w2_stride = ex.w13_stride, ex.w2_stride
         a.lut_table = None if ex.lut_table is None else ex.lut_table.data_ptr()

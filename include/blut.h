@@ -55,7 +55,14 @@ enum {
 
 enum { BLUT_F16 = 0, BLUT_BF16 = 1, BLUT_F32 = 2 };
 
-enum { BLUT_LAYOUT_PAIRED = 1 };
+/* Tiled layout flags (blut_mat_desc.layout).
+ *  BLUT_LAYOUT_PAIRED  row tile t of the first half (gate) and tile t of the
+ *                      second half (up) are stored next to each other.
+ *  BLUT_LAYOUT_TC      128-row tiles with one row's codes and tables per
+ *                      thread, for the tcgen05 (tensor memory) matmuls;
+ *                      FMT_B 4-bit and FMT_DENSE.  Without it: 16-row tiles
+ *                      in mma.sync fragment order, every format. */
+enum { BLUT_LAYOUT_PAIRED = 1, BLUT_LAYOUT_TC = 2 };
 
 /* Description of one weight matrix W [rows, cols] (y = W x, cols = K). */
 typedef struct {
@@ -68,9 +75,9 @@ typedef struct {
                      FMT_NESTED: 0 full (coarse + residual), 1 coarse only       */
   int32_t dtype;  /* compute dtype of weights and activations: BLUT_F16 / BF16.
                      FMT_R8 computes in bf16, FMT_B / NESTED in fp16             */
-  int32_t layout; /* tiled layout flags: BLUT_LAYOUT_PAIRED stores row tile t
-                     of the first half (gate) and tile t of the second half (up)
-                     next to each other; blut_moe_forward needs it on w13     */
+  int32_t layout; /* tiled layout flags (BLUT_LAYOUT_*); blut_moe_forward needs
+                     BLUT_LAYOUT_PAIRED on w13 / s13 and the same
+                     BLUT_LAYOUT_TC choice on w13 and w2 (and on s13, s2)     */
   int64_t rows;   /* N: output features                                        */
   int64_t cols;   /* K: input features                                         */
 } blut_mat_desc;

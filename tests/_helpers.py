@@ -75,8 +75,9 @@ def qm_from_numpy(fmt: LUTFormat, rows: int, cols: int, d: dict) -> QuantizedMat
     return QuantizedMatrix(fmt, rows, cols, g("codes"), g("tables"), g("codes2"), g("tables2"), g("scales"))
 
 
-def build_b_layer(fmt: LUTFormat, E: int, H: int, I: int, seed: int = 0):
-    """Oracle-encoded experts -> (LUTExperts, W13 list fp32, W2 list fp32)."""
+def build_b_layer(fmt: LUTFormat, E: int, H: int, I: int, seed: int = 0, tc=None):
+    """Oracle-encoded experts -> (LUTExperts, W13 list fp32, W2 list fp32).
+    ``tc``: tiled layout (None: tcgen05 when available, else mma.sync)."""
     rng = np.random.Generator(np.random.PCG64(seed))
     W13, W2, q13, q2 = [], [], [], []
     for _ in range(E):
@@ -88,7 +89,7 @@ def build_b_layer(fmt: LUTFormat, E: int, H: int, I: int, seed: int = 0):
         q2.append(qm_from_numpy(fmt, H, I, c2))
         W13.append(d13)
         W2.append(d2)
-    return LUTExperts.from_quantized(q13, q2), W13, W2
+    return LUTExperts.from_quantized(q13, q2, tc=tc), W13, W2
 
 
 def build_r8_layer(E: int, H: int, I: int, seed: int = 0, tier: int = 0, table_u16=None):

@@ -7,6 +7,7 @@ import shutil
 import subprocess
 
 import pytest
+import torch
 
 from tests.conftest import ROOT
 
@@ -53,6 +54,36 @@ def test_tiled_bytes_match_format_bytes(fmt, bpw):
     # weight); planes are 256-aligned, so at most 256 B of padding per plane
     stored = 1.125 if fmt.kind == "nested" else bpw
     assert rows * cols * stored <= n <= rows * cols * stored + 4 * 256
+
+
+@pytest.mark.parametrize("fmt,bpw", [
+    (LUTFormat("b", 4, 64), 1.0), (LUTFormat("b", 4, 32), 1.5), (LUTFormat("b", 4, 128), 0.75),
+    (LUTFormat("dense", 16, 0, dense_dtype=torch.float16), 2.0),
+    (LUTFormat("dense", 16, 0, dense_dtype=torch.bfloat16), 2.0),
+])
+@pytest.mark.parametrize("paired", [False, True])
+def test_tc_tiled_bytes_are_the_format_bytes(fmt, bpw, paired):
+    """The tcgen05 layout stores exactly the format's bytes (no padding at these shapes)."""
+    for rows, cols in ((2816, 2048), (2048, 1408), (11264, 2048), (2048, 5632)):
+        assert tiled_bytes(fmt, rows, cols, paired, tc=True) == rows * cols * bpw
+
+
+def test_tc_layout_availability():
+    b4 = LUTFormat("b", 4, 64)
+    assert b4.has_tc_layout(2816, 2048, paired=True) and b4.has_tc_layout(2048, 1408)
+    assert not b4.has_tc_layout(2688, 2048, paired=True)        # paired rows % 256
+    assert not b4.has_tc_layout(2048 + 48, 2048)                 # rows % 128
+    assert not b4.has_tc_layout(2048, 1408 + 32)                 # cols % 64
+    for fmt in (LUTFormat("b", 2, 64), LUTFormat("b", 3, 64), LUTFormat("nested", 4, 64, 0),
+                LUTFormat("r8", 8, 128)):
+        assert not fmt.has_tc_layout(2048, 2048)                 # mma.sync layout only
+
+
+def test_moe_forward_rejects_mixed_matmul_paths():
+    fmt = LUTFormat("b", 4, 64)
+    a = _args(w13=fmt.desc(2816, 2048, paired=True, tc=True),
+              w13_stride=tiled_bytes(fmt, 2816, 2048, True, tc=True))
+    assert _lib.lib().blut_moe_forward(C.byref(a), None, 0, None) == _lib.BLUT_ERR_INVALID
 
 
 def test_tiled_bytes_rejects_bad_shapes():

@@ -159,6 +159,31 @@ def test_tiled_layout_lookup_bit_exact(fmt, paired):
     assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
 
 
+@pytest.mark.parametrize("paired", [False, True])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_tc_layout_lookup_bit_exact(group, paired):
+    """BLUT_LAYOUT_TC: pack + the tcgen05 matmul's per-row decode reproduce the canonical dequant."""
+    from block_lut_b200.formats import dequant_tiled, pack_tiled
+    fmt = LUTFormat("b", 4, group)
+    rng = np.random.Generator(np.random.PCG64(500 + group))
+    rows, cols = 512, 384
+    qm = encode(cuda(O.student_t_weights(rng, (rows, cols))), fmt)
+    buf, _ = pack_tiled([qm], paired=paired, tc=True)
+    out = dequant_tiled(fmt, rows, cols, buf, paired=paired, tc=True)
+    assert torch.equal(out.view(torch.int16), dequant(qm).view(torch.int16))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_tc_layout_dense_round_trip(dtype):
+    from block_lut_b200.formats import dense_matrix, dequant_tiled, pack_tiled
+    rng = np.random.Generator(np.random.PCG64(77))
+    w = torch.from_numpy(rng.standard_normal((256, 160)).astype(np.float32)).to("cuda", dtype)
+    dm = dense_matrix(w)
+    for paired in (False, True):
+        buf, _ = pack_tiled([dm], paired=paired, tc=True)
+        assert torch.equal(dequant_tiled(dm.fmt, 256, 160, buf, paired=paired, tc=True), w)
+
+
 @pytest.mark.parametrize("tier", [0, 1, 2])
 def test_tiled_layout_r8_and_dense(tier):
     from block_lut_b200.formats import dense_matrix, dequant_tiled, pack_tiled

@@ -13,14 +13,21 @@ from block_lut_b200.moe import LUTExperts, LUTMoELayer, SharedExpert
 
 pytestmark = pytest.mark.gpu
 
-FORMATS = [LUTFormat("b", 4, 64), LUTFormat("b", 4, 32), LUTFormat("b", 4, 128), LUTFormat("b", 3, 64),
-           LUTFormat("b", 2, 64), LUTFormat("b", 2, 128), LUTFormat("nested", 4, 64, 0),
-           LUTFormat("nested", 4, 64, 1)]
+# (format, tiled layout): 4-bit formats run on the tcgen05 path by default;
+# the mma.sync path is kept for every format.
+FORMATS = [(LUTFormat("b", 4, 64), True), (LUTFormat("b", 4, 32), True), (LUTFormat("b", 4, 128), True),
+           (LUTFormat("b", 4, 64), False), (LUTFormat("b", 3, 64), False), (LUTFormat("b", 2, 64), False),
+           (LUTFormat("b", 2, 128), False), (LUTFormat("nested", 4, 64, 0), False),
+           (LUTFormat("nested", 4, 64, 1), False)]
 
 
-@pytest.fixture(scope="module", params=FORMATS, ids=lambda f: f"{f.kind}{f.bits}g{f.group}t{f.tier}")
+@pytest.fixture(scope="module", params=FORMATS,
+                ids=lambda p: f"{p[0].kind}{p[0].bits}g{p[0].group}t{p[0].tier}-{'tc' if p[1] else 'mma'}")
 def b_layer(request):
-    return request.param, build_b_layer(request.param, E=6, H=256, I=256, seed=1)
+    fmt, tc = request.param
+    layer = build_b_layer(fmt, E=6, H=256, I=256, seed=1, tc=tc)
+    assert layer[0].tc == tc
+    return fmt, layer
 
 
 @pytest.mark.parametrize("T,k", [(1, 2), (3, 2), (8, 2), (16, 3), (80, 2)])
@@ -140,9 +147,10 @@ def test_qwen15_layer_format_b_4bit_g64(T):
     check_layer(out, ref, torch.float16, f"qwen1.5 layer T={T}")
 
 
-def test_shared_expert_modes_and_graph_capture():
+@pytest.mark.parametrize("tc", [True, False], ids=["tc", "mma"])
+def test_shared_expert_modes_and_graph_capture(tc):
     fmt = LUTFormat("b", 4, 64)
-    experts, W13, W2 = build_b_layer(fmt, E=4, H=256, I=128, seed=5)
+    experts, W13, W2 = build_b_layer(fmt, E=4, H=256, I=128, seed=5, tc=tc)
     rng = np.random.Generator(np.random.PCG64(12))
     s13 = O.student_t_weights(rng, (256, 256)).astype(np.float16)
     s2 = O.student_t_weights(rng, (256, 128)).astype(np.float16)
@@ -151,7 +159,7 @@ def test_shared_expert_modes_and_graph_capture():
     x = cuda(O.rms_activations(rng, T, 256).astype(np.float16))
     ids, tw = routing_inputs(rng, T, 4, 2)
     for mode in (0, 1):
-        sh = SharedExpert.from_dense(cuda(s13), cuda(s2), cuda(gate) if mode else None)
+        sh = SharedExpert.from_dense(cuda(s13), cuda(s2), cuda(gate) if mode else None, tc=tc)
         layer = LUTMoELayer(experts, 2, shared=sh, shared_gate_mode=mode)
         out = layer.forward(x, cuda(ids), cuda(tw))
         if mode == 1:
