@@ -309,7 +309,8 @@ def run_ours(a):
                    "parallelism": "single GPU", "graph": "CUDA graph of the 24-layer step",
                    "l2": f"inputs larger than L2: {sum(n_active) * 3 * I * H * bpw / 1e9:.1f} GB of expert "
                          f"weights streamed per step"},
-        "roofline": {"kernel": "lut_mm_kernel (routed gate/up+SiLU*up and down, per layer)", "bound": "hbm",
+        "roofline": {"kernel": ("tc_mm_kernel (tcgen05" if moes[0].experts.tc else "lut_mm_kernel (mma.sync") +
+                               "; routed gate/up+SiLU*up and down, per layer)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s", "traffic": None,

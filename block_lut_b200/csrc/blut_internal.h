@@ -24,6 +24,15 @@ struct PlanPtrs {
   int* tk_slot;   // [T*k] slot of (token, j), -1 if the id was invalid
   int* slot_tok;  // [T*k] token of each slot
   int* counters;  // [kNumCounters] work-item counters of the tcgen05 launches
+  int* zero;      // [nzero] split-K arrival counters, zeroed by the plan kernel
+  int nzero;
+};
+
+// K slices of the four matmul passes: 0 routed gate/up, 1 routed down,
+// 2 shared gate/up, 3 shared down (tcgen05 passes only; 1 = no split).
+struct MoESplit {
+  int ks[4], bps[4], units[4];
+  int64_t groups[4];  // bound on token groups of the pass
 };
 
 constexpr int kNumCounters = 4;  // routed gate/up, routed down, shared gate/up, shared down
@@ -36,12 +45,17 @@ struct MoEWs {
   float* logits;  // [T][E (+1)] router logits (fp32)
   PlanPtrs pp;
   uint8_t *xf, *af, *xfs, *afs;
-  float *y, *ys;
+  float *y, *ys;               // expert outputs, ks[1] / ks[3] slices
+  int64_t y_sstride, ys_sstride;
+  float *part_r, *part_s;      // gate/up partial sums of split K
+  int *cnt_r, *cnt_s;          // their arrival counters
   int64_t ntmax, sntmax;
+  MoESplit split;
 };
 
 int num_sms();
 size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws);
+void moe_split(const blut_moe_args& a, MoESplit& s);
 int validate_moe(const blut_moe_args& a);
 int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaStream_t stream);
 int moe_launch_count(const blut_moe_args& a);

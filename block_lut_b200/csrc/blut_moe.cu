@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) *pp.status = 0;
   if (threadIdx.x < kNumCounters) pp.counters[threadIdx.x] = 0;
+  for (int i = threadIdx.x; i < pp.nzero; i += blockDim.x) pp.zero[i] = 0;
   if (logits) {  // row t: topk_e expert logits, then the gate logit when has_gate
     for (int t = warp; t < num_tokens; t += 32) {
       warp_topk(logits + (int64_t)t * R, topk_e, ids_in ? 0 : top_k, renorm, ids_out + (int64_t)t * top_k,
@@ -318,11 +319,23 @@ __global__ void __launch_bounds__(32) gather_bfrag_kernel(const uint16_t* __rest
 
 // -------------------------------------------------------------- combine ---
 // out[t] = sum_j w[t,j] * y[slot(t,j)] (+ g_t * y_shared[t]), fp32, one rounding.
+// Expert outputs computed in K slices are summed slice by slice first (in
+// slice order, so the result does not depend on which slice finished first).
+__device__ __forceinline__ float4 sum_slices(const float* p, int ks, int64_t stride) {
+  float4 v = *reinterpret_cast<const float4*>(p);
+  for (int s = 1; s < ks; ++s) {
+    const float4 w = *reinterpret_cast<const float4*>(p + s * stride);
+    v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+  }
+  return v;
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, const float* __restrict__ ys,
                                                       const float* __restrict__ tw, const int* __restrict__ tk_slot,
                                                       const float* __restrict__ sg, int top_k, int hidden,
-                                                      int shared_mode, void* __restrict__ out_v, int out_f32) {
+                                                      int shared_mode, void* __restrict__ out_v, int out_f32,
+                                                      int ks_r, int64_t ystride, int ks_s, int64_t ysstride) {
   const int t = blockIdx.x;
   for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < hidden; h += gridDim.y * blockDim.x * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -330,12 +343,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
       const int slot = tk_slot[(int64_t)t * top_k + j];
       if (slot < 0) continue;
       const float w = tw[(int64_t)t * top_k + j];
-      const float4 v = *reinterpret_cast<const float4*>(y + (int64_t)slot * hidden + h);
+      const float4 v = sum_slices(y + (int64_t)slot * hidden + h, ks_r, ystride);
       acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
     }
     if (shared_mode >= 0) {
       const float g = shared_mode == 1 ? sg[t] : 1.f;
-      const float4 v = *reinterpret_cast<const float4*>(ys + (int64_t)t * hidden + h);
+      const float4 v = sum_slices(ys + (int64_t)t * hidden + h, ks_s, ysstride);
       acc.x += g * v.x; acc.y += g * v.y; acc.z += g * v.z; acc.w += g * v.w;
     }
     if (out_f32) {
@@ -366,6 +379,44 @@ static bool same_format(const blut_mat_desc& a, const blut_mat_desc& b) {
   return a.format == b.format && a.bits == b.bits && a.group == b.group && a.tier == b.tier && a.dtype == b.dtype;
 }
 
+// Expected number of experts hit by T tokens choosing k of E uniformly.
+static double expected_active(int T, int k, int E) {
+  double miss = 1.0;
+  for (int t = 0; t < T; ++t) miss *= 1.0 - (double)k / E;
+  return E * (1.0 - miss);
+}
+
+// K slices per tcgen05 pass: split while the expected work items are fewer
+// than two per resident CTA (two CTAs per SM) and every slice keeps at least
+// two column blocks.  Gate/up passes split at most 8 ways (their partial sums
+// go through memory), down passes 16.
+void moe_split(const blut_moe_args& a, MoESplit& s) {
+  const int sms = num_sms();
+  const int64_t T = a.num_tokens, K = a.top_k, E = a.num_experts, S = T * K;
+  const double est_r = expected_active((int)T, (int)K, (int)E) + (double)S / kGroupTok;
+  const int64_t gmax_r = std::min(E, S) + (S + kGroupTok - 1) / kGroupTok + 1;
+  const int64_t gmax_s = (T + kGroupTok - 1) / kGroupTok;
+  const blut_mat_desc* d[4] = {&a.w13, &a.w2, &a.s13, &a.s2};
+  for (int i = 0; i < 4; ++i) {
+    s.ks[i] = 1;
+    s.bps[i] = 0;
+    s.units[i] = 0;
+    s.groups[i] = i < 2 ? gmax_r : gmax_s;
+    TiledLayout L;
+    if ((i >= 2 && a.shared_inter <= 0) || !make_layout(*d[i], L)) continue;
+    s.bps[i] = (int)L.nchunks;
+    if (!L.tc) continue;
+    s.units[i] = (int)((L.ntiles + 1) / 2);
+    const double est = (i < 2 ? est_r : (double)gmax_s) * s.units[i];
+    const int max_ks = (i % 2 == 0) ? 8 : 16;
+    int ks = 1;
+    while (ks * 2 <= max_ks && L.nchunks / (ks * 2) >= 2 && est * ks < 4.0 * sms) ks *= 2;
+    const int bps = (int)((L.nchunks + ks - 1) / ks);
+    s.ks[i] = (int)((L.nchunks + bps - 1) / bps);
+    s.bps[i] = bps;
+  }
+}
+
 // Workspace carve-up; returns total bytes, fills pointers when base != null.
 size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
   const int64_t T = a.num_tokens, K = a.top_k, E = a.num_experts, H = a.hidden, I = a.inter;
@@ -390,11 +441,28 @@ size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
   size_t o_tk = take(S * 4), o_st = take(S * 4);
   size_t o_xf = take(ntmax * (H / kChunk) * kBfragChunkBytes);
   size_t o_af = take(ntmax * (I / kChunk) * kBfragChunkBytes);
-  size_t o_y = take(S * H * 4);
+  MoESplit sp;
+  moe_split(a, sp);
+  size_t o_y = take(S * H * 4 * sp.ks[1]);
   size_t o_xfs = sh ? take(sntmax * (H / kChunk) * kBfragChunkBytes) : 0;
   size_t o_afs = sh ? take(sntmax * (a.shared_inter / kChunk) * kBfragChunkBytes) : 0;
-  size_t o_ys = sh ? take(T * H * 4) : 0;
+  size_t o_ys = sh ? take(T * H * 4 * sp.ks[3]) : 0;
+  // split-K partial sums of the gate/up passes: [item][gate|up][128 rows][32 tokens] fp32
+  const int64_t ku_r = sp.ks[0] > 1 ? sp.groups[0] * sp.units[0] : 0;
+  const int64_t ku_s = sp.ks[2] > 1 ? sp.groups[2] * sp.units[2] : 0;
+  size_t o_part_r = take(ku_r * sp.ks[0] * 2 * kTcRows * 32 * 4);
+  size_t o_part_s = take(ku_s * sp.ks[2] * 2 * kTcRows * 32 * 4);
+  size_t o_cnt = take((ku_r + ku_s) * kTcDecodeWarps * 4);
   if (base && ws) {
+    w.split = sp;
+    w.y_sstride = S * H;
+    w.ys_sstride = T * H;
+    w.part_r = reinterpret_cast<float*>(base + o_part_r);
+    w.part_s = reinterpret_cast<float*>(base + o_part_s);
+    w.cnt_r = reinterpret_cast<int*>(base + o_cnt);
+    w.cnt_s = w.cnt_r + ku_r * kTcDecodeWarps;
+    w.pp.zero = w.cnt_r;
+    w.pp.nzero = (int)((ku_r + ku_s) * kTcDecodeWarps);
     w.status = reinterpret_cast<int*>(base + o_status);
     w.ids = reinterpret_cast<int32_t*>(base + o_ids);
     w.tw = reinterpret_cast<float*>(base + o_tw);
@@ -509,13 +577,6 @@ static int choose_units_per_item(double est_groups, int units, int sms) {
   return w;
 }
 
-// Expected number of experts hit by T tokens choosing k of E uniformly.
-static double expected_active(int T, int k, int E) {
-  double miss = 1.0;
-  for (int t = 0; t < T; ++t) miss *= 1.0 - (double)k / E;
-  return E * (1.0 - miss);
-}
-
 // Error check after a stage.  With BLUT_DEBUG_SYNC set, every stage also
 // synchronises the stream, so a failing kernel is named by its own stage.
 static bool debug_sync() {
@@ -595,7 +656,8 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   const GroupTab routed{ws.pp.meta + 0, ws.pp.g_expert, ws.pp.g_slot0, ws.pp.g_ntok, ws.pp.g_nt0};
   const GroupTab shared{ws.pp.meta + 2, ws.pp.sg_expert, ws.pp.sg_slot0, ws.pp.sg_ntok, ws.pp.sg_nt0};
   auto pass = [&](const blut_mat_desc& d, const void* w, int64_t stride, const GroupTab& gt, double est,
-                  const uint8_t* bin, uint8_t* act, int out_k, float* y, int counter) -> int {
+                  const uint8_t* bin, uint8_t* act, int out_k, float* y, int counter, float* part, int* cnt,
+                  int64_t y_sstride) -> int {
     const bool pair = act != nullptr;
     const int K = (int)d.cols;
     if (d.layout & BLUT_LAYOUT_TC) {
@@ -612,6 +674,11 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.y_ld = H;
       t.counter = ws.pp.counters + counter;
       t.status = ws.status;
+      t.ks = ws.split.ks[counter];
+      t.bps = ws.split.bps[counter];
+      t.part = part;
+      t.part_cnt = cnt;
+      t.y_sstride = y_sstride;
       return launch_tc_mm(d, t, sms, stream) == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
     }
     MMParams m{};
@@ -634,36 +701,43 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
 
   // 4. gate/up + SiLU*up (routed, then shared)
   if (ev && cudaEventRecord(ev[0], stream) != cudaSuccess) return BLUT_ERR_INVALID;
-  if ((rc = pass(a.w13, a.w13_tiled, a.w13_stride, routed, est_groups, ws.xf, ws.af, a.inter, nullptr, 0)) !=
+  if ((rc = pass(a.w13, a.w13_tiled, a.w13_stride, routed, est_groups, ws.xf, ws.af, a.inter, nullptr, 0,
+                 ws.part_r, ws.cnt_r, 0)) !=
       BLUT_OK)
     return rc;
   if ((rc = stage_done("routed gate/up", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[1], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if (sh) {
-    if ((rc = pass(a.s13, a.s13_tiled, 0, shared, est_sgroups, ws.xfs, ws.afs, a.shared_inter, nullptr, 2)) !=
+    if ((rc = pass(a.s13, a.s13_tiled, 0, shared, est_sgroups, ws.xfs, ws.afs, a.shared_inter, nullptr, 2,
+                   ws.part_s, ws.cnt_s, 0)) !=
         BLUT_OK)
       return rc;
     if ((rc = stage_done("shared gate/up", stream)) != BLUT_OK) return rc;
   }
   // 5. down (routed, then shared)
   if (ev && cudaEventRecord(ev[2], stream) != cudaSuccess) return BLUT_ERR_INVALID;
-  if ((rc = pass(a.w2, a.w2_tiled, a.w2_stride, routed, est_groups, ws.af, nullptr, 0, ws.y, 1)) != BLUT_OK)
+  if ((rc = pass(a.w2, a.w2_tiled, a.w2_stride, routed, est_groups, ws.af, nullptr, 0, ws.y, 1, nullptr,
+                 nullptr, ws.y_sstride)) != BLUT_OK)
     return rc;
   if ((rc = stage_done("routed down", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[3], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if (sh) {
-    if ((rc = pass(a.s2, a.s2_tiled, 0, shared, est_sgroups, ws.afs, nullptr, 0, ws.ys, 3)) != BLUT_OK) return rc;
+    if ((rc = pass(a.s2, a.s2_tiled, 0, shared, est_sgroups, ws.afs, nullptr, 0, ws.ys, 3, nullptr, nullptr,
+                   ws.ys_sstride)) != BLUT_OK) return rc;
     if ((rc = stage_done("shared down", stream)) != BLUT_OK) return rc;
   }
 
   // 6. combine
   const int smode = sh ? a.shared_gate_mode : -1;
+  const dim3 cgrid(T, (H + 1023) / 1024);
   if (bf16)
-    combine_kernel<true><<<dim3(T, (H + 1023) / 1024), 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
-                                                a.out_f32);
+    combine_kernel<true><<<cgrid, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
+                                                    a.out_f32, ws.split.ks[1], ws.y_sstride, ws.split.ks[3],
+                                                    ws.ys_sstride);
   else
-    combine_kernel<false><<<dim3(T, (H + 1023) / 1024), 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
-                                                 a.out_f32);
+    combine_kernel<false><<<cgrid, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
+                                                     a.out_f32, ws.split.ks[1], ws.y_sstride, ws.split.ks[3],
+                                                     ws.ys_sstride);
   return stage_done("combine", stream);
 }
 

@@ -13,7 +13,7 @@
 //    activations into a ring of shared-memory stages;
 //  * warp 1 (MMA): allocates the tensor memory and issues, from one thread,
 //    tcgen05.mma M=128 x N=16|32 x K=16 per tile and slab, fp32 accumulators
-//    in tensor memory (double-buffered across items);
+//    in tensor memory;
 //  * warps 2..9 (decode): one thread per weight row.  For LUT formats each
 //    thread looks its row's codes up in its row's tables (byte permutes in
 //    registers) and writes the fp16 A operand of a 64-column half-block to
@@ -38,7 +38,13 @@ constexpr int kTcThreads = 32 * (2 + kTcDecodeWarps);
 constexpr int kTcRingBudget = 96 * 1024;
 constexpr int kTcQueue = 4;          // depth of the shared-memory item queue
 constexpr int kTcDCols = 64;         // tensor-memory columns of one accumulator buffer (2 tiles x N<=32)
-constexpr int kTcACol0 = 2 * kTcDCols;  // first column of the A ring (2 slots x 2 tiles x 32)
+// Tensor memory of a CTA (256 columns, two CTAs per SM): LUT formats keep one
+// accumulator buffer (columns 0-63) and a ring of three A slots of 64 columns
+// (2 tiles x 64 fp16 columns of K); dense weights need no A slots and
+// double-buffer the accumulators so the MMA runs one item ahead of the
+// epilogue.
+constexpr int kTcASlots = 3;
+constexpr int kTcACol0 = kTcDCols;
 
 struct TcParams {
   const uint8_t* w;        // tiled (BLUT_LAYOUT_TC) matrices of all experts
@@ -56,8 +62,18 @@ struct TcParams {
   int bin_nch;             // K / 128
   uint8_t* act_out;        // pair epilogue: down-projection activations, same order
   int out_nch;             // I / 128
-  float* y_out;            // single epilogue: y[slot][y_ld]
+  float* y_out;            // single epilogue: y[slot][y_ld] (slice s of split K at y_out + s * y_sstride)
   int y_ld;
+  int64_t y_sstride;
+  // Split K: each (group, unit) is cut into ks slices of bps blocks.  Gate/up
+  // slices write fp32 partials (part, [item][gate|up][128 rows][32 tokens]);
+  // per epilogue warp, the slice that arrives last at
+  // part_cnt[(group * units + unit) * 8 + warp] sums them in slice order and
+  // runs the epilogue of that warp's rows and tokens.  Down slices write
+  // separate output rows that the combine sums in slice order.
+  int ks, bps;
+  float* part;
+  int* part_cnt;
   int* counter;            // item counter (zeroed by the plan kernel)
   int* status;
   int stages;
@@ -232,19 +248,20 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
   constexpr bool kDense = Dec::kDense;
   constexpr int KB = Dec::KB;
   constexpr uint32_t kCols = kDense ? 128 : 256;  // tensor-memory columns of this CTA
+  constexpr int kDBufs = kDense ? 2 : 1;           // accumulator buffers
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [8]
   uint64_t* empty = full + 8;                          // [8]
-  uint64_t* afull = full + 16;                         // [2] A slot written (decode warps)
-  uint64_t* aempty = full + 18;                        // [2] A slot read (MMA commit)
-  uint64_t* dfull = full + 20;                         // [2] accumulators complete (MMA commit)
-  uint64_t* dempty = full + 22;                        // [2] accumulators read (epilogue warps)
-  uint64_t* qfull = full + 24;                         // [kTcQueue] item posted
-  uint64_t* qempty = full + 28;                        // [kTcQueue] item taken by every role
-  uint64_t* fin = full + 32;                           // last MMAs complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 33);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 34);
-  volatile int* qitem = reinterpret_cast<volatile int*>(full + 35);  // [kTcQueue]
+  uint64_t* afull = full + 16;                         // [kTcASlots] A slot written (decode warps)
+  uint64_t* aempty = full + 20;                        // [kTcASlots] A slot read (MMA commit)
+  uint64_t* dfull = full + 24;                         // [kDBufs] accumulators complete (MMA commit)
+  uint64_t* dempty = full + 26;                        // [kDBufs] accumulators read (epilogue warps)
+  uint64_t* qfull = full + 28;                         // [kTcQueue] item posted
+  uint64_t* qempty = full + 32;                        // [kTcQueue] item taken by every role
+  uint64_t* fin = full + 36;                           // last MMAs complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 37);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 38);
+  volatile int* qitem = reinterpret_cast<volatile int*>(full + 39);  // [kTcQueue]
   uint8_t* ring = smem + 512;
   const int S = p.stages;
   const int stage_bytes = tc_stage_bytes<Dec>(p);
@@ -258,9 +275,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
       mbar_init(smem_u32(full + s), 1);
       mbar_init(smem_u32(empty + s), kDense ? 1 : 1 + kTcDecodeWarps);
     }
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < kTcASlots; ++j) {
       mbar_init(smem_u32(afull + j), kTcDecodeWarps);
       mbar_init(smem_u32(aempty + j), 1);
+    }
+    for (int j = 0; j < kDBufs; ++j) {
       mbar_init(smem_u32(dfull + j), 1);
       mbar_init(smem_u32(dempty + j), kTcDecodeWarps);
     }
@@ -281,7 +300,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_items = *p.gt.n_groups * p.units;
+  const int n_items = *p.gt.n_groups * p.units * p.ks;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
@@ -297,13 +316,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         qitem[qs] = item;
         mbar_arrive(smem_u32(qfull + qs));
         if (item < 0) break;
-        const int gi = item / p.units, u = item % p.units;
+        const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
+        const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
         const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
         const int nt0 = p.gt.nt0[gi];
         const int ntl = min(2, p.ntiles - 2 * u);
         const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
         bool ok = true;
-        for (int b = 0; b < p.nblocks; ++b, ++it) {
+        for (int b = b0; b < b1; ++b, ++it) {
           const int s = (int)(it % S);
           const int64_t use = it / S;
           if (use > 0 && !wait_or_abort(smem_u32(empty + s), (uint32_t)((use - 1) & 1), abort_flag, p.status)) {
@@ -341,17 +361,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         const int item = qitem[qs];
         mbar_arrive(smem_u32(qempty + qs));
         if (item < 0) break;
-        const int gi = item / p.units, u = item % p.units;
+        const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
+        const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
         const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
         const int ntl = min(2, p.ntiles - 2 * u);
         const uint32_t idesc = tc_idesc(Dec::kBF16, nnt <= 2 ? 16 : 32);
-        const int db = (int)(id & 1);
-        if (id >= 2 && !wait_or_abort(smem_u32(dempty + db), (uint32_t)(((id >> 1) - 1) & 1), abort_flag, p.status))
+        const int db = (int)(id % kDBufs);
+        if (id >= kDBufs &&
+            !wait_or_abort(smem_u32(dempty + db), (uint32_t)(((id / kDBufs) - 1) & 1), abort_flag, p.status))
           break;
         tc_fence_after();
         const uint32_t dcol = tmem + db * kTcDCols;
         bool ok = true;
-        for (int b = 0; b < p.nblocks && ok; ++b, ++it) {
+        for (int b = b0; b < b1 && ok; ++b, ++it) {
           const int s = (int)(it % S);
           if (!wait_or_abort(smem_u32(full + s), (uint32_t)((it / S) & 1), abort_flag, p.status)) {
             ok = false;
@@ -365,14 +387,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
               const uint64_t bd = tc_desc(st + boff + sl * 256, 128, KB * 16);
               for (int t = 0; t < ntl; ++t) {
                 const uint64_t ad = tc_desc(st + t * p.piece[0] + sl * 2 * 2048, 2048, 128);
-                tc_mma_ss(dcol + t * 32, ad, bd, idesc, (b | sl) != 0);
+                tc_mma_ss(dcol + t * 32, ad, bd, idesc, ((b - b0) | sl) != 0);
               }
             }
           } else {
 #pragma unroll
             for (int h = 0; h < Dec::kHalves; ++h, ++ia) {
-              const int j = (int)(ia & 1);
-              if (!wait_or_abort(smem_u32(afull + j), (uint32_t)((ia >> 1) & 1), abort_flag, p.status)) {
+              const int j = (int)(ia % kTcASlots);
+              if (!wait_or_abort(smem_u32(afull + j), (uint32_t)((ia / kTcASlots) & 1), abort_flag, p.status)) {
                 ok = false;
                 break;
               }
@@ -381,7 +403,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
               for (int sl = 0; sl < 4; ++sl) {
                 const uint64_t bd = tc_desc(st + boff + (h * 4 + sl) * 256, 128, KB * 16);
                 for (int t = 0; t < ntl; ++t)
-                  tc_mma_ts(dcol + t * 32, tmem + kTcACol0 + j * 64 + t * 32 + sl * 8, bd, idesc, (b | h | sl) != 0);
+                  tc_mma_ts(dcol + t * 32, tmem + kTcACol0 + j * 64 + t * 32 + sl * 8, bd, idesc,
+                            ((b - b0) | h | sl) != 0);
               }
               tc_commit(smem_u32(aempty + j));
             }
@@ -413,12 +436,13 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(qempty + qs));
       if (item < 0) break;
-      const int gi = item / p.units, u = item % p.units;
+      const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
+        const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
       const int ntok = p.gt.ntok[gi];
       const int ntl = min(2, p.ntiles - 2 * u);
       if constexpr (!kDense) {
         const bool active = t < ntl;
-        for (int b = 0; b < p.nblocks; ++b, ++it) {
+        for (int b = b0; b < b1; ++b, ++it) {
           const int s = (int)(it % S);
           ok = wait_or_abort(smem_u32(full + s), (uint32_t)((it / S) & 1), abort_flag, p.status);
           if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
@@ -427,9 +451,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
           const uint8_t* tp = st + qoff1 + t * p.piece[1];
 #pragma unroll
           for (int h = 0; h < Dec::kHalves; ++h, ++ia) {
-            const int j = (int)(ia & 1);
-            if (ia >= 2) {
-              ok = wait_or_abort(smem_u32(aempty + j), (uint32_t)(((ia >> 1) - 1) & 1), abort_flag, p.status);
+            const int j = (int)(ia % kTcASlots);
+            if (ia >= kTcASlots) {
+              ok = wait_or_abort(smem_u32(aempty + j), (uint32_t)(((ia / kTcASlots) - 1) & 1), abort_flag,
+                                 p.status);
               if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
             }
             tc_fence_after();
@@ -450,8 +475,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         if (*abort_flag) break;
       }
       // epilogue
-      const int db = (int)(id & 1);
-      ok = wait_or_abort(smem_u32(dfull + db), (uint32_t)((id >> 1) & 1), abort_flag, p.status);
+      const int db = (int)(id % kDBufs);
+      ok = wait_or_abort(smem_u32(dfull + db), (uint32_t)((id / kDBufs) & 1), abort_flag, p.status);
       if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
       tc_fence_after();
       const uint32_t dcol = tmem + lane_base + db * kTcDCols;
@@ -465,6 +490,48 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(dempty + db));
+        if (p.ks > 1) {
+          // partial sums of this slice; the last slice to arrive finishes the unit
+          float* mine = p.part + (int64_t)item * (2 * kTcRows * 32) + row * 32 + 16 * t;
+#pragma unroll
+          for (int n = 0; n < 16; n += 4) {
+            __stcg(reinterpret_cast<float4*>(mine + n),
+                   make_float4(__uint_as_float(g[n]), __uint_as_float(g[n + 1]), __uint_as_float(g[n + 2]),
+                               __uint_as_float(g[n + 3])));
+            __stcg(reinterpret_cast<float4*>(mine + kTcRows * 32 + n),
+                   make_float4(__uint_as_float(v[n]), __uint_as_float(v[n + 1]), __uint_as_float(v[n + 2]),
+                               __uint_as_float(v[n + 3])));
+          }
+          // Each warp owns its 32 rows x 16 tokens, so it counts its own slices:
+          // no barrier across warps (which an aborting warp could leave waiting).
+          __threadfence();
+          __syncwarp();
+          int last = 0;
+          if (lane == 0) last = atomicAdd(p.part_cnt + ku * kTcDecodeWarps + dw, 1) == p.ks - 1;
+          if (__shfl_sync(0xffffffffu, last, 0) == 0) {
+            ++id;
+            continue;
+          }
+          __threadfence();
+          float gs[16], us[16];
+#pragma unroll
+          for (int n = 0; n < 16; ++n) gs[n] = us[n] = 0.f;
+          for (int sl = 0; sl < p.ks; ++sl) {
+            const float* src = p.part + ((int64_t)ku * p.ks + sl) * (2 * kTcRows * 32) + row * 32 + 16 * t;
+#pragma unroll
+            for (int n = 0; n < 16; n += 4) {
+              const float4 a = __ldcg(reinterpret_cast<const float4*>(src + n));
+              const float4 c = __ldcg(reinterpret_cast<const float4*>(src + kTcRows * 32 + n));
+              gs[n] += a.x; gs[n + 1] += a.y; gs[n + 2] += a.z; gs[n + 3] += a.w;
+              us[n] += c.x; us[n + 1] += c.y; us[n + 2] += c.z; us[n + 3] += c.w;
+            }
+          }
+#pragma unroll
+          for (int n = 0; n < 16; ++n) {
+            g[n] = __float_as_uint(gs[n]);
+            v[n] = __float_as_uint(us[n]);
+          }
+        }
         const int col = u * kTcRows + row;  // K index of the down projection
         const int nt0 = p.gt.nt0[gi];
         uint8_t* dst = p.act_out + (int64_t)(col >> 7) * 2048 + tc_bact_byte(0, col & 127);
@@ -491,7 +558,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         if (lane == 0) mbar_arrive(smem_u32(dempty + db));
         if (t < ntl) {
           const int hrow = (2 * u + t) * kTcRows + row;
-          float* y = p.y_out + (int64_t)p.gt.slot0[gi] * p.y_ld + hrow;
+          float* y = p.y_out + (item % p.ks) * p.y_sstride + (int64_t)p.gt.slot0[gi] * p.y_ld + hrow;
 #pragma unroll
           for (int n = 0; n < 16; ++n)
             if (n < ntok) y[(int64_t)n * p.y_ld] = __uint_as_float(v0[n]);
@@ -527,11 +594,18 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
     if (cached_smem != smem) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
-      int nb = 0;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kTcThreads, smem);
+      // Two CTAs per SM share its 512 tensor-memory columns when their shared
+      // memory fits (the occupancy query can answer one here, as it models a
+      // smaller shared-memory carveout); a CTA that finds no SM slot free just
+      // starts later and finds the work counter exhausted.
+      int dev = 0, smem_sm = 0, nb = 0;
+      e = cudaGetDevice(&dev);
+      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+      if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kTcThreads, smem);
       if (e != cudaSuccess) return e;
-      // two CTAs share the 512 tensor-memory columns of an SM
-      cached_per_sm = nb < 1 ? 1 : (nb > 2 ? 2 : nb);
+      cached_per_sm = (nb >= 2 || 2 * (smem + 1024) <= smem_sm) ? 2 : 1;
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      if (e != cudaSuccess) return e;
       cached_smem = smem;
     }
     per_sm = cached_per_sm;
