@@ -31,6 +31,7 @@ namespace blut {
 constexpr int kMaxConsumers = 6;
 constexpr int kRingBudget = 96 * 1024;       // shared-memory ring bytes per CTA
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint32_t kWaitSleepNs = 20000;  // longest hardware sleep of one try (woken early on completion)
 
 struct GroupTab {
   const int* n_groups;  // device scalar
@@ -85,8 +86,8 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
   if (*abort_flag) return false;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1; i < (1u << 31); ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0) {
+    if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
+    if ((i & 15) == 0) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) break;
     }

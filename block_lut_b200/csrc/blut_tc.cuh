@@ -231,6 +231,22 @@ struct TcDecDense {
   __device__ __forceinline__ static void decode(const uint8_t*, const uint8_t*, int, int, uint32_t (&)[32]) {}
 };
 
+// Position in a ring of n barrier-guarded slots: slot index, the parity of
+// the slot's current phase, and whether the ring has wrapped (a slot being
+// reused must first see its previous phase released).
+struct TcRing {
+  int i = 0;
+  uint32_t ph = 0;
+  bool wrapped = false;
+  __device__ __forceinline__ void next(int n) {
+    if (++i == n) {
+      i = 0;
+      ph ^= 1u;
+      wrapped = true;
+    }
+  }
+};
+
 // ------------------------------------------------------------------ kernel --
 template <class Dec>
 __host__ __device__ inline int tc_stage_bytes(const TcParams& p) {
@@ -305,12 +321,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
-      int64_t it = 0;
-      for (int k = 0;; ++k) {
-        const int qs = k % kTcQueue;
-        if (k >= kTcQueue &&
-            !wait_or_abort(smem_u32(qempty + qs), (uint32_t)(((k / kTcQueue) - 1) & 1), abort_flag, p.status))
-          break;
+      TcRing r, rq;
+      uint32_t issued = 0, lastph = 0;  // per stage: issued at least once, parity of the last issue
+      for (;; rq.next(kTcQueue)) {
+        const int qs = rq.i;
+        if (rq.wrapped && !wait_or_abort(smem_u32(qempty + qs), rq.ph ^ 1u, abort_flag, p.status)) break;
         int item = atomicAdd(p.counter, 1);
         if (item >= n_items || *abort_flag) item = -1;
         qitem[qs] = item;
@@ -323,13 +338,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         const int ntl = min(2, p.ntiles - 2 * u);
         const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
         bool ok = true;
-        for (int b = b0; b < b1; ++b, ++it) {
-          const int s = (int)(it % S);
-          const int64_t use = it / S;
-          if (use > 0 && !wait_or_abort(smem_u32(empty + s), (uint32_t)((use - 1) & 1), abort_flag, p.status)) {
+        for (int b = b0; b < b1; ++b, r.next(S)) {
+          const int s = r.i;
+          if (r.wrapped && !wait_or_abort(smem_u32(empty + s), r.ph ^ 1u, abort_flag, p.status)) {
             ok = false;
             break;
           }
+          issued |= 1u << s;
+          lastph = (lastph & ~(1u << s)) | (r.ph << s);
           uint8_t* dst = ring + (int64_t)s * stage_bytes;
           const uint32_t bar = smem_u32(full + s);
           mbar_expect_tx(bar, (uint32_t)(ntl * p.tile_bytes + nnt * KB * 16));
@@ -347,17 +363,18 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
       }
       if (*abort_flag) {
         // let the copies already issued land before the CTA's shared memory goes away
-        for (int64_t m = it - S > 0 ? it - S : 0; m < it; ++m) wait_drain(smem_u32(full + m % S), (uint32_t)((m / S) & 1));
+        for (int st = 0; st < S; ++st)
+          if ((issued >> st) & 1u) wait_drain(smem_u32(full + st), (lastph >> st) & 1u);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA --
     if (lane == 0) {
-      int64_t it = 0, ia = 0, id = 0;
-      for (int k = 0;; ++k) {
-        const int qs = k % kTcQueue;
-        if (!wait_or_abort(smem_u32(qfull + qs), (uint32_t)((k / kTcQueue) & 1), abort_flag, p.status)) break;
+      TcRing r, ra, rd, rq;
+      for (;; rq.next(kTcQueue)) {
+        const int qs = rq.i;
+        if (!wait_or_abort(smem_u32(qfull + qs), rq.ph, abort_flag, p.status)) break;
         const int item = qitem[qs];
         mbar_arrive(smem_u32(qempty + qs));
         if (item < 0) break;
@@ -366,16 +383,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
         const int ntl = min(2, p.ntiles - 2 * u);
         const uint32_t idesc = tc_idesc(Dec::kBF16, nnt <= 2 ? 16 : 32);
-        const int db = (int)(id % kDBufs);
-        if (id >= kDBufs &&
-            !wait_or_abort(smem_u32(dempty + db), (uint32_t)(((id / kDBufs) - 1) & 1), abort_flag, p.status))
-          break;
+        const int db = rd.i;
+        if (rd.wrapped && !wait_or_abort(smem_u32(dempty + db), rd.ph ^ 1u, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t dcol = tmem + db * kTcDCols;
         bool ok = true;
-        for (int b = b0; b < b1 && ok; ++b, ++it) {
-          const int s = (int)(it % S);
-          if (!wait_or_abort(smem_u32(full + s), (uint32_t)((it / S) & 1), abort_flag, p.status)) {
+        for (int b = b0; b < b1 && ok; ++b, r.next(S)) {
+          const int s = r.i;
+          if (!wait_or_abort(smem_u32(full + s), r.ph, abort_flag, p.status)) {
             ok = false;
             break;
           }
@@ -392,9 +407,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
             }
           } else {
 #pragma unroll
-            for (int h = 0; h < Dec::kHalves; ++h, ++ia) {
-              const int j = (int)(ia % kTcASlots);
-              if (!wait_or_abort(smem_u32(afull + j), (uint32_t)((ia / kTcASlots) & 1), abort_flag, p.status)) {
+            for (int h = 0; h < Dec::kHalves; ++h, ra.next(kTcASlots)) {
+              const int j = ra.i;
+              if (!wait_or_abort(smem_u32(afull + j), ra.ph, abort_flag, p.status)) {
                 ok = false;
                 break;
               }
@@ -413,7 +428,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         }
         if (!ok) break;
         tc_commit(smem_u32(dfull + db));
-        ++id;
+        rd.next(kDBufs);
       }
       // all MMAs this thread issued are complete before the memory goes away
       tc_commit(smem_u32(fin));
@@ -427,10 +442,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
     const int q = warp & 3;            // tensor-memory lane quarter this warp may access
     const int row = 32 * q + lane;     // row inside the 128-row tile
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-    int64_t it = 0, ia = 0, id = 0;
-    for (int k = 0;; ++k) {
-      const int qs = k % kTcQueue;
-      bool ok = wait_or_abort(smem_u32(qfull + qs), (uint32_t)((k / kTcQueue) & 1), abort_flag, p.status);
+    TcRing r, ra, rd, rq;
+    for (;; rq.next(kTcQueue)) {
+      const int qs = rq.i;
+      bool ok = wait_or_abort(smem_u32(qfull + qs), rq.ph, abort_flag, p.status);
       if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
       const int item = qitem[qs];
       __syncwarp();
@@ -442,19 +457,18 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
       const int ntl = min(2, p.ntiles - 2 * u);
       if constexpr (!kDense) {
         const bool active = t < ntl;
-        for (int b = b0; b < b1; ++b, ++it) {
-          const int s = (int)(it % S);
-          ok = wait_or_abort(smem_u32(full + s), (uint32_t)((it / S) & 1), abort_flag, p.status);
+        for (int b = b0; b < b1; ++b, r.next(S)) {
+          const int s = r.i;
+          ok = wait_or_abort(smem_u32(full + s), r.ph, abort_flag, p.status);
           if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
           const uint8_t* st = ring + (int64_t)s * stage_bytes;
           const uint8_t* cp = st + t * p.piece[0];
           const uint8_t* tp = st + qoff1 + t * p.piece[1];
 #pragma unroll
-          for (int h = 0; h < Dec::kHalves; ++h, ++ia) {
-            const int j = (int)(ia % kTcASlots);
-            if (ia >= kTcASlots) {
-              ok = wait_or_abort(smem_u32(aempty + j), (uint32_t)(((ia / kTcASlots) - 1) & 1), abort_flag,
-                                 p.status);
+          for (int h = 0; h < Dec::kHalves; ++h, ra.next(kTcASlots)) {
+            const int j = ra.i;
+            if (ra.wrapped) {
+              ok = wait_or_abort(smem_u32(aempty + j), ra.ph ^ 1u, abort_flag, p.status);
               if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
             }
             tc_fence_after();
@@ -475,8 +489,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         if (*abort_flag) break;
       }
       // epilogue
-      const int db = (int)(id % kDBufs);
-      ok = wait_or_abort(smem_u32(dfull + db), (uint32_t)((id / kDBufs) & 1), abort_flag, p.status);
+      const int db = rd.i;
+      ok = wait_or_abort(smem_u32(dfull + db), rd.ph, abort_flag, p.status);
       if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
       tc_fence_after();
       const uint32_t dcol = tmem + lane_base + db * kTcDCols;
@@ -509,21 +523,34 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
           int last = 0;
           if (lane == 0) last = atomicAdd(p.part_cnt + ku * kTcDecodeWarps + dw, 1) == p.ks - 1;
           if (__shfl_sync(0xffffffffu, last, 0) == 0) {
-            ++id;
+            rd.next(kDBufs);
             continue;
           }
           __threadfence();
           float gs[16], us[16];
 #pragma unroll
           for (int n = 0; n < 16; ++n) gs[n] = us[n] = 0.f;
-          for (int sl = 0; sl < p.ks; ++sl) {
-            const float* src = p.part + ((int64_t)ku * p.ks + sl) * (2 * kTcRows * 32) + row * 32 + 16 * t;
+          // two slices' loads in flight per step, summed in slice order
+          const float* base = p.part + (int64_t)ku * p.ks * (2 * kTcRows * 32) + row * 32 + 16 * t;
+          for (int sl = 0; sl < p.ks; sl += 2) {
+            float4 a[2][4], c[2][4];
 #pragma unroll
-            for (int n = 0; n < 16; n += 4) {
-              const float4 a = __ldcg(reinterpret_cast<const float4*>(src + n));
-              const float4 c = __ldcg(reinterpret_cast<const float4*>(src + kTcRows * 32 + n));
-              gs[n] += a.x; gs[n + 1] += a.y; gs[n + 2] += a.z; gs[n + 3] += a.w;
-              us[n] += c.x; us[n + 1] += c.y; us[n + 2] += c.z; us[n + 3] += c.w;
+            for (int j = 0; j < 2; ++j) {
+              const float* src = base + (int64_t)(sl + j < p.ks ? sl + j : sl) * (2 * kTcRows * 32);
+#pragma unroll
+              for (int n = 0; n < 4; ++n) {
+                a[j][n] = __ldcg(reinterpret_cast<const float4*>(src + 4 * n));
+                c[j][n] = __ldcg(reinterpret_cast<const float4*>(src + kTcRows * 32 + 4 * n));
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              if (sl + j >= p.ks) break;
+#pragma unroll
+              for (int n = 0; n < 4; ++n) {
+                gs[4 * n] += a[j][n].x; gs[4 * n + 1] += a[j][n].y; gs[4 * n + 2] += a[j][n].z; gs[4 * n + 3] += a[j][n].w;
+                us[4 * n] += c[j][n].x; us[4 * n + 1] += c[j][n].y; us[4 * n + 2] += c[j][n].z; us[4 * n + 3] += c[j][n].w;
+              }
             }
           }
 #pragma unroll
@@ -567,7 +594,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
             if (16 + n < ntok) y[(int64_t)(16 + n) * p.y_ld] = __uint_as_float(v1[n]);
         }
       }
-      ++id;
+      rd.next(kDBufs);
     }
   }
   tc_fence_before();
