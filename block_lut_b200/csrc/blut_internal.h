@@ -24,8 +24,6 @@ struct PlanPtrs {
   int* tk_slot;   // [T*k] slot of (token, j), -1 if the id was invalid
   int* slot_tok;  // [T*k] token of each slot
   int* counters;  // [kNumCounters] work-item counters of the tcgen05 launches
-  int* zero;      // [nzero] split-K arrival counters, zeroed by the plan kernel
-  int nzero;
 };
 
 // K slices of the four matmul passes: 0 routed gate/up, 1 routed down,
@@ -48,7 +46,6 @@ struct MoEWs {
   float *y, *ys;               // expert outputs, ks[1] / ks[3] slices
   int64_t y_sstride, ys_sstride;
   float *part_r, *part_s;      // gate/up partial sums of split K
-  int *cnt_r, *cnt_s;          // their arrival counters
   int64_t ntmax, sntmax;
   MoESplit split;
 };

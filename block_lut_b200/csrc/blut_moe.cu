@@ -151,7 +151,6 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) *pp.status = 0;
   if (threadIdx.x < kNumCounters) pp.counters[threadIdx.x] = 0;
-  for (int i = threadIdx.x; i < pp.nzero; i += blockDim.x) pp.zero[i] = 0;
   if (logits) {  // row t: topk_e expert logits, then the gate logit when has_gate
     for (int t = warp; t < num_tokens; t += 32) {
       warp_topk(logits + (int64_t)t * R, topk_e, ids_in ? 0 : top_k, renorm, ids_out + (int64_t)t * top_k,
@@ -317,6 +316,32 @@ __global__ void __launch_bounds__(32) gather_bfrag_kernel(const uint16_t* __rest
   for (int i = 0; i < 4; ++i) d4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
 }
 
+// ------------------------------------------------------ split-K epilogue ---
+// Gate/up passes computed in K slices: for unit ku = group * units + u and
+// each of its (row, token), sum the slices' fp32 partials in slice order and
+// write SiLU(gate) * up into the down projection's activations.  Block
+// (ku, j): 256 threads = 8 rows x 32 tokens, rows 8j .. 8j + 7 of the unit.
+template <bool BF16>
+__global__ void __launch_bounds__(256) splitk_silu_kernel(const float* __restrict__ part, int ks, int units,
+                                                          GroupTab gt, uint8_t* __restrict__ act, int out_nch) {
+  const int ku = blockIdx.x;
+  const int gi = ku / units, u = ku % units;
+  if (gi >= *gt.n_groups) return;
+  const int ntok = gt.ntok[gi], nt0 = gt.nt0[gi];
+  const int idx = blockIdx.y * 256 + threadIdx.x;  // row * 32 + token
+  const int row = idx >> 5, n = idx & 31;
+  if (row >= kTcRows || n >= ntok) return;
+  const float* src = part + (int64_t)ku * ks * (2 * kTcRows * 32) + idx;
+  float g = 0.f, v = 0.f;
+  for (int s = 0; s < ks; ++s) {
+    g += src[(int64_t)s * (2 * kTcRows * 32)];
+    v += src[(int64_t)s * (2 * kTcRows * 32) + kTcRows * 32];
+  }
+  const int col = u * kTcRows + row;
+  uint8_t* dst = act + ((int64_t)(nt0 + (n >> 3)) * out_nch + (col >> 7)) * 2048 + tc_bact_byte(n & 7, col & 127);
+  *reinterpret_cast<uint16_t*>(dst) = f32_to_act<BF16>(silu_f(g) * v);
+}
+
 // -------------------------------------------------------------- combine ---
 // out[t] = sum_j w[t,j] * y[slot(t,j)] (+ g_t * y_shared[t]), fp32, one rounding.
 // Expert outputs computed in K slices are summed slice by slice first (in
@@ -452,17 +477,13 @@ size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
   const int64_t ku_s = sp.ks[2] > 1 ? sp.groups[2] * sp.units[2] : 0;
   size_t o_part_r = take(ku_r * sp.ks[0] * 2 * kTcRows * 32 * 4);
   size_t o_part_s = take(ku_s * sp.ks[2] * 2 * kTcRows * 32 * 4);
-  size_t o_cnt = take((ku_r + ku_s) * kTcDecodeWarps * 4);
   if (base && ws) {
     w.split = sp;
     w.y_sstride = S * H;
     w.ys_sstride = T * H;
     w.part_r = reinterpret_cast<float*>(base + o_part_r);
     w.part_s = reinterpret_cast<float*>(base + o_part_s);
-    w.cnt_r = reinterpret_cast<int*>(base + o_cnt);
-    w.cnt_s = w.cnt_r + ku_r * kTcDecodeWarps;
-    w.pp.zero = w.cnt_r;
-    w.pp.nzero = (int)((ku_r + ku_s) * kTcDecodeWarps);
+
     w.status = reinterpret_cast<int*>(base + o_status);
     w.ids = reinterpret_cast<int32_t*>(base + o_ids);
     w.tw = reinterpret_cast<float*>(base + o_tw);
@@ -656,7 +677,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   const GroupTab routed{ws.pp.meta + 0, ws.pp.g_expert, ws.pp.g_slot0, ws.pp.g_ntok, ws.pp.g_nt0};
   const GroupTab shared{ws.pp.meta + 2, ws.pp.sg_expert, ws.pp.sg_slot0, ws.pp.sg_ntok, ws.pp.sg_nt0};
   auto pass = [&](const blut_mat_desc& d, const void* w, int64_t stride, const GroupTab& gt, double est,
-                  const uint8_t* bin, uint8_t* act, int out_k, float* y, int counter, float* part, int* cnt,
+                  const uint8_t* bin, uint8_t* act, int out_k, float* y, int counter, float* part,
                   int64_t y_sstride) -> int {
     const bool pair = act != nullptr;
     const int K = (int)d.cols;
@@ -677,9 +698,17 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.ks = ws.split.ks[counter];
       t.bps = ws.split.bps[counter];
       t.part = part;
-      t.part_cnt = cnt;
       t.y_sstride = y_sstride;
-      return launch_tc_mm(d, t, sms, stream) == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
+      if (launch_tc_mm(d, t, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+      if (pair && t.ks > 1) {
+        // sum the gate/up slices in order, SiLU(gate) * up into the down projection's activations
+        const dim3 grid((unsigned)(ws.split.groups[counter] * t.units), (unsigned)(kTcRows * 32 / 256));
+        if (a.dtype == BLUT_BF16)
+          splitk_silu_kernel<true><<<grid, 256, 0, stream>>>(part, t.ks, t.units, gt, act, t.out_nch);
+        else
+          splitk_silu_kernel<false><<<grid, 256, 0, stream>>>(part, t.ks, t.units, gt, act, t.out_nch);
+      }
+      return cudaGetLastError() == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
     }
     MMParams m{};
     if (!mm_planes(d, pair, m)) return BLUT_ERR_UNSUPPORTED;
@@ -702,14 +731,14 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   // 4. gate/up + SiLU*up (routed, then shared)
   if (ev && cudaEventRecord(ev[0], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if ((rc = pass(a.w13, a.w13_tiled, a.w13_stride, routed, est_groups, ws.xf, ws.af, a.inter, nullptr, 0,
-                 ws.part_r, ws.cnt_r, 0)) !=
+                 ws.part_r, 0)) !=
       BLUT_OK)
     return rc;
   if ((rc = stage_done("routed gate/up", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[1], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if (sh) {
     if ((rc = pass(a.s13, a.s13_tiled, 0, shared, est_sgroups, ws.xfs, ws.afs, a.shared_inter, nullptr, 2,
-                   ws.part_s, ws.cnt_s, 0)) !=
+                   ws.part_s, 0)) !=
         BLUT_OK)
       return rc;
     if ((rc = stage_done("shared gate/up", stream)) != BLUT_OK) return rc;
@@ -717,12 +746,12 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   // 5. down (routed, then shared)
   if (ev && cudaEventRecord(ev[2], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if ((rc = pass(a.w2, a.w2_tiled, a.w2_stride, routed, est_groups, ws.af, nullptr, 0, ws.y, 1, nullptr,
-                 nullptr, ws.y_sstride)) != BLUT_OK)
+                 ws.y_sstride)) != BLUT_OK)
     return rc;
   if ((rc = stage_done("routed down", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[3], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if (sh) {
-    if ((rc = pass(a.s2, a.s2_tiled, 0, shared, est_sgroups, ws.afs, nullptr, 0, ws.ys, 3, nullptr, nullptr,
+    if ((rc = pass(a.s2, a.s2_tiled, 0, shared, est_sgroups, ws.afs, nullptr, 0, ws.ys, 3, nullptr,
                    ws.ys_sstride)) != BLUT_OK) return rc;
     if ((rc = stage_done("shared down", stream)) != BLUT_OK) return rc;
   }
@@ -749,6 +778,9 @@ int moe_launch_count(const blut_moe_args& a) {
   n += 2;                                                  // routed gate/up, down
   if (sh) n += 2;                                          // shared gate/up, down
   n += 1;                                                  // combine
+  MoESplit sp;
+  moe_split(a, sp);
+  n += (sp.ks[0] > 1) + (sh && sp.ks[2] > 1);              // split-K gate/up sums
   return n;
 }
 

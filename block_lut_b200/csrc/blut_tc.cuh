@@ -66,14 +66,11 @@ struct TcParams {
   int y_ld;
   int64_t y_sstride;
   // Split K: each (group, unit) is cut into ks slices of bps blocks.  Gate/up
-  // slices write fp32 partials (part, [item][gate|up][128 rows][32 tokens]);
-  // per epilogue warp, the slice that arrives last at
-  // part_cnt[(group * units + unit) * 8 + warp] sums them in slice order and
-  // runs the epilogue of that warp's rows and tokens.  Down slices write
-  // separate output rows that the combine sums in slice order.
+  // slices write fp32 partials (part, [item][gate|up][128 rows][32 tokens])
+  // that splitk_silu_kernel sums in slice order; down slices write separate
+  // output rows that the combine sums in slice order.
   int ks, bps;
   float* part;
-  int* part_cnt;
   int* counter;            // item counter (zeroed by the plan kernel)
   int* status;
   int stages;
@@ -505,59 +502,20 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(dempty + db));
         if (p.ks > 1) {
-          // partial sums of this slice; the last slice to arrive finishes the unit
+          // partial sums of this slice; splitk_silu_kernel adds the slices up
+          // after this launch (a kernel boundary orders them without fences)
           float* mine = p.part + (int64_t)item * (2 * kTcRows * 32) + row * 32 + 16 * t;
 #pragma unroll
           for (int n = 0; n < 16; n += 4) {
-            __stcg(reinterpret_cast<float4*>(mine + n),
-                   make_float4(__uint_as_float(g[n]), __uint_as_float(g[n + 1]), __uint_as_float(g[n + 2]),
-                               __uint_as_float(g[n + 3])));
-            __stcg(reinterpret_cast<float4*>(mine + kTcRows * 32 + n),
-                   make_float4(__uint_as_float(v[n]), __uint_as_float(v[n + 1]), __uint_as_float(v[n + 2]),
-                               __uint_as_float(v[n + 3])));
+            *reinterpret_cast<float4*>(mine + n) =
+                make_float4(__uint_as_float(g[n]), __uint_as_float(g[n + 1]), __uint_as_float(g[n + 2]),
+                            __uint_as_float(g[n + 3]));
+            *reinterpret_cast<float4*>(mine + kTcRows * 32 + n) =
+                make_float4(__uint_as_float(v[n]), __uint_as_float(v[n + 1]), __uint_as_float(v[n + 2]),
+                            __uint_as_float(v[n + 3]));
           }
-          // Each warp owns its 32 rows x 16 tokens, so it counts its own slices:
-          // no barrier across warps (which an aborting warp could leave waiting).
-          __threadfence();
-          __syncwarp();
-          int last = 0;
-          if (lane == 0) last = atomicAdd(p.part_cnt + ku * kTcDecodeWarps + dw, 1) == p.ks - 1;
-          if (__shfl_sync(0xffffffffu, last, 0) == 0) {
-            rd.next(kDBufs);
-            continue;
-          }
-          __threadfence();
-          float gs[16], us[16];
-#pragma unroll
-          for (int n = 0; n < 16; ++n) gs[n] = us[n] = 0.f;
-          // two slices' loads in flight per step, summed in slice order
-          const float* base = p.part + (int64_t)ku * p.ks * (2 * kTcRows * 32) + row * 32 + 16 * t;
-          for (int sl = 0; sl < p.ks; sl += 2) {
-            float4 a[2][4], c[2][4];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const float* src = base + (int64_t)(sl + j < p.ks ? sl + j : sl) * (2 * kTcRows * 32);
-#pragma unroll
-              for (int n = 0; n < 4; ++n) {
-                a[j][n] = __ldcg(reinterpret_cast<const float4*>(src + 4 * n));
-                c[j][n] = __ldcg(reinterpret_cast<const float4*>(src + kTcRows * 32 + 4 * n));
-              }
-            }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              if (sl + j >= p.ks) break;
-#pragma unroll
-              for (int n = 0; n < 4; ++n) {
-                gs[4 * n] += a[j][n].x; gs[4 * n + 1] += a[j][n].y; gs[4 * n + 2] += a[j][n].z; gs[4 * n + 3] += a[j][n].w;
-                us[4 * n] += c[j][n].x; us[4 * n + 1] += c[j][n].y; us[4 * n + 2] += c[j][n].z; us[4 * n + 3] += c[j][n].w;
-              }
-            }
-          }
-#pragma unroll
-          for (int n = 0; n < 16; ++n) {
-            g[n] = __float_as_uint(gs[n]);
-            v[n] = __float_as_uint(us[n]);
-          }
+          rd.next(kDBufs);
+          continue;
         }
         const int col = u * kTcRows + row;  // K index of the down projection
         const int nt0 = p.gt.nt0[gi];

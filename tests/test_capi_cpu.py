@@ -134,7 +134,14 @@ def test_moe_forward_rejects_small_workspace():
 
 def test_launch_count():
     lib = _lib.lib()
-    assert lib.blut_moe_launch_count(C.byref(_args())) == 5  # plan, gather, gate/up, down, combine
+    # plan, gather, gate/up, down, combine; the tcgen05 layout at T = 8 also
+    # splits the gate/up pass over K, which adds its slice-sum kernel
+    assert lib.blut_moe_launch_count(C.byref(_args())) == 5
+    fmt = LUTFormat("b", 4, 64)
+    tc = _args(w13=fmt.desc(2816, 2048, paired=True, tc=True), w2=fmt.desc(2048, 1408, tc=True))
+    assert lib.blut_moe_launch_count(C.byref(tc)) == 6
+    tc.num_tokens = 256  # enough items without a split
+    assert lib.blut_moe_launch_count(C.byref(tc)) == 5
 
 
 LAYOUT_PROBE = r"""
