@@ -46,6 +46,11 @@ constexpr int kTcDCols = 64;         // tensor-memory columns of one accumulator
 constexpr int kTcASlots = 3;
 constexpr int kTcACol0 = kTcDCols;
 
+// Multipliers {1 << 31, 1 << 16} handed to the decode (see tc_lut16x8).
+struct TcMul {
+  uint32_t k31, k16;
+};
+
 struct TcParams {
   const uint8_t* w;        // tiled (BLUT_LAYOUT_TC) matrices of all experts
   int64_t wstride;         // bytes between experts
@@ -72,8 +77,10 @@ struct TcParams {
   int ks, bps;
   float* part;
   int* counter;            // item counter (zeroed by the plan kernel)
+  TcMul mul;               // {1 << 31, 1 << 16}, see tc_lut16x8
   int* status;
-  int stages;
+  int stages;              // weight stages (LUT formats) or weight + activation stages (dense)
+  int xstages;             // activation stages (LUT formats)
 };
 
 // Byte offset of activation (token n in [0, 8), column k in [0, 128)) inside
@@ -133,6 +140,25 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&v)[32])
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 16 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+// Waits for this thread's tcgen05.st; `v` (the registers of the store in
+// flight) is tied to the wait so the compiler keeps them unchanged until then.
+__device__ __forceinline__ void tc_wait_st_keep(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::st.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
+}
+
 // 16 consecutive 32-bit columns, then the wait; the registers are tied to the
 // wait so that no use is scheduled before it.
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
@@ -160,13 +186,26 @@ __device__ __forceinline__ uint4 tc_lds128(const uint8_t* p) { return *reinterpr
 // third permute picks between them with bit 3, and two more interleave the
 // low and high bytes into fp16 pairs.  `w` holds 8 codes (k = 0..7, code j
 // in bits 4j..4j+3); out[0..3] receive the fp16 pairs (k, k+1).
-__device__ __forceinline__ void tc_lut16x8(uint32_t w, const uint4& th, const uint4& tl, uint32_t* out) {
+//
+// The lookups are byte permutes on the integer ALU, the kernel's limiting
+// pipe.  The three right shifts per 8 codes therefore run as high-half
+// multiplies (mul.hi by 2^31 or 2^16) on the otherwise idle FMA pipe; the
+// multipliers come from the kernel parameters (TcMul) so that the compiler
+// cannot fold them back into shifts.
+__device__ __forceinline__ uint32_t tc_mulhi(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ void tc_lut16x8(uint32_t w, const uint4& th, const uint4& tl, uint32_t* out,
+                                           const TcMul& m) {
   const uint32_t s1 = w & 0x77777777u;
-  const uint32_t s2 = ((w >> 1) & 0x44444444u) | 0x32103210u;
+  const uint32_t s2 = (tc_mulhi(w, m.k31) & 0x44444444u) | 0x32103210u;  // bit 3 of each code to bit 2
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const uint32_t a = h ? s1 >> 16 : s1;
-    const uint32_t b = h ? s2 >> 16 : s2;
+    const uint32_t a = h ? tc_mulhi(s1, m.k16) : s1;
+    const uint32_t b = h ? tc_mulhi(s2, m.k16) : s2;
     const uint32_t hi = prmt(prmt(th.x, th.y, a), prmt(th.z, th.w, a), b);
     const uint32_t lo = prmt(prmt(tl.x, tl.y, a), prmt(tl.z, tl.w, a), b);
     out[2 * h] = prmt(lo, hi, 0x5140u);
@@ -182,10 +221,22 @@ struct TcDecB4 {
   static constexpr int KB = G > 64 ? G : 64;  // columns per block
   static constexpr int kHalves = KB / 64;     // 64-column halves per block
   static constexpr int kNumPlanes = 2;
-  // Decodes half h (64 columns) of row `row` of one tile: cp / tp are the
-  // tile's code and table pieces inside the stage.
+  // Decodes quarter qq (32 columns) of half h of row `row` of one tile: cp /
+  // tp are the tile's code and table pieces inside the stage.
+  __device__ __forceinline__ static void decode_q(const uint8_t* cp, const uint8_t* tp, int row, int h, int qq,
+                                                  uint32_t (&out)[16], const TcMul& m) {
+    const uint4 c = tc_lds128(cp + ((2 * h + qq) * kTcRows + row) * 16);
+    const int tb = G == 32 ? 2 * h + qq : (G == 64 ? h : 0);  // table of these columns
+    const uint4 th = tc_lds128(tp + ((2 * tb) * kTcRows + row) * 16);
+    const uint4 tl = tc_lds128(tp + ((2 * tb + 1) * kTcRows + row) * 16);
+    tc_lut16x8(c.x, th, tl, out + 0, m);
+    tc_lut16x8(c.y, th, tl, out + 4, m);
+    tc_lut16x8(c.z, th, tl, out + 8, m);
+    tc_lut16x8(c.w, th, tl, out + 12, m);
+  }
+  // Decodes half h (64 columns) of row `row` of one tile.
   __device__ __forceinline__ static void decode(const uint8_t* cp, const uint8_t* tp, int row, int h,
-                                                uint32_t (&out)[32]) {
+                                                uint32_t (&out)[32], const TcMul& m) {
     const uint4 c0 = tc_lds128(cp + ((2 * h) * kTcRows + row) * 16);
     const uint4 c1 = tc_lds128(cp + ((2 * h + 1) * kTcRows + row) * 16);
     if constexpr (G == 32) {
@@ -193,26 +244,26 @@ struct TcDecB4 {
       const uint4 tl0 = tc_lds128(tp + ((4 * h + 1) * kTcRows + row) * 16);
       const uint4 th1 = tc_lds128(tp + ((4 * h + 2) * kTcRows + row) * 16);
       const uint4 tl1 = tc_lds128(tp + ((4 * h + 3) * kTcRows + row) * 16);
-      tc_lut16x8(c0.x, th0, tl0, out + 0);
-      tc_lut16x8(c0.y, th0, tl0, out + 4);
-      tc_lut16x8(c0.z, th0, tl0, out + 8);
-      tc_lut16x8(c0.w, th0, tl0, out + 12);
-      tc_lut16x8(c1.x, th1, tl1, out + 16);
-      tc_lut16x8(c1.y, th1, tl1, out + 20);
-      tc_lut16x8(c1.z, th1, tl1, out + 24);
-      tc_lut16x8(c1.w, th1, tl1, out + 28);
+      tc_lut16x8(c0.x, th0, tl0, out + 0, m);
+      tc_lut16x8(c0.y, th0, tl0, out + 4, m);
+      tc_lut16x8(c0.z, th0, tl0, out + 8, m);
+      tc_lut16x8(c0.w, th0, tl0, out + 12, m);
+      tc_lut16x8(c1.x, th1, tl1, out + 16, m);
+      tc_lut16x8(c1.y, th1, tl1, out + 20, m);
+      tc_lut16x8(c1.z, th1, tl1, out + 24, m);
+      tc_lut16x8(c1.w, th1, tl1, out + 28, m);
     } else {
-      const int m = G == 64 ? h : 0;
-      const uint4 th = tc_lds128(tp + ((2 * m) * kTcRows + row) * 16);
-      const uint4 tl = tc_lds128(tp + ((2 * m + 1) * kTcRows + row) * 16);
-      tc_lut16x8(c0.x, th, tl, out + 0);
-      tc_lut16x8(c0.y, th, tl, out + 4);
-      tc_lut16x8(c0.z, th, tl, out + 8);
-      tc_lut16x8(c0.w, th, tl, out + 12);
-      tc_lut16x8(c1.x, th, tl, out + 16);
-      tc_lut16x8(c1.y, th, tl, out + 20);
-      tc_lut16x8(c1.z, th, tl, out + 24);
-      tc_lut16x8(c1.w, th, tl, out + 28);
+      const int tb = G == 64 ? h : 0;  // table of this half
+      const uint4 th = tc_lds128(tp + ((2 * tb) * kTcRows + row) * 16);
+      const uint4 tl = tc_lds128(tp + ((2 * tb + 1) * kTcRows + row) * 16);
+      tc_lut16x8(c0.x, th, tl, out + 0, m);
+      tc_lut16x8(c0.y, th, tl, out + 4, m);
+      tc_lut16x8(c0.z, th, tl, out + 8, m);
+      tc_lut16x8(c0.w, th, tl, out + 12, m);
+      tc_lut16x8(c1.x, th, tl, out + 16, m);
+      tc_lut16x8(c1.y, th, tl, out + 20, m);
+      tc_lut16x8(c1.z, th, tl, out + 24, m);
+      tc_lut16x8(c1.w, th, tl, out + 28, m);
     }
   }
 };
@@ -225,7 +276,10 @@ struct TcDecDense {
   static constexpr int KB = 32;
   static constexpr int kHalves = 0;
   static constexpr int kNumPlanes = 1;
-  __device__ __forceinline__ static void decode(const uint8_t*, const uint8_t*, int, int, uint32_t (&)[32]) {}
+  __device__ __forceinline__ static void decode(const uint8_t*, const uint8_t*, int, int, uint32_t (&)[32],
+                                                const TcMul&) {}
+  __device__ __forceinline__ static void decode_q(const uint8_t*, const uint8_t*, int, int, int, uint32_t (&)[16],
+                                                  const TcMul&) {}
 };
 
 // Position in a ring of n barrier-guarded slots: slot index, the parity of
@@ -245,15 +299,25 @@ struct TcRing {
 };
 
 // ------------------------------------------------------------------ kernel --
+// Shared-memory rings.  Dense weights and their activations are both read by
+// the MMA, so one stage holds both and the MMA's commit frees it.  For LUT
+// formats the weight stage is read only by the decode warps, which free it
+// as soon as their loads are done; the activations, read by the MMA, sit in
+// a separate small ring freed by the MMA's commit.  Weight stages therefore
+// recycle without waiting for the tensor core.
 template <class Dec>
 __host__ __device__ inline int tc_stage_bytes(const TcParams& p) {
-  return (2 * p.tile_bytes + kMaxNT * Dec::KB * 16 + 127) & ~127;
+  return (2 * p.tile_bytes + (Dec::kDense ? kMaxNT * Dec::KB * 16 : 0) + 127) & ~127;
+}
+template <class Dec>
+__host__ __device__ constexpr int tc_xstage_bytes() {
+  return Dec::kDense ? 0 : kMaxNT * Dec::KB * 16;
 }
 
-// Barriers, queue and flags take the first 512 bytes, the ring follows.
+// Barriers, queue and flags take the first 512 bytes, the rings follow.
 template <class Dec>
 __host__ inline int tc_smem_bytes(const TcParams& p) {
-  return 512 + p.stages * tc_stage_bytes<Dec>(p);
+  return 512 + p.stages * tc_stage_bytes<Dec>(p) + p.xstages * tc_xstage_bytes<Dec>();
 }
 
 template <class Dec>
@@ -275,10 +339,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 37);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 38);
   volatile int* qitem = reinterpret_cast<volatile int*>(full + 39);  // [kTcQueue]
+  uint64_t* xfull = full + 41;                         // [4] activation stage loaded (LUT formats)
+  uint64_t* xempty = full + 45;                        // [4] activation stage read (MMA commit)
   uint8_t* ring = smem + 512;
-  const int S = p.stages;
+  const int S = p.stages, SX = p.xstages;
   const int stage_bytes = tc_stage_bytes<Dec>(p);
-  const int boff = 2 * p.tile_bytes;  // activations inside a stage
+  constexpr int xstage_bytes = tc_xstage_bytes<Dec>();
+  uint8_t* xring = ring + (int64_t)S * stage_bytes;
+  const int boff = 2 * p.tile_bytes;  // activations inside a dense stage
   const int qoff1 = 2 * p.piece[0];   // second plane inside a stage
 
   const int warp = threadIdx.x >> 5;
@@ -286,7 +354,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(full + s), 1);
-      mbar_init(smem_u32(empty + s), kDense ? 1 : 1 + kTcDecodeWarps);
+      mbar_init(smem_u32(empty + s), kDense ? 1 : kTcDecodeWarps);
+    }
+    for (int s = 0; s < SX; ++s) {
+      mbar_init(smem_u32(xfull + s), 1);
+      mbar_init(smem_u32(xempty + s), 1);
     }
     for (int j = 0; j < kTcASlots; ++j) {
       mbar_init(smem_u32(afull + j), kTcDecodeWarps);
@@ -318,8 +390,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
-      TcRing r, rq;
-      uint32_t issued = 0, lastph = 0;  // per stage: issued at least once, parity of the last issue
+      TcRing r, rx, rq;
+      uint32_t issued = 0, lastph = 0;    // per weight stage: issued at least once, parity of the last issue
+      uint32_t xissued = 0, xlastph = 0;  // the same per activation stage
       for (;; rq.next(kTcQueue)) {
         const int qs = rq.i;
         if (rq.wrapped && !wait_or_abort(smem_u32(qempty + qs), rq.ph ^ 1u, abort_flag, p.status)) break;
@@ -344,16 +417,30 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
           issued |= 1u << s;
           lastph = (lastph & ~(1u << s)) | (r.ph << s);
           uint8_t* dst = ring + (int64_t)s * stage_bytes;
-          const uint32_t bar = smem_u32(full + s);
-          mbar_expect_tx(bar, (uint32_t)(ntl * p.tile_bytes + nnt * KB * 16));
+          uint32_t bar = smem_u32(full + s);
+          mbar_expect_tx(bar, (uint32_t)(ntl * p.tile_bytes + (kDense ? nnt * KB * 16 : 0)));
           const int64_t pt = (int64_t)b * p.ntiles + 2 * u;
           bulk_g2s(smem_u32(dst), base + p.plane_off[0] + pt * p.piece[0], (uint32_t)(ntl * p.piece[0]), bar);
           if (Dec::kNumPlanes > 1)
             bulk_g2s(smem_u32(dst + qoff1), base + p.plane_off[1] + pt * p.piece[1], (uint32_t)(ntl * p.piece[1]),
                      bar);
+          uint8_t* xdst = dst + boff;
+          if constexpr (!kDense) {
+            const int sx = rx.i;
+            if (rx.wrapped && !wait_or_abort(smem_u32(xempty + sx), rx.ph ^ 1u, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            xissued |= 1u << sx;
+            xlastph = (xlastph & ~(1u << sx)) | (rx.ph << sx);
+            xdst = xring + sx * xstage_bytes;
+            bar = smem_u32(xfull + sx);
+            mbar_expect_tx(bar, (uint32_t)(nnt * KB * 16));
+            rx.next(SX);
+          }
           const int64_t boffg = (int64_t)((b * KB) >> 7) * 2048 + ((b * KB) & 127) * 16;
           for (int i = 0; i < nnt; ++i)
-            bulk_g2s(smem_u32(dst + boff + i * KB * 16), p.bin + (int64_t)(nt0 + i) * p.bin_nch * 2048 + boffg,
+            bulk_g2s(smem_u32(xdst + i * KB * 16), p.bin + (int64_t)(nt0 + i) * p.bin_nch * 2048 + boffg,
                      (uint32_t)(KB * 16), bar);
         }
         if (!ok) break;
@@ -362,6 +449,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         // let the copies already issued land before the CTA's shared memory goes away
         for (int st = 0; st < S; ++st)
           if ((issued >> st) & 1u) wait_drain(smem_u32(full + st), (lastph >> st) & 1u);
+        for (int st = 0; st < SX; ++st)
+          if ((xissued >> st) & 1u) wait_drain(smem_u32(xfull + st), (xlastph >> st) & 1u);
       }
     }
     __syncwarp();
@@ -385,14 +474,15 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         tc_fence_after();
         const uint32_t dcol = tmem + db * kTcDCols;
         bool ok = true;
-        for (int b = b0; b < b1 && ok; ++b, r.next(S)) {
+        // dense: r walks the combined stages; LUT formats: r walks the activation stages
+        for (int b = b0; b < b1 && ok; ++b, r.next(kDense ? S : SX)) {
           const int s = r.i;
-          if (!wait_or_abort(smem_u32(full + s), r.ph, abort_flag, p.status)) {
+          if (!wait_or_abort(smem_u32((kDense ? full : xfull) + s), r.ph, abort_flag, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t st = smem_u32(ring + (int64_t)s * stage_bytes);
+          const uint32_t st = smem_u32(kDense ? ring + (int64_t)s * stage_bytes : xring + s * xstage_bytes);
           if constexpr (kDense) {
 #pragma unroll
             for (int sl = 0; sl < KB / 16; ++sl) {
@@ -413,7 +503,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
               tc_fence_after();
 #pragma unroll
               for (int sl = 0; sl < 4; ++sl) {
-                const uint64_t bd = tc_desc(st + boff + (h * 4 + sl) * 256, 128, KB * 16);
+                const uint64_t bd = tc_desc(st + (h * 4 + sl) * 256, 128, KB * 16);
                 for (int t = 0; t < ntl; ++t)
                   tc_mma_ts(dcol + t * 32, tmem + kTcACol0 + j * 64 + t * 32 + sl * 8, bd, idesc,
                             ((b - b0) | h | sl) != 0);
@@ -421,7 +511,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
               tc_commit(smem_u32(aempty + j));
             }
           }
-          tc_commit(smem_u32(empty + s));
+          tc_commit(smem_u32((kDense ? empty : xempty) + s));
         }
         if (!ok) break;
         tc_commit(smem_u32(dfull + db));
@@ -449,15 +539,21 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
       if (lane == 0) mbar_arrive(smem_u32(qempty + qs));
       if (item < 0) break;
       const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
-        const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
+      const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
       const int ntok = p.gt.ntok[gi];
       const int ntl = min(2, p.ntiles - 2 * u);
       if constexpr (!kDense) {
         const bool active = t < ntl;
-        for (int b = b0; b < b1; ++b, r.next(S)) {
+        bool aborted = false;
+        // A half is decoded as two quarters (qa, qb): the store of the first
+        // runs while the second is decoded.
+        for (int b = b0; b < b1 && !aborted; ++b, r.next(S)) {
           const int s = r.i;
           ok = wait_or_abort(smem_u32(full + s), r.ph, abort_flag, p.status);
-          if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+          if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
+            aborted = true;
+            break;
+          }
           const uint8_t* st = ring + (int64_t)s * stage_bytes;
           const uint8_t* cp = st + t * p.piece[0];
           const uint8_t* tp = st + qoff1 + t * p.piece[1];
@@ -466,24 +562,32 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
             const int j = ra.i;
             if (ra.wrapped) {
               ok = wait_or_abort(smem_u32(aempty + j), ra.ph ^ 1u, abort_flag, p.status);
-              if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+              if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
+                aborted = true;
+                break;
+              }
             }
             tc_fence_after();
+            const uint32_t aslot = tmem + lane_base + kTcACol0 + j * 64 + t * 32;
             if (active) {
-              uint32_t a[32];
-              Dec::decode(cp, tp, row, h, a);
-              tc_st32(tmem + lane_base + kTcACol0 + j * 64 + t * 32, a);
-              tc_wait_st();
+              uint32_t qa[16], qb[16];
+              Dec::decode_q(cp, tp, row, h, 0, qa, p.mul);
+              tc_st16(aslot, qa);
+              Dec::decode_q(cp, tp, row, h, 1, qb, p.mul);
+              tc_st16(aslot + 16, qb);
+              tc_wait_st_keep(qa);
+              tc_wait_st_keep(qb);
+            }
+            if (h == Dec::kHalves - 1) {  // this stage's shared memory is no longer read
+              __syncwarp();
+              if (lane == 0) mbar_arrive(smem_u32(empty + s));
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(afull + j));
           }
-          if (*abort_flag) break;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(empty + s));
         }
-        if (*abort_flag) break;
+        if (aborted) break;
       }
       // epilogue
       const int db = rd.i;
@@ -568,7 +672,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
 template <class Dec>
 inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
   const int stage = tc_stage_bytes<Dec>(p);
-  p.stages = std::max(2, std::min(8, kTcRingBudget / stage));
+  const int xstage = tc_xstage_bytes<Dec>();
+  p.xstages = xstage ? std::max(2, std::min(4, (kTcRingBudget / 6) / xstage)) : 0;
+  p.stages = std::max(2, std::min(8, (kTcRingBudget - p.xstages * xstage) / stage));
   const int smem = tc_smem_bytes<Dec>(p);
   auto kern = tc_mm_kernel<Dec>;
   static std::mutex mu;

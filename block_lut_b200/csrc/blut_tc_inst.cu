@@ -19,6 +19,7 @@ bool tc_planes(const blut_mat_desc& d, bool pair, TcParams& p) {
   p.nblocks = (int)L.nchunks;
   p.units = (p.ntiles + 1) / 2;
   p.pair = pair ? 1 : 0;
+  p.mul = TcMul{1u << 31, 1u << 16};
   return true;
 }
 
@@ -42,7 +43,8 @@ cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int sms, cud
 template <class Dec>
 __global__ void __launch_bounds__(kTcRows) tc_dequant_kernel(const uint8_t* __restrict__ w, int64_t off0,
                                                              int64_t off1, int piece0, int piece1, int ntiles,
-                                                             int64_t cols, int paired, uint16_t* __restrict__ out) {
+                                                             int64_t cols, int paired, uint16_t* __restrict__ out,
+                                                             TcMul mul) {
   const int pt = blockIdx.x, b = blockIdx.y, row = threadIdx.x;
   const int64_t r = logical_tile(pt, ntiles, paired != 0) * kTcRows + row;
   const uint8_t* cp = w + off0 + ((int64_t)b * ntiles + pt) * piece0;
@@ -55,7 +57,7 @@ __global__ void __launch_bounds__(kTcRows) tc_dequant_kernel(const uint8_t* __re
 #pragma unroll
     for (int h = 0; h < Dec::kHalves; ++h) {
       uint32_t a[32];
-      Dec::decode(cp, tp, row, h, a);
+      Dec::decode(cp, tp, row, h, a, mul);
 #pragma unroll
       for (int i = 0; i < 8; ++i) dst[h * 8 + i] = make_uint4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]);
     }
@@ -68,7 +70,7 @@ static cudaError_t tc_dequant(const TiledLayout& L, const uint8_t* w, int64_t co
   dim3 grid((unsigned)L.ntiles, (unsigned)L.nchunks);
   tc_dequant_kernel<Dec><<<grid, kTcRows, 0, stream>>>(w, L.off[0], L.nplanes > 1 ? L.off[1] : 0, (int)L.piece[0],
                                                        L.nplanes > 1 ? (int)L.piece[1] : 0, (int)L.ntiles, cols,
-                                                       paired, out);
+                                                       paired, out, TcMul{1u << 31, 1u << 16});
   return cudaGetLastError();
 }
 
