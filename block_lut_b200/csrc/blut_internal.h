@@ -9,7 +9,9 @@
 namespace blut {
 
 constexpr int kMaxExperts = 1024;
-constexpr int kMaxSlots = 2048;   // T * top_k of the decode path
+constexpr int kMaxSlots = 1 << 22;  // T * top_k
+constexpr int kWideGroupTok = 128;  // token groups of the tcgen05 prefill regime
+constexpr int kPlanTopkTokens = 256;  // above this many tokens the top-k runs as its own launch
 constexpr int kDevBadExpert = 2;  // device status bit: an expert id was out of range
 
 struct MMParams;
@@ -31,6 +33,7 @@ struct PlanPtrs {
 struct MoESplit {
   int ks[4], bps[4], units[4];
   int64_t groups[4];  // bound on token groups of the pass
+  int gtok[2];        // tokens per group: routed, shared (32, or kWideGroupTok for prefill)
 };
 
 constexpr int kNumCounters = 4;  // routed gate/up, routed down, shared gate/up, shared down
@@ -73,7 +76,7 @@ bool mm_planes(const blut_mat_desc& d, bool pair, MMParams& p);
 // tcgen05 matmul for BLUT_LAYOUT_TC matrices (blut_tc_inst.cu).
 struct TcParams;
 bool tc_planes(const blut_mat_desc& d, bool pair, TcParams& p);
-cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int group_tokens, int sms, cudaStream_t stream);
 int dequant_tiled_tc(const blut_mat_desc& d, const void* tiled, void* out, cudaStream_t stream);
 int dequant_tiled(const blut_mat_desc& d, const void* tiled, const void* table, void* out, cudaStream_t stream);
 

@@ -138,9 +138,9 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
 __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ ids_in,
                                                     const float* __restrict__ logits, int topk_e, int R,
                                                     int num_tokens, int top_k, int num_experts, int renorm,
-                                                    int has_gate, int has_shared, PlanPtrs pp,
-                                                    int32_t* __restrict__ ids_out, float* __restrict__ tw_out,
-                                                    float* __restrict__ sg_out) {
+                                                    int has_gate, int has_shared, int gtok, int sgtok,
+                                                    PlanPtrs pp, int32_t* __restrict__ ids_out,
+                                                    float* __restrict__ tw_out, float* __restrict__ sg_out) {
   __shared__ int cnt[kMaxExperts];
   __shared__ int off[kMaxExperts];
   __shared__ int goff[kMaxExperts];
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
     for (int base = 0; base < num_experts; base += 32) {
       const int e = base + lane;
       const int c = e < num_experts ? cnt[e] : 0;
-      int vt = c, vg = (c + kGroupTok - 1) / kGroupTok, vn = (c + kNTile - 1) / kNTile;
+      int vt = c, vg = (c + gtok - 1) / gtok, vn = (c + kNTile - 1) / kNTile;
       int st = vt, sgp = vg, sn = vn;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -203,14 +203,14 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
   for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
     const int c = cnt[e];
     int gi = goff[e], nt = toff[e];
-    for (int q = 0; q * kGroupTok < c; ++q, ++gi) {
-      const int ntok = min(kGroupTok, c - q * kGroupTok);
+    for (int q = 0; q * gtok < c; ++q, ++gi) {
+      const int ntok = min(gtok, c - q * gtok);
       pp.g_expert[gi] = e;
-      pp.g_slot0[gi] = off[e] + q * kGroupTok;
+      pp.g_slot0[gi] = off[e] + q * gtok;
       pp.g_ntok[gi] = ntok;
       pp.g_nt0[gi] = nt;
       for (int i = 0; i * kNTile < ntok; ++i, ++nt) {
-        pp.nt_slot0[nt] = off[e] + q * kGroupTok + i * kNTile;
+        pp.nt_slot0[nt] = off[e] + q * gtok + i * kNTile;
         pp.nt_cnt[nt] = min(kNTile, ntok - i * kNTile);
       }
     }
@@ -220,10 +220,10 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
     pp.meta[1] = tot[2];
     int sng = 0, snt = 0;
     if (has_shared) {
-      for (int q = 0; q * kGroupTok < num_tokens; ++q) {
-        const int ntok = min(kGroupTok, num_tokens - q * kGroupTok);
+      for (int q = 0; q * sgtok < num_tokens; ++q) {
+        const int ntok = min(sgtok, num_tokens - q * sgtok);
         pp.sg_expert[sng] = 0;
-        pp.sg_slot0[sng] = q * kGroupTok;
+        pp.sg_slot0[sng] = q * sgtok;
         pp.sg_ntok[sng] = ntok;
         pp.sg_nt0[sng] = snt;
         snt += (ntok + kNTile - 1) / kNTile;
@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(32) gather_bfrag_kernel(const uint16_t* __rest
   const int g = lane >> 2, tq = lane & 3;
   int cntv, slot0;
   if (shared) {
-    slot0 = nt * kNTile;  // shared groups are 32-aligned, n-tiles 8-aligned
+    slot0 = nt * kNTile;  // shared groups and their n-tiles are 8-aligned
     cntv = 0;
     // count tokens of this n-tile: the last group may be partial
     const int sng = pp.meta[2];
@@ -418,9 +418,16 @@ static double expected_active(int T, int k, int E) {
 void moe_split(const blut_moe_args& a, MoESplit& s) {
   const int sms = num_sms();
   const int64_t T = a.num_tokens, K = a.top_k, E = a.num_experts, S = T * K;
-  const double est_r = expected_active((int)T, (int)K, (int)E) + (double)S / kGroupTok;
-  const int64_t gmax_r = std::min(E, S) + (S + kGroupTok - 1) / kGroupTok + 1;
-  const int64_t gmax_s = (T + kGroupTok - 1) / kGroupTok;
+  // Prefill: on the tcgen05 path, with at least 64 tokens per expert on
+  // average, tokens go in groups of kWideGroupTok so one decoded weight tile
+  // feeds wide MMAs.
+  const bool tc_r = (a.w13.layout & BLUT_LAYOUT_TC) != 0;
+  const bool tc_s = a.shared_inter > 0 && (a.s13.layout & BLUT_LAYOUT_TC) != 0;
+  s.gtok[0] = tc_r && S >= 64 * E ? kWideGroupTok : kGroupTok;
+  s.gtok[1] = tc_s && T >= 64 ? kWideGroupTok : kGroupTok;
+  const double est_r = expected_active((int)T, (int)K, (int)E) + (double)S / s.gtok[0];
+  const int64_t gmax_r = std::min(E, S) + (S + s.gtok[0] - 1) / s.gtok[0] + 1;
+  const int64_t gmax_s = (T + s.gtok[1] - 1) / s.gtok[1];
   const blut_mat_desc* d[4] = {&a.w13, &a.w2, &a.s13, &a.s2};
   for (int i = 0; i < 4; ++i) {
     s.ks[i] = 1;
@@ -432,6 +439,7 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
     s.bps[i] = (int)L.nchunks;
     if (!L.tc) continue;
     s.units[i] = (int)((L.ntiles + 1) / 2);
+    if (s.gtok[i / 2] != kGroupTok) continue;  // wide groups have enough items
     const double est = (i < 2 ? est_r : (double)gmax_s) * s.units[i];
     const int max_ks = (i % 2 == 0) ? 8 : 16;
     int ks = 1;
@@ -446,9 +454,11 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
 size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
   const int64_t T = a.num_tokens, K = a.top_k, E = a.num_experts, H = a.hidden, I = a.inter;
   const int64_t S = T * K;
-  const int64_t gmax = E + (S + kGroupTok - 1) / kGroupTok + 1;
+  MoESplit sp;
+  moe_split(a, sp);
+  const int64_t gmax = E + (S + sp.gtok[0] - 1) / sp.gtok[0] + 1;
   const int64_t ntmax = (S + kNTile - 1) / kNTile + gmax;
-  const int64_t sgmax = (T + kGroupTok - 1) / kGroupTok + 1;
+  const int64_t sgmax = (T + sp.gtok[1] - 1) / sp.gtok[1] + 1;
   const int64_t sntmax = (T + kNTile - 1) / kNTile + 1;
   const bool sh = a.shared_inter > 0;
   size_t off = 0;
@@ -466,8 +476,6 @@ size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
   size_t o_tk = take(S * 4), o_st = take(S * 4);
   size_t o_xf = take(ntmax * (H / kChunk) * kBfragChunkBytes);
   size_t o_af = take(ntmax * (I / kChunk) * kBfragChunkBytes);
-  MoESplit sp;
-  moe_split(a, sp);
   size_t o_y = take(S * H * 4 * sp.ks[1]);
   size_t o_xfs = sh ? take(sntmax * (H / kChunk) * kBfragChunkBytes) : 0;
   size_t o_afs = sh ? take(sntmax * (a.shared_inter / kChunk) * kBfragChunkBytes) : 0;
@@ -633,8 +641,8 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   const bool sh = a.shared_inter > 0;
   const int T = a.num_tokens, K = a.top_k, E = a.num_experts, H = a.hidden;
   const int sms = num_sms();
-  const double est_groups = expected_active(T, K, E) + (double)T * K / kGroupTok;
-  const double est_sgroups = (T + kGroupTok - 1) / kGroupTok;
+  const double est_groups = expected_active(T, K, E) + (double)T * K / ws.split.gtok[0];
+  const double est_sgroups = (T + ws.split.gtok[1] - 1) / ws.split.gtok[1];
   const int b_ntiles = (std::min(T, kGroupTok) + kNTile - 1) / kNTile;
 
   // 1. routing (or the caller's routing) and the shared-expert gate
@@ -657,10 +665,19 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
                                                             ws.logits);
     if ((rc = stage_done("router logits", stream)) != BLUT_OK) return rc;
   }
-  // 2. top-k (when routing) + plan
-  plan_kernel<<<1, 1024, 0, stream>>>(a.topk_ids, (route || gate) ? ws.logits : nullptr, route ? E : 0,
+  // 2. top-k (when routing) + plan.  Long prompts take the top-k in a
+  // separate launch, a warp per token over the whole GPU; the plan kernel is
+  // one CTA.
+  const bool wide_topk = (route || gate) && T > kPlanTopkTokens;
+  if (wide_topk) {
+    topk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(ws.logits, T, route ? E : 0, route ? K : 0, a.renorm, gate ? 1 : 0,
+                                                 ws.ids, ws.tw, ws.sg);
+    if ((rc = stage_done("top-k", stream)) != BLUT_OK) return rc;
+  }
+  plan_kernel<<<1, 1024, 0, stream>>>(wide_topk && route ? ws.ids : a.topk_ids,
+                                      (route || gate) && !wide_topk ? ws.logits : nullptr, route ? E : 0,
                                       (route ? E : 0) + (gate ? 1 : 0), T, K, E, a.renorm, gate ? 1 : 0,
-                                      sh ? 1 : 0, ws.pp, ws.ids, ws.tw, ws.sg);
+                                      sh ? 1 : 0, ws.split.gtok[0], ws.split.gtok[1], ws.pp, ws.ids, ws.tw, ws.sg);
   if ((rc = stage_done("plan", stream)) != BLUT_OK) return rc;
   // 3. activations of x in the operand order of each matmul path
   const bool tc = (a.w13.layout & BLUT_LAYOUT_TC) != 0;
@@ -699,7 +716,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.bps = ws.split.bps[counter];
       t.part = part;
       t.y_sstride = y_sstride;
-      if (launch_tc_mm(d, t, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+      if (launch_tc_mm(d, t, ws.split.gtok[counter / 2], sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
       if (pair && t.ks > 1) {
         // sum the gate/up slices in order, SiLU(gate) * up into the down projection's activations
         const dim3 grid((unsigned)(ws.split.groups[counter] * t.units), (unsigned)(kTcRows * 32 / 256));
@@ -773,7 +790,10 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
 int moe_launch_count(const blut_moe_args& a) {
   const bool sh = a.shared_inter > 0;
   int n = 0;
-  if (!a.topk_ids || (sh && a.shared_gate_mode == 1)) ++n;  // router / gate logits
+  if (!a.topk_ids || (sh && a.shared_gate_mode == 1)) {
+    ++n;                                                   // router / gate logits
+    if (a.num_tokens > kPlanTopkTokens) ++n;               // separate top-k
+  }
   n += 2;                                                  // top-k + plan, gather
   n += 2;                                                  // routed gate/up, down
   if (sh) n += 2;                                          // shared gate/up, down

@@ -35,16 +35,21 @@ namespace blut {
 
 constexpr int kTcDecodeWarps = 8;
 constexpr int kTcThreads = 32 * (2 + kTcDecodeWarps);
-constexpr int kTcRingBudget = 96 * 1024;
+constexpr int kTcRingBudget = 96 * 1024;        // per CTA, two CTAs per SM (MT = 32)
+constexpr int kTcRingBudgetWide = 200 * 1024;   // one CTA per SM (MT = 128)
 constexpr int kTcQueue = 4;          // depth of the shared-memory item queue
-constexpr int kTcDCols = 64;         // tensor-memory columns of one accumulator buffer (2 tiles x N<=32)
-// Tensor memory of a CTA (256 columns, two CTAs per SM): LUT formats keep one
-// accumulator buffer (columns 0-63) and a ring of three A slots of 64 columns
-// (2 tiles x 64 fp16 columns of K); dense weights need no A slots and
-// double-buffer the accumulators so the MMA runs one item ahead of the
-// epilogue.
+// Token groups hold up to MT tokens: MT = 32 for decode (two CTAs per SM,
+// 256 tensor-memory columns each) and MT = 128 for prefill (one CTA per SM,
+// 512 columns), so that one decoded weight tile feeds MMAs of N up to MT.
+// An accumulator buffer is 2 tiles x MT fp32 columns.  LUT formats keep one
+// buffer and a ring of three A slots of 64 columns (2 tiles x 64 fp16
+// columns of K) after it; dense weights need no A slots and double-buffer
+// the accumulators so the MMA runs one item ahead of the epilogue.
 constexpr int kTcASlots = 3;
-constexpr int kTcACol0 = kTcDCols;
+template <int MT>
+constexpr int tc_cols(bool dense) {
+  return dense ? 4 * MT : (MT == 32 ? 256 : 512);
+}
 
 // Multipliers {1 << 31, 1 << 16} handed to the decode (see tc_lut16x8).
 struct TcMul {
@@ -305,27 +310,29 @@ struct TcRing {
 // as soon as their loads are done; the activations, read by the MMA, sit in
 // a separate small ring freed by the MMA's commit.  Weight stages therefore
 // recycle without waiting for the tensor core.
-template <class Dec>
+template <class Dec, int MT>
 __host__ __device__ inline int tc_stage_bytes(const TcParams& p) {
-  return (2 * p.tile_bytes + (Dec::kDense ? kMaxNT * Dec::KB * 16 : 0) + 127) & ~127;
+  return (2 * p.tile_bytes + (Dec::kDense ? (MT / kNTile) * Dec::KB * 16 : 0) + 127) & ~127;
 }
-template <class Dec>
+template <class Dec, int MT>
 __host__ __device__ constexpr int tc_xstage_bytes() {
-  return Dec::kDense ? 0 : kMaxNT * Dec::KB * 16;
+  return Dec::kDense ? 0 : (MT / kNTile) * Dec::KB * 16;
 }
 
 // Barriers, queue and flags take the first 512 bytes, the rings follow.
-template <class Dec>
+template <class Dec, int MT>
 __host__ inline int tc_smem_bytes(const TcParams& p) {
-  return 512 + p.stages * tc_stage_bytes<Dec>(p) + p.xstages * tc_xstage_bytes<Dec>();
+  return 512 + p.stages * tc_stage_bytes<Dec, MT>(p) + p.xstages * tc_xstage_bytes<Dec, MT>();
 }
 
-template <class Dec>
-__global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) {
+template <class Dec, int MT>
+__global__ void __launch_bounds__(kTcThreads, MT == 32 ? 2 : 1) tc_mm_kernel(const TcParams p) {
   constexpr bool kDense = Dec::kDense;
   constexpr int KB = Dec::KB;
-  constexpr uint32_t kCols = kDense ? 128 : 256;  // tensor-memory columns of this CTA
+  constexpr uint32_t kCols = tc_cols<MT>(kDense);  // tensor-memory columns of this CTA
   constexpr int kDBufs = kDense ? 2 : 1;           // accumulator buffers
+  constexpr int kDCols = 2 * MT;                   // columns of one accumulator buffer
+  constexpr int kACol0 = kDCols;                   // first A slot (LUT formats)
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [8]
   uint64_t* empty = full + 8;                          // [8]
@@ -343,8 +350,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
   uint64_t* xempty = full + 45;                        // [4] activation stage read (MMA commit)
   uint8_t* ring = smem + 512;
   const int S = p.stages, SX = p.xstages;
-  const int stage_bytes = tc_stage_bytes<Dec>(p);
-  constexpr int xstage_bytes = tc_xstage_bytes<Dec>();
+  const int stage_bytes = tc_stage_bytes<Dec, MT>(p);
+  constexpr int xstage_bytes = tc_xstage_bytes<Dec, MT>();
   uint8_t* xring = ring + (int64_t)S * stage_bytes;
   const int boff = 2 * p.tile_bytes;  // activations inside a dense stage
   const int qoff1 = 2 * p.piece[0];   // second plane inside a stage
@@ -468,11 +475,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
         const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
         const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
         const int ntl = min(2, p.ntiles - 2 * u);
-        const uint32_t idesc = tc_idesc(Dec::kBF16, nnt <= 2 ? 16 : 32);
+        const uint32_t idesc = tc_idesc(Dec::kBF16, min(MT, (nnt + 1) / 2 * 16));
         const int db = rd.i;
         if (rd.wrapped && !wait_or_abort(smem_u32(dempty + db), rd.ph ^ 1u, abort_flag, p.status)) break;
         tc_fence_after();
-        const uint32_t dcol = tmem + db * kTcDCols;
+        const uint32_t dcol = tmem + db * kDCols;
         bool ok = true;
         // dense: r walks the combined stages; LUT formats: r walks the activation stages
         for (int b = b0; b < b1 && ok; ++b, r.next(kDense ? S : SX)) {
@@ -489,7 +496,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
               const uint64_t bd = tc_desc(st + boff + sl * 256, 128, KB * 16);
               for (int t = 0; t < ntl; ++t) {
                 const uint64_t ad = tc_desc(st + t * p.piece[0] + sl * 2 * 2048, 2048, 128);
-                tc_mma_ss(dcol + t * 32, ad, bd, idesc, ((b - b0) | sl) != 0);
+                tc_mma_ss(dcol + t * MT, ad, bd, idesc, ((b - b0) | sl) != 0);
               }
             }
           } else {
@@ -505,7 +512,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
               for (int sl = 0; sl < 4; ++sl) {
                 const uint64_t bd = tc_desc(st + (h * 4 + sl) * 256, 128, KB * 16);
                 for (int t = 0; t < ntl; ++t)
-                  tc_mma_ts(dcol + t * 32, tmem + kTcACol0 + j * 64 + t * 32 + sl * 8, bd, idesc,
+                  tc_mma_ts(dcol + t * MT, tmem + kACol0 + j * 64 + t * 32 + sl * 8, bd, idesc,
                             ((b - b0) | h | sl) != 0);
               }
               tc_commit(smem_u32(aempty + j));
@@ -568,7 +575,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
               }
             }
             tc_fence_after();
-            const uint32_t aslot = tmem + lane_base + kTcACol0 + j * 64 + t * 32;
+            const uint32_t aslot = tmem + lane_base + kACol0 + j * 64 + t * 32;
             if (active) {
               uint32_t qa[16], qb[16];
               Dec::decode_q(cp, tp, row, h, 0, qa, p.mul);
@@ -594,67 +601,71 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
       ok = wait_or_abort(smem_u32(dfull + db), rd.ph, abort_flag, p.status);
       if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
       tc_fence_after();
-      const uint32_t dcol = tmem + lane_base + db * kTcDCols;
+      const uint32_t dcol = tmem + lane_base + db * kDCols;
       if (p.pair) {
-        // tokens 16t .. 16t+15 of unit row `row`: gate tile at columns 0..31, up tile at 32..63
-        uint32_t g[16], v[16];
-        tc_ld16(dcol + 16 * t, g);
-        tc_wait_ld16(g);
-        tc_ld16(dcol + 32 + 16 * t, v);
-        tc_wait_ld16(v);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(dempty + db));
-        if (p.ks > 1) {
-          // partial sums of this slice; splitk_silu_kernel adds the slices up
-          // after this launch (a kernel boundary orders them without fences)
-          float* mine = p.part + (int64_t)item * (2 * kTcRows * 32) + row * 32 + 16 * t;
-#pragma unroll
-          for (int n = 0; n < 16; n += 4) {
-            *reinterpret_cast<float4*>(mine + n) =
-                make_float4(__uint_as_float(g[n]), __uint_as_float(g[n + 1]), __uint_as_float(g[n + 2]),
-                            __uint_as_float(g[n + 3]));
-            *reinterpret_cast<float4*>(mine + kTcRows * 32 + n) =
-                make_float4(__uint_as_float(v[n]), __uint_as_float(v[n + 1]), __uint_as_float(v[n + 2]),
-                            __uint_as_float(v[n + 3]));
-          }
-          rd.next(kDBufs);
-          continue;
-        }
+        // warp t: tokens [t MT/2, (t+1) MT/2) of unit row `row`, 16 at a time;
+        // gate tile at columns 0 .. MT-1, up tile at MT .. 2MT-1
         const int col = u * kTcRows + row;  // K index of the down projection
         const int nt0 = p.gt.nt0[gi];
         uint8_t* dst = p.act_out + (int64_t)(col >> 7) * 2048 + tc_bact_byte(0, col & 127);
+#pragma unroll 1
+        for (int c = 0; c < MT / 32; ++c) {
+          const int tok0 = t * (MT / 2) + 16 * c;
+          if (tok0 >= ntok) break;  // warp-uniform
+          uint32_t g[16], v[16];
+          tc_ld16(dcol + tok0, g);
+          tc_wait_ld16(g);
+          tc_ld16(dcol + MT + tok0, v);
+          tc_wait_ld16(v);
+          if (p.ks > 1) {
+            // partial sums of this slice (MT = 32); splitk_silu_kernel adds
+            // the slices up after this launch (a kernel boundary orders them
+            // without fences)
+            float* mine = p.part + (int64_t)item * (2 * kTcRows * 32) + row * 32 + tok0;
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          const int tok = 16 * t + n;
-          if (tok < ntok) {
-            const float val = silu_f(__uint_as_float(g[n])) * __uint_as_float(v[n]);
-            *reinterpret_cast<uint16_t*>(dst + (int64_t)(nt0 + (tok >> 3)) * p.out_nch * 2048 + (tok & 7) * 16) =
-                f32_to_act<Dec::kBF16>(val);
+            for (int n = 0; n < 16; n += 4) {
+              *reinterpret_cast<float4*>(mine + n) =
+                  make_float4(__uint_as_float(g[n]), __uint_as_float(g[n + 1]), __uint_as_float(g[n + 2]),
+                              __uint_as_float(g[n + 3]));
+              *reinterpret_cast<float4*>(mine + kTcRows * 32 + n) =
+                  make_float4(__uint_as_float(v[n]), __uint_as_float(v[n + 1]), __uint_as_float(v[n + 2]),
+                              __uint_as_float(v[n + 3]));
+            }
+            continue;
           }
-        }
-      } else {
-        // tile t of the unit, tokens 0..31
-        uint32_t v0[16], v1[16];
-        if (t < ntl) {
-          tc_ld16(dcol + 32 * t, v0);
-          tc_wait_ld16(v0);
-          tc_ld16(dcol + 32 * t + 16, v1);
-          tc_wait_ld16(v1);
+#pragma unroll
+          for (int n = 0; n < 16; ++n) {
+            const int tok = tok0 + n;
+            if (tok < ntok) {
+              const float val = silu_f(__uint_as_float(g[n])) * __uint_as_float(v[n]);
+              *reinterpret_cast<uint16_t*>(dst + (int64_t)(nt0 + (tok >> 3)) * p.out_nch * 2048 + (tok & 7) * 16) =
+                  f32_to_act<Dec::kBF16>(val);
+            }
+          }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(dempty + db));
+      } else {
+        // tile t of the unit, tokens 0 .. MT-1, 16 at a time
         if (t < ntl) {
           const int hrow = (2 * u + t) * kTcRows + row;
           float* y = p.y_out + (item % p.ks) * p.y_sstride + (int64_t)p.gt.slot0[gi] * p.y_ld + hrow;
+#pragma unroll 1
+          for (int c = 0; c < MT / 16; ++c) {
+            const int tok0 = 16 * c;
+            if (tok0 >= ntok) break;  // warp-uniform
+            uint32_t v[16];
+            tc_ld16(dcol + t * MT + tok0, v);
+            tc_wait_ld16(v);
 #pragma unroll
-          for (int n = 0; n < 16; ++n)
-            if (n < ntok) y[(int64_t)n * p.y_ld] = __uint_as_float(v0[n]);
-#pragma unroll
-          for (int n = 0; n < 16; ++n)
-            if (16 + n < ntok) y[(int64_t)(16 + n) * p.y_ld] = __uint_as_float(v1[n]);
+            for (int n = 0; n < 16; ++n)
+              if (tok0 + n < ntok) y[(int64_t)(tok0 + n) * p.y_ld] = __uint_as_float(v[n]);
+          }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(dempty + db));
       }
       rd.next(kDBufs);
     }
@@ -669,14 +680,15 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_mm_kernel(const TcParams p) 
 
 // Host-side launch: ring depth from the shared-memory budget, one persistent
 // CTA per resident slot.
-template <class Dec>
+template <class Dec, int MT>
 inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
-  const int stage = tc_stage_bytes<Dec>(p);
-  const int xstage = tc_xstage_bytes<Dec>();
-  p.xstages = xstage ? std::max(2, std::min(4, (kTcRingBudget / 6) / xstage)) : 0;
-  p.stages = std::max(2, std::min(8, (kTcRingBudget - p.xstages * xstage) / stage));
-  const int smem = tc_smem_bytes<Dec>(p);
-  auto kern = tc_mm_kernel<Dec>;
+  const int budget = MT == 32 ? kTcRingBudget : kTcRingBudgetWide;
+  const int stage = tc_stage_bytes<Dec, MT>(p);
+  const int xstage = tc_xstage_bytes<Dec, MT>();
+  p.xstages = xstage ? std::max(2, std::min(4, (budget / 6) / xstage)) : 0;
+  p.stages = std::max(2, std::min(8, (budget - p.xstages * xstage) / stage));
+  const int smem = tc_smem_bytes<Dec, MT>(p);
+  auto kern = tc_mm_kernel<Dec, MT>;
   static std::mutex mu;
   static int cached_smem = -1, cached_per_sm = 1;
   int per_sm;
@@ -694,7 +706,7 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
       if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
       if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kTcThreads, smem);
       if (e != cudaSuccess) return e;
-      cached_per_sm = (nb >= 2 || 2 * (smem + 1024) <= smem_sm) ? 2 : 1;
+      cached_per_sm = MT == 32 && (nb >= 2 || 2 * (smem + 1024) <= smem_sm) ? 2 : 1;
       e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
       if (e != cudaSuccess) return e;
       cached_smem = smem;

@@ -23,17 +23,24 @@ bool tc_planes(const blut_mat_desc& d, bool pair, TcParams& p) {
   return true;
 }
 
-cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int sms, cudaStream_t stream) {
+template <int MT>
+static cudaError_t launch_tc_mt(const blut_mat_desc& d, const TcParams& p, int sms, cudaStream_t stream) {
   if (d.format == BLUT_FMT_DENSE)
-    return d.dtype == BLUT_BF16 ? launch_tc<TcDecDense<true>>(p, sms, stream)
-                                : launch_tc<TcDecDense<false>>(p, sms, stream);
+    return d.dtype == BLUT_BF16 ? launch_tc<TcDecDense<true>, MT>(p, sms, stream)
+                                : launch_tc<TcDecDense<false>, MT>(p, sms, stream);
   if (d.format == BLUT_FMT_B && d.bits == 4) {
     switch (d.group) {
-      case 32: return launch_tc<TcDecB4<32>>(p, sms, stream);
-      case 64: return launch_tc<TcDecB4<64>>(p, sms, stream);
-      case 128: return launch_tc<TcDecB4<128>>(p, sms, stream);
+      case 32: return launch_tc<TcDecB4<32>, MT>(p, sms, stream);
+      case 64: return launch_tc<TcDecB4<64>, MT>(p, sms, stream);
+      case 128: return launch_tc<TcDecB4<128>, MT>(p, sms, stream);
     }
   }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int group_tokens, int sms, cudaStream_t stream) {
+  if (group_tokens == 32) return launch_tc_mt<32>(d, p, sms, stream);
+  if (group_tokens == 128) return launch_tc_mt<128>(d, p, sms, stream);
   return cudaErrorInvalidValue;
 }
 

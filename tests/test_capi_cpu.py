@@ -118,7 +118,7 @@ def test_moe_workspace_size_host_only():
     (dict(num_tokens=0), _lib.BLUT_ERR_INVALID),
     (dict(x=None), _lib.BLUT_ERR_INVALID),
     (dict(topk_ids=None), _lib.BLUT_ERR_INVALID),  # no routing and no router weights
-    (dict(num_tokens=1024), _lib.BLUT_ERR_UNSUPPORTED),  # T*k beyond the decode path
+    (dict(num_tokens=1 << 21), _lib.BLUT_ERR_UNSUPPORTED),  # T*k beyond 4M slots
     (dict(x=(1 << 20) + 2), _lib.BLUT_ERR_INVALID),  # misaligned activations
     (dict(w13_stride=1024), _lib.BLUT_ERR_INVALID),
 ])
@@ -142,6 +142,9 @@ def test_launch_count():
     assert lib.blut_moe_launch_count(C.byref(tc)) == 6
     tc.num_tokens = 256  # enough items without a split
     assert lib.blut_moe_launch_count(C.byref(tc)) == 5
+    tc.num_tokens, tc.topk_ids = 4096, None  # prefill with routing: router, top-k, plan, gather, 2 matmuls, combine
+    tc.router_w = 1 << 22
+    assert lib.blut_moe_launch_count(C.byref(tc)) == 7
 
 
 LAYOUT_PROBE = r"""

@@ -262,3 +262,36 @@ def test_qwen15_layer_decode_batch32_bench_shape():
     ref = O.moe_forward(xn, ids, tw, lambda e: deq(q13, e), lambda e: deq(q2, e), act_dtype="f16",
                         shared13=s13.float().cpu().numpy(), shared2=s2.float().cpu().numpy(), shared_gate=rw[E])
     check_layer(out[torch.from_numpy(keep).cuda()], ref[keep], torch.float16, "bench-shaped layer")
+
+
+@pytest.mark.parametrize("T,with_shared", [(1024, False), (2048, True)])
+def test_prefill_wide_groups(T, with_shared):
+    """Prefill regime (tcgen05 path, >= 64 tokens per expert): 128-token groups,
+    the separate top-k launch, and (with the shared expert) wide shared groups."""
+    E, H, I, k, Is = 8, 512, 256, 2, 256
+    fmt = LUTFormat("b", 4, 64)
+    experts, W13, W2 = build_b_layer(fmt, E=E, H=H, I=I, seed=31, tc=True)
+    rng = np.random.Generator(np.random.PCG64(T))
+    rw = (rng.standard_normal((E + 1, H)) * 0.05).astype(np.float16)
+    sh = None
+    if with_shared:
+        s13 = O.student_t_weights(rng, (2 * Is, H)).astype(np.float16)
+        s2 = O.student_t_weights(rng, (H, Is)).astype(np.float16)
+        sh = SharedExpert.from_dense(cuda(s13), cuda(s2), tc=True)
+    layer = LUTMoELayer(experts, k, router_w=cuda(rw), shared=sh, shared_gate_mode=1)
+    x = cuda(O.rms_activations(rng, T, H).astype(np.float16))
+    out = layer.forward(x)
+    layer.check_status()
+    xn = x.float().cpu().numpy().astype(np.float64)
+    logits = xn @ rw[:E].astype(np.float64).T
+    ids, tw = O.routing(logits, k)
+    srt = np.sort(logits, axis=1)
+    keep = srt[:, -k] - srt[:, -k - 1] > 1e-4
+    kw = {}
+    if with_shared:
+        kw = dict(shared13=s13.astype(np.float32), shared2=s2.astype(np.float32), shared_gate=rw[E].astype(np.float32))
+    ref = O.moe_forward(xn, ids, tw, W13, W2, act_dtype="f16", **kw)
+    check_layer(out[torch.from_numpy(keep).cuda()], ref[keep], torch.float16, f"prefill T={T}")
+    # the same layer at decode size still matches (both regimes in one process)
+    xd = x[:5].contiguous()
+    check_layer(layer.forward(xd)[torch.from_numpy(keep[:5]).cuda()], ref[:5][keep[:5]], torch.float16, "decode")
