@@ -34,7 +34,13 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 H, E, I, TOPK, IS, LAYERS = 2048, 60, 1408, 4, 5632, 24
+QWEN = dict(H=H, E=E, I=I, IS=IS)
 METRIC = "LUT-MoE decode tokens/s; expert LUT-GEMV HBM GB/s vs ~8 TB/s peak"
+# DeepSeek-V2-Lite MoE layers (26 of 27; layer 0 is dense),
+# 64 routed experts of I 1408, top-6 softmax, two shared experts (one MLP of
+# I 2816), prefill of 8 x 4096 tokens.
+DSV2 = dict(H=2048, E=64, I=1408, IS=2816, TOPK=6, LAYERS=26, TOKENS=8 * 4096)
+PREFILL_METRIC = "LUT-MoE prefill tokens/s; grouped LUT-GEMM tensor TFLOP/s"
 
 
 def parse():
@@ -49,6 +55,8 @@ def parse():
     p.add_argument("--group", type=int, default=64)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                   help="decode: the BASELINE metric (config 2); prefill: config 4's MoE layers")
     return p.parse_args()
 
 
@@ -107,11 +115,13 @@ class Clocks:
 
 
 # ------------------------------------------------------------ workload ---
-def build_layers(n_layers, experts_local, e0, bits, group, device, seed=0):
-    """Synthetic Qwen1.5-MoE MoE layers (experts [e0, e0 + experts_local) of each)."""
+def build_layers(n_layers, experts_local, e0, bits, group, device, seed=0, shape=None):
+    """Synthetic MoE layers (experts [e0, e0 + experts_local) of each); shape
+    {H, E, I, IS} defaults to Qwen1.5-MoE-A2.7B's."""
     import torch
     from block_lut_b200.formats import LUTFormat, encode
     from block_lut_b200.moe import LUTExperts, SharedExpert
+    H, E, I, IS = (shape or QWEN)["H"], (shape or QWEN)["E"], (shape or QWEN)["I"], (shape or QWEN)["IS"]
 
     fmt = LUTFormat("b", bits, group)
     torch.manual_seed(seed)
@@ -357,9 +367,85 @@ def run_reference(a):
     print(json.dumps(res), flush=True)
 
 
+def run_prefill(a):
+    """Config 4 prefill: every MoE layer of the stack over one 8 x 4096-token
+    batch, on one GPU.  Reported as tokens/s of the whole stack and, for the
+    routed matmuls, as tensor TFLOP/s against the measured bf16 peak."""
+    import ctypes as C
+    import torch
+    from block_lut_b200.moe import LUTMoELayer
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    n_layers = a.layers if a.layers != LAYERS else DSV2["LAYERS"]
+    T, k = DSV2["TOKENS"], DSV2["TOPK"]
+    fmt, layers = build_layers(n_layers, DSV2["E"], 0, a.bits, a.group, dev, shape=DSV2)
+    moes = [LUTMoELayer(ex, k, router_w=rw[:DSV2["E"]].contiguous(), shared=sh, shared_gate_mode=0)
+            for ex, rw, sh in layers]
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(T, DSV2["H"], generator=g, device=dev)
+    x = (x / x.pow(2).mean(dim=1, keepdim=True).sqrt()).half().contiguous()
+    out = torch.empty_like(x)
+
+    def step():
+        for m in moes:
+            m.forward(x, out=out)
+    for _ in range(max(1, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    for m in moes:
+        m.check_status()
+    clk = Clocks(0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = e0.elapsed_time(e1) / a.steps
+    # routed matmul time per layer through the library's profiling events
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    for e in evs:
+        e.record()
+    torch.cuda.synchronize()
+    handles = (C.c_void_p * 4)(*[e.cuda_event for e in evs])
+    t_mm = 0.0
+    for m in moes:
+        m._args.prof_events = C.cast(handles, C.c_void_p)
+        m.forward(x, out=out)
+        m._args.prof_events = None
+        torch.cuda.synchronize()
+        t_mm += evs[0].elapsed_time(evs[1]) + evs[2].elapsed_time(evs[3])
+    t_mm /= len(moes)
+    H, I, IS = DSV2["H"], DSV2["I"], DSV2["IS"]
+    flops_routed = 2.0 * T * k * 3 * I * H
+    flops_shared = 2.0 * T * 3 * IS * H
+    pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    peak = pk.get("bf16_tflops_sustained", 1400.0)
+    achieved = flops_routed / (t_mm / 1e3) / 1e12
+    res = {"metric": PREFILL_METRIC, "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "f16", "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU Lloyd-encoded; N(0,1) tokens",
+           "config": {"workload": f"DeepSeek-V2-Lite MoE stack, prefill {T} tokens", "layers": n_layers,
+                      "tokens": T, "experts": DSV2["E"], "top_k": k, "hidden": H, "inter": I, "shared_inter": IS,
+                      "format": f"BlockLUT {a.bits}-bit g{a.group} fp16 tables", "parallelism": "single GPU"},
+           "roofline": {"kernel": "tc_mm_kernel (tcgen05, 128-token groups; routed gate/up+SiLU*up and down)",
+                        "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                        "frac": achieved / peak,
+                        "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops_sustained)" if pk else "fallback",
+                        "traffic": None, "ms_routed_mm_per_layer": t_mm,
+                        "tflop_per_layer": (flops_routed + flops_shared) / 1e12},
+           "gpu_launches": a.steps * n_layers * moes[0].launch_count(T, caller_routing=False),
+           "clocks": clocks}
+    print(json.dumps(res), flush=True)
+
+
 if __name__ == "__main__":
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     else:
         run_ours(args)

@@ -252,7 +252,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
 // (tc_bact_byte) for that destination instead of mma.sync B fragments.
 __global__ void __launch_bounds__(32) gather_bfrag_kernel(const uint16_t* __restrict__ x, int hidden, PlanPtrs pp,
                                                           uint8_t* __restrict__ xf, uint8_t* __restrict__ xfs,
-                                                          int tc_mask) {
+                                                          int tc_mask, int kb_r, int kb_s, int64_t ntstride_r,
+                                                          int64_t ntstride_s) {
   const bool shared = blockIdx.z == 1;
   const int nt = blockIdx.x;
   const int c = blockIdx.y;
@@ -287,12 +288,14 @@ __global__ void __launch_bounds__(32) gather_bfrag_kernel(const uint16_t* __rest
       const int slot = slot0 + tok;
       row = x + (int64_t)(shared ? slot : pp.slot_tok[slot]) * hidden + c * kChunk;
     }
-    uint8_t* dst = (shared ? xfs : xf) + ((int64_t)nt * nchunks + c) * kBfragChunkBytes;
+    uint8_t* dst = shared ? xfs : xf;
+    const int kb = shared ? kb_s : kb_r;
+    const int64_t nts = shared ? ntstride_s : ntstride_r;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int kg = (lane >> 3) + 4 * i;
       const uint4 v = row ? *reinterpret_cast<const uint4*>(row + kg * 8) : make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(dst + kg * 128 + tok * 16) = v;
+      *reinterpret_cast<uint4*>(dst + tc_bact_off((int64_t)nt * kNTile + tok, c * kChunk + kg * 8, kb, nts)) = v;
     }
     return;
   }
@@ -323,7 +326,8 @@ __global__ void __launch_bounds__(32) gather_bfrag_kernel(const uint16_t* __rest
 // (ku, j): 256 threads = 8 rows x 32 tokens, rows 8j .. 8j + 7 of the unit.
 template <bool BF16>
 __global__ void __launch_bounds__(256) splitk_silu_kernel(const float* __restrict__ part, int ks, int units,
-                                                          GroupTab gt, uint8_t* __restrict__ act, int out_nch) {
+                                                          GroupTab gt, uint8_t* __restrict__ act, int out_kb,
+                                                          int64_t ntstride) {
   const int ku = blockIdx.x;
   const int gi = ku / units, u = ku % units;
   if (gi >= *gt.n_groups) return;
@@ -338,7 +342,7 @@ __global__ void __launch_bounds__(256) splitk_silu_kernel(const float* __restric
     v += src[(int64_t)s * (2 * kTcRows * 32) + kTcRows * 32];
   }
   const int col = u * kTcRows + row;
-  uint8_t* dst = act + ((int64_t)(nt0 + (n >> 3)) * out_nch + (col >> 7)) * 2048 + tc_bact_byte(n & 7, col & 127);
+  uint8_t* dst = act + tc_bact_off((int64_t)nt0 * kNTile + n, col, out_kb, ntstride);
   *reinterpret_cast<uint16_t*>(dst) = f32_to_act<BF16>(silu_f(g) * v);
 }
 
@@ -685,7 +689,9 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   {
     dim3 grid((unsigned)std::max<int64_t>(ws.ntmax, sh ? ws.sntmax : 0), (unsigned)(H / kChunk), sh ? 2 : 1);
     gather_bfrag_kernel<<<grid, 32, 0, stream>>>((const uint16_t*)a.x, H, ws.pp, ws.xf, ws.xfs,
-                                                 (tc ? 1 : 0) | (stc ? 2 : 0));
+                                                 (tc ? 1 : 0) | (stc ? 2 : 0), tc_block_cols(a.w13.format, a.w13.group),
+                                                 sh ? tc_block_cols(a.s13.format, a.s13.group) : 0, ws.ntmax,
+                                                 ws.sntmax);
   }
   if ((rc = stage_done("gather", stream)) != BLUT_OK) return rc;
 
@@ -695,7 +701,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   const GroupTab shared{ws.pp.meta + 2, ws.pp.sg_expert, ws.pp.sg_slot0, ws.pp.sg_ntok, ws.pp.sg_nt0};
   auto pass = [&](const blut_mat_desc& d, const void* w, int64_t stride, const GroupTab& gt, double est,
                   const uint8_t* bin, uint8_t* act, int out_k, float* y, int counter, float* part,
-                  int64_t y_sstride) -> int {
+                  int64_t y_sstride, const blut_mat_desc* next) -> int {
     const bool pair = act != nullptr;
     const int K = (int)d.cols;
     if (d.layout & BLUT_LAYOUT_TC) {
@@ -705,9 +711,9 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.wstride = stride;
       t.gt = gt;
       t.bin = bin;
-      t.bin_nch = K / kChunk;
+      t.ntstride = counter < 2 ? ws.ntmax : ws.sntmax;
       t.act_out = act;
-      t.out_nch = out_k / kChunk;
+      t.out_kb = next ? tc_block_cols(next->format, next->group) : 0;
       t.y_out = y;
       t.y_ld = H;
       t.counter = ws.pp.counters + counter;
@@ -721,9 +727,9 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
         // sum the gate/up slices in order, SiLU(gate) * up into the down projection's activations
         const dim3 grid((unsigned)(ws.split.groups[counter] * t.units), (unsigned)(kTcRows * 32 / 256));
         if (a.dtype == BLUT_BF16)
-          splitk_silu_kernel<true><<<grid, 256, 0, stream>>>(part, t.ks, t.units, gt, act, t.out_nch);
+          splitk_silu_kernel<true><<<grid, 256, 0, stream>>>(part, t.ks, t.units, gt, act, t.out_kb, t.ntstride);
         else
-          splitk_silu_kernel<false><<<grid, 256, 0, stream>>>(part, t.ks, t.units, gt, act, t.out_nch);
+          splitk_silu_kernel<false><<<grid, 256, 0, stream>>>(part, t.ks, t.units, gt, act, t.out_kb, t.ntstride);
       }
       return cudaGetLastError() == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
     }
@@ -748,14 +754,14 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   // 4. gate/up + SiLU*up (routed, then shared)
   if (ev && cudaEventRecord(ev[0], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if ((rc = pass(a.w13, a.w13_tiled, a.w13_stride, routed, est_groups, ws.xf, ws.af, a.inter, nullptr, 0,
-                 ws.part_r, 0)) !=
+                 ws.part_r, 0, &a.w2)) !=
       BLUT_OK)
     return rc;
   if ((rc = stage_done("routed gate/up", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[1], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if (sh) {
     if ((rc = pass(a.s13, a.s13_tiled, 0, shared, est_sgroups, ws.xfs, ws.afs, a.shared_inter, nullptr, 2,
-                   ws.part_s, 0)) !=
+                   ws.part_s, 0, &a.s2)) !=
         BLUT_OK)
       return rc;
     if ((rc = stage_done("shared gate/up", stream)) != BLUT_OK) return rc;
@@ -763,13 +769,13 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   // 5. down (routed, then shared)
   if (ev && cudaEventRecord(ev[2], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if ((rc = pass(a.w2, a.w2_tiled, a.w2_stride, routed, est_groups, ws.af, nullptr, 0, ws.y, 1, nullptr,
-                 ws.y_sstride)) != BLUT_OK)
+                 ws.y_sstride, nullptr)) != BLUT_OK)
     return rc;
   if ((rc = stage_done("routed down", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[3], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if (sh) {
     if ((rc = pass(a.s2, a.s2_tiled, 0, shared, est_sgroups, ws.afs, nullptr, 0, ws.ys, 3, nullptr,
-                   ws.ys_sstride)) != BLUT_OK) return rc;
+                   ws.ys_sstride, nullptr)) != BLUT_OK) return rc;
     if ((rc = stage_done("shared down", stream)) != BLUT_OK) return rc;
   }
 

@@ -33,8 +33,17 @@
 
 namespace blut {
 
-constexpr int kTcDecodeWarps = 8;
-constexpr int kTcThreads = 32 * (2 + kTcDecodeWarps);
+constexpr int kTcDecodeWarps = 8;  // one decode set: 2 tiles x 4 tensor-memory lane quarters
+// Decode sets per CTA: one at two CTAs per SM (MT = 32); two at one CTA per
+// SM (MT = 128), taking alternate column blocks of an item.
+template <int MT>
+constexpr int tc_sets() {
+  return MT == 32 ? 1 : 2;
+}
+template <int MT>
+constexpr int tc_threads() {
+  return 32 * (2 + kTcDecodeWarps * tc_sets<MT>());
+}
 constexpr int kTcRingBudget = 96 * 1024;        // per CTA, two CTAs per SM (MT = 32)
 constexpr int kTcRingBudgetWide = 200 * 1024;   // one CTA per SM (MT = 128)
 constexpr int kTcQueue = 4;          // depth of the shared-memory item queue
@@ -68,10 +77,10 @@ struct TcParams {
   int units;               // ceil(ntiles / 2)
   int pair;                // 1: gate/up epilogue (SiLU(gate) * up); 0: fp32 rows
   GroupTab gt;
-  const uint8_t* bin;      // activations, [n-tile][K / 128][2 KB] (tc_bact_byte order)
-  int bin_nch;             // K / 128
-  uint8_t* act_out;        // pair epilogue: down-projection activations, same order
-  int out_nch;             // I / 128
+  const uint8_t* bin;      // activations in the tcgen05 operand order (tc_bact_off), blocks of KB columns
+  int64_t ntstride;        // n-tiles between column blocks of bin and act_out
+  uint8_t* act_out;        // pair epilogue: down-projection activations, blocks of out_kb columns
+  int out_kb;
   float* y_out;            // single epilogue: y[slot][y_ld] (slice s of split K at y_out + s * y_sstride)
   int y_ld;
   int64_t y_sstride;
@@ -88,10 +97,15 @@ struct TcParams {
   int xstages;             // activation stages (LUT formats)
 };
 
-// Byte offset of activation (token n in [0, 8), column k in [0, 128)) inside
-// one (n-tile, 128-column chunk) block: 16 core matrices of 8 tokens x 8
-// columns, K-major, as the tcgen05.mma B operand reads them without swizzle.
-__host__ __device__ inline int tc_bact_byte(int n, int k) { return (k >> 3) * 128 + n * 16 + (k & 7) * 2; }
+// Activations for the tcgen05 matmuls: blocks of kb columns (the consumer's
+// column block), each block holding every n-tile of 8 tokens in order
+// (ntstride of them), each (block, n-tile) piece kb / 8 core matrices of 8
+// tokens x 8 columns, K-major, as tcgen05.mma reads its B operand without
+// swizzle.  A token group's n-tiles are consecutive, so one bulk copy moves
+// a group's block.  Byte offset of (token n, column k):
+__host__ __device__ inline int64_t tc_bact_off(int64_t n, int k, int kb, int64_t ntstride) {
+  return ((int64_t)(k / kb) * ntstride + (n >> 3)) * (kb * 16) + ((k % kb) >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2;
+}
 
 // ------------------------------------------------------------ PTX helpers --
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -326,13 +340,15 @@ __host__ inline int tc_smem_bytes(const TcParams& p) {
 }
 
 template <class Dec, int MT>
-__global__ void __launch_bounds__(kTcThreads, MT == 32 ? 2 : 1) tc_mm_kernel(const TcParams p) {
+__global__ void __launch_bounds__(tc_threads<MT>(), MT == 32 ? 2 : 1) tc_mm_kernel(const TcParams p) {
   constexpr bool kDense = Dec::kDense;
   constexpr int KB = Dec::KB;
   constexpr uint32_t kCols = tc_cols<MT>(kDense);  // tensor-memory columns of this CTA
   constexpr int kDBufs = kDense ? 2 : 1;           // accumulator buffers
   constexpr int kDCols = 2 * MT;                   // columns of one accumulator buffer
   constexpr int kACol0 = kDCols;                   // first A slot (LUT formats)
+  constexpr int kSets = tc_sets<MT>();
+  constexpr int kEpiWarps = kTcDecodeWarps * kSets;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [8]
   uint64_t* empty = full + 8;                          // [8]
@@ -373,11 +389,11 @@ __global__ void __launch_bounds__(kTcThreads, MT == 32 ? 2 : 1) tc_mm_kernel(con
     }
     for (int j = 0; j < kDBufs; ++j) {
       mbar_init(smem_u32(dfull + j), 1);
-      mbar_init(smem_u32(dempty + j), kTcDecodeWarps);
+      mbar_init(smem_u32(dempty + j), kEpiWarps);
     }
     for (int j = 0; j < kTcQueue; ++j) {
       mbar_init(smem_u32(qfull + j), 1);
-      mbar_init(smem_u32(qempty + j), 1 + kTcDecodeWarps);
+      mbar_init(smem_u32(qempty + j), 1 + kEpiWarps);
     }
     mbar_init(smem_u32(fin), 1);
     *abort_flag = 0;
@@ -445,10 +461,8 @@ __global__ void __launch_bounds__(kTcThreads, MT == 32 ? 2 : 1) tc_mm_kernel(con
             mbar_expect_tx(bar, (uint32_t)(nnt * KB * 16));
             rx.next(SX);
           }
-          const int64_t boffg = (int64_t)((b * KB) >> 7) * 2048 + ((b * KB) & 127) * 16;
-          for (int i = 0; i < nnt; ++i)
-            bulk_g2s(smem_u32(xdst + i * KB * 16), p.bin + (int64_t)(nt0 + i) * p.bin_nch * 2048 + boffg,
-                     (uint32_t)(KB * 16), bar);
+          bulk_g2s(smem_u32(xdst), p.bin + ((int64_t)b * p.ntstride + nt0) * (KB * 16), (uint32_t)(nnt * KB * 16),
+                   bar);
         }
         if (!ok) break;
       }
@@ -532,7 +546,8 @@ __global__ void __launch_bounds__(kTcThreads, MT == 32 ? 2 : 1) tc_mm_kernel(con
   } else {
     // ------------------------------------------------- decode and epilogue --
     const int dw = warp - 2;
-    const int t = dw >> 2;             // tile of the unit (decode) / token half or tile (epilogue)
+    const int set = dw / kTcDecodeWarps;      // decode set: takes blocks b0 + set, b0 + set + kSets, ...
+    const int t = (dw % kTcDecodeWarps) >> 2;  // tile of the unit
     const int q = warp & 3;            // tensor-memory lane quarter this warp may access
     const int row = 32 * q + lane;     // row inside the 128-row tile
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
@@ -555,6 +570,11 @@ __global__ void __launch_bounds__(kTcThreads, MT == 32 ? 2 : 1) tc_mm_kernel(con
         // A half is decoded as two quarters (qa, qb): the store of the first
         // runs while the second is decoded.
         for (int b = b0; b < b1 && !aborted; ++b, r.next(S)) {
+          if (kSets > 1 && (b - b0) % kSets != set) {  // the other decode set's block
+#pragma unroll
+            for (int h = 0; h < Dec::kHalves; ++h) ra.next(kTcASlots);
+            continue;
+          }
           const int s = r.i;
           ok = wait_or_abort(smem_u32(full + s), r.ph, abort_flag, p.status);
           if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
@@ -603,14 +623,15 @@ __global__ void __launch_bounds__(kTcThreads, MT == 32 ? 2 : 1) tc_mm_kernel(con
       tc_fence_after();
       const uint32_t dcol = tmem + lane_base + db * kDCols;
       if (p.pair) {
-        // warp t: tokens [t MT/2, (t+1) MT/2) of unit row `row`, 16 at a time;
-        // gate tile at columns 0 .. MT-1, up tile at MT .. 2MT-1
+        // warp (set, t): tokens [sub MT/(2 kSets), (sub+1) MT/(2 kSets)), sub =
+        // 2 set + t, of unit row `row`, 16 at a time; gate tile at columns
+        // 0 .. MT-1, up tile at MT .. 2MT-1
         const int col = u * kTcRows + row;  // K index of the down projection
         const int nt0 = p.gt.nt0[gi];
-        uint8_t* dst = p.act_out + (int64_t)(col >> 7) * 2048 + tc_bact_byte(0, col & 127);
+        uint8_t* dst = p.act_out + tc_bact_off((int64_t)nt0 * kNTile, col, p.out_kb, p.ntstride);
 #pragma unroll 1
-        for (int c = 0; c < MT / 32; ++c) {
-          const int tok0 = t * (MT / 2) + 16 * c;
+        for (int c = 0; c < MT / (32 * kSets); ++c) {
+          const int tok0 = (2 * set + t) * (MT / (2 * kSets)) + 16 * c;
           if (tok0 >= ntok) break;  // warp-uniform
           uint32_t g[16], v[16];
           tc_ld16(dcol + tok0, g);
@@ -638,7 +659,7 @@ __global__ void __launch_bounds__(kTcThreads, MT == 32 ? 2 : 1) tc_mm_kernel(con
             const int tok = tok0 + n;
             if (tok < ntok) {
               const float val = silu_f(__uint_as_float(g[n])) * __uint_as_float(v[n]);
-              *reinterpret_cast<uint16_t*>(dst + (int64_t)(nt0 + (tok >> 3)) * p.out_nch * 2048 + (tok & 7) * 16) =
+              *reinterpret_cast<uint16_t*>(dst + (int64_t)(tok >> 3) * (p.out_kb * 16) + (tok & 7) * 16) =
                   f32_to_act<Dec::kBF16>(val);
             }
           }
@@ -647,13 +668,13 @@ __global__ void __launch_bounds__(kTcThreads, MT == 32 ? 2 : 1) tc_mm_kernel(con
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(dempty + db));
       } else {
-        // tile t of the unit, tokens 0 .. MT-1, 16 at a time
+        // tile t of the unit, tokens [set MT/kSets, (set+1) MT/kSets), 16 at a time
         if (t < ntl) {
           const int hrow = (2 * u + t) * kTcRows + row;
           float* y = p.y_out + (item % p.ks) * p.y_sstride + (int64_t)p.gt.slot0[gi] * p.y_ld + hrow;
 #pragma unroll 1
-          for (int c = 0; c < MT / 16; ++c) {
-            const int tok0 = 16 * c;
+          for (int c = 0; c < MT / (16 * kSets); ++c) {
+            const int tok0 = set * (MT / kSets) + 16 * c;
             if (tok0 >= ntok) break;  // warp-uniform
             uint32_t v[16];
             tc_ld16(dcol + t * MT + tok0, v);
@@ -704,7 +725,7 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
       int dev = 0, smem_sm = 0, nb = 0;
       e = cudaGetDevice(&dev);
       if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-      if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kTcThreads, smem);
+      if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, tc_threads<MT>(), smem);
       if (e != cudaSuccess) return e;
       cached_per_sm = MT == 32 && (nb >= 2 || 2 * (smem + 1024) <= smem_sm) ? 2 : 1;
       e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -713,7 +734,7 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
     }
     per_sm = cached_per_sm;
   }
-  kern<<<num_sms * per_sm, kTcThreads, smem, stream>>>(p);
+  kern<<<num_sms * per_sm, tc_threads<MT>(), smem, stream>>>(p);
   return cudaGetLastError();
 }
 
