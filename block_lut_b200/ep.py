@@ -134,15 +134,32 @@ def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, 
         eps.append(EPMoELayer(ex, E, TOPK, rw, shared=(s13, s2)))
     xs = make_inputs(a.layers, a.batch, rank, dev)
 
+    outs = [None] * len(eps)
+
     def step():
-        for m, x in zip(eps, xs):
-            m.forward(x)
+        for i, (m, x) in enumerate(zip(eps, xs)):
+            outs[i] = m.forward(x)
 
     for _ in range(max(2, a.warmup)):
         step()
     torch.cuda.synchronize()
     for m in eps:
         m.local.check_status()
+    # the whole step (routing, exchanges, expert kernels) as one CUDA graph;
+    # every rank captures the same collectives in the same order
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(1, a.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
     dist.barrier()
     clk = Clocks(torch.cuda.current_device())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -150,16 +167,44 @@ def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, 
     dist.barrier()
     e0.record()
     for _ in range(a.steps):
-        step()
+        graph.replay()
     e1.record()
     torch.cuda.synchronize()
     dist.barrier()
+    del graph  # a graph holding NCCL work is released before the process group
     clocks = clk.stop()
     ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
     total_tokens = a.batch * world
     peak, _ = peaks()
+    # e2e through EPMoELayer.forward: each rank's tokens from pinned host
+    # memory to the device and its layer outputs back, every step
+    xh = [x.cpu().pin_memory() for x in xs]
+    oh = [torch.empty_like(x, device="cpu").pin_memory() for x in xs]
+    xd = [torch.empty_like(x) for x in xs]
+
+    def e2e_step():
+        for m, h_in, d_in, h_out in zip(eps, xh, xd, oh):
+            d_in.copy_(h_in, non_blocking=True)
+            h_out.copy_(m.forward(d_in), non_blocking=True)
+    e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(a.steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    e_ms = torch.tensor([f0.elapsed_time(f1) / a.steps], device=dev)
+    dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e_ms = float(e_ms.item())
+    # this library's kernels per step: router (logits + top-k), local experts
+    # on all ranks' tokens, shared expert on the rank's own tokens
+    m0 = eps[0]
+    per_layer = 2 + m0.local.launch_count(world * a.batch, caller_routing=True) + (
+        m0.shared.launch_count(a.batch, caller_routing=True) if m0.shared is not None else 0)
     if rank == 0:
         res = {"metric": metric, "value": total_tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
                "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -169,8 +214,13 @@ def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, 
                           "layers": a.layers, "global_batch": total_tokens, "experts": E, "top_k": TOPK,
                           "format": f"BlockLUT {a.bits}-bit g{a.group}", "parallelism": f"ep{world}",
                           "exchange": "NCCL all_to_all_single dispatch (x, ids, w) + combine (fp32 partials)"},
-               "roofline": None, "cpu_baseline": None, "e2e": None,
-               "gpu_launches": None, "clocks": clocks}
+               "graph": "CUDA graph of the 24-layer step, NCCL collectives included",
+               "roofline": None, "cpu_baseline": None,
+               "e2e": {"value": total_tokens / (e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e_ms,
+                       "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs) * world,
+                       "d2h_bytes_per_step": sum(x.numel() * 2 for x in xs) * world,
+                       "path": "EPMoELayer.forward per layer with pinned host I/O on every rank"},
+               "gpu_launches": a.steps * a.layers * per_layer, "clocks": clocks}
         print(json.dumps(res), flush=True)
     dist.barrier()
     dist.destroy_process_group()
