@@ -35,6 +35,7 @@ sys.path.insert(0, ROOT)
 
 H, E, I, TOPK, IS, LAYERS = 2048, 60, 1408, 4, 5632, 24
 QWEN = dict(H=H, E=E, I=I, IS=IS)
+TRAFFIC_RATIO = 1.028  # measured DRAM bytes / algorithmic bytes of the routed tcgen05 launches
 METRIC = "LUT-MoE decode tokens/s; expert LUT-GEMV HBM GB/s vs ~8 TB/s peak"
 # DeepSeek-V2-Lite MoE layers (26 of 27; layer 0 is dense),
 # 64 routed experts of I 1408, top-6 softmax, two shared experts (one MLP of
@@ -323,9 +324,13 @@ def run_ours(a):
                                "; routed gate/up+SiLU*up and down, per layer)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                     else "fallback 6650 GB/s", "traffic": None,
+                     else "fallback 6650 GB/s",
+                     # DRAM read + write per layer: the algorithmic bytes times the ratio the ncu
+                     # capture in profiles/tc_mm_kernel_qwen15_decode_b32.md measured for the
+                     # routed gate/up + down launches (1.028)
+                     "traffic": (b_gu + b_dn) * TRAFFIC_RATIO if moes[0].experts.tc else None,
                      "bytes_per_layer": b_gu + b_dn, "ms_gateup": t_gu, "ms_down": t_dn,
-                     "active_experts": na},
+                     "active_experts": na, "active_experts_per_layer": n_active[:4]},
         "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": a.steps * a.layers * per_layer_launches,
         "clocks": clocks,
