@@ -34,11 +34,18 @@
 namespace blut {
 
 constexpr int kTcDecodeWarps = 8;  // one decode set: 2 tiles x 4 tensor-memory lane quarters
-// Decode sets per CTA: one at two CTAs per SM (MT = 32); two at one CTA per
-// SM (MT = 128), taking alternate column blocks of an item.
+// Decode sets per CTA, taking turns over the column blocks of an item.
+// Decode (MT = 32) runs two CTAs per SM with one set each (one producer and
+// one MMA thread per 8 decode warps); measured faster than one CTA with three
+// sets.  Prefill (MT = 128) runs one CTA per SM with two sets.
+constexpr int kTcNarrowSets = 1;
 template <int MT>
 constexpr int tc_sets() {
-  return MT == 32 ? 1 : 2;
+  return MT == 32 ? kTcNarrowSets : 2;
+}
+template <int MT>
+constexpr int tc_ctas_per_sm() {
+  return MT == 32 && kTcNarrowSets == 1 ? 2 : 1;
 }
 template <int MT>
 constexpr int tc_threads() {
@@ -54,10 +61,13 @@ constexpr int kTcQueue = 4;          // depth of the shared-memory item queue
 // buffer and a ring of three A slots of 64 columns (2 tiles x 64 fp16
 // columns of K) after it; dense weights need no A slots and double-buffer
 // the accumulators so the MMA runs one item ahead of the epilogue.
-constexpr int kTcASlots = 3;
+template <int MT>
+constexpr int tc_aslots() {  // A slots: two per decode set at one CTA per SM (at most 6)
+  return tc_ctas_per_sm<MT>() == 2 ? 3 : (2 * tc_sets<MT>() > 6 ? 6 : 2 * tc_sets<MT>());
+}
 template <int MT>
 constexpr int tc_cols(bool dense) {
-  return dense ? 4 * MT : (MT == 32 ? 256 : 512);
+  return tc_ctas_per_sm<MT>() == 2 ? (dense ? 4 * MT : 256) : 512;
 }
 
 // Multipliers {1 << 31, 1 << 16} handed to the decode (see tc_lut16x8).
@@ -154,8 +164,7 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&v)[32])
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
       "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
       "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-      : "memory");
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]));
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -165,8 +174,7 @@ __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16])
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
       "%15, %16};" ::"r"(taddr),
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]));
 }
 // Waits for this thread's tcgen05.st; `v` (the registers of the store in
 // flight) is tied to the wait so the compiler keeps them unchanged until then.
@@ -240,18 +248,29 @@ struct TcDecB4 {
   static constexpr int KB = G > 64 ? G : 64;  // columns per block
   static constexpr int kHalves = KB / 64;     // 64-column halves per block
   static constexpr int kNumPlanes = 2;
-  // Decodes quarter qq (32 columns) of half h of row `row` of one tile: cp /
-  // tp are the tile's code and table pieces inside the stage.
-  __device__ __forceinline__ static void decode_q(const uint8_t* cp, const uint8_t* tp, int row, int h, int qq,
-                                                  uint32_t (&out)[16], const TcMul& m) {
-    const uint4 c = tc_lds128(cp + ((2 * h + qq) * kTcRows + row) * 16);
-    const int tb = G == 32 ? 2 * h + qq : (G == 64 ? h : 0);  // table of these columns
-    const uint4 th = tc_lds128(tp + ((2 * tb) * kTcRows + row) * 16);
-    const uint4 tl = tc_lds128(tp + ((2 * tb + 1) * kTcRows + row) * 16);
-    tc_lut16x8(c.x, th, tl, out + 0, m);
-    tc_lut16x8(c.y, th, tl, out + 4, m);
-    tc_lut16x8(c.z, th, tl, out + 8, m);
-    tc_lut16x8(c.w, th, tl, out + 12, m);
+  // Shared-memory data of half h (64 columns) of row `row` of one tile: cp /
+  // tp are the tile's code and table pieces inside the stage.  Both
+  // quarters' codes and tables are loaded before any lookup.
+  struct Half {
+    uint4 c[2], th[2], tl[2];
+  };
+  __device__ __forceinline__ static void load_half(const uint8_t* cp, const uint8_t* tp, int row, int h, Half& d) {
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq) d.c[qq] = tc_lds128(cp + ((2 * h + qq) * kTcRows + row) * 16);
+#pragma unroll
+    for (int qq = 0; qq < (G == 32 ? 2 : 1); ++qq) {
+      const int tb = G == 32 ? 2 * h + qq : (G == 64 ? h : 0);  // table of these columns
+      d.th[qq] = tc_lds128(tp + ((2 * tb) * kTcRows + row) * 16);
+      d.tl[qq] = tc_lds128(tp + ((2 * tb + 1) * kTcRows + row) * 16);
+    }
+  }
+  // Looks up quarter qq (32 columns) of a loaded half.
+  __device__ __forceinline__ static void lookup_q(const Half& d, int qq, uint32_t (&out)[16], const TcMul& m) {
+    const int tq = G == 32 ? qq : 0;
+    tc_lut16x8(d.c[qq].x, d.th[tq], d.tl[tq], out + 0, m);
+    tc_lut16x8(d.c[qq].y, d.th[tq], d.tl[tq], out + 4, m);
+    tc_lut16x8(d.c[qq].z, d.th[tq], d.tl[tq], out + 8, m);
+    tc_lut16x8(d.c[qq].w, d.th[tq], d.tl[tq], out + 12, m);
   }
   // Decodes half h (64 columns) of row `row` of one tile.
   __device__ __forceinline__ static void decode(const uint8_t* cp, const uint8_t* tp, int row, int h,
@@ -297,8 +316,9 @@ struct TcDecDense {
   static constexpr int kNumPlanes = 1;
   __device__ __forceinline__ static void decode(const uint8_t*, const uint8_t*, int, int, uint32_t (&)[32],
                                                 const TcMul&) {}
-  __device__ __forceinline__ static void decode_q(const uint8_t*, const uint8_t*, int, int, int, uint32_t (&)[16],
-                                                  const TcMul&) {}
+  struct Half {};
+  __device__ __forceinline__ static void load_half(const uint8_t*, const uint8_t*, int, int, Half&) {}
+  __device__ __forceinline__ static void lookup_q(const Half&, int, uint32_t (&)[16], const TcMul&) {}
 };
 
 // Position in a ring of n barrier-guarded slots: slot index, the parity of
@@ -340,7 +360,7 @@ __host__ inline int tc_smem_bytes(const TcParams& p) {
 }
 
 template <class Dec, int MT>
-__global__ void __launch_bounds__(tc_threads<MT>(), MT == 32 ? 2 : 1) tc_mm_kernel(const TcParams p) {
+__global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_kernel(const TcParams p) {
   constexpr bool kDense = Dec::kDense;
   constexpr int KB = Dec::KB;
   constexpr uint32_t kCols = tc_cols<MT>(kDense);  // tensor-memory columns of this CTA
@@ -348,22 +368,23 @@ __global__ void __launch_bounds__(tc_threads<MT>(), MT == 32 ? 2 : 1) tc_mm_kern
   constexpr int kDCols = 2 * MT;                   // columns of one accumulator buffer
   constexpr int kACol0 = kDCols;                   // first A slot (LUT formats)
   constexpr int kSets = tc_sets<MT>();
+  constexpr int kTcASlots = tc_aslots<MT>();
   constexpr int kEpiWarps = kTcDecodeWarps * kSets;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [8]
   uint64_t* empty = full + 8;                          // [8]
-  uint64_t* afull = full + 16;                         // [kTcASlots] A slot written (decode warps)
-  uint64_t* aempty = full + 20;                        // [kTcASlots] A slot read (MMA commit)
-  uint64_t* dfull = full + 24;                         // [kDBufs] accumulators complete (MMA commit)
-  uint64_t* dempty = full + 26;                        // [kDBufs] accumulators read (epilogue warps)
-  uint64_t* qfull = full + 28;                         // [kTcQueue] item posted
-  uint64_t* qempty = full + 32;                        // [kTcQueue] item taken by every role
-  uint64_t* fin = full + 36;                           // last MMAs complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 37);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 38);
-  volatile int* qitem = reinterpret_cast<volatile int*>(full + 39);  // [kTcQueue]
-  uint64_t* xfull = full + 41;                         // [4] activation stage loaded (LUT formats)
-  uint64_t* xempty = full + 45;                        // [4] activation stage read (MMA commit)
+  uint64_t* afull = full + 16;                         // [kTcASlots <= 8] A slot written (decode warps)
+  uint64_t* aempty = full + 24;                        // [kTcASlots] A slot read (MMA commit)
+  uint64_t* dfull = full + 32;                         // [kDBufs] accumulators complete (MMA commit)
+  uint64_t* dempty = full + 34;                        // [kDBufs] accumulators read (epilogue warps)
+  uint64_t* qfull = full + 36;                         // [kTcQueue] item posted
+  uint64_t* qempty = full + 40;                        // [kTcQueue] item taken by every role
+  uint64_t* fin = full + 44;                           // last MMAs complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 45);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 46);
+  volatile int* qitem = reinterpret_cast<volatile int*>(full + 47);  // [kTcQueue]
+  uint64_t* xfull = full + 49;                         // [4] activation stage loaded (LUT formats)
+  uint64_t* xempty = full + 53;                        // [4] activation stage read (MMA commit)
   uint8_t* ring = smem + 512;
   const int S = p.stages, SX = p.xstages;
   const int stage_bytes = tc_stage_bytes<Dec, MT>(p);
@@ -598,9 +619,11 @@ __global__ void __launch_bounds__(tc_threads<MT>(), MT == 32 ? 2 : 1) tc_mm_kern
             const uint32_t aslot = tmem + lane_base + kACol0 + j * 64 + t * 32;
             if (active) {
               uint32_t qa[16], qb[16];
-              Dec::decode_q(cp, tp, row, h, 0, qa, p.mul);
+              typename Dec::Half hd;
+              Dec::load_half(cp, tp, row, h, hd);
+              Dec::lookup_q(hd, 0, qa, p.mul);
               tc_st16(aslot, qa);
-              Dec::decode_q(cp, tp, row, h, 1, qb, p.mul);
+              Dec::lookup_q(hd, 1, qb, p.mul);
               tc_st16(aslot + 16, qb);
               tc_wait_st_keep(qa);
               tc_wait_st_keep(qb);
@@ -623,15 +646,15 @@ __global__ void __launch_bounds__(tc_threads<MT>(), MT == 32 ? 2 : 1) tc_mm_kern
       tc_fence_after();
       const uint32_t dcol = tmem + lane_base + db * kDCols;
       if (p.pair) {
-        // warp (set, t): tokens [sub MT/(2 kSets), (sub+1) MT/(2 kSets)), sub =
-        // 2 set + t, of unit row `row`, 16 at a time; gate tile at columns
+        // chunks of 16 tokens of unit row `row`, chunk c to the warp pair
+        // (set, t) with c % (2 kSets) == 2 set + t; gate tile at columns
         // 0 .. MT-1, up tile at MT .. 2MT-1
         const int col = u * kTcRows + row;  // K index of the down projection
         const int nt0 = p.gt.nt0[gi];
         uint8_t* dst = p.act_out + tc_bact_off((int64_t)nt0 * kNTile, col, p.out_kb, p.ntstride);
 #pragma unroll 1
-        for (int c = 0; c < MT / (32 * kSets); ++c) {
-          const int tok0 = (2 * set + t) * (MT / (2 * kSets)) + 16 * c;
+        for (int c = 2 * set + t; c < MT / 16; c += 2 * kSets) {
+          const int tok0 = 16 * c;
           if (tok0 >= ntok) break;  // warp-uniform
           uint32_t g[16], v[16];
           tc_ld16(dcol + tok0, g);
@@ -668,13 +691,13 @@ __global__ void __launch_bounds__(tc_threads<MT>(), MT == 32 ? 2 : 1) tc_mm_kern
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(dempty + db));
       } else {
-        // tile t of the unit, tokens [set MT/kSets, (set+1) MT/kSets), 16 at a time
+        // tile t of the unit, chunks of 16 tokens c with c % kSets == set
         if (t < ntl) {
           const int hrow = (2 * u + t) * kTcRows + row;
           float* y = p.y_out + (item % p.ks) * p.y_sstride + (int64_t)p.gt.slot0[gi] * p.y_ld + hrow;
 #pragma unroll 1
-          for (int c = 0; c < MT / (16 * kSets); ++c) {
-            const int tok0 = set * (MT / kSets) + 16 * c;
+          for (int c = set; c < MT / 16; c += kSets) {
+            const int tok0 = 16 * c;
             if (tok0 >= ntok) break;  // warp-uniform
             uint32_t v[16];
             tc_ld16(dcol + t * MT + tok0, v);
@@ -703,7 +726,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), MT == 32 ? 2 : 1) tc_mm_kern
 // CTA per resident slot.
 template <class Dec, int MT>
 inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
-  const int budget = MT == 32 ? kTcRingBudget : kTcRingBudgetWide;
+  const int budget = tc_ctas_per_sm<MT>() == 2 ? kTcRingBudget : kTcRingBudgetWide;
   const int stage = tc_stage_bytes<Dec, MT>(p);
   const int xstage = tc_xstage_bytes<Dec, MT>();
   p.xstages = xstage ? std::max(2, std::min(4, (budget / 6) / xstage)) : 0;
@@ -727,7 +750,7 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
       if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
       if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, tc_threads<MT>(), smem);
       if (e != cudaSuccess) return e;
-      cached_per_sm = MT == 32 && (nb >= 2 || 2 * (smem + 1024) <= smem_sm) ? 2 : 1;
+      cached_per_sm = tc_ctas_per_sm<MT>() == 2 && (nb >= 2 || 2 * (smem + 1024) <= smem_sm) ? 2 : 1;
       e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
       if (e != cudaSuccess) return e;
       cached_smem = smem;
