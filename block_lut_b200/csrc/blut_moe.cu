@@ -337,7 +337,21 @@ __global__ void __launch_bounds__(256) splitk_silu_kernel(const float* __restric
   if (row >= kTcRows || n >= ntok) return;
   const float* src = part + (int64_t)ku * ks * (2 * kTcRows * 32) + idx;
   float g = 0.f, v = 0.f;
-  for (int s = 0; s < ks; ++s) {
+  int s = 0;
+  for (; s + 3 < ks; s += 4) {  // four slices' loads in flight, added in slice order
+    float gs[4], vs[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      gs[i] = src[(int64_t)(s + i) * (2 * kTcRows * 32)];
+      vs[i] = src[(int64_t)(s + i) * (2 * kTcRows * 32) + kTcRows * 32];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      g += gs[i];
+      v += vs[i];
+    }
+  }
+  for (; s < ks; ++s) {
     g += src[(int64_t)s * (2 * kTcRows * 32)];
     v += src[(int64_t)s * (2 * kTcRows * 32) + kTcRows * 32];
   }
@@ -350,17 +364,26 @@ __global__ void __launch_bounds__(256) splitk_silu_kernel(const float* __restric
 // out[t] = sum_j w[t,j] * y[slot(t,j)] (+ g_t * y_shared[t]), fp32, one rounding.
 // Expert outputs computed in K slices are summed slice by slice first (in
 // slice order, so the result does not depend on which slice finished first).
+// Four slices' loads are in flight at a time; the additions stay in order.
+__device__ __forceinline__ void add4(float4& v, const float4& w) {
+  v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+}
 __device__ __forceinline__ float4 sum_slices(const float* p, int ks, int64_t stride) {
   float4 v = *reinterpret_cast<const float4*>(p);
-  for (int s = 1; s < ks; ++s) {
-    const float4 w = *reinterpret_cast<const float4*>(p + s * stride);
-    v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+  int s = 1;
+  for (; s + 3 < ks; s += 4) {
+    float4 w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = *reinterpret_cast<const float4*>(p + (s + i) * stride);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) add4(v, w[i]);
   }
+  for (; s < ks; ++s) add4(v, *reinterpret_cast<const float4*>(p + s * stride));
   return v;
 }
 
 template <bool BF16>
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, const float* __restrict__ ys,
+__global__ void __launch_bounds__(64) combine_kernel(const float* __restrict__ y, const float* __restrict__ ys,
                                                       const float* __restrict__ tw, const int* __restrict__ tk_slot,
                                                       const float* __restrict__ sg, int top_k, int hidden,
                                                       int shared_mode, void* __restrict__ out_v, int out_f32,
@@ -781,13 +804,13 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
 
   // 6. combine
   const int smode = sh ? a.shared_gate_mode : -1;
-  const dim3 cgrid(T, (H + 1023) / 1024);
+  const dim3 cgrid(T, (H + 255) / 256);  // 64 threads x 4 columns per CTA
   if (bf16)
-    combine_kernel<true><<<cgrid, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
+    combine_kernel<true><<<cgrid, 64, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
                                                     a.out_f32, ws.split.ks[1], ws.y_sstride, ws.split.ks[3],
                                                     ws.ys_sstride);
   else
-    combine_kernel<false><<<cgrid, 256, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
+    combine_kernel<false><<<cgrid, 64, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
                                                      a.out_f32, ws.split.ks[1], ws.y_sstride, ws.split.ks[3],
                                                      ws.ys_sstride);
   return stage_done("combine", stream);
