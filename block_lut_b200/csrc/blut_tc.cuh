@@ -39,13 +39,14 @@ constexpr int kTcDecodeWarps = 8;  // one decode set: 2 tiles x 4 tensor-memory 
 // one MMA thread per 8 decode warps); measured faster than one CTA with three
 // sets.  Prefill (MT = 128) runs one CTA per SM with two sets.
 constexpr int kTcNarrowSets = 1;
+constexpr int kTcNarrowCtas = 2;  // CTAs per SM in decode (2 measured faster than 3 with one A slot each)
 template <int MT>
 constexpr int tc_sets() {
   return MT == 32 ? kTcNarrowSets : 2;
 }
 template <int MT>
 constexpr int tc_ctas_per_sm() {
-  return MT == 32 && kTcNarrowSets == 1 ? 2 : 1;
+  return MT == 32 && kTcNarrowSets == 1 ? kTcNarrowCtas : 1;
 }
 template <int MT>
 constexpr int tc_threads() {
@@ -63,11 +64,12 @@ constexpr int kTcQueue = 4;          // depth of the shared-memory item queue
 // the accumulators so the MMA runs one item ahead of the epilogue.
 template <int MT>
 constexpr int tc_aslots() {  // A slots: two per decode set at one CTA per SM (at most 6)
-  return tc_ctas_per_sm<MT>() == 2 ? 3 : (2 * tc_sets<MT>() > 6 ? 6 : 2 * tc_sets<MT>());
+  return tc_ctas_per_sm<MT>() == 3 ? 1
+         : tc_ctas_per_sm<MT>() == 2 ? 3 : (2 * tc_sets<MT>() > 6 ? 6 : 2 * tc_sets<MT>());
 }
 template <int MT>
 constexpr int tc_cols(bool dense) {
-  return tc_ctas_per_sm<MT>() == 2 ? (dense ? 4 * MT : 256) : 512;
+  return tc_ctas_per_sm<MT>() == 3 ? 128 : tc_ctas_per_sm<MT>() == 2 ? (dense ? 4 * MT : 256) : 512;
 }
 
 // Multipliers {1 << 31, 1 << 16} handed to the decode (see tc_lut16x8).
@@ -608,6 +610,12 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
 #pragma unroll
           for (int h = 0; h < Dec::kHalves; ++h, ra.next(kTcASlots)) {
             const int j = ra.i;
+            uint32_t qa[16], qb[16];
+            typename Dec::Half hd;
+            if (active) {  // the first quarter's lookups run before the slot is known free
+              Dec::load_half(cp, tp, row, h, hd);
+              Dec::lookup_q(hd, 0, qa, p.mul);
+            }
             if (ra.wrapped) {
               ok = wait_or_abort(smem_u32(aempty + j), ra.ph ^ 1u, abort_flag, p.status);
               if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
@@ -618,15 +626,18 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
             tc_fence_after();
             const uint32_t aslot = tmem + lane_base + kACol0 + j * 64 + t * 32;
             if (active) {
-              uint32_t qa[16], qb[16];
-              typename Dec::Half hd;
-              Dec::load_half(cp, tp, row, h, hd);
-              Dec::lookup_q(hd, 0, qa, p.mul);
               tc_st16(aslot, qa);
-              Dec::lookup_q(hd, 1, qb, p.mul);
-              tc_st16(aslot + 16, qb);
-              tc_wait_st_keep(qa);
-              tc_wait_st_keep(qb);
+              if constexpr (tc_ctas_per_sm<MT>() >= 3) {  // register-lean: one quarter buffer
+                tc_wait_st_keep(qa);
+                Dec::lookup_q(hd, 1, qa, p.mul);
+                tc_st16(aslot + 16, qa);
+                tc_wait_st_keep(qa);
+              } else {  // the first quarter's store overlaps the second's lookups
+                Dec::lookup_q(hd, 1, qb, p.mul);
+                tc_st16(aslot + 16, qb);
+                tc_wait_st_keep(qa);
+                tc_wait_st_keep(qb);
+              }
             }
             if (h == Dec::kHalves - 1) {  // this stage's shared memory is no longer read
               __syncwarp();
@@ -726,7 +737,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
 // CTA per resident slot.
 template <class Dec, int MT>
 inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
-  const int budget = tc_ctas_per_sm<MT>() == 2 ? kTcRingBudget : kTcRingBudgetWide;
+  const int budget = tc_ctas_per_sm<MT>() == 3 ? 72 * 1024 : tc_ctas_per_sm<MT>() == 2 ? kTcRingBudget : kTcRingBudgetWide;
   const int stage = tc_stage_bytes<Dec, MT>(p);
   const int xstage = tc_xstage_bytes<Dec, MT>();
   p.xstages = xstage ? std::max(2, std::min(4, (budget / 6) / xstage)) : 0;
@@ -750,7 +761,8 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
       if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
       if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, tc_threads<MT>(), smem);
       if (e != cudaSuccess) return e;
-      cached_per_sm = tc_ctas_per_sm<MT>() == 2 && (nb >= 2 || 2 * (smem + 1024) <= smem_sm) ? 2 : 1;
+      const int want = tc_ctas_per_sm<MT>();
+      cached_per_sm = want > 1 && (nb >= want || want * (smem + 1024) <= smem_sm) ? want : 1;
       e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
       if (e != cudaSuccess) return e;
       cached_smem = smem;
