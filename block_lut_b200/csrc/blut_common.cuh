@@ -39,7 +39,8 @@ enum PlaneKind : int {
   kPlaneCodes8 = 4,   // 8-bit codes (FMT_R8): 2048 B
   kPlaneTables = 5,   // per (row, block) tables as hi/lo byte planes
   kPlaneScales = 6,   // FMT_R8 absmax per (row, chunk): 32 B
-  kPlaneDense = 7     // fp16/bf16 weights: 4096 B
+  kPlaneDense = 7,    // fp16/bf16 weights: 4096 B
+  kPlaneCombined = 8  // NESTED (TC layout): 16-entry tables fp16(coarse[c] + refine[c][r])
 };
 
 struct TiledLayout {
@@ -69,8 +70,21 @@ __host__ __device__ inline int64_t align256(int64_t x) { return (x + 255) & ~int
 // layout of tcgen05.mma (8-row x 16-byte core matrices).  Per plane and row,
 // the block's bytes are:
 //   codes4  the row's canonical 4-bit code bytes of the block (LSB first)
+//   codes2  32-bit words of 16 two-bit codes: bits 2i..2i+1 of byte j of
+//           word w hold weight 16w + 4i + j (so that masking the word with
+//           0x03030303 after a shift by 2i yields four consecutive codes)
+//   codes1  32-bit words of 32 one-bit codes (bit 2 of a 3-bit code): bit
+//           4n + s of word w holds weight 32w + 16(s >> 1) + 8(n & 1) +
+//           (n >> 1) + 4(s & 1), the nibble order that codes2 words take
+//           when masked with 0x33333333
 //   tables  per table of the block: 2^b high bytes, then 2^b low bytes
+//   combined (NESTED) per table: 16 high bytes, then 16 low bytes of
+//           fp16(f32(coarse[c]) + f32(refine[c][r])) at entry 4c + r
 //   dense   the row's fp16 / bf16 values of the block
+// B 4-bit: codes4 + tables.  B 3-bit: codes2 (low bits) + codes1 + tables.
+// B 2-bit: codes2 + tables.  NESTED: coarse codes2 + coarse tables +
+// residual codes2 + combined tables (the full tier reads planes 0, 2, 3,
+// the coarse tier planes 0, 1).
 // ------------------------------------------------------------------------
 constexpr int kTcRows = 128;
 
@@ -101,12 +115,30 @@ __host__ inline bool make_tc_layout(const blut_mat_desc& d, TiledLayout& L) {
     L.entries[L.nplanes] = entries;
     L.nplanes++;
   };
+  const bool g_ok = d.group == 32 || d.group == 64 || d.group == 128;
   switch (d.format) {
     case BLUT_FMT_B:
-      if (d.bits != 4 || d.dtype != BLUT_F16) return false;
-      if (d.group != 32 && d.group != 64 && d.group != 128) return false;
-      add(kPlaneCodes4, L.kb / 2, 0);
-      add(kPlaneTables, (L.kb / d.group) * 32, 16);
+      if (d.dtype != BLUT_F16 || !g_ok) return false;
+      if (d.bits == 4) {
+        add(kPlaneCodes4, L.kb / 2, 0);
+        add(kPlaneTables, (L.kb / d.group) * 32, 16);
+      } else if (d.bits == 3) {
+        add(kPlaneCodes2, L.kb / 4, 0);
+        add(kPlaneCodes1, L.kb / 8, 0);
+        add(kPlaneTables, (L.kb / d.group) * 16, 8);
+      } else if (d.bits == 2) {
+        add(kPlaneCodes2, L.kb / 4, 0);
+        add(kPlaneTables, (L.kb / d.group) * 8, 4);
+      } else {
+        return false;
+      }
+      break;
+    case BLUT_FMT_NESTED:
+      if (d.dtype != BLUT_F16 || !g_ok) return false;
+      add(kPlaneCodes2, L.kb / 4, 0);                  // coarse codes
+      add(kPlaneTables, (L.kb / d.group) * 8, 4);      // coarse tables
+      add(kPlaneCodes2, L.kb / 4, 0);                  // residual codes
+      add(kPlaneCombined, (L.kb / d.group) * 32, 16);  // combined tables
       break;
     case BLUT_FMT_DENSE:
       if (d.dtype != BLUT_F16 && d.dtype != BLUT_BF16) return false;
@@ -187,6 +219,22 @@ __host__ inline bool make_layout(const blut_mat_desc& d, TiledLayout& L) {
   }
   L.total = off;
   return true;
+}
+
+// Planes a matmul of `d` reads, in the order its decode takes them: every
+// plane, except NESTED, whose full tier reads the coarse codes, residual
+// codes and combined tables (planes 0, 2, 3) and whose coarse tier reads the
+// coarse codes and tables (planes 0, 1).  Returns their number.
+__host__ inline int plane_select(const blut_mat_desc& d, const TiledLayout& L, int (&idx)[3]) {
+  idx[0] = 0; idx[1] = 1; idx[2] = 2;
+  if (d.format == BLUT_FMT_NESTED) {
+    if (d.tier == 0) {
+      idx[1] = 2; idx[2] = 3;
+      return 3;
+    }
+    return 2;
+  }
+  return L.nplanes < 3 ? L.nplanes : 3;
 }
 
 // Pieces are stored chunk-major inside each plane: piece (chunk c, physical

@@ -599,15 +599,8 @@ int validate_moe(const blut_moe_args& a) {
 bool mm_planes(const blut_mat_desc& d, bool pair, MMParams& p) {
   TiledLayout L;
   if (!make_layout(d, L)) return false;
-  int idx[3] = {0, 1, 2};
-  int np = L.nplanes;
-  if (d.format == BLUT_FMT_NESTED) {
-    if (d.tier == 0) {
-      idx[0] = 0; idx[1] = 2; idx[2] = 3; np = 3;
-    } else {
-      np = 2;
-    }
-  }
+  int idx[3];
+  const int np = plane_select(d, L, idx);
   int tb = 0;
   for (int q = 0; q < 3; ++q) {
     p.plane_off[q] = q < np ? L.off[idx[q]] : 0;

@@ -234,6 +234,16 @@ __global__ void pack_tables_kernel(PackArgs a) {
   }
 }
 
+// Code of element k of row r in a canonical b-bit stream (element k at bits
+// k*b .. k*b+b-1 of the row's little-endian bit stream).
+__device__ __forceinline__ uint32_t canon_code(const uint8_t* codes, int64_t cols, int b, int64_t r, int64_t k) {
+  const int64_t bit = k * b;
+  const uint8_t* q = codes + r * (cols * b / 8) + (bit >> 3);
+  uint32_t v = q[0];
+  if ((bit & 7) + b > 8) v |= uint32_t(q[1]) << 8;
+  return (v >> (bit & 7)) & ((1u << b) - 1u);
+}
+
 // TC layout: one thread per byte of plane `plane` (block-major, then physical
 // tile, then the unit-major piece), fetching that byte from the canonical
 // arrays.
@@ -257,6 +267,35 @@ __global__ void pack_tc_kernel(PackArgs a, int plane) {
       case kPlaneCodes4:
         v = a.codes[r * (a.cols / 2) + blk * (L.kb / 2) + o];
         break;
+      case kPlaneCodes2: {  // byte j of word w: weights 16w + 4i + j at bits 2i
+        const bool resid = a.format == BLUT_FMT_NESTED && plane == 2;
+        const uint8_t* src = resid ? a.codes2 : a.codes;
+        const int b = a.format == BLUT_FMT_NESTED ? 2 : a.bits;
+        const int64_t k0 = blk * L.kb + (o >> 2) * 16 + (o & 3);
+        uint32_t acc = 0;
+        for (int i = 0; i < 4; ++i) acc |= (canon_code(src, a.cols, b, r, k0 + 4 * i) & 3u) << (2 * i);
+        v = uint8_t(acc);
+        break;
+      }
+      case kPlaneCodes1: {  // bit 4n + s of word w: bit 2 of weight 32w + 16(s>>1) + 8(n&1) + (n>>1) + 4(s&1)
+        uint32_t acc = 0;
+        for (int bb = 0; bb < 8; ++bb) {
+          const int pos = 8 * (o & 3) + bb, n = pos >> 2, sb = pos & 3;
+          const int64_t k = blk * L.kb + (o >> 2) * 32 + 16 * (sb >> 1) + 8 * (n & 1) + (n >> 1) + 4 * (sb & 1);
+          acc |= ((canon_code(a.codes, a.cols, 3, r, k) >> 2) & 1u) << bb;
+        }
+        v = uint8_t(acc);
+        break;
+      }
+      case kPlaneCombined: {  // entry e = 4c + r: fp16(coarse[c] + refine[c][r])
+        const int m = o / 32, wb = o % 32, e = wb % 16;
+        const int64_t tb = r * (a.cols / a.group) + blk * (L.kb / a.group) + m;
+        const float cv = __half2float(__ushort_as_half(a.tables[tb * 4 + (e >> 2)]));
+        const float rv = __half2float(__ushort_as_half(a.tables2[tb * 16 + e]));
+        const uint16_t x = __half_as_ushort(__float2half_rn(__fadd_rn(cv, rv)));
+        v = wb < 16 ? uint8_t(x >> 8) : uint8_t(x & 0xFF);
+        break;
+      }
       case kPlaneTables: {
         const int ent = L.entries[plane];
         const int m = o / (2 * ent), wb = o % (2 * ent);

@@ -72,16 +72,24 @@ constexpr int tc_cols(bool dense) {
   return tc_ctas_per_sm<MT>() == 3 ? 128 : tc_ctas_per_sm<MT>() == 2 ? (dense ? 4 * MT : 256) : 512;
 }
 
-// Multipliers {1 << 31, 1 << 16} handed to the decode (see tc_lut16x8).
+// Multipliers handed to the decode (see tc_mulhi): shifts and selector
+// arithmetic run as integer multiplies on the FMA pipe, and values the
+// compiler cannot see keep it from folding them back into shifts on the
+// integer ALU, the pipe the byte permutes already load.
 struct TcMul {
-  uint32_t k31, k16;
+  uint32_t k31, k30, k28, k26, k16;  // mul.hi by 2^n: right shift by 32 - n
+  uint32_t k4, k2;                   // mul.lo by 4, 2: left shift by 2, 1
+  uint32_t k11, k11h;                // 0x11, 0x110000: selector nibble doubling (tc_lut4x4)
 };
+__host__ inline TcMul tc_mul_consts() {
+  return TcMul{1u << 31, 1u << 30, 1u << 28, 1u << 26, 1u << 16, 4u, 2u, 0x11u, 0x110000u};
+}
 
 struct TcParams {
   const uint8_t* w;        // tiled (BLUT_LAYOUT_TC) matrices of all experts
   int64_t wstride;         // bytes between experts
-  int64_t plane_off[2];    // plane offsets inside one matrix
-  int piece[2];            // bytes of one (tile, block) piece per plane
+  int64_t plane_off[3];    // offsets inside one matrix of the planes the decode reads
+  int piece[3];            // bytes of one (tile, block) piece per plane
   int nplanes;
   int tile_bytes;          // sum of piece[]
   int ntiles;              // 128-row tiles of the matrix
@@ -103,7 +111,7 @@ struct TcParams {
   int ks, bps;
   float* part;
   int* counter;            // item counter (zeroed by the plan kernel)
-  TcMul mul;               // {1 << 31, 1 << 16}, see tc_lut16x8
+  TcMul mul;               // tc_mul_consts()
   int* status;
   int stages;              // weight stages (LUT formats) or weight + activation stages (dense)
   int xstages;             // activation stages (LUT formats)
@@ -210,25 +218,41 @@ __device__ __forceinline__ void tc_wait_ld16(uint32_t (&v)[16]) {
 __device__ __forceinline__ uint4 tc_lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
 // ------------------------------------------------------- decode policies --
-// 4-bit codes into a 16-entry fp16 table held as high / low byte planes:
-// byte permutes pick entries 0-7 and 8-15 with the low three code bits, a
-// third permute picks between them with bit 3, and two more interleave the
-// low and high bytes into fp16 pairs.  `w` holds 8 codes (k = 0..7, code j
-// in bits 4j..4j+3); out[0..3] receive the fp16 pairs (k, k+1).
+// One thread decodes one weight row.  A policy reads the row's codes and
+// tables for 64 columns (a "half" of a block of KB columns) from the stage's
+// planes (load_half) and turns them into 16 fp16 pairs per 32 columns
+// (lookup_q, quarter qq of the half): out[i] = (weight 2i, weight 2i + 1).
 //
-// The lookups are byte permutes on the integer ALU, the kernel's limiting
-// pipe.  The three right shifts per 8 codes therefore run as high-half
-// multiplies (mul.hi by 2^31 or 2^16) on the otherwise idle FMA pipe; the
-// multipliers come from the kernel parameters (TcMul) so that the compiler
-// cannot fold them back into shifts.
+// The lookups are byte permutes (prmt) on the integer ALU, the kernel's
+// limiting pipe.  Tables sit as a plane of high bytes and a plane of low
+// bytes, so a permute picks one byte of up to 8 entries per output byte.
+// Shifts run as multiplies (mul.hi by 2^n for right shifts, mul.lo for left
+// ones) on the otherwise idle FMA pipe; the multipliers come from the kernel
+// parameters (TcMul) so that the compiler cannot fold them back into shifts.
 __device__ __forceinline__ uint32_t tc_mulhi(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+__device__ __forceinline__ uint32_t tc_mullo(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.lo.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
-__device__ __forceinline__ void tc_lut16x8(uint32_t w, const uint4& th, const uint4& tl, uint32_t* out,
-                                           const TcMul& m) {
+// Per-stage pointers to this tile's piece of each plane the decode reads.
+struct TcPtrs {
+  const uint8_t* p[3];
+};
+
+// 16-entry tables (4-bit codes): `w` holds 8 codes, one per nibble.  Permutes
+// pick entries 0-7 and 8-15 with the low three code bits, a third picks
+// between them with bit 3, for the high and the low bytes; two more (SA, SB)
+// interleave the bytes of nibbles into fp16 pairs.  o0 / o1 come from nibbles
+// 0-3, o2 / o3 from nibbles 4-7.
+template <uint32_t SA, uint32_t SB>
+__device__ __forceinline__ void tc_lut16(uint32_t w, const uint4& th, const uint4& tl, const TcMul& m,
+                                         uint32_t& o0, uint32_t& o1, uint32_t& o2, uint32_t& o3) {
   const uint32_t s1 = w & 0x77777777u;
   const uint32_t s2 = (tc_mulhi(w, m.k31) & 0x44444444u) | 0x32103210u;  // bit 3 of each code to bit 2
 #pragma unroll
@@ -237,12 +261,54 @@ __device__ __forceinline__ void tc_lut16x8(uint32_t w, const uint4& th, const ui
     const uint32_t b = h ? tc_mulhi(s2, m.k16) : s2;
     const uint32_t hi = prmt(prmt(th.x, th.y, a), prmt(th.z, th.w, a), b);
     const uint32_t lo = prmt(prmt(tl.x, tl.y, a), prmt(tl.z, tl.w, a), b);
-    out[2 * h] = prmt(lo, hi, 0x5140u);
-    out[2 * h + 1] = prmt(lo, hi, 0x7362u);
+    (h ? o2 : o0) = prmt(lo, hi, SA);
+    (h ? o3 : o1) = prmt(lo, hi, SB);
+  }
+}
+// Canonical 4-bit codes (nibble j = weight j): out[0..3] = pairs (0,1) .. (6,7).
+__device__ __forceinline__ void tc_lut16x8(uint32_t w, const uint4& th, const uint4& tl, uint32_t* out,
+                                           const TcMul& m) {
+  tc_lut16<0x5140u, 0x7362u>(w, th, tl, m, out[0], out[1], out[2], out[3]);
+}
+
+// 8-entry tables (3-bit codes): `a` holds 8 codes with bit 3 of every nibble
+// clear, nibbles 0-7 = weights (x, x+8, x+1, x+9, x+2, x+10, x+3, x+11) of a
+// 16-weight run; t = {high bytes 0-3, 4-7, low bytes 0-3, 4-7}.  Gives the
+// pairs (x, x+1), (x+8, x+9), (x+2, x+3), (x+10, x+11).
+__device__ __forceinline__ void tc_lut8x8(uint32_t a, const uint4& t, const TcMul& m, uint32_t& o0, uint32_t& o1,
+                                          uint32_t& o2, uint32_t& o3) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t s = h ? tc_mulhi(a, m.k16) : a;
+    const uint32_t lo = prmt(t.z, t.w, s);
+    const uint32_t hi = prmt(t.x, t.y, s);
+    (h ? o2 : o0) = prmt(lo, hi, 0x6240u);
+    (h ? o3 : o1) = prmt(lo, hi, 0x7351u);
   }
 }
 
-// FMT_B, 4-bit codes, tables per `G` columns.
+// 4-entry tables (2-bit codes): x holds the codes of 4 consecutive weights in
+// bits 0-1 of its bytes; th / tl are the table's high / low bytes.  One
+// multiply-add turns x into the selector nibbles (c0, c0 + 4, c1, c1 + 4, ...)
+// and one permute then yields an fp16 pair: out[0] = (0, 1), out[1] = (2, 3).
+__device__ __forceinline__ void tc_lut4x4(uint32_t x, uint32_t th, uint32_t tl, uint32_t* out, const TcMul& m) {
+  uint32_t s0, s1;
+  asm("mad.lo.u32 %0, %1, %2, 0x40404040;" : "=r"(s0) : "r"(x), "r"(m.k11));
+  asm("mad.hi.u32 %0, %1, %2, 0x4040;" : "=r"(s1) : "r"(x), "r"(m.k11h));
+  out[0] = prmt(tl, th, s0);
+  out[1] = prmt(tl, th, s1);
+}
+// 16 weights of a codes2 word into out[0..7].
+__device__ __forceinline__ void tc_lut4x16(uint32_t w, uint32_t th, uint32_t tl, uint32_t* out, const TcMul& m) {
+  tc_lut4x4(w & 0x03030303u, th, tl, out + 0, m);
+  tc_lut4x4(tc_mulhi(w, m.k30) & 0x03030303u, th, tl, out + 2, m);
+  tc_lut4x4(tc_mulhi(w, m.k28) & 0x03030303u, th, tl, out + 4, m);
+  tc_lut4x4(tc_mulhi(w, m.k26) & 0x03030303u, th, tl, out + 6, m);
+}
+
+__device__ __forceinline__ uint2 tc_lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+
+// FMT_B, 4-bit codes, tables per `G` columns.  Planes: codes4, tables.
 template <int G>
 struct TcDecB4 {
   static constexpr bool kDense = false;
@@ -250,23 +316,19 @@ struct TcDecB4 {
   static constexpr int KB = G > 64 ? G : 64;  // columns per block
   static constexpr int kHalves = KB / 64;     // 64-column halves per block
   static constexpr int kNumPlanes = 2;
-  // Shared-memory data of half h (64 columns) of row `row` of one tile: cp /
-  // tp are the tile's code and table pieces inside the stage.  Both
-  // quarters' codes and tables are loaded before any lookup.
   struct Half {
     uint4 c[2], th[2], tl[2];
   };
-  __device__ __forceinline__ static void load_half(const uint8_t* cp, const uint8_t* tp, int row, int h, Half& d) {
+  __device__ __forceinline__ static void load_half(const TcPtrs& pp, int row, int h, Half& d) {
 #pragma unroll
-    for (int qq = 0; qq < 2; ++qq) d.c[qq] = tc_lds128(cp + ((2 * h + qq) * kTcRows + row) * 16);
+    for (int qq = 0; qq < 2; ++qq) d.c[qq] = tc_lds128(pp.p[0] + ((2 * h + qq) * kTcRows + row) * 16);
 #pragma unroll
     for (int qq = 0; qq < (G == 32 ? 2 : 1); ++qq) {
       const int tb = G == 32 ? 2 * h + qq : (G == 64 ? h : 0);  // table of these columns
-      d.th[qq] = tc_lds128(tp + ((2 * tb) * kTcRows + row) * 16);
-      d.tl[qq] = tc_lds128(tp + ((2 * tb + 1) * kTcRows + row) * 16);
+      d.th[qq] = tc_lds128(pp.p[1] + ((2 * tb) * kTcRows + row) * 16);
+      d.tl[qq] = tc_lds128(pp.p[1] + ((2 * tb + 1) * kTcRows + row) * 16);
     }
   }
-  // Looks up quarter qq (32 columns) of a loaded half.
   __device__ __forceinline__ static void lookup_q(const Half& d, int qq, uint32_t (&out)[16], const TcMul& m) {
     const int tq = G == 32 ? qq : 0;
     tc_lut16x8(d.c[qq].x, d.th[tq], d.tl[tq], out + 0, m);
@@ -274,37 +336,109 @@ struct TcDecB4 {
     tc_lut16x8(d.c[qq].z, d.th[tq], d.tl[tq], out + 8, m);
     tc_lut16x8(d.c[qq].w, d.th[tq], d.tl[tq], out + 12, m);
   }
-  // Decodes half h (64 columns) of row `row` of one tile.
-  __device__ __forceinline__ static void decode(const uint8_t* cp, const uint8_t* tp, int row, int h,
-                                                uint32_t (&out)[32], const TcMul& m) {
-    const uint4 c0 = tc_lds128(cp + ((2 * h) * kTcRows + row) * 16);
-    const uint4 c1 = tc_lds128(cp + ((2 * h + 1) * kTcRows + row) * 16);
-    if constexpr (G == 32) {
-      const uint4 th0 = tc_lds128(tp + ((4 * h + 0) * kTcRows + row) * 16);
-      const uint4 tl0 = tc_lds128(tp + ((4 * h + 1) * kTcRows + row) * 16);
-      const uint4 th1 = tc_lds128(tp + ((4 * h + 2) * kTcRows + row) * 16);
-      const uint4 tl1 = tc_lds128(tp + ((4 * h + 3) * kTcRows + row) * 16);
-      tc_lut16x8(c0.x, th0, tl0, out + 0, m);
-      tc_lut16x8(c0.y, th0, tl0, out + 4, m);
-      tc_lut16x8(c0.z, th0, tl0, out + 8, m);
-      tc_lut16x8(c0.w, th0, tl0, out + 12, m);
-      tc_lut16x8(c1.x, th1, tl1, out + 16, m);
-      tc_lut16x8(c1.y, th1, tl1, out + 20, m);
-      tc_lut16x8(c1.z, th1, tl1, out + 24, m);
-      tc_lut16x8(c1.w, th1, tl1, out + 28, m);
+};
+
+// FMT_B, 2-bit codes (and the NESTED coarse tier).  Planes: codes2, tables
+// (8 bytes per table).
+template <int G>
+struct TcDecB2 {
+  static constexpr bool kDense = false;
+  static constexpr bool kBF16 = false;
+  static constexpr int KB = G > 64 ? G : 64;
+  static constexpr int kHalves = KB / 64;
+  static constexpr int kNumPlanes = 2;
+  struct Half {
+    uint4 c;
+    uint32_t th[2], tl[2];
+  };
+  __device__ __forceinline__ static void load_half(const TcPtrs& pp, int row, int h, Half& d) {
+    d.c = tc_lds128(pp.p[0] + (h * kTcRows + row) * 16);
+    if constexpr (G == 32) {  // two tables in one 16-byte unit
+      const uint4 t = tc_lds128(pp.p[1] + row * 16);
+      d.th[0] = t.x; d.tl[0] = t.y; d.th[1] = t.z; d.tl[1] = t.w;
     } else {
-      const int tb = G == 64 ? h : 0;  // table of this half
-      const uint4 th = tc_lds128(tp + ((2 * tb) * kTcRows + row) * 16);
-      const uint4 tl = tc_lds128(tp + ((2 * tb + 1) * kTcRows + row) * 16);
-      tc_lut16x8(c0.x, th, tl, out + 0, m);
-      tc_lut16x8(c0.y, th, tl, out + 4, m);
-      tc_lut16x8(c0.z, th, tl, out + 8, m);
-      tc_lut16x8(c0.w, th, tl, out + 12, m);
-      tc_lut16x8(c1.x, th, tl, out + 16, m);
-      tc_lut16x8(c1.y, th, tl, out + 20, m);
-      tc_lut16x8(c1.z, th, tl, out + 24, m);
-      tc_lut16x8(c1.w, th, tl, out + 28, m);
+      const uint2 t = tc_lds64(pp.p[1] + row * 8);
+      d.th[0] = t.x; d.tl[0] = t.y; d.th[1] = t.x; d.tl[1] = t.y;
     }
+  }
+  __device__ __forceinline__ static void lookup_q(const Half& d, int qq, uint32_t (&out)[16], const TcMul& m) {
+    const int tq = G == 32 ? qq : 0;
+    tc_lut4x16(qq ? d.c.z : d.c.x, d.th[tq], d.tl[tq], out + 0, m);
+    tc_lut4x16(qq ? d.c.w : d.c.y, d.th[tq], d.tl[tq], out + 8, m);
+  }
+};
+
+// FMT_B, 3-bit codes.  Planes: codes2 (bits 0-1), codes1 (bit 2), tables
+// (16 bytes per table).
+template <int G>
+struct TcDecB3 {
+  static constexpr bool kDense = false;
+  static constexpr bool kBF16 = false;
+  static constexpr int KB = G > 64 ? G : 64;
+  static constexpr int kHalves = KB / 64;
+  static constexpr int kNumPlanes = 3;
+  struct Half {
+    uint4 c2;
+    uint2 c1;
+    uint4 t[G == 32 ? 2 : 1];
+  };
+  __device__ __forceinline__ static void load_half(const TcPtrs& pp, int row, int h, Half& d) {
+    d.c2 = tc_lds128(pp.p[0] + (h * kTcRows + row) * 16);
+    d.c1 = tc_lds64(pp.p[1] + row * (KB / 8) + h * 8);
+#pragma unroll
+    for (int i = 0; i < (G == 32 ? 2 : 1); ++i) d.t[i] = tc_lds128(pp.p[2] + (i * kTcRows + row) * 16);
+  }
+  // 16 weights: codes2 word w2, the codes1 bits at nibble bit 2 of y (bit 3 clear)
+  __device__ __forceinline__ static void run16(uint32_t w2, uint32_t ya, uint32_t yb, const uint4& t, uint32_t* out,
+                                               const TcMul& m) {
+    const uint32_t a = (w2 & 0x33333333u) | ya;                   // weights 0, 8, 1, 9, 2, 10, 3, 11
+    const uint32_t b = (tc_mulhi(w2, m.k30) & 0x33333333u) | yb;  // weights 4, 12, 5, 13, 6, 14, 7, 15
+    tc_lut8x8(a, t, m, out[0], out[4], out[1], out[5]);
+    tc_lut8x8(b, t, m, out[2], out[6], out[3], out[7]);
+  }
+  __device__ __forceinline__ static void lookup_q(const Half& d, int qq, uint32_t (&out)[16], const TcMul& m) {
+    const uint4& t = d.t[G == 32 ? qq : 0];
+    const uint32_t w1 = qq ? d.c1.y : d.c1.x;
+    run16(qq ? d.c2.z : d.c2.x, tc_mullo(w1, m.k4) & 0x44444444u, tc_mullo(w1, m.k2) & 0x44444444u, t, out + 0, m);
+    run16(qq ? d.c2.w : d.c2.y, w1 & 0x44444444u, tc_mulhi(w1, m.k31) & 0x44444444u, t, out + 8, m);
+  }
+};
+
+// FMT_NESTED, full tier: the coarse and residual codes form the 4-bit index
+// 4c + r into the combined table.  Planes: coarse codes2, residual codes2,
+// combined tables (32 bytes per table).
+template <int G>
+struct TcDecNested {
+  static constexpr bool kDense = false;
+  static constexpr bool kBF16 = false;
+  static constexpr int KB = G > 64 ? G : 64;
+  static constexpr int kHalves = KB / 64;
+  static constexpr int kNumPlanes = 3;
+  struct Half {
+    uint4 cc, cr;
+    uint4 th[G == 32 ? 2 : 1], tl[G == 32 ? 2 : 1];
+  };
+  __device__ __forceinline__ static void load_half(const TcPtrs& pp, int row, int h, Half& d) {
+    d.cc = tc_lds128(pp.p[0] + (h * kTcRows + row) * 16);
+    d.cr = tc_lds128(pp.p[1] + (h * kTcRows + row) * 16);
+#pragma unroll
+    for (int i = 0; i < (G == 32 ? 2 : 1); ++i) {
+      d.th[i] = tc_lds128(pp.p[2] + ((2 * i) * kTcRows + row) * 16);
+      d.tl[i] = tc_lds128(pp.p[2] + ((2 * i + 1) * kTcRows + row) * 16);
+    }
+  }
+  // 16 weights of one coarse word wc and residual word wr into out[0..7]
+  __device__ __forceinline__ static void run16(uint32_t wc, uint32_t wr, const uint4& th, const uint4& tl,
+                                               uint32_t* out, const TcMul& m) {
+    const uint32_t a = (wr & 0x33333333u) | (tc_mullo(wc, m.k4) & 0xCCCCCCCCu);  // weights 0, 8, 1, 9, ...
+    const uint32_t b = (tc_mulhi(wr, m.k30) & 0x33333333u) | (wc & 0xCCCCCCCCu);  // weights 4, 12, 5, 13, ...
+    tc_lut16<0x6240u, 0x7351u>(a, th, tl, m, out[0], out[4], out[1], out[5]);
+    tc_lut16<0x6240u, 0x7351u>(b, th, tl, m, out[2], out[6], out[3], out[7]);
+  }
+  __device__ __forceinline__ static void lookup_q(const Half& d, int qq, uint32_t (&out)[16], const TcMul& m) {
+    const int tq = G == 32 ? qq : 0;
+    run16(qq ? d.cc.z : d.cc.x, qq ? d.cr.z : d.cr.x, d.th[tq], d.tl[tq], out + 0, m);
+    run16(qq ? d.cc.w : d.cc.y, qq ? d.cr.w : d.cr.y, d.th[tq], d.tl[tq], out + 8, m);
   }
 };
 
@@ -316,10 +450,8 @@ struct TcDecDense {
   static constexpr int KB = 32;
   static constexpr int kHalves = 0;
   static constexpr int kNumPlanes = 1;
-  __device__ __forceinline__ static void decode(const uint8_t*, const uint8_t*, int, int, uint32_t (&)[32],
-                                                const TcMul&) {}
   struct Half {};
-  __device__ __forceinline__ static void load_half(const uint8_t*, const uint8_t*, int, int, Half&) {}
+  __device__ __forceinline__ static void load_half(const TcPtrs&, int, int, Half&) {}
   __device__ __forceinline__ static void lookup_q(const Half&, int, uint32_t (&)[16], const TcMul&) {}
 };
 
@@ -393,7 +525,8 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
   constexpr int xstage_bytes = tc_xstage_bytes<Dec, MT>();
   uint8_t* xring = ring + (int64_t)S * stage_bytes;
   const int boff = 2 * p.tile_bytes;  // activations inside a dense stage
-  const int qoff1 = 2 * p.piece[0];   // second plane inside a stage
+  // planes inside a stage: each holds the pieces of the unit's two tiles
+  const int qoff[3] = {0, 2 * p.piece[0], 2 * (p.piece[0] + p.piece[1])};
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -466,9 +599,9 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
           uint32_t bar = smem_u32(full + s);
           mbar_expect_tx(bar, (uint32_t)(ntl * p.tile_bytes + (kDense ? nnt * KB * 16 : 0)));
           const int64_t pt = (int64_t)b * p.ntiles + 2 * u;
-          bulk_g2s(smem_u32(dst), base + p.plane_off[0] + pt * p.piece[0], (uint32_t)(ntl * p.piece[0]), bar);
-          if (Dec::kNumPlanes > 1)
-            bulk_g2s(smem_u32(dst + qoff1), base + p.plane_off[1] + pt * p.piece[1], (uint32_t)(ntl * p.piece[1]),
+#pragma unroll
+          for (int k = 0; k < Dec::kNumPlanes; ++k)
+            bulk_g2s(smem_u32(dst + qoff[k]), base + p.plane_off[k] + pt * p.piece[k], (uint32_t)(ntl * p.piece[k]),
                      bar);
           uint8_t* xdst = dst + boff;
           if constexpr (!kDense) {
@@ -605,15 +738,16 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
             break;
           }
           const uint8_t* st = ring + (int64_t)s * stage_bytes;
-          const uint8_t* cp = st + t * p.piece[0];
-          const uint8_t* tp = st + qoff1 + t * p.piece[1];
+          TcPtrs pp;
+#pragma unroll
+          for (int k = 0; k < 3; ++k) pp.p[k] = st + qoff[k] + t * p.piece[k];
 #pragma unroll
           for (int h = 0; h < Dec::kHalves; ++h, ra.next(kTcASlots)) {
             const int j = ra.i;
             uint32_t qa[16], qb[16];
             typename Dec::Half hd;
             if (active) {  // the first quarter's lookups run before the slot is known free
-              Dec::load_half(cp, tp, row, h, hd);
+              Dec::load_half(pp, row, h, hd);
               Dec::lookup_q(hd, 0, qa, p.mul);
             }
             if (ra.wrapped) {
@@ -772,5 +906,83 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
   kern<<<num_sms * per_sm, tc_threads<MT>(), smem, stream>>>(p);
   return cudaGetLastError();
 }
+
+// One CTA per (physical tile, block), one thread per row: decode the row's
+// block straight from global memory with the matmul's decode policy and
+// write it to out[rows][cols] (the diagnostic dequantisation of the layout).
+struct TcDequantArgs {
+  const uint8_t* w;
+  int64_t off[3];
+  int piece[3];
+  int ntiles;
+  int64_t cols;
+  int paired;
+  uint16_t* out;
+  TcMul mul;
+};
+
+template <class Dec>
+__global__ void __launch_bounds__(kTcRows) tc_dequant_kernel(const TcDequantArgs a) {
+  const int pt = blockIdx.x, b = blockIdx.y, row = threadIdx.x;
+  const int64_t r = logical_tile(pt, a.ntiles, a.paired != 0) * kTcRows + row;
+  uint4* dst = reinterpret_cast<uint4*>(a.out + r * a.cols + (int64_t)b * Dec::KB);
+  TcPtrs pp;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) pp.p[k] = a.w + a.off[k] + ((int64_t)b * a.ntiles + pt) * a.piece[k];
+  if constexpr (Dec::kDense) {
+#pragma unroll
+    for (int u = 0; u < Dec::KB / 8; ++u)
+      dst[u] = *reinterpret_cast<const uint4*>(pp.p[0] + (u * kTcRows + row) * 16);
+  } else {
+#pragma unroll
+    for (int h = 0; h < Dec::kHalves; ++h) {
+      typename Dec::Half d;
+      Dec::load_half(pp, row, h, d);
+#pragma unroll
+      for (int qq = 0; qq < 2; ++qq) {
+        uint32_t o[16];
+        Dec::lookup_q(d, qq, o, a.mul);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[h * 8 + qq * 4 + i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      }
+    }
+  }
+}
+
+// Launchers of a decode family over its table blocks (32, 64, 128 columns)
+// and token-group widths (32, 128).
+template <template <int> class DecT>
+inline cudaError_t launch_tc_family(int group, int group_tokens, const TcParams& p, int sms, cudaStream_t stream) {
+  const bool wide = group_tokens == 128;
+  if (group_tokens != 32 && !wide) return cudaErrorInvalidValue;
+  switch (group) {
+    case 32: return wide ? launch_tc<DecT<32>, 128>(p, sms, stream) : launch_tc<DecT<32>, 32>(p, sms, stream);
+    case 64: return wide ? launch_tc<DecT<64>, 128>(p, sms, stream) : launch_tc<DecT<64>, 32>(p, sms, stream);
+    case 128: return wide ? launch_tc<DecT<128>, 128>(p, sms, stream) : launch_tc<DecT<128>, 32>(p, sms, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+template <class Dec>
+inline cudaError_t tc_dequant_launch(const TcDequantArgs& a, int64_t nblocks, cudaStream_t stream) {
+  tc_dequant_kernel<Dec><<<dim3((unsigned)a.ntiles, (unsigned)nblocks), kTcRows, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+template <template <int> class DecT>
+inline cudaError_t tc_dequant_family(int group, const TcDequantArgs& a, int64_t nblocks, cudaStream_t stream) {
+  switch (group) {
+    case 32: return tc_dequant_launch<DecT<32>>(a, nblocks, stream);
+    case 64: return tc_dequant_launch<DecT<64>>(a, nblocks, stream);
+    case 128: return tc_dequant_launch<DecT<128>>(a, nblocks, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// Per-family entry points, each in its own translation unit.
+cudaError_t launch_tc_b2(int group, int group_tokens, const TcParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_tc_b3(int group, int group_tokens, const TcParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_tc_nested(int group, int group_tokens, const TcParams& p, int sms, cudaStream_t stream);
+cudaError_t dequant_tc_b2(int group, const TcDequantArgs& a, int64_t nblocks, cudaStream_t stream);
+cudaError_t dequant_tc_b3(int group, const TcDequantArgs& a, int64_t nblocks, cudaStream_t stream);
+cudaError_t dequant_tc_nested(int group, const TcDequantArgs& a, int64_t nblocks, cudaStream_t stream);
 
 }  // namespace blut

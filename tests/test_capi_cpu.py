@@ -58,6 +58,11 @@ def test_tiled_bytes_match_format_bytes(fmt, bpw):
 
 @pytest.mark.parametrize("fmt,bpw", [
     (LUTFormat("b", 4, 64), 1.0), (LUTFormat("b", 4, 32), 1.5), (LUTFormat("b", 4, 128), 0.75),
+    (LUTFormat("b", 3, 32), 0.875), (LUTFormat("b", 3, 64), 0.625), (LUTFormat("b", 3, 128), 0.5),
+    (LUTFormat("b", 2, 32), 0.5), (LUTFormat("b", 2, 64), 0.375), (LUTFormat("b", 2, 128), 0.3125),
+    # NestedLUT stores both tiers: 2 x 0.25 B of codes + (8 + 32) B of tables per block
+    (LUTFormat("nested", 4, 32, 0), 1.75), (LUTFormat("nested", 4, 64, 1), 1.125),
+    (LUTFormat("nested", 4, 128, 0), 0.8125),
     (LUTFormat("dense", 16, 0, dense_dtype=torch.float16), 2.0),
     (LUTFormat("dense", 16, 0, dense_dtype=torch.bfloat16), 2.0),
 ])
@@ -74,9 +79,10 @@ def test_tc_layout_availability():
     assert not b4.has_tc_layout(2688, 2048, paired=True)        # paired rows % 256
     assert not b4.has_tc_layout(2048 + 48, 2048)                 # rows % 128
     assert not b4.has_tc_layout(2048, 1408 + 32)                 # cols % 64
-    for fmt in (LUTFormat("b", 2, 64), LUTFormat("b", 3, 64), LUTFormat("nested", 4, 64, 0),
-                LUTFormat("r8", 8, 128)):
-        assert not fmt.has_tc_layout(2048, 2048)                 # mma.sync layout only
+    for fmt in (LUTFormat("b", 2, 64), LUTFormat("b", 3, 32), LUTFormat("b", 3, 128),
+                LUTFormat("nested", 4, 64, 0), LUTFormat("nested", 4, 64, 1)):
+        assert fmt.has_tc_layout(1536, 2048, paired=True) and fmt.has_tc_layout(2048, 768)
+    assert not LUTFormat("r8", 8, 128).has_tc_layout(2048, 2048)  # mma.sync layout only
 
 
 def test_moe_forward_rejects_mixed_matmul_paths():

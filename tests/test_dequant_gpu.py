@@ -161,11 +161,13 @@ def test_tiled_layout_lookup_bit_exact(fmt, paired):
 
 @pytest.mark.parametrize("paired", [False, True])
 @pytest.mark.parametrize("group", [32, 64, 128])
-def test_tc_layout_lookup_bit_exact(group, paired):
+@pytest.mark.parametrize("kind,bits,tier", [("b", 4, 0), ("b", 3, 0), ("b", 2, 0), ("nested", 4, 0),
+                                            ("nested", 4, 1)])
+def test_tc_layout_lookup_bit_exact(kind, bits, tier, group, paired):
     """BLUT_LAYOUT_TC: pack + the tcgen05 matmul's per-row decode reproduce the canonical dequant."""
     from block_lut_b200.formats import dequant_tiled, pack_tiled
-    fmt = LUTFormat("b", 4, group)
-    rng = np.random.Generator(np.random.PCG64(500 + group))
+    fmt = LUTFormat(kind, bits, group, tier)
+    rng = np.random.Generator(np.random.PCG64(500 + group + 7 * bits + tier))
     rows, cols = 512, 384
     qm = encode(cuda(O.student_t_weights(rng, (rows, cols))), fmt)
     buf, _ = pack_tiled([qm], paired=paired, tc=True)

@@ -13,9 +13,13 @@ from block_lut_b200.moe import LUTExperts, LUTMoELayer, SharedExpert
 
 pytestmark = pytest.mark.gpu
 
-# (format, tiled layout): 4-bit formats run on the tcgen05 path by default;
-# the mma.sync path is kept for every format.
+# (format, tiled layout): Format B and NestedLUT run on the tcgen05 path by
+# default; the mma.sync path is kept for every format.
 FORMATS = [(LUTFormat("b", 4, 64), True), (LUTFormat("b", 4, 32), True), (LUTFormat("b", 4, 128), True),
+           (LUTFormat("b", 3, 64), True), (LUTFormat("b", 3, 32), True), (LUTFormat("b", 3, 128), True),
+           (LUTFormat("b", 2, 64), True), (LUTFormat("b", 2, 32), True), (LUTFormat("b", 2, 128), True),
+           (LUTFormat("nested", 4, 64, 0), True), (LUTFormat("nested", 4, 64, 1), True),
+           (LUTFormat("nested", 4, 32, 0), True), (LUTFormat("nested", 4, 128, 0), True),
            (LUTFormat("b", 4, 64), False), (LUTFormat("b", 3, 64), False), (LUTFormat("b", 2, 64), False),
            (LUTFormat("b", 2, 128), False), (LUTFormat("nested", 4, 64, 0), False),
            (LUTFormat("nested", 4, 64, 1), False)]
@@ -264,12 +268,15 @@ def test_qwen15_layer_decode_batch32_bench_shape():
     check_layer(out[torch.from_numpy(keep).cuda()], ref[keep], torch.float16, "bench-shaped layer")
 
 
-@pytest.mark.parametrize("T,with_shared", [(1024, False), (2048, True)])
-def test_prefill_wide_groups(T, with_shared):
+@pytest.mark.parametrize("T,with_shared,fmt", [
+    (1024, False, LUTFormat("b", 4, 64)), (2048, True, LUTFormat("b", 4, 64)),
+    (1024, False, LUTFormat("b", 3, 64)), (1024, False, LUTFormat("nested", 4, 64, 0)),
+    (1024, False, LUTFormat("b", 2, 128))], ids=lambda v: str(v) if not isinstance(v, LUTFormat) else
+    f"{v.kind}{v.bits}g{v.group}t{v.tier}")
+def test_prefill_wide_groups(T, with_shared, fmt):
     """Prefill regime (tcgen05 path, >= 64 tokens per expert): 128-token groups,
     the separate top-k launch, and (with the shared expert) wide shared groups."""
     E, H, I, k, Is = 8, 512, 256, 2, 256
-    fmt = LUTFormat("b", 4, 64)
     experts, W13, W2 = build_b_layer(fmt, E=E, H=H, I=I, seed=31, tc=True)
     rng = np.random.Generator(np.random.PCG64(T))
     rw = (rng.standard_normal((E + 1, H)) * 0.05).astype(np.float16)
