@@ -34,13 +34,20 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 H, E, I, TOPK, IS, LAYERS = 2048, 60, 1408, 4, 5632, 24
-QWEN = dict(H=H, E=E, I=I, IS=IS)
+QWEN = dict(H=H, E=E, I=I, IS=IS, TOPK=TOPK, LAYERS=LAYERS, RENORM=False, BATCH=32,
+            NAME="Qwen1.5-MoE-A2.7B MoE stack", KIND="b")
+# the 48 MoE layers of Qwen3-30B-A3B at decode -- 128 routed
+# experts of I 768, top-8 softmax renormalised, no shared expert, batch 64,
+# NestedLUT 2+2 with g 64 (full tier, or coarse only with --tier 1).
+QWEN3 = dict(H=2048, E=128, I=768, IS=0, TOPK=8, LAYERS=48, RENORM=True, BATCH=64,
+             NAME="Qwen3-30B-A3B MoE stack", KIND="nested")
 TRAFFIC_RATIO = 1.028  # measured DRAM bytes / algorithmic bytes of the routed tcgen05 launches
 METRIC = "LUT-MoE decode tokens/s; expert LUT-GEMV HBM GB/s vs ~8 TB/s peak"
 # DeepSeek-V2-Lite MoE layers (26 of 27; layer 0 is dense),
 # 64 routed experts of I 1408, top-6 softmax, two shared experts (one MLP of
 # I 2816), prefill of 8 x 4096 tokens.
-DSV2 = dict(H=2048, E=64, I=1408, IS=2816, TOPK=6, LAYERS=26, TOKENS=8 * 4096)
+DSV2 = dict(H=2048, E=64, I=1408, IS=2816, TOPK=6, LAYERS=26, TOKENS=8 * 4096, RENORM=False,
+            NAME="DeepSeek-V2-Lite MoE stack", KIND="b")
 PREFILL_METRIC = "LUT-MoE prefill tokens/s; grouped LUT-GEMM tensor TFLOP/s"
 
 
@@ -50,15 +57,34 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--batch", type=int, default=32, help="decode tokens per rank")
-    p.add_argument("--layers", type=int, default=LAYERS)
-    p.add_argument("--bits", type=int, default=4)
+    p.add_argument("--batch", type=int, default=None, help="decode tokens per rank (workload default)")
+    p.add_argument("--layers", type=int, default=None, help="MoE layers (workload default)")
+    p.add_argument("--kind", choices=["b", "nested"], default=None, help="expert format (workload default)")
+    p.add_argument("--bits", type=int, default=4, help="Format B code bits")
     p.add_argument("--group", type=int, default=64)
+    p.add_argument("--tier", type=int, default=0, help="NestedLUT tier: 0 full, 1 coarse only")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    p.add_argument("--workload", choices=["decode", "prefill"], default="decode",
-                   help="decode: the BASELINE metric (config 2); prefill: config 4's MoE layers")
-    return p.parse_args()
+    p.add_argument("--workload", choices=["decode", "qwen3", "prefill"], default="decode",
+                   help="decode: the BASELINE metric (config 2); qwen3: config 3's MoE stack at decode; "
+                        "prefill: config 4's MoE layers")
+    a = p.parse_args()
+    a.shape = QWEN3 if a.workload == "qwen3" else DSV2 if a.workload == "prefill" else QWEN
+    a.batch = a.batch if a.batch is not None else a.shape.get("BATCH", 32)
+    a.layers = a.layers if a.layers is not None else a.shape["LAYERS"]
+    a.kind = a.kind or a.shape.get("KIND", "b")
+    return a
+
+
+def bench_format(a):
+    from block_lut_b200.formats import LUTFormat
+    return LUTFormat("nested", 4, a.group, a.tier) if a.kind == "nested" else LUTFormat("b", a.bits, a.group)
+
+
+def format_name(fmt):
+    if fmt.kind == "nested":
+        return f"NestedLUT 2+2 g{fmt.group} {'coarse-only' if fmt.tier == 1 else 'full'} tier fp16 tables"
+    return f"BlockLUT {fmt.bits}-bit g{fmt.group} fp16 tables"
 
 
 def peaks():
@@ -116,15 +142,15 @@ class Clocks:
 
 
 # ------------------------------------------------------------ workload ---
-def build_layers(n_layers, experts_local, e0, bits, group, device, seed=0, shape=None):
-    """Synthetic MoE layers (experts [e0, e0 + experts_local) of each); shape
-    {H, E, I, IS} defaults to Qwen1.5-MoE-A2.7B's."""
+def build_layers(n_layers, experts_local, e0, fmt, device, seed=0, shape=None):
+    """Synthetic MoE layers (experts [e0, e0 + experts_local) of each) in
+    format `fmt`; shape {H, E, I, IS} defaults to Qwen1.5-MoE-A2.7B's (IS 0:
+    no shared expert)."""
     import torch
-    from block_lut_b200.formats import LUTFormat, encode
+    from block_lut_b200.formats import encode
     from block_lut_b200.moe import LUTExperts, SharedExpert
     H, E, I, IS = (shape or QWEN)["H"], (shape or QWEN)["E"], (shape or QWEN)["I"], (shape or QWEN)["IS"]
 
-    fmt = LUTFormat("b", bits, group)
     torch.manual_seed(seed)
     st = torch.distributions.StudentT(torch.tensor(5.0, device=device))
     scale = 0.02 / (5.0 / 3.0) ** 0.5
@@ -140,53 +166,71 @@ def build_layers(n_layers, experts_local, e0, bits, group, device, seed=0, shape
         experts = LUTExperts.from_quantized(q13, q2)
         del q13, q2
         router_w = (torch.randn(E + 1, H, generator=gen, device=device) * 0.02).half()
-        s13 = (torch.randn(2 * IS, H, generator=gen, device=device) * 0.02).half()
-        s2 = (torch.randn(H, IS, generator=gen, device=device) * 0.02).half()
-        shared = SharedExpert.from_dense(s13, s2)
+        shared = None
+        if IS > 0:
+            s13 = (torch.randn(2 * IS, H, generator=gen, device=device) * 0.02).half()
+            s2 = (torch.randn(H, IS, generator=gen, device=device) * 0.02).half()
+            shared = SharedExpert.from_dense(s13, s2)
         layers.append((experts, router_w, shared))
     torch.cuda.synchronize()
     return fmt, layers
 
 
-def make_inputs(n_layers, batch, rank, device):
+def make_inputs(n_layers, batch, rank, device, hidden=H):
     import torch
     g = torch.Generator(device=device).manual_seed(7 + rank)
     xs = []
     for _ in range(n_layers):
-        x = torch.randn(batch, H, generator=g, device=device)
+        x = torch.randn(batch, hidden, generator=g, device=device)
         x = x / x.pow(2).mean(dim=1, keepdim=True).sqrt()
         xs.append(x.half().contiguous())
     return xs
 
 
-def cpu_sample(threads, batch, bits=4, group=64, seed=0):
+def cpu_sample(threads, batch, fmt, shape=None, seed=0):
     """Bounded CPU sample: one MoE layer of the workload through the oracle port
     (table-gather dequant + matmul per active expert, all threads).  Returns
     (seconds per layer, description)."""
     from oracle import blut_oracle as O
+    sh = shape or QWEN
+    h_, e_, i_, is_, k_ = sh["H"], sh["E"], sh["I"], sh["IS"], sh["TOPK"]
     rng = np.random.Generator(np.random.PCG64(seed))
-    ent, nb13, nb2 = 1 << bits, H // group, I // group
-    codes13 = rng.integers(0, 256, size=(E, 2 * I, H * bits // 8), dtype=np.uint8)
-    codes2 = rng.integers(0, 256, size=(E, H, I * bits // 8), dtype=np.uint8)
-    t13 = np.sort(rng.standard_normal((E, 2 * I, nb13, ent)).astype(np.float16) * np.float16(0.02), axis=-1)
-    t2 = np.sort(rng.standard_normal((E, H, nb2, ent)).astype(np.float16) * np.float16(0.02), axis=-1)
-    x = O.rms_activations(rng, batch, H)
-    ids, tw = O.routing(rng.standard_normal((batch, E)).astype(np.float32), TOPK)
-    g13 = lambda e: O.dequant_b(codes13[e], t13[e], bits, group).astype(np.float32)  # noqa: E731
-    g2 = lambda e: O.dequant_b(codes2[e], t2[e], bits, group).astype(np.float32)  # noqa: E731
-    s13 = (rng.standard_normal((2 * IS, H)) * 0.02).astype(np.float32)
-    s2 = (rng.standard_normal((H, IS)) * 0.02).astype(np.float32)
-    sg = (rng.standard_normal(H) * 0.02).astype(np.float32)
+    group = fmt.group
+
+    def tables(rows, cols, ent):
+        return np.sort(rng.standard_normal((e_, rows, cols // group, ent)).astype(np.float16) * np.float16(0.02),
+                       axis=-1)
+
+    def mats(rows, cols):
+        if fmt.kind == "nested":
+            cc = rng.integers(0, 256, size=(e_, rows, cols // 4), dtype=np.uint8)
+            cr = rng.integers(0, 256, size=(e_, rows, cols // 4), dtype=np.uint8)
+            ct, rt = tables(rows, cols, 4), tables(rows, cols, 16) * np.float16(0.25)
+            return lambda e: O.dequant_nested(cc[e], cr[e], ct[e], rt[e], group,  # noqa: E731
+                                              coarse_only=fmt.tier == 1).astype(np.float32)
+        codes = rng.integers(0, 256, size=(e_, rows, cols * fmt.bits // 8), dtype=np.uint8)
+        t = tables(rows, cols, 1 << fmt.bits)
+        return lambda e: O.dequant_b(codes[e], t[e], fmt.bits, group).astype(np.float32)  # noqa: E731
+
+    g13, g2 = mats(2 * i_, h_), mats(h_, i_)
+    x = O.rms_activations(rng, batch, h_)
+    ids, tw = O.routing(rng.standard_normal((batch, e_)).astype(np.float32), k_, renorm=sh["RENORM"])
+    if is_ > 0:
+        s13 = (rng.standard_normal((2 * is_, h_)) * 0.02).astype(np.float32)
+        s2 = (rng.standard_normal((h_, is_)) * 0.02).astype(np.float32)
+        sg = (rng.standard_normal(h_) * 0.02).astype(np.float32)
     t0 = time.perf_counter()
     out = O.moe_forward_threaded(x, ids, tw, g13, g2, "f16", threads)
-    xs = x.astype(np.float64)
-    h = xs @ s13.T
-    a = O.round_to((O.silu(h[:, :IS]) * h[:, IS:]).astype(np.float32), "f16").astype(np.float64)
-    out += (1 / (1 + np.exp(-(xs @ sg))))[:, None] * (a @ s2.T)
+    if is_ > 0:
+        xs = x.astype(np.float64)
+        h = xs @ s13.T
+        a = O.round_to((O.silu(h[:, :is_]) * h[:, is_:]).astype(np.float32), "f16").astype(np.float64)
+        out += (1 / (1 + np.exp(-(xs @ sg))))[:, None] * (a @ s2.T)
     dt = time.perf_counter() - t0
     n_active = len(np.unique(ids))
-    return dt, f"1 of {LAYERS} MoE layers at batch {batch} ({n_active} active experts + shared expert), " \
-               f"oracle port: numpy table-gather dequant + matmul, {threads} threads"
+    return dt, f"1 of {sh['LAYERS']} MoE layers at batch {batch} ({n_active} active experts" \
+               f"{' + shared expert' if is_ > 0 else ''}), oracle port: numpy table-gather dequant + matmul, " \
+               f"{threads} threads"
 
 
 # ------------------------------------------------------------------ ours --
@@ -206,9 +250,12 @@ def run_ours(a):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
         return run_ep(a, rank, world, dev)
 
-    fmt, layers = build_layers(a.layers, E, 0, a.bits, a.group, dev)
-    moes = [LUTMoELayer(ex, TOPK, router_w=rw, shared=sh, shared_gate_mode=1) for ex, rw, sh in layers]
-    xs = make_inputs(a.layers, a.batch, rank, dev)
+    W = a.shape
+    Hh, Ee, Ii, ISs, K = W["H"], W["E"], W["I"], W["IS"], W["TOPK"]
+    fmt, layers = build_layers(a.layers, Ee, 0, bench_format(a), dev, shape=W)
+    moes = [LUTMoELayer(ex, K, router_w=rw if sh is not None else rw[:Ee].contiguous(), renorm=W["RENORM"],
+                        shared=sh, shared_gate_mode=1) for ex, rw, sh in layers]
+    xs = make_inputs(a.layers, a.batch, rank, dev, Hh)
     outs = [torch.empty_like(x) for x in xs]
 
     def step():
@@ -247,7 +294,7 @@ def run_ours(a):
     # dominant kernel: routed LUT matmuls (gate/up + down), per-launch CUDA events
     n_active = []
     for m, x in zip(moes, xs):
-        ids, _, _ = router(x, m.router_w, TOPK, shared_gate=True)
+        ids, _, _ = router(x, m.router_w, K, renorm=W["RENORM"], shared_gate=m.shared is not None)
         n_active.append(int(torch.unique(ids).numel()))
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in moes]
     for ev in evs:  # torch creates the CUDA event on its first record
@@ -270,8 +317,8 @@ def run_ours(a):
     t_dn /= reps * len(moes)
     bpw = fmt.bytes_per_weight()
     na = sum(n_active) / len(n_active)
-    b_gu = na * 2 * I * H * bpw
-    b_dn = na * H * I * bpw
+    b_gu = na * 2 * Ii * Hh * bpw
+    b_dn = na * Hh * Ii * bpw
     achieved = (b_gu + b_dn) / ((t_gu + t_dn) / 1e3) / 1e9
     peak, peak_kind = peaks()
 
@@ -304,7 +351,7 @@ def run_ours(a):
     cpu = None
     if not a.no_cpu:
         threads = os.cpu_count() or 1
-        dt, desc = cpu_sample(threads, a.batch, a.bits, a.group)
+        dt, desc = cpu_sample(threads, a.batch, fmt, W)
         cpu = {"value": a.batch / (dt * a.layers), "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": desc}
 
@@ -314,11 +361,11 @@ def run_ours(a):
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16",
         "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU Lloyd-encoded; N(0,1) RMS-normalised fp16 tokens",
-        "config": {"workload": f"Qwen1.5-MoE-A2.7B MoE stack, decode batch {a.batch}", "layers": a.layers,
-                   "global_batch": a.batch, "experts": E, "top_k": TOPK, "hidden": H, "inter": I,
-                   "shared_inter": IS, "format": f"BlockLUT {a.bits}-bit g{a.group} fp16 tables",
-                   "parallelism": "single GPU", "graph": "CUDA graph of the 24-layer step",
-                   "l2": f"inputs larger than L2: {sum(n_active) * 3 * I * H * bpw / 1e9:.1f} GB of expert "
+        "config": {"workload": f"{W['NAME']}, decode batch {a.batch}", "layers": a.layers,
+                   "global_batch": a.batch, "experts": Ee, "top_k": K, "renorm": W["RENORM"], "hidden": Hh,
+                   "inter": Ii, "shared_inter": ISs, "format": format_name(fmt),
+                   "parallelism": "single GPU", "graph": f"CUDA graph of the {a.layers}-layer step",
+                   "l2": f"inputs larger than L2: {sum(n_active) * 3 * Ii * Hh * bpw / 1e9:.1f} GB of expert "
                          f"weights streamed per step"},
         "roofline": {"kernel": ("tc_mm_kernel (tcgen05" if moes[0].experts.tc else "lut_mm_kernel (mma.sync") +
                                "; routed gate/up+SiLU*up and down, per layer)", "bound": "hbm",
@@ -328,7 +375,8 @@ def run_ours(a):
                      # DRAM read + write per layer: the algorithmic bytes times the ratio the ncu
                      # capture in profiles/tc_mm_kernel_qwen15_decode_b32.md measured for the
                      # routed gate/up + down launches (1.028)
-                     "traffic": (b_gu + b_dn) * TRAFFIC_RATIO if moes[0].experts.tc else None,
+                     "traffic": (b_gu + b_dn) * TRAFFIC_RATIO if moes[0].experts.tc and fmt.kind == "b" and
+                     fmt.bits == 4 and fmt.group == 64 else None,
                      "bytes_per_layer": b_gu + b_dn, "ms_gateup": t_gu, "ms_down": t_dn,
                      "active_experts": na, "active_experts_per_layer": n_active[:4]},
         "cpu_baseline": cpu, "e2e": e2e,
@@ -340,8 +388,8 @@ def run_ours(a):
 
 def run_ep(a, rank, world, dev):
     from block_lut_b200.ep import run_bench_ep
-    return run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, METRIC,
-                        dict(H=H, E=E, I=I, TOPK=TOPK, IS=IS))
+    return run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, METRIC, a.shape,
+                        bench_format(a), format_name)
 
 
 # ------------------------------------------------------------- reference --
@@ -353,8 +401,9 @@ def run_reference(a):
     threads = os.cpu_count() or 1
     times = []
     desc = ""
+    fmt = bench_format(a)
     for i in range(a.warmup + a.steps):
-        dt, desc = cpu_sample(threads, a.batch, a.bits, a.group, seed=i % 2)
+        dt, desc = cpu_sample(threads, a.batch, fmt, a.shape, seed=i % 2)
         if i >= a.warmup:
             times.append(dt)
         if sum(times) > 120:  # keep the whole run within a few minutes
@@ -365,8 +414,8 @@ def run_reference(a):
            "steps": len(times), "warmup": a.warmup, "ms_per_step": dt * a.layers * 1e3, "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
            "data": "synthetic random codes and sorted fp16 tables of the workload's shapes",
-           "config": {"workload": f"Qwen1.5-MoE-A2.7B MoE stack, decode batch {a.batch}", "layers": a.layers,
-                      "global_batch": a.batch, "format": f"BlockLUT {a.bits}-bit g{a.group}"},
+           "config": {"workload": f"{a.shape['NAME']}, decode batch {a.batch}", "layers": a.layers,
+                      "global_batch": a.batch, "format": format_name(fmt)},
            "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)
@@ -381,9 +430,9 @@ def run_prefill(a):
     from block_lut_b200.moe import LUTMoELayer
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
-    n_layers = a.layers if a.layers != LAYERS else DSV2["LAYERS"]
+    n_layers = a.layers
     T, k = DSV2["TOKENS"], DSV2["TOPK"]
-    fmt, layers = build_layers(n_layers, DSV2["E"], 0, a.bits, a.group, dev, shape=DSV2)
+    fmt, layers = build_layers(n_layers, DSV2["E"], 0, bench_format(a), dev, shape=DSV2)
     moes = [LUTMoELayer(ex, k, router_w=rw[:DSV2["E"]].contiguous(), shared=sh, shared_gate_mode=0)
             for ex, rw, sh in layers]
     g = torch.Generator(device=dev).manual_seed(7)
@@ -434,7 +483,7 @@ def run_prefill(a):
            "dtype": "f16", "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU Lloyd-encoded; N(0,1) tokens",
            "config": {"workload": f"DeepSeek-V2-Lite MoE stack, prefill {T} tokens", "layers": n_layers,
                       "tokens": T, "experts": DSV2["E"], "top_k": k, "hidden": H, "inter": I, "shared_inter": IS,
-                      "format": f"BlockLUT {a.bits}-bit g{a.group} fp16 tables", "parallelism": "single GPU"},
+                      "format": format_name(fmt), "parallelism": "single GPU"},
            "roofline": {"kernel": "tc_mm_kernel (tcgen05, 128-token groups; routed gate/up+SiLU*up and down)",
                         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak,

@@ -118,21 +118,25 @@ class EPMoELayer:
     __call__ = forward
 
 
-def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, metric, shp):
+def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, metric, shp, fmt, format_name):
     """bench.py --gpus N: every rank owns E/N experts of each layer and a decode
     batch of its own; value = total tokens of all ranks / max step time."""
     import json
 
     H, E, I, TOPK, IS = shp["H"], shp["E"], shp["I"], shp["TOPK"], shp["IS"]
     s, c = expert_ranges(E, world)[rank]
-    fmt, layers = build_layers(a.layers, c, s, a.bits, a.group, dev)
+    fmt, layers = build_layers(a.layers, c, s, fmt, dev, shape=dict(shp, IS=0))
     eps = []
     g = torch.Generator(device=dev).manual_seed(99)
-    for ex, rw, sh in layers:
-        s13 = (torch.randn(2 * IS, H, generator=g, device=dev) * 0.02).half()
-        s2 = (torch.randn(H, IS, generator=g, device=dev) * 0.02).half()
-        eps.append(EPMoELayer(ex, E, TOPK, rw, shared=(s13, s2)))
-    xs = make_inputs(a.layers, a.batch, rank, dev)
+    for ex, rw, _ in layers:
+        shared = None
+        if IS > 0:
+            s13 = (torch.randn(2 * IS, H, generator=g, device=dev) * 0.02).half()
+            s2 = (torch.randn(H, IS, generator=g, device=dev) * 0.02).half()
+            shared = (s13, s2)
+        eps.append(EPMoELayer(ex, E, TOPK, rw if shared is not None else rw[:E].contiguous(),
+                              shared=shared, renorm=shp["RENORM"]))
+    xs = make_inputs(a.layers, a.batch, rank, dev, H)
 
     outs = [None] * len(eps)
 
@@ -210,11 +214,11 @@ def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, 
                "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
                "scaling": "weak", "vs_baseline": None, "dtype": "f16",
                "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU Lloyd-encoded; N(0,1) RMS-normalised fp16",
-               "config": {"workload": f"Qwen1.5-MoE-A2.7B MoE stack, decode batch {a.batch} per rank",
+               "config": {"workload": f"{shp['NAME']}, decode batch {a.batch} per rank",
                           "layers": a.layers, "global_batch": total_tokens, "experts": E, "top_k": TOPK,
-                          "format": f"BlockLUT {a.bits}-bit g{a.group}", "parallelism": f"ep{world}",
+                          "format": format_name(fmt), "parallelism": f"ep{world}",
                           "exchange": "NCCL all_to_all_single dispatch (x, ids, w) + combine (fp32 partials)"},
-               "graph": "CUDA graph of the 24-layer step, NCCL collectives included",
+               "graph": f"CUDA graph of the {a.layers}-layer step, NCCL collectives included",
                "roofline": None, "cpu_baseline": None,
                "e2e": {"value": total_tokens / (e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e_ms,
                        "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs) * world,
