@@ -64,6 +64,9 @@ SIGNATURES = [
     ("blut_tiled_bytes", C.c_int64, [C.POINTER(MatDesc)]),
     ("blut_pack_tiled", C.c_int, [C.POINTER(MatDesc), C.POINTER(Canon), _VP, _VP]),
     ("blut_dequant_tiled", C.c_int, [C.POINTER(MatDesc), _VP, _VP, _VP, _VP]),
+    ("blut_matmul_workspace_size", C.c_size_t, [C.POINTER(MatDesc), _I64]),
+    ("blut_matmul", C.c_int, [C.POINTER(MatDesc), _VP, _VP, _VP, _I64, _VP, _I32, _VP, C.c_size_t, _VP]),
+    ("blut_matmul_launch_count", C.c_int, [C.POINTER(MatDesc), _I64]),
     ("blut_encode", C.c_int, [C.POINTER(MatDesc), _VP, _VP, _VP, _VP, _VP, _VP]),
     ("blut_encode_r", C.c_int, [_VP, _I64, _VP, _I32, _VP, _VP, _VP]),
     ("blut_lut_gemv", C.c_int, [_VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _VP]),

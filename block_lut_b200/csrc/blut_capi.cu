@@ -111,4 +111,19 @@ int blut_moe_launch_count(const blut_moe_args* args) {
   return moe_launch_count(*args);
 }
 
+size_t blut_matmul_workspace_size(const blut_mat_desc* desc, int64_t m) {
+  return desc ? matmul_workspace(*desc, m) : 0;
+}
+
+int blut_matmul(const blut_mat_desc* desc, const void* w_tiled, const void* lut_table, const void* x, int64_t m,
+                void* y, int32_t y_f32, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!desc) return BLUT_ERR_INVALID;
+  return matmul(*desc, w_tiled, lut_table, x, m, y, y_f32, workspace, workspace_bytes, S(stream));
+}
+
+int blut_matmul_launch_count(const blut_mat_desc* desc, int64_t m) {
+  if (!desc) return BLUT_ERR_INVALID;
+  return matmul_launch_count(*desc, m);
+}
+
 }  // extern "C"

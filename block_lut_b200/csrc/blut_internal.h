@@ -54,6 +54,11 @@ struct MoEWs {
 };
 
 int num_sms();
+// Consumer warps (units) per work item of the mma.sync matmul for the expected
+// number of token groups.
+int choose_units_per_item(double est_groups, int units, int sms);
+// Error check after a launch stage (synchronises with BLUT_DEBUG_SYNC set).
+int stage_done(const char* stage, cudaStream_t s);
 size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws);
 void moe_split(const blut_moe_args& a, MoESplit& s);
 int validate_moe(const blut_moe_args& a);
@@ -79,6 +84,12 @@ bool tc_planes(const blut_mat_desc& d, bool pair, TcParams& p);
 cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int group_tokens, int sms, cudaStream_t stream);
 int dequant_tiled_tc(const blut_mat_desc& d, const void* tiled, void* out, cudaStream_t stream);
 int dequant_tiled(const blut_mat_desc& d, const void* tiled, const void* table, void* out, cudaStream_t stream);
+
+// Single-matrix matmul y = W x on either path (blut_matmul.cu).
+size_t matmul_workspace(const blut_mat_desc& d, int64_t m);
+int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const void* x, int64_t m, void* y,
+           int y_f32, void* workspace, size_t ws_bytes, cudaStream_t stream);
+int matmul_launch_count(const blut_mat_desc& d, int64_t m);
 
 // Canonical-layout kernels (blut_pack.cu, blut_gemv.cu).
 int dequant(const blut_mat_desc& d, const blut_canon& c, void* out, cudaStream_t stream);

@@ -1,0 +1,260 @@
+// Single-matrix LUT matmul y = W x, x [M][K] and y [M][N], on the matmul
+// path of the matrix's tiled layout (tcgen05 for BLUT_LAYOUT_TC, mma.sync
+// otherwise).  Four launches: a plan kernel writes the token groups (one
+// "expert", groups of 32 tokens, or 128 on the tcgen05 path from 128 tokens
+// on), a gather kernel puts x into the path's operand order, the matmul
+// writes fp32 rows (in K slices when the tcgen05 path has too few work items
+// to fill the GPU), and a reduce kernel sums the slices in slice order into
+// y.  This is the single-matrix LUT GEMV/GEMM of the reference
+// (vllm_lut/cuda_lut_gemv.py:153-169, fused_kernel.py:13-46) for every
+// format of this library and every token count.
+#include <algorithm>
+
+#include "blut_internal.h"
+#include "blut_mm.cuh"
+#include "blut_tc.cuh"
+
+namespace blut {
+
+namespace {
+
+constexpr int64_t kMatmulMaxTokens = 1 << 20;
+
+struct MatmulPlan {
+  bool tc;
+  int gtok;         // tokens per group
+  int64_t groups;   // token groups
+  int64_t nt8;      // n-tiles of 8 tokens
+  int ks, bps;      // K slices and column blocks per slice
+  int units;        // tcgen05 units (pairs of 128-row tiles)
+};
+
+struct MatmulWs {
+  int* status;      // status word (the first word of the workspace)
+  int* counter;     // tcgen05 work-item counter
+  int* n_groups;
+  int *expert, *slot0, *ntok, *nt0;
+  uint8_t* bin;     // x in the operand order of the path
+  float* ys;        // ks slices of fp32 y
+};
+
+bool matmul_plan(const blut_mat_desc& d, int64_t m, MatmulPlan& p, TiledLayout& L) {
+  if (!make_layout(d, L)) return false;
+  p.tc = L.tc != 0;
+  p.gtok = p.tc && m >= kWideGroupTok ? kWideGroupTok : kGroupTok;
+  p.groups = (m + p.gtok - 1) / p.gtok;
+  p.nt8 = (m + kNTile - 1) / kNTile;
+  p.ks = 1;
+  p.bps = (int)L.nchunks;
+  p.units = 0;
+  if (p.tc) {
+    p.units = (int)((L.ntiles + 1) / 2);
+    if (p.gtok == kGroupTok) {  // split K while the items are fewer than four per SM
+      const int sms = num_sms();
+      int ks = 1;
+      while (ks * 2 <= 16 && L.nchunks / (ks * 2) >= 2 && (double)p.groups * p.units * ks < 4.0 * sms) ks *= 2;
+      p.bps = (int)((L.nchunks + ks - 1) / ks);
+      p.ks = (int)((L.nchunks + p.bps - 1) / p.bps);
+    }
+  }
+  return true;
+}
+
+size_t matmul_carve(const blut_mat_desc& d, int64_t m, const MatmulPlan& p, uint8_t* base, MatmulWs* w) {
+  size_t off = 0;
+  auto take = [&](int64_t bytes) {
+    const size_t o = off;
+    off = (size_t)align256(off + bytes);
+    return o;
+  };
+  const size_t o_status = take(256);
+  const size_t o_groups = take(4 * p.groups * 4);
+  const size_t o_bin = take(p.nt8 * kNTile * d.cols * 2);
+  const size_t o_ys = take((int64_t)p.ks * m * d.rows * 4);
+  if (base && w) {
+    w->status = reinterpret_cast<int*>(base + o_status);
+    w->counter = w->status + 4;
+    w->n_groups = w->status + 8;
+    int* g = reinterpret_cast<int*>(base + o_groups);
+    w->expert = g;
+    w->slot0 = g + p.groups;
+    w->ntok = g + 2 * p.groups;
+    w->nt0 = g + 3 * p.groups;
+    w->bin = base + o_bin;
+    w->ys = reinterpret_cast<float*>(base + o_ys);
+  }
+  return off;
+}
+
+int validate_matmul(const blut_mat_desc& d, int64_t m) {
+  if (m <= 0 || m > kMatmulMaxTokens) return BLUT_ERR_UNSUPPORTED;
+  if (d.layout & BLUT_LAYOUT_PAIRED) return BLUT_ERR_INVALID;  // a single projection
+  if (d.cols % kChunk) return BLUT_ERR_UNSUPPORTED;
+  if (d.dtype != BLUT_F16 && d.dtype != BLUT_BF16) return BLUT_ERR_INVALID;
+  TiledLayout L;
+  if (!make_layout(d, L)) return BLUT_ERR_UNSUPPORTED;
+  return BLUT_OK;
+}
+
+}  // namespace
+
+// Token groups of one matrix: group g holds tokens g * gtok .. (one expert).
+// Also clears the status word (it reports this call) and the work counter.
+__global__ void matmul_plan_kernel(int64_t m, int gtok, int64_t groups, int* __restrict__ n_groups,
+                                   int* __restrict__ expert, int* __restrict__ slot0, int* __restrict__ ntok,
+                                   int* __restrict__ nt0, int* __restrict__ status, int* __restrict__ counter) {
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
+    expert[g] = 0;
+    slot0[g] = (int)(g * gtok);
+    ntok[g] = (int)std::min<int64_t>(gtok, m - g * gtok);
+    nt0[g] = (int)(g * gtok / kNTile);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *n_groups = (int)groups;
+    *status = 0;
+    *counter = 0;
+  }
+}
+
+// x of one (n-tile of 8 tokens, 128-column chunk), 32 threads: the tcgen05
+// operand order (tc_bact_off) or mma.sync B fragments.
+__global__ void __launch_bounds__(32) matmul_gather_kernel(const uint16_t* __restrict__ x, int64_t m, int k,
+                                                           uint8_t* __restrict__ bin, int tc, int kb,
+                                                           int64_t ntstride) {
+  const int64_t nt = blockIdx.x;
+  const int c = blockIdx.y;
+  const int lane = threadIdx.x;
+  const int64_t t0 = nt * kNTile;
+  const int cnt = (int)std::min<int64_t>(kNTile, m - t0);
+  if (tc) {
+    const int tok = lane & 7;
+    const uint16_t* row = tok < cnt ? x + (t0 + tok) * k + c * kChunk : nullptr;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int kg = (lane >> 3) + 4 * i;
+      const uint4 v = row ? *reinterpret_cast<const uint4*>(row + kg * 8) : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(bin + tc_bact_off(t0 + tok, c * kChunk + kg * 8, kb, ntstride)) = v;
+    }
+    return;
+  }
+  const int g = lane >> 2, tq = lane & 3;
+  uint32_t wv[16];
+  if (g < cnt) {
+    const uint32_t* row = reinterpret_cast<const uint32_t*>(x + (t0 + g) * k + c * kChunk);
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      wv[2 * s] = row[(16 * s + 2 * tq) >> 1];
+      wv[2 * s + 1] = row[(16 * s + 2 * tq + 8) >> 1];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) wv[i] = 0;
+  }
+  uint4* d4 = reinterpret_cast<uint4*>(bin + (nt * (k / kChunk) + c) * kBfragChunkBytes + lane * 64);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
+}
+
+// y = sum of the ks fp32 slices in slice order, four values per thread.
+template <bool BF16>
+__global__ void __launch_bounds__(256) matmul_reduce_kernel(const float* __restrict__ ys, int ks, int64_t sstride,
+                                                            int64_t n4, void* __restrict__ y, int y_f32) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = *reinterpret_cast<const float4*>(ys + 4 * i);
+    for (int s = 1; s < ks; ++s) {
+      const float4 u = *reinterpret_cast<const float4*>(ys + s * sstride + 4 * i);
+      v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
+    }
+    if (y_f32) {
+      reinterpret_cast<float4*>(y)[i] = v;
+    } else {
+      uint2 o;
+      o.x = uint32_t(f32_to_act<BF16>(v.x)) | (uint32_t(f32_to_act<BF16>(v.y)) << 16);
+      o.y = uint32_t(f32_to_act<BF16>(v.z)) | (uint32_t(f32_to_act<BF16>(v.w)) << 16);
+      reinterpret_cast<uint2*>(y)[i] = o;
+    }
+  }
+}
+
+size_t matmul_workspace(const blut_mat_desc& d, int64_t m) {
+  if (validate_matmul(d, m) != BLUT_OK) return 0;
+  MatmulPlan p;
+  TiledLayout L;
+  if (!matmul_plan(d, m, p, L)) return 0;
+  return matmul_carve(d, m, p, nullptr, nullptr);
+}
+
+int matmul_launch_count(const blut_mat_desc& d, int64_t m) {
+  const int rc = validate_matmul(d, m);
+  return rc != BLUT_OK ? rc : 4;  // plan, gather, matmul, reduce
+}
+
+int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const void* x, int64_t m, void* y,
+           int y_f32, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  int rc = validate_matmul(d, m);
+  if (rc != BLUT_OK) return rc;
+  if (!w || !x || !y || !workspace) return BLUT_ERR_INVALID;
+  if (d.format == BLUT_FMT_R8 && !lut_table) return BLUT_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15)
+    return BLUT_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return BLUT_ERR_INVALID;
+  MatmulPlan p;
+  TiledLayout L;
+  if (!matmul_plan(d, m, p, L)) return BLUT_ERR_UNSUPPORTED;
+  if (ws_bytes < matmul_carve(d, m, p, nullptr, nullptr)) return BLUT_ERR_WORKSPACE;
+  MatmulWs ws;
+  matmul_carve(d, m, p, static_cast<uint8_t*>(workspace), &ws);
+  const int sms = num_sms();
+  const int64_t N = d.rows, K = d.cols;
+
+  matmul_plan_kernel<<<(unsigned)std::min<int64_t>((p.groups + 255) / 256, 1024), 256, 0, stream>>>(
+      m, p.gtok, p.groups, ws.n_groups, ws.expert, ws.slot0, ws.ntok, ws.nt0, ws.status, ws.counter);
+  if ((rc = stage_done("matmul plan", stream)) != BLUT_OK) return rc;
+  matmul_gather_kernel<<<dim3((unsigned)p.nt8, (unsigned)(K / kChunk)), 32, 0, stream>>>(
+      static_cast<const uint16_t*>(x), m, (int)K, ws.bin, p.tc ? 1 : 0, p.tc ? L.kb : 0, p.nt8);
+  if ((rc = stage_done("matmul gather", stream)) != BLUT_OK) return rc;
+
+  const GroupTab gt{ws.n_groups, ws.expert, ws.slot0, ws.ntok, ws.nt0};
+  if (p.tc) {
+    TcParams t{};
+    if (!tc_planes(d, false, t)) return BLUT_ERR_UNSUPPORTED;
+    t.w = static_cast<const uint8_t*>(w);
+    t.wstride = 0;
+    t.gt = gt;
+    t.bin = ws.bin;
+    t.ntstride = p.nt8;
+    t.y_out = ws.ys;
+    t.y_ld = (int)N;
+    t.y_sstride = m * N;
+    t.counter = ws.counter;
+    t.status = ws.status;
+    t.ks = p.ks;
+    t.bps = p.bps;
+    if (launch_tc_mm(d, t, p.gtok, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  } else {
+    MMParams mp{};
+    if (!mm_planes(d, false, mp)) return BLUT_ERR_UNSUPPORTED;
+    mp.status = ws.status;
+    mp.r8_table = static_cast<const uint16_t*>(lut_table);
+    mp.gt = gt;
+    mp.w = static_cast<const uint8_t*>(w);
+    mp.wstride = 0;
+    mp.bin = ws.bin;
+    mp.y_out = ws.ys;
+    mp.y_ld = (int)N;
+    mp.W = choose_units_per_item((double)p.groups, mp.units, sms);
+    mp.b_ntiles = (int)((std::min<int64_t>(m, kGroupTok) + kNTile - 1) / kNTile);
+    if (launch_lut_mm(d, false, mp, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  }
+  if ((rc = stage_done("matmul", stream)) != BLUT_OK) return rc;
+
+  const int64_t n4 = m * N / 4;
+  const unsigned grid = (unsigned)std::min<int64_t>((n4 + 255) / 256, 8 * sms);
+  if (d.dtype == BLUT_BF16)
+    matmul_reduce_kernel<true><<<grid, 256, 0, stream>>>(ws.ys, p.ks, m * N, n4, y, y_f32);
+  else
+    matmul_reduce_kernel<false><<<grid, 256, 0, stream>>>(ws.ys, p.ks, m * N, n4, y, y_f32);
+  return stage_done("matmul reduce", stream);
+}
+
+}  // namespace blut

@@ -620,7 +620,7 @@ bool mm_planes(const blut_mat_desc& d, bool pair, MMParams& p) {
 
 // Units per work item: as many consumer warps per CTA as keeps at least two
 // items per SM for the expected number of token groups.
-static int choose_units_per_item(double est_groups, int units, int sms) {
+int choose_units_per_item(double est_groups, int units, int sms) {
   int w = kMaxConsumers;
   while (w > 1 && est_groups * ((units + w - 1) / w) < 2.0 * sms) w /= 2;
   return w;
@@ -633,7 +633,7 @@ static bool debug_sync() {
   return on;
 }
 
-static int stage_done(const char* stage, cudaStream_t s) {
+int stage_done(const char* stage, cudaStream_t s) {
   cudaError_t e = cudaGetLastError();
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (e == cudaSuccess && debug_sync() && cudaStreamIsCapturing(s, &cap) == cudaSuccess &&

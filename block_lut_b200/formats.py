@@ -175,7 +175,8 @@ def tiled_bytes(fmt: LUTFormat, rows: int, cols: int, paired: bool = False, tc: 
     d = fmt.desc(rows, cols, paired, tc)
     n = _lib.lib().blut_tiled_bytes(C.byref(d))
     if n < 0:
-        need = "rows % 128 (256 paired) == 0, a 4-bit or dense format" if tc else "rows % 16 and cols % 128 == 0"
+        need = "rows % 128 (256 paired) == 0, cols % 64, a Format B, NestedLUT or dense format" if tc else \
+            "rows % 16 and cols % 128 == 0"
         raise ValueError(f"no tiled layout for {fmt} [{rows}, {cols}]: needs {need}")
     return int(n)
 

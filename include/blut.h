@@ -152,6 +152,25 @@ BLUT_API int blut_pack_tiled(const blut_mat_desc* desc, const blut_canon* src, v
 BLUT_API int blut_dequant_tiled(const blut_mat_desc* desc, const void* tiled, const void* lut_table, void* out,
                                 void* stream);
 
+/* --------------------------------------------------- single-matrix matmul -- */
+
+/* y = W x for one matrix in the tiled layout: x [m][cols] and y [m][rows]
+ * in desc->dtype (fp32 when y_f32 != 0), 1 <= m <= 2^20, cols % 128 == 0,
+ * desc->layout without BLUT_LAYOUT_PAIRED.  Runs on the tcgen05 matmul for
+ * BLUT_LAYOUT_TC matrices and on the mma.sync matmul otherwise, fp32
+ * accumulation; lut_table is FMT_R8's table (NULL otherwise).  Four launches
+ * on `stream`, no allocation, no synchronisation; the workspace (256-byte
+ * aligned, blut_matmul_workspace_size bytes) holds the status word that
+ * blut_moe_check_status reads.  Replaces the reference's single-matrix LUT
+ * GEMV lut_gemv (vllm_lut/cuda_lut_gemv.py:153-169) and fused_lut_gemv
+ * (vllm_lut/fused_kernel.py:13-46), for every format and token count. */
+BLUT_API size_t blut_matmul_workspace_size(const blut_mat_desc* desc, int64_t m);
+BLUT_API int blut_matmul(const blut_mat_desc* desc, const void* w_tiled, const void* lut_table, const void* x,
+                         int64_t m, void* y, int32_t y_f32, void* workspace, size_t workspace_bytes,
+                         void* stream);
+/* Kernel launches one blut_matmul call makes (< 0 for invalid arguments). */
+BLUT_API int blut_matmul_launch_count(const blut_mat_desc* desc, int64_t m);
+
 /* ---------------------------------------------------------------- encode -- */
 
 /* Format B / NestedLUT encoder: per (row, block) 1-D Lloyd k-means (10

@@ -209,3 +209,21 @@ def test_tiled_layout_position_maps_are_bijective(tmp_path):
     assert r.returncode == 0, r.stderr
     r = subprocess.run([str(exe)], capture_output=True, text=True)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout
+
+
+def test_matmul_workspace_and_launches():
+    """blut_matmul's host-side checks: sizes, layouts and launch count, without a GPU call."""
+    lib = _lib.lib()
+    for fmt, tc in ((LUTFormat("b", 4, 64), True), (LUTFormat("b", 2, 64), False), (LUTFormat("r8", 8, 128), False)):
+        d = fmt.desc(2048, 1408, tc=tc)
+        for m in (1, 32, 4096):
+            n = lib.blut_matmul_workspace_size(C.byref(d), m)
+            assert n >= m * 1408 * 2 + m * 2048 * 4          # activations + fp32 rows
+            assert lib.blut_matmul_launch_count(C.byref(d), m) == 4
+        assert lib.blut_matmul_workspace_size(C.byref(d), 0) == 0
+        assert lib.blut_matmul_workspace_size(C.byref(d), (1 << 20) + 1) == 0
+    paired = LUTFormat("b", 4, 64).desc(2816, 2048, paired=True, tc=True)
+    assert lib.blut_matmul_workspace_size(C.byref(paired), 8) == 0
+    assert lib.blut_matmul_launch_count(C.byref(paired), 8) == _lib.BLUT_ERR_INVALID
+    d = LUTFormat("b", 4, 64).desc(2048, 1408, tc=True)
+    assert lib.blut_matmul(C.byref(d), None, None, None, 8, None, 0, None, 0, None) == _lib.BLUT_ERR_INVALID
