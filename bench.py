@@ -65,9 +65,12 @@ def parse():
     p.add_argument("--tier", type=int, default=0, help="NestedLUT tier: 0 full, 1 coarse only")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    p.add_argument("--workload", choices=["decode", "qwen3", "prefill"], default="decode",
+    p.add_argument("--workload", choices=["decode", "qwen3", "prefill", "sweep"], default="decode",
                    help="decode: the BASELINE metric (config 2); qwen3: config 3's MoE stack at decode; "
-                        "prefill: config 4's MoE layers")
+                        "prefill: config 4's MoE layers; sweep: config 5's single-matrix kernel sweep")
+    p.add_argument("--sweep-bits", default="2,3,4")
+    p.add_argument("--sweep-groups", default="32,64,128")
+    p.add_argument("--sweep-m", default="1,2,4,8,16,64,256,1024,4096")
     a = p.parse_args()
     a.shape = QWEN3 if a.workload == "qwen3" else DSV2 if a.workload == "prefill" else QWEN
     a.batch = a.batch if a.batch is not None else a.shape.get("BATCH", 32)
@@ -495,11 +498,101 @@ def run_prefill(a):
     print(json.dumps(res), flush=True)
 
 
+# single-matrix LUT GEMV/GEMM sweep, N x K of the MoE
+# projections, M tokens, Format B b bits and table block g.
+SWEEP_NK = [(1408, 2048), (2048, 1408), (768, 2048), (2048, 768), (5632, 2048)]
+SWEEP_METRIC = "LUT GEMV/GEMM kernel sweep: fraction of the attainable roofline (geometric mean)"
+
+
+def run_sweep(a):
+    """Config 5: y = x W^T through blut_matmul (LUTLinear) for every (N x K,
+    M, b, g).  Each case is timed as a CUDA graph of its four launches, L2
+    flushed (a 256 MB write) before every timed call; attainable time =
+    max(bytes / HBM peak, 2MNK / bf16 peak) with bytes = N K bpe + 2 M K +
+    2 M N; frac = attainable / measured."""
+    import torch
+    from block_lut_b200.formats import LUTFormat, QuantizedMatrix
+    from block_lut_b200.linear import LUTLinear
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    bw, _ = peaks()
+    pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    tf = pk.get("bf16_tflops", 1590.0)
+    bits_l = [int(v) for v in a.sweep_bits.split(",")]
+    groups_l = [int(v) for v in a.sweep_groups.split(",")]
+    ms_l = [int(v) for v in a.sweep_m.split(",")]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    rows, fracs, launches = [], [], 0
+    reps = max(3, a.steps)
+    clk = Clocks(0)
+    for (n, k) in SWEEP_NK:
+        for b in bits_l:
+            for grp in groups_l:
+                fmt = LUTFormat("b", b, grp)
+                codes = torch.randint(0, 256, (n, k * b // 8), generator=g, device=dev, dtype=torch.uint8)
+                tables = torch.sort((torch.randn(n, k // grp, 1 << b, generator=g, device=dev) * 0.02).half(),
+                                    dim=-1).values.contiguous()
+                lin = LUTLinear(QuantizedMatrix(fmt, n, k, codes, tables))
+                for m in ms_l:
+                    x = torch.randn(m, k, generator=g, device=dev).half()
+                    out = torch.empty(m, n, dtype=torch.float16, device=dev)
+                    for _ in range(2):
+                        lin(x, out=out)
+                    s_ = torch.cuda.Stream()
+                    s_.wait_stream(torch.cuda.current_stream())
+                    with torch.cuda.stream(s_):
+                        lin(x, out=out)
+                    torch.cuda.current_stream().wait_stream(s_)
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph):
+                        lin(x, out=out)
+                    ts = []
+                    for _ in range(reps):
+                        flush.fill_(1)
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record()
+                        graph.replay()
+                        e1.record()
+                        torch.cuda.synchronize()
+                        ts.append(e0.elapsed_time(e1) / 1e3)
+                    launches += reps * lin.launch_count(m)
+                    t = statistics.median(ts)
+                    byt = n * k * fmt.bytes_per_weight() + 2 * m * k + 2 * m * n
+                    fl = 2.0 * m * n * k
+                    t_att = max(byt / (bw * 1e9), fl / (tf * 1e12))
+                    frac = t_att / t
+                    fracs.append(frac)
+                    rows.append([n, k, m, b, grp, round(t * 1e6, 2), round(byt / t / 1e9, 1),
+                                 round(fl / t / 1e12, 2), "hbm" if byt / (bw * 1e9) >= fl / (tf * 1e12) else "tensor",
+                                 round(frac, 3)])
+                    del graph
+                lin.check_status()
+    clocks = clk.stop()
+    geo = float(np.exp(np.mean(np.log(np.maximum(fracs, 1e-9)))))
+    res = {"metric": SWEEP_METRIC, "value": geo, "unit": "fraction", "n_gpus": 1, "steps": reps,
+           "warmup": 2, "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "f16", "data": "synthetic random codes and sorted random fp16 tables; N(0,1) fp16 tokens",
+           "config": {"workload": "config 5 single-matrix LUT GEMV/GEMM sweep (blut_matmul, tcgen05 path)",
+                      "nk": SWEEP_NK, "m": ms_l, "bits": bits_l, "groups": groups_l,
+                      "l2": "256 MB write before every timed call",
+                      "timing": "median of the per-call CUDA-event times of a CUDA graph of the call's 4 launches"},
+           "roofline": {"kernel": "blut_matmul (plan + gather + tc_mm_kernel + reduce)", "bound": "per case",
+                        "peak_hbm_gbs": bw, "peak_bf16_tflops": tf,
+                        "frac_min": min(fracs), "frac_max": max(fracs), "traffic": None},
+           "sweep_columns": ["N", "K", "M", "bits", "group", "us", "GB/s", "TFLOP/s", "bound", "frac"],
+           "sweep": rows, "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}
+    print(json.dumps(res), flush=True)
+
+
 if __name__ == "__main__":
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
