@@ -52,8 +52,10 @@ template <int MT>
 constexpr int tc_threads() {
   return 32 * (2 + kTcDecodeWarps * tc_sets<MT>());
 }
-constexpr int kTcRingBudget = 96 * 1024;        // per CTA, two CTAs per SM (MT = 32)
+constexpr int kTcRingBudget = 104 * 1024;       // per CTA, two CTAs per SM (MT = 32)
 constexpr int kTcRingBudgetWide = 200 * 1024;   // one CTA per SM (MT = 128)
+constexpr int kTcMaxStages = 16;                // barrier slots per ring
+constexpr int kTcHeader = 1024;                 // barriers, queue and flags before the rings
 constexpr int kTcQueue = 4;          // depth of the shared-memory item queue
 // Token groups hold up to MT tokens: MT = 32 for decode (two CTAs per SM,
 // 256 tensor-memory columns each) and MT = 128 for prefill (one CTA per SM,
@@ -487,10 +489,10 @@ __host__ __device__ constexpr int tc_xstage_bytes() {
   return Dec::kDense ? 0 : (MT / kNTile) * Dec::KB * 16;
 }
 
-// Barriers, queue and flags take the first 512 bytes, the rings follow.
+// Barriers, queue and flags take the first kTcHeader bytes, the rings follow.
 template <class Dec, int MT>
 __host__ inline int tc_smem_bytes(const TcParams& p) {
-  return 512 + p.stages * tc_stage_bytes<Dec, MT>(p) + p.xstages * tc_xstage_bytes<Dec, MT>();
+  return kTcHeader + p.stages * tc_stage_bytes<Dec, MT>(p) + p.xstages * tc_xstage_bytes<Dec, MT>();
 }
 
 template <class Dec, int MT>
@@ -505,21 +507,21 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
   constexpr int kTcASlots = tc_aslots<MT>();
   constexpr int kEpiWarps = kTcDecodeWarps * kSets;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [8]
-  uint64_t* empty = full + 8;                          // [8]
-  uint64_t* afull = full + 16;                         // [kTcASlots <= 8] A slot written (decode warps)
-  uint64_t* aempty = full + 24;                        // [kTcASlots] A slot read (MMA commit)
-  uint64_t* dfull = full + 32;                         // [kDBufs] accumulators complete (MMA commit)
-  uint64_t* dempty = full + 34;                        // [kDBufs] accumulators read (epilogue warps)
-  uint64_t* qfull = full + 36;                         // [kTcQueue] item posted
-  uint64_t* qempty = full + 40;                        // [kTcQueue] item taken by every role
-  uint64_t* fin = full + 44;                           // last MMAs complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 45);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 46);
-  volatile int* qitem = reinterpret_cast<volatile int*>(full + 47);  // [kTcQueue]
-  uint64_t* xfull = full + 49;                         // [4] activation stage loaded (LUT formats)
-  uint64_t* xempty = full + 53;                        // [4] activation stage read (MMA commit)
-  uint8_t* ring = smem + 512;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [kTcMaxStages] weight stage loaded
+  uint64_t* empty = full + 16;                         // [kTcMaxStages] weight stage read
+  uint64_t* afull = full + 32;                         // [kTcASlots <= 8] A slot written (decode warps)
+  uint64_t* aempty = full + 40;                        // [kTcASlots] A slot read (MMA commit)
+  uint64_t* dfull = full + 48;                         // [kDBufs] accumulators complete (MMA commit)
+  uint64_t* dempty = full + 50;                        // [kDBufs] accumulators read (epilogue warps)
+  uint64_t* qfull = full + 52;                         // [kTcQueue] item posted
+  uint64_t* qempty = full + 56;                        // [kTcQueue] item taken by every role
+  uint64_t* fin = full + 60;                           // last MMAs complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 61);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 62);
+  volatile int* qitem = reinterpret_cast<volatile int*>(full + 63);  // [kTcQueue]
+  uint64_t* xfull = full + 66;                         // [kTcMaxStages] activation stage loaded (LUT formats)
+  uint64_t* xempty = full + 82;                        // [kTcMaxStages] activation stage read (MMA commit)
+  uint8_t* ring = smem + kTcHeader;                    // barriers end at full + 98 (784 bytes)
   const int S = p.stages, SX = p.xstages;
   const int stage_bytes = tc_stage_bytes<Dec, MT>(p);
   constexpr int xstage_bytes = tc_xstage_bytes<Dec, MT>();
@@ -874,8 +876,14 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
   const int budget = tc_ctas_per_sm<MT>() == 3 ? 72 * 1024 : tc_ctas_per_sm<MT>() == 2 ? kTcRingBudget : kTcRingBudgetWide;
   const int stage = tc_stage_bytes<Dec, MT>(p);
   const int xstage = tc_xstage_bytes<Dec, MT>();
-  p.xstages = xstage ? std::max(2, std::min(4, (budget / 6) / xstage)) : 0;
-  p.stages = std::max(2, std::min(8, (budget - p.xstages * xstage) / stage));
+  // LUT formats: as many activation stages as weight stages.  The producer
+  // issues a block's activations right after its weights and an activation
+  // stage is freed only by the block's MMAs, so the activation ring bounds
+  // the weight bytes in flight; with small (2- and 3-bit) weight stages a
+  // shallow activation ring would starve the loads.
+  const int depth = std::min(kTcMaxStages, budget / (stage + xstage));
+  p.stages = std::max(2, depth);
+  p.xstages = xstage ? p.stages : 0;
   const int smem = tc_smem_bytes<Dec, MT>(p);
   auto kern = tc_mm_kernel<Dec, MT>;
   static std::mutex mu;
