@@ -59,10 +59,13 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=None, help="decode tokens per rank (workload default)")
     p.add_argument("--layers", type=int, default=None, help="MoE layers (workload default)")
-    p.add_argument("--kind", choices=["b", "nested"], default=None, help="expert format (workload default)")
+    p.add_argument("--kind", choices=["b", "nested", "r8"], default=None,
+                   help="expert format (workload default): Format B, NestedLUT, or the reference's Format R")
     p.add_argument("--bits", type=int, default=4, help="Format B code bits")
     p.add_argument("--group", type=int, default=64)
-    p.add_argument("--tier", type=int, default=0, help="NestedLUT tier: 0 full, 1 coarse only")
+    p.add_argument("--tier", type=int, default=0, help="NestedLUT tier (0 full, 1 coarse only) or Format R tier")
+    p.add_argument("--path", choices=["auto", "tc", "mma"], default="auto",
+                   help="matmul path of the experts: tcgen05 where the format has it (auto), or forced")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--workload", choices=["decode", "qwen3", "prefill", "sweep"], default="decode",
@@ -81,10 +84,19 @@ def parse():
 
 def bench_format(a):
     from block_lut_b200.formats import LUTFormat
+    if a.kind == "r8":
+        return LUTFormat("r8", 8, 128, a.tier)
     return LUTFormat("nested", 4, a.group, a.tier) if a.kind == "nested" else LUTFormat("b", a.bits, a.group)
 
 
+def bench_path(a):
+    return None if a.path == "auto" else a.path == "tc"
+
+
 def format_name(fmt):
+    if fmt.kind == "r8":
+        return f"Format R (reference BlockLUT): uint8 index, bf16 256-entry table (tier {fmt.tier}), " \
+               "bf16 absmax per 128 weights"
     if fmt.kind == "nested":
         return f"NestedLUT 2+2 g{fmt.group} {'coarse-only' if fmt.tier == 1 else 'full'} tier fp16 tables"
     return f"BlockLUT {fmt.bits}-bit g{fmt.group} fp16 tables"
@@ -145,14 +157,24 @@ class Clocks:
 
 
 # ------------------------------------------------------------ workload ---
-def build_layers(n_layers, experts_local, e0, fmt, device, seed=0, shape=None):
+def build_layers(n_layers, experts_local, e0, fmt, device, seed=0, shape=None, tc=None):
     """Synthetic MoE layers (experts [e0, e0 + experts_local) of each) in
     format `fmt`; shape {H, E, I, IS} defaults to Qwen1.5-MoE-A2.7B's (IS 0:
     no shared expert)."""
     import torch
-    from block_lut_b200.formats import encode
+    from block_lut_b200.formats import QuantizedMatrix, encode, encode_r
     from block_lut_b200.moe import LUTExperts, SharedExpert
     H, E, I, IS = (shape or QWEN)["H"], (shape or QWEN)["E"], (shape or QWEN)["I"], (shape or QWEN)["IS"]
+    dt = fmt.compute_dtype
+    # Format R: one 256-entry table for every matrix (evenly spaced over the
+    # absmax-normalised range [-1, 1]), uint8 nearest-entry indices
+    cb = torch.linspace(-1.0, 1.0, 256, device=device).to(torch.bfloat16)
+
+    def quantise(w, rows, cols):
+        if fmt.kind == "r8":
+            idx, am = encode_r(w, cb)
+            return QuantizedMatrix(fmt, rows, cols, idx, cb, scales=am)
+        return encode(w, fmt)
 
     torch.manual_seed(seed)
     st = torch.distributions.StudentT(torch.tensor(5.0, device=device))
@@ -164,29 +186,30 @@ def build_layers(n_layers, experts_local, e0, fmt, device, seed=0, shape=None):
         for e in range(E):
             if e0 <= e < e0 + experts_local:
                 torch.manual_seed(seed * 100000 + li * 100 + e)
-                q13.append(encode(st.sample((2 * I, H)) * scale, fmt))
-                q2.append(encode(st.sample((H, I)) * scale, fmt))
-        experts = LUTExperts.from_quantized(q13, q2)
+                q13.append(quantise(st.sample((2 * I, H)) * scale, 2 * I, H))
+                q2.append(quantise(st.sample((H, I)) * scale, H, I))
+        experts = LUTExperts.from_quantized(q13, q2, tc=tc)
         del q13, q2
-        router_w = (torch.randn(E + 1, H, generator=gen, device=device) * 0.02).half()
+        router_w = (torch.randn(E + 1, H, generator=gen, device=device) * 0.02).to(dt)
         shared = None
         if IS > 0:
-            s13 = (torch.randn(2 * IS, H, generator=gen, device=device) * 0.02).half()
-            s2 = (torch.randn(H, IS, generator=gen, device=device) * 0.02).half()
+            s13 = (torch.randn(2 * IS, H, generator=gen, device=device) * 0.02).to(dt)
+            s2 = (torch.randn(H, IS, generator=gen, device=device) * 0.02).to(dt)
             shared = SharedExpert.from_dense(s13, s2)
         layers.append((experts, router_w, shared))
     torch.cuda.synchronize()
     return fmt, layers
 
 
-def make_inputs(n_layers, batch, rank, device, hidden=H):
+def make_inputs(n_layers, batch, rank, device, hidden=H, dtype=None):
     import torch
+    dtype = dtype or torch.float16
     g = torch.Generator(device=device).manual_seed(7 + rank)
     xs = []
     for _ in range(n_layers):
         x = torch.randn(batch, hidden, generator=g, device=device)
         x = x / x.pow(2).mean(dim=1, keepdim=True).sqrt()
-        xs.append(x.half().contiguous())
+        xs.append(x.to(dtype).contiguous())
     return xs
 
 
@@ -205,6 +228,12 @@ def cpu_sample(threads, batch, fmt, shape=None, seed=0):
                        axis=-1)
 
     def mats(rows, cols):
+        if fmt.kind == "r8":
+            table = O.f32_to_bf16(np.linspace(-1.0, 1.0, 256).astype(np.float32))
+            idx = rng.integers(0, 256, size=(e_, rows * cols), dtype=np.uint8)
+            am = O.f32_to_bf16(rng.uniform(0.02, 0.08, (e_, rows * cols // 128)).astype(np.float32))
+            return lambda e: O.bf16_to_f32(O.dequant_r(idx[e], am[e], table, 128, fmt.tier)).reshape(  # noqa: E731
+                rows, cols)
         if fmt.kind == "nested":
             cc = rng.integers(0, 256, size=(e_, rows, cols // 4), dtype=np.uint8)
             cr = rng.integers(0, 256, size=(e_, rows, cols // 4), dtype=np.uint8)
@@ -222,12 +251,15 @@ def cpu_sample(threads, batch, fmt, shape=None, seed=0):
         s13 = (rng.standard_normal((2 * is_, h_)) * 0.02).astype(np.float32)
         s2 = (rng.standard_normal((h_, is_)) * 0.02).astype(np.float32)
         sg = (rng.standard_normal(h_) * 0.02).astype(np.float32)
+    act = "bf16" if fmt.kind == "r8" else "f16"
+    if act == "bf16":
+        x = O.bf16_to_f32(O.f32_to_bf16(x.astype(np.float32)))
     t0 = time.perf_counter()
-    out = O.moe_forward_threaded(x, ids, tw, g13, g2, "f16", threads)
+    out = O.moe_forward_threaded(x, ids, tw, g13, g2, act, threads)
     if is_ > 0:
         xs = x.astype(np.float64)
         h = xs @ s13.T
-        a = O.round_to((O.silu(h[:, :is_]) * h[:, is_:]).astype(np.float32), "f16").astype(np.float64)
+        a = O.round_to((O.silu(h[:, :is_]) * h[:, is_:]).astype(np.float32), act).astype(np.float64)
         out += (1 / (1 + np.exp(-(xs @ sg))))[:, None] * (a @ s2.T)
     dt = time.perf_counter() - t0
     n_active = len(np.unique(ids))
@@ -255,10 +287,10 @@ def run_ours(a):
 
     W = a.shape
     Hh, Ee, Ii, ISs, K = W["H"], W["E"], W["I"], W["IS"], W["TOPK"]
-    fmt, layers = build_layers(a.layers, Ee, 0, bench_format(a), dev, shape=W)
+    fmt, layers = build_layers(a.layers, Ee, 0, bench_format(a), dev, shape=W, tc=bench_path(a))
     moes = [LUTMoELayer(ex, K, router_w=rw if sh is not None else rw[:Ee].contiguous(), renorm=W["RENORM"],
                         shared=sh, shared_gate_mode=1) for ex, rw, sh in layers]
-    xs = make_inputs(a.layers, a.batch, rank, dev, Hh)
+    xs = make_inputs(a.layers, a.batch, rank, dev, Hh, fmt.compute_dtype)
     outs = [torch.empty_like(x) for x in xs]
 
     def step():
@@ -362,8 +394,9 @@ def run_ours(a):
     res = {
         "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU Lloyd-encoded; N(0,1) RMS-normalised fp16 tokens",
+        "vs_baseline": None, "dtype": "bf16" if fmt.kind == "r8" else "f16",
+        "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU-encoded (Lloyd tables, or Format R nearest "
+                "entry of an evenly spaced table); N(0,1) RMS-normalised tokens",
         "config": {"workload": f"{W['NAME']}, decode batch {a.batch}", "layers": a.layers,
                    "global_batch": a.batch, "experts": Ee, "top_k": K, "renorm": W["RENORM"], "hidden": Hh,
                    "inter": Ii, "shared_inter": ISs, "format": format_name(fmt),

@@ -131,12 +131,12 @@ def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, 
     for ex, rw, _ in layers:
         shared = None
         if IS > 0:
-            s13 = (torch.randn(2 * IS, H, generator=g, device=dev) * 0.02).half()
-            s2 = (torch.randn(H, IS, generator=g, device=dev) * 0.02).half()
+            s13 = (torch.randn(2 * IS, H, generator=g, device=dev) * 0.02).to(fmt.compute_dtype)
+            s2 = (torch.randn(H, IS, generator=g, device=dev) * 0.02).to(fmt.compute_dtype)
             shared = (s13, s2)
         eps.append(EPMoELayer(ex, E, TOPK, rw if shared is not None else rw[:E].contiguous(),
                               shared=shared, renorm=shp["RENORM"]))
-    xs = make_inputs(a.layers, a.batch, rank, dev, H)
+    xs = make_inputs(a.layers, a.batch, rank, dev, H, fmt.compute_dtype)
 
     outs = [None] * len(eps)
 
@@ -212,7 +212,7 @@ def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, 
     if rank == 0:
         res = {"metric": metric, "value": total_tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
                "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
-               "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+               "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if fmt.kind == "r8" else "f16",
                "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU Lloyd-encoded; N(0,1) RMS-normalised fp16",
                "config": {"workload": f"{shp['NAME']}, decode batch {a.batch} per rank",
                           "layers": a.layers, "global_batch": total_tokens, "experts": E, "top_k": TOPK,
