@@ -84,7 +84,9 @@ __host__ __device__ inline int64_t align256(int64_t x) { return (x + 255) & ~int
 // B 4-bit: codes4 + tables.  B 3-bit: codes2 (low bits) + codes1 + tables.
 // B 2-bit: codes2 + tables.  NESTED: coarse codes2 + coarse tables +
 // residual codes2 + combined tables (the full tier reads planes 0, 2, 3,
-// the coarse tier planes 0, 1).
+// the coarse tier planes 0, 1).  R8 (blocks of 64 columns): codes8, the
+// row's uint8 indices of the block, + scales, the bf16 absmax of the
+// 128-weight block holding these 64 columns (stored once per 64 columns).
 // ------------------------------------------------------------------------
 constexpr int kTcRows = 128;
 
@@ -96,7 +98,7 @@ __host__ __device__ inline int tc_pos(int bpr, int row, int o) {
 // Columns per block: dense 32 (two k16 MMA slabs per pipeline stage), LUT
 // formats max(64, group) so that a block holds whole tables.
 __host__ __device__ inline int tc_block_cols(int format, int group) {
-  return format == BLUT_FMT_DENSE ? 32 : (group > 64 ? group : 64);
+  return format == BLUT_FMT_DENSE ? 32 : format == BLUT_FMT_R8 ? 64 : (group > 64 ? group : 64);
 }
 
 __host__ inline bool make_tc_layout(const blut_mat_desc& d, TiledLayout& L) {
@@ -139,6 +141,11 @@ __host__ inline bool make_tc_layout(const blut_mat_desc& d, TiledLayout& L) {
       add(kPlaneTables, (L.kb / d.group) * 8, 4);      // coarse tables
       add(kPlaneCodes2, L.kb / 4, 0);                  // residual codes
       add(kPlaneCombined, (L.kb / d.group) * 32, 16);  // combined tables
+      break;
+    case BLUT_FMT_R8:  // absmax blocks of 128 weights lie in one row when cols % 128 == 0
+      if (d.group != 128 || d.dtype != BLUT_BF16 || d.cols % 128) return false;
+      add(kPlaneCodes8, L.kb, 0);
+      add(kPlaneScales, 2, 0);
       break;
     case BLUT_FMT_DENSE:
       if (d.dtype != BLUT_F16 && d.dtype != BLUT_BF16) return false;

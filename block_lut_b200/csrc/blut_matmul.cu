@@ -228,6 +228,7 @@ int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const v
     t.y_sstride = m * N;
     t.counter = ws.counter;
     t.status = ws.status;
+    t.r8_table = static_cast<const uint16_t*>(lut_table);
     t.ks = p.ks;
     t.bps = p.bps;
     if (launch_tc_mm(d, t, p.gtok, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;

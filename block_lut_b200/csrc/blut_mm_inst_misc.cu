@@ -35,7 +35,7 @@ namespace blut {
 
 int dequant_tiled(const blut_mat_desc& d, const void* tiled, const void* table, void* out, cudaStream_t stream) {
   if (!tiled || !out) return BLUT_ERR_INVALID;
-  if (d.layout & BLUT_LAYOUT_TC) return dequant_tiled_tc(d, tiled, out, stream);
+  if (d.layout & BLUT_LAYOUT_TC) return dequant_tiled_tc(d, tiled, table, out, stream);
   MMParams p{};
   if (!mm_planes(d, false, p)) return BLUT_ERR_UNSUPPORTED;
   if (d.format == BLUT_FMT_R8 && !table) return BLUT_ERR_INVALID;

@@ -734,6 +734,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.y_ld = H;
       t.counter = ws.pp.counters + counter;
       t.status = ws.status;
+      t.r8_table = (const uint16_t*)a.lut_table;
       t.ks = ws.split.ks[counter];
       t.bps = ws.split.bps[counter];
       t.part = part;

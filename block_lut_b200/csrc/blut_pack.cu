@@ -287,6 +287,14 @@ __global__ void pack_tc_kernel(PackArgs a, int plane) {
         v = uint8_t(acc);
         break;
       }
+      case kPlaneCodes8:  // FMT_R8 indices, row-major canonical
+        v = a.codes[r * a.cols + blk * L.kb + o];
+        break;
+      case kPlaneScales: {  // FMT_R8 absmax of the 128-weight block holding columns blk * kb ..
+        const uint16_t e = a.scales[(r * a.cols + blk * L.kb) / 128];
+        v = o ? uint8_t(e >> 8) : uint8_t(e & 0xFF);
+        break;
+      }
       case kPlaneCombined: {  // entry e = 4c + r: fp16(coarse[c] + refine[c][r])
         const int m = o / 32, wb = o % 32, e = wb % 16;
         const int64_t tb = r * (a.cols / a.group) + blk * (L.kb / a.group) + m;

@@ -82,9 +82,12 @@ struct TcMul {
   uint32_t k31, k30, k28, k26, k16;  // mul.hi by 2^n: right shift by 32 - n
   uint32_t k4, k2;                   // mul.lo by 4, 2: left shift by 2, 1
   uint32_t k11, k11h;                // 0x11, 0x110000: selector nibble doubling (tc_lut4x4)
+  uint32_t k128;                     // bytes between table entries of one lane (TcDecR8)
+  uint32_t r8mask;                   // FMT_R8 tier mask of four indices (0xFFFFFFFF, 0x3F3F3F3F, 0x0F0F0F0F)
 };
-__host__ inline TcMul tc_mul_consts() {
-  return TcMul{1u << 31, 1u << 30, 1u << 28, 1u << 26, 1u << 16, 4u, 2u, 0x11u, 0x110000u};
+__host__ inline TcMul tc_mul_consts(int r8_tier = 0) {
+  return TcMul{1u << 31, 1u << 30, 1u << 28, 1u << 26, 1u << 16, 4u, 2u, 0x11u, 0x110000u, 128u,
+               r8_tier == 1 ? 0x3F3F3F3Fu : r8_tier == 2 ? 0x0F0F0F0Fu : 0xFFFFFFFFu};
 }
 
 struct TcParams {
@@ -114,6 +117,7 @@ struct TcParams {
   float* part;
   int* counter;            // item counter (zeroed by the plan kernel)
   TcMul mul;               // tc_mul_consts()
+  const uint16_t* r8_table;  // FMT_R8: the tier's bf16 [256] table
   int* status;
   int stages;              // weight stages (LUT formats) or weight + activation stages (dense)
   int xstages;             // activation stages (LUT formats)
@@ -242,9 +246,12 @@ __device__ __forceinline__ uint32_t tc_mullo(uint32_t a, uint32_t b) {
   return d;
 }
 
-// Per-stage pointers to this tile's piece of each plane the decode reads.
+// Per-stage pointers to this tile's piece of each plane the decode reads;
+// tab is the shared-memory address of this lane's column of the replicated
+// FMT_R8 table.
 struct TcPtrs {
   const uint8_t* p[3];
+  uint32_t tab;
 };
 
 // 16-entry tables (4-bit codes): `w` holds 8 codes, one per nibble.  Permutes
@@ -315,6 +322,7 @@ template <int G>
 struct TcDecB4 {
   static constexpr bool kDense = false;
   static constexpr bool kBF16 = false;
+  static constexpr bool kR8 = false;
   static constexpr int KB = G > 64 ? G : 64;  // columns per block
   static constexpr int kHalves = KB / 64;     // 64-column halves per block
   static constexpr int kNumPlanes = 2;
@@ -346,6 +354,7 @@ template <int G>
 struct TcDecB2 {
   static constexpr bool kDense = false;
   static constexpr bool kBF16 = false;
+  static constexpr bool kR8 = false;
   static constexpr int KB = G > 64 ? G : 64;
   static constexpr int kHalves = KB / 64;
   static constexpr int kNumPlanes = 2;
@@ -376,6 +385,7 @@ template <int G>
 struct TcDecB3 {
   static constexpr bool kDense = false;
   static constexpr bool kBF16 = false;
+  static constexpr bool kR8 = false;
   static constexpr int KB = G > 64 ? G : 64;
   static constexpr int kHalves = KB / 64;
   static constexpr int kNumPlanes = 3;
@@ -413,6 +423,7 @@ template <int G>
 struct TcDecNested {
   static constexpr bool kDense = false;
   static constexpr bool kBF16 = false;
+  static constexpr bool kR8 = false;
   static constexpr int KB = G > 64 ? G : 64;
   static constexpr int kHalves = KB / 64;
   static constexpr int kNumPlanes = 3;
@@ -444,11 +455,83 @@ struct TcDecNested {
   }
 };
 
+// FMT_R8, the reference's BlockLUT: uint8 indices into one 256-entry bf16
+// table (masked to the tier's 64 or 16 entries), times the bf16 absmax of
+// the weight's 128-weight block.  The table sits in shared memory once per
+// CTA, replicated across the 32 banks (entry e of lane l at word 32 e + l),
+// so the 32 lanes' lookups never conflict.  Each looked-up pair is scaled by
+// one bf16x2 multiply: the product of two bf16 values is exact in fp32, so
+// its single rounding to nearest even equals bf16(f32(table) * f32(absmax)).
+// Planes: codes8, scales (blocks of 64 columns).
+__device__ __forceinline__ uint32_t tc_lds32(uint32_t addr) {
+  uint32_t v;
+  asm("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t tc_mad(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t tc_bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+constexpr int kTcR8TableBytes = 256 * 32 * 4;
+
+struct TcDecR8 {
+  static constexpr bool kDense = false;
+  static constexpr bool kBF16 = true;
+  static constexpr bool kR8 = true;
+  static constexpr int KB = 64;
+  static constexpr int kHalves = 1;
+  static constexpr int kNumPlanes = 2;
+  struct Half {
+    uint4 c[4];
+    uint32_t s2, tab;
+  };
+  __device__ __forceinline__ static void load_half(const TcPtrs& pp, int row, int, Half& d) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) d.c[u] = tc_lds128(pp.p[0] + (u * kTcRows + row) * 16);
+    const uint32_t s = *reinterpret_cast<const uint16_t*>(pp.p[1] + row * 2);
+    d.s2 = s | (s << 16);
+    d.tab = pp.tab;
+  }
+  // four weights of index word w into out[0..1]
+  __device__ __forceinline__ static void run4(uint32_t w, uint32_t s2, uint32_t tab, uint32_t* out,
+                                              const TcMul& m) {
+    w &= m.r8mask;
+    const uint32_t v0 = tc_lds32(tc_mad(prmt(w, 0u, 0x4440u), m.k128, tab));
+    const uint32_t v1 = tc_lds32(tc_mad(prmt(w, 0u, 0x4441u), m.k128, tab));
+    const uint32_t v2 = tc_lds32(tc_mad(prmt(w, 0u, 0x4442u), m.k128, tab));
+    const uint32_t v3 = tc_lds32(tc_mad(prmt(w, 0u, 0x4443u), m.k128, tab));
+    out[0] = tc_bmul2(prmt(v0, v1, 0x5410u), s2);
+    out[1] = tc_bmul2(prmt(v2, v3, 0x5410u), s2);
+  }
+  __device__ __forceinline__ static void lookup_q(const Half& d, int qq, uint32_t (&out)[16], const TcMul& m) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint4& c = d.c[2 * qq + u];
+      run4(c.x, d.s2, d.tab, out + 8 * u + 0, m);
+      run4(c.y, d.s2, d.tab, out + 8 * u + 2, m);
+      run4(c.z, d.s2, d.tab, out + 8 * u + 4, m);
+      run4(c.w, d.s2, d.tab, out + 8 * u + 6, m);
+    }
+  }
+};
+
+// Fills the replicated FMT_R8 table (entry e of lane l at word 32 e + l).
+__device__ __forceinline__ void tc_fill_r8_table(uint32_t* tab, const uint16_t* __restrict__ src) {
+  for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) tab[i] = src[i >> 5];
+}
+
 // Dense fp16 / bf16 weights: the MMA reads them from shared memory.
 template <bool BF16>
 struct TcDecDense {
   static constexpr bool kDense = true;
   static constexpr bool kBF16 = BF16;
+  static constexpr bool kR8 = false;
   static constexpr int KB = 32;
   static constexpr int kHalves = 0;
   static constexpr int kNumPlanes = 1;
@@ -489,10 +572,16 @@ __host__ __device__ constexpr int tc_xstage_bytes() {
   return Dec::kDense ? 0 : (MT / kNTile) * Dec::KB * 16;
 }
 
-// Barriers, queue and flags take the first kTcHeader bytes, the rings follow.
+// Barriers, queue and flags take the first kTcHeader bytes, then the FMT_R8
+// table (TcDecR8 only), then the rings.
+template <class Dec>
+__host__ __device__ constexpr int tc_table_bytes() {
+  return Dec::kR8 ? kTcR8TableBytes : 0;
+}
 template <class Dec, int MT>
 __host__ inline int tc_smem_bytes(const TcParams& p) {
-  return kTcHeader + p.stages * tc_stage_bytes<Dec, MT>(p) + p.xstages * tc_xstage_bytes<Dec, MT>();
+  return kTcHeader + tc_table_bytes<Dec>() + p.stages * tc_stage_bytes<Dec, MT>(p) +
+         p.xstages * tc_xstage_bytes<Dec, MT>();
 }
 
 template <class Dec, int MT>
@@ -521,7 +610,8 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
   volatile int* qitem = reinterpret_cast<volatile int*>(full + 63);  // [kTcQueue]
   uint64_t* xfull = full + 66;                         // [kTcMaxStages] activation stage loaded (LUT formats)
   uint64_t* xempty = full + 82;                        // [kTcMaxStages] activation stage read (MMA commit)
-  uint8_t* ring = smem + kTcHeader;                    // barriers end at full + 98 (784 bytes)
+  uint32_t* r8tab = reinterpret_cast<uint32_t*>(smem + kTcHeader);  // barriers end at full + 98 (784 bytes)
+  uint8_t* ring = smem + kTcHeader + tc_table_bytes<Dec>();
   const int S = p.stages, SX = p.xstages;
   const int stage_bytes = tc_stage_bytes<Dec, MT>(p);
   constexpr int xstage_bytes = tc_xstage_bytes<Dec, MT>();
@@ -557,6 +647,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if constexpr (Dec::kR8) tc_fill_r8_table(r8tab, p.r8_table);
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kCols));
@@ -743,6 +834,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
           TcPtrs pp;
 #pragma unroll
           for (int k = 0; k < 3; ++k) pp.p[k] = st + qoff[k] + t * p.piece[k];
+          pp.tab = smem_u32(r8tab) + lane * 4;
 #pragma unroll
           for (int h = 0; h < Dec::kHalves; ++h, ra.next(kTcASlots)) {
             const int j = ra.i;
@@ -873,7 +965,9 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
 // CTA per resident slot.
 template <class Dec, int MT>
 inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
-  const int budget = tc_ctas_per_sm<MT>() == 3 ? 72 * 1024 : tc_ctas_per_sm<MT>() == 2 ? kTcRingBudget : kTcRingBudgetWide;
+  const int budget = (tc_ctas_per_sm<MT>() == 3 ? 72 * 1024 : tc_ctas_per_sm<MT>() == 2 ? kTcRingBudget
+                                                                                        : kTcRingBudgetWide) -
+                     tc_table_bytes<Dec>();
   const int stage = tc_stage_bytes<Dec, MT>(p);
   const int xstage = tc_xstage_bytes<Dec, MT>();
   // LUT formats: as many activation stages as weight stages.  The producer
@@ -927,6 +1021,7 @@ struct TcDequantArgs {
   int paired;
   uint16_t* out;
   TcMul mul;
+  const uint16_t* r8_table;
 };
 
 template <class Dec>
@@ -937,6 +1032,13 @@ __global__ void __launch_bounds__(kTcRows) tc_dequant_kernel(const TcDequantArgs
   TcPtrs pp;
 #pragma unroll
   for (int k = 0; k < 3; ++k) pp.p[k] = a.w + a.off[k] + ((int64_t)b * a.ntiles + pt) * a.piece[k];
+  pp.tab = 0;
+  if constexpr (Dec::kR8) {
+    __shared__ uint32_t tab[256 * 32];
+    tc_fill_r8_table(tab, a.r8_table);
+    __syncthreads();
+    pp.tab = smem_u32(tab) + (threadIdx.x & 31) * 4;
+  }
   if constexpr (Dec::kDense) {
 #pragma unroll
     for (int u = 0; u < Dec::KB / 8; ++u)
@@ -989,8 +1091,10 @@ inline cudaError_t tc_dequant_family(int group, const TcDequantArgs& a, int64_t 
 cudaError_t launch_tc_b2(int group, int group_tokens, const TcParams& p, int sms, cudaStream_t stream);
 cudaError_t launch_tc_b3(int group, int group_tokens, const TcParams& p, int sms, cudaStream_t stream);
 cudaError_t launch_tc_nested(int group, int group_tokens, const TcParams& p, int sms, cudaStream_t stream);
+cudaError_t launch_tc_r8(int group_tokens, const TcParams& p, int sms, cudaStream_t stream);
 cudaError_t dequant_tc_b2(int group, const TcDequantArgs& a, int64_t nblocks, cudaStream_t stream);
 cudaError_t dequant_tc_b3(int group, const TcDequantArgs& a, int64_t nblocks, cudaStream_t stream);
 cudaError_t dequant_tc_nested(int group, const TcDequantArgs& a, int64_t nblocks, cudaStream_t stream);
+cudaError_t dequant_tc_r8(const TcDequantArgs& a, int64_t nblocks, cudaStream_t stream);
 
 }  // namespace blut

@@ -1,8 +1,8 @@
 // Instantiations of the tcgen05 LUT matmul for FMT_B 4-bit and dense
 // weights, the dispatch over every format of the TC layout, and the
 // diagnostic dequantisation of that layout through the same decode.  The
-// 2-bit, 3-bit and NestedLUT families are instantiated in their own
-// translation units (blut_tc_inst_{b2,b3,nested}.cu).
+// 2-bit, 3-bit, NestedLUT and FMT_R8 families are instantiated in their own
+// translation units (blut_tc_inst_{b2,b3,nested,r8}.cu).
 #include "blut_internal.h"
 #include "blut_tc.cuh"
 
@@ -24,7 +24,7 @@ bool tc_planes(const blut_mat_desc& d, bool pair, TcParams& p) {
   p.nblocks = (int)L.nchunks;
   p.units = (p.ntiles + 1) / 2;
   p.pair = pair ? 1 : 0;
-  p.mul = tc_mul_consts();
+  p.mul = tc_mul_consts(d.format == BLUT_FMT_R8 ? d.tier : 0);
   return true;
 }
 
@@ -47,11 +47,14 @@ cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int group_to
     case BLUT_FMT_NESTED:  // the coarse tier is a 2-bit lookup of planes 0, 1
       return d.tier == 1 ? launch_tc_b2(d.group, group_tokens, p, sms, stream)
                          : launch_tc_nested(d.group, group_tokens, p, sms, stream);
+    case BLUT_FMT_R8:
+      return p.r8_table ? launch_tc_r8(group_tokens, p, sms, stream) : cudaErrorInvalidValue;
   }
   return cudaErrorInvalidValue;
 }
 
-int dequant_tiled_tc(const blut_mat_desc& d, const void* tiled, void* out, cudaStream_t stream) {
+int dequant_tiled_tc(const blut_mat_desc& d, const void* tiled, const void* r8_table, void* out,
+                     cudaStream_t stream) {
   TiledLayout L;
   if (!make_layout(d, L) || !L.tc) return BLUT_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(tiled) | reinterpret_cast<uintptr_t>(out)) & 15) return BLUT_ERR_INVALID;
@@ -67,7 +70,8 @@ int dequant_tiled_tc(const blut_mat_desc& d, const void* tiled, void* out, cudaS
   a.cols = d.cols;
   a.paired = (d.layout & BLUT_LAYOUT_PAIRED) ? 1 : 0;
   a.out = static_cast<uint16_t*>(out);
-  a.mul = tc_mul_consts();
+  a.mul = tc_mul_consts(d.format == BLUT_FMT_R8 ? d.tier : 0);
+  a.r8_table = static_cast<const uint16_t*>(r8_table);
   cudaError_t e = cudaErrorInvalidValue;
   switch (d.format) {
     case BLUT_FMT_DENSE:
@@ -82,6 +86,10 @@ int dequant_tiled_tc(const blut_mat_desc& d, const void* tiled, void* out, cudaS
       break;
     case BLUT_FMT_NESTED:
       e = d.tier == 1 ? dequant_tc_b2(d.group, a, L.nchunks, stream) : dequant_tc_nested(d.group, a, L.nchunks, stream);
+      break;
+    case BLUT_FMT_R8:
+      if (!r8_table) return BLUT_ERR_INVALID;
+      e = dequant_tc_r8(a, L.nchunks, stream);
       break;
     default:
       return BLUT_ERR_UNSUPPORTED;

@@ -26,7 +26,7 @@ class LUTLinear:
     def __init__(self, qm: QuantizedMatrix, tc: Optional[bool] = None, stream=None):
         fmt = qm.fmt
         if tc is None:
-            tc = fmt.kind != "r8" and fmt.has_tc_layout(qm.rows, qm.cols)
+            tc = fmt.has_tc_layout(qm.rows, qm.cols)
         self.fmt, self.rows, self.cols, self.tc = fmt, qm.rows, qm.cols, bool(tc)
         self.buf, _ = pack_tiled([qm], stream, tc=self.tc)
         self.lut_table = qm.tables if fmt.kind == "r8" else None

@@ -92,8 +92,9 @@ def build_b_layer(fmt: LUTFormat, E: int, H: int, I: int, seed: int = 0, tc=None
     return LUTExperts.from_quantized(q13, q2, tc=tc), W13, W2
 
 
-def build_r8_layer(E: int, H: int, I: int, seed: int = 0, tier: int = 0, table_u16=None):
-    """Random reference-format experts -> (LUTExperts, W13 list, W2 list, table)."""
+def build_r8_layer(E: int, H: int, I: int, seed: int = 0, tier: int = 0, table_u16=None, tc=None):
+    """Random reference-format experts -> (LUTExperts, W13 list, W2 list, table).
+    ``tc``: tiled layout (None: tcgen05 when available, else mma.sync)."""
     rng = np.random.Generator(np.random.PCG64(seed))
     if table_u16 is None:
         table_u16 = O.f32_to_bf16(np.sort(rng.uniform(-1, 1, 256)).astype(np.float32))
@@ -106,4 +107,4 @@ def build_r8_layer(E: int, H: int, I: int, seed: int = 0, tier: int = 0, table_u
             am = O.f32_to_bf16(rng.uniform(0.02, 0.08, (rows * cols + 127) // 128).astype(np.float32))
             qs.append(QuantizedMatrix(fmt, rows, cols, cuda(idx), tab, scales=bf16_tensor(am)))
             Ws.append(O.bf16_to_f32(O.dequant_r(idx, am, table_u16, 128, tier)).reshape(rows, cols))
-    return LUTExperts.from_quantized(q13, q2, tab), W13, W2, table_u16
+    return LUTExperts.from_quantized(q13, q2, tab, tc=tc), W13, W2, table_u16

@@ -63,6 +63,8 @@ def test_tiled_bytes_match_format_bytes(fmt, bpw):
     # NestedLUT stores both tiers: 2 x 0.25 B of codes + (8 + 32) B of tables per block
     (LUTFormat("nested", 4, 32, 0), 1.75), (LUTFormat("nested", 4, 64, 1), 1.125),
     (LUTFormat("nested", 4, 128, 0), 0.8125),
+    # Format R stores its absmax once per 64 columns in this layout (1 + 2/64)
+    (LUTFormat("r8", 8, 128), 1 + 2 / 64),
     (LUTFormat("dense", 16, 0, dense_dtype=torch.float16), 2.0),
     (LUTFormat("dense", 16, 0, dense_dtype=torch.bfloat16), 2.0),
 ])
@@ -82,7 +84,9 @@ def test_tc_layout_availability():
     for fmt in (LUTFormat("b", 2, 64), LUTFormat("b", 3, 32), LUTFormat("b", 3, 128),
                 LUTFormat("nested", 4, 64, 0), LUTFormat("nested", 4, 64, 1)):
         assert fmt.has_tc_layout(1536, 2048, paired=True) and fmt.has_tc_layout(2048, 768)
-    assert not LUTFormat("r8", 8, 128).has_tc_layout(2048, 2048)  # mma.sync layout only
+    r8 = LUTFormat("r8", 8, 128)
+    assert r8.has_tc_layout(2816, 2048, paired=True) and r8.has_tc_layout(2048, 1408)
+    assert not r8.has_tc_layout(2048, 1408 + 64)                    # absmax blocks must stay in a row
 
 
 def test_moe_forward_rejects_mixed_matmul_paths():

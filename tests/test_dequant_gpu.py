@@ -175,6 +175,31 @@ def test_tc_layout_lookup_bit_exact(kind, bits, tier, group, paired):
     assert torch.equal(out.view(torch.int16), dequant(qm).view(torch.int16))
 
 
+@pytest.mark.parametrize("paired", [False, True])
+@pytest.mark.parametrize("tier", [0, 1, 2])
+def test_tc_layout_r8_lookup_bit_exact(tier, paired):
+    """FMT_R8 in the tcgen05 layout: the shared-memory table lookup and the
+    bf16x2 absmax multiply reproduce bf16(f32(table[tier(idx)]) * f32(absmax))
+    bit for bit, with absmax spanning 1e-12 .. 1e4 and a table holding zeros,
+    signed tiny and large values (products stay above the fp32 subnormal
+    range, where the reference's fp32-then-bf16 rounding could differ from one
+    bf16 rounding)."""
+    from block_lut_b200.formats import dequant_tiled, pack_tiled
+    rng = np.random.Generator(np.random.PCG64(70 + tier))
+    rows, cols = 512, 384
+    idx = rng.integers(0, 256, rows * cols, dtype=np.uint8)
+    am = O.f32_to_bf16((10.0 ** rng.uniform(-12, 4, rows * cols // 128)).astype(np.float32))
+    t = rng.uniform(-1, 1, 256).astype(np.float32)
+    t[:8] = [0.0, -0.0, 1e-20, -1e-20, 3e4, -3e4, 1.0, -1.0]
+    tab = bf16_tensor(O.f32_to_bf16(t))
+    fmt = LUTFormat("r8", 8, 128, tier)
+    qm = QuantizedMatrix(fmt, rows, cols, cuda(idx), tab, scales=bf16_tensor(am))
+    assert fmt.has_tc_layout(rows, cols, paired)
+    buf, _ = pack_tiled([qm], paired=paired, tc=True)
+    out = dequant_tiled(fmt, rows, cols, buf, tab, paired=paired, tc=True)
+    assert torch.equal(out.view(torch.int16), dequant(qm).view(torch.int16))
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_tc_layout_dense_round_trip(dtype):
     from block_lut_b200.formats import dense_matrix, dequant_tiled, pack_tiled

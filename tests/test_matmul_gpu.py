@@ -56,8 +56,9 @@ def test_dense_matmul_tcgen05(dtype):
         check_layer(lin(x), ref, dtype, f"dense {dtype} m={m}")
 
 
+@pytest.mark.parametrize("tc", [True, False], ids=["tc", "mma"])
 @pytest.mark.parametrize("tier", [0, 2])
-def test_r8_matmul(tier):
+def test_r8_matmul(tier, tc):
     rng = np.random.Generator(np.random.PCG64(60 + tier))
     table = O.f32_to_bf16(np.sort(rng.uniform(-1, 1, 256)).astype(np.float32))
     idx = rng.integers(0, 256, size=N * K, dtype=np.uint8)
@@ -65,9 +66,9 @@ def test_r8_matmul(tier):
     fmt = LUTFormat("r8", 8, 128, tier)
     qm = QuantizedMatrix(fmt, N, K, cuda(idx), bf16_tensor(table), scales=bf16_tensor(am))
     W = O.bf16_to_f32(O.dequant_r(idx, am, table, 128, tier)).reshape(N, K).astype(np.float64)
-    lin = LUTLinear(qm)
-    assert not lin.tc
-    for m in (1, 8, 70):
+    lin = LUTLinear(qm, tc=tc)
+    assert lin.tc == tc
+    for m in (1, 8, 70, 200):
         x = cuda(O.f32_to_bf16(O.rms_activations(rng, m, K))).view(torch.bfloat16)
         check_layer(lin(x), x.double().cpu().numpy() @ W.T, torch.bfloat16, f"r8 tier {tier} m={m}")
 

@@ -48,9 +48,11 @@ def test_format_b_layer(b_layer, T, k):
     layer.check_status()
 
 
-def test_r8_layer_and_tiers():
+@pytest.mark.parametrize("tc", [True, False], ids=["tc", "mma"])
+def test_r8_layer_and_tiers(tc):
     for tier in (0, 1, 2):
-        experts, W13, W2, _ = build_r8_layer(5, 256, 384, seed=tier, tier=tier)
+        experts, W13, W2, _ = build_r8_layer(5, 256, 384, seed=tier, tier=tier, tc=tc)
+        assert experts.tc == tc
         rng = np.random.Generator(np.random.PCG64(4 + tier))
         for T in (1, 8, 24):
             x = O.rms_activations(rng, T, 256)
