@@ -556,6 +556,7 @@ def run_sweep(a):
     groups_l = [int(v) for v in a.sweep_groups.split(",")]
     ms_l = [int(v) for v in a.sweep_m.split(",")]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_sum = None
     g = torch.Generator(device=dev).manual_seed(5)
     rows, fracs, launches = [], [], 0
     reps = max(3, a.steps)
@@ -583,7 +584,11 @@ def run_sweep(a):
                         lin(x, out=out)
                     ts = []
                     for _ in range(reps):
+                        # write the 256 MB buffer, then read it back: L2 ends up
+                        # holding only clean lines of it, so no write-back of
+                        # flush data lands inside the timed call
                         flush.fill_(1)
+                        flush_sum = flush.sum()
                         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         e0.record()
                         graph.replay()
@@ -609,7 +614,8 @@ def run_sweep(a):
            "dtype": "f16", "data": "synthetic random codes and sorted random fp16 tables; N(0,1) fp16 tokens",
            "config": {"workload": "config 5 single-matrix LUT GEMV/GEMM sweep (blut_matmul, tcgen05 path)",
                       "nk": SWEEP_NK, "m": ms_l, "bits": bits_l, "groups": groups_l,
-                      "l2": "256 MB write before every timed call",
+                      "l2": "256 MB write + read-back before every timed call (clean L2, no dirty write-back "
+                            "in the timed region)",
                       "timing": "median of the per-call CUDA-event times of a CUDA graph of the call's 4 launches"},
            "roofline": {"kernel": "blut_matmul (plan + gather + tc_mm_kernel + reduce)", "bound": "per case",
                         "peak_hbm_gbs": bw, "peak_bf16_tflops": tf,
