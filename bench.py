@@ -616,7 +616,7 @@ def run_sweep(a):
                       "nk": SWEEP_NK, "m": ms_l, "bits": bits_l, "groups": groups_l,
                       "l2": "256 MB write + read-back before every timed call (clean L2, no dirty write-back "
                             "in the timed region)",
-                      "timing": "median of the per-call CUDA-event times of a CUDA graph of the call's 4 launches"},
+                      "timing": "median of the per-call CUDA-event times of a CUDA graph of the call's 3 launches"},
            "roofline": {"kernel": "blut_matmul (plan + gather + tc_mm_kernel + reduce)", "bound": "per case",
                         "peak_hbm_gbs": bw, "peak_bf16_tflops": tf,
                         "frac_min": min(fracs), "frac_max": max(fracs), "traffic": None},

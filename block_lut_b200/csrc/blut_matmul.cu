@@ -1,11 +1,10 @@
 // Single-matrix LUT matmul y = W x, x [M][K] and y [M][N], on the matmul
 // path of the matrix's tiled layout (tcgen05 for BLUT_LAYOUT_TC, mma.sync
-// otherwise).  Four launches: a plan kernel writes the token groups (one
-// "expert", groups of 32 tokens, or 128 on the tcgen05 path from 128 tokens
-// on), a gather kernel puts x into the path's operand order, the matmul
-// writes fp32 rows (in K slices when the tcgen05 path has too few work items
-// to fill the GPU), and a reduce kernel sums the slices in slice order into
-// y.  This is the single-matrix LUT GEMV/GEMM of the reference
+// otherwise).  Three launches: a gather kernel puts x into the path's operand
+// order and writes the token groups (one "expert", groups of 32 tokens, or
+// 128 on the tcgen05 path from 128 tokens on), the matmul writes fp32 rows
+// (in K slices when the tcgen05 path has too few work items to fill the
+// GPU), and a reduce kernel sums the slices in slice order into y.  This is the single-matrix LUT GEMV/GEMM of the reference
 // (vllm_lut/cuda_lut_gemv.py:153-169, fused_kernel.py:13-46) for every
 // format of this library and every token count.
 #include <algorithm>
@@ -98,32 +97,36 @@ int validate_matmul(const blut_mat_desc& d, int64_t m) {
 
 }  // namespace
 
-// Token groups of one matrix: group g holds tokens g * gtok .. (one expert).
-// Also clears the status word (it reports this call) and the work counter.
-__global__ void matmul_plan_kernel(int64_t m, int gtok, int64_t groups, int* __restrict__ n_groups,
-                                   int* __restrict__ expert, int* __restrict__ slot0, int* __restrict__ ntok,
-                                   int* __restrict__ nt0, int* __restrict__ status, int* __restrict__ counter) {
-  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
-    expert[g] = 0;
-    slot0[g] = (int)(g * gtok);
-    ntok[g] = (int)std::min<int64_t>(gtok, m - g * gtok);
-    nt0[g] = (int)(g * gtok / kNTile);
-  }
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    *n_groups = (int)groups;
-    *status = 0;
-    *counter = 0;
-  }
-}
+struct MatmulGroups {
+  int64_t groups;   // token groups: group g holds tokens g * gtok .. (one expert)
+  int gtok;
+  int *n_groups, *expert, *slot0, *ntok, *nt0;
+  int *status, *counter;
+};
 
 // x of one (n-tile of 8 tokens, 128-column chunk), 32 threads: the tcgen05
-// operand order (tc_bact_off) or mma.sync B fragments.
+// operand order (tc_bact_off) or mma.sync B fragments.  The CTAs of chunk 0
+// also write the token groups, and the first clears the status word (it
+// reports this call) and the work counter.
 __global__ void __launch_bounds__(32) matmul_gather_kernel(const uint16_t* __restrict__ x, int64_t m, int k,
                                                            uint8_t* __restrict__ bin, int tc, int kb,
-                                                           int64_t ntstride) {
+                                                           int64_t ntstride, MatmulGroups gp) {
   const int64_t nt = blockIdx.x;
   const int c = blockIdx.y;
   const int lane = threadIdx.x;
+  if (c == 0) {
+    for (int64_t g = nt * 32 + lane; g < gp.groups && g < (nt + 1) * 32; g += 32) {
+      gp.expert[g] = 0;
+      gp.slot0[g] = (int)(g * gp.gtok);
+      gp.ntok[g] = (int)std::min<int64_t>(gp.gtok, m - g * gp.gtok);
+      gp.nt0[g] = (int)(g * gp.gtok / kNTile);
+    }
+    if (nt == 0 && lane == 0) {
+      *gp.n_groups = (int)gp.groups;
+      *gp.status = 0;
+      *gp.counter = 0;
+    }
+  }
   const int64_t t0 = nt * kNTile;
   const int cnt = (int)std::min<int64_t>(kNTile, m - t0);
   if (tc) {
@@ -155,14 +158,26 @@ __global__ void __launch_bounds__(32) matmul_gather_kernel(const uint16_t* __res
   for (int i = 0; i < 4; ++i) d4[i] = make_uint4(wv[4 * i], wv[4 * i + 1], wv[4 * i + 2], wv[4 * i + 3]);
 }
 
-// y = sum of the ks fp32 slices in slice order, four values per thread.
+// y = sum of the ks fp32 slices in slice order, four values per thread;
+// four slices' loads are in flight at a time.
 template <bool BF16>
 __global__ void __launch_bounds__(256) matmul_reduce_kernel(const float* __restrict__ ys, int ks, int64_t sstride,
                                                             int64_t n4, void* __restrict__ y, int y_f32) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-    float4 v = *reinterpret_cast<const float4*>(ys + 4 * i);
-    for (int s = 1; s < ks; ++s) {
-      const float4 u = *reinterpret_cast<const float4*>(ys + s * sstride + 4 * i);
+    const float* p = ys + 4 * i;
+    float4 v = *reinterpret_cast<const float4*>(p);
+    int s = 1;
+    for (; s + 4 <= ks; s += 4) {
+      float4 u[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) u[q] = *reinterpret_cast<const float4*>(p + (s + q) * sstride);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v.x += u[q].x; v.y += u[q].y; v.z += u[q].z; v.w += u[q].w;
+      }
+    }
+    for (; s < ks; ++s) {
+      const float4 u = *reinterpret_cast<const float4*>(p + s * sstride);
       v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
     }
     if (y_f32) {
@@ -186,7 +201,7 @@ size_t matmul_workspace(const blut_mat_desc& d, int64_t m) {
 
 int matmul_launch_count(const blut_mat_desc& d, int64_t m) {
   const int rc = validate_matmul(d, m);
-  return rc != BLUT_OK ? rc : 4;  // plan, gather, matmul, reduce
+  return rc != BLUT_OK ? rc : 3;  // gather (+ token groups), matmul, reduce
 }
 
 int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const void* x, int64_t m, void* y,
@@ -207,11 +222,13 @@ int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const v
   const int sms = num_sms();
   const int64_t N = d.rows, K = d.cols;
 
-  matmul_plan_kernel<<<(unsigned)std::min<int64_t>((p.groups + 255) / 256, 1024), 256, 0, stream>>>(
-      m, p.gtok, p.groups, ws.n_groups, ws.expert, ws.slot0, ws.ntok, ws.nt0, ws.status, ws.counter);
-  if ((rc = stage_done("matmul plan", stream)) != BLUT_OK) return rc;
+  // n-tile nt of chunk 0 writes groups 32 nt .. 32 nt + 31: there are at
+  // most nt8 / 4 + 1 groups (32-token groups, 4 n-tiles each), so nt8
+  // n-tiles cover them
+  const MatmulGroups gp{p.groups, p.gtok, ws.n_groups, ws.expert, ws.slot0, ws.ntok, ws.nt0, ws.status,
+                        ws.counter};
   matmul_gather_kernel<<<dim3((unsigned)p.nt8, (unsigned)(K / kChunk)), 32, 0, stream>>>(
-      static_cast<const uint16_t*>(x), m, (int)K, ws.bin, p.tc ? 1 : 0, p.tc ? L.kb : 0, p.nt8);
+      static_cast<const uint16_t*>(x), m, (int)K, ws.bin, p.tc ? 1 : 0, p.tc ? L.kb : 0, p.nt8, gp);
   if ((rc = stage_done("matmul gather", stream)) != BLUT_OK) return rc;
 
   const GroupTab gt{ws.n_groups, ws.expert, ws.slot0, ws.ntok, ws.nt0};

@@ -438,10 +438,12 @@ static double expected_active(int T, int k, int E) {
   return E * (1.0 - miss);
 }
 
-// K slices per tcgen05 pass: split while the expected work items are fewer
-// than two per resident CTA (two CTAs per SM) and every slice keeps at least
-// two column blocks.  Gate/up passes split at most 8 ways (their partial sums
-// go through memory), down passes 16.
+// K slices per tcgen05 pass, every slice keeping at least two column blocks;
+// gate/up passes split at most 8 ways (their partial sums go through
+// memory), down passes 16.  Routed passes split while the expected work
+// items are fewer than two per resident CTA (two CTAs per SM); the shared
+// expert, whose item count is exact, takes the split with the fewest rounds
+// of items times blocks per item.
 void moe_split(const blut_moe_args& a, MoESplit& s) {
   const int sms = num_sms();
   const int64_t T = a.num_tokens, K = a.top_k, E = a.num_experts, S = T * K;
@@ -470,7 +472,27 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
     const double est = (i < 2 ? est_r : (double)gmax_s) * s.units[i];
     const int max_ks = (i % 2 == 0) ? 8 : 16;
     int ks = 1;
-    while (ks * 2 <= max_ks && L.nchunks / (ks * 2) >= 2 && est * ks < 4.0 * sms) ks *= 2;
+    if (i < 2) {
+      // routed passes: the group count is only an expectation, so split
+      // while the expected items are fewer than two per resident CTA
+      while (ks * 2 <= max_ks && L.nchunks / (ks * 2) >= 2 && est * ks < 4.0 * sms) ks *= 2;
+    } else {
+      // shared expert: the items are known, so pick the split with the
+      // fewest block-times on the busiest CTA, rounds x (blocks + 1), over
+      // the 2 x sms resident CTAs (ties keep fewer slices)
+      const int64_t slots = 2LL * sms;
+      int64_t best = -1;
+      for (int c = 1; c <= max_ks && L.nchunks / c >= 2; ++c) {
+        const int64_t bps_c = (L.nchunks + c - 1) / c;
+        const int64_t ks_c = (L.nchunks + bps_c - 1) / bps_c;
+        const int64_t items = gmax_s * s.units[i] * ks_c;
+        const int64_t cost = ((items + slots - 1) / slots) * (bps_c + 1);
+        if (best < 0 || cost < best) {
+          best = cost;
+          ks = c;
+        }
+      }
+    }
     const int bps = (int)((L.nchunks + ks - 1) / ks);
     s.ks[i] = (int)((L.nchunks + bps - 1) / bps);
     s.bps[i] = bps;

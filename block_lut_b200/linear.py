@@ -1,7 +1,7 @@
 """Single-matrix LUT matmul: ``LUTLinear(qm)(x) = x @ dequant(W).T``.
 
 The matrix is tiled once (the tcgen05 layout when the format and shape have
-one, else the mma.sync layout) and every call is one ``blut_matmul``: four
+one, else the mma.sync layout) and every call is one ``blut_matmul``: three
 stream-ordered launches, fp32 accumulation, no allocation beyond the shared
 grow-only workspace.  This is the single-matrix LUT GEMV of the reference
 (``lut_gemv``, vllm_lut/cuda_lut_gemv.py:153-169; ``fused_lut_gemv``,

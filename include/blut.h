@@ -158,7 +158,7 @@ BLUT_API int blut_dequant_tiled(const blut_mat_desc* desc, const void* tiled, co
  * in desc->dtype (fp32 when y_f32 != 0), 1 <= m <= 2^20, cols % 128 == 0,
  * desc->layout without BLUT_LAYOUT_PAIRED.  Runs on the tcgen05 matmul for
  * BLUT_LAYOUT_TC matrices and on the mma.sync matmul otherwise, fp32
- * accumulation; lut_table is FMT_R8's table (NULL otherwise).  Four launches
+ * accumulation; lut_table is FMT_R8's table (NULL otherwise).  Three launches
  * on `stream`, no allocation, no synchronisation; the workspace (256-byte
  * aligned, blut_matmul_workspace_size bytes) holds the status word that
  * blut_moe_check_status reads.  Replaces the reference's single-matrix LUT
