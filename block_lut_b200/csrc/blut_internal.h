@@ -34,7 +34,12 @@ struct MoESplit {
   int ks[4], bps[4], units[4];
   int64_t groups[4];  // bound on token groups of the pass
   int gtok[2];        // tokens per group: routed, shared (32, or kWideGroupTok for prefill)
+  bool gemv[2];       // routed, shared passes run the small-batch GEMV instead of tcgen05
 };
+
+// Batches of at most this many tokens run the tcgen05-layout matrices
+// through the small-batch GEMV (tc_gemv_kernel).
+constexpr int kGemvMaxTokens = 16;
 
 constexpr int kNumCounters = 4;  // routed gate/up, routed down, shared gate/up, shared down
 

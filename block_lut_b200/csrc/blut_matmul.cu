@@ -21,6 +21,7 @@ constexpr int64_t kMatmulMaxTokens = 1 << 20;
 
 struct MatmulPlan {
   bool tc;
+  bool gemv;        // tcgen05 layout, at most kGemvMaxTokens tokens: small-batch GEMV
   int gtok;         // tokens per group
   int64_t groups;   // token groups
   int64_t nt8;      // n-tiles of 8 tokens
@@ -46,7 +47,17 @@ bool matmul_plan(const blut_mat_desc& d, int64_t m, MatmulPlan& p, TiledLayout& 
   p.ks = 1;
   p.bps = (int)L.nchunks;
   p.units = 0;
-  if (p.tc) {
+  p.gemv = p.tc && m <= kGemvMaxTokens;
+  if (p.gemv) {  // one CTA per (tile, K slice): split K until about four CTAs per SM
+    const int sms = num_sms();
+    int ks = 1;
+    while (ks * 2 <= 32 && L.nchunks / (ks * 2) >= 1 && (double)L.ntiles * ks < 4.0 * sms) ks *= 2;
+    int64_t bps = (L.nchunks + ks - 1) / ks;
+    while (bps * L.kb > kGemvMaxCols) bps = (L.nchunks + ++ks - 1) / ks;
+    p.bps = (int)bps;
+    p.ks = (int)((L.nchunks + bps - 1) / bps);
+    p.units = (int)((L.ntiles + 1) / 2);
+  } else if (p.tc) {
     p.units = (int)((L.ntiles + 1) / 2);
     if (p.gtok == kGroupTok) {  // split K while the items are fewer than four per SM
       const int sms = num_sms();
@@ -248,7 +259,8 @@ int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const v
     t.r8_table = static_cast<const uint16_t*>(lut_table);
     t.ks = p.ks;
     t.bps = p.bps;
-    if (launch_tc_mm(d, t, p.gtok, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+    t.gemv_groups = p.groups;
+    if (launch_tc_mm(d, t, p.gemv ? 1 : p.gtok, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
   } else {
     MMParams mp{};
     if (!mm_planes(d, false, mp)) return BLUT_ERR_UNSUPPORTED;

@@ -454,6 +454,8 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
   const bool tc_s = a.shared_inter > 0 && (a.s13.layout & BLUT_LAYOUT_TC) != 0;
   s.gtok[0] = tc_r && S >= 64 * E ? kWideGroupTok : kGroupTok;
   s.gtok[1] = tc_s && T >= 64 ? kWideGroupTok : kGroupTok;
+  s.gemv[0] = tc_r && T <= kGemvMaxTokens;
+  s.gemv[1] = tc_s && T <= kGemvMaxTokens;
   const double est_r = expected_active((int)T, (int)K, (int)E) + (double)S / s.gtok[0];
   const int64_t gmax_r = std::min(E, S) + (S + s.gtok[0] - 1) / s.gtok[0] + 1;
   const int64_t gmax_s = (T + s.gtok[1] - 1) / s.gtok[1];
@@ -468,6 +470,18 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
     s.bps[i] = (int)L.nchunks;
     if (!L.tc) continue;
     s.units[i] = (int)((L.ntiles + 1) / 2);
+    if (s.gemv[i / 2]) {
+      // small-batch GEMV, one CTA per (group, tile, K slice): split K until
+      // there are about four CTAs per SM, at most kGemvMaxCols columns each
+      const double ctas = (i < 2 ? est_r : (double)gmax_s) * L.ntiles;
+      int ks = 1;
+      while (ks * 2 <= 32 && L.nchunks / (ks * 2) >= 1 && ctas * ks < 4.0 * sms) ks *= 2;
+      int64_t bps = (L.nchunks + ks - 1) / ks;
+      while (bps * L.kb > kGemvMaxCols) bps = (L.nchunks + ++ks - 1) / ks;
+      s.ks[i] = (int)((L.nchunks + bps - 1) / bps);
+      s.bps[i] = (int)bps;
+      continue;
+    }
     if (s.gtok[i / 2] != kGroupTok) continue;  // wide groups have enough items
     const double est = (i < 2 ? est_r : (double)gmax_s) * s.units[i];
     const int max_ks = (i % 2 == 0) ? 8 : 16;
@@ -530,8 +544,8 @@ size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
   size_t o_afs = sh ? take(sntmax * (a.shared_inter / kChunk) * kBfragChunkBytes) : 0;
   size_t o_ys = sh ? take(T * H * 4 * sp.ks[3]) : 0;
   // split-K partial sums of the gate/up passes: [item][gate|up][128 rows][32 tokens] fp32
-  const int64_t ku_r = sp.ks[0] > 1 ? sp.groups[0] * sp.units[0] : 0;
-  const int64_t ku_s = sp.ks[2] > 1 ? sp.groups[2] * sp.units[2] : 0;
+  const int64_t ku_r = sp.ks[0] > 1 || sp.gemv[0] ? sp.groups[0] * sp.units[0] : 0;
+  const int64_t ku_s = sp.ks[2] > 1 || sp.gemv[1] ? sp.groups[2] * sp.units[2] : 0;
   size_t o_part_r = take(ku_r * sp.ks[0] * 2 * kTcRows * 32 * 4);
   size_t o_part_s = take(ku_s * sp.ks[2] * 2 * kTcRows * 32 * 4);
   if (base && ws) {
@@ -761,8 +775,11 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.bps = ws.split.bps[counter];
       t.part = part;
       t.y_sstride = y_sstride;
-      if (launch_tc_mm(d, t, ws.split.gtok[counter / 2], sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
-      if (pair && t.ks > 1) {
+      const bool gemv = ws.split.gemv[counter / 2];
+      t.gemv_groups = ws.split.groups[counter];
+      if (launch_tc_mm(d, t, gemv ? 1 : ws.split.gtok[counter / 2], sms, stream) != cudaSuccess)
+        return BLUT_ERR_LAUNCH;
+      if (pair && (t.ks > 1 || gemv)) {
         // sum the gate/up slices in order, SiLU(gate) * up into the down projection's activations
         const dim3 grid((unsigned)(ws.split.groups[counter] * t.units), (unsigned)(kTcRows * 32 / 256));
         if (a.dtype == BLUT_BF16)
@@ -845,7 +862,7 @@ int moe_launch_count(const blut_moe_args& a) {
   n += 1;                                                  // combine
   MoESplit sp;
   moe_split(a, sp);
-  n += (sp.ks[0] > 1) + (sh && sp.ks[2] > 1);              // split-K gate/up sums
+  n += (sp.ks[0] > 1 || sp.gemv[0]) + (sh && (sp.ks[2] > 1 || sp.gemv[1]));  // gate/up slice sums
   return n;
 }
 

@@ -118,6 +118,7 @@ struct TcParams {
   int* counter;            // item counter (zeroed by the plan kernel)
   TcMul mul;               // tc_mul_consts()
   const uint16_t* r8_table;  // FMT_R8: the tier's bf16 [256] table
+  int64_t gemv_groups;     // small-batch GEMV: bound on the token groups (the grid is sized by it)
   int* status;
   int stages;              // weight stages (LUT formats) or weight + activation stages (dense)
   int xstages;             // activation stages (LUT formats)
@@ -1009,6 +1010,177 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------ small-batch GEMV --
+// With one to a few tokens per expert (decode batches of up to
+// kGemvMaxTokens tokens) the tensor core has nothing to amortise: every
+// weight is used once per token, and the tcgen05 pipeline's fill and drain
+// dominate.  tc_gemv_kernel reads the same TC-layout buffer straight from
+// global memory, one thread per weight row, decodes it with the format's
+// policy and accumulates the group's tokens in fp32 on the FMA pipe.  A CTA
+// is one (token group, 128-row tile, K slice); the next block's codes are
+// loaded while the current one is decoded.  It writes exactly what
+// tc_mm_kernel writes (gate/up partial sums for splitk_silu_kernel, or fp32
+// output rows per K slice), so the kernels around it are unchanged.
+constexpr int kGemvTok = 8;         // tokens accumulated per pass over the weights
+constexpr int kGemvMaxCols = 2048;  // columns per CTA (K slice): at most 64 KB of staged fp32 activations
+
+template <bool BF16>
+__device__ __forceinline__ float2 tc_unpack2(uint32_t v) {
+  if constexpr (BF16) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+  } else {
+    return __half22float2(*reinterpret_cast<const __half2*>(&v));
+  }
+}
+
+// Accumulates 16 pairs (32 consecutive columns starting at column c of the
+// slice) into acc[NT]; xs holds the chunk's tokens as fp32 [token][column].
+template <bool BF16, int NT>
+__device__ __forceinline__ void tc_gemv_fma32(const uint32_t (&o)[16], const float* __restrict__ xs, int ldx, int c,
+                                              float2 (&acc)[NT]) {
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    const float2 w0 = tc_unpack2<BF16>(o[i]);
+    const float2 w1 = tc_unpack2<BF16>(o[i + 1]);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float4 x = *reinterpret_cast<const float4*>(xs + t * ldx + c + 2 * i);
+      acc[t].x = fmaf(w0.x, x.x, acc[t].x);
+      acc[t].y = fmaf(w0.y, x.y, acc[t].y);
+      acc[t].x = fmaf(w1.x, x.z, acc[t].x);
+      acc[t].y = fmaf(w1.y, x.w, acc[t].y);
+    }
+  }
+}
+
+template <class Dec>
+__device__ __forceinline__ void tc_gemv_ptrs(const TcParams& p, const uint8_t* base, int b, int pt, uint32_t tab,
+                                             TcPtrs& pp) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) pp.p[k] = base + p.plane_off[k] + ((int64_t)b * p.ntiles + pt) * p.piece[k];
+  pp.tab = tab;
+}
+
+// One pass over the slice's weights for NT tokens of the chunk.
+template <class Dec, int NT>
+__device__ __forceinline__ void tc_gemv_pass(const TcParams& p, const uint8_t* base, int pt, int b0, int b1, int row,
+                                             uint32_t tab, const float* xs, int ldx, float (&out)[kGemvTok]) {
+  float2 acc[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] = make_float2(0.f, 0.f);
+  if constexpr (Dec::kDense) {
+    // KB = 32 columns: four 16-byte units of 8 values per row
+    for (int b = b0; b < b1; ++b) {
+      TcPtrs pp;
+      tc_gemv_ptrs<Dec>(p, base, b, pt, tab, pp);
+      uint32_t o[16];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 v = *reinterpret_cast<const uint4*>(pp.p[0] + (u * kTcRows + row) * 16);
+        o[4 * u] = v.x; o[4 * u + 1] = v.y; o[4 * u + 2] = v.z; o[4 * u + 3] = v.w;
+      }
+      tc_gemv_fma32<Dec::kBF16, NT>(o, xs, ldx, (b - b0) * Dec::KB, acc);
+    }
+  } else {
+    typename Dec::Half cur, nxt;
+    TcPtrs pp;
+    tc_gemv_ptrs<Dec>(p, base, b0, pt, tab, pp);
+    Dec::load_half(pp, row, 0, cur);
+    for (int b = b0; b < b1; ++b) {
+#pragma unroll
+      for (int h = 0; h < Dec::kHalves; ++h) {
+        // prefetch the next half (of this block or the next one)
+        const bool last_h = h == Dec::kHalves - 1;
+        const int nb = last_h ? b + 1 : b;
+        if (nb < b1) {
+          TcPtrs pn;
+          tc_gemv_ptrs<Dec>(p, base, nb, pt, tab, pn);
+          Dec::load_half(pn, row, last_h ? 0 : h + 1, nxt);
+        }
+        const int c = (b - b0) * Dec::KB + h * 64;
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) {
+          uint32_t o[16];
+          Dec::lookup_q(cur, qq, o, p.mul);
+          tc_gemv_fma32<Dec::kBF16, NT>(o, xs, ldx, c + 32 * qq, acc);
+        }
+        cur = nxt;
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) out[t] = acc[t].x + acc[t].y;
+}
+
+template <class Dec>
+__global__ void __launch_bounds__(kTcRows, 4) tc_gemv_kernel(const TcParams p) {
+  constexpr int KB = Dec::KB;
+  const int64_t cta = blockIdx.x;
+  const int s = (int)(cta % p.ks);
+  const int pt = (int)((cta / p.ks) % p.ntiles);
+  const int gi = (int)(cta / ((int64_t)p.ks * p.ntiles));
+  if (gi >= *p.gt.n_groups) return;
+  const int b0 = s * p.bps, b1 = min(p.nblocks, b0 + p.bps);
+  if (b0 >= b1) return;
+  const int row = threadIdx.x;
+  const int ntok = p.gt.ntok[gi], nt0 = p.gt.nt0[gi];
+  const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
+  extern __shared__ __align__(16) uint8_t gsm[];
+  uint32_t tab = 0;
+  if constexpr (Dec::kR8) {
+    tc_fill_r8_table(reinterpret_cast<uint32_t*>(gsm), p.r8_table);
+    tab = smem_u32(gsm) + (row & 31) * 4;
+  }
+  float* xs = reinterpret_cast<float*>(gsm + tc_table_bytes<Dec>());  // [kGemvTok][ldx]
+  const int ncols = (b1 - b0) * KB, ldx = ncols;
+  for (int c0 = 0; c0 < ntok; c0 += kGemvTok) {
+    const int nc = min(kGemvTok, ntok - c0);
+    __syncthreads();  // the previous chunk's reads of xs are done (and the R8 table is filled)
+    for (int i = threadIdx.x; i < nc * ncols; i += blockDim.x) {
+      const int t = i / ncols, col = i - t * ncols;
+      const uint16_t h = *reinterpret_cast<const uint16_t*>(
+          p.bin + tc_bact_off((int64_t)nt0 * kNTile + c0 + t, b0 * KB + col, KB, p.ntstride));
+      xs[t * ldx + col] = act_to_f32<Dec::kBF16>(h);
+    }
+    __syncthreads();
+    float out[kGemvTok];
+    if (nc == 1) tc_gemv_pass<Dec, 1>(p, base, pt, b0, b1, row, tab, xs, ldx, out);
+    else if (nc == 2) tc_gemv_pass<Dec, 2>(p, base, pt, b0, b1, row, tab, xs, ldx, out);
+    else if (nc <= 4) tc_gemv_pass<Dec, 4>(p, base, pt, b0, b1, row, tab, xs, ldx, out);
+    else tc_gemv_pass<Dec, 8>(p, base, pt, b0, b1, row, tab, xs, ldx, out);
+    if (p.pair) {
+      // partial sums [item = (group, unit, slice)][gate | up][row][token]
+      const int64_t item = ((int64_t)gi * p.units + (pt >> 1)) * p.ks + s;
+      float* dst = p.part + item * (2 * kTcRows * 32) + (pt & 1) * (kTcRows * 32) + row * 32 + c0;
+      for (int t = 0; t < nc; ++t) dst[t] = out[t];
+    } else {
+      float* y = p.y_out + (int64_t)s * p.y_sstride + (int64_t)(p.gt.slot0[gi] + c0) * p.y_ld + pt * kTcRows + row;
+      for (int t = 0; t < nc; ++t) y[(int64_t)t * p.y_ld] = out[t];
+    }
+  }
+}
+
+// Host launch of the GEMV: one CTA per (group bound, tile, K slice).
+template <class Dec>
+inline cudaError_t launch_tc_gemv(const TcParams& p, int64_t group_bound, cudaStream_t stream) {
+  const int64_t ctas = group_bound * p.ntiles * p.ks;
+  const int smem = tc_table_bytes<Dec>() + kGemvTok * p.bps * Dec::KB * 4;
+  if (p.bps * Dec::KB > kGemvMaxCols || ctas <= 0 || ctas > (1LL << 31) - 1) return cudaErrorInvalidValue;
+  auto kern = tc_gemv_kernel<Dec>;
+  static std::mutex mu;
+  static int cached = -1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached < smem) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, std::max(smem, 48 * 1024));
+      if (e != cudaSuccess) return e;
+      cached = std::max(smem, 48 * 1024);
+    }
+  }
+  kern<<<(unsigned)ctas, kTcRows, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
 // One CTA per (physical tile, block), one thread per row: decode the row's
 // block straight from global memory with the matmul's decode policy and
 // write it to out[rows][cols] (the diagnostic dequantisation of the layout).
@@ -1061,8 +1233,18 @@ __global__ void __launch_bounds__(kTcRows) tc_dequant_kernel(const TcDequantArgs
 
 // Launchers of a decode family over its table blocks (32, 64, 128 columns)
 // and token-group widths (32, 128).
+// group_tokens: 32 or 128 for the tcgen05 matmul with that token-group
+// width, 1 for the small-batch GEMV (groups of up to 32 tokens).
 template <template <int> class DecT>
 inline cudaError_t launch_tc_family(int group, int group_tokens, const TcParams& p, int sms, cudaStream_t stream) {
+  if (group_tokens == 1) {
+    switch (group) {
+      case 32: return launch_tc_gemv<DecT<32>>(p, p.gemv_groups, stream);
+      case 64: return launch_tc_gemv<DecT<64>>(p, p.gemv_groups, stream);
+      case 128: return launch_tc_gemv<DecT<128>>(p, p.gemv_groups, stream);
+    }
+    return cudaErrorInvalidValue;
+  }
   const bool wide = group_tokens == 128;
   if (group_tokens != 32 && !wide) return cudaErrorInvalidValue;
   switch (group) {

@@ -34,10 +34,14 @@ static cudaError_t launch_tc_dense(const blut_mat_desc& d, const TcParams& p, in
                               : launch_tc<TcDecDense<false>, MT>(p, sms, stream);
 }
 
+// group_tokens: 32 or 128 (tcgen05 matmul), 1 (small-batch GEMV).
 cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int group_tokens, int sms, cudaStream_t stream) {
-  if (group_tokens != 32 && group_tokens != 128) return cudaErrorInvalidValue;
+  if (group_tokens != 32 && group_tokens != 128 && group_tokens != 1) return cudaErrorInvalidValue;
   switch (d.format) {
     case BLUT_FMT_DENSE:
+      if (group_tokens == 1)
+        return d.dtype == BLUT_BF16 ? launch_tc_gemv<TcDecDense<true>>(p, p.gemv_groups, stream)
+                                    : launch_tc_gemv<TcDecDense<false>>(p, p.gemv_groups, stream);
       return group_tokens == 32 ? launch_tc_dense<32>(d, p, sms, stream) : launch_tc_dense<128>(d, p, sms, stream);
     case BLUT_FMT_B:
       if (d.bits == 4) return launch_tc_family<TcDecB4>(d.group, group_tokens, p, sms, stream);

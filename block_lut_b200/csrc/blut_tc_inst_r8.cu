@@ -6,6 +6,7 @@
 namespace blut {
 
 cudaError_t launch_tc_r8(int group_tokens, const TcParams& p, int sms, cudaStream_t stream) {
+  if (group_tokens == 1) return launch_tc_gemv<TcDecR8>(p, p.gemv_groups, stream);
   if (group_tokens == 32) return launch_tc<TcDecR8, 32>(p, sms, stream);
   if (group_tokens == 128) return launch_tc<TcDecR8, 128>(p, sms, stream);
   return cudaErrorInvalidValue;
