@@ -39,7 +39,7 @@ struct MoESplit {
 
 // Batches of at most this many tokens run the tcgen05-layout matrices
 // through the small-batch GEMV (tc_gemv_kernel).
-constexpr int kGemvMaxTokens = 16;
+constexpr int kGemvMaxTokens = 4;
 
 constexpr int kNumCounters = 4;  // routed gate/up, routed down, shared gate/up, shared down
 

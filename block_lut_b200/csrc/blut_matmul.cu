@@ -48,10 +48,10 @@ bool matmul_plan(const blut_mat_desc& d, int64_t m, MatmulPlan& p, TiledLayout& 
   p.bps = (int)L.nchunks;
   p.units = 0;
   p.gemv = p.tc && m <= kGemvMaxTokens;
-  if (p.gemv) {  // one CTA per (tile, K slice): split K until about four CTAs per SM
+  if (p.gemv) {  // one CTA per (tile, K slice): split K until about eight CTAs per SM
     const int sms = num_sms();
     int ks = 1;
-    while (ks * 2 <= 32 && L.nchunks / (ks * 2) >= 1 && (double)L.ntiles * ks < 4.0 * sms) ks *= 2;
+    while (ks * 2 <= 32 && L.nchunks / (ks * 2) >= 1 && (double)L.ntiles * ks < 8.0 * sms) ks *= 2;
     int64_t bps = (L.nchunks + ks - 1) / ks;
     while (bps * L.kb > kGemvMaxCols) bps = (L.nchunks + ++ks - 1) / ks;
     p.bps = (int)bps;
@@ -260,6 +260,7 @@ int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const v
     t.ks = p.ks;
     t.bps = p.bps;
     t.gemv_groups = p.groups;
+    t.gemv_nt = m == 1 ? 1 : kGemvTok;
     if (launch_tc_mm(d, t, p.gemv ? 1 : p.gtok, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
   } else {
     MMParams mp{};

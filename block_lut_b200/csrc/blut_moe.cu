@@ -472,10 +472,10 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
     s.units[i] = (int)((L.ntiles + 1) / 2);
     if (s.gemv[i / 2]) {
       // small-batch GEMV, one CTA per (group, tile, K slice): split K until
-      // there are about four CTAs per SM, at most kGemvMaxCols columns each
+      // there are about eight CTAs per SM, at most kGemvMaxCols columns each
       const double ctas = (i < 2 ? est_r : (double)gmax_s) * L.ntiles;
       int ks = 1;
-      while (ks * 2 <= 32 && L.nchunks / (ks * 2) >= 1 && ctas * ks < 4.0 * sms) ks *= 2;
+      while (ks * 2 <= 32 && L.nchunks / (ks * 2) >= 1 && ctas * ks < 8.0 * sms) ks *= 2;
       int64_t bps = (L.nchunks + ks - 1) / ks;
       while (bps * L.kb > kGemvMaxCols) bps = (L.nchunks + ++ks - 1) / ks;
       s.ks[i] = (int)((L.nchunks + bps - 1) / bps);
@@ -777,6 +777,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.y_sstride = y_sstride;
       const bool gemv = ws.split.gemv[counter / 2];
       t.gemv_groups = ws.split.groups[counter];
+      t.gemv_nt = a.num_tokens == 1 ? 1 : kGemvTok;
       if (launch_tc_mm(d, t, gemv ? 1 : ws.split.gtok[counter / 2], sms, stream) != cudaSuccess)
         return BLUT_ERR_LAUNCH;
       if (pair && (t.ks > 1 || gemv)) {

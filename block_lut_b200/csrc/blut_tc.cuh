@@ -119,6 +119,7 @@ struct TcParams {
   TcMul mul;               // tc_mul_consts()
   const uint16_t* r8_table;  // FMT_R8: the tier's bf16 [256] table
   int64_t gemv_groups;     // small-batch GEMV: bound on the token groups (the grid is sized by it)
+  int gemv_nt;             // small-batch GEMV: tokens accumulated per pass (1 or kGemvTok)
   int* status;
   int stages;              // weight stages (LUT formats) or weight + activation stages (dense)
   int xstages;             // activation stages (LUT formats)
@@ -1021,7 +1022,7 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
 // loaded while the current one is decoded.  It writes exactly what
 // tc_mm_kernel writes (gate/up partial sums for splitk_silu_kernel, or fp32
 // output rows per K slice), so the kernels around it are unchanged.
-constexpr int kGemvTok = 8;         // tokens accumulated per pass over the weights
+constexpr int kGemvTok = 4;         // tokens accumulated per pass over the weights (batches > 1 token)
 constexpr int kGemvMaxCols = 2048;  // columns per CTA (K slice): at most 64 KB of staged fp32 activations
 
 template <bool BF16>
@@ -1061,10 +1062,12 @@ __device__ __forceinline__ void tc_gemv_ptrs(const TcParams& p, const uint8_t* b
   pp.tab = tab;
 }
 
-// One pass over the slice's weights for NT tokens of the chunk.
+// One pass over the slice's weights for NT tokens of the chunk; `cur`
+// holds the slice's first half, already loaded.
 template <class Dec, int NT>
 __device__ __forceinline__ void tc_gemv_pass(const TcParams& p, const uint8_t* base, int pt, int b0, int b1, int row,
-                                             uint32_t tab, const float* xs, int ldx, float (&out)[kGemvTok]) {
+                                             uint32_t tab, const float* xs, int ldx, typename Dec::Half& cur,
+                                             float (&out)[NT]) {
   float2 acc[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t] = make_float2(0.f, 0.f);
@@ -1082,10 +1085,7 @@ __device__ __forceinline__ void tc_gemv_pass(const TcParams& p, const uint8_t* b
       tc_gemv_fma32<Dec::kBF16, NT>(o, xs, ldx, (b - b0) * Dec::KB, acc);
     }
   } else {
-    typename Dec::Half cur, nxt;
-    TcPtrs pp;
-    tc_gemv_ptrs<Dec>(p, base, b0, pt, tab, pp);
-    Dec::load_half(pp, row, 0, cur);
+    typename Dec::Half nxt;
     for (int b = b0; b < b1; ++b) {
 #pragma unroll
       for (int h = 0; h < Dec::kHalves; ++h) {
@@ -1112,7 +1112,9 @@ __device__ __forceinline__ void tc_gemv_pass(const TcParams& p, const uint8_t* b
   for (int t = 0; t < NT; ++t) out[t] = acc[t].x + acc[t].y;
 }
 
-template <class Dec>
+// NT: tokens accumulated per pass over the weights (1, or kGemvTok with
+// groups of more tokens taking several passes).
+template <class Dec, int NT>
 __global__ void __launch_bounds__(kTcRows, 4) tc_gemv_kernel(const TcParams p) {
   constexpr int KB = Dec::KB;
   const int64_t cta = blockIdx.x;
@@ -1127,58 +1129,80 @@ __global__ void __launch_bounds__(kTcRows, 4) tc_gemv_kernel(const TcParams p) {
   const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
   extern __shared__ __align__(16) uint8_t gsm[];
   uint32_t tab = 0;
-  if constexpr (Dec::kR8) {
-    tc_fill_r8_table(reinterpret_cast<uint32_t*>(gsm), p.r8_table);
-    tab = smem_u32(gsm) + (row & 31) * 4;
+  if constexpr (Dec::kR8) tab = smem_u32(gsm) + (row & 31) * 4;
+  // the slice's first weights are in flight while the activations are staged
+  typename Dec::Half first;
+  if constexpr (!Dec::kDense) {
+    TcPtrs pp;
+    tc_gemv_ptrs<Dec>(p, base, b0, pt, tab, pp);
+    Dec::load_half(pp, row, 0, first);
   }
-  float* xs = reinterpret_cast<float*>(gsm + tc_table_bytes<Dec>());  // [kGemvTok][ldx]
+  if constexpr (Dec::kR8) tc_fill_r8_table(reinterpret_cast<uint32_t*>(gsm), p.r8_table);
+  float* xs = reinterpret_cast<float*>(gsm + tc_table_bytes<Dec>());  // [NT][ldx]
   const int ncols = (b1 - b0) * KB, ldx = ncols;
-  for (int c0 = 0; c0 < ntok; c0 += kGemvTok) {
-    const int nc = min(kGemvTok, ntok - c0);
-    __syncthreads();  // the previous chunk's reads of xs are done (and the R8 table is filled)
-    for (int i = threadIdx.x; i < nc * ncols; i += blockDim.x) {
+  for (int c0 = 0; c0 < ntok; c0 += NT) {
+    const int nc = min(NT, ntok - c0);
+    if (c0 > 0 && !Dec::kDense) {  // a further pass reloads the slice's first half
+      TcPtrs pp;
+      tc_gemv_ptrs<Dec>(p, base, b0, pt, tab, pp);
+      Dec::load_half(pp, row, 0, first);
+    }
+    __syncthreads();  // the previous pass's reads of xs are done (and the R8 table is filled)
+    for (int i = threadIdx.x; i < NT * ncols; i += blockDim.x) {
       const int t = i / ncols, col = i - t * ncols;
-      const uint16_t h = *reinterpret_cast<const uint16_t*>(
-          p.bin + tc_bact_off((int64_t)nt0 * kNTile + c0 + t, b0 * KB + col, KB, p.ntstride));
-      xs[t * ldx + col] = act_to_f32<Dec::kBF16>(h);
+      float v = 0.f;
+      if (t < nc) {
+        const uint16_t h = *reinterpret_cast<const uint16_t*>(
+            p.bin + tc_bact_off((int64_t)nt0 * kNTile + c0 + t, b0 * KB + col, KB, p.ntstride));
+        v = act_to_f32<Dec::kBF16>(h);
+      }
+      xs[t * ldx + col] = v;
     }
     __syncthreads();
-    float out[kGemvTok];
-    if (nc == 1) tc_gemv_pass<Dec, 1>(p, base, pt, b0, b1, row, tab, xs, ldx, out);
-    else if (nc == 2) tc_gemv_pass<Dec, 2>(p, base, pt, b0, b1, row, tab, xs, ldx, out);
-    else if (nc <= 4) tc_gemv_pass<Dec, 4>(p, base, pt, b0, b1, row, tab, xs, ldx, out);
-    else tc_gemv_pass<Dec, 8>(p, base, pt, b0, b1, row, tab, xs, ldx, out);
+    float out[NT];
+    tc_gemv_pass<Dec, NT>(p, base, pt, b0, b1, row, tab, xs, ldx, first, out);
     if (p.pair) {
       // partial sums [item = (group, unit, slice)][gate | up][row][token]
       const int64_t item = ((int64_t)gi * p.units + (pt >> 1)) * p.ks + s;
       float* dst = p.part + item * (2 * kTcRows * 32) + (pt & 1) * (kTcRows * 32) + row * 32 + c0;
-      for (int t = 0; t < nc; ++t) dst[t] = out[t];
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < nc) dst[t] = out[t];
     } else {
       float* y = p.y_out + (int64_t)s * p.y_sstride + (int64_t)(p.gt.slot0[gi] + c0) * p.y_ld + pt * kTcRows + row;
-      for (int t = 0; t < nc; ++t) y[(int64_t)t * p.y_ld] = out[t];
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < nc) y[(int64_t)t * p.y_ld] = out[t];
     }
   }
 }
 
-// Host launch of the GEMV: one CTA per (group bound, tile, K slice).
-template <class Dec>
-inline cudaError_t launch_tc_gemv(const TcParams& p, int64_t group_bound, cudaStream_t stream) {
+// Host launch of the GEMV: one CTA per (group bound, tile, K slice);
+// p.gemv_nt tokens per pass (1 or kGemvTok).
+template <class Dec, int NT>
+inline cudaError_t launch_tc_gemv_nt(const TcParams& p, int64_t group_bound, cudaStream_t stream) {
   const int64_t ctas = group_bound * p.ntiles * p.ks;
-  const int smem = tc_table_bytes<Dec>() + kGemvTok * p.bps * Dec::KB * 4;
+  const int smem = tc_table_bytes<Dec>() + NT * p.bps * Dec::KB * 4;
   if (p.bps * Dec::KB > kGemvMaxCols || ctas <= 0 || ctas > (1LL << 31) - 1) return cudaErrorInvalidValue;
-  auto kern = tc_gemv_kernel<Dec>;
+  auto kern = tc_gemv_kernel<Dec, NT>;
   static std::mutex mu;
   static int cached = -1;
   {
     std::lock_guard<std::mutex> lock(mu);
     if (cached < smem) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, std::max(smem, 48 * 1024));
+      const int attr = std::max(smem, 48 * 1024);
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, attr);
       if (e != cudaSuccess) return e;
-      cached = std::max(smem, 48 * 1024);
+      cached = attr;
     }
   }
   kern<<<(unsigned)ctas, kTcRows, smem, stream>>>(p);
   return cudaGetLastError();
+}
+template <class Dec>
+inline cudaError_t launch_tc_gemv(const TcParams& p, int64_t group_bound, cudaStream_t stream) {
+  return p.gemv_nt == 1 ? launch_tc_gemv_nt<Dec, 1>(p, group_bound, stream)
+                        : launch_tc_gemv_nt<Dec, kGemvTok>(p, group_bound, stream);
 }
 
 // One CTA per (physical tile, block), one thread per row: decode the row's
