@@ -87,6 +87,7 @@ bool mm_planes(const blut_mat_desc& d, bool pair, MMParams& p);
 struct TcParams;
 bool tc_planes(const blut_mat_desc& d, bool pair, TcParams& p);
 cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int group_tokens, int sms, cudaStream_t stream);
+int tc_gemv_blocks(const blut_mat_desc& d);
 int dequant_tiled_tc(const blut_mat_desc& d, const void* tiled, const void* r8_table, void* out,
                      cudaStream_t stream);
 int dequant_tiled(const blut_mat_desc& d, const void* tiled, const void* table, void* out, cudaStream_t stream);

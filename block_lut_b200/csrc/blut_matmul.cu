@@ -48,12 +48,10 @@ bool matmul_plan(const blut_mat_desc& d, int64_t m, MatmulPlan& p, TiledLayout& 
   p.bps = (int)L.nchunks;
   p.units = 0;
   p.gemv = p.tc && m <= kGemvMaxTokens;
-  if (p.gemv) {  // one CTA per (tile, K slice): split K until about eight CTAs per SM
+  if (p.gemv) {  // one CTA per (tile, K slice), sized as in the MoE passes
     const int sms = num_sms();
-    int ks = 1;
-    while (ks * 2 <= 32 && L.nchunks / (ks * 2) >= 1 && (double)L.ntiles * ks < 8.0 * sms) ks *= 2;
-    int64_t bps = (L.nchunks + ks - 1) / ks;
-    while (bps * L.kb > kGemvMaxCols) bps = (L.nchunks + ++ks - 1) / ks;
+    int64_t bps = tc_gemv_blocks(d);
+    while (bps > 1 && (double)L.ntiles * ((L.nchunks + bps - 1) / bps) < 4.0 * sms) bps = (bps + 1) / 2;
     p.bps = (int)bps;
     p.ks = (int)((L.nchunks + bps - 1) / bps);
     p.units = (int)((L.ntiles + 1) / 2);

@@ -471,13 +471,12 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
     if (!L.tc) continue;
     s.units[i] = (int)((L.ntiles + 1) / 2);
     if (s.gemv[i / 2]) {
-      // small-batch GEMV, one CTA per (group, tile, K slice): split K until
-      // there are about eight CTAs per SM, at most kGemvMaxCols columns each
-      const double ctas = (i < 2 ? est_r : (double)gmax_s) * L.ntiles;
-      int ks = 1;
-      while (ks * 2 <= 32 && L.nchunks / (ks * 2) >= 1 && ctas * ks < 8.0 * sms) ks *= 2;
-      int64_t bps = (L.nchunks + ks - 1) / ks;
-      while (bps * L.kb > kGemvMaxCols) bps = (L.nchunks + ++ks - 1) / ks;
+      // small-batch GEMV, one CTA per (group, tile, K slice): a slice is
+      // the blocks a thread keeps in flight, halved while that leaves fewer
+      // than four CTAs per SM
+      const double tiles = (i < 2 ? est_r : (double)gmax_s) * L.ntiles;
+      int64_t bps = tc_gemv_blocks(*d[i]);
+      while (bps > 1 && tiles * ((L.nchunks + bps - 1) / bps) < 4.0 * sms) bps = (bps + 1) / 2;
       s.ks[i] = (int)((L.nchunks + bps - 1) / bps);
       s.bps[i] = (int)bps;
       continue;

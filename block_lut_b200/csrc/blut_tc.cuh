@@ -29,6 +29,8 @@
 // and the tensor memory is released before the CTA exits.
 #pragma once
 
+#include <type_traits>
+
 #include "blut_mm.cuh"
 
 namespace blut {
@@ -1062,49 +1064,67 @@ __device__ __forceinline__ void tc_gemv_ptrs(const TcParams& p, const uint8_t* b
   pp.tab = tab;
 }
 
-// One pass over the slice's weights for NT tokens of the chunk; `cur`
-// holds the slice's first half, already loaded.
-template <class Dec, int NT>
-__device__ __forceinline__ void tc_gemv_pass(const TcParams& p, const uint8_t* base, int pt, int b0, int b1, int row,
-                                             uint32_t tab, const float* xs, int ldx, typename Dec::Half& cur,
+// Halves (64-column pieces; dense: 32-column blocks) a GEMV thread keeps in
+// flight: four, or two when a half's registers exceed 64 bytes.
+template <class Dec>
+__host__ __device__ constexpr int tc_gemv_pf() {
+  return Dec::kDense ? 4 : (sizeof(typename Dec::Half) <= 64 ? 4 : 2);
+}
+template <bool BF16>
+struct TcDenseBlk {
+  uint4 v[4];
+};
+
+// Loads piece i (half i % kHalves of block b0 + i / kHalves; dense: block
+// b0 + i) of this thread's row.
+template <class Dec, class U>
+__device__ __forceinline__ void tc_gemv_load(const TcParams& p, const uint8_t* base, int pt, int b0, int i, int row,
+                                             uint32_t tab, U& u) {
+  const int kh = Dec::kDense ? 1 : Dec::kHalves;
+  TcPtrs pp;
+  tc_gemv_ptrs<Dec>(p, base, b0 + i / kh, pt, tab, pp);
+  if constexpr (Dec::kDense) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) u.v[k] = *reinterpret_cast<const uint4*>(pp.p[0] + (k * kTcRows + row) * 16);
+  } else {
+    Dec::load_half(pp, row, i % kh, u);
+  }
+}
+
+// One pass over the slice's n pieces for NT tokens of the chunk: a register
+// ring of PF pieces, refilled as each is consumed, so a thread has PF loads
+// in flight.  ring[] arrives with pieces 0 .. PF-1 already requested.
+template <class Dec, int NT, class U>
+__device__ __forceinline__ void tc_gemv_pass(const TcParams& p, const uint8_t* base, int pt, int b0, int n, int row,
+                                             uint32_t tab, const float* xs, int ldx, U (&ring)[tc_gemv_pf<Dec>()],
                                              float (&out)[NT]) {
+  constexpr int PF = tc_gemv_pf<Dec>();
+  constexpr int W = Dec::kDense ? Dec::KB : 64;  // columns per piece
   float2 acc[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t] = make_float2(0.f, 0.f);
-  if constexpr (Dec::kDense) {
-    // KB = 32 columns: four 16-byte units of 8 values per row
-    for (int b = b0; b < b1; ++b) {
-      TcPtrs pp;
-      tc_gemv_ptrs<Dec>(p, base, b, pt, tab, pp);
-      uint32_t o[16];
+  for (int i0 = 0; i0 < n; i0 += PF) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint4 v = *reinterpret_cast<const uint4*>(pp.p[0] + (u * kTcRows + row) * 16);
-        o[4 * u] = v.x; o[4 * u + 1] = v.y; o[4 * u + 2] = v.z; o[4 * u + 3] = v.w;
-      }
-      tc_gemv_fma32<Dec::kBF16, NT>(o, xs, ldx, (b - b0) * Dec::KB, acc);
-    }
-  } else {
-    typename Dec::Half nxt;
-    for (int b = b0; b < b1; ++b) {
-#pragma unroll
-      for (int h = 0; h < Dec::kHalves; ++h) {
-        // prefetch the next half (of this block or the next one)
-        const bool last_h = h == Dec::kHalves - 1;
-        const int nb = last_h ? b + 1 : b;
-        if (nb < b1) {
-          TcPtrs pn;
-          tc_gemv_ptrs<Dec>(p, base, nb, pt, tab, pn);
-          Dec::load_half(pn, row, last_h ? 0 : h + 1, nxt);
-        }
-        const int c = (b - b0) * Dec::KB + h * 64;
-#pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
+    for (int j = 0; j < PF; ++j) {
+      const int i = i0 + j;
+      if (i < n) {
+        if constexpr (Dec::kDense) {
           uint32_t o[16];
-          Dec::lookup_q(cur, qq, o, p.mul);
-          tc_gemv_fma32<Dec::kBF16, NT>(o, xs, ldx, c + 32 * qq, acc);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            o[4 * k] = ring[j].v[k].x; o[4 * k + 1] = ring[j].v[k].y;
+            o[4 * k + 2] = ring[j].v[k].z; o[4 * k + 3] = ring[j].v[k].w;
+          }
+          tc_gemv_fma32<Dec::kBF16, NT>(o, xs, ldx, i * W, acc);
+        } else {
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            uint32_t o[16];
+            Dec::lookup_q(ring[j], qq, o, p.mul);
+            tc_gemv_fma32<Dec::kBF16, NT>(o, xs, ldx, i * W + 32 * qq, acc);
+          }
         }
-        cur = nxt;
+        if (i + PF < n) tc_gemv_load<Dec>(p, base, pt, b0, i + PF, row, tab, ring[j]);
       }
     }
   }
@@ -1117,37 +1137,38 @@ __device__ __forceinline__ void tc_gemv_pass(const TcParams& p, const uint8_t* b
 template <class Dec, int NT>
 __global__ void __launch_bounds__(kTcRows, 4) tc_gemv_kernel(const TcParams p) {
   constexpr int KB = Dec::KB;
+  constexpr int PF = tc_gemv_pf<Dec>();
+  using U = typename std::conditional<Dec::kDense, TcDenseBlk<Dec::kBF16>, typename Dec::Half>::type;
   const int64_t cta = blockIdx.x;
   const int s = (int)(cta % p.ks);
   const int pt = (int)((cta / p.ks) % p.ntiles);
   const int gi = (int)(cta / ((int64_t)p.ks * p.ntiles));
-  if (gi >= *p.gt.n_groups) return;
+  // the group's entries are in bounds for every gi below the group bound, so
+  // they load together with the group count
+  const int ng = *p.gt.n_groups;
+  const int ntok = p.gt.ntok[gi], nt0 = p.gt.nt0[gi], ex = p.gt.expert[gi], slot0 = p.gt.slot0[gi];
+  if (gi >= ng) return;
   const int b0 = s * p.bps, b1 = min(p.nblocks, b0 + p.bps);
   if (b0 >= b1) return;
   const int row = threadIdx.x;
-  const int ntok = p.gt.ntok[gi], nt0 = p.gt.nt0[gi];
-  const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
+  const uint8_t* base = p.w + (int64_t)ex * p.wstride;
+  const int n = (b1 - b0) * (Dec::kDense ? 1 : Dec::kHalves);  // pieces of the slice
   extern __shared__ __align__(16) uint8_t gsm[];
   uint32_t tab = 0;
   if constexpr (Dec::kR8) tab = smem_u32(gsm) + (row & 31) * 4;
-  // the slice's first weights are in flight while the activations are staged
-  typename Dec::Half first;
-  if constexpr (!Dec::kDense) {
-    TcPtrs pp;
-    tc_gemv_ptrs<Dec>(p, base, b0, pt, tab, pp);
-    Dec::load_half(pp, row, 0, first);
-  }
-  if constexpr (Dec::kR8) tc_fill_r8_table(reinterpret_cast<uint32_t*>(gsm), p.r8_table);
   float* xs = reinterpret_cast<float*>(gsm + tc_table_bytes<Dec>());  // [NT][ldx]
   const int ncols = (b1 - b0) * KB, ldx = ncols;
   for (int c0 = 0; c0 < ntok; c0 += NT) {
     const int nc = min(NT, ntok - c0);
-    if (c0 > 0 && !Dec::kDense) {  // a further pass reloads the slice's first half
-      TcPtrs pp;
-      tc_gemv_ptrs<Dec>(p, base, b0, pt, tab, pp);
-      Dec::load_half(pp, row, 0, first);
+    // the slice's first pieces are in flight while the activations are staged
+    U ring[PF];
+#pragma unroll
+    for (int j = 0; j < PF; ++j)
+      if (j < n) tc_gemv_load<Dec>(p, base, pt, b0, j, row, tab, ring[j]);
+    if (c0 == 0) {
+      if constexpr (Dec::kR8) tc_fill_r8_table(reinterpret_cast<uint32_t*>(gsm), p.r8_table);
     }
-    __syncthreads();  // the previous pass's reads of xs are done (and the R8 table is filled)
+    __syncthreads();  // the previous pass's reads of xs are done
     for (int i = threadIdx.x; i < NT * ncols; i += blockDim.x) {
       const int t = i / ncols, col = i - t * ncols;
       float v = 0.f;
@@ -1158,9 +1179,9 @@ __global__ void __launch_bounds__(kTcRows, 4) tc_gemv_kernel(const TcParams p) {
       }
       xs[t * ldx + col] = v;
     }
-    __syncthreads();
+    __syncthreads();  // xs (and the R8 table) complete
     float out[NT];
-    tc_gemv_pass<Dec, NT>(p, base, pt, b0, b1, row, tab, xs, ldx, first, out);
+    tc_gemv_pass<Dec, NT>(p, base, pt, b0, n, row, tab, xs, ldx, ring, out);
     if (p.pair) {
       // partial sums [item = (group, unit, slice)][gate | up][row][token]
       const int64_t item = ((int64_t)gi * p.units + (pt >> 1)) * p.ks + s;
@@ -1169,7 +1190,7 @@ __global__ void __launch_bounds__(kTcRows, 4) tc_gemv_kernel(const TcParams p) {
       for (int t = 0; t < NT; ++t)
         if (t < nc) dst[t] = out[t];
     } else {
-      float* y = p.y_out + (int64_t)s * p.y_sstride + (int64_t)(p.gt.slot0[gi] + c0) * p.y_ld + pt * kTcRows + row;
+      float* y = p.y_out + (int64_t)s * p.y_sstride + (int64_t)(slot0 + c0) * p.y_ld + pt * kTcRows + row;
 #pragma unroll
       for (int t = 0; t < NT; ++t)
         if (t < nc) y[(int64_t)t * p.y_ld] = out[t];

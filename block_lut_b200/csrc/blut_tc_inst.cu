@@ -34,6 +34,26 @@ static cudaError_t launch_tc_dense(const blut_mat_desc& d, const TcParams& p, in
                               : launch_tc<TcDecDense<false>, MT>(p, sms, stream);
 }
 
+// Column blocks per small-batch GEMV item: the blocks holding the pieces a
+// thread keeps in flight (tc_gemv_pf), at least one.
+int tc_gemv_blocks(const blut_mat_desc& d) {
+  int pf = 4, kb = tc_block_cols(d.format, d.group);
+  switch (d.format) {
+    case BLUT_FMT_DENSE: return 4;
+    case BLUT_FMT_R8: pf = tc_gemv_pf<TcDecR8>(); break;
+    case BLUT_FMT_NESTED:
+      pf = d.tier == 1 ? tc_gemv_pf<TcDecB2<64>>()
+                       : (d.group == 32 ? tc_gemv_pf<TcDecNested<32>>() : tc_gemv_pf<TcDecNested<64>>());
+      break;
+    case BLUT_FMT_B:
+      pf = d.bits == 4 ? (d.group == 32 ? tc_gemv_pf<TcDecB4<32>>() : tc_gemv_pf<TcDecB4<64>>())
+         : d.bits == 3 ? (d.group == 32 ? tc_gemv_pf<TcDecB3<32>>() : tc_gemv_pf<TcDecB3<64>>())
+                       : tc_gemv_pf<TcDecB2<64>>();
+      break;
+  }
+  return std::max(1, pf * 64 / kb);
+}
+
 // group_tokens: 32 or 128 (tcgen05 matmul), 1 (small-batch GEMV).
 cudaError_t launch_tc_mm(const blut_mat_desc& d, const TcParams& p, int group_tokens, int sms, cudaStream_t stream) {
   if (group_tokens != 32 && group_tokens != 128 && group_tokens != 1) return cudaErrorInvalidValue;
