@@ -327,6 +327,7 @@ struct TcDecB4 {
   static constexpr bool kDense = false;
   static constexpr bool kBF16 = false;
   static constexpr bool kR8 = false;
+  static constexpr int kHalfBytes = G == 32 ? 96 : 64;  // bytes of a half's codes and tables a thread holds
   static constexpr int KB = G > 64 ? G : 64;  // columns per block
   static constexpr int kHalves = KB / 64;     // 64-column halves per block
   static constexpr int kNumPlanes = 2;
@@ -359,6 +360,7 @@ struct TcDecB2 {
   static constexpr bool kDense = false;
   static constexpr bool kBF16 = false;
   static constexpr bool kR8 = false;
+  static constexpr int kHalfBytes = G == 32 ? 32 : 24;
   static constexpr int KB = G > 64 ? G : 64;
   static constexpr int kHalves = KB / 64;
   static constexpr int kNumPlanes = 2;
@@ -390,6 +392,7 @@ struct TcDecB3 {
   static constexpr bool kDense = false;
   static constexpr bool kBF16 = false;
   static constexpr bool kR8 = false;
+  static constexpr int kHalfBytes = G == 32 ? 56 : 40;
   static constexpr int KB = G > 64 ? G : 64;
   static constexpr int kHalves = KB / 64;
   static constexpr int kNumPlanes = 3;
@@ -428,6 +431,7 @@ struct TcDecNested {
   static constexpr bool kDense = false;
   static constexpr bool kBF16 = false;
   static constexpr bool kR8 = false;
+  static constexpr int kHalfBytes = G == 32 ? 96 : 64;
   static constexpr int KB = G > 64 ? G : 64;
   static constexpr int kHalves = KB / 64;
   static constexpr int kNumPlanes = 3;
@@ -488,6 +492,7 @@ struct TcDecR8 {
   static constexpr bool kDense = false;
   static constexpr bool kBF16 = true;
   static constexpr bool kR8 = true;
+  static constexpr int kHalfBytes = 72;
   static constexpr int KB = 64;
   static constexpr int kHalves = 1;
   static constexpr int kNumPlanes = 2;
@@ -536,6 +541,7 @@ struct TcDecDense {
   static constexpr bool kDense = true;
   static constexpr bool kBF16 = BF16;
   static constexpr bool kR8 = false;
+  static constexpr int kHalfBytes = 64;
   static constexpr int KB = 32;
   static constexpr int kHalves = 0;
   static constexpr int kNumPlanes = 1;
@@ -1068,7 +1074,7 @@ __device__ __forceinline__ void tc_gemv_ptrs(const TcParams& p, const uint8_t* b
 // flight: four, or two when a half's registers exceed 64 bytes.
 template <class Dec>
 __host__ __device__ constexpr int tc_gemv_pf() {
-  return Dec::kDense ? 4 : (sizeof(typename Dec::Half) <= 64 ? 4 : 2);
+  return Dec::kDense ? 4 : (Dec::kHalfBytes <= 64 ? 4 : 2);
 }
 template <bool BF16>
 struct TcDenseBlk {
