@@ -38,8 +38,10 @@ struct MoESplit {
 };
 
 // Batches of at most this many tokens run the tcgen05-layout matrices
-// through the small-batch GEMV (tc_gemv_kernel).
-constexpr int kGemvMaxTokens = 4;
+// through the small-batch GEMV (tc_gemv_kernel).  Measured on config 1
+// (Qwen1.5-MoE, 24 layers): one token 529 tokens/s against 495 on the
+// tcgen05 matmul; two and four tokens are faster on the tcgen05 matmul.
+constexpr int kGemvMaxTokens = 1;
 
 constexpr int kNumCounters = 4;  // routed gate/up, routed down, shared gate/up, shared down
 

@@ -258,7 +258,6 @@ int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const v
     t.ks = p.ks;
     t.bps = p.bps;
     t.gemv_groups = p.groups;
-    t.gemv_nt = m == 1 ? 1 : kGemvTok;
     if (launch_tc_mm(d, t, p.gemv ? 1 : p.gtok, sms, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
   } else {
     MMParams mp{};

@@ -776,7 +776,6 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.y_sstride = y_sstride;
       const bool gemv = ws.split.gemv[counter / 2];
       t.gemv_groups = ws.split.groups[counter];
-      t.gemv_nt = a.num_tokens == 1 ? 1 : kGemvTok;
       if (launch_tc_mm(d, t, gemv ? 1 : ws.split.gtok[counter / 2], sms, stream) != cudaSuccess)
         return BLUT_ERR_LAUNCH;
       if (pair && (t.ks > 1 || gemv)) {

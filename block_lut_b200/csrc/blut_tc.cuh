@@ -121,7 +121,6 @@ struct TcParams {
   TcMul mul;               // tc_mul_consts()
   const uint16_t* r8_table;  // FMT_R8: the tier's bf16 [256] table
   int64_t gemv_groups;     // small-batch GEMV: bound on the token groups (the grid is sized by it)
-  int gemv_nt;             // small-batch GEMV: tokens accumulated per pass (1 or kGemvTok)
   int* status;
   int stages;              // weight stages (LUT formats) or weight + activation stages (dense)
   int xstages;             // activation stages (LUT formats)
@@ -1030,7 +1029,6 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
 // loaded while the current one is decoded.  It writes exactly what
 // tc_mm_kernel writes (gate/up partial sums for splitk_silu_kernel, or fp32
 // output rows per K slice), so the kernels around it are unchanged.
-constexpr int kGemvTok = 4;         // tokens accumulated per pass over the weights (batches > 1 token)
 constexpr int kGemvMaxCols = 2048;  // columns per CTA (K slice): at most 64 KB of staged fp32 activations
 
 template <bool BF16>
@@ -1138,8 +1136,8 @@ __device__ __forceinline__ void tc_gemv_pass(const TcParams& p, const uint8_t* b
   for (int t = 0; t < NT; ++t) out[t] = acc[t].x + acc[t].y;
 }
 
-// NT: tokens accumulated per pass over the weights (1, or kGemvTok with
-// groups of more tokens taking several passes).
+// NT: tokens accumulated per pass over the weights; a group of more tokens
+// takes several passes.
 template <class Dec, int NT>
 __global__ void __launch_bounds__(kTcRows, 4) tc_gemv_kernel(const TcParams p) {
   constexpr int KB = Dec::KB;
@@ -1204,8 +1202,8 @@ __global__ void __launch_bounds__(kTcRows, 4) tc_gemv_kernel(const TcParams p) {
   }
 }
 
-// Host launch of the GEMV: one CTA per (group bound, tile, K slice);
-// p.gemv_nt tokens per pass (1 or kGemvTok).
+// Host launch of the GEMV: one CTA per (group bound, tile, K slice), one
+// token per pass (the GEMV serves single-token batches).
 template <class Dec, int NT>
 inline cudaError_t launch_tc_gemv_nt(const TcParams& p, int64_t group_bound, cudaStream_t stream) {
   const int64_t ctas = group_bound * p.ntiles * p.ks;
@@ -1228,8 +1226,7 @@ inline cudaError_t launch_tc_gemv_nt(const TcParams& p, int64_t group_bound, cud
 }
 template <class Dec>
 inline cudaError_t launch_tc_gemv(const TcParams& p, int64_t group_bound, cudaStream_t stream) {
-  return p.gemv_nt == 1 ? launch_tc_gemv_nt<Dec, 1>(p, group_bound, stream)
-                        : launch_tc_gemv_nt<Dec, kGemvTok>(p, group_bound, stream);
+  return launch_tc_gemv_nt<Dec, 1>(p, group_bound, stream);
 }
 
 // One CTA per (physical tile, block), one thread per row: decode the row's
