@@ -683,6 +683,37 @@ int stage_done(const char* stage, cudaStream_t s) {
   return BLUT_OK;
 }
 
+// A side stream and its fork / join events per device and host thread, made
+// on first use.  They are not made while `stream` is being captured into a
+// CUDA graph (the forward then runs on `stream` alone), so a capture that
+// wants the concurrency follows one ordinary call on that thread.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+static SideStream* side_stream(cudaStream_t stream) {
+  constexpr int kMaxDevices = 64;
+  thread_local SideStream per_device[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  SideStream& ss = per_device[dev];
+  if (ss.s) return &ss;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
+  SideStream n;
+  if (cudaStreamCreateWithFlags(&n.s, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&n.fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&n.join, cudaEventDisableTiming) != cudaSuccess) {
+    if (n.join) cudaEventDestroy(n.join);
+    if (n.fork) cudaEventDestroy(n.fork);
+    if (n.s) cudaStreamDestroy(n.s);
+    cudaGetLastError();
+    return nullptr;
+  }
+  ss = n;
+  return &ss;
+}
+
 int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaStream_t stream) {
   int rc = validate_moe(a);
   if (rc != BLUT_OK) return rc;
@@ -750,6 +781,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   // activations, down writes fp32 rows.
   const GroupTab routed{ws.pp.meta + 0, ws.pp.g_expert, ws.pp.g_slot0, ws.pp.g_ntok, ws.pp.g_nt0};
   const GroupTab shared{ws.pp.meta + 2, ws.pp.sg_expert, ws.pp.sg_slot0, ws.pp.sg_ntok, ws.pp.sg_nt0};
+  cudaStream_t cur = stream;  // stream of the pass being launched
   auto pass = [&](const blut_mat_desc& d, const void* w, int64_t stride, const GroupTab& gt, double est,
                   const uint8_t* bin, uint8_t* act, int out_k, float* y, int counter, float* part,
                   int64_t y_sstride, const blut_mat_desc* next) -> int {
@@ -776,15 +808,15 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.y_sstride = y_sstride;
       const bool gemv = ws.split.gemv[counter / 2];
       t.gemv_groups = ws.split.groups[counter];
-      if (launch_tc_mm(d, t, gemv ? 1 : ws.split.gtok[counter / 2], sms, stream) != cudaSuccess)
+      if (launch_tc_mm(d, t, gemv ? 1 : ws.split.gtok[counter / 2], sms, cur) != cudaSuccess)
         return BLUT_ERR_LAUNCH;
       if (pair && (t.ks > 1 || gemv)) {
         // sum the gate/up slices in order, SiLU(gate) * up into the down projection's activations
         const dim3 grid((unsigned)(ws.split.groups[counter] * t.units), (unsigned)(kTcRows * 32 / 256));
         if (a.dtype == BLUT_BF16)
-          splitk_silu_kernel<true><<<grid, 256, 0, stream>>>(part, t.ks, t.units, gt, act, t.out_kb, t.ntstride);
+          splitk_silu_kernel<true><<<grid, 256, 0, cur>>>(part, t.ks, t.units, gt, act, t.out_kb, t.ntstride);
         else
-          splitk_silu_kernel<false><<<grid, 256, 0, stream>>>(part, t.ks, t.units, gt, act, t.out_kb, t.ntstride);
+          splitk_silu_kernel<false><<<grid, 256, 0, cur>>>(part, t.ks, t.units, gt, act, t.out_kb, t.ntstride);
       }
       return cudaGetLastError() == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
     }
@@ -802,36 +834,50 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
     m.y_ld = H;
     m.W = choose_units_per_item(est, m.units, sms);
     m.b_ntiles = b_ntiles;
-    return launch_lut_mm(d, pair, m, sms, stream) == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
+    return launch_lut_mm(d, pair, m, sms, cur) == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
   };
   cudaEvent_t* ev = a.prof_events ? (cudaEvent_t*)a.prof_events : nullptr;
 
-  // 4. gate/up + SiLU*up (routed, then shared)
+  // 4. The shared expert depends only on the gathered activations, so its
+  // gate/up and down passes run on a side stream beside the routed passes
+  // (when one is available, see side_stream); the combine waits for both.
+  SideStream* side = sh ? side_stream(stream) : nullptr;
+  auto shared_passes = [&]() -> int {
+    int r;
+    if ((r = pass(a.s13, a.s13_tiled, 0, shared, est_sgroups, ws.xfs, ws.afs, a.shared_inter, nullptr, 2,
+                  ws.part_s, 0, &a.s2)) != BLUT_OK)
+      return r;
+    if ((r = stage_done("shared gate/up", cur)) != BLUT_OK) return r;
+    if ((r = pass(a.s2, a.s2_tiled, 0, shared, est_sgroups, ws.afs, nullptr, 0, ws.ys, 3, nullptr,
+                  ws.ys_sstride, nullptr)) != BLUT_OK)
+      return r;
+    return stage_done("shared down", cur);
+  };
+  if (side) {
+    if (cudaEventRecord(side->fork, stream) != cudaSuccess || cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess)
+      return BLUT_ERR_CUDA;
+    cur = side->s;
+    if ((rc = shared_passes()) != BLUT_OK) return rc;
+    if (cudaEventRecord(side->join, side->s) != cudaSuccess) return BLUT_ERR_CUDA;
+    cur = stream;
+  }
+  // 5. routed gate/up + SiLU*up, then down
   if (ev && cudaEventRecord(ev[0], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if ((rc = pass(a.w13, a.w13_tiled, a.w13_stride, routed, est_groups, ws.xf, ws.af, a.inter, nullptr, 0,
-                 ws.part_r, 0, &a.w2)) !=
-      BLUT_OK)
+                 ws.part_r, 0, &a.w2)) != BLUT_OK)
     return rc;
   if ((rc = stage_done("routed gate/up", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[1], stream) != cudaSuccess) return BLUT_ERR_INVALID;
-  if (sh) {
-    if ((rc = pass(a.s13, a.s13_tiled, 0, shared, est_sgroups, ws.xfs, ws.afs, a.shared_inter, nullptr, 2,
-                   ws.part_s, 0, &a.s2)) !=
-        BLUT_OK)
-      return rc;
-    if ((rc = stage_done("shared gate/up", stream)) != BLUT_OK) return rc;
-  }
-  // 5. down (routed, then shared)
   if (ev && cudaEventRecord(ev[2], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if ((rc = pass(a.w2, a.w2_tiled, a.w2_stride, routed, est_groups, ws.af, nullptr, 0, ws.y, 1, nullptr,
                  ws.y_sstride, nullptr)) != BLUT_OK)
     return rc;
   if ((rc = stage_done("routed down", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[3], stream) != cudaSuccess) return BLUT_ERR_INVALID;
-  if (sh) {
-    if ((rc = pass(a.s2, a.s2_tiled, 0, shared, est_sgroups, ws.afs, nullptr, 0, ws.ys, 3, nullptr,
-                   ws.ys_sstride, nullptr)) != BLUT_OK) return rc;
-    if ((rc = stage_done("shared down", stream)) != BLUT_OK) return rc;
+  if (side) {
+    if (cudaStreamWaitEvent(stream, side->join, 0) != cudaSuccess) return BLUT_ERR_CUDA;
+  } else if (sh) {
+    if ((rc = shared_passes()) != BLUT_OK) return rc;
   }
 
   // 6. combine

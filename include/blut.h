@@ -265,7 +265,13 @@ BLUT_API size_t blut_moe_workspace_size(const blut_moe_args* args);
  * with e = topk_ids[t, j]; every active (token, expert) pair of the layer runs
  * in one launch per stage (router, plan, gate/up+SiLU*up, down, combine).
  * Replaces LUTFusedMoEMethod.apply (vllm_lut/quant_method.py:230-279) and
- * fused_lut_moe (vllm_lut/fast_moe.py:30-80).  Decode regime: T*k <= 2048. */
+ * fused_lut_moe (vllm_lut/fast_moe.py:30-80).  Any T*k up to 2^22 slots
+ * (decode and prefill).  Work is ordered after earlier work on `stream` and
+ * the call returns with all of it ordered before later work on `stream`;
+ * the shared expert's passes run on a library-owned side stream (one per
+ * device and host thread, made by the first call that is not inside a stream
+ * capture) forked from and joined back into `stream` with events, so the
+ * call can be captured into a CUDA graph. */
 BLUT_API int blut_moe_forward(const blut_moe_args* args, void* workspace, size_t workspace_bytes,
                      void* stream);
 
