@@ -54,7 +54,7 @@ PREFILL_METRIC = "LUT-MoE prefill tokens/s; grouped LUT-GEMM tensor TFLOP/s"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=None, help="decode tokens per rank (workload default)")
