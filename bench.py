@@ -54,7 +54,8 @@ PREFILL_METRIC = "LUT-MoE prefill tokens/s; grouped LUT-GEMM tensor TFLOP/s"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--steps", type=int, default=None,
+                   help="timed steps (default: 200 decode, 100 qwen3, 5 prefill / sweep; about a second each)")
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=None, help="decode tokens per rank (workload default)")
@@ -75,6 +76,8 @@ def parse():
     p.add_argument("--sweep-groups", default="32,64,128")
     p.add_argument("--sweep-m", default="1,2,4,8,16,64,256,1024,4096")
     a = p.parse_args()
+    if a.steps is None:
+        a.steps = {"decode": 200, "qwen3": 100}.get(a.workload, 5)
     a.shape = QWEN3 if a.workload == "qwen3" else DSV2 if a.workload == "prefill" else QWEN
     a.batch = a.batch if a.batch is not None else a.shape.get("BATCH", 32)
     a.layers = a.layers if a.layers is not None else a.shape["LAYERS"]
