@@ -442,8 +442,8 @@ static double expected_active(int T, int k, int E) {
 // gate/up passes split at most 8 ways (their partial sums go through
 // memory), down passes 16.  Routed passes split while the expected work
 // items are fewer than two per resident CTA (two CTAs per SM); the shared
-// expert, whose item count is exact, takes the split with the fewest rounds
-// of items times blocks per item.
+// expert does not split (its passes overlap the routed ones).  The
+// small-batch GEMV sizes its slices by the pieces a thread keeps in flight.
 void moe_split(const blut_moe_args& a, MoESplit& s) {
   const int sms = num_sms();
   const int64_t T = a.num_tokens, K = a.top_k, E = a.num_experts, S = T * K;
@@ -489,23 +489,10 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
       // routed passes: the group count is only an expectation, so split
       // while the expected items are fewer than two per resident CTA
       while (ks * 2 <= max_ks && L.nchunks / (ks * 2) >= 2 && est * ks < 4.0 * sms) ks *= 2;
-    } else {
-      // shared expert: the items are known, so pick the split with the
-      // fewest block-times on the busiest CTA, rounds x (blocks + 1), over
-      // the 2 x sms resident CTAs (ties keep fewer slices)
-      const int64_t slots = 2LL * sms;
-      int64_t best = -1;
-      for (int c = 1; c <= max_ks && L.nchunks / c >= 2; ++c) {
-        const int64_t bps_c = (L.nchunks + c - 1) / c;
-        const int64_t ks_c = (L.nchunks + bps_c - 1) / bps_c;
-        const int64_t items = gmax_s * s.units[i] * ks_c;
-        const int64_t cost = ((items + slots - 1) / slots) * (bps_c + 1);
-        if (best < 0 || cost < best) {
-          best = cost;
-          ks = c;
-        }
-      }
     }
+    // the shared expert (i >= 2) keeps ks = 1: its passes run on a side
+    // stream beside the routed ones, so fewer, longer items cost nothing
+    // there and leave the combine one slice to read
     const int bps = (int)((L.nchunks + ks - 1) / ks);
     s.ks[i] = (int)((L.nchunks + bps - 1) / bps);
     s.bps[i] = bps;
