@@ -13,7 +13,8 @@ One layer:
 3. each rank runs its local experts on the N*T received tokens in one
    ``blut_moe_forward`` (empty slots are skipped) with fp32 partial sums;
 4. combine: ``all_to_all_single`` sends the partials back; the owner sums the
-   N partials and adds its shared expert.
+   N partials and adds its shared expert, which ran on a side stream beside
+   the exchanges and the local experts (it needs only the rank's own tokens).
 
 These are the message shapes of the reference's only EP code (the DeepSeek
 remote code's dispatch/combine all_to_all, models/deepseek/modeling_deepseek.py:604-660).
@@ -100,19 +101,35 @@ class EPMoELayer:
             s13, s2 = shared
             ex = LUTExperts.from_quantized([dense_matrix(s13)], [dense_matrix(s2)])
             self.shared = LUTMoELayer(ex, 1)
+            self.shared.ws_slot = 1  # runs concurrently with self.local: its own workspace
             self._zero_ids = None
+            self._side = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         T, H = x.shape
         ids, tw, sg = router(x, self.router_w, self.top_k, self.renorm, shared_gate=self.shared is not None)
+        shared_out = None
+        if self.shared is not None:
+            # the shared expert needs only this rank's tokens: it runs on a side
+            # stream while the tokens are exchanged and the local experts run;
+            # every tensor it touches was made on the main stream, which waits
+            # for the side stream before returning
+            if self._zero_ids is None or self._zero_ids.shape[0] != T:
+                self._zero_ids = torch.zeros(T, 1, dtype=torch.int32, device=x.device)
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=x.device)
+            main = torch.cuda.current_stream(x.device)
+            shared_out = torch.empty(T, H, dtype=torch.float32, device=x.device)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                self.shared.forward(x, self._zero_ids, sg.view(T, 1), out=shared_out, out_f32=True)
         sx, si, sw = build_dispatch(x, ids, tw, self.owner, self.local_id, self.world)
         rx, ri, rw = exchange(sx, si, sw, self.group)
         part = self.local.forward(rx.view(-1, H), ri.view(-1, self.top_k), rw.view(-1, self.top_k), out_f32=True)
         out = combine(part.view(self.world, T, H), self.group)
-        if self.shared is not None:
-            if self._zero_ids is None or self._zero_ids.shape[0] != T:
-                self._zero_ids = torch.zeros(T, 1, dtype=torch.int32, device=x.device)
-            out += self.shared.forward(x, self._zero_ids, sg.view(T, 1), out_f32=True)
+        if shared_out is not None:
+            main.wait_stream(self._side)
+            out += shared_out
         return out.to(x.dtype)
 
     __call__ = forward

@@ -66,5 +66,5 @@ class LUTLinear:
 
     def check_status(self, stream=None) -> None:
         """Raise if a device-side wait of the last call timed out."""
-        ws = workspace(self.buf.device, 256)
+        ws = workspace(self.buf.device, 256, 0)
         _lib.check(_lib.lib().blut_moe_check_status(ws.data_ptr(), _lib.stream_ptr(stream)), "matmul status")

@@ -86,9 +86,11 @@ class SharedExpert:
 _WS: dict = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Grow-only workspace per device (layers run in stream order and share it)."""
-    key = (device.type, device.index)
+def workspace(device: torch.device, nbytes: int, slot: int = 0) -> torch.Tensor:
+    """Grow-only workspace per (device, slot).  Layers whose calls run in one
+    stream's order share a slot; a layer that runs concurrently with others
+    on another stream takes a slot of its own (``LUTMoELayer.ws_slot``)."""
+    key = (device.type, device.index, slot)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
@@ -111,6 +113,7 @@ class LUTMoELayer:
         self.router_w = None if router_w is None else router_w.to(experts.fmt.compute_dtype).contiguous()
         self.renorm = bool(renorm)
         self.shared = shared
+        self.ws_slot = 0  # workspace slot (see workspace); 1 for a layer run beside others on a side stream
         self.shared_gate_mode = int(shared_gate_mode)
         self.dtype = experts.fmt.compute_dtype
         self._args = self._make_args()
@@ -167,7 +170,7 @@ class LUTMoELayer:
         need = lib.blut_moe_workspace_size(C.byref(a))
         if need == 0:
             raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
-        ws = workspace(x2.device, need)
+        ws = workspace(x2.device, need, self.ws_slot)
         _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
                    "moe_forward")
         if out is not None and res.data_ptr() != out.data_ptr():
@@ -215,7 +218,7 @@ class LUTMoELayer:
             need = lib.blut_moe_workspace_size(C.byref(a))
             if need == 0:
                 raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
-            ws = workspace(x2.device, need)
+            ws = workspace(x2.device, need, self.ws_slot)
             _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
                        "moe_forward")
         finally:
@@ -224,7 +227,7 @@ class LUTMoELayer:
 
     def check_status(self, stream=None) -> None:
         """Synchronise and raise if a kernel reported a device-side error."""
-        ws = _WS.get((self.experts.w13.device.type, self.experts.w13.device.index))
+        ws = _WS.get((self.experts.w13.device.type, self.experts.w13.device.index, self.ws_slot))
         if ws is not None:
             _lib.check(_lib.lib().blut_moe_check_status(ws.data_ptr(), _lib.stream_ptr(stream)), "device status")
 
