@@ -38,17 +38,16 @@ namespace blut {
 constexpr int kTcDecodeWarps = 8;  // one decode set: 2 tiles x 4 tensor-memory lane quarters
 // Decode sets per CTA, taking turns over the column blocks of an item.
 // Decode (MT = 32) runs two CTAs per SM with one set each (one producer and
-// one MMA thread per 8 decode warps); measured faster than one CTA with three
-// sets.  Prefill (MT = 128) runs one CTA per SM with two sets.
-constexpr int kTcNarrowSets = 1;
-constexpr int kTcNarrowCtas = 2;  // CTAs per SM in decode (2 measured faster than 3 with one A slot each)
+// one MMA thread per 8 decode warps).  That measured faster than one CTA with
+// two or three sets (4 or 6 A slots) and than three CTAs with one A slot
+// each.  Prefill (MT = 128) runs one CTA per SM with two sets.
 template <int MT>
 constexpr int tc_sets() {
-  return MT == 32 ? kTcNarrowSets : 2;
+  return MT == 32 ? 1 : 2;
 }
 template <int MT>
 constexpr int tc_ctas_per_sm() {
-  return MT == 32 && kTcNarrowSets == 1 ? kTcNarrowCtas : 1;
+  return MT == 32 ? 2 : 1;
 }
 template <int MT>
 constexpr int tc_threads() {
@@ -67,13 +66,12 @@ constexpr int kTcQueue = 4;          // depth of the shared-memory item queue
 // columns of K) after it; dense weights need no A slots and double-buffer
 // the accumulators so the MMA runs one item ahead of the epilogue.
 template <int MT>
-constexpr int tc_aslots() {  // A slots: two per decode set at one CTA per SM (at most 6)
-  return tc_ctas_per_sm<MT>() == 3 ? 1
-         : tc_ctas_per_sm<MT>() == 2 ? 3 : (2 * tc_sets<MT>() > 6 ? 6 : 2 * tc_sets<MT>());
+constexpr int tc_aslots() {  // A slots: three at two CTAs per SM, two per decode set at one
+  return tc_ctas_per_sm<MT>() == 2 ? 3 : 2 * tc_sets<MT>();
 }
 template <int MT>
 constexpr int tc_cols(bool dense) {
-  return tc_ctas_per_sm<MT>() == 3 ? 128 : tc_ctas_per_sm<MT>() == 2 ? (dense ? 4 * MT : 256) : 512;
+  return tc_ctas_per_sm<MT>() == 2 ? (dense ? 4 * MT : 256) : 512;
 }
 
 // Multipliers handed to the decode (see tc_mulhi): shifts and selector
@@ -863,18 +861,11 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
             tc_fence_after();
             const uint32_t aslot = tmem + lane_base + kACol0 + j * 64 + t * 32;
             if (active) {
-              tc_st16(aslot, qa);
-              if constexpr (tc_ctas_per_sm<MT>() >= 3) {  // register-lean: one quarter buffer
-                tc_wait_st_keep(qa);
-                Dec::lookup_q(hd, 1, qa, p.mul);
-                tc_st16(aslot + 16, qa);
-                tc_wait_st_keep(qa);
-              } else {  // the first quarter's store overlaps the second's lookups
-                Dec::lookup_q(hd, 1, qb, p.mul);
-                tc_st16(aslot + 16, qb);
-                tc_wait_st_keep(qa);
-                tc_wait_st_keep(qb);
-              }
+              tc_st16(aslot, qa);  // the first quarter's store overlaps the second's lookups
+              Dec::lookup_q(hd, 1, qb, p.mul);
+              tc_st16(aslot + 16, qb);
+              tc_wait_st_keep(qa);
+              tc_wait_st_keep(qb);
             }
             if (h == Dec::kHalves - 1) {  // this stage's shared memory is no longer read
               __syncwarp();
@@ -974,9 +965,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
 // CTA per resident slot.
 template <class Dec, int MT>
 inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
-  const int budget = (tc_ctas_per_sm<MT>() == 3 ? 72 * 1024 : tc_ctas_per_sm<MT>() == 2 ? kTcRingBudget
-                                                                                        : kTcRingBudgetWide) -
-                     tc_table_bytes<Dec>();
+  const int budget = (tc_ctas_per_sm<MT>() == 2 ? kTcRingBudget : kTcRingBudgetWide) - tc_table_bytes<Dec>();
   const int stage = tc_stage_bytes<Dec, MT>(p);
   const int xstage = tc_xstage_bytes<Dec, MT>();
   // LUT formats: as many activation stages as weight stages.  The producer
