@@ -153,15 +153,17 @@ def test_qwen15_layer_format_b_4bit_g64(T):
     check_layer(out, ref, torch.float16, f"qwen1.5 layer T={T}")
 
 
+@pytest.mark.parametrize("T", [12, 1])  # T = 1: the single-token GEMV on the tcgen05 layout
 @pytest.mark.parametrize("tc", [True, False], ids=["tc", "mma"])
-def test_shared_expert_modes_and_graph_capture(tc):
+def test_shared_expert_modes_and_graph_capture(tc, T):
+    """Shared expert (run on the library's side stream) with and without its
+    gate, then the whole layer captured in a CUDA graph and replayed."""
     fmt = LUTFormat("b", 4, 64)
     experts, W13, W2 = build_b_layer(fmt, E=4, H=256, I=128, seed=5, tc=tc)
     rng = np.random.Generator(np.random.PCG64(12))
     s13 = O.student_t_weights(rng, (256, 256)).astype(np.float16)
     s2 = O.student_t_weights(rng, (256, 128)).astype(np.float16)
     gate = O.student_t_weights(rng, (256,)).astype(np.float16)
-    T = 12
     x = cuda(O.rms_activations(rng, T, 256).astype(np.float16))
     ids, tw = routing_inputs(rng, T, 4, 2)
     for mode in (0, 1):
