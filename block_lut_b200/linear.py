@@ -51,6 +51,8 @@ class LUTLinear:
             out = torch.empty(m, self.rows, dtype=dt, device=x.device)
         elif tuple(out.shape) != (m, self.rows) or out.dtype != dt or not out.is_contiguous():
             raise ValueError("out has the wrong shape, dtype or layout")
+        if m == 0:  # an empty batch: nothing to launch
+            return out
         lib = _lib.lib()
         need = lib.blut_matmul_workspace_size(C.byref(self.desc), m)
         if need == 0:

@@ -155,6 +155,10 @@ class LUTMoELayer:
         """
         if not x.is_cuda:
             raise ValueError("LUTMoELayer.forward expects CUDA tensors (no CPU path)")
+        if x.numel() == 0:  # an empty batch (as torch's ops return for the reference): nothing to launch
+            dt = torch.float32 if out_f32 else x.dtype
+            res = out if out is not None else torch.empty(x.shape, dtype=dt, device=x.device)
+            return res
         if out_f32:
             return self._forward_f32(x, topk_ids, topk_weights, out, stream)
         in_dtype = x.dtype

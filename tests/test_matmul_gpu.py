@@ -80,5 +80,5 @@ def test_matmul_rejects_bad_arguments():
         lin(torch.zeros(3, K + 128, dtype=torch.float16, device="cuda"))
     with pytest.raises(ValueError):
         lin(torch.zeros(3, K, dtype=torch.bfloat16, device="cuda"))
-    with pytest.raises(RuntimeError):
-        lin(torch.zeros(0, K, dtype=torch.float16, device="cuda"))
+    # an empty batch gives an empty result without a launch, as torch's matmul does
+    assert lin(torch.zeros(0, K, dtype=torch.float16, device="cuda")).shape == (0, N)

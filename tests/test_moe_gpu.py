@@ -236,6 +236,19 @@ def test_deterministic_and_invalid_ids_reported():
     layer.check_status()  # the status word was cleared by the read
 
 
+def test_empty_batch_returns_empty():
+    """A rank or a scheduler step with no tokens: empty outputs, no launch, no error."""
+    fmt = LUTFormat("b", 4, 64)
+    experts, _, _ = build_b_layer(fmt, E=4, H=256, I=128, seed=3)
+    layer = LUTMoELayer(experts, 2)
+    x = torch.zeros(0, 256, dtype=torch.float16, device="cuda")
+    ids = torch.zeros(0, 2, dtype=torch.int32, device="cuda")
+    tw = torch.zeros(0, 2, dtype=torch.float32, device="cuda")
+    assert layer.forward(x, ids, tw).shape == (0, 256)
+    assert layer.forward(x, ids, tw, out_f32=True).dtype == torch.float32
+    layer.check_status()
+
+
 def test_qwen15_layer_decode_batch32_bench_shape():
     """The bench's layer at its decode batch (config 2: batch 32), router + shared expert."""
     H, I, E, k, Is, T = 2048, 1408, 60, 4, 5632, 32
