@@ -371,6 +371,13 @@ __device__ __forceinline__ void add4(float4& v, const float4& w) {
 __device__ __forceinline__ float4 sum_slices(const float* p, int ks, int64_t stride) {
   float4 v = *reinterpret_cast<const float4*>(p);
   int s = 1;
+  for (; s + 7 < ks; s += 8) {  // eight slices' loads in flight, added in slice order
+    float4 w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = *reinterpret_cast<const float4*>(p + (s + i) * stride);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) add4(v, w[i]);
+  }
   for (; s + 3 < ks; s += 4) {
     float4 w[4];
 #pragma unroll
@@ -473,10 +480,16 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
     if (s.gemv[i / 2]) {
       // small-batch GEMV, one CTA per (group, tile, K slice): a slice is
       // the blocks a thread keeps in flight, halved while that leaves fewer
-      // than four CTAs per SM
+      // than four CTAs per SM.  The shared expert runs beside the routed
+      // passes, so its slices only grow until its CTAs would exceed two per
+      // SM (fewer slices for the combine to read).
       const double tiles = (i < 2 ? est_r : (double)gmax_s) * L.ntiles;
       int64_t bps = tc_gemv_blocks(*d[i]);
-      while (bps > 1 && tiles * ((L.nchunks + bps - 1) / bps) < 4.0 * sms) bps = (bps + 1) / 2;
+      if (i < 2) {
+        while (bps > 1 && tiles * ((L.nchunks + bps - 1) / bps) < 4.0 * sms) bps = (bps + 1) / 2;
+      } else {
+        while (tiles * ((L.nchunks + bps - 1) / bps) > 2.0 * sms && bps * 2 * L.kb <= kGemvMaxCols) bps *= 2;
+      }
       s.ks[i] = (int)((L.nchunks + bps - 1) / bps);
       s.bps[i] = (int)bps;
       continue;
