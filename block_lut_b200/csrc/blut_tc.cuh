@@ -1008,17 +1008,16 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
 }
 
 // ------------------------------------------------------ small-batch GEMV --
-// With one to a few tokens per expert (decode batches of up to
-// kGemvMaxTokens tokens) the tensor core has nothing to amortise: every
-// weight is used once per token, and the tcgen05 pipeline's fill and drain
-// dominate.  tc_gemv_kernel reads the same TC-layout buffer straight from
-// global memory, one thread per weight row, decodes it with the format's
-// policy and accumulates the group's tokens in fp32 on the FMA pipe.  A CTA
-// is one (token group, 128-row tile, K slice); the next block's codes are
-// loaded while the current one is decoded.  It writes exactly what
+// A single-token batch (kGemvMaxTokens) leaves the tensor core nothing to
+// amortise: every weight is used once, and the tcgen05 pipeline's fill and
+// drain dominate.  tc_gemv_kernel reads the same TC-layout buffer straight
+// from global memory, one thread per weight row, decodes it with the
+// format's policy and accumulates in fp32 on the FMA pipe.  A CTA is one
+// (token group, 128-row tile, K slice); each thread keeps a ring of
+// tc_gemv_pf() pieces of its row in flight.  It writes exactly what
 // tc_mm_kernel writes (gate/up partial sums for splitk_silu_kernel, or fp32
 // output rows per K slice), so the kernels around it are unchanged.
-constexpr int kGemvMaxCols = 2048;  // columns per CTA (K slice): at most 64 KB of staged fp32 activations
+constexpr int kGemvMaxCols = 2048;  // columns per CTA (K slice): bounds the staged fp32 activations
 
 template <bool BF16>
 __device__ __forceinline__ float2 tc_unpack2(uint32_t v) {
