@@ -480,16 +480,10 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
     if (s.gemv[i / 2]) {
       // small-batch GEMV, one CTA per (group, tile, K slice): a slice is
       // the blocks a thread keeps in flight, halved while that leaves fewer
-      // than four CTAs per SM.  The shared expert runs beside the routed
-      // passes, so its slices only grow until its CTAs would exceed two per
-      // SM (fewer slices for the combine to read).
+      // than four CTAs per SM
       const double tiles = (i < 2 ? est_r : (double)gmax_s) * L.ntiles;
       int64_t bps = tc_gemv_blocks(*d[i]);
-      if (i < 2) {
-        while (bps > 1 && tiles * ((L.nchunks + bps - 1) / bps) < 4.0 * sms) bps = (bps + 1) / 2;
-      } else {
-        while (tiles * ((L.nchunks + bps - 1) / bps) > 2.0 * sms && bps * 2 * L.kb <= kGemvMaxCols) bps *= 2;
-      }
+      while (bps > 1 && tiles * ((L.nchunks + bps - 1) / bps) < 4.0 * sms) bps = (bps + 1) / 2;
       s.ks[i] = (int)((L.nchunks + bps - 1) / bps);
       s.bps[i] = (int)bps;
       continue;
