@@ -59,9 +59,11 @@ enum { BLUT_F16 = 0, BLUT_BF16 = 1, BLUT_F32 = 2 };
  *  BLUT_LAYOUT_PAIRED  row tile t of the first half (gate) and tile t of the
  *                      second half (up) are stored next to each other.
  *  BLUT_LAYOUT_TC      128-row tiles with one row's codes and tables per
- *                      thread, for the tcgen05 (tensor memory) matmuls;
- *                      FMT_B 4-bit and FMT_DENSE.  Without it: 16-row tiles
- *                      in mma.sync fragment order, every format. */
+ *                      thread, for the tcgen05 (tensor memory) matmuls and
+ *                      the single-token GEMV; every format (rows % 128, 256
+ *                      paired; cols % 64, % 128 for g128 and FMT_R8).
+ *                      Without it: 16-row tiles in mma.sync fragment order,
+ *                      every format (cols % 128). */
 enum { BLUT_LAYOUT_PAIRED = 1, BLUT_LAYOUT_TC = 2 };
 
 /* Description of one weight matrix W [rows, cols] (y = W x, cols = K). */
