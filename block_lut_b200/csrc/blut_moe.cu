@@ -801,7 +801,12 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
       t.part = part;
       t.y_sstride = y_sstride;
       const bool gemv = ws.split.gemv[counter / 2];
-      t.gemv_groups = ws.split.groups[counter];
+      // the GEMV grid covers every group the plan can form: an expert with c
+      // tokens forms ceil(c / gtok) groups, so the A active experts of S
+      // slots form at most A + (S - A) / gtok <= min(E, S) + S / gtok
+      const int64_t slots = (int64_t)a.num_tokens * a.top_k;
+      t.gemv_groups = counter < 2 ? std::min<int64_t>(a.num_experts, slots) + slots / ws.split.gtok[0]
+                                  : ws.split.groups[counter];
       if (launch_tc_mm(d, t, gemv ? 1 : ws.split.gtok[counter / 2], sms, cur) != cudaSuccess)
         return BLUT_ERR_LAUNCH;
       if (pair && (t.ks > 1 || gemv)) {
