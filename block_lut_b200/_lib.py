@@ -113,3 +113,15 @@ def stream_ptr(stream=None) -> int:
     import torch
     s = stream if stream is not None else torch.cuda.current_stream()
     return int(s.cuda_stream)
+
+
+def on_device(t):
+    """Context making the device of CUDA tensor ``t`` current.  The library
+    launches on the current device, so every call runs under the device of
+    its tensors (a kernel launched on another device than its buffers' would
+    access peer memory)."""
+    import contextlib
+    import torch
+    if isinstance(t, torch.Tensor) and t.is_cuda:
+        return torch.cuda.device(t.device)
+    return contextlib.nullcontext()

@@ -59,6 +59,16 @@ struct TiledLayout {
 
 __host__ __device__ inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
+// Host: the current device, for caches of per-device launch set-up (function
+// attributes and occupancy are per device).  Devices at or beyond
+// kMaxDevices are not cached (-1).
+constexpr int kMaxDevices = 64;
+__host__ inline int cache_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices) return -1;
+  return d;
+}
+
 // ------------------------------------------------------------------------
 // TC layout (BLUT_LAYOUT_TC): 128-row tiles for the tcgen05 matmuls, where
 // one thread decodes one weight row into tensor memory.  A (tile, block)

@@ -331,23 +331,29 @@ inline cudaError_t launch_mm(MMParams p, int num_sms, cudaStream_t stream) {
   const int smem = mm_smem_bytes<Pol, kPair>(p);
   const int threads = 32 * (p.W + 1);
   auto kern = lut_mm_kernel<Pol, kPair>;
-  // attribute + occupancy per (instantiation, smem size, block size), computed once
+  // attribute + occupancy per (instantiation, device, smem size, block size),
+  // computed once (zero: not yet computed)
   static std::mutex mu;
-  static int cached_smem = -1, cached_threads = -1, cached_per_sm = 1;
+  static int cached_smem[kMaxDevices], cached_threads[kMaxDevices], cached_per_sm[kMaxDevices];
+  const int dev = cache_device();
   int per_sm;
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (cached_smem != smem || cached_threads != threads) {
+    if (dev < 0 || cached_smem[dev] != smem || cached_threads[dev] != threads) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
       int nb = 0;
       e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, threads, smem);
       if (e != cudaSuccess) return e;
-      cached_per_sm = nb < 1 ? 1 : nb;
-      cached_smem = smem;
-      cached_threads = threads;
+      per_sm = nb < 1 ? 1 : nb;
+      if (dev >= 0) {
+        cached_per_sm[dev] = per_sm;
+        cached_smem[dev] = smem;
+        cached_threads[dev] = threads;
+      }
+    } else {
+      per_sm = cached_per_sm[dev];
     }
-    per_sm = cached_per_sm;
   }
   kern<<<num_sms * per_sm, threads, smem, stream>>>(p);
   return cudaGetLastError();

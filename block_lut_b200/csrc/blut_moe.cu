@@ -2,6 +2,7 @@
 // matmul launches and the weighted combine.  All launches go on the caller's
 // stream; nothing synchronises the host and nothing allocates.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
@@ -422,15 +423,17 @@ __global__ void __launch_bounds__(64) combine_kernel(const float* __restrict__ y
 }
 
 // ------------------------------------------------------------ host side ---
+// SM count of the current device (cached per device).
 int num_sms() {
-  static int sms = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  });
+  static std::atomic<int> cache[kMaxDevices];
+  const int dev = cache_device();
+  int sms = dev >= 0 ? cache[dev].load(std::memory_order_relaxed) : 0;
+  if (sms > 0) return sms;
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess ||
+      sms <= 0)
+    sms = 148;
+  if (dev >= 0) cache[dev].store(sms, std::memory_order_relaxed);
   return sms;
 }
 

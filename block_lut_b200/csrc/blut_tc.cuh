@@ -978,12 +978,15 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
   p.xstages = xstage ? p.stages : 0;
   const int smem = tc_smem_bytes<Dec, MT>(p);
   auto kern = tc_mm_kernel<Dec, MT>;
+  // per (instantiation, device): shared-memory attribute and CTAs per SM
+  // (zero: not yet computed)
   static std::mutex mu;
-  static int cached_smem = -1, cached_per_sm = 1;
+  static int cached_smem[kMaxDevices], cached_per_sm[kMaxDevices];
+  const int dev = cache_device();
   int per_sm;
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (cached_smem != smem) {
+    if (dev < 0 || cached_smem[dev] != smem) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
       // Two CTAs per SM share its 512 tensor-memory columns when their shared
@@ -996,12 +999,16 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
       if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, tc_threads<MT>(), smem);
       if (e != cudaSuccess) return e;
       const int want = tc_ctas_per_sm<MT>();
-      cached_per_sm = want > 1 && (nb >= want || want * (smem + 1024) <= smem_sm) ? want : 1;
+      per_sm = want > 1 && (nb >= want || want * (smem + 1024) <= smem_sm) ? want : 1;
       e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
       if (e != cudaSuccess) return e;
-      cached_smem = smem;
+      if (dev >= 0) {
+        cached_per_sm[dev] = per_sm;
+        cached_smem[dev] = smem;
+      }
+    } else {
+      per_sm = cached_per_sm[dev];
     }
-    per_sm = cached_per_sm;
   }
   kern<<<num_sms * per_sm, tc_threads<MT>(), smem, stream>>>(p);
   return cudaGetLastError();
@@ -1199,14 +1206,15 @@ inline cudaError_t launch_tc_gemv_nt(const TcParams& p, int64_t group_bound, cud
   if (p.bps * Dec::KB > kGemvMaxCols || ctas <= 0 || ctas > (1LL << 31) - 1) return cudaErrorInvalidValue;
   auto kern = tc_gemv_kernel<Dec, NT>;
   static std::mutex mu;
-  static int cached = -1;
+  static int cached[kMaxDevices];  // shared-memory attribute set per device (zero: not yet)
+  const int dev = cache_device();
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (cached < smem) {
+    if (dev < 0 || cached[dev] < smem) {
       const int attr = std::max(smem, 48 * 1024);
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, attr);
       if (e != cudaSuccess) return e;
-      cached = attr;
+      if (dev >= 0) cached[dev] = attr;
     }
   }
   kern<<<(unsigned)ctas, kTcRows, smem, stream>>>(p);

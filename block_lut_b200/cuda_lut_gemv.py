@@ -22,8 +22,9 @@ def lut_gemv(input_vec: torch.Tensor, indices: torch.Tensor, codebook: torch.Ten
     cb = codebook.to(device=idx.device, dtype=torch.bfloat16).contiguous()
     am = absmax.reshape(-1).to(device=idx.device, dtype=torch.bfloat16).contiguous()
     y = torch.empty(m, dtype=torch.bfloat16, device=idx.device)
-    _lib.check(_lib.lib().blut_lut_gemv(x.data_ptr(), idx.data_ptr(), cb.data_ptr(), am.data_ptr(), y.data_ptr(),
-                                        m, k, am.numel(), _lib.stream_ptr()), "lut_gemv")
+    with _lib.on_device(idx):
+        _lib.check(_lib.lib().blut_lut_gemv(x.data_ptr(), idx.data_ptr(), cb.data_ptr(), am.data_ptr(), y.data_ptr(),
+                                            m, k, am.numel(), _lib.stream_ptr()), "lut_gemv")
     return y
 
 

@@ -143,8 +143,9 @@ def encode(w: torch.Tensor, fmt: LUTFormat, stream=None) -> QuantizedMatrix:
         tables2 = torch.empty(rows, nb, 16, dtype=torch.float16, device=dev)
     d = fmt.desc(rows, cols)
     p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
-    _lib.check(_lib.lib().blut_encode(C.byref(d), w.data_ptr(), codes.data_ptr(), tables.data_ptr(), p(codes2),
-                                      p(tables2), _lib.stream_ptr(stream)), "encode")
+    with _lib.on_device(w):
+        _lib.check(_lib.lib().blut_encode(C.byref(d), w.data_ptr(), codes.data_ptr(), tables.data_ptr(), p(codes2),
+                                          p(tables2), _lib.stream_ptr(stream)), "encode")
     return QuantizedMatrix(fmt, rows, cols, codes, tables, codes2, tables2)
 
 
@@ -156,8 +157,9 @@ def encode_r(w: torch.Tensor, codebook: torch.Tensor, block_size: int = 128, str
     n = w.numel()
     idx = torch.empty(n, dtype=torch.uint8, device=w.device)
     absmax = torch.empty((n + block_size - 1) // block_size, dtype=torch.bfloat16, device=w.device)
-    _lib.check(_lib.lib().blut_encode_r(w.data_ptr(), n, cb.data_ptr(), block_size, idx.data_ptr(),
-                                        absmax.data_ptr(), _lib.stream_ptr(stream)), "encode_r")
+    with _lib.on_device(w):
+        _lib.check(_lib.lib().blut_encode_r(w.data_ptr(), n, cb.data_ptr(), block_size, idx.data_ptr(),
+                                            absmax.data_ptr(), _lib.stream_ptr(stream)), "encode_r")
     return idx, absmax
 
 
@@ -167,7 +169,9 @@ def dequant(qm: QuantizedMatrix, stream=None) -> torch.Tensor:
     out = torch.empty(qm.rows, qm.cols, dtype=out_dtype, device=qm.codes.device)
     d = qm.fmt.desc(qm.rows, qm.cols)
     c = qm.canon()
-    _lib.check(_lib.lib().blut_dequant(C.byref(d), C.byref(c), out.data_ptr(), _lib.stream_ptr(stream)), "dequant")
+    with _lib.on_device(out):
+        _lib.check(_lib.lib().blut_dequant(C.byref(d), C.byref(c), out.data_ptr(), _lib.stream_ptr(stream)),
+                   "dequant")
     return out
 
 
@@ -192,10 +196,12 @@ def pack_tiled(mats, stream=None, paired: bool = False, tc: bool = False) -> tup
     dev = mats[0].codes.device
     buf = torch.empty(len(mats) * stride, dtype=torch.uint8, device=dev)
     d = fmt.desc(rows, cols, paired, tc)
-    s = _lib.stream_ptr(stream)
-    for i, m in enumerate(mats):
-        c = m.canon()
-        _lib.check(_lib.lib().blut_pack_tiled(C.byref(d), C.byref(c), buf.data_ptr() + i * stride, s), "pack_tiled")
+    with _lib.on_device(buf):
+        s = _lib.stream_ptr(stream)
+        for i, m in enumerate(mats):
+            c = m.canon()
+            _lib.check(_lib.lib().blut_pack_tiled(C.byref(d), C.byref(c), buf.data_ptr() + i * stride, s),
+                       "pack_tiled")
     return buf, stride
 
 
@@ -204,9 +210,10 @@ def dequant_tiled(fmt: LUTFormat, rows: int, cols: int, tiled: torch.Tensor, lut
     """Dense matrix rebuilt from one tiled matrix through the kernels' lookups."""
     out = torch.empty(rows, cols, dtype=fmt.compute_dtype, device=tiled.device)
     d = fmt.desc(rows, cols, paired, tc)
-    _lib.check(_lib.lib().blut_dequant_tiled(C.byref(d), tiled.data_ptr(),
-                                             None if lut_table is None else lut_table.data_ptr(), out.data_ptr(),
-                                             _lib.stream_ptr(stream)), "dequant_tiled")
+    with _lib.on_device(out):
+        _lib.check(_lib.lib().blut_dequant_tiled(C.byref(d), tiled.data_ptr(),
+                                                 None if lut_table is None else lut_table.data_ptr(), out.data_ptr(),
+                                                 _lib.stream_ptr(stream)), "dequant_tiled")
     return out
 
 

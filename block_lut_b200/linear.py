@@ -58,10 +58,11 @@ class LUTLinear:
         if need == 0:
             raise RuntimeError(f"blut_matmul rejects m={m} for {self.fmt} [{self.rows}, {self.cols}]")
         ws = workspace(x.device, need)
-        _lib.check(lib.blut_matmul(C.byref(self.desc), self.buf.data_ptr(),
-                                   None if self.lut_table is None else self.lut_table.data_ptr(), x.data_ptr(), m,
-                                   out.data_ptr(), 1 if out_f32 else 0, ws.data_ptr(), ws.numel(),
-                                   _lib.stream_ptr(stream)), "matmul")
+        with _lib.on_device(x):
+            _lib.check(lib.blut_matmul(C.byref(self.desc), self.buf.data_ptr(),
+                                       None if self.lut_table is None else self.lut_table.data_ptr(), x.data_ptr(),
+                                       m, out.data_ptr(), 1 if out_f32 else 0, ws.data_ptr(), ws.numel(),
+                                       _lib.stream_ptr(stream)), "matmul")
         return out
 
     __call__ = forward
@@ -69,4 +70,5 @@ class LUTLinear:
     def check_status(self, stream=None) -> None:
         """Raise if a device-side wait of the last call timed out."""
         ws = workspace(self.buf.device, 256, 0)
-        _lib.check(_lib.lib().blut_moe_check_status(ws.data_ptr(), _lib.stream_ptr(stream)), "matmul status")
+        with _lib.on_device(ws):
+            _lib.check(_lib.lib().blut_moe_check_status(ws.data_ptr(), _lib.stream_ptr(stream)), "matmul status")

@@ -175,8 +175,9 @@ class LUTMoELayer:
         if need == 0:
             raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
         ws = workspace(x2.device, need, self.ws_slot)
-        _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
-                   "moe_forward")
+        with _lib.on_device(x2):
+            _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
+                       "moe_forward")
         if out is not None and res.data_ptr() != out.data_ptr():
             out.copy_(res.reshape(out.shape))
             return out
@@ -223,8 +224,9 @@ class LUTMoELayer:
             if need == 0:
                 raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
             ws = workspace(x2.device, need, self.ws_slot)
-            _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
-                       "moe_forward")
+            with _lib.on_device(x2):
+                _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
+                           "moe_forward")
         finally:
             a.out_f32 = 0
         return res
@@ -233,7 +235,9 @@ class LUTMoELayer:
         """Synchronise and raise if a kernel reported a device-side error."""
         ws = _WS.get((self.experts.w13.device.type, self.experts.w13.device.index, self.ws_slot))
         if ws is not None:
-            _lib.check(_lib.lib().blut_moe_check_status(ws.data_ptr(), _lib.stream_ptr(stream)), "device status")
+            with _lib.on_device(ws):
+                _lib.check(_lib.lib().blut_moe_check_status(ws.data_ptr(), _lib.stream_ptr(stream)),
+                           "device status")
 
 
 def router(x: torch.Tensor, w_router: torch.Tensor, top_k: int, renorm: bool = False,
@@ -248,7 +252,8 @@ def router(x: torch.Tensor, w_router: torch.Tensor, top_k: int, renorm: bool = F
     sg = torch.empty(T, dtype=torch.float32, device=x.device) if shared_gate else None
     logits = torch.empty(T, w.shape[0], dtype=torch.float32, device=x.device)
     dt = _lib.BF16 if x.dtype == torch.bfloat16 else _lib.F16
-    _lib.check(_lib.lib().blut_router(x.data_ptr(), w.data_ptr(), T, H, E, top_k, int(renorm), int(shared_gate), dt,
-                                      ids.data_ptr(), tw.data_ptr(), None if sg is None else sg.data_ptr(),
-                                      logits.data_ptr(), _lib.stream_ptr(stream)), "router")
+    with _lib.on_device(x):
+        _lib.check(_lib.lib().blut_router(x.data_ptr(), w.data_ptr(), T, H, E, top_k, int(renorm), int(shared_gate),
+                                          dt, ids.data_ptr(), tw.data_ptr(), None if sg is None else sg.data_ptr(),
+                                          logits.data_ptr(), _lib.stream_ptr(stream)), "router")
     return ids, tw, sg

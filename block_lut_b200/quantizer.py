@@ -154,9 +154,10 @@ def decompress_blocklut(indices: torch.Tensor, absmax: torch.Tensor, codebook: t
     am = absmax.reshape(-1).to(device=dev, dtype=torch.bfloat16).contiguous()
     cb = codebook.to(device=dev, dtype=torch.bfloat16).contiguous()
     out = torch.empty(idx.numel(), dtype=torch.bfloat16, device=dev)
-    _lib.check(_lib.lib().blut_batch_blocklut_decompress(out.data_ptr(), idx.data_ptr(), am.data_ptr(), cb.data_ptr(),
-                                                         1, idx.numel(), am.numel(), block_size,
-                                                         _lib.stream_ptr()), "decompress_blocklut")
+    with _lib.on_device(out):
+        _lib.check(_lib.lib().blut_batch_blocklut_decompress(out.data_ptr(), idx.data_ptr(), am.data_ptr(),
+                                                             cb.data_ptr(), 1, idx.numel(), am.numel(), block_size,
+                                                             _lib.stream_ptr()), "decompress_blocklut")
     return out
 
 

@@ -78,3 +78,39 @@ def test_ep_nccl_two_gpus_matches_single_gpu():
         p.join(timeout=60)
     for rank, status, msg in sorted(results):
         assert status == "ok", f"rank {rank}:\n{msg}"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_one_process_drives_two_devices():
+    """Launch set-up (shared-memory attributes, occupancy, SM count, the side
+    stream) is per device: the same layer built on cuda:0 and cuda:1 in one
+    process gives the same result on both."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from oracle import blut_oracle as O
+    from block_lut_b200.formats import LUTFormat, QuantizedMatrix
+    from block_lut_b200.moe import LUTExperts, LUTMoELayer, SharedExpert
+    fmt = LUTFormat("b", 4, 64)
+    rng = np.random.Generator(np.random.PCG64(9))
+    mats = []
+    for _ in range(E):
+        for rows, cols in ((2 * I, H), (H, I)):
+            packed, tables = O.encode_b(O.student_t_weights(rng, (rows, cols)), 4, 64)
+            mats.append((rows, cols, packed, tables))
+    s13 = O.student_t_weights(rng, (2 * IS, H)).astype(np.float16)
+    s2 = O.student_t_weights(rng, (H, IS)).astype(np.float16)
+    x = O.rms_activations(rng, T, H).astype(np.float16)
+    ids, tw = O.routing(rng.standard_normal((T, E)).astype(np.float32), K)
+    outs = []
+    for dev in ("cuda:0", "cuda:1"):
+        q = [QuantizedMatrix(fmt, r, c, torch.from_numpy(p).to(dev), torch.from_numpy(t).to(dev)) for r, c, p, t in mats]
+        ex = LUTExperts.from_quantized(q[0::2], q[1::2])
+        sh = SharedExpert.from_dense(torch.from_numpy(s13).to(dev), torch.from_numpy(s2).to(dev))
+        layer = LUTMoELayer(ex, K, shared=sh, shared_gate_mode=0)
+        with torch.cuda.device(dev):
+            out = layer.forward(torch.from_numpy(x).to(dev), torch.from_numpy(ids).to(dev),
+                                torch.from_numpy(tw).to(dev))
+            torch.cuda.synchronize()
+            layer.check_status()
+        outs.append(out.cpu())
+    assert torch.equal(outs[0], outs[1])
