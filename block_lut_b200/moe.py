@@ -8,6 +8,7 @@ caller-owned workspace, so it can be captured in a CUDA graph.
 from __future__ import annotations
 
 import ctypes as C
+import threading
 from dataclasses import dataclass
 from typing import Optional, Sequence
 
@@ -84,17 +85,21 @@ class SharedExpert:
 
 
 _WS: dict = {}
+_WS_LOCK = threading.Lock()
 
 
 def workspace(device: torch.device, nbytes: int, slot: int = 0) -> torch.Tensor:
     """Grow-only workspace per (device, slot).  Layers whose calls run in one
     stream's order share a slot; a layer that runs concurrently with others
-    on another stream takes a slot of its own (``LUTMoELayer.ws_slot``)."""
+    on another stream takes a slot of its own (``LUTMoELayer.ws_slot``): the
+    lock only keeps the table consistent across host threads, it does not
+    order their kernels."""
     key = (device.type, device.index, slot)
-    buf = _WS.get(key)
-    if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        _WS[key] = buf
+    with _WS_LOCK:
+        buf = _WS.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _WS[key] = buf
     return buf
 
 
