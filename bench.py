@@ -41,7 +41,12 @@ QWEN = dict(H=H, E=E, I=I, IS=IS, TOPK=TOPK, LAYERS=LAYERS, RENORM=False, BATCH=
 # NestedLUT 2+2 with g 64 (full tier, or coarse only with --tier 1).
 QWEN3 = dict(H=2048, E=128, I=768, IS=0, TOPK=8, LAYERS=48, RENORM=True, BATCH=64,
              NAME="Qwen3-30B-A3B MoE stack", KIND="nested")
-TRAFFIC_RATIO = 1.028  # measured DRAM bytes / algorithmic bytes of the routed tcgen05 launches
+# DRAM read + write over algorithmic bytes of the routed tcgen05 launches, from
+# one ncu capture per format (profiles/: tc_mm_kernel_qwen15_decode_b32.md,
+# tc_mm_kernel_qwen15_formatR_decode_b32.md,
+# tc_mm_kernel_qwen3_nested_coarse_b64.md); formats without a capture report
+# no traffic
+TRAFFIC_RATIOS = {("b", 4, 64, 0): 1.024, ("r8", 8, 128, 0): 1.035, ("nested", 4, 64, 1): 1.06}
 METRIC = "LUT-MoE decode tokens/s; expert LUT-GEMV HBM GB/s vs ~8 TB/s peak"
 # DeepSeek-V2-Lite MoE layers (26 of 27; layer 0 is dense),
 # 64 routed experts of I 1408, top-6 softmax, two shared experts (one MLP of
@@ -354,6 +359,7 @@ def run_ours(a):
     t_gu /= reps * len(moes)
     t_dn /= reps * len(moes)
     bpw = fmt.bytes_per_weight()
+    key = (fmt.kind, fmt.bits, fmt.group, fmt.tier if fmt.kind != "b" else 0)
     na = sum(n_active) / len(n_active)
     b_gu = na * 2 * Ii * Hh * bpw
     b_dn = na * Hh * Ii * bpw
@@ -411,11 +417,10 @@ def run_ours(a):
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s",
-                     # DRAM read + write per layer: the algorithmic bytes times the ratio the ncu
-                     # capture in profiles/tc_mm_kernel_qwen15_decode_b32.md measured for the
-                     # routed gate/up + down launches (1.028)
-                     "traffic": (b_gu + b_dn) * TRAFFIC_RATIO if moes[0].experts.tc and fmt.kind == "b" and
-                     fmt.bits == 4 and fmt.group == 64 else None,
+                     # DRAM read + write per layer: the algorithmic bytes times the ratio an
+                     # ncu capture of this format's routed launches measured (TRAFFIC_RATIOS)
+                     "traffic": (b_gu + b_dn) * TRAFFIC_RATIOS[key] if moes[0].experts.tc and key in
+                     TRAFFIC_RATIOS else None,
                      "bytes_per_layer": b_gu + b_dn, "ms_gateup": t_gu, "ms_down": t_dn,
                      "active_experts": na, "active_experts_per_layer": n_active[:4]},
         "cpu_baseline": cpu, "e2e": e2e,
