@@ -190,3 +190,20 @@ def test_codes1_and_codes2_arrangements_are_bijective():
     seen = sorted(16 * (s >> 1) + 8 * (n & 1) + (n >> 1) + 4 * (s & 1) for n in range(8) for s in range(4))
     assert seen == list(range(32))
     assert sorted(4 * i + j for i in range(4) for j in range(4)) == list(range(16))
+
+
+def test_bf16_products_are_exact_in_fp32():
+    """The Format R decode scales each table entry by its absmax with one
+    bf16x2 multiply (one rounding of the exact product).  The reference
+    computes bf16(f32(t) * f32(s)).  Both agree because the product of two
+    bf16 values (8 significant bits each) is exact in fp32 (24 bits), away
+    from the fp32 subnormal range."""
+    rng = np.random.Generator(np.random.PCG64(7))
+    t = rng.standard_normal(200000).astype(np.float32)
+    s = (10.0 ** rng.uniform(-12, 4, 200000)).astype(np.float32)
+    to_bf16 = lambda v: (np.asarray(v, dtype=np.float32).view(np.uint32) & 0xFFFF0000).view(np.float32)  # noqa: E731
+    tb, sb = to_bf16(t), to_bf16(s)
+    p32 = tb * sb
+    p64 = tb.astype(np.float64) * sb.astype(np.float64)
+    normal = np.abs(p64) >= np.finfo(np.float32).tiny
+    assert np.array_equal(p32[normal].astype(np.float64), p64[normal])
