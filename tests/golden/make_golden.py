@@ -22,6 +22,11 @@ It imports the reference's own ``vllm_lut.quantizer`` and
 * ``apply_small.npz``  -- ``LUTFusedMoEMethod.apply`` (``quant_method.py:230-279``)
   on a small layer (E=8, H=256, I=128, top-2) at T=2 and T=8; the uint8
   indices are regenerated from a stored seed, everything else is stored.
+* ``convert_r.npz``    -- the reference converter's encoder ``quantize_weight``
+  (``vllm_lut/convert_checkpoint.py:61-104``) with the shipped Qwen codebook,
+  on a bf16 matrix of 8000 elements (a zero-padded tail block) whose first
+  block is all zeros (the absmax clamp).  ``python make_golden.py <ref> convert``
+  regenerates only this file.
 * ``apply_qwen.npz``   -- ``apply`` on a Qwen1.5-MoE-shaped layer (E=60, H=2048,
   I=1408, top-4, T=8).  The 519 MB of weights are not stored: they are
   regenerated from the stored seed with numpy's PCG64 integer stream (stable
@@ -186,5 +191,26 @@ def main(ref_root):
     print("wrote fixtures to", HERE)
 
 
+def convert_fixture(ref_root):
+    sys.path.insert(0, ref_root)
+    import torch
+    from vllm_lut.convert_checkpoint import quantize_weight
+    cb = torch.from_numpy(np.load(os.path.join(ref_root, "models/qwen/blocklut_256.npy"))).to(torch.bfloat16)
+    rng = np.random.Generator(np.random.PCG64(11))
+    df = 5.0
+    w = (rng.standard_t(df, size=(40, 200)) * (0.02 / np.sqrt(df / (df - 2)))).astype(np.float32)
+    w.reshape(-1)[:128] = 0.0
+    wb = torch.from_numpy(w).to(torch.bfloat16)
+    idx, absmax = quantize_weight(wb, cb)
+    np.savez_compressed(os.path.join(HERE, "convert_r.npz"), w=bits(wb), table=bits(cb), idx=idx.numpy(),
+                        absmax=bits(absmax))
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <block_lut checkout> [convert]")
+    if sys.argv[2:] == ["convert"]:
+        convert_fixture(sys.argv[1])
+    else:
+        main(sys.argv[1])
+        convert_fixture(sys.argv[1])

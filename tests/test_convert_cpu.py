@@ -1,0 +1,84 @@
+"""Host logic of the checkpoint converter (block_lut_b200/convert_checkpoint.py):
+tensor selection, codebook choice, shard discovery, index remapping, side
+files and the quantization_config it writes.  Encoding needs the GPU and is
+tested in tests/test_convert_gpu.py; here the converter must refuse to run."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from block_lut_b200 import convert_checkpoint as CC
+
+
+def test_tensor_selection_follows_reference():
+    # convert_model.py:91-95: routed experts' bf16 .weight tensors only
+    assert CC.should_encode("model.layers.3.mlp.experts.7.gate_proj.weight", torch.bfloat16)
+    assert not CC.should_encode("model.layers.3.mlp.experts.7.gate_proj.weight", torch.float16)
+    assert not CC.should_encode("model.layers.3.mlp.shared_expert.gate_proj.weight", torch.bfloat16)
+    assert not CC.should_encode("model.layers.3.mlp.shared_experts.gate_proj.weight", torch.bfloat16)
+    assert not CC.should_encode("model.layers.3.mlp.gate.weight", torch.bfloat16)
+    assert not CC.should_encode("model.layers.3.mlp.experts.7.gate_proj.bias", torch.bfloat16)
+
+
+def test_codebook_choice(tmp_path):
+    with pytest.raises(FileNotFoundError):
+        CC.codebook_file(str(tmp_path), "BLOCKLUT")
+    np.save(tmp_path / "blocklut_256.npy", np.linspace(-1, 1, 256, dtype=np.float32))
+    assert CC.codebook_file(str(tmp_path), "BLOCKLUT").endswith("blocklut_256.npy")
+    # NESTEDLUT falls back to the BlockLUT table (convert_model.py:48-50)
+    assert CC.codebook_file(str(tmp_path), "NESTEDLUT").endswith("blocklut_256.npy")
+    np.save(tmp_path / "nested_lut_mapped16.npy", np.zeros(256, dtype=np.uint16))
+    assert CC.codebook_file(str(tmp_path), "NESTEDLUT").endswith("nested_lut_mapped16.npy")
+
+
+def test_shards_index_and_side_files(tmp_path):
+    for f in ("model-00002-of-00002.safetensors", "model-00001-of-00002.safetensors", "config.json",
+              "tokenizer.model", "blocklut_256.npy", "README.md", CC.INDEX_NAME, "modeling_x.py"):
+        (tmp_path / f).write_bytes(b"{}")
+    shards = [os.path.basename(f) for f in CC.shard_files(str(tmp_path))]
+    assert shards == ["model-00001-of-00002.safetensors", "model-00002-of-00002.safetensors"]
+    # the index is rewritten, not copied over (the reference copies it last)
+    assert CC.side_files(str(tmp_path)) == ["blocklut_256.npy", "config.json", "modeling_x.py", "tokenizer.model"]
+    idx = CC.remap_index({"metadata": {"total_size": 1},
+                          "weight_map": {"a.weight": "model-00001-of-00002.safetensors"}})
+    assert idx == {"metadata": {"total_size": 1}, "weight_map": {"a.weight": "model-00001-of-00002_lut.safetensors"}}
+
+
+def test_single_file_checkpoint(tmp_path):
+    (tmp_path / "model.safetensors").write_bytes(b"")
+    assert CC.shard_files(str(tmp_path)) == [str(tmp_path / "model.safetensors")]
+    assert CC.lut_name("model.safetensors") == "model_lut.safetensors"
+
+
+@pytest.mark.parametrize("argv,expect", [
+    (["--format", "b", "--bits", "3", "--group", "32"],
+     {"codebook_scope": "row_block", "index_bits": 3, "lut_block": 32}),
+    (["--format", "nested", "--group", "64", "--tier", "coarse"],
+     {"codebook_scope": "row_block", "lut_block": 64,
+      "nested": {"coarse_bits": 2, "residual_bits": 2, "tier": "coarse"}}),
+    (["--write_quant_config"], {"code_type": "BLOCKLUT", "block_size": 128}),
+])
+def test_quant_config_selects_the_converted_format(tmp_path, argv, expect):
+    from block_lut_b200.quant_method import LUTConfig
+    args = CC.parse_args(["--model", str(tmp_path)] + argv)
+    cfg = CC.quant_config(args, str(tmp_path / "out"))
+    for k, v in expect.items():
+        assert cfg[k] == v
+    assert cfg["quant_method"] == "lut" and os.path.isabs(cfg["lut_path"])
+    # the loader reads it back as the converted format
+    fmt = LUTConfig.from_config(json.loads(json.dumps(cfg))).lut_format()
+    want = CC.format_of(args)
+    assert fmt.kind == (want.kind if want else "r8")
+    if want:
+        assert (fmt.bits, fmt.group, fmt.tier) == (want.bits, want.group, want.tier)
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU refusal")
+def test_converter_refuses_without_gpu(tmp_path):
+    np.save(tmp_path / "blocklut_256.npy", np.linspace(-1, 1, 256, dtype=np.float32))
+    with pytest.raises(RuntimeError, match="GPU"):
+        CC.convert_checkpoint(CC.parse_args(["--model", str(tmp_path), "--output", str(tmp_path / "o")]))
+    with pytest.raises(Exception):
+        CC.quantize_weight(torch.zeros(256, dtype=torch.bfloat16), torch.zeros(256, dtype=torch.bfloat16))

@@ -27,6 +27,16 @@ def test_encode_r_bit_exact(golden):
     assert np.array_equal(deq.reshape(-1), e["dequant"].reshape(-1))
 
 
+def test_encode_r_matches_reference_converter(golden):
+    # convert_checkpoint.quantize_weight (convert_checkpoint.py:61-104): flat
+    # blocks over the whole tensor, zero-padded tail, absmax clamp at 1e-10
+    e = golden("convert_r.npz")
+    idx, am = O.encode_r(e["w"], e["table"], 128)
+    assert e["w"].size % 128 != 0 and int(e["absmax"][0]) == int(O.f32_to_bf16(np.float32(1e-10)))
+    assert np.array_equal(idx, e["idx"])
+    assert np.array_equal(am, e["absmax"])
+
+
 @pytest.mark.parametrize("tier,table", [(1, "mapped64"), (2, "mapped16")])
 def test_nested_tiers_bit_exact(golden, tier, table):
     t = golden("tiers.npz")
