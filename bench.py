@@ -74,9 +74,10 @@ def parse():
                    help="matmul path of the experts: tcgen05 where the format has it (auto), or forced")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    p.add_argument("--workload", choices=["decode", "qwen3", "prefill", "sweep"], default="decode",
+    p.add_argument("--workload", choices=["decode", "qwen3", "prefill", "sweep", "tiers"], default="decode",
                    help="decode: the BASELINE metric (config 2); qwen3: config 3's MoE stack at decode; "
-                        "prefill: config 4's MoE layers; sweep: config 5's single-matrix kernel sweep")
+                        "prefill: config 4's MoE layers; sweep: config 5's single-matrix kernel sweep; "
+                        "tiers: Format R progressive bit-plane tier recover")
     p.add_argument("--sweep-bits", default="2,3,4")
     p.add_argument("--sweep-groups", default="32,64,128")
     p.add_argument("--sweep-m", default="1,2,4,8,16,64,256,1024,4096")
@@ -633,6 +634,101 @@ def run_sweep(a):
     print(json.dumps(res), flush=True)
 
 
+TIERS_METRIC = "Format R progressive-tier recover: fraction of HBM bandwidth (geometric mean over tiers 0-2)"
+
+
+def run_tiers(a):
+    """Progressive bit-plane tiers of the HF offload engine
+    (runtime/model_offload.py:751-758): blut_bitplane_recover over the routed
+    experts of one Qwen1.5-MoE layer as one buffer (60 x 3 x 1408 x 2048 =
+    519 M indices). Per tier, algorithmic bytes = the planes the tier reads
+    (n/2, 3n/4, n) + 2 n / 128 of absmax + 2 n of bf16 output; the planes
+    (>= 260 MB) and the output (1 GB) are larger than L2. e2e: the cold tier
+    (2) from pinned host memory, with the H2D copy of its planes and absmax in
+    the timed region; the bf16 output stays on the device for the expert
+    matmul, so nothing is read back."""
+    import torch
+    from block_lut_b200.bitplanes import bitplane_bytes, pack_bitplanes, recover_tier
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    bw, src = peaks()
+    n = E * 3 * I * H
+    g = torch.Generator(device=dev).manual_seed(7)
+    idx = torch.randint(0, 256, (n,), generator=g, dtype=torch.uint8, device=dev)
+    planes = pack_bitplanes(idx)
+    del idx
+    am = (torch.rand(n // 128, generator=g, device=dev) * 0.05 + 0.01).to(torch.bfloat16)
+    table = torch.randn(256, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    steps = max(1, a.steps)
+    clk = Clocks(0)
+    rows, fracs = [], []
+    for tier in (0, 1, 2):
+        for _ in range(max(3, a.warmup)):
+            recover_tier(planes, am, table, n, tier, out=out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            recover_tier(planes, am, table, n, tier, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1e3 / steps
+        byt = bitplane_bytes(n, tier) + 2 * (n // 128) + 2 * n
+        fracs.append(byt / t / 1e9 / bw)
+        rows.append([tier, bitplane_bytes(n, tier), round(t * 1e6, 1), round(byt / t / 1e9, 1), round(fracs[-1], 3),
+                     round(n / t / 1e9, 1)])
+    # e2e, cold tier: pinned host planes + absmax -> device -> bf16
+    nb2 = bitplane_bytes(n, 2)
+    h_planes = planes[:nb2].cpu().pin_memory()
+    h_am = am.cpu().pin_memory()
+    d_planes = torch.empty(nb2, dtype=torch.uint8, device=dev)
+    d_am = torch.empty_like(am)
+    for _ in range(3):
+        d_planes.copy_(h_planes, non_blocking=True)
+        d_am.copy_(h_am, non_blocking=True)
+        recover_tier(d_planes, d_am, table, n, 2, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        d_planes.copy_(h_planes, non_blocking=True)
+        d_am.copy_(h_am, non_blocking=True)
+        recover_tier(d_planes, d_am, table, n, 2, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    t_e2e = e0.elapsed_time(e1) / 1e3 / steps
+    clocks = clk.stop()
+    cpu = None
+    if not a.no_cpu:
+        from oracle import blut_oracle as O
+        ns = 1 << 24
+        idx_s = np.random.Generator(np.random.PCG64(1)).integers(0, 256, ns, dtype=np.uint8)
+        p_np = O.bitplane_pack(idx_s)
+        am_np = O.f32_to_bf16(np.full(ns // 128, 0.03, dtype=np.float32))
+        tab_np = O.f32_to_bf16(np.linspace(-1, 1, 256, dtype=np.float32))
+        t0 = time.perf_counter()
+        O.dequant_r(O.bitplane_index(p_np[: ns // 2], ns, 2), am_np, tab_np, 128, 2)
+        tc = time.perf_counter() - t0
+        cpu = {"value": round((ns // 2 + 2 * (ns // 128) + 2 * ns) / tc / 1e9, 3), "unit": "GB/s", "cores": 1,
+               "kind": "port", "sample": f"tier 2, {ns} indices through the numpy oracle (unpack + dequant)"}
+    res = {"metric": TIERS_METRIC, "value": float(np.exp(np.mean(np.log(fracs)))), "unit": "fraction", "n_gpus": 1,
+           "steps": steps,
+           "warmup": max(3, a.warmup), "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "u8->bf16", "data": "synthetic uniform indices, random absmax and table",
+           "config": {"workload": "bit-plane tier recover, one Qwen1.5-MoE layer's routed experts",
+                      "elements": n, "block_size": 128,
+                      "l2": "planes (>= 260 MB) and output (1 GB) larger than L2, no flush"},
+           "tiers_columns": ["tier", "plane bytes", "us", "GB/s", "frac", "G elements/s"], "tiers": rows,
+           "roofline": {"bound": "hbm", "achieved": rows[0][3], "peak": bw, "unit": "GB/s", "frac": rows[0][4],
+                        "traffic": None, "kernel": "bitplane_recover_kernel<0>", "peak_source": src},
+           "cpu_baseline": cpu,
+           "e2e": {"value": round(n / t_e2e / 1e9, 2), "unit": "G elements/s (tier 2 from pinned host memory)",
+                   "h2d_bytes_per_step": nb2 + 2 * (n // 128), "d2h_bytes_per_step": 0},
+           "gpu_launches": 4 * steps, "clocks": clocks}
+    print(json.dumps(res), flush=True)
+
+
 if __name__ == "__main__":
     args = parse()
     if args.impl == "reference":
@@ -641,5 +737,7 @@ if __name__ == "__main__":
         run_prefill(args)
     elif args.workload == "sweep":
         run_sweep(args)
+    elif args.workload == "tiers":
+        run_tiers(args)
     else:
         run_ours(args)

@@ -61,6 +61,9 @@ SIGNATURES = [
     ("blut_blocklut_decompress", C.c_int, [_VP, _VP, _VP, _VP, _I64, _I32, _VP]),
     ("blut_batch_blocklut_decompress", C.c_int, [_VP, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _VP]),
     ("blut_lut_recover", C.c_int, [_VP, _VP, _VP, _I64, _VP]),
+    ("blut_bitplane_bytes", C.c_int64, [_I64, _I32]),
+    ("blut_bitplane_pack", C.c_int, [_VP, _VP, _I64, _VP]),
+    ("blut_bitplane_recover", C.c_int, [_VP, _VP, _VP, _VP, _I64, _I32, _I32, _VP]),
     ("blut_tiled_bytes", C.c_int64, [C.POINTER(MatDesc)]),
     ("blut_pack_tiled", C.c_int, [C.POINTER(MatDesc), C.POINTER(Canon), _VP, _VP]),
     ("blut_dequant_tiled", C.c_int, [C.POINTER(MatDesc), _VP, _VP, _VP, _VP]),

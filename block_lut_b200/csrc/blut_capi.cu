@@ -44,6 +44,17 @@ int blut_lut_recover(void* out_u16, const void* idx_u8, const void* lut_u16, int
   return lut_recover(out_u16, idx_u8, lut_u16, n, S(stream));
 }
 
+int64_t blut_bitplane_bytes(int64_t n, int32_t tier) { return bitplane_bytes(n, tier); }
+
+int blut_bitplane_pack(void* planes_u8, const void* idx_u8, int64_t n, void* stream) {
+  return bitplane_pack(planes_u8, idx_u8, n, S(stream));
+}
+
+int blut_bitplane_recover(void* out_bf16, const void* planes_u8, const void* absmax_bf16, const void* table_bf16,
+                          int64_t n, int32_t tier, int32_t block_size, void* stream) {
+  return bitplane_recover(out_bf16, planes_u8, absmax_bf16, table_bf16, n, tier, block_size, S(stream));
+}
+
 int64_t blut_tiled_bytes(const blut_mat_desc* desc) {
   TiledLayout L;
   if (!desc || !make_layout(*desc, L)) return BLUT_ERR_UNSUPPORTED;

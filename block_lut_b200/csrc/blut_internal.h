@@ -61,6 +61,11 @@ struct MoEWs {
 };
 
 int num_sms();
+// Progressive bit-plane storage of Format R indices (blut_bitplane.cu).
+int64_t bitplane_bytes(int64_t n, int tier);
+int bitplane_pack(void* planes, const void* idx, int64_t n, cudaStream_t stream);
+int bitplane_recover(void* out, const void* planes, const void* absmax, const void* table, int64_t n, int tier,
+                     int bs, cudaStream_t stream);
 // Consumer warps (units) per work item of the mma.sync matmul for the expected
 // number of token groups.
 int choose_units_per_item(double est_groups, int units, int sms);

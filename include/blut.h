@@ -136,6 +136,39 @@ BLUT_API int blut_batch_blocklut_decompress(void* out_bf16, const void* idx_u8, 
  * Replaces lut_moe_launch_lut_recover (csrc/kernels/tensor_recover.hpp:23-29). */
 BLUT_API int blut_lut_recover(void* out_u16, const void* idx_u8, const void* lut_u16, int64_t n, void* stream);
 
+/* ------------------------------------------ progressive bit-plane tiers -- */
+
+/* Progressive bit-plane storage of n Format R indices (n % 4 == 0), as
+ * runtime/model_offload.py:751-758 writes it: one buffer of n bytes holding
+ *   low4  [n/2]  byte q: element 2q in bits 0-3, element 2q+1 in bits 4-7
+ *   mid2  [n/4]  byte q: bits 4-5 of element 4q+j in bits 2j..2j+1
+ *   high2 [n/4]  byte q: bits 6-7 of element 4q+j in bits 2j..2j+1
+ * A tier reads a prefix of it (csrc/tensor_engine/tensor_engine.cpp:505-509):
+ * tier 2 the low section, tier 1 low + mid, tier 0 everything. */
+
+/* Bytes of the buffer that `tier` reads: n/2, 3n/4 or n; BLUT_ERR_INVALID
+ * when n <= 0, n % 4 != 0 or tier is not 0, 1, 2. */
+BLUT_API int64_t blut_bitplane_bytes(int64_t n, int32_t tier);
+
+/* Write the bit-plane buffer planes [n] of idx [n] on the GPU.
+ * Replaces the host packing of runtime/model_offload.py:751-758. */
+BLUT_API int blut_bitplane_pack(void* planes_u8, const void* idx_u8, int64_t n, void* stream);
+
+/* One pass from a tier's sections to bf16:
+ *   out[i] = bf16(table[index(i)] * absmax[min(i / block_size, nb - 1)])
+ * with index = low | mid << 4 | high << 6 over the sections the tier reads
+ * (idx & 0x0F, idx & 0x3F, idx). Only the first blut_bitplane_bytes(n, tier)
+ * bytes of planes are read, and only the first 16 / 64 / 256 entries of table
+ * (the tier's table: mapped16, mapped64, full).
+ * Replaces, for one tensor of a tier, lut_moe_launch_unpack_4bit
+ * (csrc/kernels/tensor_recover.cu:166-192), the host 6-bit unpack
+ * (csrc/tensor_engine/tensor_engine.cpp:535-547) and the
+ * lut_moe_launch_blocklut_recover that follows them
+ * (csrc/topology/model_topology.cpp:597-618). */
+BLUT_API int blut_bitplane_recover(void* out_bf16, const void* planes_u8, const void* absmax_bf16,
+                                   const void* table_bf16, int64_t n, int32_t tier, int32_t block_size,
+                                   void* stream);
+
 /* ------------------------------------------------------- tiled layout ---- */
 
 /* Bytes of the tiled device layout of one matrix (16-row tiles x 128-column

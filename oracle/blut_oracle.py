@@ -91,6 +91,43 @@ def tier_index(idx: np.ndarray, tier: int) -> np.ndarray:
     raise ValueError(f"tier {tier}")
 
 
+def bitplane_pack(idx: np.ndarray) -> np.ndarray:
+    """Progressive 3-section bit-plane buffer of n uint8 indices, n % 4 == 0
+    (runtime/model_offload.py:751-758): [low4 | mid2 | high2], where
+
+    * low4  [n/2]: byte q holds element 2q in bits 0-3 and 2q+1 in bits 4-7;
+    * mid2  [n/4]: byte q holds bits 4-5 of element 4q+j in bits 2j..2j+1;
+    * high2 [n/4]: the same for bits 6-7.
+    """
+    quads = np.asarray(idx, dtype=np.uint8).reshape(-1, 4).astype(np.uint32)
+    low = (quads[:, 0::2] & 0xF) | ((quads[:, 1::2] & 0xF) << 4)   # 2 bytes per quad
+    sh = np.arange(0, 8, 2, dtype=np.uint32)
+    mid = (((quads >> 4) & 3) << sh).sum(axis=1)
+    high = ((quads >> 6) << sh).sum(axis=1)
+    return np.concatenate([low.reshape(-1), mid, high]).astype(np.uint8)
+
+
+def bitplane_index(planes: np.ndarray, n: int, tier: int) -> np.ndarray:
+    """The index a tier reads back from the first bytes of a bit-plane buffer.
+
+    Tier 2 reads the low section (n/2 bytes), tier 1 low + mid (3n/4), tier 0
+    all n bytes (tensor_engine.cpp:505-509). The index is low | mid << 4 |
+    high << 6 over the sections read. This is the tier-2 GPU unpack of
+    tensor_recover.cu:166-192 and the tier-1 host unpack of
+    tensor_engine.cpp:535-547, so it equals ``tier_index(idx, tier)``.
+    """
+    planes = np.asarray(planes, dtype=np.uint8)
+    assert n % 4 == 0 and planes.size >= {2: n // 2, 1: 3 * n // 4, 0: n}[tier]
+    lo = planes[: n // 2]
+    out = np.stack([lo & 0xF, lo >> 4], axis=1).reshape(-1)
+    sh = np.arange(0, 8, 2, dtype=np.uint8)
+    if tier <= 1:
+        out |= (((planes[n // 2: 3 * n // 4, None] >> sh) & 3) << 4).reshape(-1).astype(np.uint8)
+    if tier == 0:
+        out |= (((planes[3 * n // 4: n, None] >> sh) & 3) << 6).reshape(-1).astype(np.uint8)
+    return out
+
+
 def dequant_r(idx: np.ndarray, absmax_bf16: np.ndarray, table_bf16: np.ndarray,
               block_size: int = 128, tier: int = 0) -> np.ndarray:
     """bf16(f32(table[idx[i]]) * f32(absmax[min(i // bs, nb - 1)])) as bf16 bits.

@@ -27,6 +27,12 @@ It imports the reference's own ``vllm_lut.quantizer`` and
   on a bf16 matrix of 8000 elements (a zero-padded tail block) whose first
   block is all zeros (the absmax clamp).  ``python make_golden.py <ref> convert``
   regenerates only this file.
+* ``bitplane.npz``     -- the progressive bit-plane buffer of
+  ``runtime/model_offload.py:751-758``. The reference's own
+  ``split_and_extract_from_tensor`` is lifted from that file's source with
+  ``ast``, because the module imports a compiled extension, and run on seeded
+  indices (n = 4100) with three file chunks. ``python make_golden.py <ref>
+  bitplane`` regenerates only this file.
 * ``apply_qwen.npz``   -- ``apply`` on a Qwen1.5-MoE-shaped layer (E=60, H=2048,
   I=1408, top-4, T=8).  The 519 MB of weights are not stored: they are
   regenerated from the stored seed with numpy's PCG64 integer stream (stable
@@ -206,11 +212,34 @@ def convert_fixture(ref_root):
                         absmax=bits(absmax))
 
 
+def bitplane_fixture(ref_root):
+    import ast
+    from types import SimpleNamespace
+    import torch
+    path = os.path.join(ref_root, "runtime/model_offload.py")
+    tree = ast.parse(open(path).read())
+    fn = next(n for n in ast.walk(tree) if isinstance(n, ast.FunctionDef) and n.name == "split_and_extract_from_tensor")
+    ns = {"np": np, "torch": torch}
+    exec(compile(ast.Module(body=[fn], type_ignores=[]), path, "exec"), ns)
+    rng = np.random.Generator(np.random.PCG64(17))
+    n = 4100
+    idx = rng.integers(0, 256, size=n, dtype=np.uint8)
+    am = rng.integers(0, 1 << 16, size=(n + 127) // 128, dtype=np.uint16)
+    fake = SimpleNamespace(lut_moe_config=SimpleNamespace(code_type="BLOCKLUT"),
+                           _quantize_weight_to_blocklut=lambda w: (idx, am))
+    chunks, _ = ns["split_and_extract_from_tensor"](fake, torch.zeros(1), 3)
+    np.savez_compressed(os.path.join(HERE, "bitplane.npz"), idx=idx, planes=np.concatenate(chunks),
+                        chunk_sizes=np.array([c.size for c in chunks]))
+
+
 if __name__ == "__main__":
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <block_lut checkout> [convert]")
+        sys.exit("usage: make_golden.py <block_lut checkout> [convert | bitplane]")
     if sys.argv[2:] == ["convert"]:
         convert_fixture(sys.argv[1])
+    elif sys.argv[2:] == ["bitplane"]:
+        bitplane_fixture(sys.argv[1])
     else:
         main(sys.argv[1])
         convert_fixture(sys.argv[1])
+        bitplane_fixture(sys.argv[1])

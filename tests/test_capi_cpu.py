@@ -238,3 +238,18 @@ def test_matmul_workspace_and_launches():
     assert lib.blut_matmul_launch_count(C.byref(paired), 8) == _lib.BLUT_ERR_INVALID
     d = LUTFormat("b", 4, 64).desc(2048, 1408, tc=True)
     assert lib.blut_matmul(C.byref(d), None, None, None, 8, None, 0, None, 0, None) == _lib.BLUT_ERR_INVALID
+
+
+def test_bitplane_host_checks():
+    lib = _lib.lib()
+    # sections read per tier: low (n/2), low + mid (3n/4), all (n)
+    assert [lib.blut_bitplane_bytes(4100, t) for t in (2, 1, 0)] == [2050, 3075, 4100]
+    for n, t in ((4102, 0), (0, 0), (-4, 1), (64, 3), (64, -1)):
+        assert lib.blut_bitplane_bytes(n, t) == _lib.BLUT_ERR_INVALID
+    # argument checks answer before any launch
+    assert lib.blut_bitplane_pack(None, None, 64, None) == _lib.BLUT_ERR_INVALID
+    assert lib.blut_bitplane_pack(1 << 20, 1 << 21, 66, None) == _lib.BLUT_ERR_UNSUPPORTED
+    assert lib.blut_bitplane_recover(1 << 20, 1 << 21, 1 << 22, 1 << 23, 64, 3, 128, None) == _lib.BLUT_ERR_INVALID
+    assert lib.blut_bitplane_recover(1 << 20, 1 << 21, 1 << 22, 1 << 23, 66, 0, 128, None) == \
+        _lib.BLUT_ERR_UNSUPPORTED
+    assert lib.blut_bitplane_recover(1 << 20, 1 << 21, 1 << 22, 1 << 23, 64, 0, 0, None) == _lib.BLUT_ERR_INVALID

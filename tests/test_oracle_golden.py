@@ -37,6 +37,17 @@ def test_encode_r_matches_reference_converter(golden):
     assert np.array_equal(am, e["absmax"])
 
 
+def test_bitplane_pack_matches_reference(golden):
+    # runtime/model_offload.py:751-758, run from the reference's source
+    d = golden("bitplane.npz")
+    n = d["idx"].size
+    assert n % 32 != 0 and int(d["chunk_sizes"].sum()) == n
+    assert np.array_equal(O.bitplane_pack(d["idx"]), d["planes"])
+    # each tier's prefix reads back the tier's index (tensor_engine.cpp:505-509,535-547)
+    for tier, need in ((2, n // 2), (1, 3 * n // 4), (0, n)):
+        assert np.array_equal(O.bitplane_index(d["planes"][:need], n, tier), O.tier_index(d["idx"], tier))
+
+
 @pytest.mark.parametrize("tier,table", [(1, "mapped64"), (2, "mapped16")])
 def test_nested_tiers_bit_exact(golden, tier, table):
     t = golden("tiers.npz")
