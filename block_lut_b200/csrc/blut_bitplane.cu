@@ -29,7 +29,8 @@ namespace blut {
 namespace {
 
 constexpr int kBpThreads = 256;
-constexpr int kBpGroup = 32;  // elements per thread and step on the vector path
+constexpr int kBpGroup = 32;    // elements per thread and step of the packer's vector path
+constexpr int kBpChunk = 1024;  // elements per warp and step of the recover's vector path
 
 inline unsigned bp_grid(int64_t work, int per_sm) {
   const int64_t want = std::max<int64_t>((work + kBpThreads - 1) / kBpThreads, 1);
@@ -85,6 +86,15 @@ __global__ void __launch_bounds__(kBpThreads) bitplane_pack_kernel(uint8_t* __re
 // The tier's table is replicated per lane in shared memory: entry e for lane l
 // at word 32e + l (the bf16 in the low half), so the 32 lookups of a warp hit
 // 32 different banks whatever the indices.
+//
+// Vector path: warp w takes chunks of 1024 elements, c = w, w + warps, ...;
+// lane l handles the four runs of 8 elements at 1024c + 256r + 8l (r < 4).
+// A run's indices are a u32 of the low section and a u16 of the mid and high
+// sections (element k at bits 4k, 2k), and its output is one 16-byte store,
+// so every load and store instruction of the warp covers one contiguous span.
+// With n % 8 == 0, bs % 8 == 0, 4-byte aligned planes and a 16-byte aligned
+// output, every access is aligned and a run never crosses an absmax block.
+// The elements after the last whole chunk go through the per-quad path.
 template <int kTier>
 __global__ void __launch_bounds__(kBpThreads) bitplane_recover_kernel(uint16_t* __restrict__ out,
                                                                       const uint8_t* __restrict__ planes,
@@ -95,43 +105,46 @@ __global__ void __launch_bounds__(kBpThreads) bitplane_recover_kernel(uint16_t* 
   extern __shared__ uint32_t bp_tab[];
   for (int w = threadIdx.x; w < kEntries * 32; w += blockDim.x) bp_tab[w] = table[w >> 5];
   __syncthreads();
-  const uint32_t* tab = bp_tab + (threadIdx.x & 31);
+  const int lane = threadIdx.x & 31;
+  const uint32_t* tab = bp_tab + lane;
   const uint8_t* lo = planes;
   const uint8_t* mi = planes + n / 2;
   const uint8_t* hi = planes + n / 2 + n / 4;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t nv = vec ? n / kBpGroup : 0;
-  for (int64_t v = tid; v < nv; v += stride) {
-    const uint4 L = *reinterpret_cast<const uint4*>(lo + v * 16);
-    uint2 M = make_uint2(0, 0), H = make_uint2(0, 0);
-    if (kTier <= 1) M = *reinterpret_cast<const uint2*>(mi + v * 8);
-    if (kTier == 0) H = *reinterpret_cast<const uint2*>(hi + v * 8);
-    // a 32-element step never crosses an absmax block when bs % 32 == 0
-    const uint32_t s = absmax[std::min<int64_t>(v * kBpGroup / bs, nb - 1)];
-    const uint32_t s2 = s | (s << 16);
-    const uint32_t lw[4] = {L.x, L.y, L.z, L.w};
-    const uint32_t mw[2] = {M.x, M.y};
-    const uint32_t hw[2] = {H.x, H.y};
-    uint32_t o[16];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t nchunk = vec ? n / kBpChunk : 0;
+  for (int64_t c = tid >> 5; c < nchunk; c += stride >> 5) {
+    const int64_t e0 = c * kBpChunk + 8 * lane;
+    uint32_t L[4], M[4] = {0, 0, 0, 0}, H[4] = {0, 0, 0, 0}, S[4];
 #pragma unroll
-    for (int p = 0; p < 16; ++p) {
-      uint32_t t = 0;
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int k = 2 * p + u;
-        uint32_t x = (lw[k >> 3] >> (4 * (k & 7))) & 0xFu;
-        if (kTier <= 1) x |= ((mw[k >> 4] >> (2 * (k & 15))) & 3u) << 4;
-        if (kTier == 0) x |= ((hw[k >> 4] >> (2 * (k & 15))) & 3u) << 6;
-        t |= tab[32 * x] << (16 * u);
-      }
-      o[p] = bf16x2_mul(t, s2);
+    for (int r = 0; r < 4; ++r) {
+      const int64_t e = e0 + 256 * r;
+      L[r] = *reinterpret_cast<const uint32_t*>(lo + e / 2);
+      if (kTier <= 1) M[r] = *reinterpret_cast<const uint16_t*>(mi + e / 4);
+      if (kTier == 0) H[r] = *reinterpret_cast<const uint16_t*>(hi + e / 4);
+      S[r] = absmax[std::min<int64_t>(e / bs, nb - 1)];
     }
-    uint4* op = reinterpret_cast<uint4*>(out + v * kBpGroup);
 #pragma unroll
-    for (int r = 0; r < 4; ++r) op[r] = make_uint4(o[4 * r], o[4 * r + 1], o[4 * r + 2], o[4 * r + 3]);
+    for (int r = 0; r < 4; ++r) {
+      const uint32_t s2 = S[r] | (S[r] << 16);
+      uint32_t o[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        uint32_t t = 0;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int k = 2 * p + u;
+          uint32_t x = (L[r] >> (4 * k)) & 0xFu;
+          if (kTier <= 1) x |= ((M[r] >> (2 * k)) & 3u) << 4;
+          if (kTier == 0) x |= ((H[r] >> (2 * k)) & 3u) << 6;
+          t |= tab[32 * x] << (16 * u);
+        }
+        o[p] = bf16x2_mul(t, s2);
+      }
+      *reinterpret_cast<uint4*>(out + e0 + 256 * r) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
-  for (int64_t q = nv * (kBpGroup / 4) + tid; q < n / 4; q += stride) {
+  for (int64_t q = nchunk * (kBpChunk / 4) + tid; q < n / 4; q += stride) {
     const uint32_t l = uint32_t(lo[2 * q]) | (uint32_t(lo[2 * q + 1]) << 8);
     const uint32_t m = kTier <= 1 ? mi[q] : 0u;
     const uint32_t h = kTier == 0 ? hi[q] : 0u;
@@ -193,9 +206,8 @@ int bitplane_recover(void* out, const void* planes, const void* absmax, const vo
   if (!out || !planes || !absmax || !table || n <= 0 || bs <= 0 || tier < 0 || tier > 2) return BLUT_ERR_INVALID;
   if (n % 4) return BLUT_ERR_UNSUPPORTED;
   const int64_t nb = (n + bs - 1) / bs;
-  const bool vec = n % kBpGroup == 0 && bs % kBpGroup == 0 && ((uintptr_t)planes & 15) == 0 &&
-                   ((uintptr_t)out & 15) == 0;
-  const int64_t work = vec ? n / kBpGroup : n / 4;
+  const bool vec = n % 8 == 0 && bs % 8 == 0 && ((uintptr_t)planes & 3) == 0 && ((uintptr_t)out & 15) == 0;
+  const int64_t work = vec ? std::max<int64_t>(n / kBpChunk * 32, n / 4 - n / kBpChunk * (kBpChunk / 4)) : n / 4;
   const size_t smem = recover_smem(tier);
   const auto* pl = (const uint8_t*)planes;
   const auto* am = (const uint16_t*)absmax;

@@ -50,7 +50,10 @@ def _case(n, bs, seed):
 
 
 @pytest.mark.parametrize("tier", [0, 1, 2])
-@pytest.mark.parametrize("n,bs", [(4100, 128), (1 << 20, 128), (65536, 100), (96, 32), (4, 128)])
+# (1 << 20) + 8 and 3088 take the warp-chunk path and then the per-quad tail;
+# 4100 and bs 100 only the per-quad path
+@pytest.mark.parametrize("n,bs", [(4100, 128), (1 << 20, 128), ((1 << 20) + 8, 96), (3088, 128), (65536, 100),
+                                  (96, 32), (4, 128)])
 def test_recover_tier_bit_exact(tier, n, bs):
     idx, am, table = _case(n, bs, n + bs + tier)
     planes = O.bitplane_pack(idx)
