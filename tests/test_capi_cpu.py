@@ -253,3 +253,43 @@ def test_bitplane_host_checks():
     assert lib.blut_bitplane_recover(1 << 20, 1 << 21, 1 << 22, 1 << 23, 66, 0, 128, None) == \
         _lib.BLUT_ERR_UNSUPPORTED
     assert lib.blut_bitplane_recover(1 << 20, 1 << 21, 1 << 22, 1 << 23, 64, 0, 0, None) == _lib.BLUT_ERR_INVALID
+
+
+C_CALLER = r"""
+#include <stdio.h>
+#include <string.h>
+#include "blut.h"
+
+int main(void) {
+  blut_mat_desc d;
+  memset(&d, 0, sizeof d);
+  d.format = BLUT_FMT_B; d.bits = 4; d.group = 64; d.dtype = BLUT_F16;
+  d.layout = BLUT_LAYOUT_TC; d.rows = 2816; d.cols = 2048;
+  if (blut_tiled_bytes(&d) != 2816LL * 2048) return 1;            /* 1 byte per weight at 4-bit g64 */
+  if (blut_bitplane_bytes(4100, 1) != 3075) return 2;
+  if (blut_bitplane_bytes(4102, 0) != BLUT_ERR_INVALID) return 3;
+  if (blut_bitplane_pack(NULL, NULL, 64, NULL) != BLUT_ERR_INVALID) return 4;
+  if (strcmp(blut_status_string(BLUT_OK), "ok") != 0) return 5;
+  blut_moe_args a;
+  memset(&a, 0, sizeof a);
+  if (blut_moe_workspace_size(&a) != 0) return 6;                  /* an empty layer needs nothing */
+  puts("c caller ok");
+  return 0;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_header_compiles_as_c99_and_links(tmp_path):
+    """A native caller (the HF engine's C/C++ side) includes blut.h as plain C,
+    links libblut.so, and gets host-side answers without a GPU."""
+    src = tmp_path / "caller.c"
+    src.write_text(C_CALLER)
+    exe = tmp_path / "caller"
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                        str(src), "-L", libdir, "-lblut", "-Wl,-rpath," + libdir, "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and "c caller ok" in r.stdout, (r.returncode, r.stdout, r.stderr)
