@@ -33,6 +33,11 @@ It imports the reference's own ``vllm_lut.quantizer`` and
   ``ast``, because the module imports a compiled extension, and run on seeded
   indices (n = 4100) with three file chunks. ``python make_golden.py <ref>
   bitplane`` regenerates only this file.
+* ``additive.npz``     -- ``dequantize_additive_lut``
+  (``evaluation/explore_additive_lut.py:266-276``), the reference's additive
+  two-table reconstruction (coarse[c] + fine[f]) times absmax, on seeded
+  codes. Its tables are dyadic, so every sum is exact in fp16, and its absmax
+  is 1. ``python make_golden.py <ref> additive`` regenerates only this file.
 * ``apply_qwen.npz``   -- ``apply`` on a Qwen1.5-MoE-shaped layer (E=60, H=2048,
   I=1408, top-4, T=8).  The 519 MB of weights are not stored: they are
   regenerated from the stored seed with numpy's PCG64 integer stream (stable
@@ -232,14 +237,34 @@ def bitplane_fixture(ref_root):
                         chunk_sizes=np.array([c.size for c in chunks]))
 
 
+def additive_fixture(ref_root):
+    import importlib.util
+    path = os.path.join(ref_root, "evaluation/explore_additive_lut.py")
+    spec = importlib.util.spec_from_file_location("explore_additive_lut", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    rng = np.random.Generator(np.random.PCG64(23))
+    coarse = np.sort(rng.integers(-64, 64, 4)).astype(np.float32) / 64.0
+    fine = np.sort(rng.integers(-16, 16, 4)).astype(np.float32) / 1024.0
+    n = 512
+    ic = rng.integers(0, 4, n).astype(np.uint8)
+    ifn = rng.integers(0, 4, n).astype(np.uint8)
+    absmax = np.ones(n // 128, dtype=np.float32)
+    x = mod.dequantize_additive_lut(ic, ifn, absmax, coarse, fine, 128, n)
+    np.savez_compressed(os.path.join(HERE, "additive.npz"), coarse=coarse, fine=fine, ic=ic, ifn=ifn, x=x)
+
+
 if __name__ == "__main__":
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <block_lut checkout> [convert | bitplane]")
+        sys.exit("usage: make_golden.py <block_lut checkout> [convert | bitplane | additive]")
     if sys.argv[2:] == ["convert"]:
         convert_fixture(sys.argv[1])
     elif sys.argv[2:] == ["bitplane"]:
         bitplane_fixture(sys.argv[1])
+    elif sys.argv[2:] == ["additive"]:
+        additive_fixture(sys.argv[1])
     else:
         main(sys.argv[1])
         convert_fixture(sys.argv[1])
         bitplane_fixture(sys.argv[1])
+        additive_fixture(sys.argv[1])

@@ -37,6 +37,20 @@ def test_encode_r_matches_reference_converter(golden):
     assert np.array_equal(am, e["absmax"])
 
 
+def test_nested_reconstruction_matches_reference_additive_rule(golden):
+    # evaluation/explore_additive_lut.py:266-276 reconstructs coarse[c] + fine[f]
+    # (times absmax, 1 here). The NestedLUT table with refine[c][r] = fine[r]
+    # for every c must give the same values from the same two code streams.
+    d = golden("additive.npz")
+    n, group = d["ic"].size, 64
+    coarse_t = np.tile(d["coarse"].astype(np.float16), (1, n // group, 1))
+    refine_t = np.tile(np.tile(d["fine"].astype(np.float16), 4), (1, n // group, 1))
+    cp = O.pack_codes(d["ic"].reshape(1, n), 2)
+    rp = O.pack_codes(d["ifn"].reshape(1, n), 2)
+    out = O.dequant_nested(cp, rp, coarse_t, refine_t, group)
+    assert np.array_equal(out.astype(np.float32).reshape(-1), d["x"])
+
+
 def test_bitplane_pack_matches_reference(golden):
     # runtime/model_offload.py:751-758, run from the reference's source
     d = golden("bitplane.npz")
