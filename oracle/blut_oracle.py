@@ -18,6 +18,12 @@ by running the reference's Python code, see ``tests/golden/make_golden.py``):
                           bf16 normalisation, first-index argmin).
   * ``tier_index``     -- progressive tiers of ``runtime/model_offload.py:751-758``
                           and ``csrc/tensor_engine/tensor_engine.hpp:287-291``.
+  * ``bitplane_pack``, ``bitplane_index`` -- the 3-section bit-plane buffer of
+                          ``runtime/model_offload.py:751-758`` and the tier
+                          unpacks of ``csrc/kernels/tensor_recover.cu:166-192``
+                          and ``csrc/tensor_engine/tensor_engine.cpp:535-547``.
+  * ``encode_r`` also equals the reference converter's ``quantize_weight``
+                          (``vllm_lut/convert_checkpoint.py:61-104``).
   * ``routing``        -- ``vllm_lut/moe_layer.py:358-376`` and
                           ``customized/qwen.py:44-54`` (softmax -> top-k -> renorm).
   * ``moe_forward``    -- ``vllm_lut/quant_method.py:230-279`` (apply) with the
@@ -30,8 +36,10 @@ restatement of the reference's building blocks -- Lloyd iterations of
 ``quantizer.py:292-296``, the additive coarse+fine value of
 ``evaluation/explore_additive_lut.py:3-8,72-140`` and the bit-plane packing
 convention of ``runtime/model_offload.py:751-758`` (element 0 in the low bits).
-PARITY UNPINNED for Format B and NestedLUT: no reference test or golden vector
-exists for them.
+PARITY UNPINNED for Format B and for the per-block Lloyd encoders: no
+reference test or golden vector exists for them. The NestedLUT reconstruction
+rule alone is pinned, by the reference's ``dequantize_additive_lut``
+(``evaluation/explore_additive_lut.py:266-276``) run on seeded codes.
 
 bf16 values are carried as uint16 bit patterns (numpy has no bfloat16), fp16
 as numpy float16.
