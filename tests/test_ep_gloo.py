@@ -110,11 +110,15 @@ def test_expert_ranges():
     assert sum(c for _, c in expert_ranges(64, 3)) == 64
 
 
-def test_ep_dispatch_combine_matches_single_process():
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_dispatch_combine_matches_single_process(world):
+    # 4 ranks split the 6 experts unevenly (2, 2, 1, 1), as 60 experts on 8 GPUs do
+    from block_lut_b200.ep import expert_ranges
     from oracle import blut_oracle as O
-    res = _run(2)
+    assert len({c for _, c in expert_ranges(E, world)}) == (2 if world == 4 else 1)
+    res = _run(world)
     W13, W2 = _weights()
-    for r in (0, 1):
+    for r in range(world):
         status, out = res[r]
         assert status == "ok", out
         x, ids, tw = _tokens(r)
