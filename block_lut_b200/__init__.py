@@ -9,6 +9,10 @@ Python / PyTorch host code over ``libblut.so`` (C ABI in ``include/blut.h``):
 * ``cuda_lut_gemv``  -- ``lut_gemv`` (reference ``vllm_lut/cuda_lut_gemv.py``)
 * ``quantizer``      -- ``LUTQuantizer``, ``decompress_blocklut`` (reference ``vllm_lut/quantizer.py``)
 * ``moe_layer``      -- ``DeepseekV2MoE_LUT``, ``_routing`` (reference ``vllm_lut/moe_layer.py``)
+* ``linear``         -- ``LUTLinear``: one weight matrix, any format and token count
+* ``ep``             -- ``EPMoELayer``: expert parallelism over NCCL
+* ``bitplanes``      -- progressive bit-plane tiers of Format R (``runtime/model_offload.py``)
+* ``convert_checkpoint`` -- bf16 checkpoint -> LUT checkpoint (reference ``vllm_lut/convert_checkpoint.py``)
 """
 from . import _lib
 from .formats import LUTFormat, QuantizedMatrix, dequant, encode, encode_r, pack_tiled, tiled_bytes
