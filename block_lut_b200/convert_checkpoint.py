@@ -39,6 +39,10 @@ Format B and NestedLUT (``--format b | nested``, ``--bits``, ``--group``):
   (…) parameters that ``LUTFusedMoEMethod.create_weights`` registers;
 * ``config.json`` gets the ``quantization_config`` that selects the format.
 
+``--from_lut`` starts from a Format R checkpoint instead (this converter's
+output or the reference's): each routed-expert weight is dequantised on the
+GPU to bf16 and re-encoded to Format B or NestedLUT.
+
 Codebooks stored as uint16 arrays (the NestedLUT ``mapped`` tables) are read as
 bf16 bit patterns, as the runtime's tier tables are; the reference converters
 cast their integer values instead.
@@ -59,7 +63,7 @@ from typing import Dict, List, Optional, Tuple
 import numpy as np
 import torch
 
-from .formats import LUTFormat, encode, encode_r
+from .formats import LUTFormat, QuantizedMatrix, dequant, encode, encode_r
 from .quantizer import _load_table
 
 SIDE_SUFFIXES = (".json", ".py", ".txt", ".model", ".npy")
@@ -81,6 +85,9 @@ def parse_args(argv: Optional[List[str]] = None) -> argparse.Namespace:
     p.add_argument("--tier", default="full", choices=["full", "coarse"], help="NestedLUT tier the config selects")
     p.add_argument("--write_quant_config", action="store_true",
                    help="also write quantization_config for Format R (always written for b / nested)")
+    p.add_argument("--from_lut", action="store_true",
+                   help="read a Format R checkpoint (uint8 indices, lut_absmax.npz, codebook) instead of a bf16 "
+                        "one, and re-encode its routed experts to --format b | nested")
     p.add_argument("--device", default="cuda", help="CUDA device of the encoder")
     return p.parse_args(argv)
 
@@ -94,6 +101,12 @@ def is_routed_expert(name: str) -> bool:
 def should_encode(name: str, dtype: torch.dtype) -> bool:
     """Encoded: routed-expert ``.weight`` tensors stored in bf16 (convert_model.py:91-95)."""
     return is_routed_expert(name) and name.endswith(".weight") and dtype == torch.bfloat16
+
+
+def is_lut_weight(name: str, dtype: torch.dtype, absmax_keys) -> bool:
+    """In a Format R checkpoint: a routed-expert ``.weight`` stored as uint8
+    indices whose absmax is in ``lut_absmax.npz``."""
+    return is_routed_expert(name) and name.endswith(".weight") and dtype == torch.uint8 and name in absmax_keys
 
 
 def codebook_file(model_path: str, code_type: str) -> str:
@@ -117,7 +130,9 @@ def shard_files(model_path: str) -> List[str]:
 
 
 def lut_name(fname: str) -> str:
-    return os.path.basename(fname).replace(".safetensors", "_lut.safetensors")
+    """``<shard>_lut.safetensors``; a shard that already has the suffix keeps its name."""
+    base = os.path.basename(fname)
+    return base if base.endswith("_lut.safetensors") else base.replace(".safetensors", "_lut.safetensors")
 
 
 def remap_index(index_data: Dict) -> Dict:
@@ -171,6 +186,18 @@ def quantize_weight(weight: torch.Tensor, codebook: torch.Tensor, device: str = 
     return idx.cpu(), absmax.cpu()
 
 
+def dequant_lut_weight(idx: torch.Tensor, absmax: np.ndarray, table: torch.Tensor, device: str = "cuda") -> torch.Tensor:
+    """A Format R weight (uint8 indices [rows, cols], absmax per flat block of
+    128, 256-entry table) back to bf16 [rows, cols] on the GPU, bit-exact
+    (quantizer.py:449-477)."""
+    rows, cols = idx.shape
+    qm = QuantizedMatrix(LUTFormat("r8", 8, BLOCK_SIZE), rows, cols, idx.to(device).contiguous().reshape(-1),
+                         table.to(device=device, dtype=torch.bfloat16).contiguous(),
+                         scales=torch.from_numpy(np.asarray(absmax, dtype=np.float32)).to(device=device,
+                                                                                         dtype=torch.bfloat16))
+    return dequant(qm)
+
+
 def encode_expert(name: str, weight: torch.Tensor, fmt: LUTFormat, device: str = "cuda") -> Dict[str, torch.Tensor]:
     """Format B / NestedLUT encoding of one [rows, cols] expert weight: the
     checkpoint entries (codes under ``name``, tables, NestedLUT residual codes
@@ -198,7 +225,16 @@ def convert_checkpoint(args: argparse.Namespace) -> Dict:
     output_path = args.output or (model_path.rstrip("/") + "_lut")
     os.makedirs(output_path, exist_ok=True)
     fmt = format_of(args)
-    codebook = _load_table(codebook_file(model_path, args.code_type)) if fmt is None else None
+    codebook = _load_table(codebook_file(model_path, args.code_type)) if fmt is None or args.from_lut else None
+    src_absmax = None
+    if args.from_lut:
+        if fmt is None:
+            raise ValueError("--from_lut re-encodes a Format R checkpoint: pass --format b or --format nested")
+        npz = os.path.join(model_path, ABSMAX_NAME)
+        if not os.path.exists(npz):
+            raise FileNotFoundError(f"--from_lut needs {ABSMAX_NAME} in {model_path}")
+        src_absmax = np.load(npz)
+        src_keys = set(src_absmax.files)
     shards = shard_files(model_path)
     if not shards:
         raise FileNotFoundError(f"no safetensors shards in {model_path}")
@@ -211,11 +247,16 @@ def convert_checkpoint(args: argparse.Namespace) -> Dict:
         with safe_open(ckpt, framework="pt", device="cpu") as f:
             for name in f.keys():
                 t = f.get_tensor(name)
-                if not should_encode(name, t.dtype):
+                take = is_lut_weight(name, t.dtype, src_keys) if src_absmax is not None else \
+                    should_encode(name, t.dtype)
+                if not take:
                     new_state[name] = t
                     stats["copied"] += 1
                     continue
-                if fmt is None:
+                if src_absmax is not None:
+                    w = dequant_lut_weight(t, src_absmax[name], codebook, args.device)
+                    new_state.update(encode_expert(name, w, fmt, args.device))
+                elif fmt is None:
                     idx, am = quantize_weight(t, codebook, args.device)
                     new_state[name] = idx.reshape(t.shape)
                     absmax[name] = am.float().numpy()

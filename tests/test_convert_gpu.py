@@ -186,3 +186,37 @@ def test_format_b_conversion_bit_exact_and_loads(ckpt, tmp_path, argv):
     y = method.apply(layer, x, cuda(tw), cuda(ids))
     ref = O.moe_forward(x.float().cpu().numpy(), ids, tw, W13, W2, act_dtype="f16")
     check_layer(y, ref, torch.float16, f"converted {fmt} layer")
+
+
+@pytest.mark.parametrize("argv", [["--format", "b", "--bits", "4", "--group", "64"],
+                                  ["--format", "nested", "--group", "64"]])
+def test_from_lut_reencodes_a_format_r_checkpoint(ckpt, tmp_path, argv):
+    """Format R checkpoint -> Format B / NestedLUT: each routed-expert weight is
+    the Format R dequant (bf16) re-encoded, bit for bit as the oracle does it."""
+    src, tensors = ckpt
+    r_out, out = tmp_path / "r", tmp_path / "b"
+    assert CC.main(["--model", str(src), "--output", str(r_out)]) == 0
+    assert CC.main(["--model", str(r_out), "--output", str(out), "--from_lut"] + argv) == 0
+    fmt = CC.format_of(CC.parse_args(["--model", str(src)] + argv))
+    assert sorted(p.name for p in out.glob("*.safetensors")) == sorted(CC.lut_name(f) for f in SHARDS)
+    r_conv, conv = _converted(r_out), _converted(out)
+    absmax = np.load(r_out / CC.ABSMAX_NAME)
+    table = to_u16(torch.from_numpy(np.load(src / "blocklut_256.npy")).to(torch.bfloat16))
+    for name, w in tensors.items():
+        if not CC.should_encode(name, w.dtype):
+            assert torch.equal(conv[name], w), name
+            continue
+        deq = O.bf16_to_f32(O.dequant_r(r_conv[name].numpy().reshape(-1), O.f32_to_bf16(absmax[name]), table,
+                                        128)).reshape(w.shape)
+        stem = name[:-len(".weight")]
+        if fmt.kind == "nested":
+            want = dict(zip(("", ".residual", ".tables", ".refine"), O.encode_nested(deq, fmt.group)))
+        else:
+            want = dict(zip(("", ".tables"), O.encode_b(deq, fmt.bits, fmt.group)))
+        for suffix, ref in want.items():
+            got = conv[name if suffix == "" else stem + suffix].numpy()
+            assert np.array_equal(got.view(np.uint8), ref.view(np.uint8)), name + suffix
+    cfg = json.loads((out / "config.json").read_text())["quantization_config"]
+    assert cfg["codebook_scope"] == "row_block" and cfg["lut_block"] == fmt.group
+    with pytest.raises(ValueError):
+        CC.main(["--model", str(r_out), "--output", str(tmp_path / "bad"), "--from_lut"])
