@@ -223,6 +223,8 @@ def convert_checkpoint(args: argparse.Namespace) -> Dict:
         raise RuntimeError("convert_checkpoint encodes on the GPU; no CUDA device is available")
     model_path = args.model
     output_path = args.output or (model_path.rstrip("/") + "_lut")
+    if os.path.realpath(output_path) == os.path.realpath(model_path):
+        raise ValueError("--output must differ from --model: the shards would overwrite their own inputs")
     os.makedirs(output_path, exist_ok=True)
     fmt = format_of(args)
     codebook = _load_table(codebook_file(model_path, args.code_type)) if fmt is None or args.from_lut else None

@@ -75,6 +75,14 @@ def test_quant_config_selects_the_converted_format(tmp_path, argv, expect):
         assert (fmt.bits, fmt.group, fmt.tier) == (want.bits, want.group, want.tier)
 
 
+def test_shard_names_and_in_place_refusal(tmp_path, monkeypatch):
+    # a shard already named *_lut keeps its name, so a re-conversion in place is refused
+    assert CC.lut_name("model-00001-of-00002_lut.safetensors") == "model-00001-of-00002_lut.safetensors"
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    with pytest.raises(ValueError, match="differ"):
+        CC.convert_checkpoint(CC.parse_args(["--model", str(tmp_path), "--output", str(tmp_path)]))
+
+
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU refusal")
 def test_converter_refuses_without_gpu(tmp_path):
     np.save(tmp_path / "blocklut_256.npy", np.linspace(-1, 1, 256, dtype=np.float32))
