@@ -90,3 +90,39 @@ def test_converter_refuses_without_gpu(tmp_path):
         CC.convert_checkpoint(CC.parse_args(["--model", str(tmp_path), "--output", str(tmp_path / "o")]))
     with pytest.raises(Exception):
         CC.quantize_weight(torch.zeros(256, dtype=torch.bfloat16), torch.zeros(256, dtype=torch.bfloat16))
+
+
+def test_absmax_file_feeds_the_loader(tmp_path):
+    """lut_absmax.npz as the converter writes it (float32 copies of bf16, keyed
+    by .weight names) loads into w13_absmax (gate blocks, then up blocks) and
+    w2_absmax of the right layer (quant_method.py:189-222): by layer_id when
+    the layer has one, else in call order."""
+    from types import SimpleNamespace
+    from block_lut_b200.quant_method import LUTConfig, LUTFusedMoEMethod
+    E, nb = 2, 3
+    data = {}
+    for layer in (0, 1):
+        for e in range(E):
+            for j, proj in enumerate(("gate", "up", "down")):
+                v = torch.tensor([layer * 100 + e * 10 + j + q / 4 for q in range(nb)]).to(torch.bfloat16)
+                data[f"model.layers.{layer}.mlp.experts.{e}.{proj}_proj.weight"] = v.float().numpy()
+    data["model.layers.0.mlp.shared_expert.gate_proj.weight"] = np.zeros(nb, dtype=np.float32)
+    np.savez(tmp_path / CC.ABSMAX_NAME, **data)
+    method = LUTFusedMoEMethod(LUTConfig(code_type="BLOCKLUT"))
+
+    def fresh(layer_id=None):
+        ns = SimpleNamespace(w13_weight=torch.zeros(E, 4, 4, dtype=torch.uint8),
+                             w13_absmax=torch.zeros(E, 2 * nb, dtype=torch.bfloat16),
+                             w2_absmax=torch.zeros(E, nb, dtype=torch.bfloat16))
+        if layer_id is not None:
+            ns.layer_id = layer_id
+        return ns
+
+    def want(layer, e, proj):
+        return torch.from_numpy(data[f"model.layers.{layer}.mlp.experts.{e}.{proj}_proj.weight"]).to(torch.bfloat16)
+
+    for expect_layer, lay in ((0, fresh()), (1, fresh()), (1, fresh(layer_id=1))):
+        method._load_absmax(lay, str(tmp_path / CC.ABSMAX_NAME))
+        for e in range(E):
+            assert torch.equal(lay.w13_absmax[e], torch.cat([want(expect_layer, e, "gate"), want(expect_layer, e, "up")]))
+            assert torch.equal(lay.w2_absmax[e], want(expect_layer, e, "down"))
