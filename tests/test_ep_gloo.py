@@ -23,18 +23,18 @@ def _free_port():
 E, H, I, K, T = 6, 32, 16, 2, 5
 
 
-def _weights():
+def _weights(n_exp=E):
     rng = np.random.Generator(np.random.PCG64(123))
-    W13 = [rng.standard_normal((2 * I, H)).astype(np.float32) * 0.1 for _ in range(E)]
-    W2 = [rng.standard_normal((H, I)).astype(np.float32) * 0.1 for _ in range(E)]
+    W13 = [rng.standard_normal((2 * I, H)).astype(np.float32) * 0.1 for _ in range(n_exp)]
+    W2 = [rng.standard_normal((H, I)).astype(np.float32) * 0.1 for _ in range(n_exp)]
     return W13, W2
 
 
-def _tokens(rank):
+def _tokens(rank, n_exp=E):
     from oracle import blut_oracle as O
     rng = np.random.Generator(np.random.PCG64(7 + rank))
     x = O.rms_activations(rng, T, H)
-    ids, tw = O.routing(rng.standard_normal((T, E)).astype(np.float32), K)
+    ids, tw = O.routing(rng.standard_normal((T, n_exp)).astype(np.float32), K)
     return x, ids, tw
 
 
@@ -53,7 +53,7 @@ def _local_partial(x, ids, tw, W13, W2, start):
     return out
 
 
-def _rank_main(rank, world, port, q, fail_rank):
+def _rank_main(rank, world, port, q, fail_rank, n_exp):
     try:
         import sys
         from datetime import timedelta
@@ -66,9 +66,9 @@ def _rank_main(rank, world, port, q, fail_rank):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
         if rank == fail_rank:
             raise RuntimeError("injected failure before the exchange")
-        W13, W2 = _weights()
-        x, ids, tw = _tokens(rank)
-        owner, local = ep.owner_tables(E, world, "cpu")
+        W13, W2 = _weights(n_exp)
+        x, ids, tw = _tokens(rank, n_exp)
+        owner, local = ep.owner_tables(n_exp, world, "cpu")
         sx, si, sw = ep.build_dispatch(torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(tw),
                                        owner, local, world)
         try:
@@ -76,7 +76,7 @@ def _rank_main(rank, world, port, q, fail_rank):
         except Exception as exc:  # the peer died: the collective must fail, not hang
             q.put((rank, "collective-error", type(exc).__name__))
             return
-        start = ep.expert_ranges(E, world)[rank][0]
+        start = ep.expert_ranges(n_exp, world)[rank][0]
         part = _local_partial(rx.view(-1, H).numpy(), ri.view(-1, K).numpy(), rw.view(-1, K).numpy(), W13, W2, start)
         out = ep.combine(torch.from_numpy(part).view(world, T, H))
         q.put((rank, "ok", out.numpy()))
@@ -85,11 +85,11 @@ def _rank_main(rank, world, port, q, fail_rank):
         q.put((rank, "raised", traceback.format_exc()))
 
 
-def _run(world, fail_rank=-1):
+def _run(world, fail_rank=-1, n_exp=E):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_rank_main, args=(r, world, port, q, fail_rank)) for r in range(world)]
+    ps = [ctx.Process(target=_rank_main, args=(r, world, port, q, fail_rank, n_exp)) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
@@ -110,18 +110,19 @@ def test_expert_ranges():
     assert sum(c for _, c in expert_ranges(64, 3)) == 64
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ep_dispatch_combine_matches_single_process(world):
-    # 4 ranks split the 6 experts unevenly (2, 2, 1, 1), as 60 experts on 8 GPUs do
+@pytest.mark.parametrize("world,n_exp", [(2, E), (4, E), (8, 60)])
+def test_ep_dispatch_combine_matches_single_process(world, n_exp):
+    # 4 ranks split 6 experts unevenly (2, 2, 1, 1); 8 ranks take Qwen1.5's 60
+    # experts as 8, 8, 8, 8, 7, 7, 7, 7 (the 8-GPU bench)
     from block_lut_b200.ep import expert_ranges
     from oracle import blut_oracle as O
-    assert len({c for _, c in expert_ranges(E, world)}) == (2 if world == 4 else 1)
-    res = _run(world)
-    W13, W2 = _weights()
+    assert len({c for _, c in expert_ranges(n_exp, world)}) == (1 if world == 2 else 2)
+    res = _run(world, n_exp=n_exp)
+    W13, W2 = _weights(n_exp)
     for r in range(world):
         status, out = res[r]
         assert status == "ok", out
-        x, ids, tw = _tokens(r)
+        x, ids, tw = _tokens(r, n_exp)
         ref = O.moe_forward(x, ids, tw, W13, W2, act_dtype="f16")
         np.testing.assert_allclose(out, ref, rtol=1e-9, atol=1e-12)
 
