@@ -7,6 +7,7 @@ Python / PyTorch host code over ``libblut.so`` (C ABI in ``include/blut.h``):
 * ``quant_method``   -- vLLM plugin ``"lut"`` (reference ``vllm_lut/quant_method.py``)
 * ``fast_moe``       -- ``fused_lut_moe`` (reference ``vllm_lut/fast_moe.py``)
 * ``cuda_lut_gemv``  -- ``lut_gemv`` (reference ``vllm_lut/cuda_lut_gemv.py``)
+* ``fused_kernel``   -- ``fused_lut_gemv`` (reference ``vllm_lut/fused_kernel.py``)
 * ``quantizer``      -- ``LUTQuantizer``, ``decompress_blocklut`` (reference ``vllm_lut/quantizer.py``)
 * ``moe_layer``      -- ``DeepseekV2MoE_LUT``, ``_routing`` (reference ``vllm_lut/moe_layer.py``)
 * ``linear``         -- ``LUTLinear``: one weight matrix, any format and token count

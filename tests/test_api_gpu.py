@@ -12,6 +12,7 @@ from tests.golden.make_golden import small_layer_indices
 
 from block_lut_b200.cuda_lut_gemv import lut_gemv
 from block_lut_b200.fast_moe import fused_lut_moe
+from block_lut_b200.fused_kernel import fused_lut_gemv
 from block_lut_b200.moe import router
 
 pytestmark = pytest.mark.gpu
@@ -89,6 +90,9 @@ def test_lut_gemv(m, k):
     o = y.float().cpu().numpy()
     ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(rb), 1e-30))) - 7)
     assert (np.abs(o - rb) <= ulp).all()
+    # fused_kernel.fused_lut_gemv (fused_kernel.py:13-46) is the same kernel
+    f = fused_lut_gemv(bf16_tensor(x), cuda(idx), bf16_tensor(tab), bf16_tensor(am))
+    assert torch.equal(f.view(torch.int16), y.view(torch.int16))
 
 
 def test_router_kernel_against_oracle(golden):

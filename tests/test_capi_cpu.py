@@ -293,3 +293,10 @@ def test_header_compiles_as_c99_and_links(tmp_path):
     assert r.returncode == 0, r.stderr
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and "c caller ok" in r.stdout, (r.returncode, r.stdout, r.stderr)
+
+
+def test_fused_lut_gemv_rejects_other_block_sizes():
+    from block_lut_b200.fused_kernel import fused_lut_gemv
+    z = torch.zeros(4)
+    with pytest.raises(ValueError, match="128"):
+        fused_lut_gemv(z, torch.zeros(2, 4, dtype=torch.uint8), z, z, block_size=64)
