@@ -34,9 +34,10 @@ from typing import Any, Dict
 import numpy as np
 import torch
 
+from . import _lib
 from .formats import LUTFormat, QuantizedMatrix
 from .moe import LUTExperts, LUTMoELayer
-from .quantizer import LUTQuantizer
+from .quantizer import LUTQuantizer, decompress_blocklut
 
 try:  # vLLM is the caller; the classes subclass its bases when it is importable
     from vllm.model_executor.layers.quantization.base_config import QuantizationConfig as _QCBase
@@ -246,6 +247,26 @@ class LUTFusedMoEMethod(_MoEBase):
         """MoE over the LUT experts: [T, H] -> [T, H] in x's dtype."""
         moe = self._layer(layer, topk_ids.shape[-1])
         return moe.forward(x, topk_ids, topk_weights)
+
+    # ------------------------------------------------ reference helpers --
+    def _decompress_one(self, indices, absmax, codebook, block_size=128):
+        """One expert's Format R weights to bf16, flattened (quant_method.py:281-290)."""
+        return decompress_blocklut(indices, absmax, codebook, block_size)
+
+    def _batch_decompress(self, indices, absmax, codebook, block_size=128):
+        """Every expert at once, expert e scaled by absmax[e], in the shape of
+        ``indices`` (quant_method.py:292-308); one ``blut_batch_blocklut_decompress``."""
+        n_exp = indices.shape[0]
+        dev = indices.device if indices.is_cuda else torch.device("cuda")
+        idx = indices.reshape(n_exp, -1).to(dev).contiguous()
+        am = absmax.reshape(n_exp, -1).to(device=dev, dtype=torch.bfloat16).contiguous()
+        cb = codebook.to(device=dev, dtype=torch.bfloat16).contiguous()
+        out = torch.empty(idx.shape, dtype=torch.bfloat16, device=dev)
+        with _lib.on_device(out):
+            _lib.check(_lib.lib().blut_batch_blocklut_decompress(out.data_ptr(), idx.data_ptr(), am.data_ptr(),
+                                                                 cb.data_ptr(), n_exp, idx.shape[1], am.shape[1],
+                                                                 block_size, _lib.stream_ptr()), "_batch_decompress")
+        return out.reshape(indices.shape)
 
     def get_fused_moe_quant_config(self, layer=None):
         from vllm.model_executor.layers.fused_moe.config import FusedMoEQuantConfig, FusedMoEQuantDesc

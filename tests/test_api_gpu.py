@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from oracle import blut_oracle as O
-from tests._helpers import bf16_tensor, check_layer, cuda, routing_inputs
+from tests._helpers import bf16_tensor, check_layer, cuda, routing_inputs, to_u16
 from tests.golden.make_golden import small_layer_indices
 
 from block_lut_b200.cuda_lut_gemv import lut_gemv
@@ -40,6 +40,25 @@ def test_quant_method_apply_matches_reference_golden(golden):
         f = fused_lut_moe(bf16_tensor(s[f"x{T}"]), cuda(s[f"ti{T}"]), bf16_tensor(s[f"tw{T}"]), layer.w13_weight,
                           layer.w13_absmax, layer.w2_weight, layer.w2_absmax, layer._codebook)
         assert torch.equal(f, out)
+
+
+def test_quant_method_decompress_helpers():
+    # _decompress_one / _batch_decompress (quant_method.py:281-308), bit-exact
+    from block_lut_b200.quant_method import LUTConfig, LUTFusedMoEMethod
+    method = LUTFusedMoEMethod(LUTConfig(code_type="BLOCKLUT"))
+    rng = np.random.Generator(np.random.PCG64(12))
+    E, rows, cols = 3, 64, 256
+    nb = rows * cols // 128
+    idx = rng.integers(0, 256, (E, rows, cols), dtype=np.uint8)
+    am = O.f32_to_bf16(rng.uniform(0.01, 0.1, (E, nb)).astype(np.float32))
+    tab = O.f32_to_bf16(rng.uniform(-1, 1, 256).astype(np.float32))
+    one = method._decompress_one(cuda(idx[1]), bf16_tensor(am[1]), bf16_tensor(tab))
+    assert tuple(one.shape) == (rows * cols,)
+    assert np.array_equal(to_u16(one), O.dequant_r(idx[1].reshape(-1), am[1], tab, 128))
+    every = method._batch_decompress(cuda(idx), bf16_tensor(am), bf16_tensor(tab))
+    assert tuple(every.shape) == idx.shape
+    ref = np.stack([O.dequant_r(idx[e].reshape(-1), am[e], tab, 128).reshape(rows, cols) for e in range(E)])
+    assert np.array_equal(to_u16(every), ref)
 
 
 def test_quant_method_create_weights_format_b():
