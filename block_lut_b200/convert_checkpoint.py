@@ -109,6 +109,26 @@ def is_lut_weight(name: str, dtype: torch.dtype, absmax_keys) -> bool:
     return is_routed_expert(name) and name.endswith(".weight") and dtype == torch.uint8 and name in absmax_keys
 
 
+def load_codebooks(model_path: str, code_type: str = "BLOCKLUT") -> Dict[str, torch.Tensor]:
+    """The codebook files of a checkpoint directory as bf16 tables, keyed
+    ``blocklut``, ``mapped16``, ``mapped64`` (convert_checkpoint.py:36-58).
+    BLOCKLUT needs ``blocklut_256.npy``. For NESTEDLUT a missing mapped
+    table falls back to the BlockLUT table."""
+    books: Dict[str, torch.Tensor] = {}
+    for fname, key in (("blocklut_256.npy", "blocklut"), ("nested_lut_mapped16.npy", "mapped16"),
+                       ("nested_lut_mapped64.npy", "mapped64")):
+        path = os.path.join(model_path, fname)
+        if os.path.exists(path):
+            books[key] = _load_table(path)
+    if code_type == "BLOCKLUT" and "blocklut" not in books:
+        raise FileNotFoundError(f"blocklut_256.npy not found in {model_path}")
+    if code_type == "NESTEDLUT":
+        for key in ("blocklut", "mapped16", "mapped64"):
+            if key not in books:
+                books[key] = books.get("blocklut")
+    return books
+
+
 def codebook_file(model_path: str, code_type: str) -> str:
     """The codebook the reference converter picks (convert_model.py:43-52)."""
     name = "blocklut_256.npy" if code_type == "BLOCKLUT" else "nested_lut_mapped16.npy"

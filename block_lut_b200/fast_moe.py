@@ -43,6 +43,17 @@ def r8_layer(w13_weight, w13_absmax, w2_weight, w2_absmax, codebook, top_k: int,
     return layer
 
 
+def _fused_expert_compute(x, w13_slices, w2_slices, cb, a13, a2):
+    """One expert on one token (fast_moe.py:14-27): W2 (SiLU(gate) * up) with
+    [gate; up] = W13 x. Runs as one ``blut_moe_forward`` over a single-expert
+    stack with routing weight 1; returns [hidden] in x's dtype."""
+    layer = r8_layer(w13_slices.unsqueeze(0), a13.reshape(1, -1), w2_slices.unsqueeze(0), a2.reshape(1, -1), cb, 1)
+    xt = x.reshape(1, -1)
+    ids = torch.zeros(1, 1, dtype=torch.int32, device=xt.device)
+    w = torch.ones(1, 1, dtype=torch.float32, device=xt.device)
+    return layer.forward(xt, ids, w).reshape(-1)
+
+
 def fused_lut_moe(x, topk_ids, topk_weights, w13_weight, w13_absmax, w2_weight, w2_absmax, codebook):
     """[T, H] (or [H]) activations -> [T, H] MoE output (reference-format experts)."""
     x2 = x.reshape(1, -1) if x.dim() == 1 else x

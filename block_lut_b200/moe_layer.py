@@ -6,7 +6,8 @@ router (fused logits + softmax + top-k kernel), all routed LUT experts in one
 instead of the reference's Python loop over (k, expert) masks.
 ``_routing(router_logits, top_k)`` keeps the reference's semantics
 (moe_layer.py:358-376): softmax in float32, top-k, weights cast back to the
-logits' dtype.
+logits' dtype. ``LUTMoEExpertWrapper`` (moe_layer.py:32-143) holds one
+expert's Format R weights and multiplies by them through ``LUTLinear``.
 """
 from __future__ import annotations
 
@@ -14,15 +15,107 @@ from typing import Optional, Tuple
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
-from .formats import LUTFormat, encode
+from .formats import LUTFormat, QuantizedMatrix, encode
+from .linear import LUTLinear
 from .moe import LUTExperts, LUTMoELayer, SharedExpert
+from .quantizer import LUTQuantizer, decompress_blocklut
 
 
 def _routing(router_logits: torch.Tensor, top_k: int) -> Tuple[torch.Tensor, torch.Tensor]:
     routing_weights = torch.softmax(router_logits.float(), dim=-1)
     topk_weights, topk_indices = torch.topk(routing_weights, top_k, dim=-1)
     return topk_weights.to(router_logits.dtype), topk_indices
+
+
+class LUTMoEExpertWrapper(nn.Module):
+    """One expert's Format R weights: uint8 indices, bf16 absmax and the bf16[256]
+    codebook for the fused gate/up matrix ``w13`` [2I, H] and the down matrix
+    ``w2`` [H, I] (moe_layer.py:32-143).
+
+    ``forward(x, name)`` is ``x @ W^T``. It uses the cached bf16 weights when
+    ``set_decompressed`` stored them, as the reference does for hot experts.
+    Otherwise it is a ``LUTLinear`` matmul straight from the indices. Shapes
+    without a tiled layout, and absmax blocks other than 128, are decompressed
+    on the GPU and multiplied with ``F.linear``, which is the reference's own
+    path."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int, quantizer: LUTQuantizer,
+                 device: Optional[torch.device] = None):
+        super().__init__()
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.quantizer = quantizer
+        self.device = device or torch.device("cuda")
+        for name in ("w13_indices", "w13_absmax", "w2_indices", "w2_absmax", "codebook"):
+            self.register_buffer(name, None)
+        self._w13_bf16: Optional[torch.Tensor] = None
+        self._w2_bf16: Optional[torch.Tensor] = None
+        self._linear: dict = {}
+
+    def set_weights(self, w13_weight: torch.Tensor, w2_weight: torch.Tensor, codebook: torch.Tensor) -> None:
+        """Quantise bf16 weights with the GPU encoder and keep the result."""
+        self.codebook = codebook.to(device=self.device, dtype=torch.bfloat16)
+        q13 = self.quantizer.quantize(w13_weight, codebook)
+        q2 = self.quantizer.quantize(w2_weight, codebook)
+        self.w13_indices, self.w13_absmax = q13["indices"].to(self.device), q13["absmax"].to(self.device)
+        self.w2_indices, self.w2_absmax = q2["indices"].to(self.device), q2["absmax"].to(self.device)
+        self._linear.clear()
+
+    def set_decompressed(self, w13_bf16: torch.Tensor, w2_bf16: torch.Tensor) -> None:
+        self._w13_bf16 = w13_bf16.to(self.device)
+        self._w2_bf16 = w2_bf16.to(self.device)
+
+    def has_decompressed(self) -> bool:
+        return self._w13_bf16 is not None
+
+    def clear_decompressed(self) -> None:
+        self._w13_bf16 = None
+        self._w2_bf16 = None
+
+    def _shape(self, name: str) -> Tuple[int, int]:
+        if name == "w13":
+            return 2 * self.intermediate_size, self.hidden_size
+        if name == "w2":
+            return self.hidden_size, self.intermediate_size
+        raise ValueError(f"Unknown weight name: {name}")
+
+    def get_weight(self, name: str) -> torch.Tensor:
+        """bf16 weight: the cached copy, else decompressed on the GPU."""
+        rows, cols = self._shape(name)
+        cached = self._w13_bf16 if name == "w13" else self._w2_bf16
+        if cached is not None:
+            return cached
+        idx, am = (self.w13_indices, self.w13_absmax) if name == "w13" else (self.w2_indices, self.w2_absmax)
+        return decompress_blocklut(idx, am, self.codebook, self.quantizer.block_size).reshape(rows, cols)
+
+    def _lut_linear(self, name: str) -> Optional[LUTLinear]:
+        if name not in self._linear:
+            rows, cols = self._shape(name)
+            idx, am = (self.w13_indices, self.w13_absmax) if name == "w13" else (self.w2_indices, self.w2_absmax)
+            lin = None
+            if self.quantizer.block_size == 128:
+                qm = QuantizedMatrix(LUTFormat("r8", 8, 128), rows, cols, idx.reshape(-1).contiguous(),
+                                     self.codebook.contiguous(), scales=am.reshape(-1).to(torch.bfloat16).contiguous())
+                try:
+                    lin = LUTLinear(qm)
+                except ValueError:  # no tiled layout for this shape
+                    lin = None
+            self._linear[name] = lin
+        return self._linear[name]
+
+    def forward(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        rows, cols = self._shape(name)
+        cached = self._w13_bf16 if name == "w13" else self._w2_bf16
+        lin = None if cached is not None else self._lut_linear(name)
+        if lin is None:
+            return F.linear(x, self.get_weight(name))
+        x2 = x.reshape(-1, cols).to(torch.bfloat16)
+        return lin(x2).reshape(*x.shape[:-1], rows).to(x.dtype)
+
+    def extra_repr(self) -> str:
+        return f"hidden={self.hidden_size}, intermediate={self.intermediate_size}, codebook_size=256"
 
 
 class DeepseekV2MoE_LUT(nn.Module):
@@ -51,6 +144,16 @@ class DeepseekV2MoE_LUT(nn.Module):
         self.shared_down: Optional[torch.Tensor] = None
         self.layer_id: int = 0
         self._moe: Optional[LUTMoELayer] = None
+
+    def load_codebook(self, lut_path: str) -> bool:
+        """Load the checkpoint's codebook files (moe_layer.py:229-237); True when
+        ``blocklut_256.npy`` was found. The table becomes the ``_codebook`` buffer."""
+        q = LUTQuantizer()
+        loaded = q.load(lut_path)
+        if loaded and q.lut_codebook is not None:
+            self._codebook_loaded = True
+            self.register_buffer("_codebook", q.lut_codebook.to("cuda"))
+        return loaded
 
     def lut_format(self) -> LUTFormat:
         if self.lut_config is not None and hasattr(self.lut_config, "lut_format"):

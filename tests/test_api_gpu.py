@@ -42,6 +42,50 @@ def test_quant_method_apply_matches_reference_golden(golden):
         assert torch.equal(f, out)
 
 
+def test_fused_expert_compute_one_expert(golden):
+    # fast_moe._fused_expert_compute (fast_moe.py:14-27): one expert, one token
+    from block_lut_b200.fast_moe import _fused_expert_compute
+    s, layer = _small_r8_layer(golden)
+    table, a13, a2 = s["table"], s["a13"], s["a2"]
+    w13, w2 = layer.w13_weight.cpu().numpy(), layer.w2_weight.cpu().numpy()
+    e = 3
+    x = bf16_tensor(s["x2"])[0]
+    y = _fused_expert_compute(x, layer.w13_weight[e], layer.w2_weight[e], layer._codebook, layer.w13_absmax[e],
+                              layer.w2_absmax[e])
+    assert y.dtype == torch.bfloat16 and tuple(y.shape) == (256,)
+    W13 = [O.bf16_to_f32(O.dequant_r(w13[e].reshape(-1), a13[e], table, 128)).reshape(256, 256)]
+    W2 = [O.bf16_to_f32(O.dequant_r(w2[e].reshape(-1), a2[e], table, 128)).reshape(256, 128)]
+    ref = O.moe_forward(x.float().cpu().numpy()[None], np.zeros((1, 1), dtype=np.int64),
+                        np.ones((1, 1), dtype=np.float32), W13, W2, act_dtype="bf16")
+    check_layer(y[None], ref, torch.bfloat16, "_fused_expert_compute")
+
+
+def test_expert_wrapper_on_lut_linear():
+    # moe_layer.LUTMoEExpertWrapper (moe_layer.py:32-143)
+    from block_lut_b200.moe_layer import LUTMoEExpertWrapper
+    from block_lut_b200.quantizer import LUTQuantizer
+    H, I = 256, 128
+    rng = np.random.Generator(np.random.PCG64(31))
+    w13 = O.f32_to_bf16(O.student_t_weights(rng, (2 * I, H)))
+    w2 = O.f32_to_bf16(O.student_t_weights(rng, (H, I)))
+    tab = O.f32_to_bf16(np.sort(rng.uniform(-1, 1, 256)).astype(np.float32))
+    wr = LUTMoEExpertWrapper(H, I, LUTQuantizer(block_size=128))
+    wr.set_weights(bf16_tensor(w13), bf16_tensor(w2), bf16_tensor(tab))
+    x = cuda(O.f32_to_bf16(O.rms_activations(rng, 5, H))).view(torch.bfloat16)
+    for name, w, rows, cols in (("w13", w13, 2 * I, H), ("w2", w2, H, I)):
+        idx, am = O.encode_r(w.reshape(-1), tab, 128)
+        W = O.bf16_to_f32(O.dequant_r(idx, am, tab, 128)).reshape(rows, cols)
+        assert np.array_equal(to_u16(wr.get_weight(name)), O.f32_to_bf16(W))
+        xin = x if name == "w13" else x[:, :I].contiguous()
+        y = wr(xin, name)
+        assert tuple(y.shape) == (5, rows) and wr._linear[name] is not None
+        check_layer(y, xin.double().cpu().numpy() @ W.astype(np.float64).T, torch.bfloat16, f"wrapper {name}")
+    wr.set_decompressed(wr.get_weight("w13"), wr.get_weight("w2"))
+    assert wr.has_decompressed() and tuple(wr(x, "w13").shape) == (5, 2 * I)
+    wr.clear_decompressed()
+    assert not wr.has_decompressed()
+
+
 def test_quant_method_decompress_helpers():
     # _decompress_one / _batch_decompress (quant_method.py:281-308), bit-exact
     from block_lut_b200.quant_method import LUTConfig, LUTFusedMoEMethod

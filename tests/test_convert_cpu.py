@@ -126,3 +126,31 @@ def test_absmax_file_feeds_the_loader(tmp_path):
         for e in range(E):
             assert torch.equal(lay.w13_absmax[e], torch.cat([want(expect_layer, e, "gate"), want(expect_layer, e, "up")]))
             assert torch.equal(lay.w2_absmax[e], want(expect_layer, e, "down"))
+
+
+def test_load_codebooks(tmp_path):
+    # convert_checkpoint.py:36-58: BLOCKLUT needs blocklut_256.npy; NESTEDLUT falls back to it
+    with pytest.raises(FileNotFoundError):
+        CC.load_codebooks(str(tmp_path), "BLOCKLUT")
+    np.save(tmp_path / "blocklut_256.npy", np.linspace(-1, 1, 256, dtype=np.float32))
+    books = CC.load_codebooks(str(tmp_path), "NESTEDLUT")
+    assert set(books) == {"blocklut", "mapped16", "mapped64"}
+    assert books["blocklut"].dtype == torch.bfloat16 and torch.equal(books["mapped16"], books["blocklut"])
+    m16 = np.arange(256, dtype=np.uint16) | 0x3F00       # bf16 bit patterns of numbers in [0.5, 1)
+    np.save(tmp_path / "nested_lut_mapped16.npy", m16)
+    books = CC.load_codebooks(str(tmp_path), "NESTEDLUT")
+    assert np.array_equal(books["mapped16"].view(torch.int16).numpy().view(np.uint16), m16)
+    assert set(CC.load_codebooks(str(tmp_path), "BLOCKLUT")) == {"blocklut", "mapped16"}
+
+
+def test_moe_layer_host_paths(tmp_path):
+    from types import SimpleNamespace
+    from block_lut_b200.moe_layer import DeepseekV2MoE_LUT, LUTMoEExpertWrapper
+    from block_lut_b200.quantizer import LUTQuantizer
+    cfg = SimpleNamespace(hidden_size=64, moe_intermediate_size=32, n_routed_experts=4, num_experts_per_tok=2)
+    assert DeepseekV2MoE_LUT(cfg).load_codebook(str(tmp_path)) is False   # no codebook files
+    wr = LUTMoEExpertWrapper(64, 32, LUTQuantizer())
+    assert not wr.has_decompressed() and "hidden=64" in wr.extra_repr()
+    assert wr._shape("w13") == (64, 64) and wr._shape("w2") == (64, 32)
+    with pytest.raises(ValueError):
+        wr._shape("w3")
