@@ -41,6 +41,16 @@ class LUTQuantizer:
     # ---------------------------------------------------------------- train --
     @torch.no_grad()
     def train(self, expert_weights: torch.Tensor, n_iter: int = 50) -> None:
+        """Codebook training (quantizer.py:66-117): block-normalise, then k-means.
+
+        NESTEDLUT also trains the K=64 codebook and merges it to 16.  The
+        reference's ``_train_kmeans`` stores every codebook it trains in
+        ``lut_codebook``, so after its NESTEDLUT training ``lut_codebook``
+        holds the 64 entries (quantizer.py:112-113,177); here it keeps the
+        ``lut_size`` codebook, the one ``quantize`` needs.  Both consume the
+        same random numbers, so ``nested_mapped64`` / ``nested_mapped16`` are
+        the reference's.
+        """
         flat = expert_weights.reshape(-1)
         if self.code_type == "LUT":
             self._train_kmeans(flat, self.lut_size, n_iter)
@@ -54,15 +64,23 @@ class LUTQuantizer:
         blocks = flat.view(-1, self.block_size)
         amax = blocks.abs().max(dim=1, keepdim=True).values.clamp(min=1e-10)
         data = (blocks / amax).reshape(-1)
-        self._train_kmeans(data, self.lut_size, n_iter)
+        full = self._train_kmeans(data, self.lut_size, n_iter)
         if self.code_type == "NESTEDLUT":
             c64 = self._train_kmeans(data, 64, n_iter)
             c16 = self._greedy_merge(c64.float(), 16)
             self.nested_mapped64 = self._build_mapped_table(c64.float(), 256)
             self.nested_mapped16 = self._build_mapped_table(c16, 256)
-            self._train_kmeans(data, self.lut_size, n_iter)
+            self.lut_codebook = full
 
     def _train_kmeans(self, data: torch.Tensor, k: int, n_iter: int, max_samples: int = 200000) -> torch.Tensor:
+        """1-D Lloyd k-means (quantizer.py:120-178): a random subset of at most
+        ``max_samples`` values, random initial centroids, nearest-centroid
+        assignment (first minimum), each non-empty cluster's centroid set to
+        its members' mean, centroids sorted and rounded to bf16.  Random
+        numbers are drawn in the reference's order (subset, then initial
+        centroids) and each mean is a ``Tensor.mean`` of the members in data
+        order, so a CPU run under the same ``torch.manual_seed`` reproduces
+        the reference's codebook."""
         data = data.to(self.device).float()
         if data.shape[0] > max_samples:
             data = data[torch.randperm(data.shape[0], device=data.device)[:max_samples]]
@@ -70,16 +88,25 @@ class LUTQuantizer:
         cent = data[torch.randperm(data.shape[0], device=data.device)[:n_init]].clone()
         if n_init < k:
             cent = torch.cat([cent, torch.zeros(k - n_init, device=data.device)])
+        chunk = 1 << 16  # rows of the [n, k] distance matrix held at once
         for _ in range(n_iter):
-            a = torch.abs(data[:, None] - cent[None, :]).argmin(dim=1)
-            sums = torch.zeros(k, device=data.device).index_add_(0, a, data)
-            cnt = torch.bincount(a, minlength=k).float()
-            cent = torch.where(cnt > 0, sums / cnt.clamp(min=1), cent)
+            a = torch.cat([torch.abs(data[s:s + chunk, None] - cent[None, :]).argmin(dim=1)
+                           for s in range(0, data.shape[0], chunk)])
+            order = torch.argsort(a, stable=True)       # members of each cluster, in data order
+            counts = torch.bincount(a, minlength=k).tolist()
+            members = torch.split(data[order], counts)
+            for c, m in enumerate(members):
+                if m.numel():
+                    cent[c] = m.mean()
         cent, _ = torch.sort(cent)
         self.lut_codebook = cent.to(torch.bfloat16).cpu()
         return self.lut_codebook
 
     def _greedy_merge(self, centroids: torch.Tensor, target_k: int) -> torch.Tensor:
+        """Merges centroid pairs to ``target_k`` (quantizer.py:202-221), with the
+        reference's distance matrix ``|c_i - c_j| + eye * inf``: its zero
+        entries times inf are NaN, so the argmin (which returns the first NaN)
+        always picks the pair (0, 1)."""
         c = centroids.clone()
         while c.shape[0] > target_k:
             d = torch.abs(c[None, :] - c[:, None]) + torch.eye(c.shape[0], device=c.device) * float("inf")

@@ -254,17 +254,63 @@ def additive_fixture(ref_root):
     np.savez_compressed(os.path.join(HERE, "additive.npz"), coarse=coarse, fine=fine, ic=ic, ifn=ifn, x=x)
 
 
+def train_fixture(ref_root):
+    """``train.npz``: the reference's codebook training (``vllm_lut/quantizer.py:66-236``)
+    on CPU under fixed ``torch.manual_seed`` values.
+
+    * ``LUTQuantizer("BLOCKLUT", lut_size=64).train`` (block normalisation,
+      ``_train_kmeans``) and ``LUTQuantizer("NESTEDLUT", lut_size=64).train``
+      (adds the K=64 codebook, ``_greedy_merge`` to 16, ``_build_mapped_table``),
+      both seeded with 7, on 8192 Student-t weights with a zero-padded tail block.
+    * ``_train_kmeans(data, 16, 4, max_samples=1500)`` (the random-subset path), seed 11.
+    * ``_greedy_merge`` of a fixed 24-value array to 6, and ``_build_mapped_table``
+      of 12 and 5 values to 256 (the remainder path).
+    """
+    sys.path.insert(0, ref_root)
+    import torch
+    from vllm_lut import quantizer as Q
+
+    torch.set_num_threads(1)
+    rng = np.random.Generator(np.random.PCG64(31))
+    w = (rng.standard_t(5, size=8000) * 0.02 / np.sqrt(5.0 / 3.0)).astype(np.float32)
+    out = {"w": w}
+    for name in ("BLOCKLUT", "NESTEDLUT"):
+        torch.manual_seed(7)
+        q = Q.LUTQuantizer(code_type=name, block_size=128, lut_size=64, device="cpu")
+        q.train(torch.from_numpy(w), n_iter=6)
+        out[f"{name.lower()}_codebook"] = bits(q.lut_codebook)
+        if name == "NESTEDLUT":
+            out["mapped64"] = bits(q.nested_mapped64)
+            out["mapped16"] = bits(q.nested_mapped16)
+    torch.manual_seed(11)
+    q = Q.LUTQuantizer(code_type="BLOCKLUT", device="cpu")
+    data = torch.from_numpy(rng.standard_normal(3000).astype(np.float32))
+    out["km_data"] = data.numpy()
+    out["km16"] = bits(q._train_kmeans(data, 16, 4, max_samples=1500))
+    merge_in = torch.from_numpy(np.sort(rng.standard_normal(24)).astype(np.float32))
+    out["merge_in"] = merge_in.numpy()
+    out["merge6"] = q._greedy_merge(merge_in, 6).numpy()
+    for n in (12, 5):
+        c = torch.from_numpy(np.sort(rng.standard_normal(n)).astype(np.float32))
+        out[f"map_in{n}"] = c.numpy()
+        out[f"map{n}"] = bits(q._build_mapped_table(c, 256))
+    np.savez_compressed(os.path.join(HERE, "train.npz"), **out)
+
+
 if __name__ == "__main__":
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <block_lut checkout> [convert | bitplane | additive]")
+        sys.exit("usage: make_golden.py <block_lut checkout> [convert | bitplane | additive | train]")
     if sys.argv[2:] == ["convert"]:
         convert_fixture(sys.argv[1])
     elif sys.argv[2:] == ["bitplane"]:
         bitplane_fixture(sys.argv[1])
     elif sys.argv[2:] == ["additive"]:
         additive_fixture(sys.argv[1])
+    elif sys.argv[2:] == ["train"]:
+        train_fixture(sys.argv[1])
     else:
         main(sys.argv[1])
         convert_fixture(sys.argv[1])
         bitplane_fixture(sys.argv[1])
         additive_fixture(sys.argv[1])
+        train_fixture(sys.argv[1])
