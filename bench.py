@@ -222,59 +222,102 @@ def make_inputs(n_layers, batch, rank, device, hidden=H, dtype=None):
     return xs
 
 
-def cpu_sample(threads, batch, fmt, shape=None, seed=0):
-    """Bounded CPU sample: one MoE layer of the workload through the oracle port
-    (table-gather dequant + matmul per active expert, all threads).  Returns
-    (seconds per layer, description)."""
-    from oracle import blut_oracle as O
-    sh = shape or QWEN
-    h_, e_, i_, is_, k_ = sh["H"], sh["E"], sh["I"], sh["IS"], sh["TOPK"]
-    rng = np.random.Generator(np.random.PCG64(seed))
-    group = fmt.group
+def cpu_model() -> str:
+    """The host CPU's model name (lscpu's "Model name", from /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    def tables(rows, cols, ent):
-        return np.sort(rng.standard_normal((e_, rows, cols // group, ent)).astype(np.float16) * np.float16(0.02),
-                       axis=-1)
 
-    def mats(rows, cols):
-        if fmt.kind == "r8":
-            table = O.f32_to_bf16(np.linspace(-1.0, 1.0, 256).astype(np.float32))
-            idx = rng.integers(0, 256, size=(e_, rows * cols), dtype=np.uint8)
-            am = O.f32_to_bf16(rng.uniform(0.02, 0.08, (e_, rows * cols // 128)).astype(np.float32))
-            return lambda e: O.bf16_to_f32(O.dequant_r(idx[e], am[e], table, 128, fmt.tier)).reshape(  # noqa: E731
-                rows, cols)
-        if fmt.kind == "nested":
-            cc = rng.integers(0, 256, size=(e_, rows, cols // 4), dtype=np.uint8)
-            cr = rng.integers(0, 256, size=(e_, rows, cols // 4), dtype=np.uint8)
-            ct, rt = tables(rows, cols, 4), tables(rows, cols, 16) * np.float16(0.25)
-            return lambda e: O.dequant_nested(cc[e], cr[e], ct[e], rt[e], group,  # noqa: E731
-                                              coarse_only=fmt.tier == 1).astype(np.float32)
-        codes = rng.integers(0, 256, size=(e_, rows, cols * fmt.bits // 8), dtype=np.uint8)
-        t = tables(rows, cols, 1 << fmt.bits)
-        return lambda e: O.dequant_b(codes[e], t[e], fmt.bits, group).astype(np.float32)  # noqa: E731
+class CpuLayer:
+    """Bounded CPU sample of the workload: one MoE layer at the bench batch,
+    run by the torch restatement of the reference's apply
+    (``oracle/blut_torch_ref.py``: per active expert, dequantise the whole
+    expert, F.linear over all tokens, SiLU * up, F.linear, weighted
+    scatter-add) on all host cores.  Its experts carry random codes of the
+    workload's format (Format R: uint8 indices, bf16 absmax, a bf16 table;
+    Format B / NestedLUT: packed codes and sorted fp16 tables per (row,
+    block)); dequantisation is timed, as it is part of every reference call."""
 
-    g13, g2 = mats(2 * i_, h_), mats(h_, i_)
-    x = O.rms_activations(rng, batch, h_)
-    ids, tw = O.routing(rng.standard_normal((batch, e_)).astype(np.float32), k_, renorm=sh["RENORM"])
-    if is_ > 0:
-        s13 = (rng.standard_normal((2 * is_, h_)) * 0.02).astype(np.float32)
-        s2 = (rng.standard_normal((h_, is_)) * 0.02).astype(np.float32)
-        sg = (rng.standard_normal(h_) * 0.02).astype(np.float32)
-    act = "bf16" if fmt.kind == "r8" else "f16"
-    if act == "bf16":
-        x = O.bf16_to_f32(O.f32_to_bf16(x.astype(np.float32)))
-    t0 = time.perf_counter()
-    out = O.moe_forward_threaded(x, ids, tw, g13, g2, act, threads)
-    if is_ > 0:
-        xs = x.astype(np.float64)
-        h = xs @ s13.T
-        a = O.round_to((O.silu(h[:, :is_]) * h[:, is_:]).astype(np.float32), act).astype(np.float64)
-        out += (1 / (1 + np.exp(-(xs @ sg))))[:, None] * (a @ s2.T)
-    dt = time.perf_counter() - t0
-    n_active = len(np.unique(ids))
-    return dt, f"1 of {sh['LAYERS']} MoE layers at batch {batch} ({n_active} active experts" \
-               f"{' + shared expert' if is_ > 0 else ''}), oracle port: numpy table-gather dequant + matmul, " \
-               f"{threads} threads"
+    def __init__(self, batch, fmt, shape=None, seed=0):
+        import torch
+        from oracle import blut_oracle as O
+        from oracle import blut_torch_ref as R
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.threads = torch.get_num_threads()
+        sh = shape or QWEN
+        h_, e_, i_, is_, k_ = sh["H"], sh["E"], sh["I"], sh["IS"], sh["TOPK"]
+        rng = np.random.Generator(np.random.PCG64(seed))
+        g = torch.Generator().manual_seed(seed)
+        x = O.rms_activations(rng, batch, h_).astype(np.float32)
+        ids, tw = O.routing(rng.standard_normal((batch, e_)).astype(np.float32), k_, renorm=sh["RENORM"])
+        self.active = sorted(set(ids.reshape(-1).tolist()))
+        bf16 = fmt.kind == "r8"
+        self.x = torch.from_numpy(x).to(torch.bfloat16 if bf16 else torch.float16)
+        self.ids = torch.from_numpy(ids).long()
+        self.tw = torch.from_numpy(tw).to(self.x.dtype)
+
+        def tables(rows, cols, ent):
+            t = torch.randn(rows, cols // fmt.group, ent, generator=g) * 0.02
+            return t.sort(dim=-1).values.half()
+
+        def expert(rows, cols):
+            if fmt.kind == "r8":
+                idx = torch.randint(0, 256, (rows * cols,), generator=g, dtype=torch.uint8)
+                am = (torch.rand(rows * cols // 128, generator=g) * 0.06 + 0.02).to(torch.bfloat16)
+                return lambda: R.dequant_r(idx, am, self.cb, rows, cols)  # noqa: E731
+            if fmt.kind == "nested":
+                cc = torch.randint(0, 256, (rows, cols // 4), generator=g, dtype=torch.uint8)
+                cr = torch.randint(0, 256, (rows, cols // 4), generator=g, dtype=torch.uint8)
+                ct, rt = tables(rows, cols, 4), tables(rows, cols, 16)
+                return lambda: R.dequant_nested(cc, cr, ct, rt, fmt.group, rows, cols,  # noqa: E731
+                                                coarse_only=fmt.tier == 1)
+            codes = torch.randint(0, 256, (rows, cols * fmt.bits // 8), generator=g, dtype=torch.uint8)
+            t = tables(rows, cols, 1 << fmt.bits)
+            return lambda: R.dequant_b(codes, t, fmt.bits, fmt.group, rows, cols)  # noqa: E731
+
+        self.cb = torch.linspace(-1.0, 1.0, 256).to(torch.bfloat16)
+        self.w13 = {e: expert(2 * i_, h_) for e in self.active}
+        self.w2 = {e: expert(h_, i_) for e in self.active}
+        self.shared = None
+        if is_ > 0:
+            dt = self.x.dtype if bf16 else torch.float32
+            self.shared = ((torch.randn(2 * is_, h_, generator=g) * 0.02).to(dt),
+                           (torch.randn(h_, is_, generator=g) * 0.02).to(dt),
+                           (torch.randn(h_, generator=g) * 0.02).to(dt))
+        self.desc = (f"1 of {sh['LAYERS']} MoE layers at batch {batch} ({len(self.active)} active experts"
+                     f"{' + shared expert' if is_ > 0 else ''}), torch CPU restatement of the reference's "
+                     f"LUTFusedMoEMethod.apply (quant_method.py:261-277): per active expert whole-expert "
+                     f"dequant + F.linear over all tokens, {'bf16' if bf16 else 'fp32'}; "
+                     f"{self.threads} threads, {cpu_model()}")
+
+    def run(self) -> float:
+        """Seconds for one layer forward."""
+        import torch
+        import torch.nn.functional as F
+        from oracle import blut_torch_ref as R
+        t0 = time.perf_counter()
+        out = R.apply(self.x, self.tw, self.ids, lambda e: self.w13[e](), lambda e: self.w2[e]())
+        if self.shared is not None:
+            s13, s2, sg = self.shared
+            xs = self.x.to(s13.dtype)
+            h = F.linear(xs, s13)
+            si = s13.shape[0] // 2
+            y = F.linear(F.silu(h[:, :si]) * h[:, si:], s2)
+            out = out + (torch.sigmoid(xs @ sg)[:, None] * y).to(out.dtype)
+        return time.perf_counter() - t0
+
+
+def cpu_sample(batch, fmt, shape=None, seed=0, reps=2):
+    """(seconds per layer: the faster of ``reps`` runs after one warm-up, CpuLayer)."""
+    c = CpuLayer(batch, fmt, shape, seed)
+    c.run()
+    return min(c.run() for _ in range(reps)), c
 
 
 # ------------------------------------------------------------------ ours --
@@ -395,10 +438,9 @@ def run_ours(a):
 
     cpu = None
     if not a.no_cpu:
-        threads = os.cpu_count() or 1
-        dt, desc = cpu_sample(threads, a.batch, fmt, W)
-        cpu = {"value": a.batch / (dt * a.layers), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": desc}
+        dt, c = cpu_sample(a.batch, fmt, W)
+        cpu = {"value": a.batch / (dt * a.layers), "unit": "tokens/s", "cores": c.threads, "kind": "port",
+               "sample": c.desc, "ms_per_layer": dt * 1e3}
 
     per_layer_launches = moes[0].launch_count(a.batch, caller_routing=False)
     res = {
@@ -439,29 +481,37 @@ def run_ep(a, rank, world, dev):
 
 # ------------------------------------------------------------- reference --
 def run_reference(a):
+    """The reference arm: the torch CPU restatement of the reference's apply
+    (CpuLayer) on the host cores.  A step is one MoE layer of the workload at
+    the bench batch (the bounded sample); ``ms_per_step`` is that layer's
+    time and ``value`` scales it to the whole stack (batch / (layers x
+    time)).  Timing stops after about a minute of steps, so that the run
+    ends within a few minutes whatever ``--steps`` asks for."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    times = []
-    desc = ""
     fmt = bench_format(a)
-    for i in range(a.warmup + a.steps):
-        dt, desc = cpu_sample(threads, a.batch, fmt, a.shape, seed=i % 2)
-        if i >= a.warmup:
-            times.append(dt)
-        if sum(times) > 120:  # keep the whole run within a few minutes
+    c = CpuLayer(a.batch, fmt, a.shape, seed=0)
+    for _ in range(a.warmup):
+        c.run()
+    times = []
+    for _ in range(a.steps):
+        times.append(c.run())
+        if sum(times) > 60:
             break
-    dt = statistics.median(times) if times else dt
+    dt = statistics.median(times)
     val = a.batch / (dt * a.layers)
     res = {"impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world,
-           "steps": len(times), "warmup": a.warmup, "ms_per_step": dt * a.layers * 1e3, "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-           "data": "synthetic random codes and sorted fp16 tables of the workload's shapes",
+           "steps": len(times), "steps_requested": a.steps, "warmup": a.warmup, "ms_per_step": dt * 1e3,
+           "step": f"one of the {a.layers} MoE layers (value = batch / ({a.layers} x median step time))",
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16" if fmt.kind == "r8" else "f32",
+           "data": "synthetic random codes, absmax and sorted fp16 tables of the workload's shapes",
            "config": {"workload": f"{a.shape['NAME']}, decode batch {a.batch}", "layers": a.layers,
-                      "global_batch": a.batch, "format": format_name(fmt)},
-           "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
+                      "global_batch": a.batch, "format": format_name(fmt), "cpu": cpu_model()},
+           "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": c.threads, "kind": "port",
+                            "sample": c.desc},
            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)
 
