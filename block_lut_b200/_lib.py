@@ -79,6 +79,7 @@ SIGNATURES = [
     ("blut_moe_forward_noalloc", C.c_int, [C.POINTER(MoEArgs), _VP]),
     ("blut_moe_check_status", C.c_int, [_VP, _VP]),
     ("blut_moe_launch_count", C.c_int, [C.POINTER(MoEArgs)]),
+    ("blut_debug_set_wait_limit", C.c_int, [C.c_uint64]),
 ]
 
 _lib = None

@@ -1,10 +1,17 @@
 // extern "C" entry points of libblut.so (declared in include/blut.h).
 #include "blut_common.cuh"
 #include "blut_internal.h"
+#include "blut_mm.cuh"
+
+#include <atomic>
 
 using namespace blut;
 
 static inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Process-wide limit of the bounded device waits (blut_debug_set_wait_limit).
+static std::atomic<uint64_t> g_wait_limit_ns{kWaitLimitNs};
+uint64_t blut::wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 
 extern "C" {
 
@@ -19,6 +26,11 @@ const char* blut_status_string(int status) {
     case BLUT_ERR_CUDA: return "CUDA runtime error";
     default: return "unknown status";
   }
+}
+
+int blut_debug_set_wait_limit(uint64_t ns) {
+  g_wait_limit_ns.store(ns ? ns : kWaitLimitNs, std::memory_order_relaxed);
+  return BLUT_OK;
 }
 
 int blut_dequant(const blut_mat_desc* desc, const blut_canon* src, void* out, void* stream) {
@@ -106,7 +118,8 @@ int blut_moe_forward(const blut_moe_args* args, void* workspace, size_t workspac
 }
 
 int blut_moe_check_status(void* workspace, void* stream) {
-  if (!workspace) return BLUT_ERR_INVALID;
+  // NULL: the status of blut_moe_forward_noalloc, in its scratch on the current device
+  if (!workspace && noalloc_scratch(&workspace) != BLUT_OK) return BLUT_ERR_CUDA;
   int st = 0;
   if (cudaMemcpyAsync(&st, workspace, sizeof(int), cudaMemcpyDeviceToHost, S(stream)) != cudaSuccess)
     return BLUT_ERR_CUDA;

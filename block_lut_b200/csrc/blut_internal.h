@@ -61,6 +61,11 @@ struct MoEWs {
 };
 
 int num_sms();
+// Limit of the tcgen05 kernels' bounded device-side waits, in nanoseconds
+// (2 s unless blut_debug_set_wait_limit changed it).
+uint64_t wait_limit_ns();
+// Device address of the current device's blut_moe_forward_noalloc scratch.
+int noalloc_scratch(void** out);
 // Progressive bit-plane storage of Format R indices (blut_bitplane.cu).
 int64_t bitplane_bytes(int64_t n, int tier);
 int bitplane_pack(void* planes, const void* idx, int64_t n, cudaStream_t stream);

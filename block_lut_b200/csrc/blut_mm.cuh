@@ -79,17 +79,22 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Bounded wait that also gives up as soon as another warp aborted.
+// Bounded wait that also gives up as soon as another warp aborted, or after
+// `limit_ns` of wall time.  With the default limit each poll may sleep up to
+// kWaitSleepNs and the clock is read every 16 polls; a limit shorter than one
+// sleep (a test forcing the abort path) polls without sleeping and reads the
+// clock every time, so such a wait gives up as soon as its first poll fails.
 __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                              int* status) {
+                                              int* status, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   if (*abort_flag) return false;
+  const bool short_limit = limit_ns < kWaitSleepNs;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1; i < (1u << 31); ++i) {
-    if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
-    if ((i & 15) == 0) {
+    if (short_limit ? mbar_try_wait(bar, parity) : mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
+    if (short_limit || (i & 15) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      if (globaltimer_ns() - t0 > limit_ns) break;
     }
   }
   *abort_flag = 1;

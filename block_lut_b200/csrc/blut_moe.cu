@@ -844,6 +844,20 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   // gate/up and down passes run on a side stream beside the routed passes
   // (when one is available, see side_stream); the combine waits for both.
   SideStream* side = sh ? side_stream(stream) : nullptr;
+  // Once the side stream is forked, every return joins it back into `stream`
+  // (recording the join event first if the shared passes stopped early), so
+  // an error never leaves a capture with an unjoined fork or side-stream
+  // kernels unordered with the caller's next use of the workspace.
+  struct JoinGuard {
+    SideStream* side = nullptr;
+    cudaStream_t stream = nullptr;
+    bool recorded = false;
+    ~JoinGuard() {
+      if (!side) return;
+      if (!recorded) cudaEventRecord(side->join, side->s);
+      cudaStreamWaitEvent(stream, side->join, 0);
+    }
+  } join_guard;
   auto shared_passes = [&]() -> int {
     int r;
     if ((r = pass(a.s13, a.s13_tiled, 0, shared, est_sgroups, ws.xfs, ws.afs, a.shared_inter, nullptr, 2,
@@ -856,11 +870,14 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
     return stage_done("shared down", cur);
   };
   if (side) {
-    if (cudaEventRecord(side->fork, stream) != cudaSuccess || cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess)
-      return BLUT_ERR_CUDA;
+    if (cudaEventRecord(side->fork, stream) != cudaSuccess) return BLUT_ERR_CUDA;
+    if (cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess) return BLUT_ERR_CUDA;
+    join_guard.side = side;
+    join_guard.stream = stream;
     cur = side->s;
     if ((rc = shared_passes()) != BLUT_OK) return rc;
     if (cudaEventRecord(side->join, side->s) != cudaSuccess) return BLUT_ERR_CUDA;
+    join_guard.recorded = true;
     cur = stream;
   }
   // 5. routed gate/up + SiLU*up, then down
@@ -877,6 +894,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   if ((rc = stage_done("routed down", stream)) != BLUT_OK) return rc;
   if (ev && cudaEventRecord(ev[3], stream) != cudaSuccess) return BLUT_ERR_INVALID;
   if (side) {
+    join_guard.side = nullptr;  // joined here, with the error checked
     if (cudaStreamWaitEvent(stream, side->join, 0) != cudaSuccess) return BLUT_ERR_CUDA;
   } else if (sh) {
     if ((rc = shared_passes()) != BLUT_OK) return rc;

@@ -5,10 +5,12 @@
 // must not call cudaMalloc because of its implicit device synchronisation.
 //
 // The scratch the forward needs lives in one file-scope device array of
-// kNoAllocScratchBytes (16 MiB).  Every GPU that loads libblut reserves that
-// array until the process exits.  The launches are exactly those of
+// kNoAllocScratchBytes (16 MiB).  Each GPU holds that array from the
+// library's first use there (from load time with eager module loading)
+// until the process exits.  The launches are exactly those of
 // blut_moe_forward; only the scratch comes from the array instead of a
-// caller workspace.
+// caller workspace.  The array's first word is the device status word, which
+// blut_moe_check_status(NULL, stream) reads back.
 #include <mutex>
 
 #include "blut_common.cuh"
@@ -42,6 +44,12 @@ int scratch_for_current_device(void** out) {
 }
 
 }  // namespace
+
+namespace blut {
+// Address of the current device's no-allocation scratch (its first word is
+// the device status of the last blut_moe_forward_noalloc call there).
+int noalloc_scratch(void** out) { return scratch_for_current_device(out); }
+}  // namespace blut
 
 extern "C" {
 

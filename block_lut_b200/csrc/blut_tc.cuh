@@ -31,6 +31,7 @@
 
 #include <type_traits>
 
+#include "blut_internal.h"
 #include "blut_mm.cuh"
 
 namespace blut {
@@ -122,6 +123,7 @@ struct TcParams {
   int* status;
   int stages;              // weight stages (LUT formats) or weight + activation stages (dense)
   int xstages;             // activation stages (LUT formats)
+  uint64_t wait_ns;        // limit of every bounded wait (wait_limit_ns())
 };
 
 // Activations for the tcgen05 matmuls: blocks of kb columns (the consumer's
@@ -193,16 +195,6 @@ __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16])
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
       "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]));
 }
-// Waits for this thread's tcgen05.st; `v` (the registers of the store in
-// flight) is tied to the wait so the compiler keeps them unchanged until then.
-__device__ __forceinline__ void tc_wait_st_keep(uint32_t (&v)[16]) {
-  asm volatile("tcgen05.wait::st.sync.aligned;"
-               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
-                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
-               :
-               : "memory");
-}
-
 // 16 consecutive 32-bit columns, then the wait; the registers are tied to the
 // wait so that no use is scheduled before it.
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
@@ -591,6 +583,41 @@ __host__ inline int tc_smem_bytes(const TcParams& p) {
          p.xstages * tc_xstage_bytes<Dec, MT>();
 }
 
+// A work item as the producer posts it to the shared-memory queue: the item
+// number (-1: no more work) and its decomposition, resolved once per CTA
+// (divisions and the group table's global loads) instead of by every role.
+struct TcItem {
+  int item;    // global item index, or -1
+  int u;       // unit: tiles 2u and 2u + 1 of the matrix
+  int b0, b1;  // column blocks [b0, b1) of the item's K slice
+  int slice;   // K slice index (item % ks)
+  int ntok;    // tokens of the group
+  int nt0;     // first n-tile of the group in the activations
+  int slot0;   // first output slot of the group
+};
+constexpr int kTcQInfo = 800;  // byte offset of the TcItem queue in the header (the barriers end at 784)
+static_assert(kTcQInfo + kTcQueue * (int)sizeof(TcItem) <= kTcHeader, "item queue exceeds the header");
+
+// Bounded wait by a whole warp: every lane polls and the warp leaves on a
+// vote, so the branch is warp-uniform and no lane's result needs to be
+// broadcast.  The slow path (sleeping polls, the time limit, the abort flag)
+// only runs when the first poll finds the phase incomplete.
+__device__ __forceinline__ bool tc_warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                             uint64_t limit_ns) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort_flag, status, limit_ns));
+}
+// Arrive once on behalf of the warp: lane 0's arrive is predicated, not a
+// divergent branch.  The caller has synchronised the warp first.
+__device__ __forceinline__ void tc_arrive_lane0(uint32_t bar, int lane) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.eq.u32 p, %1, 0;\n\t"
+      "@p mbarrier.arrive.shared::cta.b64 _, [%0];\n\t}" ::"r"(bar),
+      "r"(lane)
+      : "memory");
+}
+
 template <class Dec, int MT>
 __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_kernel(const TcParams p) {
   constexpr bool kDense = Dec::kDense;
@@ -614,9 +641,9 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
   uint64_t* fin = full + 60;                           // last MMAs complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 61);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 62);
-  volatile int* qitem = reinterpret_cast<volatile int*>(full + 63);  // [kTcQueue]
   uint64_t* xfull = full + 66;                         // [kTcMaxStages] activation stage loaded (LUT formats)
   uint64_t* xempty = full + 82;                        // [kTcMaxStages] activation stage read (MMA commit)
+  TcItem* qinfo = reinterpret_cast<TcItem*>(smem + kTcQInfo);      // [kTcQueue] posted items
   uint32_t* r8tab = reinterpret_cast<uint32_t*>(smem + kTcHeader);  // barriers end at full + 98 (784 bytes)
   uint8_t* ring = smem + kTcHeader + tc_table_bytes<Dec>();
   const int S = p.stages, SX = p.xstages;
@@ -626,6 +653,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
   const int boff = 2 * p.tile_bytes;  // activations inside a dense stage
   // planes inside a stage: each holds the pieces of the unit's two tiles
   const int qoff[3] = {0, 2 * p.piece[0], 2 * (p.piece[0] + p.piece[1])};
+  const uint64_t wlim = p.wait_ns;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -664,32 +692,44 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_items = *p.gt.n_groups * p.units * p.ks;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
+      const int n_items = *p.gt.n_groups * p.units * p.ks;
       TcRing r, rx, rq;
       uint32_t issued = 0, lastph = 0;    // per weight stage: issued at least once, parity of the last issue
       uint32_t xissued = 0, xlastph = 0;  // the same per activation stage
       for (;; rq.next(kTcQueue)) {
         const int qs = rq.i;
-        if (rq.wrapped && !wait_or_abort(smem_u32(qempty + qs), rq.ph ^ 1u, abort_flag, p.status)) break;
+        if (rq.wrapped && !wait_or_abort(smem_u32(qempty + qs), rq.ph ^ 1u, abort_flag, p.status, wlim)) break;
         int item = atomicAdd(p.counter, 1);
         if (item >= n_items || *abort_flag) item = -1;
-        qitem[qs] = item;
-        mbar_arrive(smem_u32(qfull + qs));
+        TcItem it{};
+        it.item = item;
+        int expert = 0;
+        if (item >= 0) {
+          const int ku = item / p.ks;
+          const int gi = ku / p.units;
+          it.slice = item - ku * p.ks;
+          it.u = ku - gi * p.units;
+          it.b0 = it.slice * p.bps;
+          it.b1 = min(p.nblocks, it.b0 + p.bps);
+          it.ntok = p.gt.ntok[gi];
+          it.nt0 = p.gt.nt0[gi];
+          it.slot0 = p.gt.slot0[gi];
+          expert = p.gt.expert[gi];
+        }
+        qinfo[qs] = it;
+        mbar_arrive(smem_u32(qfull + qs));  // release: the posted item is visible to the roles that wait on it
         if (item < 0) break;
-        const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
-        const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
-        const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
-        const int nt0 = p.gt.nt0[gi];
-        const int ntl = min(2, p.ntiles - 2 * u);
-        const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
+        const int nnt = (it.ntok + kNTile - 1) / kNTile;
+        const int ntl = min(2, p.ntiles - 2 * it.u);
+        const uint8_t* base = p.w + (int64_t)expert * p.wstride;
         bool ok = true;
-        for (int b = b0; b < b1; ++b, r.next(S)) {
+        for (int b = it.b0; b < it.b1; ++b, r.next(S)) {
           const int s = r.i;
-          if (r.wrapped && !wait_or_abort(smem_u32(empty + s), r.ph ^ 1u, abort_flag, p.status)) {
+          if (r.wrapped && !wait_or_abort(smem_u32(empty + s), r.ph ^ 1u, abort_flag, p.status, wlim)) {
             ok = false;
             break;
           }
@@ -698,7 +738,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
           uint8_t* dst = ring + (int64_t)s * stage_bytes;
           uint32_t bar = smem_u32(full + s);
           mbar_expect_tx(bar, (uint32_t)(ntl * p.tile_bytes + (kDense ? nnt * KB * 16 : 0)));
-          const int64_t pt = (int64_t)b * p.ntiles + 2 * u;
+          const int64_t pt = (int64_t)b * p.ntiles + 2 * it.u;
 #pragma unroll
           for (int k = 0; k < Dec::kNumPlanes; ++k)
             bulk_g2s(smem_u32(dst + qoff[k]), base + p.plane_off[k] + pt * p.piece[k], (uint32_t)(ntl * p.piece[k]),
@@ -706,7 +746,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
           uint8_t* xdst = dst + boff;
           if constexpr (!kDense) {
             const int sx = rx.i;
-            if (rx.wrapped && !wait_or_abort(smem_u32(xempty + sx), rx.ph ^ 1u, abort_flag, p.status)) {
+            if (rx.wrapped && !wait_or_abort(smem_u32(xempty + sx), rx.ph ^ 1u, abort_flag, p.status, wlim)) {
               ok = false;
               break;
             }
@@ -717,7 +757,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
             mbar_expect_tx(bar, (uint32_t)(nnt * KB * 16));
             rx.next(SX);
           }
-          bulk_g2s(smem_u32(xdst), p.bin + ((int64_t)b * p.ntstride + nt0) * (KB * 16), (uint32_t)(nnt * KB * 16),
+          bulk_g2s(smem_u32(xdst), p.bin + ((int64_t)b * p.ntstride + it.nt0) * (KB * 16), (uint32_t)(nnt * KB * 16),
                    bar);
         }
         if (!ok) break;
@@ -737,24 +777,22 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
       TcRing r, ra, rd, rq;
       for (;; rq.next(kTcQueue)) {
         const int qs = rq.i;
-        if (!wait_or_abort(smem_u32(qfull + qs), rq.ph, abort_flag, p.status)) break;
-        const int item = qitem[qs];
+        if (!wait_or_abort(smem_u32(qfull + qs), rq.ph, abort_flag, p.status, wlim)) break;
+        const TcItem it = qinfo[qs];
         mbar_arrive(smem_u32(qempty + qs));
-        if (item < 0) break;
-        const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
-        const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
-        const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
-        const int ntl = min(2, p.ntiles - 2 * u);
+        if (it.item < 0) break;
+        const int nnt = (it.ntok + kNTile - 1) / kNTile;
+        const int ntl = min(2, p.ntiles - 2 * it.u);
         const uint32_t idesc = tc_idesc(Dec::kBF16, min(MT, (nnt + 1) / 2 * 16));
         const int db = rd.i;
-        if (rd.wrapped && !wait_or_abort(smem_u32(dempty + db), rd.ph ^ 1u, abort_flag, p.status)) break;
+        if (rd.wrapped && !wait_or_abort(smem_u32(dempty + db), rd.ph ^ 1u, abort_flag, p.status, wlim)) break;
         tc_fence_after();
         const uint32_t dcol = tmem + db * kDCols;
         bool ok = true;
         // dense: r walks the combined stages; LUT formats: r walks the activation stages
-        for (int b = b0; b < b1 && ok; ++b, r.next(kDense ? S : SX)) {
+        for (int b = it.b0; b < it.b1 && ok; ++b, r.next(kDense ? S : SX)) {
           const int s = r.i;
-          if (!wait_or_abort(smem_u32((kDense ? full : xfull) + s), r.ph, abort_flag, p.status)) {
+          if (!wait_or_abort(smem_u32((kDense ? full : xfull) + s), r.ph, abort_flag, p.status, wlim)) {
             ok = false;
             break;
           }
@@ -766,14 +804,14 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
               const uint64_t bd = tc_desc(st + boff + sl * 256, 128, KB * 16);
               for (int t = 0; t < ntl; ++t) {
                 const uint64_t ad = tc_desc(st + t * p.piece[0] + sl * 2 * 2048, 2048, 128);
-                tc_mma_ss(dcol + t * MT, ad, bd, idesc, ((b - b0) | sl) != 0);
+                tc_mma_ss(dcol + t * MT, ad, bd, idesc, ((b - it.b0) | sl) != 0);
               }
             }
           } else {
 #pragma unroll
             for (int h = 0; h < Dec::kHalves; ++h, ra.next(kTcASlots)) {
               const int j = ra.i;
-              if (!wait_or_abort(smem_u32(afull + j), ra.ph, abort_flag, p.status)) {
+              if (!wait_or_abort(smem_u32(afull + j), ra.ph, abort_flag, p.status, wlim)) {
                 ok = false;
                 break;
               }
@@ -783,7 +821,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
                 const uint64_t bd = tc_desc(st + (h * 4 + sl) * 256, 128, KB * 16);
                 for (int t = 0; t < ntl; ++t)
                   tc_mma_ts(dcol + t * MT, tmem + kACol0 + j * 64 + t * 32 + sl * 8, bd, idesc,
-                            ((b - b0) | h | sl) != 0);
+                            ((b - it.b0) | h | sl) != 0);
               }
               tc_commit(smem_u32(aempty + j));
             }
@@ -801,49 +839,49 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
     __syncwarp();
   } else {
     // ------------------------------------------------- decode and epilogue --
+    // Every wait here is a warp-uniform vote and every arrive a predicated
+    // lane-0 instruction, so the loop has no divergent branches.
     const int dw = warp - 2;
     const int set = dw / kTcDecodeWarps;      // decode set: takes blocks b0 + set, b0 + set + kSets, ...
     const int t = (dw % kTcDecodeWarps) >> 2;  // tile of the unit
     const int q = warp & 3;            // tensor-memory lane quarter this warp may access
     const int row = 32 * q + lane;     // row inside the 128-row tile
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    const uint32_t abase = tmem + lane_base + kACol0 + t * 32;  // this tile's columns of A slot 0
+    const int toff[3] = {qoff[0] + t * p.piece[0], qoff[1] + t * p.piece[1], qoff[2] + t * p.piece[2]};
+    const uint32_t tab = smem_u32(r8tab) + lane * 4;
     TcRing r, ra, rd, rq;
     for (;; rq.next(kTcQueue)) {
       const int qs = rq.i;
-      bool ok = wait_or_abort(smem_u32(qfull + qs), rq.ph, abort_flag, p.status);
-      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
-      const int item = qitem[qs];
+      if (!tc_warp_wait(smem_u32(qfull + qs), rq.ph, abort_flag, p.status, wlim)) break;
+      const TcItem it = qinfo[qs];
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(qempty + qs));
-      if (item < 0) break;
-      const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
-      const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
-      const int ntok = p.gt.ntok[gi];
-      const int ntl = min(2, p.ntiles - 2 * u);
+      tc_arrive_lane0(smem_u32(qempty + qs), lane);
+      if (it.item < 0) break;
+      const int ntl = min(2, p.ntiles - 2 * it.u);
       if constexpr (!kDense) {
-        const bool active = t < ntl;
+        const bool active = t < ntl;  // warp-uniform: the unit's second tile may not exist
         bool aborted = false;
         // A half is decoded as two quarters (qa, qb): the store of the first
         // runs while the second is decoded.
-        for (int b = b0; b < b1 && !aborted; ++b, r.next(S)) {
-          if (kSets > 1 && (b - b0) % kSets != set) {  // the other decode set's block
+        for (int b = it.b0; b < it.b1; ++b, r.next(S)) {
+          if (kSets > 1 && (b - it.b0) % kSets != set) {  // the other decode set's block
 #pragma unroll
             for (int h = 0; h < Dec::kHalves; ++h) ra.next(kTcASlots);
             continue;
           }
           const int s = r.i;
-          ok = wait_or_abort(smem_u32(full + s), r.ph, abort_flag, p.status);
-          if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
+          if (!tc_warp_wait(smem_u32(full + s), r.ph, abort_flag, p.status, wlim)) {
             aborted = true;
             break;
           }
-          const uint8_t* st = ring + (int64_t)s * stage_bytes;
+          const uint8_t* st = ring + s * stage_bytes;
           TcPtrs pp;
 #pragma unroll
-          for (int k = 0; k < 3; ++k) pp.p[k] = st + qoff[k] + t * p.piece[k];
-          pp.tab = smem_u32(r8tab) + lane * 4;
+          for (int k = 0; k < 3; ++k) pp.p[k] = st + toff[k];
+          pp.tab = tab;
 #pragma unroll
-          for (int h = 0; h < Dec::kHalves; ++h, ra.next(kTcASlots)) {
+          for (int h = 0; h < Dec::kHalves; ++h) {
             const int j = ra.i;
             uint32_t qa[16], qb[16];
             typename Dec::Half hd;
@@ -851,46 +889,43 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
               Dec::load_half(pp, row, h, hd);
               Dec::lookup_q(hd, 0, qa, p.mul);
             }
-            if (ra.wrapped) {
-              ok = wait_or_abort(smem_u32(aempty + j), ra.ph ^ 1u, abort_flag, p.status);
-              if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
-                aborted = true;
-                break;
-              }
+            if (ra.wrapped && !tc_warp_wait(smem_u32(aempty + j), ra.ph ^ 1u, abort_flag, p.status, wlim)) {
+              aborted = true;
+              break;
             }
             tc_fence_after();
-            const uint32_t aslot = tmem + lane_base + kACol0 + j * 64 + t * 32;
+            const uint32_t aslot = abase + j * 64;
             if (active) {
               tc_st16(aslot, qa);  // the first quarter's store overlaps the second's lookups
               Dec::lookup_q(hd, 1, qb, p.mul);
               tc_st16(aslot + 16, qb);
-              tc_wait_st_keep(qa);
-              tc_wait_st_keep(qb);
             }
             if (h == Dec::kHalves - 1) {  // this stage's shared memory is no longer read
               __syncwarp();
-              if (lane == 0) mbar_arrive(smem_u32(empty + s));
+              tc_arrive_lane0(smem_u32(empty + s), lane);
             }
+            if (active) tc_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(afull + j));
+            tc_arrive_lane0(smem_u32(afull + j), lane);
+            ra.next(kTcASlots);
           }
+          if (aborted) break;
         }
         if (aborted) break;
       }
       // epilogue
       const int db = rd.i;
-      ok = wait_or_abort(smem_u32(dfull + db), rd.ph, abort_flag, p.status);
-      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+      if (!tc_warp_wait(smem_u32(dfull + db), rd.ph, abort_flag, p.status, wlim)) break;
       tc_fence_after();
       const uint32_t dcol = tmem + lane_base + db * kDCols;
+      const int ntok = it.ntok;
       if (p.pair) {
         // chunks of 16 tokens of unit row `row`, chunk c to the warp pair
         // (set, t) with c % (2 kSets) == 2 set + t; gate tile at columns
         // 0 .. MT-1, up tile at MT .. 2MT-1
-        const int col = u * kTcRows + row;  // K index of the down projection
-        const int nt0 = p.gt.nt0[gi];
-        uint8_t* dst = p.act_out + tc_bact_off((int64_t)nt0 * kNTile, col, p.out_kb, p.ntstride);
+        const int col = it.u * kTcRows + row;  // K index of the down projection
+        uint8_t* dst = p.act_out + tc_bact_off((int64_t)it.nt0 * kNTile, col, p.out_kb, p.ntstride);
 #pragma unroll 1
         for (int c = 2 * set + t; c < MT / 16; c += 2 * kSets) {
           const int tok0 = 16 * c;
@@ -904,7 +939,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
             // partial sums of this slice (MT = 32); splitk_silu_kernel adds
             // the slices up after this launch (a kernel boundary orders them
             // without fences)
-            float* mine = p.part + (int64_t)item * (2 * kTcRows * 32) + row * 32 + tok0;
+            float* mine = p.part + (int64_t)it.item * (2 * kTcRows * 32) + row * 32 + tok0;
 #pragma unroll
             for (int n = 0; n < 16; n += 4) {
               *reinterpret_cast<float4*>(mine + n) =
@@ -926,30 +961,25 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
             }
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(dempty + db));
-      } else {
+      } else if (t < ntl) {
         // tile t of the unit, chunks of 16 tokens c with c % kSets == set
-        if (t < ntl) {
-          const int hrow = (2 * u + t) * kTcRows + row;
-          float* y = p.y_out + (item % p.ks) * p.y_sstride + (int64_t)p.gt.slot0[gi] * p.y_ld + hrow;
+        const int hrow = (2 * it.u + t) * kTcRows + row;
+        float* y = p.y_out + it.slice * p.y_sstride + (int64_t)it.slot0 * p.y_ld + hrow;
 #pragma unroll 1
-          for (int c = set; c < MT / 16; c += kSets) {
-            const int tok0 = 16 * c;
-            if (tok0 >= ntok) break;  // warp-uniform
-            uint32_t v[16];
-            tc_ld16(dcol + t * MT + tok0, v);
-            tc_wait_ld16(v);
+        for (int c = set; c < MT / 16; c += kSets) {
+          const int tok0 = 16 * c;
+          if (tok0 >= ntok) break;  // warp-uniform
+          uint32_t v[16];
+          tc_ld16(dcol + t * MT + tok0, v);
+          tc_wait_ld16(v);
 #pragma unroll
-            for (int n = 0; n < 16; ++n)
-              if (tok0 + n < ntok) y[(int64_t)(tok0 + n) * p.y_ld] = __uint_as_float(v[n]);
-          }
+          for (int n = 0; n < 16; ++n)
+            if (tok0 + n < ntok) y[(int64_t)(tok0 + n) * p.y_ld] = __uint_as_float(v[n]);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(dempty + db));
       }
+      tc_fence_before();
+      __syncwarp();
+      tc_arrive_lane0(smem_u32(dempty + db), lane);
       rd.next(kDBufs);
     }
   }
@@ -975,6 +1005,7 @@ inline cudaError_t launch_tc(TcParams p, int num_sms, cudaStream_t stream) {
   // shallow activation ring would starve the loads.
   const int depth = std::min(kTcMaxStages, budget / (stage + xstage));
   p.stages = std::max(2, depth);
+  if (p.wait_ns == 0) p.wait_ns = wait_limit_ns();
   p.xstages = xstage ? p.stages : 0;
   const int smem = tc_smem_bytes<Dec, MT>(p);
   auto kern = tc_mm_kernel<Dec, MT>;

@@ -7,6 +7,7 @@ caller-owned workspace, so it can be captured in a CUDA graph.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 import threading
 from dataclasses import dataclass
@@ -86,18 +87,24 @@ class SharedExpert:
 
 _WS: dict = {}
 _WS_LOCK = threading.Lock()
+_nullctx = contextlib.nullcontext
 
 
-def workspace(device: torch.device, nbytes: int, slot: int = 0) -> torch.Tensor:
+def workspace(device: torch.device, nbytes: int, slot: int = 0, stream=None) -> torch.Tensor:
     """Grow-only workspace per (device, slot).  Layers whose calls run in one
     stream's order share a slot; a layer that runs concurrently with others
     on another stream takes a slot of its own (``LUTMoELayer.ws_slot``): the
     lock only keeps the table consistent across host threads, it does not
-    order their kernels."""
+    order their kernels.  ``stream``: the stream the caller launches on, when
+    it is not torch's current one; a buffer outgrown there is marked as used
+    by that stream, so the caching allocator does not hand its memory out
+    while the stream's kernels may still read it."""
     key = (device.type, device.index, slot)
     with _WS_LOCK:
         buf = _WS.get(key)
         if buf is None or buf.numel() < nbytes:
+            if buf is not None and stream is not None:
+                buf.record_stream(stream)
             buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
             _WS[key] = buf
     return buf
@@ -122,6 +129,7 @@ class LUTMoELayer:
         self.shared_gate_mode = int(shared_gate_mode)
         self.dtype = experts.fmt.compute_dtype
         self._args = self._make_args()
+        self._ws_need = {}  # workspace bytes per token count (they depend on nothing else that changes)
 
     def _make_args(self) -> _lib.MoEArgs:
         ex = self.experts
@@ -167,22 +175,15 @@ class LUTMoELayer:
         if out_f32:
             return self._forward_f32(x, topk_ids, topk_weights, out, stream)
         in_dtype = x.dtype
-        x2, keep = self._prepare(x, topk_ids, topk_weights)
+        x2, a, keep = self._prepare(x, topk_ids, topk_weights)
         T = x2.shape[0]
-        a = self._args
         if out is None or out.dtype != self.dtype:
-            res = torch.empty(T, x2.shape[1], dtype=self.dtype, device=x2.device)
+            with torch.cuda.stream(stream) if stream is not None else _nullctx():
+                res = torch.empty(T, x2.shape[1], dtype=self.dtype, device=x2.device)
         else:
             res = out.reshape(T, -1)
         a.out = res.data_ptr()
-        lib = _lib.lib()
-        need = lib.blut_moe_workspace_size(C.byref(a))
-        if need == 0:
-            raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
-        ws = workspace(x2.device, need, self.ws_slot)
-        with _lib.on_device(x2):
-            _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
-                       "moe_forward")
+        self._launch(a, x2, stream)
         if out is not None and res.data_ptr() != out.data_ptr():
             out.copy_(res.reshape(out.shape))
             return out
@@ -191,13 +192,31 @@ class LUTMoELayer:
 
     __call__ = forward
 
+    def _launch(self, a: _lib.MoEArgs, x2: torch.Tensor, stream) -> None:
+        """blut_moe_forward with this call's arguments ``a`` on the layer's workspace."""
+        lib = _lib.lib()
+        T = int(a.num_tokens)
+        need = self._ws_need.get(T)
+        if need is None:
+            need = lib.blut_moe_workspace_size(C.byref(a))
+            if need == 0:
+                raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
+            self._ws_need[T] = need
+        ws = workspace(x2.device, need, self.ws_slot, stream)
+        with _lib.on_device(x2):
+            _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
+                       "moe_forward")
+
     def _prepare(self, x, topk_ids, topk_weights):
+        """Input rows, a per-call copy of the layer's argument block (so calls
+        from several host threads never share one), and the tensors it points
+        to (kept alive until the launch)."""
         x2 = x.reshape(-1, x.shape[-1])
         if x2.dtype != self.dtype:
             x2 = x2.to(self.dtype)
         x2 = x2.contiguous()
         T = x2.shape[0]
-        a = self._args
+        a = _lib.MoEArgs.from_buffer_copy(self._args)
         a.num_tokens = T
         a.x = x2.data_ptr()
         keep = [x2]
@@ -212,28 +231,20 @@ class LUTMoELayer:
             if self.router_w is None:
                 raise ValueError("no routing given and the layer has no router weights")
             a.topk_ids = a.topk_weights = None
-        return x2, keep
+        return x2, a, keep
 
     def _forward_f32(self, x, topk_ids, topk_weights, out, stream):
-        x2, keep = self._prepare(x, topk_ids, topk_weights)
-        a = self._args
-        res = out if out is not None else torch.empty(x2.shape[0], x2.shape[1], dtype=torch.float32,
-                                                      device=x2.device)
+        x2, a, keep = self._prepare(x, topk_ids, topk_weights)
+        if out is None:
+            with torch.cuda.stream(stream) if stream is not None else _nullctx():
+                res = torch.empty(x2.shape[0], x2.shape[1], dtype=torch.float32, device=x2.device)
+        else:
+            res = out
         if res.dtype != torch.float32 or not res.is_contiguous():
             raise ValueError("out_f32 needs a contiguous float32 output")
         a.out = res.data_ptr()
         a.out_f32 = 1
-        try:
-            lib = _lib.lib()
-            need = lib.blut_moe_workspace_size(C.byref(a))
-            if need == 0:
-                raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
-            ws = workspace(x2.device, need, self.ws_slot)
-            with _lib.on_device(x2):
-                _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
-                           "moe_forward")
-        finally:
-            a.out_f32 = 0
+        self._launch(a, x2, stream)
         return res
 
     def check_status(self, stream=None) -> None:

@@ -314,25 +314,38 @@ BLUT_API int blut_moe_forward(const blut_moe_args* args, void* workspace, size_t
  * allocate device memory when they call (a plugin that a host framework hands
  * only its input and output pointers, a serving loop that must not call
  * cudaMalloc).  No counterpart in the reference.  The scratch is one
- * library-owned device array of 16 MiB per GPU, reserved from the moment the
- * library is loaded until the process exits; layers whose
- * blut_moe_workspace_size exceeds 16 MiB are rejected with
- * BLUT_ERR_WORKSPACE before anything is launched.  The first call on a
- * device looks the array's device address up (make it before any stream
- * capture).  Nothing is allocated and nothing synchronised.  All calls on a
- * GPU share the array, so calls that can overlap on that GPU (different
- * streams without ordering between them) race and must be serialised by the
- * caller. */
+ * library-owned device array of 16 MiB per GPU, held on each GPU from the
+ * library's first use there (from load time with eager module loading)
+ * until the process exits; layers whose blut_moe_workspace_size exceeds
+ * 16 MiB are rejected with BLUT_ERR_WORKSPACE before anything is launched.
+ * The first call on a device looks the array's device address up (make it
+ * before any stream capture).  Nothing is allocated and nothing
+ * synchronised.  All calls on a GPU share the array, so calls that can
+ * overlap on that GPU (different streams without ordering between them) race
+ * and must be serialised by the caller.  The device status of the last call
+ * (a bounded wait that timed out, an expert id out of range) is read with
+ * blut_moe_check_status(NULL, stream). */
 BLUT_API int blut_moe_forward_noalloc(const blut_moe_args* args, void* stream);
 
 /* Read (and clear) the device-side status word of a workspace last used by
- * blut_moe_forward on `stream`: synchronises the stream, returns BLUT_OK or
- * BLUT_ERR_TIMEOUT when a kernel's bounded wait gave up.  Diagnostic only. */
+ * blut_moe_forward on `stream` (workspace NULL: the current device's
+ * blut_moe_forward_noalloc scratch): synchronises the stream, returns
+ * BLUT_OK, BLUT_ERR_TIMEOUT when a kernel's bounded wait gave up, or
+ * BLUT_ERR_INVALID when a caller-supplied expert id was out of range.
+ * Diagnostic only. */
 BLUT_API int blut_moe_check_status(void* workspace, void* stream);
 
 /* Number of this library's kernel launches one blut_moe_forward issues for
  * these arguments (used to report launch counts). */
 BLUT_API int blut_moe_launch_count(const blut_moe_args* args);
+
+/* Diagnostic, no counterpart in the reference: sets the limit, in
+ * nanoseconds, of every bounded device-side wait in the tcgen05 kernels
+ * launched after this call (0 restores the default of 2 s).  A wait that
+ * runs out aborts its kernel cleanly and the next blut_moe_check_status
+ * returns BLUT_ERR_TIMEOUT; tests use a tiny limit to exercise that path.
+ * Process-wide; not for use while other threads launch. */
+BLUT_API int blut_debug_set_wait_limit(uint64_t ns);
 
 #ifdef __cplusplus
 }
