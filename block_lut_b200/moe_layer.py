@@ -119,16 +119,40 @@ class LUTMoEExpertWrapper(nn.Module):
 
 
 class DeepseekV2MoE_LUT(nn.Module):
-    """LUT-quantised MoE block (routed experts LUT, shared experts dense).
+    """LUT-quantised MoE block (moe_layer.py:146-355): routed experts LUT, shared experts dense.
+
+    Built as the reference builds it:
+
+    * ``__init__`` makes the router ``gate`` [E, H], the shared experts
+      (``n_shared_experts`` x ``moe_intermediate_size`` columns) as dense
+      ``shared_gate_up`` [2 I_s, H] (gate rows, then up rows) and
+      ``shared_down`` [H, I_s], and a ``LUTQuantizer`` of ``lut_config.code_type``
+      (BLOCKLUT when there is no config).  The reference declares the shared
+      gate/up projection I_s wide, which its SiLU-and-mul halves before a
+      down projection that expects I_s inputs; here it is 2 I_s wide, so the
+      shared MLP has the intermediate size the config names.
+    * ``load_codebook(lut_path)`` loads ``blocklut_256.npy``;
+      ``quantize_expert_weights(w13, w2)`` trains the codebook on all the
+      expert weights when none was loaded, then quantises every expert to
+      the reference's BlockLUT format (uint8 index, bf16 absmax per 128,
+      the 256-entry codebook) in ``experts`` (one ``LUTMoEExpertWrapper``
+      each).  A ``lut_config`` with a ``lut_format()`` that names a per-block
+      format (Format B, NestedLUT) encodes that format instead.
+    * ``forward(hidden_states)``: router logits, softmax top-k (renormalised
+      when ``config.norm_topk_prob``), every routed expert and the shared
+      experts (added unscaled, as the reference adds them) in one
+      ``blut_moe_forward`` call, where the reference loops over (k, expert)
+      masks with a decompression and three matmuls per expert.
 
     ``config`` needs ``hidden_size``, ``moe_intermediate_size``,
     ``n_routed_experts``, ``num_experts_per_tok`` and optionally
-    ``n_shared_experts`` and ``norm_topk_prob``.  ``lut_config`` is a
-    ``LUTConfig`` (its ``lut_format()`` picks the weight format).
+    ``n_shared_experts`` and ``norm_topk_prob``; ``lut_config`` is the
+    patcher's ``LUT_MoE_vLLMConfig`` (``code_type``, ``lut_path``, ``lut_tier``)
+    or a ``LUTConfig``.
     """
 
     def __init__(self, config, parallel_config=None, quant_config=None, reduce_results: bool = True,
-                 prefix: str = "", lut_config=None, dtype: torch.dtype = torch.float16):
+                 prefix: str = "", lut_config=None, dtype: torch.dtype = torch.bfloat16):
         super().__init__()
         self.config = config
         self.lut_config = lut_config
@@ -140,45 +164,73 @@ class DeepseekV2MoE_LUT(nn.Module):
         self.renorm = bool(getattr(config, "norm_topk_prob", False))
         self.dtype = dtype
         self.gate = nn.Linear(self.hidden_size, self.num_experts, bias=False, dtype=dtype)
-        self.shared_gate_up: Optional[torch.Tensor] = None
-        self.shared_down: Optional[torch.Tensor] = None
+        if self.n_shared_experts:
+            si = self.intermediate_size * self.n_shared_experts
+            self.shared_gate_up = nn.Linear(self.hidden_size, 2 * si, bias=False, dtype=dtype)
+            self.shared_down = nn.Linear(si, self.hidden_size, bias=False, dtype=dtype)
+        else:
+            self.shared_gate_up = None
+            self.shared_down = None
+        self.quantizer = LUTQuantizer(code_type=getattr(lut_config, "code_type", "BLOCKLUT") if lut_config
+                                      else "BLOCKLUT")
+        self._codebook_loaded = False
+        self.experts: nn.ModuleList = nn.ModuleList()
         self.layer_id: int = 0
         self._moe: Optional[LUTMoELayer] = None
 
     def load_codebook(self, lut_path: str) -> bool:
         """Load the checkpoint's codebook files (moe_layer.py:229-237); True when
-        ``blocklut_256.npy`` was found. The table becomes the ``_codebook`` buffer."""
-        q = LUTQuantizer()
-        loaded = q.load(lut_path)
-        if loaded and q.lut_codebook is not None:
+        ``blocklut_256.npy`` was found. The table becomes the ``_codebook`` buffer
+        that ``quantize_expert_weights`` quantises with."""
+        loaded = self.quantizer.load(lut_path)
+        if loaded and self.quantizer.lut_codebook is not None:
             self._codebook_loaded = True
-            self.register_buffer("_codebook", q.lut_codebook.to("cuda"))
+            self.register_buffer("_codebook", self.quantizer.lut_codebook.to("cuda"))
         return loaded
 
     def lut_format(self) -> LUTFormat:
+        """The routed experts' format: the reference's BlockLUT unless the
+        config names a per-block format."""
         if self.lut_config is not None and hasattr(self.lut_config, "lut_format"):
             return self.lut_config.lut_format()
-        return LUTFormat("b", 4, 64)
+        tier = int(getattr(self.lut_config, "lut_tier", 0) or 0) if self.lut_config is not None else 0
+        return LUTFormat("r8", 8, self.quantizer.block_size, tier)
 
     @torch.no_grad()
-    def quantize_expert_weights(self, w13_weights: torch.Tensor, w2_weights: torch.Tensor,
-                                shared_gate_up: Optional[torch.Tensor] = None,
-                                shared_down: Optional[torch.Tensor] = None) -> None:
-        """Encode [E, 2I, H] / [E, H, I] float weights on the GPU and build the layer."""
+    def quantize_expert_weights(self, w13_weights: torch.Tensor, w2_weights: torch.Tensor) -> None:
+        """Quantise [E, 2I, H] / [E, H, I] expert weights (moe_layer.py:239-279) and build the layer."""
         fmt = self.lut_format()
+        E = w13_weights.shape[0]
+        self.experts = nn.ModuleList()
         if fmt.kind == "r8":
-            raise ValueError("DeepseekV2MoE_LUT encodes per-block formats; load reference-format "
-                             "checkpoints through LUTFusedMoEMethod")
-        w13 = [encode(w13_weights[e].cuda(), fmt) for e in range(w13_weights.shape[0])]
-        w2 = [encode(w2_weights[e].cuda(), fmt) for e in range(w2_weights.shape[0])]
+            if not self._codebook_loaded:  # train on these weights, as the reference does
+                self.quantizer.train(torch.cat([w13_weights.reshape(-1), w2_weights.reshape(-1)]))
+                self.register_buffer("_codebook", self.quantizer.lut_codebook.to("cuda"))
+                self._codebook_loaded = True
+            cb = self._codebook.to(device="cuda", dtype=torch.bfloat16).contiguous()
+            q13, q2 = [], []
+            for e in range(E):
+                ex = LUTMoEExpertWrapper(self.hidden_size, self.intermediate_size, self.quantizer)
+                ex.set_weights(w13_weights[e], w2_weights[e], cb)
+                self.experts.append(ex)
+                q13.append(QuantizedMatrix(fmt, 2 * self.intermediate_size, self.hidden_size,
+                                           ex.w13_indices.reshape(-1).contiguous(), cb,
+                                           scales=ex.w13_absmax.reshape(-1).to(torch.bfloat16).contiguous()))
+                q2.append(QuantizedMatrix(fmt, self.hidden_size, self.intermediate_size,
+                                          ex.w2_indices.reshape(-1).contiguous(), cb,
+                                          scales=ex.w2_absmax.reshape(-1).to(torch.bfloat16).contiguous()))
+            experts = LUTExperts.from_quantized(q13, q2, cb)
+        else:
+            q13 = [encode(w13_weights[e].cuda(), fmt) for e in range(E)]
+            q2 = [encode(w2_weights[e].cuda(), fmt) for e in range(E)]
+            experts = LUTExperts.from_quantized(q13, q2)
+        cdt = fmt.compute_dtype
         shared = None
-        if shared_gate_up is not None:
-            self.shared_gate_up = shared_gate_up.to(self.dtype).cuda().contiguous()
-            self.shared_down = shared_down.to(self.dtype).cuda().contiguous()
-            shared = SharedExpert.from_dense(self.shared_gate_up, self.shared_down)
-        experts = LUTExperts.from_quantized(w13, w2)
-        self._moe = LUTMoELayer(experts, self.top_k, router_w=self.gate.weight.detach().cuda(), renorm=self.renorm,
-                                shared=shared, shared_gate_mode=0)
+        if self.shared_gate_up is not None:
+            shared = SharedExpert.from_dense(self.shared_gate_up.weight.detach().to(device="cuda", dtype=cdt),
+                                             self.shared_down.weight.detach().to(device="cuda", dtype=cdt))
+        self._moe = LUTMoELayer(experts, self.top_k, router_w=self.gate.weight.detach().to("cuda"),
+                                renorm=self.renorm, shared=shared, shared_gate_mode=0)
 
     def forward(self, hidden_states: torch.Tensor, **kwargs) -> torch.Tensor:
         if self._moe is None:

@@ -174,20 +174,23 @@ def test_router_kernel_against_oracle(golden):
 
 
 def test_deepseek_v2_moe_lut_forward():
+    """A per-block format named by the LUT config (Format B 4-bit g64)."""
     from block_lut_b200.formats import LUTFormat
     from block_lut_b200.moe_layer import DeepseekV2MoE_LUT, _routing
     cfg = SimpleNamespace(hidden_size=256, moe_intermediate_size=128, n_routed_experts=6, num_experts_per_tok=2,
                           n_shared_experts=1, norm_topk_prob=False)
     lut_cfg = SimpleNamespace(lut_format=lambda: LUTFormat("b", 4, 64))
-    m = DeepseekV2MoE_LUT(cfg, lut_config=lut_cfg)
+    m = DeepseekV2MoE_LUT(cfg, lut_config=lut_cfg, dtype=torch.float16)
     rng = np.random.Generator(np.random.PCG64(6))
-    with torch.no_grad():
-        m.gate.weight.copy_(torch.from_numpy((rng.standard_normal((6, 256)) * 0.1).astype(np.float16)))
     w13 = torch.from_numpy(O.student_t_weights(rng, (6, 256, 256)))
     w2 = torch.from_numpy(O.student_t_weights(rng, (6, 256, 128)))
     sgu = torch.from_numpy(O.student_t_weights(rng, (256, 256))).half()
     sd = torch.from_numpy(O.student_t_weights(rng, (256, 128))).half()
-    m.quantize_expert_weights(w13, w2, sgu, sd)
+    with torch.no_grad():
+        m.gate.weight.copy_(torch.from_numpy((rng.standard_normal((6, 256)) * 0.1).astype(np.float16)))
+        m.shared_gate_up.weight.copy_(sgu)
+        m.shared_down.weight.copy_(sd)
+    m.quantize_expert_weights(w13, w2)
     x = cuda(O.rms_activations(rng, 10, 256).astype(np.float16)).reshape(2, 5, 256)
     out = m(x)
     assert out.shape == x.shape
@@ -203,9 +206,67 @@ def test_deepseek_v2_moe_lut_forward():
            for q in (encode(w13[e].cuda(), LUTFormat("b", 4, 64)) for e in range(6))]
     W2 = [O.dequant_b(*[t.cpu().numpy() for t in (q.codes, q.tables)], 4, 64).astype(np.float32)
           for q in (encode(w2[e].cuda(), LUTFormat("b", 4, 64)) for e in range(6))]
-    xs = xn
-    h = xs @ sgu.double().numpy().T
+    h = xn @ sgu.double().numpy().T
     a = O.round_to((O.silu(h[:, :128]) * h[:, 128:]).astype(np.float32), "f16").astype(np.float64)
     ref = O.moe_forward(xn, ids, tw, W13, W2, act_dtype="f16") + a @ sd.double().numpy().T
     assert ex.num_experts == 6
     check_layer(out.reshape(10, 256), ref, torch.float16, "DeepseekV2MoE_LUT")
+
+
+@pytest.mark.parametrize("codebook", ["loaded", "trained"])
+def test_deepseek_v2_moe_lut_blocklut_as_patched(codebook, tmp_path):
+    """The reference's own format, driven the way vllm_lut/patcher.py drives
+    the block: a LUT_MoE_vLLMConfig-like config (code_type, lut_path,
+    lut_tier), the codebook loaded from ``blocklut_256.npy`` or trained on the
+    expert weights, then ``quantize_expert_weights(w13, w2)`` and a forward.
+    Checked against the float64 oracle on the experts' own BlockLUT weights."""
+    from block_lut_b200.moe_layer import DeepseekV2MoE_LUT
+    E, H, I, ns, k, T = 6, 256, 128, 2, 2, 12
+    cfg = SimpleNamespace(hidden_size=H, moe_intermediate_size=I, n_routed_experts=E, num_experts_per_tok=k,
+                          n_shared_experts=ns, norm_topk_prob=False, num_hidden_layers=27)
+    lut_cfg = SimpleNamespace(code_type="BLOCKLUT", lut_path=str(tmp_path), lut_tier=0,
+                              enable_progressive_loading=False)
+    rng = np.random.Generator(np.random.PCG64(41))
+    if codebook == "loaded":
+        np.save(tmp_path / "blocklut_256.npy", np.sort(rng.uniform(-1, 1, 256)).astype(np.float32))
+    m = DeepseekV2MoE_LUT(cfg, lut_config=lut_cfg)
+    assert m.load_codebook(str(tmp_path)) == (codebook == "loaded")
+    w13 = torch.from_numpy(O.student_t_weights(rng, (E, 2 * I, H))).to(torch.bfloat16)
+    w2 = torch.from_numpy(O.student_t_weights(rng, (E, H, I))).to(torch.bfloat16)
+    si = I * ns
+    sgu = torch.from_numpy(O.student_t_weights(rng, (2 * si, H))).to(torch.bfloat16)
+    sd = torch.from_numpy(O.student_t_weights(rng, (H, si))).to(torch.bfloat16)
+    with torch.no_grad():
+        m.gate.weight.copy_(torch.from_numpy((rng.standard_normal((E, H)) * 0.1).astype(np.float32)))
+        m.shared_gate_up.weight.copy_(sgu)
+        m.shared_down.weight.copy_(sd)
+    assert m.shared_gate_up.weight.shape == (2 * si, H) and m.shared_down.weight.shape == (H, si)
+    m.quantize_expert_weights(w13.cuda(), w2.cuda())
+    assert len(m.experts) == E and m._codebook.dtype == torch.bfloat16 and m._codebook.numel() == 256
+    assert m._moe.experts.fmt.kind == "r8"
+    x = torch.from_numpy(O.rms_activations(rng, T, H).astype(np.float32)).to(torch.bfloat16).cuda()
+    out = m(x.reshape(2, T // 2, H))
+    assert out.shape == (2, T // 2, H) and out.dtype == torch.bfloat16
+    # oracle: each expert's BlockLUT weights as stored by its wrapper, dequantised on the CPU
+    cb = m._codebook.cpu().view(torch.int16).numpy().view(np.uint16)
+
+    def deq(ex, name, rows, cols):
+        idx = getattr(ex, f"{name}_indices").reshape(-1).cpu().numpy()
+        am = getattr(ex, f"{name}_absmax").reshape(-1).cpu().view(torch.int16).numpy().view(np.uint16)
+        return O.bf16_to_f32(O.dequant_r(idx, am, cb, 128, 0)).reshape(rows, cols)
+    W13 = [deq(ex, "w13", 2 * I, H) for ex in m.experts]
+    W2 = [deq(ex, "w2", H, I) for ex in m.experts]
+    # the wrappers' bf16 weights are the same values (decompress_blocklut on the GPU)
+    assert np.array_equal(m.experts[0].get_weight("w13").float().cpu().numpy(), W13[0])
+    xn = x.float().cpu().numpy().astype(np.float64)
+    gw = m.gate.weight.detach().float().cpu().numpy().astype(np.float64)
+    logits = xn @ gw.T
+    ids, tw = O.routing(logits, k)
+    srt = np.sort(logits, axis=1)
+    keep = srt[:, -k] - srt[:, -k - 1] > 1e-4
+    assert keep.sum() >= T // 2
+    h = xn @ sgu.double().numpy().T
+    a = O.round_to((O.silu(h[:, :si]) * h[:, si:]).astype(np.float32), "bf16").astype(np.float64)
+    ref = O.moe_forward(xn, ids, tw, W13, W2, act_dtype="bf16") + a @ sd.double().numpy().T
+    check_layer(out.reshape(T, H)[torch.from_numpy(keep).cuda()], ref[keep], torch.bfloat16,
+                f"DeepseekV2MoE_LUT BlockLUT ({codebook} codebook)")

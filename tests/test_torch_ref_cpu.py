@@ -83,3 +83,27 @@ def test_apply_format_b_matches_oracle():
     W2 = [deq_t(e, "w2").numpy() for e in range(E)]
     ref = O.moe_forward(x, ids, tw, W13, W2, act_dtype="f32")
     assert np.abs(out.numpy() - ref).max() < 1e-5
+
+
+@pytest.mark.parametrize("kind", ["b2g128", "b3g32", "b4g64", "nested0", "nested1"])
+def test_dequant_on_random_codes_matches_oracle(kind):
+    """Uniform random codes and sorted random tables (what the config-shape GPU tests use)."""
+    rng = np.random.Generator(np.random.PCG64(7))
+    rows, cols = 96, 512
+
+    def tables(group, ent, scale=0.02):
+        return np.sort((rng.standard_normal((rows, cols // group, ent)) * scale).astype(np.float16), axis=-1)
+    if kind.startswith("nested"):
+        coarse_only = kind.endswith("1")
+        cc = rng.integers(0, 256, size=(rows, cols // 4), dtype=np.uint8)
+        cr = rng.integers(0, 256, size=(rows, cols // 4), dtype=np.uint8)
+        ct, rt = tables(64, 4), tables(64, 16, 0.004)
+        want = O.dequant_nested(cc, cr, ct, rt, 64, coarse_only=coarse_only).astype(np.float32)
+        got = R.dequant_nested(*map(torch.from_numpy, (cc, cr, ct, rt)), 64, rows, cols, coarse_only=coarse_only)
+    else:
+        bits, group = int(kind[1]), int(kind[3:])
+        packed = rng.integers(0, 256, size=(rows, cols * bits // 8), dtype=np.uint8)
+        t = tables(group, 1 << bits)
+        want = O.dequant_b(packed, t, bits, group).astype(np.float32)
+        got = R.dequant_b(torch.from_numpy(packed), torch.from_numpy(t), bits, group, rows, cols)
+    assert np.array_equal(got.numpy(), want)
