@@ -74,10 +74,11 @@ def parse():
                    help="matmul path of the experts: tcgen05 where the format has it (auto), or forced")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    p.add_argument("--workload", choices=["decode", "qwen3", "prefill", "sweep", "tiers"], default="decode",
+    p.add_argument("--workload", choices=["decode", "qwen3", "prefill", "sweep", "tiers", "vllm"], default="decode",
                    help="decode: the BASELINE metric (config 2); qwen3: config 3's MoE stack at decode; "
                         "prefill: config 4's MoE layers; sweep: config 5's single-matrix kernel sweep; "
-                        "tiers: Format R progressive bit-plane tier recover")
+                        "tiers: Format R progressive bit-plane tier recover; vllm: config 2 end to end "
+                        "through vLLM with the lut plugin")
     p.add_argument("--sweep-bits", default="2,3,4")
     p.add_argument("--sweep-groups", default="32,64,128")
     p.add_argument("--sweep-m", default="1,2,4,8,16,64,256,1024,4096")
@@ -784,10 +785,98 @@ def run_tiers(a):
     print(json.dumps(res), flush=True)
 
 
+# --------------------------------------------------------------- vllm ---
+VLLM_METRIC = "vLLM decode tokens/s, full model, LUT experts"
+
+
+def qwen15_moe_config(layers: int, quant: dict, dtype: str) -> dict:
+    """config.json of the Qwen1.5-MoE-A2.7B architecture."""
+    return {
+        "architectures": ["Qwen2MoeForCausalLM"], "model_type": "qwen2_moe",
+        "hidden_size": 2048, "intermediate_size": 5632, "moe_intermediate_size": 1408,
+        "shared_expert_intermediate_size": 5632, "num_experts": 60, "num_experts_per_tok": 4,
+        "norm_topk_prob": False, "num_hidden_layers": layers, "num_attention_heads": 16,
+        "num_key_value_heads": 16, "vocab_size": 151936, "max_position_embeddings": 8192,
+        "rope_theta": 1000000.0, "rms_norm_eps": 1e-6, "hidden_act": "silu", "decoder_sparse_step": 1,
+        "mlp_only_layers": [], "tie_word_embeddings": False, "torch_dtype": dtype, "use_sliding_window": False,
+        "sliding_window": None, "attention_dropout": 0.0, "initializer_range": 0.02,
+        "bos_token_id": 151643, "eos_token_id": 151643, "quantization_config": quant,
+    }
+
+
+def lut_quant_config(fmt) -> dict:
+    """The checkpoint's quantization_config for the LUT plugin (block_lut_b200.quant_method.LUTConfig)."""
+    q = {"quant_method": "lut", "code_type": "BLOCKLUT"}
+    if fmt.kind == "b":
+        q.update({"codebook_scope": "row_block", "index_bits": fmt.bits, "lut_block": fmt.group})
+    elif fmt.kind == "nested":
+        q.update({"codebook_scope": "row_block", "lut_block": fmt.group,
+                  "nested": {"coarse_bits": 2, "residual_bits": 2, "tier": "coarse" if fmt.tier else "full"}})
+    return q
+
+
+def run_vllm(a):
+    """Config 2 end to end: the full Qwen1.5-MoE-A2.7B architecture (24
+    layers, attention and dense layers in the model dtype, experts through
+    the lut plugin) in vLLM with CUDA graphs, weights from vLLM's dummy
+    loader (there is no checkpoint here).  Per batch size: a prompt of 512
+    random token ids per sequence, then 128 generated tokens; decode tokens/s
+    = batch x 128 / (time of prefill + 128 tokens - time of prefill + 1
+    token).  The engine runs in this process (VLLM_ENABLE_V1_MULTIPROCESSING=0)
+    so that the plugin registered on import is the one it uses."""
+    os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
+    import random
+    import torch
+    import block_lut_b200.quant_method  # noqa: F401  registers "lut" with vLLM
+    from vllm import LLM, SamplingParams
+    fmt = bench_format(a)
+    dtype = "bfloat16" if fmt.kind == "r8" else "float16"
+    layers = a.layers
+    d = tempfile.mkdtemp(prefix="blut_vllm_")
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(qwen15_moe_config(layers, lut_quant_config(fmt), dtype), f)
+    batches = sorted({1, a.batch})
+    t0 = time.time()
+    llm = LLM(model=d, quantization="lut", load_format="dummy", skip_tokenizer_init=True, max_model_len=1024,
+              gpu_memory_utilization=0.8, max_num_seqs=max(batches), dtype=dtype, enforce_eager=False, seed=0)
+    init_s = time.time() - t0
+    rng = random.Random(0)
+    res_b = {}
+    for bs in batches:
+        prompts = [{"prompt_token_ids": [rng.randrange(1000, 150000) for _ in range(512)]} for _ in range(bs)]
+
+        def gen(n):
+            sp = SamplingParams(max_tokens=n, min_tokens=n, ignore_eos=True, temperature=0.0, detokenize=False)
+            torch.cuda.synchronize()
+            t = time.perf_counter()
+            outs = llm.generate(prompts, sp, use_tqdm=False)
+            torch.cuda.synchronize()
+            assert all(len(o.outputs[0].token_ids) == n for o in outs)
+            return time.perf_counter() - t
+        for _ in range(max(1, a.warmup)):
+            gen(2)
+        t1 = min(gen(1) for _ in range(3))
+        t129 = min(gen(129) for _ in range(max(1, min(a.steps, 3))))
+        res_b[bs] = {"decode_tokens_s": bs * 128 / (t129 - t1), "ms_per_token_step": (t129 - t1) / 128 * 1e3,
+                     "prefill_s": t1}
+    top = res_b[max(batches)]
+    res = {"metric": VLLM_METRIC, "value": top["decode_tokens_s"], "unit": "tokens/s", "n_gpus": 1,
+           "steps": 128, "warmup": a.warmup, "ms_per_step": top["ms_per_token_step"], "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f16" if dtype == "float16" else "bf16",
+           "data": "vLLM dummy weights (random), random prompt token ids",
+           "config": {"workload": f"Qwen1.5-MoE-A2.7B ({layers} layers) in vLLM, prompt 512, generate 128",
+                      "format": format_name(fmt), "engine": "vLLM LLM(quantization='lut', load_format='dummy'), "
+                      "CUDA graphs on", "init_s": round(init_s, 1)},
+           "batches": {str(k): v for k, v in res_b.items()}}
+    print(json.dumps(res), flush=True)
+
+
 if __name__ == "__main__":
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "vllm":
+        run_vllm(args)
     elif args.workload == "prefill":
         run_prefill(args)
     elif args.workload == "sweep":

@@ -175,6 +175,58 @@ __device__ __forceinline__ void tc_mma_ss(uint32_t d, uint64_t adesc, uint64_t b
       : "memory");
 }
 
+// The MMAs of one 64-column half-block (4 slabs of K = 16) for one tile
+// (NT = 1) or both tiles (NT = 2) of a unit, issued from one straight-line
+// block so that the single issuing thread spends few instructions per half
+// (it shares its sub-partition with ALU-bound decode warps, so every
+// instruction it issues waits for a slot): slab sl of tile t reads A from
+// tensor-memory column a + 32 t + 8 sl and B through the descriptor
+// {b_lo + 16 sl, b_hi} (the low word's bits 0-13 are the activations'
+// shared address >> 4, and slab sl starts 256 sl bytes further).
+// Accumulators: d0 (tile 0) and d1 (tile 1).  `acc` = 0 starts them fresh
+// at slab 0; later slabs always accumulate.
+template <int NT>
+__device__ __forceinline__ void tc_mma_half(uint32_t d0, uint32_t d1, uint32_t a, uint32_t b_lo, uint32_t b_hi,
+                                            uint32_t idesc, uint32_t acc) {
+  if constexpr (NT == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t.reg .b64 bd;\n\t.reg .b32 bl, a0, a1;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "setp.eq.b32 q, %6, %6;\n\t"
+        "mov.b64 bd, {%3, %4};\n\t"
+        "add.u32 a1, %2, 32;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], bd, %5, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [a1], bd, %5, p;\n\t"
+        "add.u32 bl, %3, 16;\n\tmov.b64 bd, {bl, %4};\n\tadd.u32 a0, %2, 8;\n\tadd.u32 a1, %2, 40;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a0], bd, %5, q;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [a1], bd, %5, q;\n\t"
+        "add.u32 bl, %3, 32;\n\tmov.b64 bd, {bl, %4};\n\tadd.u32 a0, %2, 16;\n\tadd.u32 a1, %2, 48;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a0], bd, %5, q;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [a1], bd, %5, q;\n\t"
+        "add.u32 bl, %3, 48;\n\tmov.b64 bd, {bl, %4};\n\tadd.u32 a0, %2, 24;\n\tadd.u32 a1, %2, 56;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a0], bd, %5, q;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [a1], bd, %5, q;\n\t}" ::"r"(d0),
+        "r"(d1), "r"(a), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t.reg .b64 bd;\n\t.reg .b32 bl, a0;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "setp.eq.b32 q, %5, %5;\n\t"
+        "mov.b64 bd, {%2, %3};\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, p;\n\t"
+        "add.u32 bl, %2, 16;\n\tmov.b64 bd, {bl, %3};\n\tadd.u32 a0, %1, 8;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a0], bd, %4, q;\n\t"
+        "add.u32 bl, %2, 32;\n\tmov.b64 bd, {bl, %3};\n\tadd.u32 a0, %1, 16;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a0], bd, %4, q;\n\t"
+        "add.u32 bl, %2, 48;\n\tmov.b64 bd, {bl, %3};\n\tadd.u32 a0, %1, 24;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a0], bd, %4, q;\n\t}" ::"r"(d0),
+        "r"(a), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc)
+        : "memory");
+    (void)d1;
+  }
+}
+
 // 32 consecutive 32-bit columns of this thread's lane.
 __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
@@ -583,39 +635,14 @@ __host__ inline int tc_smem_bytes(const TcParams& p) {
          p.xstages * tc_xstage_bytes<Dec, MT>();
 }
 
-// A work item as the producer posts it to the shared-memory queue: the item
-// number (-1: no more work) and its decomposition, resolved once per CTA
-// (divisions and the group table's global loads) instead of by every role.
-struct TcItem {
-  int item;    // global item index, or -1
-  int u;       // unit: tiles 2u and 2u + 1 of the matrix
-  int b0, b1;  // column blocks [b0, b1) of the item's K slice
-  int slice;   // K slice index (item % ks)
-  int ntok;    // tokens of the group
-  int nt0;     // first n-tile of the group in the activations
-  int slot0;   // first output slot of the group
-};
-constexpr int kTcQInfo = 800;  // byte offset of the TcItem queue in the header (the barriers end at 784)
-static_assert(kTcQInfo + kTcQueue * (int)sizeof(TcItem) <= kTcHeader, "item queue exceeds the header");
-
-// Bounded wait by a whole warp: every lane polls and the warp leaves on a
-// vote, so the branch is warp-uniform and no lane's result needs to be
-// broadcast.  The slow path (sleeping polls, the time limit, the abort flag)
-// only runs when the first poll finds the phase incomplete.
-__device__ __forceinline__ bool tc_warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
-                                             uint64_t limit_ns) {
-  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-  return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort_flag, status, limit_ns));
-}
-// Arrive once on behalf of the warp: lane 0's arrive is predicated, not a
-// divergent branch.  The caller has synchronised the warp first.
-__device__ __forceinline__ void tc_arrive_lane0(uint32_t bar, int lane) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.eq.u32 p, %1, 0;\n\t"
-      "@p mbarrier.arrive.shared::cta.b64 _, [%0];\n\t}" ::"r"(bar),
-      "r"(lane)
-      : "memory");
+// Waits for this thread's tcgen05.st; `v` (the registers of the store in
+// flight) is tied to the wait so the compiler keeps them unchanged until then.
+__device__ __forceinline__ void tc_wait_st_keep(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::st.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
 }
 
 template <class Dec, int MT>
@@ -641,9 +668,9 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
   uint64_t* fin = full + 60;                           // last MMAs complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 61);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 62);
+  volatile int* qitem = reinterpret_cast<volatile int*>(full + 63);  // [kTcQueue]
   uint64_t* xfull = full + 66;                         // [kTcMaxStages] activation stage loaded (LUT formats)
   uint64_t* xempty = full + 82;                        // [kTcMaxStages] activation stage read (MMA commit)
-  TcItem* qinfo = reinterpret_cast<TcItem*>(smem + kTcQInfo);      // [kTcQueue] posted items
   uint32_t* r8tab = reinterpret_cast<uint32_t*>(smem + kTcHeader);  // barriers end at full + 98 (784 bytes)
   uint8_t* ring = smem + kTcHeader + tc_table_bytes<Dec>();
   const int S = p.stages, SX = p.xstages;
@@ -653,7 +680,6 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
   const int boff = 2 * p.tile_bytes;  // activations inside a dense stage
   // planes inside a stage: each holds the pieces of the unit's two tiles
   const int qoff[3] = {0, 2 * p.piece[0], 2 * (p.piece[0] + p.piece[1])};
-  const uint64_t wlim = p.wait_ns;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -692,44 +718,32 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int n_items = *p.gt.n_groups * p.units * p.ks;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
-      const int n_items = *p.gt.n_groups * p.units * p.ks;
       TcRing r, rx, rq;
       uint32_t issued = 0, lastph = 0;    // per weight stage: issued at least once, parity of the last issue
       uint32_t xissued = 0, xlastph = 0;  // the same per activation stage
       for (;; rq.next(kTcQueue)) {
         const int qs = rq.i;
-        if (rq.wrapped && !wait_or_abort(smem_u32(qempty + qs), rq.ph ^ 1u, abort_flag, p.status, wlim)) break;
+        if (rq.wrapped && !wait_or_abort(smem_u32(qempty + qs), rq.ph ^ 1u, abort_flag, p.status, p.wait_ns)) break;
         int item = atomicAdd(p.counter, 1);
         if (item >= n_items || *abort_flag) item = -1;
-        TcItem it{};
-        it.item = item;
-        int expert = 0;
-        if (item >= 0) {
-          const int ku = item / p.ks;
-          const int gi = ku / p.units;
-          it.slice = item - ku * p.ks;
-          it.u = ku - gi * p.units;
-          it.b0 = it.slice * p.bps;
-          it.b1 = min(p.nblocks, it.b0 + p.bps);
-          it.ntok = p.gt.ntok[gi];
-          it.nt0 = p.gt.nt0[gi];
-          it.slot0 = p.gt.slot0[gi];
-          expert = p.gt.expert[gi];
-        }
-        qinfo[qs] = it;
-        mbar_arrive(smem_u32(qfull + qs));  // release: the posted item is visible to the roles that wait on it
+        qitem[qs] = item;
+        mbar_arrive(smem_u32(qfull + qs));
         if (item < 0) break;
-        const int nnt = (it.ntok + kNTile - 1) / kNTile;
-        const int ntl = min(2, p.ntiles - 2 * it.u);
-        const uint8_t* base = p.w + (int64_t)expert * p.wstride;
+        const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
+        const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
+        const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
+        const int nt0 = p.gt.nt0[gi];
+        const int ntl = min(2, p.ntiles - 2 * u);
+        const uint8_t* base = p.w + (int64_t)p.gt.expert[gi] * p.wstride;
         bool ok = true;
-        for (int b = it.b0; b < it.b1; ++b, r.next(S)) {
+        for (int b = b0; b < b1; ++b, r.next(S)) {
           const int s = r.i;
-          if (r.wrapped && !wait_or_abort(smem_u32(empty + s), r.ph ^ 1u, abort_flag, p.status, wlim)) {
+          if (r.wrapped && !wait_or_abort(smem_u32(empty + s), r.ph ^ 1u, abort_flag, p.status, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -738,7 +752,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
           uint8_t* dst = ring + (int64_t)s * stage_bytes;
           uint32_t bar = smem_u32(full + s);
           mbar_expect_tx(bar, (uint32_t)(ntl * p.tile_bytes + (kDense ? nnt * KB * 16 : 0)));
-          const int64_t pt = (int64_t)b * p.ntiles + 2 * it.u;
+          const int64_t pt = (int64_t)b * p.ntiles + 2 * u;
 #pragma unroll
           for (int k = 0; k < Dec::kNumPlanes; ++k)
             bulk_g2s(smem_u32(dst + qoff[k]), base + p.plane_off[k] + pt * p.piece[k], (uint32_t)(ntl * p.piece[k]),
@@ -746,7 +760,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
           uint8_t* xdst = dst + boff;
           if constexpr (!kDense) {
             const int sx = rx.i;
-            if (rx.wrapped && !wait_or_abort(smem_u32(xempty + sx), rx.ph ^ 1u, abort_flag, p.status, wlim)) {
+            if (rx.wrapped && !wait_or_abort(smem_u32(xempty + sx), rx.ph ^ 1u, abort_flag, p.status, p.wait_ns)) {
               ok = false;
               break;
             }
@@ -757,7 +771,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
             mbar_expect_tx(bar, (uint32_t)(nnt * KB * 16));
             rx.next(SX);
           }
-          bulk_g2s(smem_u32(xdst), p.bin + ((int64_t)b * p.ntstride + it.nt0) * (KB * 16), (uint32_t)(nnt * KB * 16),
+          bulk_g2s(smem_u32(xdst), p.bin + ((int64_t)b * p.ntstride + nt0) * (KB * 16), (uint32_t)(nnt * KB * 16),
                    bar);
         }
         if (!ok) break;
@@ -777,22 +791,24 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
       TcRing r, ra, rd, rq;
       for (;; rq.next(kTcQueue)) {
         const int qs = rq.i;
-        if (!wait_or_abort(smem_u32(qfull + qs), rq.ph, abort_flag, p.status, wlim)) break;
-        const TcItem it = qinfo[qs];
+        if (!wait_or_abort(smem_u32(qfull + qs), rq.ph, abort_flag, p.status, p.wait_ns)) break;
+        const int item = qitem[qs];
         mbar_arrive(smem_u32(qempty + qs));
-        if (it.item < 0) break;
-        const int nnt = (it.ntok + kNTile - 1) / kNTile;
-        const int ntl = min(2, p.ntiles - 2 * it.u);
+        if (item < 0) break;
+        const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
+        const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
+        const int nnt = (p.gt.ntok[gi] + kNTile - 1) / kNTile;
+        const int ntl = min(2, p.ntiles - 2 * u);
         const uint32_t idesc = tc_idesc(Dec::kBF16, min(MT, (nnt + 1) / 2 * 16));
         const int db = rd.i;
-        if (rd.wrapped && !wait_or_abort(smem_u32(dempty + db), rd.ph ^ 1u, abort_flag, p.status, wlim)) break;
+        if (rd.wrapped && !wait_or_abort(smem_u32(dempty + db), rd.ph ^ 1u, abort_flag, p.status, p.wait_ns)) break;
         tc_fence_after();
         const uint32_t dcol = tmem + db * kDCols;
         bool ok = true;
         // dense: r walks the combined stages; LUT formats: r walks the activation stages
-        for (int b = it.b0; b < it.b1 && ok; ++b, r.next(kDense ? S : SX)) {
+        for (int b = b0; b < b1 && ok; ++b, r.next(kDense ? S : SX)) {
           const int s = r.i;
-          if (!wait_or_abort(smem_u32((kDense ? full : xfull) + s), r.ph, abort_flag, p.status, wlim)) {
+          if (!wait_or_abort(smem_u32((kDense ? full : xfull) + s), r.ph, abort_flag, p.status, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -804,25 +820,26 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
               const uint64_t bd = tc_desc(st + boff + sl * 256, 128, KB * 16);
               for (int t = 0; t < ntl; ++t) {
                 const uint64_t ad = tc_desc(st + t * p.piece[0] + sl * 2 * 2048, 2048, 128);
-                tc_mma_ss(dcol + t * MT, ad, bd, idesc, ((b - it.b0) | sl) != 0);
+                tc_mma_ss(dcol + t * MT, ad, bd, idesc, ((b - b0) | sl) != 0);
               }
             }
           } else {
+            const uint64_t bd0 = tc_desc(st, 128, KB * 16);  // slab 0 of half 0; later slabs add to the low word
+            const uint32_t b_lo = (uint32_t)bd0, b_hi = (uint32_t)(bd0 >> 32);
 #pragma unroll
             for (int h = 0; h < Dec::kHalves; ++h, ra.next(kTcASlots)) {
               const int j = ra.i;
-              if (!wait_or_abort(smem_u32(afull + j), ra.ph, abort_flag, p.status, wlim)) {
+              if (!wait_or_abort(smem_u32(afull + j), ra.ph, abort_flag, p.status, p.wait_ns)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-#pragma unroll
-              for (int sl = 0; sl < 4; ++sl) {
-                const uint64_t bd = tc_desc(st + (h * 4 + sl) * 256, 128, KB * 16);
-                for (int t = 0; t < ntl; ++t)
-                  tc_mma_ts(dcol + t * MT, tmem + kACol0 + j * 64 + t * 32 + sl * 8, bd, idesc,
-                            ((b - it.b0) | h | sl) != 0);
-              }
+              const uint32_t a = tmem + kACol0 + j * 64;
+              const uint32_t acc = ((b - b0) | h) != 0;
+              if (ntl == 2)
+                tc_mma_half<2>(dcol, dcol + MT, a, b_lo + h * 64, b_hi, idesc, acc);
+              else
+                tc_mma_half<1>(dcol, dcol + MT, a, b_lo + h * 64, b_hi, idesc, acc);
               tc_commit(smem_u32(aempty + j));
             }
           }
@@ -839,49 +856,49 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
     __syncwarp();
   } else {
     // ------------------------------------------------- decode and epilogue --
-    // Every wait here is a warp-uniform vote and every arrive a predicated
-    // lane-0 instruction, so the loop has no divergent branches.
     const int dw = warp - 2;
     const int set = dw / kTcDecodeWarps;      // decode set: takes blocks b0 + set, b0 + set + kSets, ...
     const int t = (dw % kTcDecodeWarps) >> 2;  // tile of the unit
     const int q = warp & 3;            // tensor-memory lane quarter this warp may access
     const int row = 32 * q + lane;     // row inside the 128-row tile
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-    const uint32_t abase = tmem + lane_base + kACol0 + t * 32;  // this tile's columns of A slot 0
-    const int toff[3] = {qoff[0] + t * p.piece[0], qoff[1] + t * p.piece[1], qoff[2] + t * p.piece[2]};
-    const uint32_t tab = smem_u32(r8tab) + lane * 4;
     TcRing r, ra, rd, rq;
     for (;; rq.next(kTcQueue)) {
       const int qs = rq.i;
-      if (!tc_warp_wait(smem_u32(qfull + qs), rq.ph, abort_flag, p.status, wlim)) break;
-      const TcItem it = qinfo[qs];
+      bool ok = wait_or_abort(smem_u32(qfull + qs), rq.ph, abort_flag, p.status, p.wait_ns);
+      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+      const int item = qitem[qs];
       __syncwarp();
-      tc_arrive_lane0(smem_u32(qempty + qs), lane);
-      if (it.item < 0) break;
-      const int ntl = min(2, p.ntiles - 2 * it.u);
+      if (lane == 0) mbar_arrive(smem_u32(qempty + qs));
+      if (item < 0) break;
+      const int ku = item / p.ks, gi = ku / p.units, u = ku % p.units;
+      const int b0 = (item % p.ks) * p.bps, b1 = min(p.nblocks, b0 + p.bps);
+      const int ntok = p.gt.ntok[gi];
+      const int ntl = min(2, p.ntiles - 2 * u);
       if constexpr (!kDense) {
-        const bool active = t < ntl;  // warp-uniform: the unit's second tile may not exist
+        const bool active = t < ntl;
         bool aborted = false;
         // A half is decoded as two quarters (qa, qb): the store of the first
         // runs while the second is decoded.
-        for (int b = it.b0; b < it.b1; ++b, r.next(S)) {
-          if (kSets > 1 && (b - it.b0) % kSets != set) {  // the other decode set's block
+        for (int b = b0; b < b1 && !aborted; ++b, r.next(S)) {
+          if (kSets > 1 && (b - b0) % kSets != set) {  // the other decode set's block
 #pragma unroll
             for (int h = 0; h < Dec::kHalves; ++h) ra.next(kTcASlots);
             continue;
           }
           const int s = r.i;
-          if (!tc_warp_wait(smem_u32(full + s), r.ph, abort_flag, p.status, wlim)) {
+          ok = wait_or_abort(smem_u32(full + s), r.ph, abort_flag, p.status, p.wait_ns);
+          if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
             aborted = true;
             break;
           }
-          const uint8_t* st = ring + s * stage_bytes;
+          const uint8_t* st = ring + (int64_t)s * stage_bytes;
           TcPtrs pp;
 #pragma unroll
-          for (int k = 0; k < 3; ++k) pp.p[k] = st + toff[k];
-          pp.tab = tab;
+          for (int k = 0; k < 3; ++k) pp.p[k] = st + qoff[k] + t * p.piece[k];
+          pp.tab = smem_u32(r8tab) + lane * 4;
 #pragma unroll
-          for (int h = 0; h < Dec::kHalves; ++h) {
+          for (int h = 0; h < Dec::kHalves; ++h, ra.next(kTcASlots)) {
             const int j = ra.i;
             uint32_t qa[16], qb[16];
             typename Dec::Half hd;
@@ -889,43 +906,46 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
               Dec::load_half(pp, row, h, hd);
               Dec::lookup_q(hd, 0, qa, p.mul);
             }
-            if (ra.wrapped && !tc_warp_wait(smem_u32(aempty + j), ra.ph ^ 1u, abort_flag, p.status, wlim)) {
-              aborted = true;
-              break;
+            if (ra.wrapped) {
+              ok = wait_or_abort(smem_u32(aempty + j), ra.ph ^ 1u, abort_flag, p.status, p.wait_ns);
+              if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) {
+                aborted = true;
+                break;
+              }
             }
             tc_fence_after();
-            const uint32_t aslot = abase + j * 64;
+            const uint32_t aslot = tmem + lane_base + kACol0 + j * 64 + t * 32;
             if (active) {
               tc_st16(aslot, qa);  // the first quarter's store overlaps the second's lookups
               Dec::lookup_q(hd, 1, qb, p.mul);
               tc_st16(aslot + 16, qb);
+              tc_wait_st_keep(qa);
+              tc_wait_st_keep(qb);
             }
             if (h == Dec::kHalves - 1) {  // this stage's shared memory is no longer read
               __syncwarp();
-              tc_arrive_lane0(smem_u32(empty + s), lane);
+              if (lane == 0) mbar_arrive(smem_u32(empty + s));
             }
-            if (active) tc_wait_st();
             tc_fence_before();
             __syncwarp();
-            tc_arrive_lane0(smem_u32(afull + j), lane);
-            ra.next(kTcASlots);
+            if (lane == 0) mbar_arrive(smem_u32(afull + j));
           }
-          if (aborted) break;
         }
         if (aborted) break;
       }
       // epilogue
       const int db = rd.i;
-      if (!tc_warp_wait(smem_u32(dfull + db), rd.ph, abort_flag, p.status, wlim)) break;
+      ok = wait_or_abort(smem_u32(dfull + db), rd.ph, abort_flag, p.status, p.wait_ns);
+      if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
       tc_fence_after();
       const uint32_t dcol = tmem + lane_base + db * kDCols;
-      const int ntok = it.ntok;
       if (p.pair) {
         // chunks of 16 tokens of unit row `row`, chunk c to the warp pair
         // (set, t) with c % (2 kSets) == 2 set + t; gate tile at columns
         // 0 .. MT-1, up tile at MT .. 2MT-1
-        const int col = it.u * kTcRows + row;  // K index of the down projection
-        uint8_t* dst = p.act_out + tc_bact_off((int64_t)it.nt0 * kNTile, col, p.out_kb, p.ntstride);
+        const int col = u * kTcRows + row;  // K index of the down projection
+        const int nt0 = p.gt.nt0[gi];
+        uint8_t* dst = p.act_out + tc_bact_off((int64_t)nt0 * kNTile, col, p.out_kb, p.ntstride);
 #pragma unroll 1
         for (int c = 2 * set + t; c < MT / 16; c += 2 * kSets) {
           const int tok0 = 16 * c;
@@ -939,7 +959,7 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
             // partial sums of this slice (MT = 32); splitk_silu_kernel adds
             // the slices up after this launch (a kernel boundary orders them
             // without fences)
-            float* mine = p.part + (int64_t)it.item * (2 * kTcRows * 32) + row * 32 + tok0;
+            float* mine = p.part + (int64_t)item * (2 * kTcRows * 32) + row * 32 + tok0;
 #pragma unroll
             for (int n = 0; n < 16; n += 4) {
               *reinterpret_cast<float4*>(mine + n) =
@@ -961,25 +981,30 @@ __global__ void __launch_bounds__(tc_threads<MT>(), tc_ctas_per_sm<MT>()) tc_mm_
             }
           }
         }
-      } else if (t < ntl) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(dempty + db));
+      } else {
         // tile t of the unit, chunks of 16 tokens c with c % kSets == set
-        const int hrow = (2 * it.u + t) * kTcRows + row;
-        float* y = p.y_out + it.slice * p.y_sstride + (int64_t)it.slot0 * p.y_ld + hrow;
+        if (t < ntl) {
+          const int hrow = (2 * u + t) * kTcRows + row;
+          float* y = p.y_out + (item % p.ks) * p.y_sstride + (int64_t)p.gt.slot0[gi] * p.y_ld + hrow;
 #pragma unroll 1
-        for (int c = set; c < MT / 16; c += kSets) {
-          const int tok0 = 16 * c;
-          if (tok0 >= ntok) break;  // warp-uniform
-          uint32_t v[16];
-          tc_ld16(dcol + t * MT + tok0, v);
-          tc_wait_ld16(v);
+          for (int c = set; c < MT / 16; c += kSets) {
+            const int tok0 = 16 * c;
+            if (tok0 >= ntok) break;  // warp-uniform
+            uint32_t v[16];
+            tc_ld16(dcol + t * MT + tok0, v);
+            tc_wait_ld16(v);
 #pragma unroll
-          for (int n = 0; n < 16; ++n)
-            if (tok0 + n < ntok) y[(int64_t)(tok0 + n) * p.y_ld] = __uint_as_float(v[n]);
+            for (int n = 0; n < 16; ++n)
+              if (tok0 + n < ntok) y[(int64_t)(tok0 + n) * p.y_ld] = __uint_as_float(v[n]);
+          }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(dempty + db));
       }
-      tc_fence_before();
-      __syncwarp();
-      tc_arrive_lane0(smem_u32(dempty + db), lane);
       rd.next(kDBufs);
     }
   }
