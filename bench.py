@@ -380,29 +380,32 @@ def run_ours(a):
     tokens_s = a.batch / (ms / 1e3)
 
     # dominant kernel: routed LUT matmuls (gate/up + down), per-launch CUDA events
-    n_active = []
-    for m, x in zip(moes, xs):
-        ids, _, _ = router(x, m.router_w, K, renorm=W["RENORM"], shared_gate=m.shared is not None)
-        n_active.append(int(torch.unique(ids).numel()))
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in moes]
-    for ev in evs:  # torch creates the CUDA event on its first record
-        for e in ev:
-            e.record()
-    torch.cuda.synchronize()
-    import ctypes as C
-    t_gu, t_dn, reps = 0.0, 0.0, 5
-    for _ in range(reps):
-        for m, x, o, ev in zip(moes, xs, outs, evs):
-            handles = (C.c_void_p * 4)(*[e.cuda_event for e in ev])
-            m._args.prof_events = C.cast(handles, C.c_void_p)
-            m.forward(x, out=o)
-            m._args.prof_events = None
+    def routed_times(xs_, outs_):
+        """(mean gate/up ms, mean down ms, active experts per layer) over the layers."""
+        import ctypes as C
+        n_act = []
+        for m, x in zip(moes, xs_):
+            ids, _, _ = router(x, m.router_w, K, renorm=W["RENORM"], shared_gate=m.shared is not None)
+            n_act.append(int(torch.unique(ids).numel()))
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in moes]
+        for ev in evs:  # torch creates the CUDA event on its first record
+            for e in ev:
+                e.record()
         torch.cuda.synchronize()
-        for ev in evs:
-            t_gu += ev[0].elapsed_time(ev[1])
-            t_dn += ev[2].elapsed_time(ev[3])
-    t_gu /= reps * len(moes)
-    t_dn /= reps * len(moes)
+        gu, dn, reps = 0.0, 0.0, 5
+        for _ in range(reps):
+            for m, x, o, ev in zip(moes, xs_, outs_, evs):
+                handles = (C.c_void_p * 4)(*[e.cuda_event for e in ev])
+                m._args.prof_events = C.cast(handles, C.c_void_p)
+                m.forward(x, out=o)
+                m._args.prof_events = None
+            torch.cuda.synchronize()
+            for ev in evs:
+                gu += ev[0].elapsed_time(ev[1])
+                dn += ev[2].elapsed_time(ev[3])
+        return gu / (reps * len(moes)), dn / (reps * len(moes)), n_act
+
+    t_gu, t_dn, n_active = routed_times(xs, outs)
     bpw = fmt.bytes_per_weight()
     key = (fmt.kind, fmt.bits, fmt.group, fmt.tier if fmt.kind != "b" else 0)
     na = sum(n_active) / len(n_active)
@@ -410,6 +413,44 @@ def run_ours(a):
     b_dn = na * Hh * Ii * bpw
     achieved = (b_gu + b_dn) / ((t_gu + t_dn) / 1e3) / 1e9
     peak, peak_kind = peaks()
+
+    # config 2's other decode point: batch 1, the same stack as its own CUDA graph
+    batch1 = None
+    if a.batch != 1:
+        x1 = make_inputs(a.layers, 1, rank, dev, Hh, fmt.compute_dtype)
+        o1 = [torch.empty_like(x) for x in x1]
+
+        def step1():
+            for m, x, o in zip(moes, x1, o1):
+                m.forward(x, out=o)
+        step1()
+        torch.cuda.synchronize()
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            step1()
+        for _ in range(a.warmup):
+            g1.replay()
+        n1 = max(10, min(a.steps, 100))
+        e0.record()
+        for _ in range(n1):
+            g1.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms1 = e0.elapsed_time(e1) / n1
+        gu1, dn1, act1 = routed_times(x1, o1)
+        na1 = sum(act1) / len(act1)
+        b1 = na1 * 3 * Ii * Hh * bpw
+        shared_b = moes[0].shared.weight_bytes() if moes[0].shared is not None else 0.0
+        batch1 = {"value": 1.0 / (ms1 / 1e3), "unit": "tokens/s", "ms_per_step": ms1, "steps": n1,
+                  "roofline": {"kernel": "routed LUT matmuls (single-token GEMV), per layer", "bound": "hbm",
+                               "achieved": b1 / ((gu1 + dn1) / 1e3) / 1e9, "peak": peak,
+                               "frac": b1 / ((gu1 + dn1) / 1e3) / 1e9 / peak, "ms_gateup": gu1, "ms_down": dn1,
+                               "bytes_per_layer": b1},
+                  "layer_roofline": {"what": "whole layer step time against its weight bytes (routed experts, "
+                                             "dense shared expert, router)",
+                                     "bytes_per_layer": b1 + shared_b + (Ee + 1) * Hh * 2,
+                                     "frac": (b1 + shared_b + (Ee + 1) * Hh * 2) / (ms1 / a.layers / 1e3) / 1e9
+                                     / peak}}
 
     # e2e through the public API: pinned host inputs -> device -> forward -> host
     e2e = None
@@ -467,7 +508,7 @@ def run_ours(a):
                      TRAFFIC_RATIOS else None,
                      "bytes_per_layer": b_gu + b_dn, "ms_gateup": t_gu, "ms_down": t_dn,
                      "active_experts": na, "active_experts_per_layer": n_active[:4]},
-        "cpu_baseline": cpu, "e2e": e2e,
+        "cpu_baseline": cpu, "e2e": e2e, "batch1": batch1,
         "gpu_launches": a.steps * a.layers * per_layer_launches,
         "clocks": clocks,
     }
@@ -806,7 +847,7 @@ def qwen15_moe_config(layers: int, quant: dict, dtype: str) -> dict:
 
 def lut_quant_config(fmt) -> dict:
     """The checkpoint's quantization_config for the LUT plugin (block_lut_b200.quant_method.LUTConfig)."""
-    q = {"quant_method": "lut", "code_type": "BLOCKLUT"}
+    q = {"quant_method": "lut", "code_type": "BLOCKLUT", "release_canonical": True}
     if fmt.kind == "b":
         q.update({"codebook_scope": "row_block", "index_bits": fmt.bits, "lut_block": fmt.group})
     elif fmt.kind == "nested":

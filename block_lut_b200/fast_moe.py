@@ -10,12 +10,17 @@ the tensors' storage and version, like the reference's id-keyed cache).
 """
 from __future__ import annotations
 
+from collections import OrderedDict
+
 import torch
 
 from .formats import LUTFormat, QuantizedMatrix
 from .moe import LUTExperts, LUTMoELayer
 
-_CACHE: dict = {}
+# Tiled layers by weight stack, least recently used first; a model's layers
+# each keep their entry while fewer than _CACHE_MAX stacks are in use.
+_CACHE: "OrderedDict" = OrderedDict()
+_CACHE_MAX = 256
 
 
 def _key(*ts):
@@ -26,9 +31,11 @@ def r8_layer(w13_weight, w13_absmax, w2_weight, w2_absmax, codebook, top_k: int,
     """Tiled ``LUTMoELayer`` for reference-format stacks (cached)."""
     key = _key(w13_weight, w13_absmax, w2_weight, w2_absmax, codebook) + (top_k, tier)
     layer = _CACHE.get(key)
-    if layer is None:
-        if len(_CACHE) > 64:
-            _CACHE.clear()
+    if layer is not None:
+        _CACHE.move_to_end(key)
+    else:
+        while len(_CACHE) >= _CACHE_MAX:
+            _CACHE.popitem(last=False)
         fmt = LUTFormat("r8", 8, 128, tier)
         e_n, two_i, h = w13_weight.shape
         cb = codebook.to(device=w13_weight.device, dtype=torch.bfloat16).contiguous()

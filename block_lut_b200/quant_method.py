@@ -75,6 +75,8 @@ class LUTConfig(_QCBase):
         nested = kwargs.get("nested")
         self.nested = dict(nested) if nested else None
         self.tier = int(kwargs.get("tier", 0))
+        # free the canonical expert parameters once the kernels' tiled copy exists
+        self.release_canonical = bool(kwargs.get("release_canonical", False))
         print(f"[LUT] LUTConfig init: code_type={code_type}, lut_path={self.lut_path}, "
               f"scope={self.codebook_scope}, kwargs keys={list(kwargs.keys())}", file=sys.stderr)
 
@@ -192,6 +194,7 @@ class LUTFusedMoEMethod(_MoEBase):
                 self._load_absmax(layer, npz_path)
         layer._lut_codebook_loaded = True
         layer._blut = None  # built on first apply (after any later weight copies)
+        layer._blut_experts = None
 
     def _load_absmax(self, layer, npz_path):
         """Absmax arrays keyed by HF ``.weight`` names (quant_method.py:189-222)."""
@@ -219,6 +222,24 @@ class LUTFusedMoEMethod(_MoEBase):
         cached = getattr(layer, "_blut", None)
         if cached is not None and cached.top_k == top_k:
             return cached
+        experts = getattr(layer, "_blut_experts", None)
+        if experts is None:
+            experts = self._tile_experts(layer)
+            layer._blut_experts = experts
+            if self.quant_config.release_canonical:
+                # the tiled copy is the only one the kernels read: give the
+                # canonical parameters' memory back (vLLM cannot reload into
+                # them afterwards)
+                for name in ("w13_weight", "w2_weight", "w13_absmax", "w2_absmax", "w13_tables", "w2_tables",
+                             "w13_residual", "w2_residual", "w13_refine", "w2_refine"):
+                    prm = getattr(layer, name, None)
+                    if prm is not None:
+                        prm.data = torch.empty(0, dtype=prm.dtype, device=prm.device)
+        layer._blut = LUTMoELayer(experts, top_k)
+        return layer._blut
+
+    def _tile_experts(self, layer) -> LUTExperts:
+        """The layer's experts in the tiled layout of the kernels (a copy of the canonical parameters)."""
         f = self.fmt
         e_n, two_i = layer.w13_weight.shape[:2]
         h_n = layer.w2_weight.shape[1]
@@ -239,8 +260,7 @@ class LUTFusedMoEMethod(_MoEBase):
                                   layer.w2_residual[e] if nested else None,
                                   layer.w2_refine[e] if nested else None) for e in range(e_n)]
             experts = LUTExperts.from_quantized(w13, w2)
-        layer._blut = LUTMoELayer(experts, top_k)
-        return layer._blut
+        return experts
 
     # ----------------------------------------------------------- forward --
     def apply(self, layer, x, topk_weights, topk_ids, **kwargs):

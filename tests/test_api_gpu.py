@@ -135,6 +135,23 @@ def test_quant_method_create_weights_format_b():
     ref = O.moe_forward(x.float().cpu().numpy(), ids, tw, W13, W2, act_dtype="f16")
     check_layer(out, ref, torch.float16, "quant_method format b")
 
+    # release_canonical: the same layer, its canonical parameters freed once tiled
+    cfg2 = LUTConfig.from_config({"quant_method": "lut", "code_type": "BLOCKLUT", "codebook_scope": "row_block",
+                                  "index_bits": 4, "lut_block": 64, "release_canonical": True})
+    m2, layer2 = LUTFusedMoEMethod(cfg2), torch.nn.Module()
+    m2.create_weights(layer2, E, H, I, torch.float16)
+    for name in ("w13_weight", "w13_tables", "w2_weight", "w2_tables"):
+        getattr(layer2, name).data.copy_(getattr(layer, name).data)
+    m2.process_weights_after_loading(layer2)
+    out2 = m2.apply(layer2, x, cuda(tw), cuda(ids))
+    assert torch.equal(out2, out)
+    assert layer2.w13_weight.numel() == 0 and layer2.w2_tables.numel() == 0
+    # another top-k is served from the kept tiled experts
+    ids1, tw1 = routing_inputs(rng, 5, E, 1)
+    out1 = m2.apply(layer2, x, cuda(tw1), cuda(ids1))
+    check_layer(out1, O.moe_forward(x.float().cpu().numpy(), ids1, tw1, W13, W2, act_dtype="f16"), torch.float16,
+                "quant_method released, top-1")
+
 
 @pytest.mark.parametrize("m,k", [(2816, 2048), (2048, 1408), (64, 1000)])
 def test_lut_gemv(m, k):

@@ -70,8 +70,10 @@ QM.LUTFusedMoEMethod.apply = apply
 from vllm import LLM, SamplingParams
 d = tempfile.mkdtemp()
 fmt = LUTFormat("b", 4, 64)
+qc = bench.lut_quant_config(fmt)
+qc["release_canonical"] = False  # the recorder reads the experts' parameters after the first calls
 with open(os.path.join(d, "config.json"), "w") as f:
-    json.dump(bench.qwen15_moe_config(2, bench.lut_quant_config(fmt), "float16"), f)
+    json.dump(bench.qwen15_moe_config(2, qc, "float16"), f)
 llm = LLM(model=d, quantization="lut", load_format="dummy", skip_tokenizer_init=True, max_model_len=256,
           gpu_memory_utilization=0.3, max_num_seqs=4, dtype="float16", enforce_eager=True, seed=0)
 prompts = [{"prompt_token_ids": list(range(1000 + 17 * i, 1032 + 17 * i))} for i in range(2)]
