@@ -362,63 +362,75 @@ __global__ void __launch_bounds__(256) splitk_silu_kernel(const float* __restric
 }
 
 // -------------------------------------------------------------- combine ---
-// out[t] = sum_j w[t,j] * y[slot(t,j)] (+ g_t * y_shared[t]), fp32, one rounding.
-// Expert outputs computed in K slices are summed slice by slice first (in
-// slice order, so the result does not depend on which slice finished first).
-// Four slices' loads are in flight at a time; the additions stay in order.
+// out[t] = sum_j w[t,j] * y[slot(t,j)] (+ g_t * y_shared[t]), fp32, one
+// rounding to the output type.
 __device__ __forceinline__ void add4(float4& v, const float4& w) {
   v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
 }
-__device__ __forceinline__ float4 sum_slices(const float* p, int ks, int64_t stride) {
-  float4 v = *reinterpret_cast<const float4*>(p);
-  int s = 1;
-  for (; s + 7 < ks; s += 8) {  // eight slices' loads in flight, added in slice order
-    float4 w[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) w[i] = *reinterpret_cast<const float4*>(p + (s + i) * stride);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) add4(v, w[i]);
-  }
-  for (; s + 3 < ks; s += 4) {
-    float4 w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) w[i] = *reinterpret_cast<const float4*>(p + (s + i) * stride);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) add4(v, w[i]);
-  }
-  for (; s < ks; ++s) add4(v, *reinterpret_cast<const float4*>(p + s * stride));
-  return v;
-}
-
+// One CTA per (token, 128 columns).  The rows to add are
+// the routed slots' split-K slices (weighted by the slot's routing weight)
+// and the shared expert's slices (weighted by its gate, or 1); eight warps
+// take every eighth row, one float4 column per lane, with four rows' loads
+// in flight per warp, and the warps' sums are added in warp order.  Every
+// call adds the same rows in the same order, so results are deterministic.
+constexpr int kCombineWarps = 8;
+constexpr int kCombineCols = 128;
 template <bool BF16>
-__global__ void __launch_bounds__(64) combine_kernel(const float* __restrict__ y, const float* __restrict__ ys,
-                                                      const float* __restrict__ tw, const int* __restrict__ tk_slot,
-                                                      const float* __restrict__ sg, int top_k, int hidden,
-                                                      int shared_mode, void* __restrict__ out_v, int out_f32,
-                                                      int ks_r, int64_t ystride, int ks_s, int64_t ysstride) {
+__global__ void __launch_bounds__(kCombineWarps * 32) combine_kernel(
+    const float* __restrict__ y, const float* __restrict__ ys, const float* __restrict__ tw,
+    const int* __restrict__ tk_slot, const float* __restrict__ sg, int top_k, int hidden, int shared_mode,
+    void* __restrict__ out_v, int out_f32, int ks_r, int64_t ystride, int ks_s, int64_t ysstride) {
   const int t = blockIdx.x;
-  for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < hidden; h += gridDim.y * blockDim.x * 4) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < top_k; ++j) {
-      const int slot = tk_slot[(int64_t)t * top_k + j];
-      if (slot < 0) continue;
-      const float w = tw[(int64_t)t * top_k + j];
-      const float4 v = sum_slices(y + (int64_t)slot * hidden + h, ks_r, ystride);
-      acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y * kCombineCols + lane * 4;
+  const int nr = top_k * ks_r;
+  const int rows = nr + (shared_mode >= 0 ? ks_s : 0);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (h < hidden) {
+    for (int r0 = warp; r0 < rows; r0 += 4 * kCombineWarps) {
+      float4 v[4];
+      float w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = r0 + i * kCombineWarps;
+        w[i] = 0.f;
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r >= rows) continue;
+        if (r < nr) {
+          const int j = r / ks_r, sl = r - j * ks_r;
+          const int slot = tk_slot[(int64_t)t * top_k + j];
+          if (slot < 0) continue;
+          w[i] = tw[(int64_t)t * top_k + j];
+          v[i] = *reinterpret_cast<const float4*>(y + sl * ystride + (int64_t)slot * hidden + h);
+        } else {
+          const int sl = r - nr;
+          w[i] = shared_mode == 1 ? sg[t] : 1.f;
+          v[i] = *reinterpret_cast<const float4*>(ys + sl * ysstride + (int64_t)t * hidden + h);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc.x = fmaf(w[i], v[i].x, acc.x);
+        acc.y = fmaf(w[i], v[i].y, acc.y);
+        acc.z = fmaf(w[i], v[i].z, acc.z);
+        acc.w = fmaf(w[i], v[i].w, acc.w);
+      }
     }
-    if (shared_mode >= 0) {
-      const float g = shared_mode == 1 ? sg[t] : 1.f;
-      const float4 v = sum_slices(ys + (int64_t)t * hidden + h, ks_s, ysstride);
-      acc.x += g * v.x; acc.y += g * v.y; acc.z += g * v.z; acc.w += g * v.w;
-    }
-    if (out_f32) {
-      *reinterpret_cast<float4*>(static_cast<float*>(out_v) + (int64_t)t * hidden + h) = acc;
-    } else {
-      uint2 o;
-      o.x = uint32_t(f32_to_act<BF16>(acc.x)) | (uint32_t(f32_to_act<BF16>(acc.y)) << 16);
-      o.y = uint32_t(f32_to_act<BF16>(acc.z)) | (uint32_t(f32_to_act<BF16>(acc.w)) << 16);
-      *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out_v) + (int64_t)t * hidden + h) = o;
-    }
+  }
+  __shared__ float4 part[kCombineWarps][32];
+  part[warp][lane] = acc;
+  __syncthreads();
+  if (warp != 0 || h >= hidden) return;
+  acc = part[0][lane];
+#pragma unroll
+  for (int i = 1; i < kCombineWarps; ++i) add4(acc, part[i][lane]);
+  if (out_f32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(out_v) + (int64_t)t * hidden + h) = acc;
+  } else {
+    uint2 o;
+    o.x = uint32_t(f32_to_act<BF16>(acc.x)) | (uint32_t(f32_to_act<BF16>(acc.y)) << 16);
+    o.y = uint32_t(f32_to_act<BF16>(acc.z)) | (uint32_t(f32_to_act<BF16>(acc.w)) << 16);
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out_v) + (int64_t)t * hidden + h) = o;
   }
 }
 
@@ -902,15 +914,10 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
 
   // 6. combine
   const int smode = sh ? a.shared_gate_mode : -1;
-  const dim3 cgrid(T, (H + 255) / 256);  // 64 threads x 4 columns per CTA
-  if (bf16)
-    combine_kernel<true><<<cgrid, 64, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
-                                                    a.out_f32, ws.split.ks[1], ws.y_sstride, ws.split.ks[3],
-                                                    ws.ys_sstride);
-  else
-    combine_kernel<false><<<cgrid, 64, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out,
-                                                     a.out_f32, ws.split.ks[1], ws.y_sstride, ws.split.ks[3],
-                                                     ws.ys_sstride);
+  const dim3 cgrid(T, (H + kCombineCols - 1) / kCombineCols);
+  auto kern = bf16 ? combine_kernel<true> : combine_kernel<false>;
+  kern<<<cgrid, kCombineWarps * 32, 0, stream>>>(ws.y, ws.ys, tw, ws.pp.tk_slot, ws.sg, K, H, smode, a.out, a.out_f32,
+                                                 ws.split.ks[1], ws.y_sstride, ws.split.ks[3], ws.ys_sstride);
   return stage_done("combine", stream);
 }
 
