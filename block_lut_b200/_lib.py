@@ -53,6 +53,15 @@ class MoEArgs(C.Structure):
                 ("out_f32", C.c_int32), ("reserved2", C.c_int32)]
 
 
+EP_MAX_RANKS = 8
+EP_HANDLE_BYTES = 64
+
+
+class EpDesc(C.Structure):
+    _fields_ = [("world", C.c_int32), ("rank", C.c_int32), ("capacity", C.c_int32), ("hidden", C.c_int32),
+                ("top_k", C.c_int32), ("dtype", C.c_int32), ("windows", C.c_void_p * EP_MAX_RANKS)]
+
+
 # (name, restype, argtypes) of every exported entry point, in blut.h order.
 _VP, _I32, _I64 = C.c_void_p, C.c_int32, C.c_int64
 SIGNATURES = [
@@ -80,6 +89,17 @@ SIGNATURES = [
     ("blut_moe_check_status", C.c_int, [_VP, _VP]),
     ("blut_moe_launch_count", C.c_int, [C.POINTER(MoEArgs)]),
     ("blut_debug_set_wait_limit", C.c_int, [C.c_uint64]),
+    ("blut_ep_window_bytes", C.c_size_t, [_I32, _I32, _I32, _I32]),
+    ("blut_ep_alloc", C.c_int, [C.c_size_t, C.POINTER(C.c_void_p)]),
+    ("blut_ep_free", C.c_int, [_VP]),
+    ("blut_ep_ipc_handle", C.c_int, [_VP, _VP]),
+    ("blut_ep_ipc_open", C.c_int, [_VP, C.POINTER(C.c_void_p)]),
+    ("blut_ep_ipc_close", C.c_int, [_VP]),
+    ("blut_ep_views", C.c_int, [C.POINTER(EpDesc), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
+    ("blut_ep_dispatch", C.c_int, [C.POINTER(EpDesc), _VP, _VP, _VP, _I32, _VP, _VP, _I32, _VP]),
+    ("blut_ep_combine", C.c_int, [C.POINTER(EpDesc), _I32, _VP, _VP, _I32, _VP]),
+    ("blut_ep_check_status", C.c_int, [C.POINTER(EpDesc), _VP]),
 ]
 
 _lib = None

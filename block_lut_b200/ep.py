@@ -1,4 +1,4 @@
-"""Expert parallelism over the GPUs of one box (torch.distributed, NCCL).
+"""Expert parallelism over the GPUs of one box (one process per GPU).
 
 Experts shard naturally: rank r owns the contiguous expert range
 ``expert_ranges(E, world)[r]`` of every layer (E=60 on 8 ranks -> 8,8,8,8,7,7,7,7),
@@ -6,30 +6,40 @@ dense weights are replicated, and every rank routes its own decode batch.
 One layer:
 
 1. router on the rank's own tokens (global expert ids, weights, shared gate);
-2. dispatch: every token travels to every rank with its k slots rewritten to
-   that rank's local expert ids, -1 where the expert lives elsewhere
-   (fixed T rows per destination, so no count exchange is needed);
-   three ``all_to_all_single`` calls (activations, ids, weights);
-3. each rank runs its local experts on the N*T received tokens in one
-   ``blut_moe_forward`` (empty slots are skipped) with fp32 partial sums;
-4. combine: ``all_to_all_single`` sends the partials back; the owner sums the
-   N partials and adds its shared expert, which ran on a side stream beside
-   the exchanges and the local experts (it needs only the rank's own tokens).
+2. dispatch: each token row goes only to the ranks owning one of its k
+   experts, with its slots rewritten to that rank's local expert ids (-1 for
+   an expert that lives elsewhere); a rank's rows for one destination keep
+   token order;
+3. each rank runs its local experts on the rows it received, in one
+   ``blut_moe_forward`` (empty slots are skipped), with fp32 outputs;
+4. combine: every token's output rows come back from its owners and are
+   summed in rank order, plus the shared expert (run on a side stream beside
+   the exchange, on the rank's own tokens), with one rounding.
 
-These are the message shapes of the reference's only EP code (the DeepSeek
-remote code's dispatch/combine all_to_all, models/deepseek/modeling_deepseek.py:604-660).
-The exchange functions are device-agnostic (CPU tensors under gloo in the
-tests); the expert compute is the CUDA path.
+This is the exchange of the reference's only EP code (the DeepSeek remote
+code's dispatch/combine, models/deepseek/modeling_deepseek.py:604-660: count
+the rows per rank, exchange the counts, send each row only to its owners).
+Two transports implement it with the same row order and summation order:
+
+* ``PeerExchange`` (the GPU path): ``blut_ep_dispatch`` / ``blut_ep_combine``
+  store and load rows directly in the other GPUs' memory over NVLink, with
+  epoch flags and bounded waits, so a layer has no host synchronisation and
+  the whole step can be captured in a CUDA graph;
+* ``routed_dispatch`` / ``routed_combine``: the same exchange over
+  ``torch.distributed`` collectives (a counts all-to-all, then variable-split
+  all-to-alls), device-agnostic; the gloo tests run it on CPU.
 """
 from __future__ import annotations
 
+import ctypes as C
 from typing import List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .formats import dense_matrix
-from .moe import LUTExperts, LUTMoELayer, SharedExpert, router
+from .moe import LUTExperts, LUTMoELayer, router
 
 
 def expert_ranges(num_experts: int, world: int) -> List[Tuple[int, int]]:
@@ -53,43 +63,208 @@ def owner_tables(num_experts: int, world: int, device) -> Tuple[torch.Tensor, to
     return owner.to(device), local.to(device)
 
 
-def build_dispatch(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, owner: torch.Tensor,
-                   local: torch.Tensor, world: int):
-    """Send buffers [world, T, ...]: x replicated, per-destination local ids (-1 elsewhere), weights."""
-    T, k = ids.shape
+# ------------------------------------------------ collective transport ---
+def route_rows(ids: torch.Tensor, owner: torch.Tensor, local: torch.Tensor, world: int):
+    """Per destination rank d: the own tokens with an expert on d (in token
+    order) and their slots' local ids on d (-1 for experts elsewhere or
+    invalid ids).  The peer kernels place rows by the same rule."""
+    E = owner.shape[0]
     ids_l = ids.long()
-    own = owner[ids_l]                                             # [T, k]
-    loc = local[ids_l]                                             # [T, k]
-    dest = torch.arange(world, device=ids.device, dtype=own.dtype).view(world, 1, 1)
-    send_ids = torch.where(own.unsqueeze(0) == dest, loc.unsqueeze(0), torch.full_like(loc, -1).unsqueeze(0))
-    send_x = x.unsqueeze(0).expand(world, T, x.shape[1]).contiguous()
-    send_w = tw.float().unsqueeze(0).expand(world, T, k).contiguous()
-    return send_x, send_ids.to(torch.int32).contiguous(), send_w
+    valid = (ids_l >= 0) & (ids_l < E)
+    safe = ids_l.clamp(0, E - 1)
+    own = torch.where(valid, owner.long()[safe], torch.full_like(safe, -1))     # [T, k]
+    loc = local.long()[safe]
+    rows, sids = [], []
+    for d in range(world):
+        hit = own == d
+        tok = torch.nonzero(hit.any(dim=1)).flatten()
+        rows.append(tok)
+        sids.append(torch.where(hit[tok], loc[tok], torch.full_like(loc[tok], -1)).to(torch.int32))
+    return rows, sids
 
 
-def exchange(send_x, send_ids, send_w, group=None):
-    """Dispatch all-to-all (equal splits): row block d of each buffer goes to rank d."""
-    recv_x, recv_ids, recv_w = torch.empty_like(send_x), torch.empty_like(send_ids), torch.empty_like(send_w)
-    dist.all_to_all_single(recv_x, send_x, group=group)
-    dist.all_to_all_single(recv_ids, send_ids, group=group)
-    dist.all_to_all_single(recv_w, send_w, group=group)
-    return recv_x, recv_ids, recv_w
+class RoutedState:
+    """What ``routed_combine`` needs from the dispatch of the same layer."""
+
+    def __init__(self, rows, send_splits, recv_splits, num_tokens):
+        self.rows, self.send_splits, self.recv_splits, self.num_tokens = rows, send_splits, recv_splits, num_tokens
 
 
-def combine(partials: torch.Tensor, group=None) -> torch.Tensor:
-    """Combine all-to-all: partials [world, T, H] (block d = tokens of rank d) -> summed [T, H]."""
-    back = torch.empty_like(partials)
-    dist.all_to_all_single(back, partials, group=group)
-    return back.sum(dim=0)
+def routed_dispatch(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, owner: torch.Tensor,
+                    local: torch.Tensor, world: int, group=None):
+    """Counts all-to-all, then each row to its owners only.  Returns the
+    received rows, their local ids and weights (sources in rank order, each
+    source's rows in its token order) and the state for ``routed_combine``."""
+    T, k = ids.shape
+    rows, sids = route_rows(ids, owner, local, world)
+    send_counts = torch.tensor([len(r) for r in rows], dtype=torch.int64)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    send_splits, recv_splits = send_counts.tolist(), recv_counts.tolist()
+    sx = torch.cat([x[r] for r in rows]) if T else x.new_empty(0, x.shape[1])
+    si = torch.cat(sids) if T else ids.new_empty(0, k, dtype=torch.int32)
+    sw = torch.cat([tw.float()[r] for r in rows]) if T else tw.new_empty(0, k, dtype=torch.float32)
+    n = sum(recv_splits)
+    rx = x.new_empty(n, x.shape[1])
+    ri = torch.empty(n, k, dtype=torch.int32, device=x.device)
+    rw = torch.empty(n, k, dtype=torch.float32, device=x.device)
+    for dst, src in ((rx, sx), (ri, si.contiguous()), (rw, sw.contiguous())):
+        dist.all_to_all_single(dst, src, recv_splits, send_splits, group=group)
+    return rx, ri, rw, RoutedState(rows, send_splits, recv_splits, T)
+
+
+def routed_combine(part: torch.Tensor, state: RoutedState, shared: Optional[torch.Tensor] = None,
+                   group=None) -> torch.Tensor:
+    """Sends each received row's fp32 output back to its source, which sums a
+    token's rows in rank order (plus ``shared``): fp32 [T, H]."""
+    H = part.shape[1]
+    back = torch.empty(sum(state.send_splits), H, dtype=torch.float32, device=part.device)
+    dist.all_to_all_single(back, part.float().contiguous(), state.send_splits, state.recv_splits, group=group)
+    out = torch.zeros(state.num_tokens, H, dtype=torch.float32, device=part.device)
+    off = 0
+    for d, r in enumerate(state.rows):
+        out[r] += back[off:off + len(r)]
+        off += len(r)
+    if shared is not None:
+        out += shared
+    return out
+
+
+# ------------------------------------------------------ peer transport ---
+class _DevArray:
+    """A device buffer seen through __cuda_array_interface__ (no copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """The exchange window of this rank and the mapped windows of its peers.
+
+    One window serves every layer (the flags order each layer's use after
+    the previous one on every rank).  ``capacity``: the most tokens a rank
+    sends per layer.  Creating it is collective over ``group`` (the IPC
+    handles travel by ``all_gather_object``); so is ``close``."""
+
+    _count = 0
+
+    def __init__(self, capacity: int, hidden: int, top_k: int, dtype: torch.dtype, device, group=None):
+        lib = _lib.lib()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _lib.EP_MAX_RANKS:
+            raise ValueError(f"the peer exchange spans at most {_lib.EP_MAX_RANKS} ranks")
+        self.device = torch.device(device)
+        self.capacity, self.hidden, self.top_k, self.dtype = int(capacity), int(hidden), int(top_k), dtype
+        nbytes = lib.blut_ep_window_bytes(self.world, self.capacity, self.hidden, self.top_k)
+        if nbytes == 0:
+            raise ValueError("blut_ep_window_bytes rejected the sizes")
+        self._own = C.c_void_p()
+        self._peers = []
+        with torch.cuda.device(self.device):
+            _lib.check(lib.blut_ep_alloc(nbytes, C.byref(self._own)), "ep alloc")
+            h = (C.c_ubyte * _lib.EP_HANDLE_BYTES)()
+            _lib.check(lib.blut_ep_ipc_handle(self._own, h), "ep ipc handle")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(h), group=group)
+            d = _lib.EpDesc()
+            d.world, d.rank, d.capacity, d.hidden, d.top_k = self.world, self.rank, self.capacity, self.hidden, self.top_k
+            d.dtype = _lib.BF16 if dtype == torch.bfloat16 else _lib.F16
+            for r, hb in enumerate(handles):
+                if r == self.rank:
+                    d.windows[r] = self._own.value
+                    continue
+                p = C.c_void_p()
+                buf = (C.c_ubyte * _lib.EP_HANDLE_BYTES).from_buffer_copy(hb)
+                _lib.check(lib.blut_ep_ipc_open(buf, C.byref(p)), f"ep ipc open (rank {r})")
+                self._peers.append(p)
+                d.windows[r] = p.value
+            self.desc = d
+            ptrs = [C.c_void_p() for _ in range(4)]
+            _lib.check(lib.blut_ep_views(C.byref(d), *[C.byref(p) for p in ptrs]), "ep views")
+        n = self.world * self.capacity
+        xs = torch.as_tensor(_DevArray(ptrs[0].value, (n, self.hidden), "<i2"), device=self.device)
+        self.recv_x = xs.view(dtype)
+        self.recv_ids = torch.as_tensor(_DevArray(ptrs[1].value, (n, self.top_k), "<i4"), device=self.device)
+        self.recv_w = torch.as_tensor(_DevArray(ptrs[2].value, (n, self.top_k), "<f4"), device=self.device)
+        self.ret = torch.as_tensor(_DevArray(ptrs[3].value, (n, self.hidden), "<f4"), device=self.device)
+        PeerExchange._count += 1  # same sequence on every rank: names this window's close counter
+        self._close_key = f"blut_ep_close/{PeerExchange._count}"
+        dist.barrier(group=group)
+
+    def dispatch(self, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, owner: torch.Tensor,
+                 local: torch.Tensor, stream=None) -> None:
+        T = x.shape[0]
+        if T > self.capacity or x.dtype != self.dtype or x.shape[1] != self.hidden or ids.shape[1] != self.top_k:
+            raise ValueError("dispatch: rows do not fit the exchange window")
+        x, ids, tw = x.contiguous(), ids.to(torch.int32).contiguous(), tw.float().contiguous()
+        with _lib.on_device(x):
+            _lib.check(_lib.lib().blut_ep_dispatch(C.byref(self.desc), x.data_ptr(), ids.data_ptr(), tw.data_ptr(), T,
+                                                   owner.data_ptr(), local.data_ptr(), owner.shape[0],
+                                                   _lib.stream_ptr(stream)), "ep dispatch")
+
+    def combine(self, num_tokens: int, out: torch.Tensor, shared: Optional[torch.Tensor] = None,
+                stream=None) -> torch.Tensor:
+        if out.shape != (num_tokens, self.hidden) or not out.is_contiguous():
+            raise ValueError("combine: out must be a contiguous [T, hidden] tensor")
+        out_f32 = out.dtype == torch.float32
+        if not out_f32 and out.dtype != self.dtype:
+            raise ValueError("combine: out must be fp32 or the window's dtype")
+        if shared is not None and (shared.dtype != torch.float32 or not shared.is_contiguous()):
+            raise ValueError("combine: shared must be contiguous fp32")
+        with _lib.on_device(out):
+            _lib.check(_lib.lib().blut_ep_combine(C.byref(self.desc), num_tokens,
+                                                  None if shared is None else shared.data_ptr(), out.data_ptr(),
+                                                  int(out_f32), _lib.stream_ptr(stream)), "ep combine")
+        return out
+
+    def check_status(self, stream=None) -> None:
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().blut_ep_check_status(C.byref(self.desc), _lib.stream_ptr(stream)), "ep status")
+
+    def close(self, drain_s: float = 120.0) -> None:
+        """Unmaps the peers' windows and frees this rank's once no rank can
+        touch it any more.  Every rank calls it, on success and on failure
+        paths alike: each first finishes its own queued work, then counts
+        itself closed in the process group's store, and frees its window when
+        every rank has counted in, or after ``drain_s`` seconds (a rank that
+        failed does not count in; by then its peers have drained what they
+        had queued, since each of their steps starts with a collective that
+        the failed rank never joins, and a wait for a silent peer gives up
+        after the wait limit and makes later waits give up at once)."""
+        import time
+
+        if self._own is None:
+            return
+        lib = _lib.lib()
+        try:
+            torch.cuda.synchronize(self.device)
+        finally:
+            store = dist.distributed_c10d._get_default_store()
+            store.add(self._close_key, 1)
+            t0 = time.monotonic()
+            while int(store.add(self._close_key, 0)) < self.world and time.monotonic() - t0 < drain_s:
+                time.sleep(0.02)
+            with torch.cuda.device(self.device):
+                for p in self._peers:
+                    lib.blut_ep_ipc_close(p)
+                self._peers = []
+                lib.blut_ep_free(self._own)
+            self._own = None
 
 
 class EPMoELayer:
-    """One MoE layer, expert-parallel: this rank's experts + replicated router and shared expert."""
+    """One MoE layer, expert-parallel: this rank's experts + replicated router
+    and shared expert; the rows move through ``exchange`` (a ``PeerExchange``
+    shared by all layers of the model)."""
 
     def __init__(self, local_experts: LUTExperts, num_experts: int, top_k: int, router_w: torch.Tensor,
-                 shared: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, renorm: bool = False, group=None):
-        self.world = dist.get_world_size(group)
-        self.group = group
+                 exchange: PeerExchange, shared: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                 renorm: bool = False):
+        self.xchg = exchange
+        self.world = exchange.world
         self.top_k = top_k
         self.renorm = renorm
         self.local = LUTMoELayer(local_experts, top_k)
@@ -97,40 +272,49 @@ class EPMoELayer:
         self.num_experts = num_experts
         self.owner, self.local_id = owner_tables(num_experts, self.world, router_w.device)
         self.shared = None
+        self._zero_ids = None
+        self._side = None
         if shared is not None:
             s13, s2 = shared
             ex = LUTExperts.from_quantized([dense_matrix(s13)], [dense_matrix(s2)])
             self.shared = LUTMoELayer(ex, 1)
             self.shared.ws_slot = 1  # runs concurrently with self.local: its own workspace
-            self._zero_ids = None
-            self._side = None
+
+    def launch_count(self, num_tokens: int) -> int:
+        """This library's kernels per forward: router (logits + top-k),
+        dispatch, local experts, shared expert, combine."""
+        n = 2 + 1 + self.local.launch_count(self.world * self.xchg.capacity, caller_routing=True) + 1
+        if self.shared is not None:
+            n += self.shared.launch_count(num_tokens, caller_routing=True)
+        return n
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         T, H = x.shape
         ids, tw, sg = router(x, self.router_w, self.top_k, self.renorm, shared_gate=self.shared is not None)
         shared_out = None
+        main = torch.cuda.current_stream(x.device)
         if self.shared is not None:
             # the shared expert needs only this rank's tokens: it runs on a side
-            # stream while the tokens are exchanged and the local experts run;
+            # stream while the rows are exchanged and the local experts run;
             # every tensor it touches was made on the main stream, which waits
-            # for the side stream before returning
+            # for the side stream before the combine reads its output
             if self._zero_ids is None or self._zero_ids.shape[0] != T:
                 self._zero_ids = torch.zeros(T, 1, dtype=torch.int32, device=x.device)
             if self._side is None:
                 self._side = torch.cuda.Stream(device=x.device)
-            main = torch.cuda.current_stream(x.device)
             shared_out = torch.empty(T, H, dtype=torch.float32, device=x.device)
             self._side.wait_stream(main)
             with torch.cuda.stream(self._side):
                 self.shared.forward(x, self._zero_ids, sg.view(T, 1), out=shared_out, out_f32=True)
-        sx, si, sw = build_dispatch(x, ids, tw, self.owner, self.local_id, self.world)
-        rx, ri, rw = exchange(sx, si, sw, self.group)
-        part = self.local.forward(rx.view(-1, H), ri.view(-1, self.top_k), rw.view(-1, self.top_k), out_f32=True)
-        out = combine(part.view(self.world, T, H), self.group)
+        xc = x if x.dtype == self.xchg.dtype else x.to(self.xchg.dtype)
+        self.xchg.dispatch(xc, ids, tw, self.owner, self.local_id)
+        xg = self.xchg
+        self.local.forward(xg.recv_x, xg.recv_ids, xg.recv_w, out=xg.ret, out_f32=True)
         if shared_out is not None:
             main.wait_stream(self._side)
-            out += shared_out
-        return out.to(x.dtype)
+        out = torch.empty(T, H, dtype=xg.dtype, device=x.device)
+        xg.combine(T, out, shared_out)
+        return out if out.dtype == x.dtype else out.to(x.dtype)
 
     __call__ = forward
 
@@ -143,105 +327,113 @@ def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, 
     H, E, I, TOPK, IS = shp["H"], shp["E"], shp["I"], shp["TOPK"], shp["IS"]
     s, c = expert_ranges(E, world)[rank]
     fmt, layers = build_layers(a.layers, c, s, fmt, dev, shape=dict(shp, IS=0))
-    eps = []
-    g = torch.Generator(device=dev).manual_seed(99)
-    for ex, rw, _ in layers:
-        shared = None
-        if IS > 0:
-            s13 = (torch.randn(2 * IS, H, generator=g, device=dev) * 0.02).to(fmt.compute_dtype)
-            s2 = (torch.randn(H, IS, generator=g, device=dev) * 0.02).to(fmt.compute_dtype)
-            shared = (s13, s2)
-        eps.append(EPMoELayer(ex, E, TOPK, rw if shared is not None else rw[:E].contiguous(),
-                              shared=shared, renorm=shp["RENORM"]))
-    xs = make_inputs(a.layers, a.batch, rank, dev, H, fmt.compute_dtype)
+    xchg = PeerExchange(a.batch, H, TOPK, fmt.compute_dtype, dev)  # one window for every layer
+    try:
+        eps = []
+        g = torch.Generator(device=dev).manual_seed(99)
+        for ex, rw, _ in layers:
+            shared = None
+            if IS > 0:
+                s13 = (torch.randn(2 * IS, H, generator=g, device=dev) * 0.02).to(fmt.compute_dtype)
+                s2 = (torch.randn(H, IS, generator=g, device=dev) * 0.02).to(fmt.compute_dtype)
+                shared = (s13, s2)
+            eps.append(EPMoELayer(ex, E, TOPK, rw if shared is not None else rw[:E].contiguous(), xchg,
+                                  shared=shared, renorm=shp["RENORM"]))
+        xs = make_inputs(a.layers, a.batch, rank, dev, H, fmt.compute_dtype)
+        torch.cuda.synchronize()
+        dist.barrier()  # every rank's layers are built before the first exchange waits for its peers
 
-    outs = [None] * len(eps)
+        outs = [None] * len(eps)
 
-    def step():
-        for i, (m, x) in enumerate(zip(eps, xs)):
-            outs[i] = m.forward(x)
+        def step():
+            for i, (m, x) in enumerate(zip(eps, xs)):
+                outs[i] = m.forward(x)
 
-    for _ in range(max(2, a.warmup)):
-        step()
-    torch.cuda.synchronize()
-    for m in eps:
-        m.local.check_status()
-    # the whole step (routing, exchanges, expert kernels) as one CUDA graph;
-    # every rank captures the same collectives in the same order
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        step()
-    torch.cuda.current_stream().wait_stream(s)
-    torch.cuda.synchronize()
-    dist.barrier()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-    for _ in range(max(1, a.warmup)):
-        graph.replay()
-    torch.cuda.synchronize()
-    dist.barrier()
-    clk = Clocks(torch.cuda.current_device())
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0.record()
-    for _ in range(a.steps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    del graph  # a graph holding NCCL work is released before the process group
-    clocks = clk.stop()
-    ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
-    total_tokens = a.batch * world
-    peak, _ = peaks()
-    # e2e through EPMoELayer.forward: each rank's tokens from pinned host
-    # memory to the device and its layer outputs back, every step
-    xh = [x.cpu().pin_memory() for x in xs]
-    oh = [torch.empty_like(x, device="cpu").pin_memory() for x in xs]
-    xd = [torch.empty_like(x) for x in xs]
+        for _ in range(max(2, a.warmup)):
+            step()
+        torch.cuda.synchronize()
+        xchg.check_status()
+        for m in eps:
+            m.local.check_status()
+        # the whole step (routing, exchanges, expert kernels) as one CUDA graph;
+        # every rank replays the same exchanges in the same order
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(max(1, a.warmup)):
+            graph.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        clk = Clocks(torch.cuda.current_device())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0.record()
+        for _ in range(a.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        del graph  # a graph holding NCCL work is released before the process group
+        clocks = clk.stop()
+        ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = float(ms.item())
+        total_tokens = a.batch * world
+        peak, _ = peaks()
+        # e2e through EPMoELayer.forward: each rank's tokens from pinned host
+        # memory to the device and its layer outputs back, every step
+        xh = [x.cpu().pin_memory() for x in xs]
+        oh = [torch.empty_like(x, device="cpu").pin_memory() for x in xs]
+        xd = [torch.empty_like(x) for x in xs]
 
-    def e2e_step():
-        for m, h_in, d_in, h_out in zip(eps, xh, xd, oh):
-            d_in.copy_(h_in, non_blocking=True)
-            h_out.copy_(m.forward(d_in), non_blocking=True)
-    e2e_step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    for _ in range(a.steps):
+        def e2e_step():
+            for m, h_in, d_in, h_out in zip(eps, xh, xd, oh):
+                d_in.copy_(h_in, non_blocking=True)
+                h_out.copy_(m.forward(d_in), non_blocking=True)
         e2e_step()
-    f1.record()
-    torch.cuda.synchronize()
-    e_ms = torch.tensor([f0.elapsed_time(f1) / a.steps], device=dev)
-    dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-    e_ms = float(e_ms.item())
-    # this library's kernels per step: router (logits + top-k), local experts
-    # on all ranks' tokens, shared expert on the rank's own tokens
-    m0 = eps[0]
-    per_layer = 2 + m0.local.launch_count(world * a.batch, caller_routing=True) + (
-        m0.shared.launch_count(a.batch, caller_routing=True) if m0.shared is not None else 0)
-    if rank == 0:
-        res = {"metric": metric, "value": total_tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
-               "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
-               "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if fmt.kind == "r8" else "f16",
-               "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU Lloyd-encoded; N(0,1) RMS-normalised fp16",
-               "config": {"workload": f"{shp['NAME']}, decode batch {a.batch} per rank",
-                          "layers": a.layers, "global_batch": total_tokens, "experts": E, "top_k": TOPK,
-                          "format": format_name(fmt), "parallelism": f"ep{world}",
-                          "exchange": "NCCL all_to_all_single dispatch (x, ids, w) + combine (fp32 partials)"},
-               "graph": f"CUDA graph of the {a.layers}-layer step, NCCL collectives included",
-               "roofline": None, "cpu_baseline": None,
-               "e2e": {"value": total_tokens / (e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e_ms,
-                       "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs) * world,
-                       "d2h_bytes_per_step": sum(x.numel() * 2 for x in xs) * world,
-                       "path": "EPMoELayer.forward per layer with pinned host I/O on every rank"},
-               "gpu_launches": a.steps * a.layers * per_layer, "clocks": clocks}
-        print(json.dumps(res), flush=True)
-    dist.barrier()
+        torch.cuda.synchronize()
+        dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(a.steps):
+            e2e_step()
+        f1.record()
+        torch.cuda.synchronize()
+        e_ms = torch.tensor([f0.elapsed_time(f1) / a.steps], device=dev)
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e_ms = float(e_ms.item())
+        xchg.check_status()
+        # this library's kernels per step: router (logits + top-k), dispatch,
+        # local experts on the received rows, shared expert, combine
+        per_layer = eps[0].launch_count(a.batch)
+        if rank == 0:
+            res = {"metric": metric, "value": total_tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+                   "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+                   "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if fmt.kind == "r8" else "f16",
+                   "data": "synthetic: Student-t(df=5) std 0.02 weights, GPU Lloyd-encoded; N(0,1) RMS-normalised fp16",
+                   "config": {"workload": f"{shp['NAME']}, decode batch {a.batch} per rank",
+                              "layers": a.layers, "global_batch": total_tokens, "experts": E, "top_k": TOPK,
+                              "format": format_name(fmt), "parallelism": f"ep{world}",
+                              "exchange": "blut_ep_dispatch / blut_ep_combine: each token row stored only in its "
+                                          "owner ranks' windows over NVLink, fp32 output rows loaded back "
+                                          "(no NCCL on the data path)"},
+                   "graph": f"CUDA graph of the {a.layers}-layer step, exchanges included",
+                   "roofline": None, "cpu_baseline": None,
+                   "e2e": {"value": total_tokens / (e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e_ms,
+                           "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs) * world,
+                           "d2h_bytes_per_step": sum(x.numel() * 2 for x in xs) * world,
+                           "path": "EPMoELayer.forward per layer with pinned host I/O on every rank"},
+                   "gpu_launches": a.steps * a.layers * per_layer, "clocks": clocks}
+            print(json.dumps(res), flush=True)
+        dist.barrier()
+    finally:
+        xchg.close()  # every rank, on success and failure alike
     dist.destroy_process_group()

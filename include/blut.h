@@ -5,7 +5,9 @@
  * Every entry point takes plain device pointers, sizes and a cudaStream_t
  * (passed as void*), launches asynchronously on that stream, never allocates,
  * never synchronises the device and returns an int status (0 = ok, < 0 =
- * error, see blut_status_string).  No C++ exceptions cross this boundary.
+ * error, see blut_status_string); the exceptions are the set-up and
+ * diagnostic calls that say so (the expert-parallel window set-up, the
+ * status reads).  No C++ exceptions cross this boundary.
  *
  * Each declaration names the reference interface it replaces
  * (paths inside the hu-jinzhao/block_lut project).
@@ -286,7 +288,9 @@ typedef struct {
   void* out;                /* [T][H]                                           */
   void* const* prof_events; /* NULL, or 4 cudaEvent_t recorded on the stream
                                before/after the routed gate/up launch and
-                               before/after the routed down launch (timing)   */
+                               before/after the routed down launch (timing);
+                               on the single-token path those launches also
+                               carry the shared expert                        */
   int32_t out_f32;          /* 1: out is float32 [T][H] (unrounded partial sums,
                                used by expert parallelism); 0: out is `dtype` */
   int32_t reserved2;
@@ -346,6 +350,76 @@ BLUT_API int blut_moe_launch_count(const blut_moe_args* args);
  * returns BLUT_ERR_TIMEOUT; tests use a tiny limit to exercise that path.
  * Process-wide; not for use while other threads launch. */
 BLUT_API int blut_debug_set_wait_limit(uint64_t ns);
+
+/* ------------------------------------- expert-parallel exchange (EP) ----
+ * Replaces the dispatch / combine all_to_all of the reference's only
+ * expert-parallel code (models/deepseek/modeling_deepseek.py:604-660: count
+ * the rows per rank, exchange the counts, send each token row only to the
+ * ranks owning one of its experts, return the outputs).  One process per
+ * GPU; each rank owns a contiguous range of every layer's experts.  The rows
+ * move by direct stores to and loads from the other GPUs' memory (NVLink),
+ * with no host synchronisation, so a layer can be captured in a CUDA graph.
+ *
+ * Setup (once, not on the hot path; these are the entry points that
+ * allocate or synchronise): every rank allocates a window of
+ * blut_ep_window_bytes with blut_ep_alloc (zeroed), shares the
+ * BLUT_EP_HANDLE_BYTES handle from blut_ep_ipc_handle with the other ranks
+ * (out of band, e.g. torch.distributed.all_gather_object), and maps theirs
+ * with blut_ep_ipc_open.  One window serves every layer of the model.
+ *
+ * Per layer, on every rank (with or without rows for a peer):
+ *   blut_ep_dispatch  rows to their owners; returns with this rank's window
+ *                     holding every source's rows (blut_ep_views: x, ids, w)
+ *   blut_moe_forward  on the window's world*capacity rows with the window's
+ *                     ids and weights (-1 ids are empty slots), out_f32 = 1,
+ *                     out = the window's `ret` region
+ *   blut_ep_combine   out[t] = sum over owners of their rows for token t
+ *                     (+ shared_out[t]), one rounding
+ * Waits are bounded (blut_debug_set_wait_limit); a wait that gives up makes
+ * blut_ep_check_status return BLUT_ERR_TIMEOUT. */
+#define BLUT_EP_MAX_RANKS 8
+#define BLUT_EP_HANDLE_BYTES 64
+
+typedef struct {
+  int32_t world;    /* ranks in the exchange, 1 .. BLUT_EP_MAX_RANKS            */
+  int32_t rank;     /* this rank                                               */
+  int32_t capacity; /* most tokens a rank sends per layer (its largest batch)  */
+  int32_t hidden;   /* row length, a multiple of 8                             */
+  int32_t top_k;    /* experts per token, 1 .. 64                              */
+  int32_t dtype;    /* BLUT_F16 / BLUT_BF16 of the rows                        */
+  void* windows[BLUT_EP_MAX_RANKS]; /* every rank's window as mapped in this
+                                       process (windows[rank]: the own one)    */
+} blut_ep_desc;
+
+/* Window bytes for these sizes, 0 if a size is out of range. */
+BLUT_API size_t blut_ep_window_bytes(int world, int capacity, int hidden, int top_k);
+/* cudaMalloc + zero fill (synchronises the device). */
+BLUT_API int blut_ep_alloc(size_t bytes, void** ptr);
+BLUT_API int blut_ep_free(void* ptr);
+/* The window's IPC handle (BLUT_EP_HANDLE_BYTES bytes), and mapping /
+ * unmapping another process's window by its handle. */
+BLUT_API int blut_ep_ipc_handle(const void* window, void* handle);
+BLUT_API int blut_ep_ipc_open(const void* handle, void** ptr);
+BLUT_API int blut_ep_ipc_close(void* ptr);
+/* Device pointers into the own window: received rows x [world*capacity,
+ * hidden] (dtype), their local expert ids and weights [world*capacity,
+ * top_k], and the expert outputs region ret [world*capacity, hidden] (fp32)
+ * that blut_moe_forward writes.  Any of them may be NULL. */
+BLUT_API int blut_ep_views(const blut_ep_desc* d, void** x, int32_t** ids, float** w, float** ret);
+/* Sends this rank's num_tokens rows (x [T, hidden], global expert ids and
+ * weights [T, top_k]) to the ranks owning their experts: owner[e] = rank of
+ * expert e, local[e] = its index on that rank (device int32 [num_experts]). */
+BLUT_API int blut_ep_dispatch(const blut_ep_desc* d, const void* x, const int32_t* topk_ids,
+                              const float* topk_weights, int num_tokens, const int32_t* owner,
+                              const int32_t* local, int num_experts, void* stream);
+/* out [T, hidden] (dtype, or fp32 with out_f32) = the sum of the owners'
+ * output rows for each of this rank's tokens, plus shared_out [T, hidden]
+ * fp32 when not NULL. */
+BLUT_API int blut_ep_combine(const blut_ep_desc* d, int num_tokens, const float* shared_out, void* out,
+                             int out_f32, void* stream);
+/* Synchronises the stream, returns (and clears) BLUT_ERR_TIMEOUT if a wait of
+ * this rank's exchanges gave up. */
+BLUT_API int blut_ep_check_status(const blut_ep_desc* d, void* stream);
 
 #ifdef __cplusplus
 }

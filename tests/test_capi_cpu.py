@@ -300,3 +300,31 @@ def test_fused_lut_gemv_rejects_other_block_sizes():
     z = torch.zeros(4)
     with pytest.raises(ValueError, match="128"):
         fused_lut_gemv(z, torch.zeros(2, 4, dtype=torch.uint8), z, z, block_size=64)
+
+
+def test_ep_window_layout_and_argument_checks():
+    """The expert-parallel window: a 256-byte header, the slot table, then the
+    received rows, ids, weights and fp32 output rows of every source, each
+    256-aligned; out-of-range sizes give 0 and the entry points refuse bad
+    descriptors before any CUDA call."""
+    lib = _lib.lib()
+
+    def al(v):
+        return (v + 255) // 256 * 256
+
+    for world, cap, hidden, k in ((2, 24, 256, 2), (8, 64, 2048, 8), (3, 5, 8, 1)):
+        o = al(256 + cap * 8 * 4)
+        o = al(o + world * cap * hidden * 2)
+        o = al(o + world * cap * k * 4)
+        o = al(o + world * cap * k * 4)
+        o = al(o + world * cap * hidden * 4)
+        assert lib.blut_ep_window_bytes(world, cap, hidden, k) == o
+    for bad in ((0, 8, 256, 2), (9, 8, 256, 2), (2, 0, 256, 2), (2, 8, 100, 2), (2, 8, 256, 0), (2, 8, 256, 65)):
+        assert lib.blut_ep_window_bytes(*bad) == 0
+    d = _lib.EpDesc()
+    d.world, d.rank, d.capacity, d.hidden, d.top_k, d.dtype = 2, 2, 8, 256, 2, _lib.F16  # rank out of range
+    assert lib.blut_ep_dispatch(C.byref(d), None, None, None, 0, None, None, 4, None) == _lib.BLUT_ERR_INVALID
+    d.rank = 0  # windows missing
+    assert lib.blut_ep_combine(C.byref(d), 0, None, None, 0, None) == _lib.BLUT_ERR_INVALID
+    assert lib.blut_ep_views(C.byref(d), None, None, None, None) == _lib.BLUT_ERR_INVALID
+    assert lib.blut_ep_alloc(0, C.byref(C.c_void_p())) == _lib.BLUT_ERR_INVALID

@@ -1,8 +1,11 @@
-"""Expert-parallel host logic on CPU: two gloo ranks run the dispatch /
-combine exchange of block_lut_b200.ep, with the oracle standing in for the
-CUDA expert compute, and must reproduce the single-process layer output.
-A rank that fails before the exchange makes its peer's collective raise
-(short process-group timeout) instead of hanging."""
+"""Expert-parallel host logic on CPU: gloo ranks run the routed exchange of
+block_lut_b200.ep (a counts all-to-all, then each token row only to the ranks
+owning one of its experts, outputs back to the source and summed in rank
+order), with the oracle standing in for the CUDA expert compute, and must
+reproduce the single-process layer output.  route_rows, the row-placement
+rule the GPU peer kernels follow too, is checked on a hand-made case.  A rank
+that fails before the exchange makes its peer's collective raise (short
+process-group timeout) instead of hanging."""
 import multiprocessing as mp
 import os
 import socket
@@ -69,17 +72,21 @@ def _rank_main(rank, world, port, q, fail_rank, n_exp):
         W13, W2 = _weights(n_exp)
         x, ids, tw = _tokens(rank, n_exp)
         owner, local = ep.owner_tables(n_exp, world, "cpu")
-        sx, si, sw = ep.build_dispatch(torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(tw),
-                                       owner, local, world)
         try:
-            rx, ri, rw = ep.exchange(sx, si, sw)
+            rx, ri, rw, st = ep.routed_dispatch(torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(tw),
+                                                owner, local, world)
         except Exception as exc:  # the peer died: the collective must fail, not hang
             q.put((rank, "collective-error", type(exc).__name__))
             return
-        start = ep.expert_ranges(n_exp, world)[rank][0]
-        part = _local_partial(rx.view(-1, H).numpy(), ri.view(-1, K).numpy(), rw.view(-1, K).numpy(), W13, W2, start)
-        out = ep.combine(torch.from_numpy(part).view(world, T, H))
-        q.put((rank, "ok", out.numpy()))
+        # every received row has at least one slot owned here, and only rows
+        # for this rank's experts arrived
+        ri_np = ri.numpy()
+        assert (ri_np >= 0).any(axis=1).all() if ri_np.size else True
+        start, count = ep.expert_ranges(n_exp, world)[rank]
+        assert ri_np.max(initial=-1) < count
+        part = _local_partial(rx.numpy(), ri_np, rw.numpy(), W13, W2, start)
+        out = ep.routed_combine(torch.from_numpy(part), st)
+        q.put((rank, "ok", (out.numpy(), sum(st.recv_splits), sum(st.send_splits))))
         dist.destroy_process_group()
     except Exception:
         q.put((rank, "raised", traceback.format_exc()))
@@ -119,12 +126,41 @@ def test_ep_dispatch_combine_matches_single_process(world, n_exp):
     assert len({c for _, c in expert_ranges(n_exp, world)}) == (1 if world == 2 else 2)
     res = _run(world, n_exp=n_exp)
     W13, W2 = _weights(n_exp)
+    sent = recv = 0
     for r in range(world):
-        status, out = res[r]
-        assert status == "ok", out
+        status, payload = res[r]
+        assert status == "ok", payload
+        out, n_recv, n_sent = payload
         x, ids, tw = _tokens(r, n_exp)
         ref = O.moe_forward(x, ids, tw, W13, W2, act_dtype="f16")
-        np.testing.assert_allclose(out, ref, rtol=1e-9, atol=1e-12)
+        # the returned rows and their sum are fp32, as on the GPU
+        np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-7)
+        # a row goes once to each distinct owner rank of its experts
+        owners = [{ep_owner(e, n_exp, world) for e in row} for row in ids]
+        assert n_sent == sum(len(o) for o in owners)
+        sent, recv = sent + n_sent, recv + n_recv
+    assert sent == recv
+
+
+def ep_owner(e, n_exp, world):
+    from block_lut_b200.ep import expert_ranges
+    for r, (s, c) in enumerate(expert_ranges(n_exp, world)):
+        if s <= e < s + c:
+            return r
+    raise ValueError(e)
+
+
+def test_route_rows_places_rows_by_owner_in_token_order():
+    import torch
+    from block_lut_b200 import ep
+    owner, local = ep.owner_tables(6, 3, "cpu")      # ranks own experts {0,1}, {2,3}, {4,5}
+    ids = torch.tensor([[0, 5], [2, 3], [4, 1], [7, -1], [3, 3]], dtype=torch.int32)
+    rows, sids = ep.route_rows(ids, owner, local, 3)
+    assert [r.tolist() for r in rows] == [[0, 2], [1, 4], [0, 2]]
+    # slots owned elsewhere (and the invalid ids 7 and -1) become -1
+    assert sids[0].tolist() == [[0, -1], [-1, 1]]
+    assert sids[1].tolist() == [[0, 1], [1, 1]]
+    assert sids[2].tolist() == [[-1, 1], [0, -1]]
 
 
 def test_rank_failure_surfaces_as_error_not_hang():
