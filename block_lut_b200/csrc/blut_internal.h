@@ -58,7 +58,20 @@ struct MoEWs {
   float *part_r, *part_s;      // gate/up partial sums of split K
   int64_t ntmax, sntmax;
   MoESplit split;
+  // single-token path (blut_tok1.cuh); set when tok1_applies
+  bool tok1;
+  int t1_ks[4], t1_bps[4];     // K slices of routed gate/up, routed down, shared gate/up, shared down
+  int* t1_groups;              // [0] routed groups, [1 + g] expert of group g
+  float* t1_gw;                // [g] routing weight
+  int* t1_cnt;                 // gate/up counters [top_k][units] + [shared units], then down [hidden / 128]
+  int t1_ncnt_pair, t1_ncnt;
+  float *t1_part_r, *t1_part_s;  // gate/up slices [group][unit][ks][2][128]
+  uint16_t *t1_act_r, *t1_act_s; // SiLU * up rows [group][inter]
+  float *t1_y_r, *t1_y_s;        // down slices [ks][group][hidden]
 };
+
+// The single-token path applies: one token, every projection in the TC layout.
+bool tok1_applies(const blut_moe_args& a, const MoESplit& s);
 
 int num_sms();
 // Limit of the tcgen05 kernels' bounded device-side waits, in nanoseconds
@@ -115,7 +128,7 @@ int dequant(const blut_mat_desc& d, const blut_canon& c, void* out, cudaStream_t
 int pack_tiled(const blut_mat_desc& d, const blut_canon& c, void* tiled, cudaStream_t stream);
 int encode(const blut_mat_desc& d, const float* w, void* codes, void* tables, void* codes2, void* tables2,
            cudaStream_t stream);
-int encode_r(const void* w, int64_t n, const void* cb, int block_size, void* idx, void* absmax,
+int encode_r(const void* w, int64_t n, const void* cb, int block_size, void* idx, void* absmax, bool f32,
              cudaStream_t stream);
 int blocklut_decompress(void* out, const void* idx, const void* absmax, const void* cb, int64_t num_experts,
                         int64_t elems, int64_t blocks_per_expert, int block_size, cudaStream_t stream);

@@ -3,12 +3,14 @@
 // stream; nothing synchronises the host and nothing allocates.
 #include <algorithm>
 #include <atomic>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
 
 #include "blut_internal.h"
 #include "blut_tc.cuh"
+#include "blut_tok1.cuh"
 
 namespace blut {
 
@@ -17,18 +19,11 @@ namespace blut {
 // 8 warps per CTA; each lane issues all of its 16-byte loads before the FMAs
 // (4 independent accumulators).  Row r < E reads w_main[r]; row E (when
 // w_gate is set) reads the shared-expert gate vector.
+// One warp's fp32 dot product of x and w (H elements); each lane issues all
+// of its 16-byte loads before the FMAs (4 independent accumulators).
 template <bool BF16>
-__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
-                                                            const uint16_t* __restrict__ w_main,
-                                                            const uint16_t* __restrict__ w_gate, int T, int H,
-                                                            int E, float* __restrict__ logits) {
-  const int lane = threadIdx.x & 31;
-  const int R = E + (w_gate ? 1 : 0);
-  const int64_t task = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (task >= (int64_t)R * T) return;
-  const int t = (int)(task / R), r = (int)(task % R);
-  const uint16_t* wr = r < E ? w_main + (int64_t)r * H : w_gate;
-  const uint16_t* xr = x + (int64_t)t * H;
+__device__ __forceinline__ float router_dot(const uint16_t* __restrict__ xr, const uint16_t* __restrict__ wr, int H,
+                                            int lane) {
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int k0 = lane * 8; k0 < H; k0 += 32 * 8 * 4) {
     uint4 xv[4], wv[4];
@@ -49,6 +44,21 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
   float s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
   for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
+                                                            const uint16_t* __restrict__ w_main,
+                                                            const uint16_t* __restrict__ w_gate, int T, int H,
+                                                            int E, float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31;
+  const int R = E + (w_gate ? 1 : 0);
+  const int64_t task = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (task >= (int64_t)R * T) return;
+  const int t = (int)(task / R), r = (int)(task % R);
+  const uint16_t* wr = r < E ? w_main + (int64_t)r * H : w_gate;
+  const float s = router_dot<BF16>(x + (int64_t)t * H, wr, H, lane);
   if (lane == 0) logits[(int64_t)t * R + r] = s;
 }
 
@@ -126,6 +136,65 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
   const int R = E + (has_gate ? 1 : 0);
   warp_topk(logits + (int64_t)t * R, E, K, renorm, ids + (int64_t)t * K, tw + (int64_t)t * K,
             has_gate ? sg + t : nullptr, has_gate != 0);
+}
+
+// Single-token path (blut_tok1.cuh), launch 1 of 3.  One CTA: the logits
+// of the R rows (experts, then the shared-expert gate row) a warp per row;
+// the completion counters of the two GEMV launches and the status word
+// zeroed; then warp 0 takes the top-k (or checks the caller's ids) and
+// writes the group table: one group per valid slot, in slot order, with its
+// routing weight.
+template <bool BF16>
+__global__ void __launch_bounds__(1024) tok1_route_kernel(const uint16_t* __restrict__ x,
+                                                          const uint16_t* __restrict__ w_main,
+                                                          const uint16_t* __restrict__ w_gate, int H, int E, int K,
+                                                          int renorm, const int32_t* __restrict__ ids_in,
+                                                          const float* __restrict__ tw_in, float* __restrict__ logits,
+                                                          int* __restrict__ groups, float* __restrict__ gw,
+                                                          float* __restrict__ sg, int* __restrict__ status,
+                                                          int* __restrict__ cnt, int ncnt, int has_shared,
+                                                          void* __restrict__ out, int out_f32) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e_main = w_main ? E : 0;
+  const int R = e_main + (w_gate ? 1 : 0);
+  for (int r = warp; r < R; r += 32) {
+    const float v = router_dot<BF16>(x, r < e_main ? w_main + (int64_t)r * H : w_gate, H, lane);
+    if (lane == 0) logits[r] = v;
+  }
+  for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
+  if (threadIdx.x == 0) *status = 0;  // the status word reports this call only, as the plan kernel's does
+  __shared__ int32_t sids[32];
+  __shared__ float stw[32];
+  __syncthreads();
+  if (warp != 0) return;
+  if (w_main) {
+    warp_topk(logits, E, K, renorm, sids, stw, sg, w_gate != nullptr);
+  } else {
+    if (w_gate && lane == 0) *sg = 1.f / (1.f + expf(-logits[0]));
+    if (lane < K) {
+      sids[lane] = ids_in[lane];
+      stw[lane] = tw_in[lane];
+    }
+  }
+  __syncwarp();
+  const int id = lane < K ? sids[lane] : -1;
+  const bool ok = lane < K && id >= 0 && id < E;
+  if (lane < K && !ok && id != -1) atomicOr(status, kDevBadExpert);  // -1 = empty slot
+  const unsigned m = __ballot_sync(0xffffffffu, ok);
+  if (ok) {
+    const int g = __popc(m & ((1u << lane) - 1u));
+    groups[1 + g] = id;
+    gw[g] = stw[lane];
+  }
+  if (lane == 0) groups[0] = __popc(m);
+  if (m == 0 && !has_shared) {  // no expert and no shared expert: the GEMV launches write nothing
+    for (int h = lane; h < H; h += 32) {
+      if (out_f32)
+        static_cast<float*>(out)[h] = 0.f;
+      else
+        static_cast<uint16_t*>(out)[h] = 0;
+    }
+  }
 }
 
 // ----------------------------------------------------------------- plan ---
@@ -521,6 +590,20 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
   }
 }
 
+bool tok1_applies(const blut_moe_args& a, const MoESplit& s) {
+  return a.num_tokens == 1 && s.gemv[0] && (a.shared_inter <= 0 || s.gemv[1]);
+}
+
+// K slices of a single-token GEMV pass: each slice the blocks of the pieces a
+// thread keeps in flight (the persistent grid needs no more items than that).
+static void tok1_slices(const blut_mat_desc& d, int& bps, int& ks) {
+  TiledLayout L;
+  bps = ks = 0;
+  if (!make_layout(d, L)) return;
+  bps = std::max(1, tc_gemv_blocks(d));
+  ks = (int)((L.nchunks + bps - 1) / bps);
+}
+
 // Workspace carve-up; returns total bytes, fills pointers when base != null.
 size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
   const int64_t T = a.num_tokens, K = a.top_k, E = a.num_experts, H = a.hidden, I = a.inter;
@@ -556,7 +639,46 @@ size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
   const int64_t ku_s = sp.ks[2] > 1 || sp.gemv[1] ? sp.groups[2] * sp.units[2] : 0;
   size_t o_part_r = take(ku_r * sp.ks[0] * 2 * kTcRows * 32 * 4);
   size_t o_part_s = take(ku_s * sp.ks[2] * 2 * kTcRows * 32 * 4);
+  // single-token path
+  const bool t1 = tok1_applies(a, sp);
+  int t1_bps[4] = {0, 0, 0, 0}, t1_ks[4] = {0, 0, 0, 0};
+  size_t o_t1g = 0, o_t1w = 0, o_t1c = 0, o_t1pr = 0, o_t1ps = 0, o_t1ar = 0, o_t1as = 0, o_t1yr = 0, o_t1ys = 0;
+  int t1_ncnt_pair = 0, t1_ncnt = 0;
+  if (t1) {
+    const blut_mat_desc* d[4] = {&a.w13, &a.w2, &a.s13, &a.s2};
+    for (int i = 0; i < (sh ? 4 : 2); ++i) tok1_slices(*d[i], t1_bps[i], t1_ks[i]);
+    const int64_t units_r = a.inter / kTcRows, units_s = sh ? a.shared_inter / kTcRows : 0;
+    t1_ncnt_pair = (int)(K * units_r + units_s);
+    t1_ncnt = t1_ncnt_pair + (int)((H + kTcRows - 1) / kTcRows);
+    o_t1g = take((1 + K) * 4);
+    o_t1w = take(K * 4);
+    o_t1c = take((int64_t)t1_ncnt * 4);
+    o_t1pr = take(K * units_r * t1_ks[0] * 2 * kTcRows * 4);
+    o_t1ps = sh ? take(units_s * t1_ks[2] * 2 * kTcRows * 4) : 0;
+    o_t1ar = take(K * I * 2);
+    o_t1as = sh ? take(a.shared_inter * 2) : 0;
+    o_t1yr = take((int64_t)t1_ks[1] * K * H * 4);
+    o_t1ys = sh ? take((int64_t)t1_ks[3] * H * 4) : 0;
+  }
   if (base && ws) {
+    w.tok1 = t1;
+    if (t1) {
+      for (int i = 0; i < 4; ++i) {
+        w.t1_ks[i] = t1_ks[i];
+        w.t1_bps[i] = t1_bps[i];
+      }
+      w.t1_groups = reinterpret_cast<int*>(base + o_t1g);
+      w.t1_gw = reinterpret_cast<float*>(base + o_t1w);
+      w.t1_cnt = reinterpret_cast<int*>(base + o_t1c);
+      w.t1_ncnt_pair = t1_ncnt_pair;
+      w.t1_ncnt = t1_ncnt;
+      w.t1_part_r = reinterpret_cast<float*>(base + o_t1pr);
+      w.t1_part_s = sh ? reinterpret_cast<float*>(base + o_t1ps) : nullptr;
+      w.t1_act_r = reinterpret_cast<uint16_t*>(base + o_t1ar);
+      w.t1_act_s = sh ? reinterpret_cast<uint16_t*>(base + o_t1as) : nullptr;
+      w.t1_y_r = reinterpret_cast<float*>(base + o_t1yr);
+      w.t1_y_s = sh ? reinterpret_cast<float*>(base + o_t1ys) : nullptr;
+    }
     w.split = sp;
     w.y_sstride = S * H;
     w.ys_sstride = T * H;
@@ -723,6 +845,91 @@ static SideStream* side_stream(cudaStream_t stream) {
   return &ss;
 }
 
+// Single-token layer in three launches (blut_tok1.cuh): route, gate/up with
+// the SiLU * up epilogue, down with the weighted combine.
+static int moe_forward_tok1(const blut_moe_args& a, const MoEWs& ws, cudaStream_t stream) {
+  const bool bf16 = a.dtype == BLUT_BF16;
+  const bool sh = a.shared_inter > 0;
+  const int K = a.top_k, E = a.num_experts, H = a.hidden;
+  const bool route = a.topk_ids == nullptr;
+  const bool gate = sh && a.shared_gate_mode == 1;
+  const uint16_t* w_main = route ? (const uint16_t*)a.router_w : nullptr;
+  const uint16_t* w_gate =
+      !gate ? nullptr : a.shared_gate_w ? (const uint16_t*)a.shared_gate_w : (const uint16_t*)a.router_w + (int64_t)E * H;
+  auto rk = bf16 ? tok1_route_kernel<true> : tok1_route_kernel<false>;
+  rk<<<1, 1024, 0, stream>>>((const uint16_t*)a.x, w_main, w_gate, H, E, K, a.renorm, a.topk_ids, a.topk_weights,
+                             ws.logits, ws.t1_groups, ws.t1_gw, ws.sg, ws.status, ws.t1_cnt, ws.t1_ncnt, sh ? 1 : 0,
+                             a.out, a.out_f32);
+  int rc = stage_done("single-token route", stream);
+  if (rc != BLUT_OK) return rc;
+
+  // the two projections: routed matrices in part 0, the shared expert in part 1
+  auto mat = [&](const blut_mat_desc& d, const void* w, int64_t stride, bool pair, int i, Tok1Mat& m) -> bool {
+    m = Tok1Mat{};
+    if (!tc_planes(d, pair, m.p)) return false;
+    m.p.w = (const uint8_t*)w;
+    m.p.wstride = stride;
+    m.p.r8_table = (const uint16_t*)a.lut_table;
+    m.p.status = ws.status;
+    m.p.ks = ws.t1_ks[i];
+    m.p.bps = ws.t1_bps[i];
+    m.n_items = (int64_t)(i < 2 ? K : 1) * m.p.ntiles * m.p.ks;
+    return m.p.ks > 0;
+  };
+  TiledLayout L13, L2, Ls13, Ls2;
+  make_layout(a.w13, L13);
+  make_layout(a.w2, L2);
+  double rb13 = (double)K * L13.total, rb2 = (double)K * L2.total, sb13 = 0, sb2 = 0;
+  if (sh) {
+    make_layout(a.s13, Ls13);
+    make_layout(a.s2, Ls2);
+    sb13 = (double)Ls13.total;
+    sb2 = (double)Ls2.total;
+  }
+  Tok1Args g{};
+  g.groups = ws.t1_groups;
+  g.gw = ws.t1_gw;
+  g.sg = gate ? ws.sg : nullptr;
+  g.gbound = K;
+  g.hidden = H;
+  if (!mat(a.w13, a.w13_tiled, a.w13_stride, true, 0, g.m[0])) return BLUT_ERR_UNSUPPORTED;
+  g.m[0].xin = (const uint16_t*)a.x;
+  g.m[0].part = ws.t1_part_r;
+  g.m[0].act = ws.t1_act_r;
+  if (sh) {
+    if (!mat(a.s13, a.s13_tiled, 0, true, 2, g.m[1])) return BLUT_ERR_UNSUPPORTED;
+    g.m[1].xin = (const uint16_t*)a.x;
+    g.m[1].part = ws.t1_part_s;
+    g.m[1].act = ws.t1_act_s;
+    g.m[1].cnt0 = K * g.m[0].p.units;
+  }
+  g.cnt = ws.t1_cnt;
+  cudaEvent_t* ev = a.prof_events ? (cudaEvent_t*)a.prof_events : nullptr;
+  if (ev && cudaEventRecord(ev[0], stream) != cudaSuccess) return BLUT_ERR_INVALID;
+  if (launch_tok1(a.w13, g, true, rb13, sb13, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  if ((rc = stage_done("single-token gate/up", stream)) != BLUT_OK) return rc;
+  if (ev && cudaEventRecord(ev[1], stream) != cudaSuccess) return BLUT_ERR_INVALID;
+
+  Tok1Args d = g;
+  if (!mat(a.w2, a.w2_tiled, a.w2_stride, false, 1, d.m[0])) return BLUT_ERR_UNSUPPORTED;
+  d.m[0].xin = ws.t1_act_r;
+  d.m[0].x_ld = a.inter;
+  d.m[0].part = ws.t1_y_r;
+  if (sh) {
+    if (!mat(a.s2, a.s2_tiled, 0, false, 3, d.m[1])) return BLUT_ERR_UNSUPPORTED;
+    d.m[1].xin = ws.t1_act_s;
+    d.m[1].part = ws.t1_y_s;
+  }
+  d.cnt = ws.t1_cnt + ws.t1_ncnt_pair;
+  d.out = a.out;
+  d.out_f32 = a.out_f32;
+  if (ev && cudaEventRecord(ev[2], stream) != cudaSuccess) return BLUT_ERR_INVALID;
+  if (launch_tok1(a.w2, d, false, rb2, sb2, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+  if ((rc = stage_done("single-token down", stream)) != BLUT_OK) return rc;
+  if (ev && cudaEventRecord(ev[3], stream) != cudaSuccess) return BLUT_ERR_INVALID;
+  return BLUT_OK;
+}
+
 int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaStream_t stream) {
   int rc = validate_moe(a);
   if (rc != BLUT_OK) return rc;
@@ -732,6 +939,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return BLUT_ERR_INVALID;
   MoEWs ws;
   moe_workspace(a, static_cast<uint8_t*>(workspace), &ws);
+  if (ws.tok1) return moe_forward_tok1(a, ws, stream);
   const bool bf16 = a.dtype == BLUT_BF16;
   const bool sh = a.shared_inter > 0;
   const int T = a.num_tokens, K = a.top_k, E = a.num_experts, H = a.hidden;
@@ -795,7 +1003,6 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
                   const uint8_t* bin, uint8_t* act, int out_k, float* y, int counter, float* part,
                   int64_t y_sstride, const blut_mat_desc* next) -> int {
     const bool pair = act != nullptr;
-    const int K = (int)d.cols;
     if (d.layout & BLUT_LAYOUT_TC) {
       TcParams t{};
       if (!tc_planes(d, pair, t)) return BLUT_ERR_UNSUPPORTED;
@@ -924,6 +1131,11 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
 int moe_launch_count(const blut_moe_args& a) {
   const bool sh = a.shared_inter > 0;
   int n = 0;
+  {
+    MoESplit sp;
+    moe_split(a, sp);
+    if (tok1_applies(a, sp)) return 3;  // route, gate/up, down
+  }
   if (!a.topk_ids || (sh && a.shared_gate_mode == 1)) {
     ++n;                                                   // router / gate logits
     if (a.num_tokens > kPlanTopkTokens) ++n;               // separate top-k

@@ -1,0 +1,254 @@
+// Single-token MoE layer (one token per call, the decode regime the
+// reference's GEMV targets): three launches instead of the general path's
+// router / plan / gather / gate-up / slice-sum / down / combine chain.
+//
+//   tok1_route_kernel (blut_moe.cu)  router logits, top-k, the group table
+//       (one group per routed expert of the token) and zeroed counters;
+//   tok1_kernel<Dec, pair = true>    gate/up of every routed group and of the
+//       shared expert in one persistent launch; the last CTA to finish a
+//       128-row unit (both of its tiles, every K slice) sums the slices and
+//       writes SiLU(gate) * up for that unit;
+//   tok1_kernel<Dec, pair = false>   down of every group and the shared
+//       expert; the last CTA to finish an output tile sums, for its rows,
+//       every group's slices weighted by the routing weight plus the shared
+//       expert's slices weighted by its gate, and rounds once.
+//
+// The GEMV is the one of tc_gemv_kernel (one thread per weight row, the
+// format's decode, fp32 FMAs) made persistent: the CTAs of the routed part
+// walk the routed items and those of the shared part the shared items, and
+// while one item is computed the thread's register ring already holds the
+// next item's weights.  Activations are read row-major (the token row for
+// gate/up, a group's SiLU * up row for down), so no gather is needed.
+#pragma once
+
+#include "blut_tc.cuh"
+
+namespace blut {
+
+constexpr int kTok1Threads = kTcRows;
+
+// One matrix of a single-token pass.
+struct Tok1Mat {
+  TcParams p;          // planes, tiles, blocks, K slices (ks, bps), decode constants, weights
+  int64_t n_items;     // group bound * ntiles * ks
+  int ctas;            // CTAs of the persistent grid that work on this matrix
+  const uint16_t* xin; // activation rows; group g reads xin + g * x_ld
+  int64_t x_ld;
+  float* part;         // gate/up: [group][unit][ks][gate | up][128]; down: [ks][group bound][hidden]
+  uint16_t* act;       // gate/up: SiLU * up rows, [group][rows / 2]
+  int cnt0;            // gate/up: first completion counter of this matrix ([group][unit])
+};
+
+struct Tok1Args {
+  Tok1Mat m[2];        // routed experts, shared expert (m[1].ctas == 0: none)
+  const int* groups;   // [0] routed groups, [1 + g] expert of group g
+  const float* gw;     // [g] routing weight of group g
+  const float* sg;     // shared expert gate (nullptr: 1)
+  int* cnt;            // completion counters (zeroed by the route kernel)
+  int gbound;          // routed group bound (the top-k)
+  void* out;           // down: the layer output [hidden], fp16 / bf16 or fp32
+  int out_f32;
+  int hidden;
+};
+
+struct Tok1Item {
+  int gi, pt, s, b0, n;
+  const uint8_t* base;
+};
+
+// Item `it` of matrix m (ordered (group, tile, slice)); false past the last
+// item or at a group that does not exist (every later item's group is larger).
+template <class Dec>
+__device__ __forceinline__ bool tok1_resolve(const Tok1Args& a, const Tok1Mat& m, bool shared, int ng, int64_t it,
+                                             Tok1Item& r) {
+  const TcParams& p = m.p;
+  if (it >= m.n_items) return false;
+  r.s = (int)(it % p.ks);
+  r.pt = (int)((it / p.ks) % p.ntiles);
+  r.gi = (int)(it / ((int64_t)p.ks * p.ntiles));
+  if (r.gi >= ng) return false;
+  r.b0 = r.s * p.bps;
+  const int b1 = min(p.nblocks, r.b0 + p.bps);
+  r.n = r.b0 < b1 ? (b1 - r.b0) * (Dec::kDense ? 1 : Dec::kHalves) : 0;
+  const int e = shared ? 0 : a.groups[1 + r.gi];
+  r.base = p.w + (int64_t)e * p.wstride;
+  return true;
+}
+
+template <class Dec, bool PAIR>
+__device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, bool shared, int cta, int nctas,
+                                         uint8_t* smem) {
+  constexpr int KB = Dec::KB;
+  constexpr int PF = tc_gemv_pf<Dec>();
+  constexpr int W = Dec::kDense ? Dec::KB : 64;  // columns per piece
+  using U = typename std::conditional<Dec::kDense, TcDenseBlk<Dec::kBF16>, typename Dec::Half>::type;
+  const TcParams& p = m.p;
+  const int row = threadIdx.x;
+  const int ng = shared ? 1 : min(a.groups[0], a.gbound);
+  __shared__ int s_last;
+  uint32_t tab = 0;
+  if constexpr (Dec::kR8) tab = smem_u32(smem) + (row & 31) * 4;
+  float* xs = reinterpret_cast<float*>(smem + tc_table_bytes<Dec>());
+  int64_t item = cta;
+  Tok1Item cur, nxt;
+  if (!tok1_resolve<Dec>(a, m, shared, ng, item, cur)) return;  // uniform over the CTA
+  if constexpr (Dec::kR8) tc_fill_r8_table(reinterpret_cast<uint32_t*>(smem), p.r8_table);
+  U ring[PF];
+#pragma unroll
+  for (int j = 0; j < PF; ++j)
+    if (j < cur.n) tc_gemv_load<Dec>(p, cur.base, cur.pt, cur.b0, j, row, tab, ring[j]);
+  for (;;) {
+    const bool more = tok1_resolve<Dec>(a, m, shared, ng, item + nctas, nxt);
+    __syncthreads();  // the previous item's reads of xs are done (and the R8 table is complete)
+    const uint16_t* xrow = m.xin + (int64_t)cur.gi * m.x_ld + cur.b0 * KB;
+    for (int col = threadIdx.x; col < cur.n * W; col += blockDim.x) xs[col] = act_to_f32<Dec::kBF16>(xrow[col]);
+    __syncthreads();  // xs complete
+    float2 acc[1] = {make_float2(0.f, 0.f)};
+#pragma unroll
+    for (int j = 0; j < PF; ++j) {
+      if (j < cur.n) {
+        if constexpr (Dec::kDense) {
+          uint32_t o[16];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            o[4 * k] = ring[j].v[k].x; o[4 * k + 1] = ring[j].v[k].y;
+            o[4 * k + 2] = ring[j].v[k].z; o[4 * k + 3] = ring[j].v[k].w;
+          }
+          tc_gemv_fma32<Dec::kBF16, 1>(o, xs, 0, j * W, acc);
+        } else {
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            uint32_t o[16];
+            Dec::lookup_q(ring[j], qq, o, p.mul);
+            tc_gemv_fma32<Dec::kBF16, 1>(o, xs, 0, j * W + 32 * qq, acc);
+          }
+        }
+      }
+      // this slot's next content: the same piece of the CTA's next item
+      if (more && j < nxt.n) tc_gemv_load<Dec>(p, nxt.base, nxt.pt, nxt.b0, j, row, tab, ring[j]);
+    }
+    const float v = acc[0].x + acc[0].y;
+    int* counter;
+    int target;
+    if constexpr (PAIR) {
+      const int unit = cur.pt >> 1;
+      float* mine = m.part + (((int64_t)cur.gi * p.units + unit) * p.ks) * (2 * kTcRows);
+      mine[cur.s * (2 * kTcRows) + (cur.pt & 1) * kTcRows + row] = v;
+      counter = a.cnt + m.cnt0 + cur.gi * p.units + unit;
+      target = 2 * p.ks;  // both tiles of the unit, every slice
+    } else {
+      m.part[((int64_t)cur.s * (shared ? 1 : a.gbound) + cur.gi) * a.hidden + cur.pt * kTcRows + row] = v;
+      counter = a.cnt + cur.pt;  // one counter per output tile, over both matrices
+      target = min(a.groups[0], a.gbound) * a.m[0].p.ks + (a.m[1].ctas > 0 ? a.m[1].p.ks : 0);
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(counter, 1) == target - 1;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      if constexpr (PAIR) {
+        // every slice of both tiles of this unit is in: SiLU(gate) * up
+        const int unit = cur.pt >> 1;
+        const float* src = m.part + (((int64_t)cur.gi * p.units + unit) * p.ks) * (2 * kTcRows) + row;
+        float g = 0.f, u = 0.f;
+        for (int sl = 0; sl < p.ks; ++sl) {
+          g += __ldcg(src + sl * (2 * kTcRows));
+          u += __ldcg(src + sl * (2 * kTcRows) + kTcRows);
+        }
+        m.act[(int64_t)cur.gi * (p.ntiles / 2) * kTcRows + unit * kTcRows + row] =
+            f32_to_act<Dec::kBF16>(silu_f(g) * u);
+      } else {
+        // every contribution to this output tile is in: the weighted combine
+        const int h = cur.pt * kTcRows + row;
+        const Tok1Mat& r = a.m[0];
+        const int ngr = min(a.groups[0], a.gbound);
+        float o = 0.f;
+        for (int g = 0; g < ngr; ++g) {
+          float y = 0.f;
+          for (int sl = 0; sl < r.p.ks; ++sl) y += __ldcg(r.part + ((int64_t)sl * a.gbound + g) * a.hidden + h);
+          o = fmaf(a.gw[g], y, o);
+        }
+        if (a.m[1].ctas > 0) {
+          const Tok1Mat& sm = a.m[1];
+          float y = 0.f;
+          for (int sl = 0; sl < sm.p.ks; ++sl) y += __ldcg(sm.part + (int64_t)sl * a.hidden + h);
+          o = fmaf(a.sg ? *a.sg : 1.f, y, o);
+        }
+        if (a.out_f32)
+          static_cast<float*>(a.out)[h] = o;
+        else
+          static_cast<uint16_t*>(a.out)[h] = f32_to_act<Dec::kBF16>(o);
+      }
+    }
+    if (!more) break;
+    cur = nxt;
+    item += nctas;
+  }
+}
+
+// CTAs [0, m[0].ctas) work on the routed experts, the rest on the shared one.
+template <class Dec, bool PAIR>
+__global__ void __launch_bounds__(kTok1Threads, 4) tok1_kernel(const Tok1Args a) {
+  extern __shared__ __align__(16) uint8_t tsm[];
+  if ((int)blockIdx.x < a.m[0].ctas)
+    tok1_run<Dec, PAIR>(a, a.m[0], false, blockIdx.x, a.m[0].ctas, tsm);
+  else
+    tok1_run<TcDecDense<Dec::kBF16>, PAIR>(a, a.m[1], true, blockIdx.x - a.m[0].ctas, a.m[1].ctas, tsm);
+}
+
+// Shared-memory bytes of a tok1 launch.
+template <class Dec>
+inline int tok1_smem(const Tok1Args& a) {
+  int cols = a.m[0].p.bps * Dec::KB;
+  if (a.m[1].ctas > 0) cols = std::max(cols, a.m[1].p.bps * TcDecDense<Dec::kBF16>::KB);
+  return tc_table_bytes<Dec>() + cols * 4;
+}
+
+// CTAs of the routed and shared parts: the resident CTAs of the GPU, split
+// in proportion to the weight bytes each part reads.
+template <class Dec, bool PAIR>
+inline cudaError_t launch_tok1_dec(Tok1Args a, double routed_bytes, double shared_bytes, cudaStream_t stream) {
+  const int smem = tok1_smem<Dec>(a);
+  auto kern = tok1_kernel<Dec, PAIR>;
+  static std::mutex mu;
+  static int cached_smem[kMaxDevices], cached_per_sm[kMaxDevices];
+  const int dev = cache_device();
+  int per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && cached_smem[dev] >= smem) {
+      per_sm = cached_per_sm[dev];
+    } else {
+      const int attr = std::max(smem, 48 * 1024);
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, attr);
+      if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTok1Threads, smem);
+      if (e != cudaSuccess) return e;
+      per_sm = std::max(1, per_sm);
+      if (dev >= 0) {
+        cached_smem[dev] = attr;
+        cached_per_sm[dev] = per_sm;
+      }
+    }
+  }
+  const int64_t total = (int64_t)num_sms() * per_sm;
+  const bool sh = a.m[1].n_items > 0;
+  int64_t cr = total, cs = 0;
+  if (sh) {
+    cs = std::max<int64_t>(1, (int64_t)(total * shared_bytes / std::max(1.0, routed_bytes + shared_bytes) + 0.5));
+    cs = std::min<int64_t>(cs, total - 1);
+    cr = total - cs;
+  }
+  cr = std::max<int64_t>(1, std::min<int64_t>(cr, a.m[0].n_items));
+  cs = std::min<int64_t>(cs, a.m[1].n_items);
+  a.m[0].ctas = (int)cr;
+  a.m[1].ctas = (int)cs;
+  kern<<<(unsigned)(cr + cs), kTok1Threads, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+// Per-format dispatch (blut_tok1.cu).
+cudaError_t launch_tok1(const blut_mat_desc& d, const Tok1Args& a, bool pair, double routed_bytes,
+                        double shared_bytes, cudaStream_t stream);
+
+}  // namespace blut

@@ -179,6 +179,32 @@ def encode_r(w_bf16: np.ndarray, table_bf16: np.ndarray, block_size: int = 128):
     return idx[:n], amax_b
 
 
+def encode_lut_f32(w_bf16: np.ndarray, codebook_f32: np.ndarray, block_size: int = 128):
+    """The fast GPU encoder's rule (vllm_lut/fast_encode.py:22-102), with the
+    exact division its own check compares against (fast_encode.py:205-221).
+
+    absmax = max(max |w| over the flat block, 1e-10) in fp32; normalised =
+    f32(w) / absmax in fp32 (not rounded to bf16); index = first argmin of
+    |normalised - codebook| over the fp32 codebook.  The stored absmax is
+    bf16(absmax).  Returns (idx u8 [N], absmax bf16 [nb]).
+    """
+    w = np.asarray(w_bf16, dtype=np.uint16).reshape(-1)
+    n = w.shape[0]
+    nb = (n + block_size - 1) // block_size
+    wp = np.zeros(nb * block_size, dtype=np.uint16)
+    wp[:n] = w
+    wf = bf16_to_f32(wp).reshape(nb, block_size)
+    amax = np.maximum(np.abs(wf).max(axis=1), np.float32(1e-10)).astype(np.float32)
+    norm = (wf / amax[:, None]).astype(np.float32).reshape(-1)
+    cb = np.asarray(codebook_f32, dtype=np.float32)
+    idx = np.empty(norm.shape[0], dtype=np.uint8)
+    step = 1 << 16
+    for s in range(0, norm.shape[0], step):
+        d = np.abs(norm[s:s + step, None] - cb[None, :])
+        idx[s:s + step] = np.argmin(d, axis=1).astype(np.uint8)
+    return idx[:n], f32_to_bf16(amax)
+
+
 # ----------------------------------------------------------------------------
 # Format B: packed b-bit codes, one sorted fp16 codebook of 2**b entries per
 # (row, block of g elements along K).  NestedLUT: 2-bit coarse code into a
@@ -424,7 +450,8 @@ def moe_forward(x: np.ndarray, topk_ids: np.ndarray, topk_w: np.ndarray,
         h = xe @ w13e.T
         a = round_to((silu(h[:, :inter]) * h[:, inter:]).astype(np.float32), act_dtype).astype(np.float64)
         y = a @ _expert(w2, e).T
-        out[tok] += np.asarray(topk_w, dtype=np.float64)[tok, slot][:, None] * y
+        # np.add.at: a token that names the same expert in two slots gets both
+        np.add.at(out, tok, np.asarray(topk_w, dtype=np.float64)[tok, slot][:, None] * y)
     if shared13 is not None:
         si = shared13.shape[0] // 2
         h = x @ np.asarray(shared13, dtype=np.float64).T

@@ -155,11 +155,12 @@ def test_launch_count():
     tc.num_tokens, tc.topk_ids = 4096, None  # prefill with routing: router, top-k, plan, gather, 2 matmuls, combine
     tc.router_w = 1 << 22
     assert lib.blut_moe_launch_count(C.byref(tc)) == 7
-    # one token on the tcgen05 layout runs the single-token GEMV, whose gate/up
-    # partials always go through the slice-sum kernel: router, plan, gather,
-    # gate/up, slice sum, down, combine; the mma.sync layout has no slice sum
+    # one token on the tcgen05 layout runs the single-token path: route,
+    # gate/up (with SiLU * up), down (with the combine), routed or not
     tc.num_tokens = 1
-    assert lib.blut_moe_launch_count(C.byref(tc)) == 7
+    assert lib.blut_moe_launch_count(C.byref(tc)) == 3
+    tc.topk_ids, tc.router_w = 1 << 22, None
+    assert lib.blut_moe_launch_count(C.byref(tc)) == 3
     mma = _args(num_tokens=1, topk_ids=None, router_w=1 << 22)
     assert lib.blut_moe_launch_count(C.byref(mma)) == 6
 

@@ -52,7 +52,7 @@ def _local_partial(x, ids, tw, W13, W2, start):
         w13, w2 = W13[start + e].astype(np.float64), W2[start + e].astype(np.float64)
         h = x[tok].astype(np.float64) @ w13.T
         a = O.round_to((O.silu(h[:, :I]) * h[:, I:]).astype(np.float32), "f16").astype(np.float64)
-        out[tok] += tw[tok, slot][:, None].astype(np.float64) * (a @ w2.T)
+        np.add.at(out, tok, tw[tok, slot][:, None].astype(np.float64) * (a @ w2.T))
     return out
 
 

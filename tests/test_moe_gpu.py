@@ -153,6 +153,47 @@ def test_qwen15_layer_format_b_4bit_g64(T):
     check_layer(out, ref, torch.float16, f"qwen1.5 layer T={T}")
 
 
+def test_single_token_path_edge_slots():
+    """The single-token path (route, gate/up, down with the combine): a token
+    whose slots are all empty (-1) gives zeros without a shared expert and the
+    shared expert alone with one; one empty slot beside a valid one, and the
+    same expert chosen twice, count like the general path; fp32 output."""
+    fmt = LUTFormat("b", 4, 64)
+    experts, W13, W2 = build_b_layer(fmt, E=4, H=256, I=128, seed=7, tc=True)
+    rng = np.random.Generator(np.random.PCG64(3))
+    x = cuda(O.rms_activations(rng, 1, 256).astype(np.float16))
+    xs = x.float().cpu().numpy()
+    s13 = O.student_t_weights(rng, (256, 256)).astype(np.float16)
+    s2 = O.student_t_weights(rng, (256, 128)).astype(np.float16)
+    layer = LUTMoELayer(experts, 2)
+    assert layer.launch_count(1, caller_routing=True) == 3
+    empty = cuda(np.array([[-1, -1]], dtype=np.int32))
+    w = cuda(np.array([[0.6, 0.4]], dtype=np.float32))
+    out = layer.forward(x, empty, w)
+    # a stale status word (left by anything that used the workspace before)
+    # does not outlive the next call: the route kernel clears it
+    from block_lut_b200.moe import _WS
+    _WS[(x.device.type, x.device.index, 0)][0] = 1
+    out = layer.forward(x, empty, w)
+    layer.check_status()
+    assert torch.count_nonzero(out).item() == 0
+    sh = LUTMoELayer(experts, 2, shared=SharedExpert.from_dense(cuda(s13), cuda(s2)), shared_gate_mode=0)
+    out = sh.forward(x, empty, w)
+    sh.check_status()
+    h = xs.astype(np.float64) @ s13.astype(np.float64).T
+    a = O.round_to((O.silu(h[:, :128]) * h[:, 128:]).astype(np.float32), "f16").astype(np.float64)
+    check_layer(out, a @ s2.astype(np.float64).T, torch.float16, "shared expert only")
+    for ids in ([[2, -1]], [[1, 1]]):
+        ids = np.array(ids, dtype=np.int32)
+        tw = np.array([[0.6, 0.4]], dtype=np.float32)
+        out = layer.forward(x, cuda(ids), cuda(tw), out_f32=True)
+        layer.check_status()
+        assert out.dtype == torch.float32
+        ref = O.moe_forward(xs, np.where(ids < 0, 0, ids), np.where(ids < 0, 0, tw), W13, W2, act_dtype="f16")
+        err = np.abs(out.cpu().numpy() - ref).max()
+        assert err <= 2e-3, (ids.tolist(), err)
+
+
 @pytest.mark.parametrize("T", [12, 1])  # T = 1: the single-token GEMV on the tcgen05 layout
 @pytest.mark.parametrize("tc", [True, False], ids=["tc", "mma"])
 def test_shared_expert_modes_and_graph_capture(tc, T):
@@ -319,3 +360,33 @@ def test_prefill_wide_groups(T, with_shared, fmt):
     # the same layer at decode size still matches (both regimes in one process)
     xd = x[:5].contiguous()
     check_layer(layer.forward(xd)[torch.from_numpy(keep[:5]).cuda()], ref[:5][keep[:5]], torch.float16, "decode")
+
+
+@pytest.mark.parametrize("T", [1, 8])
+def test_decode_step_graph_with_host_io(T):
+    """LUTMoEStep: one CUDA graph per step that copies each layer's input from
+    pinned host memory, runs the layer and copies the output back; replays
+    give the eager layers' outputs bit for bit, and new host inputs flow
+    through a replay."""
+    from block_lut_b200.moe import LUTMoEStep
+    fmt = LUTFormat("b", 4, 64)
+    layers = []
+    for seed in (3, 4):
+        experts, _, _ = build_b_layer(fmt, E=6, H=256, I=256, seed=seed, tc=True)
+        rng = np.random.Generator(np.random.PCG64(seed))
+        rw = cuda((rng.standard_normal((7, 256)) * 0.05).astype(np.float16))
+        s13 = O.student_t_weights(rng, (256, 256)).astype(np.float16)
+        s2 = O.student_t_weights(rng, (256, 128)).astype(np.float16)
+        layers.append(LUTMoELayer(experts, 2, router_w=rw, shared=SharedExpert.from_dense(cuda(s13), cuda(s2)),
+                                  shared_gate_mode=1))
+    step = LUTMoEStep(layers, T)
+    for it in range(2):
+        rng = np.random.Generator(np.random.PCG64(50 + it))
+        xs = [O.rms_activations(rng, T, 256).astype(np.float16) for _ in layers]
+        for h, x in zip(step.host_in, xs):
+            h.copy_(torch.from_numpy(x))
+        step.run()
+        torch.cuda.synchronize()
+        for m, h, x in zip(layers, step.host_out, xs):
+            assert torch.equal(h, m.forward(cuda(x)).cpu())
+    step.check_status()
