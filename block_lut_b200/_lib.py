@@ -81,6 +81,7 @@ SIGNATURES = [
     ("blut_matmul_launch_count", C.c_int, [C.POINTER(MatDesc), _I64]),
     ("blut_encode", C.c_int, [C.POINTER(MatDesc), _VP, _VP, _VP, _VP, _VP, _VP]),
     ("blut_encode_r", C.c_int, [_VP, _I64, _VP, _I32, _VP, _VP, _VP]),
+    ("blut_encode_lut_f32", C.c_int, [_VP, _I64, _VP, _I32, _VP, _VP, _VP]),
     ("blut_lut_gemv", C.c_int, [_VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _VP]),
     ("blut_router", C.c_int, [_VP, _VP, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _VP, _VP, _VP, _VP, _VP]),
     ("blut_moe_workspace_size", C.c_size_t, [C.POINTER(MoEArgs)]),

@@ -47,7 +47,13 @@ Codebooks stored as uint16 arrays (the NestedLUT ``mapped`` tables) are read as
 bf16 bit patterns, as the runtime's tier tables are; the reference converters
 cast their integer values instead.
 
-Encoding runs on the GPU through libblut (``blut_encode_r``, ``blut_encode``).
+Format R has two encoders, as the two reference scripts do: ``--encoder
+quantize`` (the default, ``LUTQuantizer.quantize`` as ``convert_checkpoint.py``
+calls it) and ``--encoder fast`` (``fast_encode.encode_lut`` as
+``convert_model.py`` calls it: fp32 normalisation against the fp32 codebook).
+
+Encoding runs on the GPU through libblut (``blut_encode_r``,
+``blut_encode_lut_f32``, ``blut_encode``).
 There is no CPU path: without CUDA the converter raises.
 """
 from __future__ import annotations
@@ -63,7 +69,7 @@ from typing import Dict, List, Optional, Tuple
 import numpy as np
 import torch
 
-from .formats import LUTFormat, QuantizedMatrix, dequant, encode, encode_r
+from .formats import LUTFormat, QuantizedMatrix, dequant, encode, encode_lut_f32, encode_r
 from .quantizer import _load_table
 
 SIDE_SUFFIXES = (".json", ".py", ".txt", ".model", ".npy")
@@ -88,6 +94,10 @@ def parse_args(argv: Optional[List[str]] = None) -> argparse.Namespace:
     p.add_argument("--from_lut", action="store_true",
                    help="read a Format R checkpoint (uint8 indices, lut_absmax.npz, codebook) instead of a bf16 "
                         "one, and re-encode its routed experts to --format b | nested")
+    p.add_argument("--encoder", default="quantize", choices=["quantize", "fast"],
+                   help="Format R encoder: quantize = LUTQuantizer.quantize, the rule of convert_checkpoint.py "
+                        "(normalised value rounded to bf16); fast = fast_encode.encode_lut, the rule of "
+                        "convert_model.py (fp32 normalisation, fp32 codebook)")
     p.add_argument("--device", default="cuda", help="CUDA device of the encoder")
     return p.parse_args(argv)
 
@@ -206,6 +216,15 @@ def quantize_weight(weight: torch.Tensor, codebook: torch.Tensor, device: str = 
     return idx.cpu(), absmax.cpu()
 
 
+def fast_encode_weight(weight: torch.Tensor, codebook: torch.Tensor, device: str = "cuda") -> Tuple[torch.Tensor, torch.Tensor]:
+    """Format R encoding by convert_model.py's rule (fast_encode.encode_lut with
+    the bf16 codebook cast to fp32, convert_model.py:53-61,99): flat uint8
+    indices [N] and bf16 absmax per block of 128, on the CPU."""
+    w = weight.to(device=device, dtype=torch.bfloat16)
+    idx, absmax = encode_lut_f32(w, codebook.to(device=device).float(), BLOCK_SIZE)
+    return idx.cpu(), absmax.cpu()
+
+
 def dequant_lut_weight(idx: torch.Tensor, absmax: np.ndarray, table: torch.Tensor, device: str = "cuda") -> torch.Tensor:
     """A Format R weight (uint8 indices [rows, cols], absmax per flat block of
     128, 256-entry table) back to bf16 [rows, cols] on the GPU, bit-exact
@@ -279,7 +298,8 @@ def convert_checkpoint(args: argparse.Namespace) -> Dict:
                     w = dequant_lut_weight(t, src_absmax[name], codebook, args.device)
                     new_state.update(encode_expert(name, w, fmt, args.device))
                 elif fmt is None:
-                    idx, am = quantize_weight(t, codebook, args.device)
+                    enc = fast_encode_weight if getattr(args, "encoder", "quantize") == "fast" else quantize_weight
+                    idx, am = enc(t, codebook, args.device)
                     new_state[name] = idx.reshape(t.shape)
                     absmax[name] = am.float().numpy()
                 else:

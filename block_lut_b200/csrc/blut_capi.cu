@@ -92,7 +92,12 @@ int blut_encode(const blut_mat_desc* desc, const float* w, void* codes, void* ta
 
 int blut_encode_r(const void* w_bf16, int64_t n, const void* codebook_bf16, int32_t block_size, void* idx_u8,
                   void* absmax_bf16, void* stream) {
-  return encode_r(w_bf16, n, codebook_bf16, block_size, idx_u8, absmax_bf16, S(stream));
+  return encode_r(w_bf16, n, codebook_bf16, block_size, idx_u8, absmax_bf16, false, S(stream));
+}
+
+int blut_encode_lut_f32(const void* w_bf16, int64_t n, const float* codebook_f32, int32_t block_size, void* idx_u8,
+                        void* absmax_bf16, void* stream) {
+  return encode_r(w_bf16, n, codebook_f32, block_size, idx_u8, absmax_bf16, true, S(stream));
 }
 
 int blut_lut_gemv(const void* x_bf16, const void* idx_u8, const void* codebook_bf16, const void* absmax_bf16,

@@ -497,13 +497,23 @@ __global__ void __launch_bounds__(256) encode_kernel(const float* __restrict__ w
   write_block_codes(sm[warp], codes2 + r * row_bytes + j * G / 4, G, 2, lane);
 }
 
-// Reference BlockLUT quantiser (quantizer.py:243-306) on bf16 input: one warp
-// per flat block of 128 values (4 per lane), zero padding past n.
+// Reference BlockLUT encoders on bf16 input: one warp per flat block of
+// bs values (bs / 32 per lane), zero padding past n.
+//   F32 = false: LUTQuantizer.quantize (quantizer.py:243-306): absmax floored
+//     at bf16(1e-10) and rounded to bf16, the normalised value rounded to
+//     bf16, the table bf16.
+//   F32 = true: fast_encode.encode_lut (fast_encode.py:22-102): absmax
+//     floored at 1e-10 in fp32, the normalised value w / absmax kept in fp32,
+//     the table fp32 (the absmax is stored rounded to bf16).
+// Both take the first index of the smallest |v - table[e]|.
+template <bool F32>
 __global__ void __launch_bounds__(256) encode_r_kernel(const uint16_t* __restrict__ w, int64_t n,
-                                                       const uint16_t* __restrict__ cb, int bs,
+                                                       const void* __restrict__ cb_v, int bs,
                                                        uint8_t* __restrict__ idx, uint16_t* __restrict__ absmax) {
   __shared__ float tab[256];
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[i] = __uint_as_float(uint32_t(cb[i]) << 16);
+  for (int i = threadIdx.x; i < 256; i += blockDim.x)
+    tab[i] = F32 ? static_cast<const float*>(cb_v)[i]
+                 : __uint_as_float(uint32_t(static_cast<const uint16_t*>(cb_v)[i]) << 16);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t nb = (n + bs - 1) / bs;
@@ -519,15 +529,17 @@ __global__ void __launch_bounds__(256) encode_r_kernel(const uint16_t* __restric
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-  const float floor_v = __uint_as_float(uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(1e-10f))) << 16);
+  const float floor_v =
+      F32 ? 1e-10f : __uint_as_float(uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(1e-10f))) << 16);
   am = fmaxf(am, floor_v);
   const uint16_t amb = __bfloat16_as_ushort(__float2bfloat16_rn(am));
-  const float amf = __uint_as_float(uint32_t(amb) << 16);
+  const float amf = F32 ? am : __uint_as_float(uint32_t(amb) << 16);
   if (lane == 0) absmax[blk] = amb;
   for (int q = 0; q < per; ++q) {
     const int64_t i = blk * bs + lane + 32 * q;
     if (i >= n) continue;
-    const float nv = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(v[q], amf)));
+    const float x = __fdiv_rn(v[q], amf);
+    const float nv = F32 ? x : __bfloat162float(__float2bfloat16_rn(x));
     int best = 0;
     float bd = fabsf(__fsub_rn(nv, tab[0]));
     for (int e = 1; e < 256; ++e) {
@@ -665,13 +677,14 @@ int encode(const blut_mat_desc& d, const float* w, void* codes, void* tables, vo
   return cudaGetLastError() == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
 }
 
-int encode_r(const void* w, int64_t n, const void* cb, int block_size, void* idx, void* absmax,
+int encode_r(const void* w, int64_t n, const void* cb, int block_size, void* idx, void* absmax, bool f32,
              cudaStream_t stream) {
   if (!w || !cb || !idx || !absmax || n <= 0) return BLUT_ERR_INVALID;
   if (block_size % 32 || block_size > 256 || block_size <= 0) return BLUT_ERR_UNSUPPORTED;
   const int64_t nb = (n + block_size - 1) / block_size;
-  encode_r_kernel<<<(unsigned)((nb + 7) / 8), 256, 0, stream>>>((const uint16_t*)w, n, (const uint16_t*)cb,
-                                                                block_size, (uint8_t*)idx, (uint16_t*)absmax);
+  auto kern = f32 ? encode_r_kernel<true> : encode_r_kernel<false>;
+  kern<<<(unsigned)((nb + 7) / 8), 256, 0, stream>>>((const uint16_t*)w, n, cb, block_size, (uint8_t*)idx,
+                                                     (uint16_t*)absmax);
   return cudaGetLastError() == cudaSuccess ? BLUT_OK : BLUT_ERR_LAUNCH;
 }
 

@@ -163,6 +163,21 @@ def encode_r(w: torch.Tensor, codebook: torch.Tensor, block_size: int = 128, str
     return idx, absmax
 
 
+def encode_lut_f32(w: torch.Tensor, codebook_f: torch.Tensor, block_size: int = 128, stream=None):
+    """The fast BlockLUT encoder's rule on the GPU (fp32 normalisation against
+    an fp32 codebook): returns (uint8 indices [N], bf16 absmax [nb])."""
+    w = w.to(torch.bfloat16).contiguous().reshape(-1)
+    cb = codebook_f.to(device=w.device, dtype=torch.float32).contiguous()
+    _check_cuda(w, cb)
+    n = w.numel()
+    idx = torch.empty(n, dtype=torch.uint8, device=w.device)
+    absmax = torch.empty((n + block_size - 1) // block_size, dtype=torch.bfloat16, device=w.device)
+    with _lib.on_device(w):
+        _lib.check(_lib.lib().blut_encode_lut_f32(w.data_ptr(), n, cb.data_ptr(), block_size, idx.data_ptr(),
+                                                  absmax.data_ptr(), _lib.stream_ptr(stream)), "encode_lut_f32")
+    return idx, absmax
+
+
 def dequant(qm: QuantizedMatrix, stream=None) -> torch.Tensor:
     """Bit-exact dequantisation of one matrix to [rows, cols] (bf16 for r8, fp16 otherwise)."""
     out_dtype = qm.fmt.compute_dtype

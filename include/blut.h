@@ -221,10 +221,22 @@ BLUT_API int blut_encode(const blut_mat_desc* desc, const float* w, void* codes,
 
 /* Reference BlockLUT encoder on bf16 input (block absmax, bf16 normalisation,
  * first-index argmin over the 256-entry table).  Bit-exact with
- * LUTQuantizer.quantize (vllm_lut/quantizer.py:243-306); replaces the GPU
- * encoder encode_blocklut_kernel (vllm_lut/fast_encode.py:22-102). */
+ * LUTQuantizer.quantize (vllm_lut/quantizer.py:243-306), the encoder of
+ * convert_checkpoint.py's quantize_weight.  block_size: 32 .. 256, a
+ * multiple of 32. */
 BLUT_API int blut_encode_r(const void* w_bf16, int64_t n, const void* codebook_bf16, int32_t block_size,
                   void* idx_u8, void* absmax_bf16, void* stream);
+
+/* The other reference BlockLUT encoder, fast_encode.encode_lut
+ * (vllm_lut/fast_encode.py:22-102,172-180, used by convert_model.py): absmax
+ * floored at 1e-10 in fp32, the normalised value w / absmax kept in fp32,
+ * nearest entry of an fp32 codebook (first index on ties); absmax stored
+ * rounded to bf16.  Near codebook midpoints its indices can differ from
+ * blut_encode_r's.  The reference kernel builds with fast math; this one
+ * divides exactly, which is what the reference's own check of that kernel
+ * compares against (fast_encode.py:205-221). */
+BLUT_API int blut_encode_lut_f32(const void* w_bf16, int64_t n, const float* codebook_f32, int32_t block_size,
+                        void* idx_u8, void* absmax_bf16, void* stream);
 
 /* ------------------------------------------------------------------ GEMV -- */
 

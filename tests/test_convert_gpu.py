@@ -220,3 +220,42 @@ def test_from_lut_reencodes_a_format_r_checkpoint(ckpt, tmp_path, argv):
     assert cfg["codebook_scope"] == "row_block" and cfg["lut_block"] == fmt.group
     with pytest.raises(ValueError):
         CC.main(["--model", str(r_out), "--output", str(tmp_path / "bad"), "--from_lut"])
+
+
+@pytest.mark.parametrize("bs", [64, 128, 256])
+def test_encode_lut_f32_bit_exact(bs):
+    """blut_encode_lut_f32 (fast_encode.encode_lut's rule) against the oracle:
+    ragged tail, an all-zero block, and block sizes of 64, 128 and 256."""
+    from block_lut_b200.fast_encode import encode_lut
+    from block_lut_b200.formats import encode_lut_f32
+    rng = np.random.Generator(np.random.PCG64(bs))
+    cb = O.bf16_to_f32(O.f32_to_bf16(np.sort(rng.standard_normal(256).astype(np.float32)) / 3.0))
+    w = O.f32_to_bf16(O.student_t_weights(rng, (bs * 301 + 77,)))
+    w[bs * 5:bs * 6] = 0
+    idx, am = encode_lut_f32(cuda(w).view(torch.bfloat16), cuda(cb), bs)
+    ridx, ram = O.encode_lut_f32(w, cb, bs)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    assert np.array_equal(to_u16(am), ram)
+    if bs == 128:  # the drop-in returns CPU tensors, as the reference's does
+        i2, a2 = encode_lut(cuda(w).view(torch.bfloat16), cuda(cb))
+        assert i2.device.type == "cpu" and a2.device.type == "cpu" and a2.dtype == torch.bfloat16
+        assert np.array_equal(i2.numpy(), ridx) and np.array_equal(to_u16(a2), ram)
+
+
+def test_format_r_conversion_with_the_fast_encoder(ckpt, tmp_path):
+    """--encoder fast: convert_model.py's rule (fp32 normalisation against the
+    bf16 codebook cast to fp32), bit-exact with the oracle."""
+    src, tensors = ckpt
+    out = tmp_path / "out"
+    assert CC.main(["--model", str(src), "--output", str(out), "--encoder", "fast"]) == 0
+    cb = torch.from_numpy(np.load(src / "blocklut_256.npy")).to(torch.bfloat16).float().numpy()
+    conv = _converted(out)
+    absmax = np.load(out / CC.ABSMAX_NAME)
+    n = 0
+    for name, w in tensors.items():
+        if CC.should_encode(name, w.dtype):
+            idx, am = O.encode_lut_f32(to_u16(w), cb, 128)
+            assert np.array_equal(conv[name].numpy().reshape(-1), idx), name
+            assert np.array_equal(O.f32_to_bf16(absmax[name]), am), name
+            n += 1
+    assert n == L * E * 3

@@ -129,3 +129,63 @@ def test_apply_qwen_shape_bit_exact(golden):
     diff = np.abs(out - ref)
     assert (diff <= ulp).all()
     assert (diff > 0).mean() < 1e-3
+
+
+def _reference_fast_encode_check(w_bf16_u16, codebook_f32, block_size=128):
+    """The rule the reference checks its fast GPU encoder against, restated
+    with torch on the CPU as fast_encode.py:205-221 writes it: zero-padded
+    flat blocks, absmax clamped at 1e-10, normalised = blocks / absmax in
+    fp32, argmin over the fp32 codebook."""
+    import torch
+    w = torch.from_numpy(O.bf16_to_f32(w_bf16_u16))
+    n = w.numel()
+    nb = (n + block_size - 1) // block_size
+    padded = torch.zeros(nb * block_size)
+    padded[:n] = w
+    blocks = padded.reshape(-1, block_size)
+    block_max = blocks.abs().max(dim=1, keepdim=True)[0].clamp(min=1e-10)
+    normalized = (blocks / block_max).reshape(-1)[:n]
+    cb = torch.from_numpy(np.asarray(codebook_f32, dtype=np.float32))
+    idx = (normalized.unsqueeze(1) - cb.unsqueeze(0)).abs().argmin(dim=1).to(torch.uint8)
+    return idx.numpy(), block_max.reshape(-1).numpy()
+
+
+def test_encode_lut_f32_follows_the_reference_fast_encoder_rule():
+    # fast_encode.encode_lut (fast_encode.py:22-102) as convert_model.py calls
+    # it: a bf16 codebook cast to fp32 (convert_model.py:53-55); a ragged tail
+    # and an all-zero block (absmax floor)
+    rng = np.random.Generator(np.random.PCG64(11))
+    table = O.f32_to_bf16(np.sort(rng.standard_normal(256).astype(np.float32)) / 3.0)
+    cb = O.bf16_to_f32(table)
+    w = O.f32_to_bf16((rng.standard_t(5, 128 * 37 + 45) * 0.02).astype(np.float32))
+    w[128 * 3:128 * 4] = 0
+    idx, am = O.encode_lut_f32(w, cb, 128)
+    ridx, rmax = _reference_fast_encode_check(w, cb, 128)
+    assert np.array_equal(idx, ridx)
+    assert np.array_equal(am, O.f32_to_bf16(rmax))
+    assert O.bf16_to_f32(am[3]) == O.bf16_to_f32(O.f32_to_bf16(np.float32(1e-10)))
+
+
+def test_encode_lut_f32_and_quantize_differ_only_by_the_bf16_rounding():
+    # The two reference encoders differ where bf16 rounding of the normalised
+    # value w / absmax moves it onto a codebook midpoint.  Entries 0.1015625
+    # and 0.10253906 are two bf16 steps apart, so their midpoint is itself a
+    # bf16 value: a quotient just above it rounds onto it (a tie, which the
+    # first index wins) while in fp32 it is nearer the second entry.  Find
+    # such a weight for absmax 3.0 and check each oracle's rule there.
+    cb = np.array([0.1015625, 0.1015625 + 2 * 2.0 ** -11] + [4.0] * 254, dtype=np.float32)
+    cb = O.bf16_to_f32(O.f32_to_bf16(cb))
+    table = O.f32_to_bf16(cb)
+    amax = np.float32(3.0)
+    cand = O.f32_to_bf16(np.linspace(0.29, 0.32, 4000).astype(np.float32))
+    q = (O.bf16_to_f32(cand) / amax).astype(np.float32)
+    qb = O.bf16_to_f32(O.f32_to_bf16(q))
+    near = lambda v: (np.abs(v - cb[1]) < np.abs(v - cb[0])).astype(int)  # noqa: E731
+    differ = np.nonzero(near(q) != near(qb))[0]
+    assert differ.size > 0
+    x = cand[differ[0]]
+    w = np.zeros(128, dtype=np.uint16)
+    w[0], w[1] = O.f32_to_bf16(amax), x
+    f_idx = O.encode_lut_f32(w, cb, 128)[0][1]
+    q_idx = O.encode_r(w, table, 128)[0][1]
+    assert f_idx == near(q[differ[0:1]])[0] and q_idx == near(qb[differ[0:1]])[0] and f_idx != q_idx
