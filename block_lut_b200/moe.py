@@ -256,6 +256,64 @@ class LUTMoELayer:
                            "device status")
 
 
+class LUTMoEStep:
+    """A decode step over several MoE layers, replayed as one CUDA graph per
+    batch size: the shape in which a serving engine runs the layers (vLLM
+    captures its decode step the same way).
+
+    ``LUTMoEStep(layers, batch)`` builds, for every layer, a pinned host input
+    buffer ``host_in[i]`` [batch, H] and a pinned host output buffer
+    ``host_out[i]``, and captures one graph that copies every input to the
+    device, runs every layer on its own input (``layer.forward``, this
+    library's routing and experts) and copies every output back.  ``run()``
+    replays it on the current stream; the caller fills ``host_in`` before and
+    reads ``host_out`` after a ``torch.cuda.synchronize()`` (or an event).
+    The layers run one after another on one stream, so they share their
+    workspace as in eager calls; a later call that grows that workspace (a
+    larger batch on the same layers) invalidates the graph, so capture a
+    step per batch size after the largest eager call.
+    """
+
+    def __init__(self, layers: Sequence[LUTMoELayer], batch: int, device=None):
+        if not layers:
+            raise ValueError("LUTMoEStep needs at least one layer")
+        self.layers = list(layers)
+        self.batch = int(batch)
+        dev = torch.device(device) if device is not None else self.layers[0].experts.w13.device
+        self.device = dev
+        H = [m.experts.hidden for m in self.layers]
+        self.host_in = [torch.zeros(self.batch, h, dtype=m.dtype).pin_memory() for h, m in zip(H, self.layers)]
+        self.host_out = [torch.zeros(self.batch, h, dtype=m.dtype).pin_memory() for h, m in zip(H, self.layers)]
+        self._dev_in = [torch.zeros(self.batch, h, dtype=m.dtype, device=dev) for h, m in zip(H, self.layers)]
+        self._dev_out = [torch.empty_like(t) for t in self._dev_in]
+        with torch.cuda.device(dev):
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):  # first calls: workspaces and the library's side stream
+                for _ in range(2):
+                    self._body()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self._body()
+        torch.cuda.synchronize(dev)
+
+    def _body(self) -> None:
+        for m, hi, di, do, ho in zip(self.layers, self.host_in, self._dev_in, self._dev_out, self.host_out):
+            di.copy_(hi, non_blocking=True)
+            m.forward(di, out=do)
+            ho.copy_(do, non_blocking=True)
+
+    def run(self) -> None:
+        """Replays the step on the current stream (asynchronous)."""
+        self.graph.replay()
+
+    def check_status(self) -> None:
+        for m in self.layers:
+            m.check_status()
+
+
 def router(x: torch.Tensor, w_router: torch.Tensor, top_k: int, renorm: bool = False,
            shared_gate: bool = False, stream=None):
     """Fused router on the GPU: (topk_ids int32 [T,k], topk_weights f32 [T,k], gate f32 [T] | None)."""
