@@ -19,26 +19,29 @@ namespace blut {
 // 8 warps per CTA; each lane issues all of its 16-byte loads before the FMAs
 // (4 independent accumulators).  Row r < E reads w_main[r]; row E (when
 // w_gate is set) reads the shared-expert gate vector.
-// One warp's fp32 dot product of x and w (H elements); each lane issues all
-// of its 16-byte loads before the FMAs (4 independent accumulators).
+// One warp's fp32 dot product of x and w (H elements).  Lane l takes the
+// 8-element chunks l, l + 32, ...; chunk c accumulates into acc[c % 4], in
+// chunk order, and the four sums are added pairwise, then across the warp.
+// Each lane issues eight chunks' weight loads before their FMAs.
 template <bool BF16>
-__device__ __forceinline__ float router_dot(const uint16_t* __restrict__ xr, const uint16_t* __restrict__ wr, int H,
-                                            int lane) {
+__device__ __forceinline__ float router_dot(const uint16_t* xr, const uint16_t* __restrict__ wr, int H, int lane) {
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int k0 = lane * 8; k0 < H; k0 += 32 * 8 * 4) {
-    uint4 xv[4], wv[4];
+  for (int k0 = lane * 8; k0 < H; k0 += 32 * 8 * 8) {
+    uint4 wv[8];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < 8; ++q) {
       const int k = k0 + q * 256;
-      xv[q] = k < H ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
       wv[q] = k < H ? *reinterpret_cast<const uint4*>(wr + k) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint16_t* xs = reinterpret_cast<const uint16_t*>(&xv[q]);
+    for (int q = 0; q < 8; ++q) {
+      const int k = k0 + q * 256;
+      if (k >= H) break;
+      const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
+      const uint16_t* xs = reinterpret_cast<const uint16_t*>(&xv);
       const uint16_t* ws = reinterpret_cast<const uint16_t*>(&wv[q]);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[q] = fmaf(act_to_f32<BF16>(xs[e]), act_to_f32<BF16>(ws[e]), acc[q]);
+      for (int e = 0; e < 8; ++e) acc[q & 3] = fmaf(act_to_f32<BF16>(xs[e]), act_to_f32<BF16>(ws[e]), acc[q & 3]);
     }
   }
   float s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
@@ -157,12 +160,16 @@ __global__ void __launch_bounds__(1024) tok1_route_kernel(const uint16_t* __rest
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e_main = w_main ? E : 0;
   const int R = e_main + (w_gate ? 1 : 0);
-  for (int r = warp; r < R; r += 32) {
-    const float v = router_dot<BF16>(x, r < e_main ? w_main + (int64_t)r * H : w_gate, H, lane);
-    if (lane == 0) logits[r] = v;
-  }
+  extern __shared__ __align__(16) uint16_t xsm[];  // the token row, read by every warp
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x)
+    reinterpret_cast<uint4*>(xsm)[i] = reinterpret_cast<const uint4*>(x)[i];
   for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
   if (threadIdx.x == 0) *status = 0;  // the status word reports this call only, as the plan kernel's does
+  __syncthreads();
+  for (int r = warp; r < R; r += 32) {
+    const float v = router_dot<BF16>(xsm, r < e_main ? w_main + (int64_t)r * H : w_gate, H, lane);
+    if (lane == 0) logits[r] = v;
+  }
   __shared__ int32_t sids[32];
   __shared__ float stw[32];
   __syncthreads();
@@ -857,7 +864,8 @@ static int moe_forward_tok1(const blut_moe_args& a, const MoEWs& ws, cudaStream_
   const uint16_t* w_gate =
       !gate ? nullptr : a.shared_gate_w ? (const uint16_t*)a.shared_gate_w : (const uint16_t*)a.router_w + (int64_t)E * H;
   auto rk = bf16 ? tok1_route_kernel<true> : tok1_route_kernel<false>;
-  rk<<<1, 1024, 0, stream>>>((const uint16_t*)a.x, w_main, w_gate, H, E, K, a.renorm, a.topk_ids, a.topk_weights,
+  if (H * 2 > 48 * 1024) return BLUT_ERR_UNSUPPORTED;  // the token row is staged in shared memory
+  rk<<<1, 1024, H * 2, stream>>>((const uint16_t*)a.x, w_main, w_gate, H, E, K, a.renorm, a.topk_ids, a.topk_weights,
                              ws.logits, ws.t1_groups, ws.t1_gw, ws.sg, ws.status, ws.t1_cnt, ws.t1_ncnt, sh ? 1 : 0,
                              a.out, a.out_f32);
   int rc = stage_done("single-token route", stream);

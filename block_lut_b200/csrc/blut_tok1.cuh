@@ -75,6 +75,66 @@ __device__ __forceinline__ bool tok1_resolve(const Tok1Args& a, const Tok1Mat& m
   return true;
 }
 
+// Columns of one item's activation slice a thread stages (the slice is at
+// most tc_gemv_pf() pieces of 64 columns, or of 32 for dense weights).
+constexpr int kTok1XPer = 2;
+constexpr int kTok1MaxCols = kTok1XPer * kTok1Threads;
+
+// Sum of n fp32 values at p, p + stride, ... in index order, eight loads in
+// flight at a time (L2: other CTAs wrote them in this launch).
+__device__ __forceinline__ float tok1_sum(const float* p, int n, int64_t stride) {
+  float s = 0.f;
+  int i = 0;
+  for (; i + 8 <= n; i += 8) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = __ldcg(p + (i + k) * stride);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += v[k];
+  }
+  for (; i < n; ++i) s += __ldcg(p + i * stride);
+  return s;
+}
+
+// The epilogue of item `it`, run by the CTA whose completion of it was the
+// last of its unit (gate/up) or output tile (down).
+template <class Dec, bool PAIR>
+__device__ __forceinline__ void tok1_epilogue(const Tok1Args& a, const Tok1Mat& m, const Tok1Item& it) {
+  const TcParams& p = m.p;
+  const int row = threadIdx.x;
+  if constexpr (PAIR) {
+    // every slice of both tiles of this unit is in: SiLU(gate) * up
+    const int unit = it.pt >> 1;
+    const float* src = m.part + (((int64_t)it.gi * p.units + unit) * p.ks) * (2 * kTcRows) + row;
+    const float g = tok1_sum(src, p.ks, 2 * kTcRows);
+    const float u = tok1_sum(src + kTcRows, p.ks, 2 * kTcRows);
+    m.act[(int64_t)it.gi * (p.ntiles / 2) * kTcRows + unit * kTcRows + row] = f32_to_act<Dec::kBF16>(silu_f(g) * u);
+  } else {
+    // every contribution to this output tile is in: the weighted combine
+    const int h = it.pt * kTcRows + row;
+    const Tok1Mat& r = a.m[0];
+    const int ngr = min(a.groups[0], a.gbound);
+    float o = 0.f;
+    for (int g = 0; g < ngr; ++g)
+      o = fmaf(a.gw[g], tok1_sum(r.part + (int64_t)g * a.hidden + h, r.p.ks, (int64_t)a.gbound * a.hidden), o);
+    if (a.m[1].ctas > 0) {
+      const Tok1Mat& sm = a.m[1];
+      o = fmaf(a.sg ? *a.sg : 1.f, tok1_sum(sm.part + h, sm.p.ks, a.hidden), o);
+    }
+    if (a.out_f32)
+      static_cast<float*>(a.out)[h] = o;
+    else
+      static_cast<uint16_t*>(a.out)[h] = f32_to_act<Dec::kBF16>(o);
+  }
+}
+
+// Loop of one CTA over its items.  Per item: the activation slice staged
+// from registers loaded during the previous item, the weights already in the
+// register ring, the dot products with the next item's loads in flight, the
+// fp32 result stored, then one thread counts the item done (fence + atomic)
+// and reads that count only after the next item's compute, so neither the
+// atomic's round trip nor the staging loads sit on the critical path.  The
+// CTA that completes a unit or output tile runs its epilogue one item later.
 template <class Dec, bool PAIR>
 __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, bool shared, int cta, int nctas,
                                          uint8_t* smem) {
@@ -82,6 +142,7 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, bo
   constexpr int PF = tc_gemv_pf<Dec>();
   constexpr int W = Dec::kDense ? Dec::KB : 64;  // columns per piece
   using U = typename std::conditional<Dec::kDense, TcDenseBlk<Dec::kBF16>, typename Dec::Half>::type;
+  static_assert(PF * W <= kTok1MaxCols, "an item's slice must fit the staging registers");
   const TcParams& p = m.p;
   const int row = threadIdx.x;
   const int ng = shared ? 1 : min(a.groups[0], a.gbound);
@@ -90,19 +151,33 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, bo
   if constexpr (Dec::kR8) tab = smem_u32(smem) + (row & 31) * 4;
   float* xs = reinterpret_cast<float*>(smem + tc_table_bytes<Dec>());
   int64_t item = cta;
-  Tok1Item cur, nxt;
+  Tok1Item cur, nxt, prev{};
   if (!tok1_resolve<Dec>(a, m, shared, ng, item, cur)) return;  // uniform over the CTA
   if constexpr (Dec::kR8) tc_fill_r8_table(reinterpret_cast<uint32_t*>(smem), p.r8_table);
   U ring[PF];
 #pragma unroll
   for (int j = 0; j < PF; ++j)
     if (j < cur.n) tc_gemv_load<Dec>(p, cur.base, cur.pt, cur.b0, j, row, tab, ring[j]);
+  auto load_x = [&](const Tok1Item& it, uint16_t (&xr)[kTok1XPer]) {
+    const uint16_t* xrow = m.xin + (int64_t)it.gi * m.x_ld + it.b0 * KB;
+#pragma unroll
+    for (int k = 0; k < kTok1XPer; ++k) {
+      const int col = threadIdx.x + k * kTok1Threads;
+      xr[k] = col < it.n * W ? xrow[col] : uint16_t(0);
+    }
+  };
+  uint16_t xr[kTok1XPer];
+  load_x(cur, xr);
+  int prev_old = 0, prev_target = 0;  // thread 0: the count before the previous item's increment, and its goal
+  bool have_prev = false;
+  const int down_target = min(a.groups[0], a.gbound) * a.m[0].p.ks + (a.m[1].ctas > 0 ? a.m[1].p.ks : 0);
   for (;;) {
     const bool more = tok1_resolve<Dec>(a, m, shared, ng, item + nctas, nxt);
     __syncthreads();  // the previous item's reads of xs are done (and the R8 table is complete)
-    const uint16_t* xrow = m.xin + (int64_t)cur.gi * m.x_ld + cur.b0 * KB;
-    for (int col = threadIdx.x; col < cur.n * W; col += blockDim.x) xs[col] = act_to_f32<Dec::kBF16>(xrow[col]);
+#pragma unroll
+    for (int k = 0; k < kTok1XPer; ++k) xs[threadIdx.x + k * kTok1Threads] = act_to_f32<Dec::kBF16>(xr[k]);
     __syncthreads();  // xs complete
+    if (more) load_x(nxt, xr);
     float2 acc[1] = {make_float2(0.f, 0.f)};
 #pragma unroll
     for (int j = 0; j < PF; ++j) {
@@ -139,51 +214,31 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, bo
     } else {
       m.part[((int64_t)cur.s * (shared ? 1 : a.gbound) + cur.gi) * a.hidden + cur.pt * kTcRows + row] = v;
       counter = a.cnt + cur.pt;  // one counter per output tile, over both matrices
-      target = min(a.groups[0], a.gbound) * a.m[0].p.ks + (a.m[1].ctas > 0 ? a.m[1].p.ks : 0);
+      target = down_target;
     }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(counter, 1) == target - 1;
-    __syncthreads();
+    __syncthreads();  // this item's results are stored (the fence below publishes them for the whole CTA)
+    if (threadIdx.x == 0) {
+      s_last = have_prev && prev_old == prev_target - 1;  // the previous item's count is back by now
+      __threadfence();
+      prev_old = atomicAdd(counter, 1);
+      prev_target = target;
+    }
+    __syncthreads();  // s_last visible
     if (s_last) {
       __threadfence();
-      if constexpr (PAIR) {
-        // every slice of both tiles of this unit is in: SiLU(gate) * up
-        const int unit = cur.pt >> 1;
-        const float* src = m.part + (((int64_t)cur.gi * p.units + unit) * p.ks) * (2 * kTcRows) + row;
-        float g = 0.f, u = 0.f;
-        for (int sl = 0; sl < p.ks; ++sl) {
-          g += __ldcg(src + sl * (2 * kTcRows));
-          u += __ldcg(src + sl * (2 * kTcRows) + kTcRows);
-        }
-        m.act[(int64_t)cur.gi * (p.ntiles / 2) * kTcRows + unit * kTcRows + row] =
-            f32_to_act<Dec::kBF16>(silu_f(g) * u);
-      } else {
-        // every contribution to this output tile is in: the weighted combine
-        const int h = cur.pt * kTcRows + row;
-        const Tok1Mat& r = a.m[0];
-        const int ngr = min(a.groups[0], a.gbound);
-        float o = 0.f;
-        for (int g = 0; g < ngr; ++g) {
-          float y = 0.f;
-          for (int sl = 0; sl < r.p.ks; ++sl) y += __ldcg(r.part + ((int64_t)sl * a.gbound + g) * a.hidden + h);
-          o = fmaf(a.gw[g], y, o);
-        }
-        if (a.m[1].ctas > 0) {
-          const Tok1Mat& sm = a.m[1];
-          float y = 0.f;
-          for (int sl = 0; sl < sm.p.ks; ++sl) y += __ldcg(sm.part + (int64_t)sl * a.hidden + h);
-          o = fmaf(a.sg ? *a.sg : 1.f, y, o);
-        }
-        if (a.out_f32)
-          static_cast<float*>(a.out)[h] = o;
-        else
-          static_cast<uint16_t*>(a.out)[h] = f32_to_act<Dec::kBF16>(o);
-      }
+      tok1_epilogue<Dec, PAIR>(a, m, prev);
     }
+    prev = cur;
+    have_prev = true;
     if (!more) break;
     cur = nxt;
     item += nctas;
+  }
+  if (threadIdx.x == 0) s_last = prev_old == prev_target - 1;
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    tok1_epilogue<Dec, PAIR>(a, m, prev);
   }
 }
 
@@ -197,12 +252,11 @@ __global__ void __launch_bounds__(kTok1Threads, 4) tok1_kernel(const Tok1Args a)
     tok1_run<TcDecDense<Dec::kBF16>, PAIR>(a, a.m[1], true, blockIdx.x - a.m[0].ctas, a.m[1].ctas, tsm);
 }
 
-// Shared-memory bytes of a tok1 launch.
+// Shared-memory bytes of a tok1 launch: the FMT_R8 table, then the staged
+// activation slice (every thread writes its kTok1XPer columns).
 template <class Dec>
-inline int tok1_smem(const Tok1Args& a) {
-  int cols = a.m[0].p.bps * Dec::KB;
-  if (a.m[1].ctas > 0) cols = std::max(cols, a.m[1].p.bps * TcDecDense<Dec::kBF16>::KB);
-  return tc_table_bytes<Dec>() + cols * 4;
+inline int tok1_smem(const Tok1Args&) {
+  return tc_table_bytes<Dec>() + kTok1MaxCols * 4;
 }
 
 // CTAs of the routed and shared parts: the resident CTAs of the GPU, split

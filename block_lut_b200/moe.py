@@ -265,7 +265,9 @@ class LUTMoEStep:
     buffer ``host_in[i]`` [batch, H] and a pinned host output buffer
     ``host_out[i]``, and captures one graph that copies every input to the
     device, runs every layer on its own input (``layer.forward``, this
-    library's routing and experts) and copies every output back.  ``run()``
+    library's routing and experts) and copies every output back.  The copies
+    run on a second stream inside the graph: layer i + 1's input arrives and
+    layer i's output leaves while the layers compute.  ``run()``
     replays it on the current stream; the caller fills ``host_in`` before and
     reads ``host_out`` after a ``torch.cuda.synchronize()`` (or an event).
     The layers run one after another on one stream, so they share their
@@ -287,6 +289,9 @@ class LUTMoEStep:
         self._dev_in = [torch.zeros(self.batch, h, dtype=m.dtype, device=dev) for h, m in zip(H, self.layers)]
         self._dev_out = [torch.empty_like(t) for t in self._dev_in]
         with torch.cuda.device(dev):
+            self._copy = torch.cuda.Stream(device=dev)
+            self._ev_in = [torch.cuda.Event() for _ in self.layers]
+            self._ev_out = [torch.cuda.Event() for _ in self.layers]
             side = torch.cuda.Stream(device=dev)
             side.wait_stream(torch.cuda.current_stream(dev))
             with torch.cuda.stream(side):  # first calls: workspaces and the library's side stream
@@ -300,10 +305,22 @@ class LUTMoEStep:
         torch.cuda.synchronize(dev)
 
     def _body(self) -> None:
-        for m, hi, di, do, ho in zip(self.layers, self.host_in, self._dev_in, self._dev_out, self.host_out):
-            di.copy_(hi, non_blocking=True)
+        main = torch.cuda.current_stream(self.device)
+        cp = self._copy
+        cp.wait_stream(main)
+        with torch.cuda.stream(cp):
+            for hi, di, ev in zip(self.host_in, self._dev_in, self._ev_in):
+                di.copy_(hi, non_blocking=True)
+                ev.record(cp)
+        for m, di, do, ei, eo in zip(self.layers, self._dev_in, self._dev_out, self._ev_in, self._ev_out):
+            main.wait_event(ei)
             m.forward(di, out=do)
-            ho.copy_(do, non_blocking=True)
+            eo.record(main)
+        with torch.cuda.stream(cp):
+            for do, ho, eo in zip(self._dev_out, self.host_out, self._ev_out):
+                cp.wait_event(eo)
+                ho.copy_(do, non_blocking=True)
+        main.wait_stream(cp)
 
     def run(self) -> None:
         """Replays the step on the current stream (asynchronous)."""
