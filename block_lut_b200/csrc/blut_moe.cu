@@ -9,6 +9,7 @@
 #include <mutex>
 
 #include "blut_internal.h"
+#include "blut_route.cuh"
 #include "blut_tc.cuh"
 #include "blut_tok1.cuh"
 
@@ -22,23 +23,24 @@ namespace blut {
 // One warp's fp32 dot product of x and w (H elements).  Lane l takes the
 // 8-element chunks l, l + 32, ...; chunk c accumulates into acc[c % 4], in
 // chunk order, and the four sums are added pairwise, then across the warp.
-// Each lane issues eight chunks' weight loads before their FMAs.
+// Each lane issues eight chunks' weight and activation loads before their
+// FMAs.
 template <bool BF16>
 __device__ __forceinline__ float router_dot(const uint16_t* xr, const uint16_t* __restrict__ wr, int H, int lane) {
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int k0 = lane * 8; k0 < H; k0 += 32 * 8 * 8) {
-    uint4 wv[8];
+    uint4 wv[8], xv[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int k = k0 + q * 256;
       wv[q] = k < H ? *reinterpret_cast<const uint4*>(wr + k) : make_uint4(0, 0, 0, 0);
+      xv[q] = k < H ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int k = k0 + q * 256;
       if (k >= H) break;
-      const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
-      const uint16_t* xs = reinterpret_cast<const uint16_t*>(&xv);
+      const uint16_t* xs = reinterpret_cast<const uint16_t*>(&xv[q]);
       const uint16_t* ws = reinterpret_cast<const uint16_t*>(&wv[q]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[q & 3] = fmaf(act_to_f32<BF16>(xs[e]), act_to_f32<BF16>(ws[e]), acc[q & 3]);
@@ -65,71 +67,6 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
   if (lane == 0) logits[(int64_t)t * R + r] = s;
 }
 
-// Softmax over E logits (fp32) and top-k with the lowest expert index winning
-// ties, optional renormalisation; one warp per token.  Row R-1 of a logits
-// row with a gate entry yields sigmoid(logit) in *sg.
-template <int kPer>  // expert logits per lane: E <= 32 * kPer
-__device__ void warp_topk_n(const float* __restrict__ lg, int E, int K, int renorm, int32_t* ids, float* tw) {
-  const int lane = threadIdx.x & 31;
-  float v[kPer];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int e = lane + 32 * i;
-    v[i] = e < E ? lg[e] : -INFINITY;
-    mx = fmaxf(mx, v[i]);
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum = 0.f;
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int e = lane + 32 * i;
-    v[i] = e < E ? expf(v[i] - mx) : -1.f;
-    sum += e < E ? v[i] : 0.f;
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float inv = 1.f / sum;
-  float wsum = 0.f, myw = 0.f;
-  int myid = 0;
-  for (int j = 0; j < K; ++j) {
-    float best = -1.f;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      if (v[i] > best) { best = v[i]; bi = lane + 32 * i; }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-    }
-    const float p = best * inv;
-    wsum += p;
-    if (lane == j) { myw = p; myid = bi; }
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      if (lane + 32 * i == bi) v[i] = -2.f;  // taken
-    }
-  }
-  if (lane < K) {
-    ids[lane] = myid;
-    tw[lane] = renorm ? myw / wsum : myw;
-  }
-}
-
-__device__ void warp_topk(const float* __restrict__ lg, int E, int K, int renorm, int32_t* ids, float* tw,
-                          float* sg_out, bool has_gate) {
-  if (has_gate && (threadIdx.x & 31) == 0) *sg_out = 1.f / (1.f + expf(-lg[E]));
-  if (K <= 0) return;
-  if (E <= 64) warp_topk_n<2>(lg, E, K, renorm, ids, tw);
-  else if (E <= 128) warp_topk_n<4>(lg, E, K, renorm, ids, tw);
-  else if (E <= 256) warp_topk_n<8>(lg, E, K, renorm, ids, tw);
-  else warp_topk_n<kMaxExperts / 32>(lg, E, K, renorm, ids, tw);
-}
-
 // Standalone top-k over router logits (the blut_router entry point).
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int T, int E, int K,
                                                    int renorm, int has_gate, int32_t* __restrict__ ids,
@@ -141,66 +78,29 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
             has_gate ? sg + t : nullptr, has_gate != 0);
 }
 
-// Single-token path (blut_tok1.cuh), launch 1 of 3.  One CTA: the logits
-// of the R rows (experts, then the shared-expert gate row) a warp per row;
-// the completion counters of the two GEMV launches and the status word
-// zeroed; then warp 0 takes the top-k (or checks the caller's ids) and
-// writes the group table: one group per valid slot, in slot order, with its
-// routing weight.
+// Single-token path (blut_tok1.cuh), launch 1 of 3: the token's router
+// logits (experts, then the shared-expert gate row, whose sigmoid goes to
+// *sg), a warp per row, eight rows per CTA; CTA 0 also zeroes the status word
+// and the completion counters of the two GEMV launches.  The top-k runs in
+// the gate/up launch, in every CTA that needs it.
 template <bool BF16>
-__global__ void __launch_bounds__(1024) tok1_route_kernel(const uint16_t* __restrict__ x,
+__global__ void __launch_bounds__(256) tok1_logits_kernel(const uint16_t* __restrict__ x,
                                                           const uint16_t* __restrict__ w_main,
-                                                          const uint16_t* __restrict__ w_gate, int H, int E, int K,
-                                                          int renorm, const int32_t* __restrict__ ids_in,
-                                                          const float* __restrict__ tw_in, float* __restrict__ logits,
-                                                          int* __restrict__ groups, float* __restrict__ gw,
-                                                          float* __restrict__ sg, int* __restrict__ status,
-                                                          int* __restrict__ cnt, int ncnt, int has_shared,
-                                                          void* __restrict__ out, int out_f32) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e_main = w_main ? E : 0;
+                                                          const uint16_t* __restrict__ w_gate, int H, int e_main,
+                                                          float* __restrict__ logits, float* __restrict__ sg,
+                                                          int* __restrict__ cnt, int ncnt, int* __restrict__ status) {
+  const int lane = threadIdx.x & 31;
   const int R = e_main + (w_gate ? 1 : 0);
-  extern __shared__ __align__(16) uint16_t xsm[];  // the token row, read by every warp
-  for (int i = threadIdx.x; i < H / 8; i += blockDim.x)
-    reinterpret_cast<uint4*>(xsm)[i] = reinterpret_cast<const uint4*>(x)[i];
-  for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
-  if (threadIdx.x == 0) *status = 0;  // the status word reports this call only, as the plan kernel's does
-  __syncthreads();
-  for (int r = warp; r < R; r += 32) {
-    const float v = router_dot<BF16>(xsm, r < e_main ? w_main + (int64_t)r * H : w_gate, H, lane);
-    if (lane == 0) logits[r] = v;
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
+    if (threadIdx.x == 0) *status = 0;  // the status word reports this call only, as the plan kernel's does
   }
-  __shared__ int32_t sids[32];
-  __shared__ float stw[32];
-  __syncthreads();
-  if (warp != 0) return;
-  if (w_main) {
-    warp_topk(logits, E, K, renorm, sids, stw, sg, w_gate != nullptr);
-  } else {
-    if (w_gate && lane == 0) *sg = 1.f / (1.f + expf(-logits[0]));
-    if (lane < K) {
-      sids[lane] = ids_in[lane];
-      stw[lane] = tw_in[lane];
-    }
-  }
-  __syncwarp();
-  const int id = lane < K ? sids[lane] : -1;
-  const bool ok = lane < K && id >= 0 && id < E;
-  if (lane < K && !ok && id != -1) atomicOr(status, kDevBadExpert);  // -1 = empty slot
-  const unsigned m = __ballot_sync(0xffffffffu, ok);
-  if (ok) {
-    const int g = __popc(m & ((1u << lane) - 1u));
-    groups[1 + g] = id;
-    gw[g] = stw[lane];
-  }
-  if (lane == 0) groups[0] = __popc(m);
-  if (m == 0 && !has_shared) {  // no expert and no shared expert: the GEMV launches write nothing
-    for (int h = lane; h < H; h += 32) {
-      if (out_f32)
-        static_cast<float*>(out)[h] = 0.f;
-      else
-        static_cast<uint16_t*>(out)[h] = 0;
-    }
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= R) return;
+  const float v = router_dot<BF16>(x, r < e_main ? w_main + (int64_t)r * H : w_gate, H, lane);
+  if (lane == 0) {
+    logits[r] = v;
+    if (r == e_main) *sg = 1.f / (1.f + expf(-v));
   }
 }
 
@@ -598,7 +498,7 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
 }
 
 bool tok1_applies(const blut_moe_args& a, const MoESplit& s) {
-  return a.num_tokens == 1 && s.gemv[0] && (a.shared_inter <= 0 || s.gemv[1]);
+  return a.num_tokens == 1 && s.gemv[0] && (a.shared_inter <= 0 || s.gemv[1]) && a.num_experts <= kTok1MaxExperts;
 }
 
 // K slices of a single-token GEMV pass: each slice the blocks of the pieces a
@@ -863,12 +763,12 @@ static int moe_forward_tok1(const blut_moe_args& a, const MoEWs& ws, cudaStream_
   const uint16_t* w_main = route ? (const uint16_t*)a.router_w : nullptr;
   const uint16_t* w_gate =
       !gate ? nullptr : a.shared_gate_w ? (const uint16_t*)a.shared_gate_w : (const uint16_t*)a.router_w + (int64_t)E * H;
-  auto rk = bf16 ? tok1_route_kernel<true> : tok1_route_kernel<false>;
-  if (H * 2 > 48 * 1024) return BLUT_ERR_UNSUPPORTED;  // the token row is staged in shared memory
-  rk<<<1, 1024, H * 2, stream>>>((const uint16_t*)a.x, w_main, w_gate, H, E, K, a.renorm, a.topk_ids, a.topk_weights,
-                             ws.logits, ws.t1_groups, ws.t1_gw, ws.sg, ws.status, ws.t1_cnt, ws.t1_ncnt, sh ? 1 : 0,
-                             a.out, a.out_f32);
-  int rc = stage_done("single-token route", stream);
+  const int e_main = route ? E : 0;
+  const int R = e_main + (gate ? 1 : 0);
+  auto lk = bf16 ? tok1_logits_kernel<true> : tok1_logits_kernel<false>;
+  lk<<<std::max(1, (R + 7) / 8), 256, 0, stream>>>((const uint16_t*)a.x, w_main, w_gate, H, e_main, ws.logits, ws.sg,
+                                                     ws.t1_cnt, ws.t1_ncnt, ws.status);
+  int rc = stage_done("single-token router logits", stream);
   if (rc != BLUT_OK) return rc;
 
   // the two projections: routed matrices in part 0, the shared expert in part 1
@@ -900,6 +800,15 @@ static int moe_forward_tok1(const blut_moe_args& a, const MoEWs& ws, cudaStream_
   g.sg = gate ? ws.sg : nullptr;
   g.gbound = K;
   g.hidden = H;
+  g.logits = route ? ws.logits : nullptr;
+  g.ids_in = a.topk_ids;
+  g.tw_in = a.topk_weights;
+  g.num_experts = E;
+  g.renorm = a.renorm;
+  g.status = ws.status;
+  g.has_shared = sh ? 1 : 0;
+  g.out = a.out;
+  g.out_f32 = a.out_f32;
   if (!mat(a.w13, a.w13_tiled, a.w13_stride, true, 0, g.m[0])) return BLUT_ERR_UNSUPPORTED;
   g.m[0].xin = (const uint16_t*)a.x;
   g.m[0].part = ws.t1_part_r;

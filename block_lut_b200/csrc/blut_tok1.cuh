@@ -2,12 +2,13 @@
 // reference's GEMV targets): three launches instead of the general path's
 // router / plan / gather / gate-up / slice-sum / down / combine chain.
 //
-//   tok1_route_kernel (blut_moe.cu)  router logits, top-k, the group table
-//       (one group per routed expert of the token) and zeroed counters;
-//   tok1_kernel<Dec, pair = true>    gate/up of every routed group and of the
-//       shared expert in one persistent launch; the last CTA to finish a
-//       128-row unit (both of its tiles, every K slice) sums the slices and
-//       writes SiLU(gate) * up for that unit;
+//   tok1_logits_kernel (blut_moe.cu)  the router logits, the shared-expert
+//       gate, zeroed counters and status;
+//   tok1_kernel<Dec, pair = true>    the top-k (in every routed CTA), then
+//       gate/up of every routed group and of the shared expert in one
+//       persistent launch; the last CTA to finish a 128-row unit (both of
+//       its tiles, every K slice) sums the slices and writes SiLU(gate) * up
+//       for that unit;
 //   tok1_kernel<Dec, pair = false>   down of every group and the shared
 //       expert; the last CTA to finish an output tile sums, for its rows,
 //       every group's slices weighted by the routing weight plus the shared
@@ -21,6 +22,7 @@
 // gate/up, a group's SiLU * up row for down), so no gather is needed.
 #pragma once
 
+#include "blut_route.cuh"
 #include "blut_tc.cuh"
 
 namespace blut {
@@ -39,17 +41,73 @@ struct Tok1Mat {
   int cnt0;            // gate/up: first completion counter of this matrix ([group][unit])
 };
 
+// Experts of at most this many: the gate/up CTAs take the top-k themselves.
+constexpr int kTok1MaxExperts = 256;
+
 struct Tok1Args {
   Tok1Mat m[2];        // routed experts, shared expert (m[1].ctas == 0: none)
-  const int* groups;   // [0] routed groups, [1 + g] expert of group g
-  const float* gw;     // [g] routing weight of group g
+  int* groups;         // [0] routed groups, [1 + g] expert of group g (written by the gate/up launch)
+  float* gw;           // [g] routing weight of group g
   const float* sg;     // shared expert gate (nullptr: 1)
-  int* cnt;            // completion counters (zeroed by the route kernel)
+  int* cnt;            // completion counters (zeroed by the logits kernel)
   int gbound;          // routed group bound (the top-k)
-  void* out;           // down: the layer output [hidden], fp16 / bf16 or fp32
+  void* out;           // the layer output [hidden], fp16 / bf16 or fp32
   int out_f32;
   int hidden;
+  // routing, used by the gate/up launch
+  const float* logits;     // router logits of the token [num_experts]; nullptr: the caller's ids
+  const int32_t* ids_in;   // the caller's top-k ids and weights [gbound]
+  const float* tw_in;
+  int num_experts, renorm;
+  int* status;
+  int has_shared;
 };
+
+// Warp 0 of a routed gate/up CTA: the token's top-k (softmax over the
+// logits, lowest index on ties, optional renormalisation) or the caller's
+// ids, as the group table in shared memory (one group per valid slot, in slot
+// order).  CTA 0 also publishes the table for the down launch, flags ids out
+// of range (-1 is an empty slot) and, when the token has no expert and there
+// is no shared expert, writes the zero output no GEMV item will write.
+__device__ __forceinline__ void tok1_route_warp(const Tok1Args& a, int* s_groups, float* s_gw, bool publish) {
+  __shared__ int32_t sids[32];
+  __shared__ float stw[32];
+  const int lane = threadIdx.x & 31;
+  const int K = a.gbound, E = a.num_experts;
+  if (a.logits) {
+    if (E <= 64) warp_topk_n<2>(a.logits, E, K, a.renorm, sids, stw);
+    else if (E <= 128) warp_topk_n<4>(a.logits, E, K, a.renorm, sids, stw);
+    else warp_topk_n<8>(a.logits, E, K, a.renorm, sids, stw);
+  } else if (lane < K) {
+    sids[lane] = a.ids_in[lane];
+    stw[lane] = a.tw_in[lane];
+  }
+  __syncwarp();
+  const int id = lane < K ? sids[lane] : -1;
+  const bool ok = lane < K && id >= 0 && id < E;
+  const unsigned msk = __ballot_sync(0xffffffffu, ok);
+  if (ok) {
+    const int g = __popc(msk & ((1u << lane) - 1u));
+    s_groups[1 + g] = id;
+    s_gw[g] = stw[lane];
+    if (publish) {
+      a.groups[1 + g] = id;
+      a.gw[g] = stw[lane];
+    }
+  }
+  if (lane == 0) s_groups[0] = __popc(msk);
+  if (!publish) return;
+  if (lane == 0) a.groups[0] = __popc(msk);
+  if (lane < K && !ok && id != -1) atomicOr(a.status, kDevBadExpert);
+  if (msk == 0 && !a.has_shared) {
+    for (int h = lane; h < a.hidden; h += 32) {
+      if (a.out_f32)
+        static_cast<float*>(a.out)[h] = 0.f;
+      else
+        static_cast<uint16_t*>(a.out)[h] = 0;
+    }
+  }
+}
 
 struct Tok1Item {
   int gi, pt, s, b0, n;
@@ -59,7 +117,7 @@ struct Tok1Item {
 // Item `it` of matrix m (ordered (group, tile, slice)); false past the last
 // item or at a group that does not exist (every later item's group is larger).
 template <class Dec>
-__device__ __forceinline__ bool tok1_resolve(const Tok1Args& a, const Tok1Mat& m, bool shared, int ng, int64_t it,
+__device__ __forceinline__ bool tok1_resolve(const int* groups, const Tok1Mat& m, bool shared, int ng, int64_t it,
                                              Tok1Item& r) {
   const TcParams& p = m.p;
   if (it >= m.n_items) return false;
@@ -70,7 +128,7 @@ __device__ __forceinline__ bool tok1_resolve(const Tok1Args& a, const Tok1Mat& m
   r.b0 = r.s * p.bps;
   const int b1 = min(p.nblocks, r.b0 + p.bps);
   r.n = r.b0 < b1 ? (b1 - r.b0) * (Dec::kDense ? 1 : Dec::kHalves) : 0;
-  const int e = shared ? 0 : a.groups[1 + r.gi];
+  const int e = shared ? 0 : groups[1 + r.gi];
   r.base = p.w + (int64_t)e * p.wstride;
   return true;
 }
@@ -136,8 +194,8 @@ __device__ __forceinline__ void tok1_epilogue(const Tok1Args& a, const Tok1Mat& 
 // atomic's round trip nor the staging loads sit on the critical path.  The
 // CTA that completes a unit or output tile runs its epilogue one item later.
 template <class Dec, bool PAIR>
-__device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, bool shared, int cta, int nctas,
-                                         uint8_t* smem) {
+__device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, const int* groups, bool shared, int cta,
+                                         int nctas, uint8_t* smem) {
   constexpr int KB = Dec::KB;
   constexpr int PF = tc_gemv_pf<Dec>();
   constexpr int W = Dec::kDense ? Dec::KB : 64;  // columns per piece
@@ -145,14 +203,14 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, bo
   static_assert(PF * W <= kTok1MaxCols, "an item's slice must fit the staging registers");
   const TcParams& p = m.p;
   const int row = threadIdx.x;
-  const int ng = shared ? 1 : min(a.groups[0], a.gbound);
+  const int ng = shared ? 1 : min(groups[0], a.gbound);
   __shared__ int s_last;
   uint32_t tab = 0;
   if constexpr (Dec::kR8) tab = smem_u32(smem) + (row & 31) * 4;
   float* xs = reinterpret_cast<float*>(smem + tc_table_bytes<Dec>());
   int64_t item = cta;
   Tok1Item cur, nxt, prev{};
-  if (!tok1_resolve<Dec>(a, m, shared, ng, item, cur)) return;  // uniform over the CTA
+  if (!tok1_resolve<Dec>(groups, m, shared, ng, item, cur)) return;  // uniform over the CTA
   if constexpr (Dec::kR8) tc_fill_r8_table(reinterpret_cast<uint32_t*>(smem), p.r8_table);
   U ring[PF];
 #pragma unroll
@@ -170,9 +228,9 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, bo
   load_x(cur, xr);
   int prev_old = 0, prev_target = 0;  // thread 0: the count before the previous item's increment, and its goal
   bool have_prev = false;
-  const int down_target = min(a.groups[0], a.gbound) * a.m[0].p.ks + (a.m[1].ctas > 0 ? a.m[1].p.ks : 0);
+  const int down_target = PAIR ? 0 : min(groups[0], a.gbound) * a.m[0].p.ks + (a.m[1].ctas > 0 ? a.m[1].p.ks : 0);
   for (;;) {
-    const bool more = tok1_resolve<Dec>(a, m, shared, ng, item + nctas, nxt);
+    const bool more = tok1_resolve<Dec>(groups, m, shared, ng, item + nctas, nxt);
     __syncthreads();  // the previous item's reads of xs are done (and the R8 table is complete)
 #pragma unroll
     for (int k = 0; k < kTok1XPer; ++k) xs[threadIdx.x + k * kTok1Threads] = act_to_f32<Dec::kBF16>(xr[k]);
@@ -243,13 +301,25 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, bo
 }
 
 // CTAs [0, m[0].ctas) work on the routed experts, the rest on the shared one.
+// In the gate/up launch every routed CTA takes the token's top-k first (the
+// shared expert's CTAs need none); the down launch reads the table CTA 0 of
+// the gate/up launch published.
 template <class Dec, bool PAIR>
 __global__ void __launch_bounds__(kTok1Threads, 4) tok1_kernel(const Tok1Args a) {
   extern __shared__ __align__(16) uint8_t tsm[];
-  if ((int)blockIdx.x < a.m[0].ctas)
-    tok1_run<Dec, PAIR>(a, a.m[0], false, blockIdx.x, a.m[0].ctas, tsm);
-  else
-    tok1_run<TcDecDense<Dec::kBF16>, PAIR>(a, a.m[1], true, blockIdx.x - a.m[0].ctas, a.m[1].ctas, tsm);
+  __shared__ int s_groups[33];
+  __shared__ float s_gw[32];
+  if ((int)blockIdx.x < a.m[0].ctas) {
+    const int* groups = a.groups;
+    if constexpr (PAIR) {
+      if (threadIdx.x < 32) tok1_route_warp(a, s_groups, s_gw, blockIdx.x == 0);
+      __syncthreads();
+      groups = s_groups;
+    }
+    tok1_run<Dec, PAIR>(a, a.m[0], groups, false, blockIdx.x, a.m[0].ctas, tsm);
+  } else {
+    tok1_run<TcDecDense<Dec::kBF16>, PAIR>(a, a.m[1], a.groups, true, blockIdx.x - a.m[0].ctas, a.m[1].ctas, tsm);
+  }
 }
 
 // Shared-memory bytes of a tok1 launch: the FMT_R8 table, then the staged
