@@ -501,13 +501,13 @@ bool tok1_applies(const blut_moe_args& a, const MoESplit& s) {
   return a.num_tokens == 1 && s.gemv[0] && (a.shared_inter <= 0 || s.gemv[1]) && a.num_experts <= kTok1MaxExperts;
 }
 
-// K slices of a single-token GEMV pass: each slice the blocks of the pieces a
-// thread keeps in flight (the persistent grid needs no more items than that).
+// K slices of a single-token GEMV pass: a slice is the 256 columns a
+// thread stages (kTok1MaxCols), one or two rounds of its register ring.
 static void tok1_slices(const blut_mat_desc& d, int& bps, int& ks) {
   TiledLayout L;
   bps = ks = 0;
   if (!make_layout(d, L)) return;
-  bps = std::max(1, tc_gemv_blocks(d));
+  bps = std::max(1, kTok1MaxCols / (int)L.kb);
   ks = (int)((L.nchunks + bps - 1) / bps);
 }
 

@@ -133,8 +133,8 @@ __device__ __forceinline__ bool tok1_resolve(const int* groups, const Tok1Mat& m
   return true;
 }
 
-// Columns of one item's activation slice a thread stages (the slice is at
-// most tc_gemv_pf() pieces of 64 columns, or of 32 for dense weights).
+// Columns of one item's activation slice a thread stages: an item is 256
+// columns (tok1_slices), one or two rounds of the thread's register ring.
 constexpr int kTok1XPer = 2;
 constexpr int kTok1MaxCols = kTok1XPer * kTok1Threads;
 
@@ -200,7 +200,7 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, co
   constexpr int PF = tc_gemv_pf<Dec>();
   constexpr int W = Dec::kDense ? Dec::KB : 64;  // columns per piece
   using U = typename std::conditional<Dec::kDense, TcDenseBlk<Dec::kBF16>, typename Dec::Half>::type;
-  static_assert(PF * W <= kTok1MaxCols, "an item's slice must fit the staging registers");
+  static_assert(kTok1MaxCols % (PF * W) == 0, "an item is whole rounds of the register ring");
   const TcParams& p = m.p;
   const int row = threadIdx.x;
   const int ng = shared ? 1 : min(groups[0], a.gbound);
@@ -237,28 +237,36 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, co
     __syncthreads();  // xs complete
     if (more) load_x(nxt, xr);
     float2 acc[1] = {make_float2(0.f, 0.f)};
+    // the item's pieces in rounds of PF: a slot's next content is the piece
+    // PF further on in this item, or in the last round the same slot's piece
+    // of the CTA's next item
+    for (int i0 = 0; i0 < cur.n; i0 += PF) {
 #pragma unroll
-    for (int j = 0; j < PF; ++j) {
-      if (j < cur.n) {
-        if constexpr (Dec::kDense) {
-          uint32_t o[16];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            o[4 * k] = ring[j].v[k].x; o[4 * k + 1] = ring[j].v[k].y;
-            o[4 * k + 2] = ring[j].v[k].z; o[4 * k + 3] = ring[j].v[k].w;
-          }
-          tc_gemv_fma32<Dec::kBF16, 1>(o, xs, 0, j * W, acc);
-        } else {
-#pragma unroll
-          for (int qq = 0; qq < 2; ++qq) {
+      for (int j = 0; j < PF; ++j) {
+        const int i = i0 + j;
+        if (i < cur.n) {
+          if constexpr (Dec::kDense) {
             uint32_t o[16];
-            Dec::lookup_q(ring[j], qq, o, p.mul);
-            tc_gemv_fma32<Dec::kBF16, 1>(o, xs, 0, j * W + 32 * qq, acc);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              o[4 * k] = ring[j].v[k].x; o[4 * k + 1] = ring[j].v[k].y;
+              o[4 * k + 2] = ring[j].v[k].z; o[4 * k + 3] = ring[j].v[k].w;
+            }
+            tc_gemv_fma32<Dec::kBF16, 1>(o, xs, 0, i * W, acc);
+          } else {
+#pragma unroll
+            for (int qq = 0; qq < 2; ++qq) {
+              uint32_t o[16];
+              Dec::lookup_q(ring[j], qq, o, p.mul);
+              tc_gemv_fma32<Dec::kBF16, 1>(o, xs, 0, i * W + 32 * qq, acc);
+            }
           }
         }
+        if (i + PF < cur.n)
+          tc_gemv_load<Dec>(p, cur.base, cur.pt, cur.b0, i + PF, row, tab, ring[j]);
+        else if (i0 + PF >= cur.n && more && j < nxt.n)
+          tc_gemv_load<Dec>(p, nxt.base, nxt.pt, nxt.b0, j, row, tab, ring[j]);
       }
-      // this slot's next content: the same piece of the CTA's next item
-      if (more && j < nxt.n) tc_gemv_load<Dec>(p, nxt.base, nxt.pt, nxt.b0, j, row, tab, ring[j]);
     }
     const float v = acc[0].x + acc[0].y;
     int* counter;
