@@ -460,8 +460,8 @@ def run_ours(a):
 
     # e2e through the public API: pinned host inputs -> device -> layers ->
     # host, every step.  The serving path is LUTMoEStep (one CUDA graph per
-    # step, copies included); the same step through per-layer eager
-    # LUTMoELayer.forward calls is reported beside it.
+    # step, both transfers included); the same step through per-layer eager
+    # LUTMoELayer.forward calls with per-layer copies is reported beside it.
     e2e = None
     if not a.no_e2e:
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -501,9 +501,9 @@ def run_ours(a):
         e2e = {"value": a.batch / (g_ms / 1e3), "unit": "tokens/s", "ms_per_step": g_ms,
                "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs),
                "d2h_bytes_per_step": sum(x.numel() * 2 for x in xs),
-               "path": "LUTMoEStep.run: one CUDA graph per step copying each layer's input from pinned host "
-                       "memory, running LUTMoELayer.forward (router + experts + shared) and copying the output "
-                       "back to pinned host memory",
+               "path": "LUTMoEStep.run: one CUDA graph per step that copies every layer's input from pinned "
+                       "host memory in one transfer, runs LUTMoELayer.forward (router + experts + shared) per "
+                       "layer and copies every output back to pinned host memory in one transfer",
                "outputs_match_device_graph": same,
                "eager": {"value": a.batch / (e_ms / 1e3), "ms_per_step": e_ms,
                          "path": "LUTMoELayer.forward per layer from Python with pinned host I/O"}}

@@ -261,16 +261,16 @@ class LUTMoEStep:
     batch size: the shape in which a serving engine runs the layers (vLLM
     captures its decode step the same way).
 
-    ``LUTMoEStep(layers, batch)`` builds, for every layer, a pinned host input
-    buffer ``host_in[i]`` [batch, H] and a pinned host output buffer
-    ``host_out[i]``, and captures one graph that copies every input to the
-    device, runs every layer on its own input (``layer.forward``, this
-    library's routing and experts) and copies every output back.  The copies
-    run on a second stream inside the graph: layer i + 1's input arrives and
-    layer i's output leaves while the layers compute.  ``run()``
-    replays it on the current stream; the caller fills ``host_in`` before and
-    reads ``host_out`` after a ``torch.cuda.synchronize()`` (or an event).
-    The layers run one after another on one stream, so they share their
+    ``LUTMoEStep(layers, batch)`` needs layers of one hidden size and dtype.
+    It builds a pinned host input buffer ``host_in`` [layers, batch, H] (one
+    [batch, H] input per layer, ``host_in[i]``) and a pinned host output
+    buffer ``host_out`` of the same shape. It then captures one graph that
+    copies all inputs to the device in one transfer, runs every layer on its
+    own input (``layer.forward``: this library's routing and experts) and
+    copies all outputs back in one transfer.  ``run()`` replays it on the
+    current stream; the caller fills ``host_in`` before and reads
+    ``host_out`` after a ``torch.cuda.synchronize()`` (or an event).  The
+    layers run one after another on one stream, so they share their
     workspace as in eager calls; a later call that grows that workspace (a
     larger batch on the same layers) invalidates the graph, so capture a
     step per batch size after the largest eager call.
@@ -280,18 +280,20 @@ class LUTMoEStep:
         if not layers:
             raise ValueError("LUTMoEStep needs at least one layer")
         self.layers = list(layers)
+        H = {m.experts.hidden for m in self.layers}
+        dt = {m.dtype for m in self.layers}
+        if len(H) != 1 or len(dt) != 1:
+            raise ValueError("LUTMoEStep stacks layers of one hidden size and dtype")
+        H, dt = H.pop(), dt.pop()
         self.batch = int(batch)
         dev = torch.device(device) if device is not None else self.layers[0].experts.w13.device
         self.device = dev
-        H = [m.experts.hidden for m in self.layers]
-        self.host_in = [torch.zeros(self.batch, h, dtype=m.dtype).pin_memory() for h, m in zip(H, self.layers)]
-        self.host_out = [torch.zeros(self.batch, h, dtype=m.dtype).pin_memory() for h, m in zip(H, self.layers)]
-        self._dev_in = [torch.zeros(self.batch, h, dtype=m.dtype, device=dev) for h, m in zip(H, self.layers)]
-        self._dev_out = [torch.empty_like(t) for t in self._dev_in]
+        n = len(self.layers)
+        self.host_in = torch.zeros(n, self.batch, H, dtype=dt).pin_memory()
+        self.host_out = torch.zeros(n, self.batch, H, dtype=dt).pin_memory()
+        self._dev_in = torch.zeros(n, self.batch, H, dtype=dt, device=dev)
+        self._dev_out = torch.empty_like(self._dev_in)
         with torch.cuda.device(dev):
-            self._copy = torch.cuda.Stream(device=dev)
-            self._ev_in = [torch.cuda.Event() for _ in self.layers]
-            self._ev_out = [torch.cuda.Event() for _ in self.layers]
             side = torch.cuda.Stream(device=dev)
             side.wait_stream(torch.cuda.current_stream(dev))
             with torch.cuda.stream(side):  # first calls: workspaces and the library's side stream
@@ -305,22 +307,10 @@ class LUTMoEStep:
         torch.cuda.synchronize(dev)
 
     def _body(self) -> None:
-        main = torch.cuda.current_stream(self.device)
-        cp = self._copy
-        cp.wait_stream(main)
-        with torch.cuda.stream(cp):
-            for hi, di, ev in zip(self.host_in, self._dev_in, self._ev_in):
-                di.copy_(hi, non_blocking=True)
-                ev.record(cp)
-        for m, di, do, ei, eo in zip(self.layers, self._dev_in, self._dev_out, self._ev_in, self._ev_out):
-            main.wait_event(ei)
-            m.forward(di, out=do)
-            eo.record(main)
-        with torch.cuda.stream(cp):
-            for do, ho, eo in zip(self._dev_out, self.host_out, self._ev_out):
-                cp.wait_event(eo)
-                ho.copy_(do, non_blocking=True)
-        main.wait_stream(cp)
+        self._dev_in.copy_(self.host_in, non_blocking=True)
+        for i, m in enumerate(self.layers):
+            m.forward(self._dev_in[i], out=self._dev_out[i])
+        self.host_out.copy_(self._dev_out, non_blocking=True)
 
     def run(self) -> None:
         """Replays the step on the current stream (asynchronous)."""

@@ -364,10 +364,10 @@ def test_prefill_wide_groups(T, with_shared, fmt):
 
 @pytest.mark.parametrize("T", [1, 8])
 def test_decode_step_graph_with_host_io(T):
-    """LUTMoEStep: one CUDA graph per step that copies each layer's input from
-    pinned host memory, runs the layer and copies the output back; replays
-    give the eager layers' outputs bit for bit, and new host inputs flow
-    through a replay."""
+    """LUTMoEStep: one CUDA graph per step that copies every layer's input
+    from pinned host memory, runs the layers and copies the outputs back;
+    replays give the eager layers' outputs bit for bit, and new host inputs
+    flow through a replay."""
     from block_lut_b200.moe import LUTMoEStep
     fmt = LUTFormat("b", 4, 64)
     layers = []
