@@ -1,17 +1,21 @@
 // Single-matrix LUT matmul y = W x, x [M][K] and y [M][N], on the matmul
 // path of the matrix's tiled layout (tcgen05 for BLUT_LAYOUT_TC, mma.sync
-// otherwise).  Three launches: a gather kernel puts x into the path's operand
-// order and writes the token groups (one "expert", groups of 32 tokens, or
-// 128 on the tcgen05 path from 128 tokens on), the matmul writes fp32 rows
-// (in K slices when the tcgen05 path has too few work items to fill the
-// GPU), and a reduce kernel sums the slices in slice order into y.  This is the single-matrix LUT GEMV/GEMM of the reference
-// (vllm_lut/cuda_lut_gemv.py:153-169, fused_kernel.py:13-46) for every
-// format of this library and every token count.
+// otherwise).  One token on the TC layout is one launch of the single-token
+// GEMV (blut_tok1.cuh), after a memset of its counters.  Otherwise three
+// launches: a gather kernel puts x into the path's operand order and writes
+// the token groups (one "expert", groups of 32 tokens, or 128 on the tcgen05
+// path from 128 tokens on), the matmul writes fp32 rows (in K slices when
+// the tcgen05 path has too few work items to fill the GPU), and a reduce
+// kernel sums the slices in slice order into y.  This is the single-matrix
+// LUT GEMV/GEMM of the reference (vllm_lut/cuda_lut_gemv.py:153-169,
+// fused_kernel.py:13-46) for every format of this library and every token
+// count.
 #include <algorithm>
 
 #include "blut_internal.h"
 #include "blut_mm.cuh"
 #include "blut_tc.cuh"
+#include "blut_tok1.cuh"
 
 namespace blut {
 
@@ -48,12 +52,9 @@ bool matmul_plan(const blut_mat_desc& d, int64_t m, MatmulPlan& p, TiledLayout& 
   p.bps = (int)L.nchunks;
   p.units = 0;
   p.gemv = p.tc && m <= kGemvMaxTokens;
-  if (p.gemv) {  // one CTA per (tile, K slice), sized as in the MoE passes
-    const int sms = num_sms();
-    int64_t bps = tc_gemv_blocks(d);
-    while (bps > 1 && (double)L.ntiles * ((L.nchunks + bps - 1) / bps) < 4.0 * sms) bps = (bps + 1) / 2;
-    p.bps = (int)bps;
-    p.ks = (int)((L.nchunks + bps - 1) / bps);
+  if (p.gemv) {  // the single-token GEMV: K slices of the 256 columns a thread stages
+    p.bps = std::max(1, kTok1MaxCols / (int)L.kb);
+    p.ks = (int)((L.nchunks + p.bps - 1) / p.bps);
     p.units = (int)((L.ntiles + 1) / 2);
   } else if (p.tc) {
     p.units = (int)((L.ntiles + 1) / 2);
@@ -75,7 +76,9 @@ size_t matmul_carve(const blut_mat_desc& d, int64_t m, const MatmulPlan& p, uint
     off = (size_t)align256(off + bytes);
     return o;
   };
-  const size_t o_status = take(256);
+  // status word; the single-token GEMV's completion counters (one per
+  // 128-row tile) follow it, so one memset clears both
+  const size_t o_status = take(256 + (p.gemv ? (d.rows + kTcRows - 1) / kTcRows * 4 : 0));
   const size_t o_groups = take(4 * p.groups * 4);
   const size_t o_bin = take(p.nt8 * kNTile * d.cols * 2);
   const size_t o_ys = take((int64_t)p.ks * m * d.rows * 4);
@@ -210,7 +213,11 @@ size_t matmul_workspace(const blut_mat_desc& d, int64_t m) {
 
 int matmul_launch_count(const blut_mat_desc& d, int64_t m) {
   const int rc = validate_matmul(d, m);
-  return rc != BLUT_OK ? rc : 3;  // gather (+ token groups), matmul, reduce
+  if (rc != BLUT_OK) return rc;
+  MatmulPlan p;
+  TiledLayout L;
+  if (!matmul_plan(d, m, p, L)) return BLUT_ERR_UNSUPPORTED;
+  return p.gemv ? 1 : 3;  // single-token GEMV (after a memset); else gather (+ token groups), matmul, reduce
 }
 
 int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const void* x, int64_t m, void* y,
@@ -230,6 +237,33 @@ int matmul(const blut_mat_desc& d, const void* w, const void* lut_table, const v
   matmul_carve(d, m, p, static_cast<uint8_t*>(workspace), &ws);
   const int sms = num_sms();
   const int64_t N = d.rows, K = d.cols;
+
+  if (p.gemv) {
+    // one token: the single-token GEMV (blut_tok1.cuh) as one matrix; the
+    // last CTA to finish a 128-row tile sums its K slices into y
+    int* cnt = ws.status + 64;  // after the 256-byte status block
+    if (cudaMemsetAsync(ws.status, 0, 256 + (N + kTcRows - 1) / kTcRows * 4, stream) != cudaSuccess)
+      return BLUT_ERR_CUDA;
+    Tok1Args a{};
+    if (!tc_planes(d, false, a.m[0].p)) return BLUT_ERR_UNSUPPORTED;
+    a.m[0].p.w = static_cast<const uint8_t*>(w);
+    a.m[0].p.wstride = 0;
+    a.m[0].p.r8_table = static_cast<const uint16_t*>(lut_table);
+    a.m[0].p.status = ws.status;
+    a.m[0].p.ks = p.ks;
+    a.m[0].p.bps = p.bps;
+    a.m[0].n_items = (int64_t)a.m[0].p.ntiles * p.ks;
+    a.m[0].xin = static_cast<const uint16_t*>(x);
+    a.m[0].part = ws.ys;
+    a.cnt = cnt;
+    a.gbound = 1;
+    a.out = y;
+    a.out_f32 = y_f32;
+    a.hidden = (int)N;
+    a.status = ws.status;
+    if (launch_tok1(d, a, false, (double)L.total, 0.0, stream) != cudaSuccess) return BLUT_ERR_LAUNCH;
+    return stage_done("matmul (single token)", stream);
+  }
 
   // n-tile nt of chunk 0 writes groups 32 nt .. 32 nt + 31: there are at
   // most nt8 / 4 + 1 groups (32-token groups, 4 n-tiles each), so nt8

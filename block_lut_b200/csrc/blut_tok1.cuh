@@ -157,7 +157,8 @@ __device__ __forceinline__ float tok1_sum(const float* p, int n, int64_t stride)
 // The epilogue of item `it`, run by the CTA whose completion of it was the
 // last of its unit (gate/up) or output tile (down).
 template <class Dec, bool PAIR>
-__device__ __forceinline__ void tok1_epilogue(const Tok1Args& a, const Tok1Mat& m, const Tok1Item& it) {
+__device__ __forceinline__ void tok1_epilogue(const Tok1Args& a, const Tok1Mat& m, const Tok1Item& it,
+                                              const int* groups, const float* gw) {
   const TcParams& p = m.p;
   const int row = threadIdx.x;
   if constexpr (PAIR) {
@@ -171,10 +172,10 @@ __device__ __forceinline__ void tok1_epilogue(const Tok1Args& a, const Tok1Mat& 
     // every contribution to this output tile is in: the weighted combine
     const int h = it.pt * kTcRows + row;
     const Tok1Mat& r = a.m[0];
-    const int ngr = min(a.groups[0], a.gbound);
+    const int ngr = min(groups[0], a.gbound);
     float o = 0.f;
     for (int g = 0; g < ngr; ++g)
-      o = fmaf(a.gw[g], tok1_sum(r.part + (int64_t)g * a.hidden + h, r.p.ks, (int64_t)a.gbound * a.hidden), o);
+      o = fmaf(gw[g], tok1_sum(r.part + (int64_t)g * a.hidden + h, r.p.ks, (int64_t)a.gbound * a.hidden), o);
     if (a.m[1].ctas > 0) {
       const Tok1Mat& sm = a.m[1];
       o = fmaf(a.sg ? *a.sg : 1.f, tok1_sum(sm.part + h, sm.p.ks, a.hidden), o);
@@ -194,8 +195,8 @@ __device__ __forceinline__ void tok1_epilogue(const Tok1Args& a, const Tok1Mat& 
 // atomic's round trip nor the staging loads sit on the critical path.  The
 // CTA that completes a unit or output tile runs its epilogue one item later.
 template <class Dec, bool PAIR>
-__device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, const int* groups, bool shared, int cta,
-                                         int nctas, uint8_t* smem) {
+__device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, const int* groups, const float* gw,
+                                         bool shared, int cta, int nctas, uint8_t* smem) {
   constexpr int KB = Dec::KB;
   constexpr int PF = tc_gemv_pf<Dec>();
   constexpr int W = Dec::kDense ? Dec::KB : 64;  // columns per piece
@@ -292,7 +293,7 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, co
     __syncthreads();  // s_last visible
     if (s_last) {
       __threadfence();
-      tok1_epilogue<Dec, PAIR>(a, m, prev);
+      tok1_epilogue<Dec, PAIR>(a, m, prev, groups, gw);
     }
     prev = cur;
     have_prev = true;
@@ -304,7 +305,7 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, co
   __syncthreads();
   if (s_last) {
     __threadfence();
-    tok1_epilogue<Dec, PAIR>(a, m, prev);
+    tok1_epilogue<Dec, PAIR>(a, m, prev, groups, gw);
   }
 }
 
@@ -312,6 +313,8 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, co
 // In the gate/up launch every routed CTA takes the token's top-k first (the
 // shared expert's CTAs need none); the down launch reads the table CTA 0 of
 // the gate/up launch published.
+// A down-mode launch with no group table (groups == nullptr) is a single
+// matrix: one group, expert 0, weight 1 (blut_matmul at one token).
 template <class Dec, bool PAIR>
 __global__ void __launch_bounds__(kTok1Threads, 4) tok1_kernel(const Tok1Args a) {
   extern __shared__ __align__(16) uint8_t tsm[];
@@ -319,14 +322,23 @@ __global__ void __launch_bounds__(kTok1Threads, 4) tok1_kernel(const Tok1Args a)
   __shared__ float s_gw[32];
   if ((int)blockIdx.x < a.m[0].ctas) {
     const int* groups = a.groups;
-    if constexpr (PAIR) {
-      if (threadIdx.x < 32) tok1_route_warp(a, s_groups, s_gw, blockIdx.x == 0);
+    const float* gw = a.gw;
+    if (PAIR || !a.groups) {
+      if (PAIR) {
+        if (threadIdx.x < 32) tok1_route_warp(a, s_groups, s_gw, blockIdx.x == 0);
+      } else if (threadIdx.x == 0) {
+        s_groups[0] = 1;
+        s_groups[1] = 0;
+        s_gw[0] = 1.f;
+      }
       __syncthreads();
       groups = s_groups;
+      gw = s_gw;
     }
-    tok1_run<Dec, PAIR>(a, a.m[0], groups, false, blockIdx.x, a.m[0].ctas, tsm);
+    tok1_run<Dec, PAIR>(a, a.m[0], groups, gw, false, blockIdx.x, a.m[0].ctas, tsm);
   } else {
-    tok1_run<TcDecDense<Dec::kBF16>, PAIR>(a, a.m[1], a.groups, true, blockIdx.x - a.m[0].ctas, a.m[1].ctas, tsm);
+    tok1_run<TcDecDense<Dec::kBF16>, PAIR>(a, a.m[1], a.groups, a.gw, true, blockIdx.x - a.m[0].ctas, a.m[1].ctas,
+                                           tsm);
   }
 }
 

@@ -231,7 +231,8 @@ def test_matmul_workspace_and_launches():
         for m in (1, 32, 4096):
             n = lib.blut_matmul_workspace_size(C.byref(d), m)
             assert n >= m * 1408 * 2 + m * 2048 * 4          # activations + fp32 rows
-            assert lib.blut_matmul_launch_count(C.byref(d), m) == 3
+            # one token on the TC layout: the single-token GEMV alone
+            assert lib.blut_matmul_launch_count(C.byref(d), m) == (1 if m == 1 and d.layout & _lib.LAYOUT_TC else 3)
         assert lib.blut_matmul_workspace_size(C.byref(d), 0) == 0
         assert lib.blut_matmul_workspace_size(C.byref(d), (1 << 20) + 1) == 0
     paired = LUTFormat("b", 4, 64).desc(2816, 2048, paired=True, tc=True)
