@@ -79,13 +79,16 @@ def parse():
                         "prefill: config 4's MoE layers; sweep: config 5's single-matrix kernel sweep; "
                         "tiers: Format R progressive bit-plane tier recover; vllm: config 2 end to end "
                         "through vLLM with the lut plugin")
+    p.add_argument("--vllm-model", choices=["qwen15", "qwen3"], default="qwen15",
+                   help="--workload vllm: config 2's Qwen1.5-MoE-A2.7B or config 3's Qwen3-30B-A3B architecture")
     p.add_argument("--sweep-bits", default="2,3,4")
     p.add_argument("--sweep-groups", default="32,64,128")
     p.add_argument("--sweep-m", default="1,2,4,8,16,64,256,1024,4096")
     a = p.parse_args()
     if a.steps is None:
         a.steps = {"decode": 200, "qwen3": 100}.get(a.workload, 5)
-    a.shape = QWEN3 if a.workload == "qwen3" else DSV2 if a.workload == "prefill" else QWEN
+    qwen3 = a.workload == "qwen3" or (a.workload == "vllm" and a.vllm_model == "qwen3")
+    a.shape = QWEN3 if qwen3 else DSV2 if a.workload == "prefill" else QWEN
     a.batch = a.batch if a.batch is not None else a.shape.get("BATCH", 32)
     a.layers = a.layers if a.layers is not None else a.shape["LAYERS"]
     a.kind = a.kind or a.shape.get("KIND", "b")
@@ -875,6 +878,22 @@ def qwen15_moe_config(layers: int, quant: dict, dtype: str) -> dict:
     }
 
 
+def qwen3_moe_config(layers: int, quant: dict, dtype: str) -> dict:
+    """config.json of the Qwen3-30B-A3B architecture: 128
+    experts of I 768, top-8 renormalised, no shared expert, 32 query and 4
+    key/value heads of 128."""
+    return {
+        "architectures": ["Qwen3MoeForCausalLM"], "model_type": "qwen3_moe",
+        "hidden_size": 2048, "intermediate_size": 6144, "moe_intermediate_size": 768, "num_experts": 128,
+        "num_experts_per_tok": 8, "norm_topk_prob": True, "num_hidden_layers": layers,
+        "num_attention_heads": 32, "num_key_value_heads": 4, "head_dim": 128, "vocab_size": 151936,
+        "max_position_embeddings": 40960, "rope_theta": 1000000.0, "rms_norm_eps": 1e-6, "hidden_act": "silu",
+        "decoder_sparse_step": 1, "mlp_only_layers": [], "tie_word_embeddings": False, "torch_dtype": dtype,
+        "use_sliding_window": False, "sliding_window": None, "attention_bias": False, "attention_dropout": 0.0,
+        "initializer_range": 0.02, "bos_token_id": 151643, "eos_token_id": 151645, "quantization_config": quant,
+    }
+
+
 def lut_quant_config(fmt) -> dict:
     """The checkpoint's quantization_config for the LUT plugin (block_lut_b200.quant_method.LUTConfig)."""
     q = {"quant_method": "lut", "code_type": "BLOCKLUT", "release_canonical": True}
@@ -890,8 +909,9 @@ def run_vllm(a):
     """Config 2 end to end: the full Qwen1.5-MoE-A2.7B architecture (24
     layers, attention and dense layers in the model dtype, experts through
     the lut plugin) in vLLM with CUDA graphs, weights from vLLM's dummy
-    loader (there is no checkpoint here).  Per batch size: a prompt of 512
-    random token ids per sequence, then 128 generated tokens; decode tokens/s
+    loader (there is no checkpoint here); with --vllm-model qwen3, config 3's
+    Qwen3-30B-A3B (48 layers, NestedLUT experts, prompt 1024).  Per batch
+    size: a prompt of random token ids per sequence, then 128 generated tokens; decode tokens/s
     = batch x 128 / (time of prefill + 128 tokens - time of prefill + 1
     token).  The engine runs in this process (VLLM_ENABLE_V1_MULTIPROCESSING=0)
     so that the plugin registered on import is the one it uses."""
@@ -903,18 +923,20 @@ def run_vllm(a):
     fmt = bench_format(a)
     dtype = "bfloat16" if fmt.kind == "r8" else "float16"
     layers = a.layers
+    qwen3 = a.vllm_model == "qwen3"
     d = tempfile.mkdtemp(prefix="blut_vllm_")
     with open(os.path.join(d, "config.json"), "w") as f:
-        json.dump(qwen15_moe_config(layers, lut_quant_config(fmt), dtype), f)
+        json.dump((qwen3_moe_config if qwen3 else qwen15_moe_config)(layers, lut_quant_config(fmt), dtype), f)
+    prompt = 1024 if qwen3 else 512
     batches = sorted({1, a.batch})
     t0 = time.time()
-    llm = LLM(model=d, quantization="lut", load_format="dummy", skip_tokenizer_init=True, max_model_len=1024,
+    llm = LLM(model=d, quantization="lut", load_format="dummy", skip_tokenizer_init=True, max_model_len=prompt + 512,
               gpu_memory_utilization=0.8, max_num_seqs=max(batches), dtype=dtype, enforce_eager=False, seed=0)
     init_s = time.time() - t0
     rng = random.Random(0)
     res_b = {}
     for bs in batches:
-        prompts = [{"prompt_token_ids": [rng.randrange(1000, 150000) for _ in range(512)]} for _ in range(bs)]
+        prompts = [{"prompt_token_ids": [rng.randrange(1000, 150000) for _ in range(prompt)]} for _ in range(bs)]
 
         def gen(n):
             sp = SamplingParams(max_tokens=n, min_tokens=n, ignore_eos=True, temperature=0.0, detokenize=False)
@@ -935,7 +957,8 @@ def run_vllm(a):
            "steps": 128, "warmup": a.warmup, "ms_per_step": top["ms_per_token_step"], "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "f16" if dtype == "float16" else "bf16",
            "data": "vLLM dummy weights (random), random prompt token ids",
-           "config": {"workload": f"Qwen1.5-MoE-A2.7B ({layers} layers) in vLLM, prompt 512, generate 128",
+           "config": {"workload": f"{'Qwen3-30B-A3B' if qwen3 else 'Qwen1.5-MoE-A2.7B'} ({layers} layers) in vLLM, "
+                                  f"prompt {prompt}, generate 128",
                       "format": format_name(fmt), "engine": "vLLM LLM(quantization='lut', load_format='dummy'), "
                       "CUDA graphs on", "init_s": round(init_s, 1)},
            "batches": {str(k): v for k, v in res_b.items()}}
