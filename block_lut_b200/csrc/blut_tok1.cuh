@@ -28,6 +28,12 @@
 namespace blut {
 
 constexpr int kTok1Threads = kTcRows;
+// Pieces of its row a thread keeps in flight, and CTAs per SM: a two-piece
+// ring leaves registers for five CTAs (20 warps) per SM, which hides the
+// per-item latencies better than a four-piece ring at four CTAs (measured
+// on config 2 at batch 1: 876 -> 946 tokens/s).
+constexpr int kTok1Ring = 2;
+constexpr int kTok1CtasPerSm = 5;
 
 // One matrix of a single-token pass.
 struct Tok1Mat {
@@ -134,7 +140,7 @@ __device__ __forceinline__ bool tok1_resolve(const int* groups, const Tok1Mat& m
 }
 
 // Columns of one item's activation slice a thread stages: an item is 256
-// columns (tok1_slices), one or two rounds of the thread's register ring.
+// columns (tok1_slices), two to four rounds of the thread's register ring.
 constexpr int kTok1XPer = 2;
 constexpr int kTok1MaxCols = kTok1XPer * kTok1Threads;
 
@@ -198,7 +204,7 @@ template <class Dec, bool PAIR>
 __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, const int* groups, const float* gw,
                                          bool shared, int cta, int nctas, uint8_t* smem) {
   constexpr int KB = Dec::KB;
-  constexpr int PF = tc_gemv_pf<Dec>();
+  constexpr int PF = kTok1Ring;
   constexpr int W = Dec::kDense ? Dec::KB : 64;  // columns per piece
   using U = typename std::conditional<Dec::kDense, TcDenseBlk<Dec::kBF16>, typename Dec::Half>::type;
   static_assert(kTok1MaxCols % (PF * W) == 0, "an item is whole rounds of the register ring");
@@ -316,7 +322,7 @@ __device__ __forceinline__ void tok1_run(const Tok1Args& a, const Tok1Mat& m, co
 // A down-mode launch with no group table (groups == nullptr) is a single
 // matrix: one group, expert 0, weight 1 (blut_matmul at one token).
 template <class Dec, bool PAIR>
-__global__ void __launch_bounds__(kTok1Threads, 4) tok1_kernel(const Tok1Args a) {
+__global__ void __launch_bounds__(kTok1Threads, kTok1CtasPerSm) tok1_kernel(const Tok1Args a) {
   extern __shared__ __align__(16) uint8_t tsm[];
   __shared__ int s_groups[33];
   __shared__ float s_gw[32];
