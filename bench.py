@@ -414,6 +414,13 @@ def run_ours(a):
     na = sum(n_active) / len(n_active)
     b_gu = na * 2 * Ii * Hh * bpw
     b_dn = na * Hh * Ii * bpw
+    # at batch 1 the single-token path streams the dense shared expert inside
+    # the same two launches as the routed experts
+    tok1 = a.batch == 1 and moes[0].launch_count(1, caller_routing=False) == 3
+    if tok1 and moes[0].shared is not None:
+        sb = moes[0].shared.weight_bytes()
+        b_gu += sb * 2 / 3
+        b_dn += sb / 3
     achieved = (b_gu + b_dn) / ((t_gu + t_dn) / 1e3) / 1e9
     peak, peak_kind = peaks()
 
@@ -530,7 +537,9 @@ def run_ours(a):
                    "parallelism": "single GPU", "graph": f"CUDA graph of the {a.layers}-layer step",
                    "l2": f"inputs larger than L2: {sum(n_active) * 3 * Ii * Hh * bpw / 1e9:.1f} GB of expert "
                          f"weights streamed per step"},
-        "roofline": {"kernel": ("tc_mm_kernel (tcgen05" if moes[0].experts.tc else "lut_mm_kernel (mma.sync") +
+        "roofline": {"kernel": "tok1_kernel (single-token GEMV launches: routed experts + dense shared expert, "
+                               "per layer)" if tok1 else
+                               ("tc_mm_kernel (tcgen05" if moes[0].experts.tc else "lut_mm_kernel (mma.sync") +
                                "; routed gate/up+SiLU*up and down, per layer)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -538,7 +547,7 @@ def run_ours(a):
                      # DRAM read + write per layer: the algorithmic bytes times the ratio an
                      # ncu capture of this format's routed launches measured (TRAFFIC_RATIOS)
                      "traffic": (b_gu + b_dn) * TRAFFIC_RATIOS[key] if moes[0].experts.tc and key in
-                     TRAFFIC_RATIOS else None,
+                     TRAFFIC_RATIOS and not tok1 else None,
                      "bytes_per_layer": b_gu + b_dn, "ms_gateup": t_gu, "ms_down": t_dn,
                      "active_experts": na, "active_experts_per_layer": n_active[:4]},
         "cpu_baseline": cpu, "e2e": e2e, "batch1": batch1,

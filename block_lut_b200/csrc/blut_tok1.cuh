@@ -389,8 +389,10 @@ inline cudaError_t launch_tok1_dec(Tok1Args a, double routed_bytes, double share
     cs = std::min<int64_t>(cs, total - 1);
     cr = total - cs;
   }
-  cr = std::max<int64_t>(1, std::min<int64_t>(cr, a.m[0].n_items));
+  // a part with fewer items than its share of the CTAs hands the rest to the other
   cs = std::min<int64_t>(cs, a.m[1].n_items);
+  cr = std::max<int64_t>(1, std::min<int64_t>(total - cs, a.m[0].n_items));
+  if (sh) cs = std::max<int64_t>(1, std::min<int64_t>(total - cr, a.m[1].n_items));
   a.m[0].ctas = (int)cr;
   a.m[1].ctas = (int)cs;
   kern<<<(unsigned)(cr + cs), kTok1Threads, smem, stream>>>(a);
