@@ -147,16 +147,16 @@ constexpr int kTok1MaxCols = kTok1XPer * kTok1Threads;
 // Sum of n fp32 values at p, p + stride, ... in index order, eight loads in
 // flight at a time (L2: other CTAs wrote them in this launch).
 __device__ __forceinline__ float tok1_sum(const float* p, int n, int64_t stride) {
+  // eight loads in flight per round, the ragged last round included
   float s = 0.f;
-  int i = 0;
-  for (; i + 8 <= n; i += 8) {
+  for (int i = 0; i < n; i += 8) {
     float v[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = __ldcg(p + (i + k) * stride);
+    for (int k = 0; k < 8; ++k) v[k] = i + k < n ? __ldcg(p + (i + k) * stride) : 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) s += v[k];
+    for (int k = 0; k < 8; ++k)
+      if (i + k < n) s += v[k];
   }
-  for (; i < n; ++i) s += __ldcg(p + i * stride);
   return s;
 }
 
@@ -180,6 +180,7 @@ __device__ __forceinline__ void tok1_epilogue(const Tok1Args& a, const Tok1Mat& 
     const Tok1Mat& r = a.m[0];
     const int ngr = min(groups[0], a.gbound);
     float o = 0.f;
+#pragma unroll 2
     for (int g = 0; g < ngr; ++g)
       o = fmaf(gw[g], tok1_sum(r.part + (int64_t)g * a.hidden + h, r.p.ks, (int64_t)a.gbound * a.hidden), o);
     if (a.m[1].ctas > 0) {
