@@ -171,26 +171,24 @@ __global__ void __launch_bounds__(32) matmul_gather_kernel(const uint16_t* __res
 }
 
 // y = sum of the ks fp32 slices in slice order, four values per thread;
-// four slices' loads are in flight at a time.
+// four slices' loads are in flight at a time, the ragged last round included.
 template <bool BF16>
 __global__ void __launch_bounds__(256) matmul_reduce_kernel(const float* __restrict__ ys, int ks, int64_t sstride,
                                                             int64_t n4, void* __restrict__ y, int y_f32) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     const float* p = ys + 4 * i;
     float4 v = *reinterpret_cast<const float4*>(p);
-    int s = 1;
-    for (; s + 4 <= ks; s += 4) {
+    for (int s = 1; s < ks; s += 4) {
       float4 u[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) u[q] = *reinterpret_cast<const float4*>(p + (s + q) * sstride);
+      for (int q = 0; q < 4; ++q)
+        u[q] = s + q < ks ? *reinterpret_cast<const float4*>(p + (s + q) * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        v.x += u[q].x; v.y += u[q].y; v.z += u[q].z; v.w += u[q].w;
+        if (s + q < ks) {
+          v.x += u[q].x; v.y += u[q].y; v.z += u[q].z; v.w += u[q].w;
+        }
       }
-    }
-    for (; s < ks; ++s) {
-      const float4 u = *reinterpret_cast<const float4*>(p + s * sstride);
-      v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
     }
     if (y_f32) {
       reinterpret_cast<float4*>(y)[i] = v;

@@ -314,23 +314,22 @@ __global__ void __launch_bounds__(256) splitk_silu_kernel(const float* __restric
   if (row >= kTcRows || n >= ntok) return;
   const float* src = part + (int64_t)ku * ks * (2 * kTcRows * 32) + idx;
   float g = 0.f, v = 0.f;
-  int s = 0;
-  for (; s + 3 < ks; s += 4) {  // four slices' loads in flight, added in slice order
+  // four slices' loads in flight, the ragged last round included, added in slice order
+  for (int s = 0; s < ks; s += 4) {
     float gs[4], vs[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      gs[i] = src[(int64_t)(s + i) * (2 * kTcRows * 32)];
-      vs[i] = src[(int64_t)(s + i) * (2 * kTcRows * 32) + kTcRows * 32];
+      const bool in = s + i < ks;
+      gs[i] = in ? src[(int64_t)(s + i) * (2 * kTcRows * 32)] : 0.f;
+      vs[i] = in ? src[(int64_t)(s + i) * (2 * kTcRows * 32) + kTcRows * 32] : 0.f;
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      g += gs[i];
-      v += vs[i];
+      if (s + i < ks) {
+        g += gs[i];
+        v += vs[i];
+      }
     }
-  }
-  for (; s < ks; ++s) {
-    g += src[(int64_t)s * (2 * kTcRows * 32)];
-    v += src[(int64_t)s * (2 * kTcRows * 32) + kTcRows * 32];
   }
   const int col = u * kTcRows + row;
   uint8_t* dst = act + tc_bact_off((int64_t)nt0 * kNTile + n, col, out_kb, ntstride);
