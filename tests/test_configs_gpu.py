@@ -124,6 +124,15 @@ def test_config3_qwen3_layer_router_renorm_nested_tiers():
                                      "f16", THREADS)
         check_layer(out[torch.from_numpy(keep).cuda()], ref[keep], torch.float16,
                     f"qwen3 layer tier {f.tier}")
+        # one token at a time: the single-token path, with the top-8 of 128
+        # experts and its renormalisation taken inside the gate/up launch
+        assert layer.launch_count(1, caller_routing=False) == 3
+        for i in np.flatnonzero(keep)[:3]:
+            out1 = layer.forward(x[i:i + 1])
+            layer.check_status()
+            ref1 = O.moe_forward_threaded(xn[i:i + 1], ids[i:i + 1], tw[i:i + 1], lambda e: _deq(f, c13[e]),
+                                          lambda e: _deq(f, c2[e]), "f16", THREADS)
+            check_layer(out1, ref1, torch.float16, f"qwen3 layer tier {f.tier}, single token {i}")
 
 
 def test_config4_dsv2_lite_prefill_wide_groups():
