@@ -50,7 +50,7 @@ class MoEArgs(C.Structure):
                 ("s13", MatDesc), ("s2", MatDesc),
                 ("s13_tiled", C.c_void_p), ("s2_tiled", C.c_void_p),
                 ("shared_gate_w", C.c_void_p), ("out", C.c_void_p), ("prof_events", C.c_void_p),
-                ("out_f32", C.c_int32), ("reserved2", C.c_int32)]
+                ("out_f32", C.c_int32), ("expected_slots", C.c_int32)]
 
 
 EP_MAX_RANKS = 8

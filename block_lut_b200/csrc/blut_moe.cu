@@ -435,6 +435,27 @@ static double expected_active(int T, int k, int E) {
   return E * (1.0 - miss);
 }
 
+// Non-empty routed slots to plan for.  Expert parallelism passes every
+// received row with all k slots, most of them empty (experts of other
+// ranks); the caller's expected count (blut_moe_args.expected_slots) then
+// stands in for T*k in the grouping and split choices.  Buffer sizes still
+// allow for all T*k slots.
+static int64_t expected_slots(const blut_moe_args& a) {
+  const int64_t S = (int64_t)a.num_tokens * a.top_k;
+  return a.num_experts > 0 && a.expected_slots > 0 && a.expected_slots < S ? (int64_t)a.expected_slots : S;
+}
+
+// Expected routed token groups of gtok tokens: the experts hit plus the
+// slots over gtok.  Experts hit: T tokens choosing k of E, or, with the
+// caller's slot count, that many slots each landing on one of E experts.
+static double expected_groups(const blut_moe_args& a, int gtok) {
+  const int64_t S = (int64_t)a.num_tokens * a.top_k, Sx = expected_slots(a);
+  const double E = (double)a.num_experts;
+  const double active = Sx < S ? E * (1.0 - std::pow(1.0 - 1.0 / E, (double)Sx))
+                               : expected_active(a.num_tokens, a.top_k, a.num_experts);
+  return active + (double)Sx / gtok;
+}
+
 // K slices per tcgen05 pass, every slice keeping at least two column blocks;
 // gate/up passes split at most 8 ways (their partial sums go through
 // memory), down passes 16.  Routed and shared passes split while the
@@ -449,13 +470,14 @@ void moe_split(const blut_moe_args& a, MoESplit& s) {
   // Prefill: on the tcgen05 path, with at least 64 tokens per expert on
   // average, tokens go in groups of kWideGroupTok so one decoded weight tile
   // feeds wide MMAs.
+  const int64_t Sx = expected_slots(a);
   const bool tc_r = (a.w13.layout & BLUT_LAYOUT_TC) != 0;
   const bool tc_s = a.shared_inter > 0 && (a.s13.layout & BLUT_LAYOUT_TC) != 0;
-  s.gtok[0] = tc_r && S >= 64 * E ? kWideGroupTok : kGroupTok;
+  s.gtok[0] = tc_r && Sx >= 64 * E ? kWideGroupTok : kGroupTok;
   s.gtok[1] = tc_s && T >= 64 ? kWideGroupTok : kGroupTok;
   s.gemv[0] = tc_r && T <= kGemvMaxTokens;
   s.gemv[1] = tc_s && T <= kGemvMaxTokens;
-  const double est_r = expected_active((int)T, (int)K, (int)E) + (double)S / s.gtok[0];
+  const double est_r = expected_groups(a, s.gtok[0]);
   const int64_t gmax_r = std::min(E, S) + (S + s.gtok[0] - 1) / s.gtok[0] + 1;
   const int64_t gmax_s = (T + s.gtok[1] - 1) / s.gtok[1];
   const blut_mat_desc* d[4] = {&a.w13, &a.w2, &a.s13, &a.s2};
@@ -857,7 +879,7 @@ int moe_forward(const blut_moe_args& a, void* workspace, size_t ws_bytes, cudaSt
   const bool sh = a.shared_inter > 0;
   const int T = a.num_tokens, K = a.top_k, E = a.num_experts, H = a.hidden;
   const int sms = num_sms();
-  const double est_groups = expected_active(T, K, E) + (double)T * K / ws.split.gtok[0];
+  const double est_groups = expected_groups(a, ws.split.gtok[0]);
   const double est_sgroups = (T + ws.split.gtok[1] - 1) / ws.split.gtok[1];
   const int b_ntiles = (std::min(T, kGroupTok) + kNTile - 1) / kNTile;
 

@@ -268,6 +268,9 @@ class EPMoELayer:
         self.top_k = top_k
         self.renorm = renorm
         self.local = LUTMoELayer(local_experts, top_k)
+        # every received row carries all k slots; about E_local / E of them
+        # name an expert of this rank, the rest are empty
+        self.local.slot_fraction = local_experts.num_experts / num_experts
         self.router_w = router_w.to(local_experts.fmt.compute_dtype).contiguous()
         self.num_experts = num_experts
         self.owner, self.local_id = owner_tables(num_experts, self.world, router_w.device)

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import contextlib
 import ctypes as C
+import math
 import threading
 from dataclasses import dataclass
 from typing import Optional, Sequence
@@ -126,6 +127,10 @@ class LUTMoELayer:
         self.renorm = bool(renorm)
         self.shared = shared
         self.ws_slot = 0  # workspace slot (see workspace); 1 for a layer run beside others on a side stream
+        # expected share of the T*k slots that name an expert of this layer:
+        # below 1 when most slots are empty (-1), as for the rows expert
+        # parallelism hands to one rank; it steers only the work split
+        self.slot_fraction = 1.0
         self.shared_gate_mode = int(shared_gate_mode)
         self.dtype = experts.fmt.compute_dtype
         self._args = self._make_args()
@@ -156,8 +161,15 @@ class LUTMoELayer:
         """Kernel launches one forward issues (the count only tests pointers for NULL)."""
         a = _lib.MoEArgs.from_buffer_copy(self._args)
         a.num_tokens = num_tokens
+        a.expected_slots = self._expected_slots(num_tokens)
         a.topk_ids = 1 if caller_routing else None
         return int(_lib.lib().blut_moe_launch_count(C.byref(a)))
+
+    def _expected_slots(self, num_tokens: int) -> int:
+        """blut_moe_args.expected_slots for a call on ``num_tokens`` rows (0: all slots may be used)."""
+        if self.slot_fraction >= 1.0:
+            return 0
+        return max(1, math.ceil(num_tokens * self.top_k * self.slot_fraction))
 
     def forward(self, x: torch.Tensor, topk_ids: Optional[torch.Tensor] = None,
                 topk_weights: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
@@ -218,6 +230,7 @@ class LUTMoELayer:
         T = x2.shape[0]
         a = _lib.MoEArgs.from_buffer_copy(self._args)
         a.num_tokens = T
+        a.expected_slots = self._expected_slots(T)
         a.x = x2.data_ptr()
         keep = [x2]
         if topk_ids is not None:

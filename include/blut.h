@@ -305,7 +305,13 @@ typedef struct {
                                carry the shared expert                        */
   int32_t out_f32;          /* 1: out is float32 [T][H] (unrounded partial sums,
                                used by expert parallelism); 0: out is `dtype` */
-  int32_t reserved2;
+  int32_t expected_slots;   /* 0: every slot of topk_ids may name a local
+                               expert.  > 0: how many of the T*k slots the
+                               caller expects to be non-empty (expert
+                               parallelism: the received rows' slots owned by
+                               this rank, about T*k*E_local/E_global).  Only
+                               the choice of token grouping and K split uses
+                               it; results never depend on it. */
 } blut_moe_args;
 
 /* Workspace bytes blut_moe_forward needs for these arguments (0 on error). */

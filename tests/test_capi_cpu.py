@@ -5,6 +5,7 @@ import os
 import re
 import shutil
 import subprocess
+from types import SimpleNamespace
 
 import pytest
 import torch
@@ -13,6 +14,7 @@ from tests.conftest import ROOT
 
 from block_lut_b200 import _lib
 from block_lut_b200.formats import LUTFormat, tiled_bytes
+from block_lut_b200.moe import LUTMoELayer
 
 HEADER = os.path.join(ROOT, "include", "blut.h")
 
@@ -163,6 +165,34 @@ def test_launch_count():
     assert lib.blut_moe_launch_count(C.byref(tc)) == 3
     mma = _args(num_tokens=1, topk_ids=None, router_w=1 << 22)
     assert lib.blut_moe_launch_count(C.byref(mma)) == 6
+
+
+@pytest.mark.parametrize("E,k,I,world,cap", [(60, 4, 1408, 8, 32), (128, 8, 768, 8, 64)])
+def test_expected_slots_steer_the_split_of_expert_parallel_rows(E, k, I, world, cap):
+    """One rank of an 8-way expert-parallel decode gets world * cap rows with
+    all k slots each, about E_local / E of them non-empty.  Counted as full,
+    the slots look like a prefill batch (128-token groups, no K split, too
+    few work items for the SMs); with expected_slots the gate/up pass is
+    split over K again, which adds its slice-sum launch.  Buffers still
+    cover every slot, so the workspace only grows."""
+    lib = _lib.lib()
+    fmt = LUTFormat("b", 4, 64)
+    e_local = -(-E // world)
+    a = _args(num_experts=e_local, top_k=k, inter=I, num_tokens=world * cap,
+              w13=fmt.desc(2 * I, 2048, paired=True, tc=True), w2=fmt.desc(2048, I, tc=True),
+              w13_stride=tiled_bytes(fmt, 2 * I, 2048, True, tc=True), w2_stride=tiled_bytes(fmt, 2048, I, tc=True))
+    n_full, ws_full = lib.blut_moe_launch_count(C.byref(a)), lib.blut_moe_workspace_size(C.byref(a))
+    layer = SimpleNamespace(top_k=k, slot_fraction=e_local / E)
+    a.expected_slots = LUTMoELayer._expected_slots(layer, world * cap)
+    assert 0 < a.expected_slots < world * cap * k
+    assert lib.blut_moe_launch_count(C.byref(a)) == n_full + 1
+    assert lib.blut_moe_workspace_size(C.byref(a)) >= ws_full
+    # no hint (0) or a count of at least T*k leaves the split as it was
+    for v in (0, world * cap * k, 1 << 30):
+        a.expected_slots = v
+        assert lib.blut_moe_launch_count(C.byref(a)) == n_full
+        assert lib.blut_moe_workspace_size(C.byref(a)) == ws_full
+    assert LUTMoELayer._expected_slots(SimpleNamespace(top_k=k, slot_fraction=1.0), 64) == 0
 
 
 LAYOUT_PROBE = r"""
