@@ -79,8 +79,9 @@ def parse():
                         "prefill: config 4's MoE layers; sweep: config 5's single-matrix kernel sweep; "
                         "tiers: Format R progressive bit-plane tier recover; vllm: config 2 end to end "
                         "through vLLM with the lut plugin")
-    p.add_argument("--vllm-model", choices=["qwen15", "qwen3"], default="qwen15",
-                   help="--workload vllm: config 2's Qwen1.5-MoE-A2.7B or config 3's Qwen3-30B-A3B architecture")
+    p.add_argument("--vllm-model", choices=["qwen15", "qwen3", "dsv2lite"], default="qwen15",
+                   help="--workload vllm: config 2's Qwen1.5-MoE-A2.7B, config 3's Qwen3-30B-A3B, or config 4's "
+                        "DeepSeek-V2-Lite architecture (prefill of 8 x 4096 tokens)")
     p.add_argument("--sweep-bits", default="2,3,4")
     p.add_argument("--sweep-groups", default="32,64,128")
     p.add_argument("--sweep-m", default="1,2,4,8,16,64,256,1024,4096")
@@ -88,7 +89,8 @@ def parse():
     if a.steps is None:
         a.steps = {"decode": 200, "qwen3": 100}.get(a.workload, 5)
     qwen3 = a.workload == "qwen3" or (a.workload == "vllm" and a.vllm_model == "qwen3")
-    a.shape = QWEN3 if qwen3 else DSV2 if a.workload == "prefill" else QWEN
+    dsv2 = a.workload == "prefill" or (a.workload == "vllm" and a.vllm_model == "dsv2lite")
+    a.shape = QWEN3 if qwen3 else DSV2 if dsv2 else QWEN
     a.batch = a.batch if a.batch is not None else a.shape.get("BATCH", 32)
     a.layers = a.layers if a.layers is not None else a.shape["LAYERS"]
     a.kind = a.kind or a.shape.get("KIND", "b")
@@ -870,6 +872,7 @@ def run_tiers(a):
 
 # --------------------------------------------------------------- vllm ---
 VLLM_METRIC = "vLLM decode tokens/s, full model, LUT experts"
+VLLM_PREFILL_METRIC = "vLLM prefill tokens/s, full model, LUT experts"
 
 
 def qwen15_moe_config(layers: int, quant: dict, dtype: str) -> dict:
@@ -903,6 +906,27 @@ def qwen3_moe_config(layers: int, quant: dict, dtype: str) -> dict:
     }
 
 
+def dsv2_lite_config(layers: int, quant: dict, dtype: str) -> dict:
+    """config.json of the DeepSeek-V2-Lite architecture:
+    27 layers, the first a dense MLP (I 10944); 64 routed experts of I 1408,
+    top-6 softmax without renormalisation, 2 shared experts; MLA attention
+    with kv_lora_rank 512, no query compression, 16 heads of 128 + 64 rope
+    dims.  ``layers`` counts MoE layers; the dense first layer comes on top."""
+    return {
+        "architectures": ["DeepseekV2ForCausalLM"], "model_type": "deepseek_v2",
+        "hidden_size": 2048, "intermediate_size": 10944, "moe_intermediate_size": 1408,
+        "n_routed_experts": 64, "n_shared_experts": 2, "num_experts_per_tok": 6, "first_k_dense_replace": 1,
+        "moe_layer_freq": 1, "num_hidden_layers": layers + 1, "num_attention_heads": 16,
+        "num_key_value_heads": 16, "kv_lora_rank": 512, "q_lora_rank": None, "qk_nope_head_dim": 128,
+        "qk_rope_head_dim": 64, "v_head_dim": 128, "topk_method": "greedy", "n_group": 1, "topk_group": 1,
+        "norm_topk_prob": False, "routed_scaling_factor": 1.0, "scoring_func": "softmax",
+        "vocab_size": 102400, "max_position_embeddings": 163840, "rope_theta": 10000.0, "rms_norm_eps": 1e-6,
+        "hidden_act": "silu", "tie_word_embeddings": False, "attention_bias": False, "attention_dropout": 0.0,
+        "initializer_range": 0.02, "torch_dtype": dtype, "bos_token_id": 100000, "eos_token_id": 100001,
+        "quantization_config": quant,
+    }
+
+
 def lut_quant_config(fmt) -> dict:
     """The checkpoint's quantization_config for the LUT plugin (block_lut_b200.quant_method.LUTConfig)."""
     q = {"quant_method": "lut", "code_type": "BLOCKLUT", "release_canonical": True}
@@ -919,7 +943,11 @@ def run_vllm(a):
     layers, attention and dense layers in the model dtype, experts through
     the lut plugin) in vLLM with CUDA graphs, weights from vLLM's dummy
     loader (there is no checkpoint here); with --vllm-model qwen3, config 3's
-    Qwen3-30B-A3B (48 layers, NestedLUT experts, prompt 1024).  Per batch
+    Qwen3-30B-A3B (48 layers, NestedLUT experts, prompt 1024); with
+    --vllm-model dsv2lite, config 4's DeepSeek-V2-Lite (26 MoE layers after
+    a dense one, MLA attention) on 8 prompts of 4096 tokens in one prefill
+    step, reported as prefill tokens/s = 8 x 4096 / time of prefill + 1
+    token.  Per batch
     size: a prompt of random token ids per sequence, then 128 generated tokens; decode tokens/s
     = batch x 128 / (time of prefill + 128 tokens - time of prefill + 1
     token).  The engine runs in this process (VLLM_ENABLE_V1_MULTIPROCESSING=0)
@@ -932,15 +960,18 @@ def run_vllm(a):
     fmt = bench_format(a)
     dtype = "bfloat16" if fmt.kind == "r8" else "float16"
     layers = a.layers
-    qwen3 = a.vllm_model == "qwen3"
+    qwen3, dsv2 = a.vllm_model == "qwen3", a.vllm_model == "dsv2lite"
     d = tempfile.mkdtemp(prefix="blut_vllm_")
+    make_config = qwen3_moe_config if qwen3 else dsv2_lite_config if dsv2 else qwen15_moe_config
     with open(os.path.join(d, "config.json"), "w") as f:
-        json.dump((qwen3_moe_config if qwen3 else qwen15_moe_config)(layers, lut_quant_config(fmt), dtype), f)
-    prompt = 1024 if qwen3 else 512
-    batches = sorted({1, a.batch})
+        json.dump(make_config(layers, lut_quant_config(fmt), dtype), f)
+    prompt = 1024 if qwen3 else 4096 if dsv2 else 512
+    batches = [8] if dsv2 else sorted({1, a.batch})
+    extra = {"max_num_batched_tokens": prompt * max(batches)} if dsv2 else {}  # the whole batch in one prefill
     t0 = time.time()
     llm = LLM(model=d, quantization="lut", load_format="dummy", skip_tokenizer_init=True, max_model_len=prompt + 512,
-              gpu_memory_utilization=0.8, max_num_seqs=max(batches), dtype=dtype, enforce_eager=False, seed=0)
+              gpu_memory_utilization=0.8, max_num_seqs=max(batches), dtype=dtype, enforce_eager=False, seed=0,
+              **extra)
     init_s = time.time() - t0
     rng = random.Random(0)
     res_b = {}
@@ -960,13 +991,16 @@ def run_vllm(a):
         t1 = min(gen(1) for _ in range(3))
         t129 = min(gen(129) for _ in range(max(1, min(a.steps, 3))))
         res_b[bs] = {"decode_tokens_s": bs * 128 / (t129 - t1), "ms_per_token_step": (t129 - t1) / 128 * 1e3,
-                     "prefill_s": t1}
+                     "prefill_s": t1, "prefill_tokens_s": bs * prompt / t1}
     top = res_b[max(batches)]
-    res = {"metric": VLLM_METRIC, "value": top["decode_tokens_s"], "unit": "tokens/s", "n_gpus": 1,
-           "steps": 128, "warmup": a.warmup, "ms_per_step": top["ms_per_token_step"], "higher_is_better": True,
+    model_name = "Qwen3-30B-A3B" if qwen3 else "DeepSeek-V2-Lite" if dsv2 else "Qwen1.5-MoE-A2.7B"
+    res = {"metric": VLLM_PREFILL_METRIC if dsv2 else VLLM_METRIC,
+           "value": top["prefill_tokens_s"] if dsv2 else top["decode_tokens_s"], "unit": "tokens/s", "n_gpus": 1,
+           "steps": 1 if dsv2 else 128, "warmup": a.warmup,
+           "ms_per_step": top["prefill_s"] * 1e3 if dsv2 else top["ms_per_token_step"], "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "f16" if dtype == "float16" else "bf16",
            "data": "vLLM dummy weights (random), random prompt token ids",
-           "config": {"workload": f"{'Qwen3-30B-A3B' if qwen3 else 'Qwen1.5-MoE-A2.7B'} ({layers} layers) in vLLM, "
+           "config": {"workload": f"{model_name} ({layers} MoE layers{' + 1 dense' if dsv2 else ''}) in vLLM, "
                                   f"prompt {prompt}, generate 128",
                       "format": format_name(fmt), "engine": "vLLM LLM(quantization='lut', load_format='dummy'), "
                       "CUDA graphs on", "init_s": round(init_s, 1)},
