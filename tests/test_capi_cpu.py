@@ -327,11 +327,31 @@ def test_header_compiles_as_c99_and_links(tmp_path):
     assert r.returncode == 0 and "c caller ok" in r.stdout, (r.returncode, r.stdout, r.stderr)
 
 
-def test_fused_lut_gemv_rejects_other_block_sizes():
+def test_fused_lut_gemv_rejects_blocks_below_128():
     from block_lut_b200.fused_kernel import fused_lut_gemv
     z = torch.zeros(4)
     with pytest.raises(ValueError, match="128"):
         fused_lut_gemv(z, torch.zeros(2, 4, dtype=torch.uint8), z, z, block_size=64)
+
+
+@pytest.mark.parametrize("block,nb_short", [(256, 0), (384, 0), (512, 3)])
+def test_fused_lut_gemv_absmax_expansion_keeps_the_reference_block_index(block, nb_short):
+    """Blocks of a multiple of 128 reach the 128-element kernel through one
+    scale per 128 elements; each flat element must get the scale of the
+    reference's saturating block index, min(flat // block, nb - 1)
+    (fused_kernel.py:40-44), including an absmax shorter than the matrix
+    needs (nb_short scales missing)."""
+    from block_lut_b200.fused_kernel import absmax_per_128
+    m, k = 6, 640
+    n = m * k
+    nb = -(-n // block) - nb_short
+    am = torch.arange(1, nb + 1, dtype=torch.float32)
+    e = absmax_per_128(am, block, n)
+    assert e.numel() == -(-n // 128)
+    flat = torch.arange(n)
+    kernel_scale = e[(flat // 128).clamp(max=e.numel() - 1)]  # what blut_lut_gemv reads
+    reference_scale = am[(flat // block).clamp(max=nb - 1)]
+    assert torch.equal(kernel_scale, reference_scale)
 
 
 def test_ep_window_layout_and_argument_checks():
