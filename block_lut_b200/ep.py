@@ -425,6 +425,9 @@ def run_bench_ep(a, rank, world, dev, build_layers, make_inputs, Clocks, peaks, 
                    "config": {"workload": f"{shp['NAME']}, decode batch {a.batch} per rank",
                               "layers": a.layers, "global_batch": total_tokens, "experts": E, "top_k": TOPK,
                               "format": format_name(fmt), "parallelism": f"ep{world}",
+                              "local_experts": c,
+                              "local_rows": world * xchg.capacity,
+                              "expected_slots": eps[0].local._expected_slots(world * xchg.capacity),
                               "exchange": "blut_ep_dispatch / blut_ep_combine: each token row stored only in its "
                                           "owner ranks' windows over NVLink, fp32 output rows loaded back "
                                           "(no NCCL on the data path)"},
