@@ -330,7 +330,6 @@ def cpu_sample(batch, fmt, shape=None, seed=0, reps=2):
 def run_ours(a):
     import torch
     import torch.distributed as dist
-    from block_lut_b200 import _lib
     from block_lut_b200.moe import LUTMoELayer, LUTMoEStep, router
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

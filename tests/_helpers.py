@@ -8,7 +8,7 @@ import torch
 from oracle import blut_oracle as O
 
 from block_lut_b200.formats import LUTFormat, QuantizedMatrix
-from block_lut_b200.moe import LUTExperts, LUTMoELayer, SharedExpert
+from block_lut_b200.moe import LUTExperts
 
 # north_star tolerance for layer outputs (fp32 accumulation): max-abs 2e-3, rel-L2 1e-3.
 MAX_ABS = 2e-3
