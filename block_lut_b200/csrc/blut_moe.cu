@@ -648,7 +648,11 @@ size_t moe_workspace(const blut_moe_args& a, uint8_t* base, MoEWs* ws) {
 
 int validate_moe(const blut_moe_args& a) {
   if (a.num_tokens <= 0 || a.hidden <= 0 || a.inter <= 0 || a.num_experts <= 0 || a.top_k <= 0) return BLUT_ERR_INVALID;
-  if (a.num_experts > kMaxExperts || a.top_k > 32 || a.top_k > a.num_experts) return BLUT_ERR_UNSUPPORTED;
+  // The router picks k distinct experts, so it needs k <= E.  Caller routing
+  // does not: under expert parallelism a rank may own fewer experts than k,
+  // the other slots of its rows being empty (-1).
+  if (a.num_experts > kMaxExperts || a.top_k > 32 || (!a.topk_ids && a.top_k > a.num_experts))
+    return BLUT_ERR_UNSUPPORTED;
   if ((int64_t)a.num_tokens * a.top_k > kMaxSlots) return BLUT_ERR_UNSUPPORTED;
   if (a.hidden % kChunk || a.inter % kChunk) return BLUT_ERR_UNSUPPORTED;
   if (a.dtype != BLUT_F16 && a.dtype != BLUT_BF16) return BLUT_ERR_INVALID;

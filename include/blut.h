@@ -270,7 +270,8 @@ typedef struct {
   int32_t hidden;      /* H                                                     */
   int32_t inter;       /* I (per routed expert)                                 */
   int32_t num_experts; /* E                                                     */
-  int32_t top_k;       /* k                                                     */
+  int32_t top_k;       /* k, at most 32; at most E when the library routes
+                          (router_w), any with the caller's topk_ids       */
   int32_t dtype;       /* activation / output dtype: BLUT_F16 or BLUT_BF16      */
   blut_mat_desc w13;   /* per expert [2I, H]: rows 0..I-1 gate, I..2I-1 up      */
   blut_mat_desc w2;    /* per expert [H, I]                                     */

@@ -139,6 +139,21 @@ def test_moe_forward_rejects_bad_arguments_before_launching(kw, rc):
     assert lib.blut_moe_forward(C.byref(_args(**kw)), None, 0, None) == rc
 
 
+def test_top_k_above_the_expert_count_needs_caller_routing():
+    """The router picks k distinct experts, so k > E is refused when the
+    library routes.  With the caller's ids it is a valid layer: under expert
+    parallelism a rank may own fewer experts than k (its other slots are -1)."""
+    lib = _lib.lib()
+    a = _args(num_experts=2, top_k=8)
+    assert lib.blut_moe_workspace_size(C.byref(a)) > 0
+    a.topk_ids, a.router_w = None, 1 << 22
+    assert lib.blut_moe_workspace_size(C.byref(a)) == 0
+    assert lib.blut_moe_forward(C.byref(a), None, 0, None) == _lib.BLUT_ERR_UNSUPPORTED
+    a.top_k = 2
+    assert lib.blut_moe_workspace_size(C.byref(a)) > 0
+    assert lib.blut_moe_workspace_size(C.byref(_args(top_k=33))) == 0
+
+
 def test_moe_forward_rejects_small_workspace():
     lib = _lib.lib()
     assert lib.blut_moe_forward(C.byref(_args()), 1 << 22, 16, None) == _lib.BLUT_ERR_WORKSPACE
