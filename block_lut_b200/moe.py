@@ -134,7 +134,7 @@ class LUTMoELayer:
         self.shared_gate_mode = int(shared_gate_mode)
         self.dtype = experts.fmt.compute_dtype
         self._args = self._make_args()
-        self._ws_need = {}  # workspace bytes per token count (they depend on nothing else that changes)
+        self._ws_need = {}  # workspace bytes per (token count, expected slots): nothing else of the args changes
 
     def _make_args(self) -> _lib.MoEArgs:
         ex = self.experts
@@ -207,13 +207,13 @@ class LUTMoELayer:
     def _launch(self, a: _lib.MoEArgs, x2: torch.Tensor, stream) -> None:
         """blut_moe_forward with this call's arguments ``a`` on the layer's workspace."""
         lib = _lib.lib()
-        T = int(a.num_tokens)
-        need = self._ws_need.get(T)
+        key = (int(a.num_tokens), int(a.expected_slots))  # the split, hence the size, depends on both
+        need = self._ws_need.get(key)
         if need is None:
             need = lib.blut_moe_workspace_size(C.byref(a))
             if need == 0:
                 raise RuntimeError("blut_moe_forward rejected the layer arguments (see blut_moe_workspace_size)")
-            self._ws_need[T] = need
+            self._ws_need[key] = need
         ws = workspace(x2.device, need, self.ws_slot, stream)
         with _lib.on_device(x2):
             _lib.check(lib.blut_moe_forward(C.byref(a), ws.data_ptr(), ws.numel(), _lib.stream_ptr(stream)),
