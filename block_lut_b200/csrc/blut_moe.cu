@@ -428,10 +428,12 @@ static bool same_format(const blut_mat_desc& a, const blut_mat_desc& b) {
   return a.format == b.format && a.bits == b.bits && a.group == b.group && a.tier == b.tier && a.dtype == b.dtype;
 }
 
-// Expected number of experts hit by T tokens choosing k of E uniformly.
+// Expected number of experts hit by T tokens choosing k of E uniformly
+// (every expert once k >= E, which caller routing allows).
 static double expected_active(int T, int k, int E) {
+  const double keep = std::max(0.0, 1.0 - (double)k / E);
   double miss = 1.0;
-  for (int t = 0; t < T; ++t) miss *= 1.0 - (double)k / E;
+  for (int t = 0; t < T; ++t) miss *= keep;
   return E * (1.0 - miss);
 }
 
