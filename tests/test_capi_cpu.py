@@ -395,3 +395,60 @@ def test_ep_window_layout_and_argument_checks():
     assert lib.blut_ep_combine(C.byref(d), 0, None, None, 0, None) == _lib.BLUT_ERR_INVALID
     assert lib.blut_ep_views(C.byref(d), None, None, None, None) == _lib.BLUT_ERR_INVALID
     assert lib.blut_ep_alloc(0, C.byref(C.c_void_p())) == _lib.BLUT_ERR_INVALID
+
+
+def test_layer_workspace_size_follows_the_expected_slots(monkeypatch):
+    """LUTMoELayer caches blut_moe_workspace_size per call shape.  The split,
+    and so the size, depends on the expected slots as well as the token
+    count: a layer whose slot_fraction changes between calls at the same
+    token count must ask again, not reuse the smaller size (which the
+    library refuses with BLUT_ERR_WORKSPACE).  The library is stubbed: this
+    checks the host bookkeeping only."""
+    from block_lut_b200 import moe as M
+
+    class FakeLib:
+        def __init__(self):
+            self.sizes, self.launched = [], []
+
+        def blut_moe_workspace_size(self, ap):
+            n = 1000 + 10 * ap._obj.expected_slots
+            self.sizes.append(n)
+            return n
+
+        def blut_moe_forward(self, ap, ws, nbytes, stream):
+            self.launched.append((ap._obj.expected_slots, nbytes))
+            return _lib.BLUT_OK
+
+    fake = FakeLib()
+    got = []
+
+    class Buf:
+        def __init__(self, n):
+            self.n = n
+
+        def data_ptr(self):
+            return 256
+
+        def numel(self):
+            return self.n
+
+    def fake_workspace(device, nbytes, slot=0, stream=None):
+        got.append(nbytes)
+        return Buf(nbytes)
+
+    monkeypatch.setattr(M._lib, "lib", lambda: fake)
+    monkeypatch.setattr(M._lib, "stream_ptr", lambda stream=None: 0)
+    monkeypatch.setattr(M, "workspace", fake_workspace)
+    layer = M.LUTMoELayer.__new__(M.LUTMoELayer)
+    layer.top_k, layer.slot_fraction, layer.ws_slot, layer._ws_need = 4, 1.0, 0, {}
+    x2 = torch.zeros(128, 8)
+    for frac, want_slots in ((1.0, 0), (0.2, 103), (1.0, 0), (0.2, 103)):
+        layer.slot_fraction = frac
+        a = _lib.MoEArgs()
+        a.num_tokens = 128
+        a.expected_slots = layer._expected_slots(128)
+        assert a.expected_slots == want_slots
+        layer._launch(a, x2, None)
+        assert got[-1] == 1000 + 10 * want_slots
+    assert fake.sizes == [1000, 2030]  # one size query per (tokens, expected slots)
+    assert fake.launched == [(0, 1000), (103, 2030), (0, 1000), (103, 2030)]
