@@ -5,11 +5,15 @@ Same arguments as the reference (fast_moe.py:30-80): reference-format
 router's ``topk_ids`` / ``topk_weights``.  Instead of a Python loop over the
 unique experts (one GEMV launch and host sync per expert), every active
 (token, expert) pair runs in one ``blut_moe_forward`` call.  The first call
-on a weight stack repacks it into the tiled layout and caches it (keyed by
-the tensors' storage and version, like the reference's id-keyed cache).
+on a weight stack repacks it into the tiled layout and caches it, keyed by
+the tensors' address, shape and version.  An entry also holds weak
+references to the tensors it was built from (their view bases), so a stack
+freed and replaced by another at the same address is repacked, not served
+from the stale entry (the reference's id-keyed cache can alias that way).
 """
 from __future__ import annotations
 
+import weakref
 from collections import OrderedDict
 
 import torch
@@ -27,13 +31,25 @@ def _key(*ts):
     return tuple((t.data_ptr(), tuple(t.shape), t._version) for t in ts)
 
 
+def _root(t: torch.Tensor) -> torch.Tensor:
+    """The tensor that owns t's memory: its view base, or t itself."""
+    return t._base if t._base is not None else t
+
+
+def _same_tensors(refs, ts) -> bool:
+    return all(r() is _root(t) for r, t in zip(refs, ts))
+
+
 def r8_layer(w13_weight, w13_absmax, w2_weight, w2_absmax, codebook, top_k: int, tier: int = 0) -> LUTMoELayer:
     """Tiled ``LUTMoELayer`` for reference-format stacks (cached)."""
-    key = _key(w13_weight, w13_absmax, w2_weight, w2_absmax, codebook) + (top_k, tier)
-    layer = _CACHE.get(key)
+    ts = (w13_weight, w13_absmax, w2_weight, w2_absmax, codebook)
+    key = _key(*ts) + (top_k, tier)
+    hit = _CACHE.get(key)
+    layer = hit[0] if hit is not None and _same_tensors(hit[1], ts) else None
     if layer is not None:
         _CACHE.move_to_end(key)
     else:
+        _CACHE.pop(key, None)
         while len(_CACHE) >= _CACHE_MAX:
             _CACHE.popitem(last=False)
         fmt = LUTFormat("r8", 8, 128, tier)
@@ -46,7 +62,7 @@ def r8_layer(w13_weight, w13_absmax, w2_weight, w2_absmax, codebook, top_k: int,
         experts = LUTExperts.from_quantized([w13.expert(e) for e in range(e_n)],
                                             [w2.expert(e) for e in range(e_n)], cb)
         layer = LUTMoELayer(experts, top_k)
-        _CACHE[key] = layer
+        _CACHE[key] = (layer, [weakref.ref(_root(t)) for t in ts])
     return layer
 
 
