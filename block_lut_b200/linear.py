@@ -10,6 +10,7 @@ number of tokens.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 from typing import Optional
 
@@ -47,8 +48,9 @@ class LUTLinear:
         x = x.contiguous()
         m = x.shape[0]
         dt = torch.float32 if out_f32 else x.dtype
-        if out is None:
-            out = torch.empty(m, self.rows, dtype=dt, device=x.device)
+        if out is None:  # allocated on the launch stream, so the caching allocator orders its reuse there
+            with torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext():
+                out = torch.empty(m, self.rows, dtype=dt, device=x.device)
         elif tuple(out.shape) != (m, self.rows) or out.dtype != dt or not out.is_contiguous():
             raise ValueError("out has the wrong shape, dtype or layout")
         if m == 0:  # an empty batch: nothing to launch
@@ -57,7 +59,7 @@ class LUTLinear:
         need = lib.blut_matmul_workspace_size(C.byref(self.desc), m)
         if need == 0:
             raise RuntimeError(f"blut_matmul rejects m={m} for {self.fmt} [{self.rows}, {self.cols}]")
-        ws = workspace(x.device, need)
+        ws = workspace(x.device, need, stream=stream)
         with _lib.on_device(x):
             _lib.check(lib.blut_matmul(C.byref(self.desc), self.buf.data_ptr(),
                                        None if self.lut_table is None else self.lut_table.data_ptr(), x.data_ptr(),
