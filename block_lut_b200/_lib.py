@@ -140,6 +140,26 @@ def stream_ptr(stream=None) -> int:
     return int(s.cuda_stream)
 
 
+def stream_ordered(fn):
+    """Decorator for wrappers with a ``stream`` argument: the body runs with
+    that stream (when given) as torch's current stream, so the tensors the
+    wrapper converts or allocates belong to the stream its kernels run on.
+    Otherwise a converted input freed on return could be handed out again by
+    the caching allocator while the kernel on ``stream`` still reads it."""
+    import contextlib
+    import functools
+    import inspect
+    import torch
+    sig = inspect.signature(fn)
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        s = sig.bind_partial(*args, **kwargs).arguments.get("stream")
+        with torch.cuda.stream(s) if s is not None else contextlib.nullcontext():
+            return fn(*args, **kwargs)
+    return wrapper
+
+
 def on_device(t):
     """Context making the device of CUDA tensor ``t`` current.  The library
     launches on the current device, so every call runs under the device of

@@ -32,6 +32,7 @@ def _check(t: torch.Tensor, dtype: torch.dtype, name: str):
         raise ValueError(f"{name}: expected a contiguous CUDA {dtype} tensor")
 
 
+@_lib.stream_ordered
 def pack_bitplanes(idx: torch.Tensor, stream=None) -> torch.Tensor:
     """uint8 indices [n] (any shape, n % 4 == 0) -> the n-byte bit-plane buffer."""
     _check(idx, torch.uint8, "idx")
@@ -44,6 +45,7 @@ def pack_bitplanes(idx: torch.Tensor, stream=None) -> torch.Tensor:
     return planes
 
 
+@_lib.stream_ordered
 def recover_tier(planes: torch.Tensor, absmax: torch.Tensor, table: torch.Tensor, n: int, tier: int,
                  block_size: int = 128, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """bf16 [n] = table[index] * absmax[i // block_size] from a tier's sections.

@@ -125,6 +125,7 @@ def _check_cuda(*ts):
             raise ValueError("libblut expects contiguous CUDA tensors")
 
 
+@_lib.stream_ordered
 def encode(w: torch.Tensor, fmt: LUTFormat, stream=None) -> QuantizedMatrix:
     """Quantise a float matrix [rows, cols] with the GPU Lloyd encoder (formats b / nested)."""
     if fmt.kind not in ("b", "nested"):
@@ -149,6 +150,7 @@ def encode(w: torch.Tensor, fmt: LUTFormat, stream=None) -> QuantizedMatrix:
     return QuantizedMatrix(fmt, rows, cols, codes, tables, codes2, tables2)
 
 
+@_lib.stream_ordered
 def encode_r(w: torch.Tensor, codebook: torch.Tensor, block_size: int = 128, stream=None):
     """Reference BlockLUT quantiser on the GPU: returns (uint8 indices [N], bf16 absmax [nb])."""
     w = w.to(torch.bfloat16).contiguous().reshape(-1)
@@ -163,6 +165,7 @@ def encode_r(w: torch.Tensor, codebook: torch.Tensor, block_size: int = 128, str
     return idx, absmax
 
 
+@_lib.stream_ordered
 def encode_lut_f32(w: torch.Tensor, codebook_f: torch.Tensor, block_size: int = 128, stream=None):
     """The fast BlockLUT encoder's rule on the GPU (fp32 normalisation against
     an fp32 codebook): returns (uint8 indices [N], bf16 absmax [nb])."""
@@ -178,6 +181,7 @@ def encode_lut_f32(w: torch.Tensor, codebook_f: torch.Tensor, block_size: int = 
     return idx, absmax
 
 
+@_lib.stream_ordered
 def dequant(qm: QuantizedMatrix, stream=None) -> torch.Tensor:
     """Bit-exact dequantisation of one matrix to [rows, cols] (bf16 for r8, fp16 otherwise)."""
     out_dtype = qm.fmt.compute_dtype
@@ -200,6 +204,7 @@ def tiled_bytes(fmt: LUTFormat, rows: int, cols: int, paired: bool = False, tc: 
     return int(n)
 
 
+@_lib.stream_ordered
 def pack_tiled(mats, stream=None, paired: bool = False, tc: bool = False) -> tuple[torch.Tensor, int]:
     """Repack canonical matrices (a list, all of one format and shape) into one
     tiled buffer; returns (uint8 buffer, per-matrix stride in bytes).
@@ -220,6 +225,7 @@ def pack_tiled(mats, stream=None, paired: bool = False, tc: bool = False) -> tup
     return buf, stride
 
 
+@_lib.stream_ordered
 def dequant_tiled(fmt: LUTFormat, rows: int, cols: int, tiled: torch.Tensor, lut_table: Optional[torch.Tensor] = None,
                   stream=None, paired: bool = False, tc: bool = False) -> torch.Tensor:
     """Dense matrix rebuilt from one tiled matrix through the kernels' lookups."""

@@ -1,6 +1,7 @@
 """libblut.so without a GPU: it loads, exports every symbol of include/blut.h,
 and its host-side argument checks answer before any CUDA call."""
 import ctypes as C
+import inspect
 import os
 import re
 import shutil
@@ -452,3 +453,30 @@ def test_layer_workspace_size_follows_the_expected_slots(monkeypatch):
         assert got[-1] == 1000 + 10 * want_slots
     assert fake.sizes == [1000, 2030]  # one size query per (tokens, expected slots)
     assert fake.launched == [(0, 1000), (103, 2030), (0, 1000), (103, 2030)]
+
+
+def test_stream_ordered_wrappers_run_on_the_callers_stream(monkeypatch):
+    """Wrappers given a stream run their body with it as torch's current
+    stream (inputs converted and outputs allocated there); without one they
+    run as before.  Positional and keyword stream arguments both count."""
+    import contextlib
+    entered = []
+
+    @contextlib.contextmanager
+    def fake_stream(s):
+        entered.append(s)
+        yield
+
+    monkeypatch.setattr(torch.cuda, "stream", fake_stream)
+
+    @_lib.stream_ordered
+    def op(x, y=1, stream=None, z=0):
+        return (x, y, stream, z, list(entered))
+
+    assert op(1) == (1, 1, None, 0, [])
+    assert op(1, 2, "s1") == (1, 2, "s1", 0, ["s1"])
+    assert op(1, stream="s2", z=3) == (1, 1, "s2", 3, ["s1", "s2"])
+    from block_lut_b200 import bitplanes, formats
+    for fn in (formats.encode, formats.encode_r, formats.encode_lut_f32, formats.dequant, formats.pack_tiled,
+               formats.dequant_tiled, bitplanes.pack_bitplanes, bitplanes.recover_tier):
+        assert "stream" in inspect.signature(fn).parameters and hasattr(fn, "__wrapped__"), fn.__name__
