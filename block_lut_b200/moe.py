@@ -7,7 +7,6 @@ caller-owned workspace, so it can be captured in a CUDA graph.
 """
 from __future__ import annotations
 
-import contextlib
 import ctypes as C
 import math
 import threading
@@ -88,7 +87,6 @@ class SharedExpert:
 
 _WS: dict = {}
 _WS_LOCK = threading.Lock()
-_nullctx = contextlib.nullcontext
 
 
 def workspace(device: torch.device, nbytes: int, slot: int = 0, stream=None) -> torch.Tensor:
@@ -177,7 +175,16 @@ class LUTMoELayer:
         """out[t] = sum_j w[t,j] * expert_{ids[t,j]}(x_t) (+ shared(x_t)); x [T, H].
 
         ``out_f32`` returns the unrounded float32 sums (expert-parallel partials).
+        ``stream``: launch there instead of on torch's current stream; the
+        input conversions, the output allocation and the copies after the
+        launch then run on it too, in order with the kernels.
         """
+        if stream is not None:
+            with torch.cuda.stream(stream):
+                return self._forward(x, topk_ids, topk_weights, out, stream, out_f32)
+        return self._forward(x, topk_ids, topk_weights, out, None, out_f32)
+
+    def _forward(self, x, topk_ids, topk_weights, out, stream, out_f32):
         if not x.is_cuda:
             raise ValueError("LUTMoELayer.forward expects CUDA tensors (no CPU path)")
         if x.numel() == 0:  # an empty batch (as torch's ops return for the reference): nothing to launch
@@ -190,8 +197,7 @@ class LUTMoELayer:
         x2, a, keep = self._prepare(x, topk_ids, topk_weights)
         T = x2.shape[0]
         if out is None or out.dtype != self.dtype:
-            with torch.cuda.stream(stream) if stream is not None else _nullctx():
-                res = torch.empty(T, x2.shape[1], dtype=self.dtype, device=x2.device)
+            res = torch.empty(T, x2.shape[1], dtype=self.dtype, device=x2.device)
         else:
             res = out.reshape(T, -1)
         a.out = res.data_ptr()
@@ -249,8 +255,7 @@ class LUTMoELayer:
     def _forward_f32(self, x, topk_ids, topk_weights, out, stream):
         x2, a, keep = self._prepare(x, topk_ids, topk_weights)
         if out is None:
-            with torch.cuda.stream(stream) if stream is not None else _nullctx():
-                res = torch.empty(x2.shape[0], x2.shape[1], dtype=torch.float32, device=x2.device)
+            res = torch.empty(x2.shape[0], x2.shape[1], dtype=torch.float32, device=x2.device)
         else:
             res = out
         if res.dtype != torch.float32 or not res.is_contiguous():
@@ -334,6 +339,7 @@ class LUTMoEStep:
             m.check_status()
 
 
+@_lib.stream_ordered
 def router(x: torch.Tensor, w_router: torch.Tensor, top_k: int, renorm: bool = False,
            shared_gate: bool = False, stream=None):
     """Fused router on the GPU: (topk_ids int32 [T,k], topk_weights f32 [T,k], gate f32 [T] | None)."""
