@@ -10,7 +10,6 @@ number of tokens.
 """
 from __future__ import annotations
 
-import contextlib
 import ctypes as C
 from typing import Optional
 
@@ -39,6 +38,7 @@ class LUTLinear:
             raise RuntimeError(f"blut_matmul rejects m={m} for {self.fmt} [{self.rows}, {self.cols}]")
         return n
 
+    @_lib.stream_ordered
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, out_f32: bool = False,
                 stream=None) -> torch.Tensor:
         if x.dim() != 2 or x.shape[1] != self.cols:
@@ -48,9 +48,8 @@ class LUTLinear:
         x = x.contiguous()
         m = x.shape[0]
         dt = torch.float32 if out_f32 else x.dtype
-        if out is None:  # allocated on the launch stream, so the caching allocator orders its reuse there
-            with torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext():
-                out = torch.empty(m, self.rows, dtype=dt, device=x.device)
+        if out is None:
+            out = torch.empty(m, self.rows, dtype=dt, device=x.device)
         elif tuple(out.shape) != (m, self.rows) or out.dtype != dt or not out.is_contiguous():
             raise ValueError("out has the wrong shape, dtype or layout")
         if m == 0:  # an empty batch: nothing to launch
