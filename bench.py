@@ -962,8 +962,9 @@ def run_vllm(a):
     qwen3, dsv2 = a.vllm_model == "qwen3", a.vllm_model == "dsv2lite"
     d = tempfile.mkdtemp(prefix="blut_vllm_")
     make_config = qwen3_moe_config if qwen3 else dsv2_lite_config if dsv2 else qwen15_moe_config
+    cfg = make_config(layers, lut_quant_config(fmt), dtype)
     with open(os.path.join(d, "config.json"), "w") as f:
-        json.dump(make_config(layers, lut_quant_config(fmt), dtype), f)
+        json.dump(cfg, f)
     prompt = 1024 if qwen3 else 4096 if dsv2 else 512
     batches = [8] if dsv2 else sorted({1, a.batch})
     extra = {"max_num_batched_tokens": prompt * max(batches)} if dsv2 else {}  # the whole batch in one prefill
@@ -975,7 +976,9 @@ def run_vllm(a):
     rng = random.Random(0)
     res_b = {}
     for bs in batches:
-        prompts = [{"prompt_token_ids": [rng.randrange(1000, 150000) for _ in range(prompt)]} for _ in range(bs)]
+        # token ids inside the model's vocabulary (102400 for DeepSeek-V2-Lite, 151936 for the Qwen models)
+        hi = min(150000, cfg["vocab_size"] - 1000)
+        prompts = [{"prompt_token_ids": [rng.randrange(1000, hi) for _ in range(prompt)]} for _ in range(bs)]
 
         def gen(n):
             sp = SamplingParams(max_tokens=n, min_tokens=n, ignore_eos=True, temperature=0.0, detokenize=False)

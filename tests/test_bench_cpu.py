@@ -37,3 +37,14 @@ def test_dsv2_lite_config_matches_the_prefill_stack():
     cfg = transformers.DeepseekV2Config(**{k: v for k, v in c.items()
                                            if k not in ("architectures", "model_type", "quantization_config")})
     assert cfg.n_group == 1 and cfg.topk_group == 1 and cfg.topk_method == "greedy"
+
+
+def test_vllm_prompt_ids_stay_inside_every_vocabulary():
+    """run_vllm draws prompt token ids below min(150000, vocab - 1000): inside
+    DeepSeek-V2-Lite's 102400-entry vocabulary as well as Qwen's 151936."""
+    import inspect
+    src = inspect.getsource(bench.run_vllm)
+    assert 'min(150000, cfg["vocab_size"] - 1000)' in src
+    for make in (bench.qwen15_moe_config, bench.qwen3_moe_config, bench.dsv2_lite_config):
+        v = make(2, {}, "float16")["vocab_size"]
+        assert min(150000, v - 1000) <= v
