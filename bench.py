@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""LUT-MoE decode throughput on B200 (BASELINE config 2's MoE stack).
+"""LUT-MoE decode throughput on B200 (config 2's MoE stack: Qwen1.5-MoE-A2.7B).
 
 Workload: the 24 MoE layers of Qwen1.5-MoE-A2.7B at decode -- per layer a
 softmax top-4 router over 60 routed experts (SwiGLU, I=1408) quantised to
@@ -36,7 +36,7 @@ sys.path.insert(0, ROOT)
 H, E, I, TOPK, IS, LAYERS = 2048, 60, 1408, 4, 5632, 24
 QWEN = dict(H=H, E=E, I=I, IS=IS, TOPK=TOPK, LAYERS=LAYERS, RENORM=False, BATCH=32,
             NAME="Qwen1.5-MoE-A2.7B MoE stack", KIND="b")
-# the 48 MoE layers of Qwen3-30B-A3B at decode -- 128 routed
+# Config 3: the 48 MoE layers of Qwen3-30B-A3B at decode -- 128 routed
 # experts of I 768, top-8 softmax renormalised, no shared expert, batch 64,
 # NestedLUT 2+2 with g 64 (full tier, or coarse only with --tier 1).
 QWEN3 = dict(H=2048, E=128, I=768, IS=0, TOPK=8, LAYERS=48, RENORM=True, BATCH=64,
@@ -48,7 +48,7 @@ QWEN3 = dict(H=2048, E=128, I=768, IS=0, TOPK=8, LAYERS=48, RENORM=True, BATCH=6
 # no traffic
 TRAFFIC_RATIOS = {("b", 4, 64, 0): 1.024, ("r8", 8, 128, 0): 1.035, ("nested", 4, 64, 1): 1.06}
 METRIC = "LUT-MoE decode tokens/s; expert LUT-GEMV HBM GB/s vs ~8 TB/s peak"
-# DeepSeek-V2-Lite MoE layers (26 of 27; layer 0 is dense),
+# Config 4: DeepSeek-V2-Lite MoE layers (26 of 27; layer 0 is dense),
 # 64 routed experts of I 1408, top-6 softmax, two shared experts (one MLP of
 # I 2816), prefill of 8 x 4096 tokens.
 DSV2 = dict(H=2048, E=64, I=1408, IS=2816, TOPK=6, LAYERS=26, TOKENS=8 * 4096, RENORM=False,
@@ -75,7 +75,7 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--workload", choices=["decode", "qwen3", "prefill", "sweep", "tiers", "vllm"], default="decode",
-                   help="decode: the BASELINE metric (config 2); qwen3: config 3's MoE stack at decode; "
+                   help="decode: the headline metric (config 2); qwen3: config 3's MoE stack at decode; "
                         "prefill: config 4's MoE layers; sweep: config 5's single-matrix kernel sweep; "
                         "tiers: Format R progressive bit-plane tier recover; vllm: config 2 end to end "
                         "through vLLM with the lut plugin")
@@ -675,7 +675,7 @@ def run_prefill(a):
     print(json.dumps(res), flush=True)
 
 
-# single-matrix LUT GEMV/GEMM sweep, N x K of the MoE
+# Config 5: single-matrix LUT GEMV/GEMM sweep, N x K of the MoE
 # projections, M tokens, Format B b bits and table block g.
 SWEEP_NK = [(1408, 2048), (2048, 1408), (768, 2048), (2048, 768), (5632, 2048)]
 SWEEP_METRIC = "LUT GEMV/GEMM kernel sweep: fraction of the attainable roofline (geometric mean)"
@@ -875,7 +875,7 @@ VLLM_PREFILL_METRIC = "vLLM prefill tokens/s, full model, LUT experts"
 
 
 def qwen15_moe_config(layers: int, quant: dict, dtype: str) -> dict:
-    """config.json of the Qwen1.5-MoE-A2.7B architecture."""
+    """config.json of the Qwen1.5-MoE-A2.7B architecture (config 2)."""
     return {
         "architectures": ["Qwen2MoeForCausalLM"], "model_type": "qwen2_moe",
         "hidden_size": 2048, "intermediate_size": 5632, "moe_intermediate_size": 1408,
@@ -890,7 +890,7 @@ def qwen15_moe_config(layers: int, quant: dict, dtype: str) -> dict:
 
 
 def qwen3_moe_config(layers: int, quant: dict, dtype: str) -> dict:
-    """config.json of the Qwen3-30B-A3B architecture: 128
+    """config.json of the Qwen3-30B-A3B architecture (config 3): 128
     experts of I 768, top-8 renormalised, no shared expert, 32 query and 4
     key/value heads of 128."""
     return {
@@ -906,7 +906,7 @@ def qwen3_moe_config(layers: int, quant: dict, dtype: str) -> dict:
 
 
 def dsv2_lite_config(layers: int, quant: dict, dtype: str) -> dict:
-    """config.json of the DeepSeek-V2-Lite architecture:
+    """config.json of the DeepSeek-V2-Lite architecture (config 4):
     27 layers, the first a dense MLP (I 10944); 64 routed experts of I 1408,
     top-6 softmax without renormalisation, 2 shared experts; MLA attention
     with kv_lora_rank 512, no query compression, 16 heads of 128 + 64 rope

@@ -29,7 +29,7 @@ by running the reference's Python code, see ``tests/golden/make_golden.py``):
   * ``moe_forward``    -- ``vllm_lut/quant_method.py:230-279`` (apply) with the
                           intermediate rounded at the points the CUDA path rounds.
 
-Format B (BASELINE's packed per-(row, block) codebooks) and NestedLUT 2+2 have
+Format B (packed codes into per-(row, block) codebooks) and NestedLUT 2+2 have
 no implementation in the reference.  Their definitions here are this build's
 restatement of the reference's building blocks -- Lloyd iterations of
 ``quantizer.py:120-178`` run per (row, block), the argmin assignment of
@@ -515,7 +515,7 @@ def moe_forward_reference_bf16(x: np.ndarray, topk_ids: np.ndarray, topk_w: np.n
 
 
 # ----------------------------------------------------------------------------
-# Synthetic inputs: Student-t(df=5) weights scaled to std
+# Synthetic inputs of the benchmark configs: Student-t(df=5) weights scaled to std
 # 0.02, N(0,1) activations RMS-normalised per token.
 # ----------------------------------------------------------------------------
 

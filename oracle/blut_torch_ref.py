@@ -15,7 +15,7 @@ dequantises the whole expert (the reference: ``cb[idx] * absmax[i // 128]``,
 tokens that chose the expert, weighted.  Format R runs in bf16 as the
 reference does; Format B and NestedLUT (per-(row, block) fp16 tables, no
 reference code) gather their tables into fp32 weights and accumulate in fp32
-(BASELINE's CPU plan: "table gather + F.linear, fp32 accumulate").
+(a table gather, then F.linear with fp32 accumulation).
 """
 from __future__ import annotations
 

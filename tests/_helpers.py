@@ -10,7 +10,7 @@ from oracle import blut_oracle as O
 from block_lut_b200.formats import LUTFormat, QuantizedMatrix
 from block_lut_b200.moe import LUTExperts
 
-# north_star tolerance for layer outputs (fp32 accumulation): max-abs 2e-3, rel-L2 1e-3.
+# Tolerance for layer outputs (fp32 accumulation): max-abs 2e-3, rel-L2 1e-3.
 MAX_ABS = 2e-3
 REL_L2 = 1e-3
 
@@ -32,8 +32,8 @@ def check_layer(out: torch.Tensor, ref64: np.ndarray, dtype: torch.dtype, what: 
     """GPU layer output vs the float64 oracle.
 
     fp16 outputs: max-abs <= 2e-3 and rel-L2 <= 1e-3 directly.  bf16 outputs
-    carry bf16's own final rounding (2^-9 relative), which alone exceeds the
-    north_star's rel-L2: they are compared with the oracle rounded to bf16,
+    carry bf16's own final rounding (2^-9 relative), which alone exceeds that
+    rel-L2: they are compared with the oracle rounded to bf16,
     allowing 1 bf16 ulp per element and rel-L2 <= 1e-3.
     """
     o = out.float().cpu().numpy().astype(np.float64)

@@ -1,6 +1,6 @@
 """bench.py's model descriptions without a GPU: the config.json each vLLM
 workload writes describes the same MoE shapes as the kernel-level workloads
-(3 and 4), and transformers reads them with the routing
+(configs 2, 3 and 4), and transformers reads them with the routing
 fields vLLM's grouped top-k needs (a group count of None would break it)."""
 import pytest
 

@@ -1,4 +1,4 @@
-"""Parity at the full shapes of BASELINE's named configurations, against the
+"""Parity at the full shapes of the named benchmark configurations, against the
 float64 oracle on the same quantised weights (tolerances in
 tests/_helpers.check_layer: max-abs 2e-3 and rel-L2 1e-3 for fp16 outputs).
 

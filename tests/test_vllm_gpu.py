@@ -1,4 +1,4 @@
-"""The LUT plugin inside vLLM (BASELINE config 2's caller): ``LLM(model=<Qwen1.5-
+"""The LUT plugin inside vLLM (config 2's caller): ``LLM(model=<Qwen1.5-
 MoE-A2.7B architecture, 2 layers>, quantization="lut", load_format="dummy")``
 generates tokens, and the routed experts of every MoE layer run through
 ``LUTFusedMoEMethod.apply`` (vllm/model_executor/layers/fused_moe/runner/
